@@ -1,0 +1,165 @@
+/*
+ * ultravec_b200.h -- C ABI of the B200 trellis codec (encode) and codes-only
+ * scan (flat + IVF).
+ *
+ * A drop-in for the two data-parallel hot paths of ultravec-ann:
+ *   - the free-start Viterbi trellis encoder (src/trellis.rs), and
+ *   - the codes-only MIPS / cosine scan with RaBitQ's rescaled estimator and a
+ *     per-query top-k (src/trellis.rs search/score, src/ivf.rs, src/bench.rs).
+ * Every entry point names the reference item it replaces (file:line).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Array arguments may live in host memory
+ *     or in device memory of the handle's GPU; the library detects which and
+ *     stages host buffers through the call's stream.  Host results are valid
+ *     when the call returns; device results are ordered on `stream`.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call returns UV_OK (0) or a UV_E* status; nothing throws across the
+ *     ABI and nothing aborts.  uv_last_error() gives a message for the calling
+ *     thread.
+ *   - Handles are immutable during a search: concurrent uv_*_search calls on one
+ *     index from several threads/streams are safe (per-call scratch).  Adds and
+ *     builds must not overlap searches of the same index.
+ *   - Rows are `dim` f32 values, already zero-padded to a power of two by the
+ *     caller exactly as the reference loader does (src/datasets.rs:95-103).
+ *   - Ranking everywhere is score descending, then id ascending; NaN scores
+ *     rank last.  Unfilled top-k slots hold id -1 and score -inf.  A query with
+ *     |q| < f32::EPSILON returns only unfilled slots (the reference returns an
+ *     empty list, src/trellis.rs:2124-2127).
+ */
+#ifndef ULTRAVEC_B200_H
+#define ULTRAVEC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UV_OK 0
+#define UV_EINVAL 1        /* bad argument or configuration */
+#define UV_ENOMEM 2        /* device or host allocation failed */
+#define UV_ECUDA 3         /* a CUDA call failed; see uv_last_error() */
+#define UV_ETIMEDOUT 4     /* a bounded device wait gave up */
+#define UV_EUNSUPPORTED 5  /* valid for the reference, not built for sm_100a yet */
+
+#define UV_ABI_VERSION 1
+
+/* Mirrors TrellisConfig (src/trellis.rs:352-391). */
+typedef struct uv_config {
+    int32_t dim;             /* padded dimension */
+    int32_t bits;            /* emitted bits per coordinate, 1..4 */
+    int32_t mem;             /* trellis memory M (state bits) */
+    int32_t rotation_rounds; /* rounds of seeded sign flip + FWHT (3) */
+    uint64_t rotation_seed;  /* 42 */
+    int32_t start_bits;      /* free-start width, <= mem (mem) */
+    int32_t rescale_bits;    /* 0 = exact f32 rescale */
+    float branch_lambda;     /* anisotropic metric weight; 0 = plain MSE */
+    int32_t device;          /* CUDA device ordinal the handle lives on */
+} uv_config;
+
+typedef struct uv_codec uv_codec;
+typedef struct uv_index uv_index;
+typedef struct uv_ivf uv_ivf;
+
+int uv_abi_version(void);
+const char *uv_last_error(void);
+
+/* TrellisConfig::new (src/trellis.rs:379-390): seed 42, 3 rounds, full free
+ * start, exact rescale, device 0. */
+void uv_config_default(uv_config *cfg, int32_t dim, int32_t bits, int32_t mem);
+
+/* TrellisQuantizer::from_config (src/trellis.rs:430-458).  Builds the code
+ * table (593-610) and rotation signs (src/lib.rs:428-463) on the host and
+ * uploads them to cfg->device. */
+int uv_codec_create(const uv_config *cfg, uv_codec **out);
+int uv_codec_destroy(uv_codec *codec);
+
+/* code_table_bits (src/trellis.rs:649-655): 2^(mem+bits) f32 bit patterns. */
+int uv_codec_code_table_bits(const uv_codec *codec, uint32_t *out, int64_t capacity);
+/* rotation_sign_rounds (src/trellis.rs:663-667): rounds x dim, +-1.0 */
+int uv_codec_rotation_sign_rounds(const uv_codec *codec, float *out, int64_t capacity);
+/* memory_bits (src/trellis.rs:658-660) */
+int uv_codec_memory_bits(const uv_codec *codec, int32_t *mem);
+/* record layout: ceil(dim*bits/8) code bytes, ceil(start_bits/8) start bytes,
+ * 4 rescale bytes (scalar_bytes, src/trellis.rs:401-418) */
+int uv_codec_record_bytes(const uv_codec *codec, int32_t *code_bytes, int32_t *start_bytes,
+                          int32_t *rescale_bytes);
+
+/* encode_codes over a batch (src/trellis.rs:672-675, 1164-1212; the per-row
+ * work of add_batch 2103-2119).  rows: n x dim.  Outputs: codes n x
+ * code_bytes (packed MSB-first), start n, rescale n (+inf when <= 1e-6),
+ * rnorm n (1.0 uncentered; may be NULL).  centroids (n_centroids x dim) turns
+ * on centering (with_centroids, 952-956): each row is assigned to its
+ * first-maximum centroid, cidx n receives it (may be NULL). */
+int uv_encode(const uv_codec *codec, const float *rows, int64_t n, const float *centroids,
+              int32_t n_centroids, uint8_t *codes, uint32_t *start, float *rescale,
+              float *rnorm, uint32_t *cidx, void *stream);
+
+/* encode_rotated (src/trellis.rs:689-699): rows are already rotated units. */
+int uv_encode_rotated(const uv_codec *codec, const float *u_r, int64_t n, uint8_t *codes,
+                      uint32_t *start, void *stream);
+
+/* rotate (src/trellis.rs:680-682 -> src/lib.rs:472-484), n rows. */
+int uv_rotate(const uv_codec *codec, const float *rows, int64_t n, float *out, void *stream);
+
+/* decode_codes (src/trellis.rs:705-720): table values by window, inverse
+ * rotated, not normalized.  n records -> n x dim. */
+int uv_decode(const uv_codec *codec, const uint8_t *codes, const uint32_t *start, int64_t n,
+              float *out, void *stream);
+
+/* window_at (src/trellis.rs:727-743) for all i: n records -> n x dim windows */
+int uv_windows(const uv_codec *codec, const uint8_t *codes, const uint32_t *start, int64_t n,
+               uint32_t *out, void *stream);
+
+/* encode_digest (src/trellis.rs:970-990) of n records: XOR of per-record
+ * FNV-1a over start (LE u32) then the code bytes. */
+int uv_digest(const uv_codec *codec, const uint8_t *codes, const uint32_t *start, int64_t n,
+              uint64_t *digest, void *stream);
+
+/* ---- flat codes-only index: VectorBackend for TrellisQuantizer
+ *      (src/lib.rs:104-155, src/trellis.rs:2088-2247) ---- */
+
+/* TrellisQuantizer::new(..).with_codes_only(true): an empty device index. */
+int uv_index_create(const uv_codec *codec, uv_index **out);
+int uv_index_destroy(uv_index *index);
+/* with_centroids / with_mean (src/trellis.rs:952-956, 746-748) */
+int uv_index_set_centroids(uv_index *index, const float *centroids, int32_t n_centroids);
+/* reserve (src/lib.rs:131, src/trellis.rs:2100-2102) */
+int uv_index_reserve(uv_index *index, int64_t additional);
+/* add (src/trellis.rs:2095-2099) for n rows with explicit ids; also stores
+ * each row's exact l2 norm, the MIPS sidecar of src/bench.rs:1019. */
+int uv_index_add(uv_index *index, const int64_t *ids, const float *rows, int64_t n,
+                 void *stream);
+/* add_batch (src/trellis.rs:2103-2119): ids 0..n-1, order preserving. */
+int uv_index_add_batch(uv_index *index, const float *rows, int64_t n, void *stream);
+/* len / dimensions / mem_bytes (src/trellis.rs:2089-2092, 2184-2201) */
+int uv_index_len(const uv_index *index, int64_t *len);
+int uv_index_dimensions(const uv_index *index, int32_t *dim);
+int uv_index_mem_bytes(const uv_index *index, int64_t *bytes);
+
+#define UV_SEARCH_COSINE 0 /* VectorBackend::search: the codec's score */
+#define UV_SEARCH_MIPS 1   /* score x exact row norm (src/bench.rs:1029-1045) */
+
+/* search (src/trellis.rs:2120-2183) for nq queries, top-k (k <= 128) per
+ * query: ids_out/scores_out are nq x k. */
+int uv_index_search(const uv_index *index, const float *queries, int64_t nq, int32_t k,
+                    int32_t mode, int64_t *ids_out, float *scores_out, void *stream);
+
+/* The records, for export or parity checks: any pointer may be NULL. */
+int uv_index_export(const uv_index *index, uint8_t *codes, uint32_t *start, float *rescale,
+                    float *rnorm, float *norms, int64_t *ids, void *stream);
+/* encode_digest of the stored records. */
+int uv_index_digest(const uv_index *index, uint64_t *digest, void *stream);
+
+/* Merge per-shard top-k lists (the multi-GPU combine after an all-gather):
+ * in_ids/in_scores are nq x n_lists x k_in, each list sorted by the ranking
+ * above; out is nq x k.  Device or host memory. */
+int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
+                  int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
+                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -313,7 +313,7 @@ void uvo_codec_free(uvo_codec *c) {
     free(c);
 }
 
-/* trellis.rs:957-961 with_centroids */
+/* trellis.rs:952-956 with_centroids */
 int uvo_codec_set_centroids(uvo_codec *c, const float *centroids, int n_centroids) {
     free(c->centroids);
     c->centroids = NULL;

@@ -1,0 +1,9 @@
+"""ultravec-ann_b200: B200-native (sm_100a) trellis encoder and codes-only
+scan behind a C ABI (include/ultravec_b200.h).
+
+The directory name is not a Python identifier, so the package is registered
+as `ultravec_ann_b200` by `load()` in ultravec_ann_b200_loader.py (repo root)
+or by any importer that points importlib at this directory.
+"""
+from .binding import (Codec, Index, UVError, build, check, lib, topk_merge,  # noqa: F401
+                      UV_SEARCH_COSINE, UV_SEARCH_MIPS, SYMBOLS)

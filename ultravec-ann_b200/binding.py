@@ -1,0 +1,353 @@
+"""ctypes binding of libultravec_b200.so (include/ultravec_b200.h).
+
+The Python face of the C ABI, mirroring the reference's codec interface:
+`Codec` is TrellisQuantizer's record API (src/trellis.rs:645-743) and
+`Index` is its VectorBackend in codes-only mode (src/lib.rs:104-155,
+src/trellis.rs:2088-2247).  Arrays may be numpy (host) or CUDA torch tensors
+(device, ordered on torch's current stream); results come back in the same
+kind.  There is no CPU fallback: a missing library or a CUDA failure raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libultravec_b200.so"
+
+UV_OK, UV_EINVAL, UV_ENOMEM, UV_ECUDA, UV_ETIMEDOUT, UV_EUNSUPPORTED = range(6)
+UV_SEARCH_COSINE, UV_SEARCH_MIPS = 0, 1
+
+# Every symbol the header declares (checked by the CPU tests).
+SYMBOLS = [
+    "uv_abi_version", "uv_last_error", "uv_config_default", "uv_codec_create",
+    "uv_codec_destroy", "uv_codec_code_table_bits", "uv_codec_rotation_sign_rounds",
+    "uv_codec_memory_bits", "uv_codec_record_bytes", "uv_encode", "uv_encode_rotated",
+    "uv_rotate", "uv_decode", "uv_windows", "uv_digest", "uv_index_create", "uv_index_destroy",
+    "uv_index_set_centroids", "uv_index_reserve", "uv_index_add", "uv_index_add_batch",
+    "uv_index_len", "uv_index_dimensions", "uv_index_mem_bytes", "uv_index_search",
+    "uv_index_export", "uv_index_digest", "uv_topk_merge",
+]
+
+
+class UVError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ultravec_b200 error {code}: {msg}")
+        self.code = code
+
+
+class uv_config(C.Structure):
+    _fields_ = [("dim", C.c_int32), ("bits", C.c_int32), ("mem", C.c_int32),
+                ("rotation_rounds", C.c_int32), ("rotation_seed", C.c_uint64),
+                ("start_bits", C.c_int32), ("rescale_bits", C.c_int32),
+                ("branch_lambda", C.c_float), ("device", C.c_int32)]
+
+
+_lib = None
+
+
+def lib():
+    """Load the in-tree library; fail loudly when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run `make -C {HERE}` (nvcc, sm_100a)")
+        L = C.CDLL(str(LIB_PATH))
+        vp, i32, i64, u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64
+        vpp = C.POINTER(C.c_void_p)
+        sig = {
+            "uv_abi_version": (C.c_int, []),
+            "uv_last_error": (C.c_char_p, []),
+            "uv_config_default": (None, [C.POINTER(uv_config), i32, i32, i32]),
+            "uv_codec_create": (C.c_int, [C.POINTER(uv_config), vpp]),
+            "uv_codec_destroy": (C.c_int, [vp]),
+            "uv_codec_code_table_bits": (C.c_int, [vp, vp, i64]),
+            "uv_codec_rotation_sign_rounds": (C.c_int, [vp, vp, i64]),
+            "uv_codec_memory_bits": (C.c_int, [vp, C.POINTER(i32)]),
+            "uv_codec_record_bytes": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32),
+                                                C.POINTER(i32)]),
+            "uv_encode": (C.c_int, [vp, vp, i64, vp, i32, vp, vp, vp, vp, vp, vp]),
+            "uv_encode_rotated": (C.c_int, [vp, vp, i64, vp, vp, vp]),
+            "uv_rotate": (C.c_int, [vp, vp, i64, vp, vp]),
+            "uv_decode": (C.c_int, [vp, vp, vp, i64, vp, vp]),
+            "uv_windows": (C.c_int, [vp, vp, vp, i64, vp, vp]),
+            "uv_digest": (C.c_int, [vp, vp, vp, i64, C.POINTER(u64), vp]),
+            "uv_index_create": (C.c_int, [vp, vpp]),
+            "uv_index_destroy": (C.c_int, [vp]),
+            "uv_index_set_centroids": (C.c_int, [vp, vp, i32]),
+            "uv_index_reserve": (C.c_int, [vp, i64]),
+            "uv_index_add": (C.c_int, [vp, vp, vp, i64, vp]),
+            "uv_index_add_batch": (C.c_int, [vp, vp, i64, vp]),
+            "uv_index_len": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_index_dimensions": (C.c_int, [vp, C.POINTER(i32)]),
+            "uv_index_mem_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_index_search": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp]),
+            "uv_index_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp]),
+            "uv_index_digest": (C.c_int, [vp, C.POINTER(u64), vp]),
+            "uv_topk_merge": (C.c_int, [i32, vp, vp, i64, i32, i32, i32, vp, vp, vp]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != UV_OK:
+        raise UVError(rc, lib().uv_last_error().decode(errors="replace"))
+
+
+# ---------------------------------------------------------------- arrays ---
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if _is_torch(x):
+        if not x.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return C.c_void_p(x.data_ptr())
+    if not x.flags["C_CONTIGUOUS"]:
+        raise ValueError("array must be C-contiguous")
+    return C.c_void_p(x.ctypes.data)
+
+
+def _stream(*arrays):
+    for a in arrays:
+        if a is not None and _is_torch(a) and a.is_cuda:
+            import torch
+
+            return C.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
+    return None
+
+
+class _Alloc:
+    """Output allocation in the same kind (numpy / torch-cuda) as an input."""
+
+    def __init__(self, like):
+        self.torch_dev = None
+        if like is not None and _is_torch(like) and like.is_cuda:
+            self.torch_dev = like.device
+
+    def __call__(self, shape, np_dtype):
+        if self.torch_dev is None:
+            return np.zeros(shape, np_dtype)
+        import torch
+
+        tmap = {np.uint8: torch.uint8, np.uint32: torch.int32, np.float32: torch.float32,
+                np.int64: torch.int64, np.int32: torch.int32}
+        return torch.zeros(shape, dtype=tmap[np_dtype], device=self.torch_dev)
+
+
+def _f32(x):
+    if _is_torch(x):
+        import torch
+
+        return x.to(torch.float32).contiguous()
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+# ----------------------------------------------------------------- codec ---
+
+class Codec:
+    """TrellisQuantizer::from_config (src/trellis.rs:430-458) on one GPU."""
+
+    def __init__(self, dim: int, bits: int, mem: int, *, seed: int = 42, rounds: int = 3,
+                 start_bits: int | None = None, rescale_bits: int = 0,
+                 branch_lambda: float = 0.0, device: int = 0):
+        cfg = uv_config()
+        lib().uv_config_default(C.byref(cfg), dim, bits, mem)
+        cfg.rotation_seed = seed
+        cfg.rotation_rounds = rounds
+        cfg.start_bits = mem if start_bits is None else start_bits
+        cfg.rescale_bits = rescale_bits
+        cfg.branch_lambda = branch_lambda
+        cfg.device = device
+        h = C.c_void_p()
+        check(lib().uv_codec_create(C.byref(cfg), C.byref(h)))
+        self.h = h
+        self.dim, self.bits, self.mem, self.device = dim, bits, mem, device
+        self.rounds = max(1, rounds)
+        cb, sb, rb = C.c_int32(), C.c_int32(), C.c_int32()
+        check(lib().uv_codec_record_bytes(self.h, C.byref(cb), C.byref(sb), C.byref(rb)))
+        self.code_bytes, self.start_bytes, self.rescale_bytes = cb.value, sb.value, rb.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uv_codec_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # record API -------------------------------------------------------
+    def code_table_bits(self) -> np.ndarray:
+        out = np.zeros(1 << (self.mem + self.bits), np.uint32)
+        check(lib().uv_codec_code_table_bits(self.h, _ptr(out), out.size))
+        return out
+
+    def code_table(self) -> np.ndarray:
+        return self.code_table_bits().view(np.float32)
+
+    def rotation_sign_rounds(self) -> np.ndarray:
+        out = np.zeros((self.rounds, self.dim), np.float32)
+        check(lib().uv_codec_rotation_sign_rounds(self.h, _ptr(out), out.size))
+        return out
+
+    def memory_bits(self) -> int:
+        m = C.c_int32()
+        check(lib().uv_codec_memory_bits(self.h, C.byref(m)))
+        return m.value
+
+    def encode(self, rows, centroids=None):
+        """encode_codes over a batch: dict(codes, start, rescale, rnorm, cidx)."""
+        rows = _f32(rows)
+        n = rows.shape[0]
+        alloc = _Alloc(rows)
+        out = dict(codes=alloc((n, self.code_bytes), np.uint8), start=alloc(n, np.uint32),
+                   rescale=alloc(n, np.float32), rnorm=alloc(n, np.float32),
+                   cidx=alloc(n, np.uint32))
+        cen = None if centroids is None else _f32(centroids)
+        ncen = 0 if cen is None else cen.shape[0]
+        check(lib().uv_encode(self.h, _ptr(rows), n, _ptr(cen), ncen, _ptr(out["codes"]),
+                              _ptr(out["start"]), _ptr(out["rescale"]), _ptr(out["rnorm"]),
+                              _ptr(out["cidx"]), _stream(rows)))
+        return out
+
+    def encode_rotated(self, u_r):
+        u_r = _f32(u_r)
+        n = u_r.shape[0]
+        alloc = _Alloc(u_r)
+        codes, start = alloc((n, self.code_bytes), np.uint8), alloc(n, np.uint32)
+        check(lib().uv_encode_rotated(self.h, _ptr(u_r), n, _ptr(codes), _ptr(start),
+                                      _stream(u_r)))
+        return codes, start
+
+    def rotate(self, rows):
+        rows = _f32(rows)
+        out = _Alloc(rows)(rows.shape, np.float32)
+        check(lib().uv_rotate(self.h, _ptr(rows), rows.shape[0], _ptr(out), _stream(rows)))
+        return out
+
+    def decode(self, codes, start):
+        n = codes.shape[0]
+        out = _Alloc(codes)((n, self.dim), np.float32)
+        check(lib().uv_decode(self.h, _ptr(codes), _ptr(start), n, _ptr(out), _stream(codes)))
+        return out
+
+    def windows(self, codes, start):
+        n = codes.shape[0]
+        out = _Alloc(codes)((n, self.dim), np.uint32)
+        check(lib().uv_windows(self.h, _ptr(codes), _ptr(start), n, _ptr(out), _stream(codes)))
+        return out
+
+    def digest(self, codes, start) -> int:
+        h = C.c_uint64()
+        check(lib().uv_digest(self.h, _ptr(codes), _ptr(start), codes.shape[0], C.byref(h),
+                              _stream(codes)))
+        return h.value
+
+
+# ----------------------------------------------------------------- index ---
+
+class Index:
+    """Codes-only VectorBackend over the device-resident SoA records."""
+
+    def __init__(self, codec: Codec):
+        h = C.c_void_p()
+        check(lib().uv_index_create(codec.h, C.byref(h)))
+        self.h, self.codec = h, codec
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uv_index_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_centroids(self, centroids):
+        cen = _f32(centroids)
+        check(lib().uv_index_set_centroids(self.h, _ptr(cen), cen.shape[0]))
+
+    def reserve(self, additional: int):
+        check(lib().uv_index_reserve(self.h, additional))
+
+    def add(self, ids, rows):
+        rows = _f32(rows)
+        ids = ids if _is_torch(ids) else np.ascontiguousarray(ids, np.int64)
+        check(lib().uv_index_add(self.h, _ptr(ids), _ptr(rows), rows.shape[0], _stream(rows)))
+
+    def add_batch(self, rows):
+        rows = _f32(rows)
+        check(lib().uv_index_add_batch(self.h, _ptr(rows), rows.shape[0], _stream(rows)))
+
+    def __len__(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_index_len(self.h, C.byref(n)))
+        return n.value
+
+    def mem_bytes(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_index_mem_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def search(self, queries, k: int, mips: bool = False):
+        """search (src/trellis.rs:2120-2183): top-k (ids, scores) per query."""
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        alloc = _Alloc(queries)
+        ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+        check(lib().uv_index_search(self.h, _ptr(queries), nq, k,
+                                    UV_SEARCH_MIPS if mips else UV_SEARCH_COSINE, _ptr(ids),
+                                    _ptr(scores), _stream(queries)))
+        return ids, scores
+
+    def export(self):
+        n = len(self)
+        cb = self.codec.code_bytes
+        out = dict(codes=np.zeros((n, cb), np.uint8), start=np.zeros(n, np.uint32),
+                   rescale=np.zeros(n, np.float32), rnorm=np.zeros(n, np.float32),
+                   norms=np.zeros(n, np.float32), ids=np.zeros(n, np.int64))
+        check(lib().uv_index_export(self.h, _ptr(out["codes"]), _ptr(out["start"]),
+                                    _ptr(out["rescale"]), _ptr(out["rnorm"]), _ptr(out["norms"]),
+                                    _ptr(out["ids"]), None))
+        return out
+
+    def digest(self) -> int:
+        h = C.c_uint64()
+        check(lib().uv_index_digest(self.h, C.byref(h), None))
+        return h.value
+
+
+def topk_merge(in_ids, in_scores, k: int, device: int = 0):
+    """Merge per-shard top-k lists: in_* are nq x n_lists x k_in."""
+    nq, n_lists, k_in = in_ids.shape
+    alloc = _Alloc(in_ids)
+    ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+    check(lib().uv_topk_merge(device, _ptr(in_ids), _ptr(in_scores), nq, n_lists, k_in, k,
+                              _ptr(ids), _ptr(scores), _stream(in_ids)))
+    return ids, scores
+
+
+def build(verbose: bool = False) -> Path:
+    """Compile the library for sm_100a with the package Makefile."""
+    import subprocess
+
+    cmd = ["make", "-C", str(HERE), f"-j{min(8, os.cpu_count() or 1)}"]
+    subprocess.run(cmd, check=True, capture_output=not verbose)
+    return LIB_PATH

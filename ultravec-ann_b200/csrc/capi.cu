@@ -1,0 +1,867 @@
+// capi.cpp -- the extern "C" boundary (include/ultravec_b200.h).
+//
+// Owns the handles, decides where each caller buffer lives (host or device),
+// stages host buffers through stream-ordered device allocations, plans and
+// launches the kernels, and turns every failure into a status code plus a
+// thread-local message.  No exception or abort crosses the ABI.
+#include "ultravec_b200.h"
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "codebook.h"
+#include "uv_kernels.h"
+#include "uv_util.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+
+#define UV_CK(call)                                                                  \
+  do {                                                                               \
+    cudaError_t e_ = (call);                                                         \
+    if (e_ != cudaSuccess)                                                           \
+      return fail(e_ == cudaErrorMemoryAllocation ? UV_ENOMEM : UV_ECUDA,            \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));               \
+  } while (0)
+
+#define UV_TRY(expr)        \
+  do {                      \
+    int rc_ = (expr);       \
+    if (rc_ != UV_OK) return rc_; \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// Where a caller pointer lives.  Returns UV_EINVAL for device memory of
+// another GPU.
+int classify(const void *p, int device, bool *on_device) {
+  *on_device = false;
+  if (p == nullptr) return UV_OK;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return UV_OK;  // unregistered host memory
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    if (a.type == cudaMemoryTypeDevice && a.device != device)
+      return fail(UV_EINVAL, "device buffer belongs to another GPU");
+    *on_device = true;
+  }
+  return UV_OK;
+}
+
+// Stream-ordered scratch freed at scope exit (on the same stream).
+struct Scratch {
+  cudaStream_t st;
+  std::vector<void *> ptrs;
+  explicit Scratch(cudaStream_t s) : st(s) {}
+  ~Scratch() {
+    for (void *p : ptrs) cudaFreeAsync(p, st);
+  }
+  template <class T>
+  int alloc(T **out, size_t count) {
+    *out = nullptr;
+    if (count == 0) count = 1;
+    void *p = nullptr;
+    cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(UV_ENOMEM, std::string("cudaMallocAsync: ") + cudaGetErrorString(e));
+    }
+    ptrs.push_back(p);
+    *out = (T *)p;
+    return UV_OK;
+  }
+};
+
+// A caller input viewed on the device: used in place when it is device
+// memory, otherwise copied through scratch.
+template <class T>
+int stage_in(const T *src, size_t count, int device, Scratch &sc, const T **dev) {
+  bool on_dev = false;
+  UV_TRY(classify(src, device, &on_dev));
+  if (src == nullptr || on_dev) {
+    *dev = src;
+    return UV_OK;
+  }
+  T *d = nullptr;
+  UV_TRY(sc.alloc(&d, count));
+  UV_CK(cudaMemcpyAsync(d, src, count * sizeof(T), cudaMemcpyHostToDevice, sc.st));
+  *dev = d;
+  return UV_OK;
+}
+
+// A caller output: written in place on the device, or produced in scratch
+// and copied back (see Outputs::finish).
+struct Outputs {
+  struct Pending {
+    void *host;
+    const void *dev;
+    size_t bytes;
+  };
+  std::vector<Pending> pend;
+  template <class T>
+  int stage(T *dst, size_t count, int device, Scratch &sc, T **dev) {
+    bool on_dev = false;
+    UV_TRY(classify(dst, device, &on_dev));
+    if (dst == nullptr || on_dev) {
+      *dev = dst;
+      return UV_OK;
+    }
+    T *d = nullptr;
+    UV_TRY(sc.alloc(&d, count));
+    pend.push_back({(void *)dst, (const void *)d, count * sizeof(T)});
+    *dev = d;
+    return UV_OK;
+  }
+  int finish(cudaStream_t st) {
+    for (auto &p : pend) UV_CK(cudaMemcpyAsync(p.host, p.dev, p.bytes, cudaMemcpyDeviceToHost, st));
+    if (!pend.empty()) UV_CK(cudaStreamSynchronize(st));
+    return UV_OK;
+  }
+};
+
+template <class T>
+int grow(T **buf, int64_t old_n, int64_t new_cap, cudaStream_t st) {
+  T *nb = nullptr;
+  UV_CK(cudaMallocAsync((void **)&nb, (size_t)std::max<int64_t>(new_cap, 1) * sizeof(T), st));
+  if (*buf != nullptr && old_n > 0)
+    UV_CK(cudaMemcpyAsync(nb, *buf, (size_t)old_n * sizeof(T), cudaMemcpyDeviceToDevice, st));
+  if (*buf != nullptr) cudaFreeAsync(*buf, st);
+  *buf = nb;
+  return UV_OK;
+}
+
+}  // namespace
+
+struct uv_codec {
+  uv_config cfg;
+  int code_bytes = 0, code_stride = 0, table_len = 0;
+  std::vector<float> h_table;
+  uvb::RotationHost rot_host;
+  float *d_table = nullptr;
+  float *d_signs = nullptr;
+  uvb::RotParams rot;
+  uvb::EncodePlan plan;
+  int plan_status = 0;
+  std::string plan_why;
+};
+
+struct uv_index {
+  const uv_codec *codec = nullptr;
+  int64_t n = 0, cap = 0;
+  uint8_t *codes = nullptr;
+  uint32_t *start = nullptr;
+  float *rescale = nullptr, *rnorm = nullptr, *norms = nullptr;
+  uint32_t *cidx = nullptr;
+  int64_t *ids = nullptr;
+  float *centroids = nullptr;
+  int n_centroids = 0;
+};
+
+extern "C" {
+
+int uv_abi_version(void) { return UV_ABI_VERSION; }
+
+const char *uv_last_error(void) { return g_err.c_str(); }
+
+void uv_config_default(uv_config *cfg, int32_t dim, int32_t bits, int32_t mem) {
+  if (cfg == nullptr) return;
+  std::memset(cfg, 0, sizeof(*cfg));
+  cfg->dim = dim;
+  cfg->bits = bits;
+  cfg->mem = mem;
+  cfg->rotation_rounds = 3;
+  cfg->rotation_seed = 42;
+  cfg->start_bits = mem;
+  cfg->rescale_bits = 0;
+  cfg->branch_lambda = 0.0f;
+  cfg->device = 0;
+}
+
+int uv_codec_create(const uv_config *cfg, uv_codec **out) {
+  if (cfg == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  *out = nullptr;
+  if (cfg->dim <= 0) return fail(UV_EINVAL, "dim must be positive");
+  if (cfg->bits < 1 || cfg->bits > 4) return fail(UV_EINVAL, "bits must be 1..4");
+  if (cfg->mem < 1 || cfg->mem + cfg->bits > 24)
+    return fail(UV_EINVAL, "mem must be >= 1 with mem + bits <= 24");
+  if (cfg->rescale_bits < 0 || cfg->rescale_bits > 24)
+    return fail(UV_EINVAL, "rescale_bits must be 0..24");
+  int ndev = 0;
+  UV_CK(cudaGetDeviceCount(&ndev));
+  if (cfg->device < 0 || cfg->device >= ndev) return fail(UV_EINVAL, "no such CUDA device");
+  uv_codec *c = new (std::nothrow) uv_codec();
+  if (c == nullptr) return fail(UV_ENOMEM, "host allocation failed");
+  c->cfg = *cfg;
+  c->cfg.start_bits = std::min(std::max(cfg->start_bits, 0), cfg->mem);
+  c->cfg.rotation_rounds = std::max(cfg->rotation_rounds, 1);
+  c->code_bytes = (cfg->dim * cfg->bits + 7) / 8;
+  c->code_stride = (c->code_bytes + 15) & ~15;
+  c->h_table = uvb::build_code_table(cfg->mem, cfg->bits);
+  c->table_len = (int)c->h_table.size();
+  c->rot_host = uvb::build_rotation(cfg->dim, cfg->rotation_seed, c->cfg.rotation_rounds);
+  if ((int)c->rot_host.blk_off.size() > uvb::kMaxBlocks) {
+    delete c;
+    return fail(UV_EUNSUPPORTED, "dimension splits into too many power-of-two blocks");
+  }
+  DeviceGuard g(cfg->device);
+  cudaError_t e = cudaMalloc(&c->d_table, sizeof(float) * c->h_table.size());
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_signs, sizeof(float) * c->rot_host.signs.size());
+  if (e == cudaSuccess)
+    e = cudaMemcpy(c->d_table, c->h_table.data(), sizeof(float) * c->h_table.size(),
+                   cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(c->d_signs, c->rot_host.signs.data(), sizeof(float) * c->rot_host.signs.size(),
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(c->d_table);
+    cudaFree(c->d_signs);
+    delete c;
+    return fail(UV_ECUDA, std::string("codec upload: ") + cudaGetErrorString(e));
+  }
+  uvb::RotParams &r = c->rot;
+  std::memset(&r, 0, sizeof(r));
+  r.dim = cfg->dim;
+  r.rounds = c->rot_host.rounds;
+  r.n_blocks = (int)c->rot_host.blk_off.size();
+  for (int b = 0; b < r.n_blocks; b++) {
+    r.blk_off[b] = c->rot_host.blk_off[b];
+    r.blk_len[b] = c->rot_host.blk_len[b];
+    r.blk_inv[b] = c->rot_host.blk_inv[b];
+  }
+  r.signs = c->d_signs;
+  c->plan_status = uvb::encode_plan(cfg->dim, cfg->bits, cfg->mem, &c->plan, &c->plan_why);
+  *out = c;
+  return UV_OK;
+}
+
+int uv_codec_destroy(uv_codec *c) {
+  if (c == nullptr) return UV_OK;
+  {
+    DeviceGuard g(c->cfg.device);
+    cudaFree(c->d_table);
+    cudaFree(c->d_signs);
+  }
+  delete c;
+  return UV_OK;
+}
+
+int uv_codec_code_table_bits(const uv_codec *c, uint32_t *out, int64_t capacity) {
+  if (c == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  if (capacity < c->table_len) return fail(UV_EINVAL, "capacity below 2^(mem+bits)");
+  std::memcpy(out, c->h_table.data(), sizeof(float) * c->table_len);
+  return UV_OK;
+}
+
+int uv_codec_rotation_sign_rounds(const uv_codec *c, float *out, int64_t capacity) {
+  if (c == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  if (capacity < (int64_t)c->rot_host.signs.size()) return fail(UV_EINVAL, "capacity below rounds*dim");
+  std::memcpy(out, c->rot_host.signs.data(), sizeof(float) * c->rot_host.signs.size());
+  return UV_OK;
+}
+
+int uv_codec_memory_bits(const uv_codec *c, int32_t *mem) {
+  if (c == nullptr || mem == nullptr) return fail(UV_EINVAL, "null argument");
+  *mem = c->cfg.mem;
+  return UV_OK;
+}
+
+int uv_codec_record_bytes(const uv_codec *c, int32_t *code_bytes, int32_t *start_bytes,
+                          int32_t *rescale_bytes) {
+  if (c == nullptr) return fail(UV_EINVAL, "null argument");
+  if (code_bytes) *code_bytes = c->code_bytes;
+  if (start_bytes) *start_bytes = (std::min(c->cfg.start_bits, c->cfg.mem) + 7) / 8;
+  if (rescale_bytes) *rescale_bytes = c->cfg.rescale_bits > 0 ? (c->cfg.rescale_bits + 7) / 8 : 4;
+  return UV_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Encode rows already on the device into device outputs (codes at
+// code_stride).  The common core of uv_encode, uv_encode_rotated and
+// uv_index_add.
+int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
+                  int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
+                  float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc) {
+  if (c->plan_status == 1) return fail(UV_EINVAL, c->plan_why);
+  if (c->plan_status != 0) return fail(UV_EUNSUPPORTED, c->plan_why);
+  if (n == 0) return UV_OK;
+  uvb::EncodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.dim = c->cfg.dim;
+  p.n = n;
+  p.rows = rows;
+  p.code = c->d_table;
+  p.rot = c->rot;
+  p.lambda = c->cfg.branch_lambda;
+  p.start_bits = c->cfg.start_bits;
+  p.rescale_bits = c->cfg.rescale_bits;
+  p.centroids = centroids;
+  p.n_centroids = n_centroids;
+  p.codes = codes;
+  p.code_stride = c->code_stride;
+  p.code_bytes = c->code_bytes;
+  p.start = start;
+  p.rescale = rescale;
+  p.rnorm = rnorm;
+  p.cidx = cidx;
+  p.norms = norms;
+  p.rotated_input = rotated ? 1 : 0;
+  int grid = 0;
+  UV_CK(uvb::encode_grid(c->plan, n, &grid));
+  if (!c->plan.back_smem) {
+    const size_t words = (size_t)grid * c->plan.teams_per_cta * (size_t)c->plan.back_words_team;
+    UV_TRY(sc.alloc(&p.back_global, words));
+  }
+  UV_CK(uvb::encode_launch(c->plan, p, grid, st));
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+static int encode_common(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
+                         int32_t n_centroids, bool rotated, uint8_t *codes, uint32_t *start,
+                         float *rescale, float *rnorm, uint32_t *cidx, void *stream) {
+  if (c == nullptr || (rows == nullptr && n > 0)) return fail(UV_EINVAL, "null argument");
+  if (n < 0 || n_centroids < 0) return fail(UV_EINVAL, "negative size");
+  if (n_centroids > 0 && centroids == nullptr) return fail(UV_EINVAL, "null centroids");
+  if (n == 0) return UV_OK;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const int dev = c->cfg.device;
+  const int d = c->cfg.dim;
+  const float *d_rows = nullptr, *d_cen = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * d, dev, sc, &d_rows));
+  UV_TRY(stage_in(centroids, (size_t)n_centroids * d, dev, sc, &d_cen));
+  uint32_t *d_start = nullptr, *d_cidx = nullptr;
+  float *d_rescale = nullptr, *d_rnorm = nullptr;
+  UV_TRY(outs.stage(start, (size_t)n, dev, sc, &d_start));
+  if (!rotated) {
+    UV_TRY(outs.stage(rescale, (size_t)n, dev, sc, &d_rescale));
+    UV_TRY(outs.stage(rnorm, (size_t)n, dev, sc, &d_rnorm));
+    UV_TRY(outs.stage(cidx, (size_t)n, dev, sc, &d_cidx));
+  }
+  // codes: written at the padded stride, then compacted into the caller's
+  // dense layout unless the two coincide on the device.
+  bool codes_dev = false;
+  UV_TRY(classify(codes, dev, &codes_dev));
+  uint8_t *d_codes = nullptr;
+  const bool direct = codes_dev && c->code_stride == c->code_bytes;
+  if (direct) {
+    d_codes = codes;
+  } else if (codes != nullptr) {
+    UV_TRY(sc.alloc(&d_codes, (size_t)n * c->code_stride));
+  }
+  UV_TRY(encode_device(c, d_rows, n, d_cen, n_centroids, rotated, d_codes, d_start, d_rescale,
+                       d_rnorm, d_cidx, nullptr, st, sc));
+  if (codes != nullptr && !direct) {
+    UV_CK(cudaMemcpy2DAsync(codes, c->code_bytes, d_codes, c->code_stride, c->code_bytes, n,
+                            codes_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+    if (!codes_dev) UV_CK(cudaStreamSynchronize(st));
+  }
+  return outs.finish(st);
+}
+
+int uv_encode(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
+              int32_t n_centroids, uint8_t *codes, uint32_t *start, float *rescale, float *rnorm,
+              uint32_t *cidx, void *stream) {
+  return encode_common(c, rows, n, centroids, n_centroids, false, codes, start, rescale, rnorm,
+                       cidx, stream);
+}
+
+int uv_encode_rotated(const uv_codec *c, const float *u_r, int64_t n, uint8_t *codes,
+                      uint32_t *start, void *stream) {
+  return encode_common(c, u_r, n, nullptr, 0, true, codes, start, nullptr, nullptr, nullptr,
+                       stream);
+}
+
+int uv_rotate(const uv_codec *c, const float *rows, int64_t n, float *out, void *stream) {
+  if (c == nullptr || rows == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  if (n <= 0) return n == 0 ? UV_OK : fail(UV_EINVAL, "negative size");
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_rows = nullptr;
+  float *d_out = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * c->cfg.dim, c->cfg.device, sc, &d_rows));
+  UV_TRY(outs.stage(out, (size_t)n * c->cfg.dim, c->cfg.device, sc, &d_out));
+  UV_CK(uvb::launch_rotate(d_rows, n, c->rot, d_out, st));
+  return outs.finish(st);
+}
+
+int uv_windows(const uv_codec *c, const uint8_t *codes, const uint32_t *start, int64_t n,
+               uint32_t *out, void *stream) {
+  if (c == nullptr || codes == nullptr || start == nullptr || out == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  if (n <= 0) return n == 0 ? UV_OK : fail(UV_EINVAL, "negative size");
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const uint8_t *d_codes = nullptr;
+  const uint32_t *d_start = nullptr;
+  uint32_t *d_out = nullptr;
+  UV_TRY(stage_in(codes, (size_t)n * c->code_bytes, c->cfg.device, sc, &d_codes));
+  UV_TRY(stage_in(start, (size_t)n, c->cfg.device, sc, &d_start));
+  UV_TRY(outs.stage(out, (size_t)n * c->cfg.dim, c->cfg.device, sc, &d_out));
+  UV_CK(uvb::launch_windows(d_codes, c->code_bytes, c->code_bytes, d_start, n, c->cfg.dim,
+                            c->cfg.mem, c->cfg.bits, d_out, st));
+  return outs.finish(st);
+}
+
+int uv_decode(const uv_codec *c, const uint8_t *codes, const uint32_t *start, int64_t n,
+              float *out, void *stream) {
+  if (c == nullptr || codes == nullptr || start == nullptr || out == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  if (n <= 0) return n == 0 ? UV_OK : fail(UV_EINVAL, "negative size");
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const uint8_t *d_codes = nullptr;
+  const uint32_t *d_start = nullptr;
+  uint32_t *d_win = nullptr;
+  float *d_out = nullptr;
+  UV_TRY(stage_in(codes, (size_t)n * c->code_bytes, c->cfg.device, sc, &d_codes));
+  UV_TRY(stage_in(start, (size_t)n, c->cfg.device, sc, &d_start));
+  UV_TRY(sc.alloc(&d_win, (size_t)n * c->cfg.dim));
+  UV_TRY(outs.stage(out, (size_t)n * c->cfg.dim, c->cfg.device, sc, &d_out));
+  UV_CK(uvb::launch_windows(d_codes, c->code_bytes, c->code_bytes, d_start, n, c->cfg.dim,
+                            c->cfg.mem, c->cfg.bits, d_win, st));
+  UV_CK(uvb::launch_decode(d_win, c->d_table, n, c->rot, d_out, st));
+  return outs.finish(st);
+}
+
+int uv_digest(const uv_codec *c, const uint8_t *codes, const uint32_t *start, int64_t n,
+              uint64_t *digest, void *stream) {
+  if (c == nullptr || digest == nullptr || (n > 0 && (codes == nullptr || start == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  *digest = 0;
+  if (n <= 0) return n == 0 ? UV_OK : fail(UV_EINVAL, "negative size");
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  const uint8_t *d_codes = nullptr;
+  const uint32_t *d_start = nullptr;
+  unsigned long long *d_acc = nullptr;
+  UV_TRY(stage_in(codes, (size_t)n * c->code_bytes, c->cfg.device, sc, &d_codes));
+  UV_TRY(stage_in(start, (size_t)n, c->cfg.device, sc, &d_start));
+  UV_TRY(sc.alloc(&d_acc, 1));
+  UV_CK(cudaMemsetAsync(d_acc, 0, sizeof(unsigned long long), st));
+  UV_CK(uvb::launch_digest(d_codes, c->code_bytes, c->code_bytes, d_start, n, d_acc, st));
+  unsigned long long h = 0;
+  UV_CK(cudaMemcpyAsync(&h, d_acc, sizeof(h), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  *digest = h;
+  return UV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// flat index
+// ---------------------------------------------------------------------------
+
+int uv_index_create(const uv_codec *c, uv_index **out) {
+  if (c == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  uv_index *ix = new (std::nothrow) uv_index();
+  if (ix == nullptr) return fail(UV_ENOMEM, "host allocation failed");
+  ix->codec = c;
+  *out = ix;
+  return UV_OK;
+}
+
+int uv_index_destroy(uv_index *ix) {
+  if (ix == nullptr) return UV_OK;
+  {
+    DeviceGuard g(ix->codec->cfg.device);
+    cudaDeviceSynchronize();
+    cudaFree(ix->codes);
+    cudaFree(ix->start);
+    cudaFree(ix->rescale);
+    cudaFree(ix->rnorm);
+    cudaFree(ix->norms);
+    cudaFree(ix->cidx);
+    cudaFree(ix->ids);
+    cudaFree(ix->centroids);
+  }
+  delete ix;
+  return UV_OK;
+}
+
+int uv_index_set_centroids(uv_index *ix, const float *centroids, int32_t n_centroids) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  if (n_centroids < 0 || (n_centroids > 0 && centroids == nullptr))
+    return fail(UV_EINVAL, "bad centroids");
+  if (ix->n > 0) return fail(UV_EINVAL, "centroids must be set before the first add");
+  DeviceGuard g(ix->codec->cfg.device);
+  cudaFree(ix->centroids);
+  ix->centroids = nullptr;
+  ix->n_centroids = 0;
+  if (n_centroids == 0) return UV_OK;
+  const size_t bytes = sizeof(float) * (size_t)n_centroids * ix->codec->cfg.dim;
+  UV_CK(cudaMalloc(&ix->centroids, bytes));
+  UV_CK(cudaMemcpy(ix->centroids, centroids, bytes, cudaMemcpyDefault));
+  ix->n_centroids = n_centroids;
+  return UV_OK;
+}
+
+static int index_ensure(uv_index *ix, int64_t need, cudaStream_t st) {
+  if (need <= ix->cap) return UV_OK;
+  int64_t cap = std::max<int64_t>(need, ix->cap * 2);
+  const uv_codec *c = ix->codec;
+  UV_TRY(grow(&ix->codes, ix->n * c->code_stride, cap * c->code_stride, st));
+  UV_TRY(grow(&ix->start, ix->n, cap, st));
+  UV_TRY(grow(&ix->rescale, ix->n, cap, st));
+  UV_TRY(grow(&ix->rnorm, ix->n, cap, st));
+  UV_TRY(grow(&ix->norms, ix->n, cap, st));
+  UV_TRY(grow(&ix->cidx, ix->n, cap, st));
+  UV_TRY(grow(&ix->ids, ix->n, cap, st));
+  ix->cap = cap;
+  return UV_OK;
+}
+
+int uv_index_reserve(uv_index *ix, int64_t additional) {
+  if (ix == nullptr || additional < 0) return fail(UV_EINVAL, "bad argument");
+  DeviceGuard g(ix->codec->cfg.device);
+  UV_TRY(index_ensure(ix, ix->n + additional, 0));
+  UV_CK(cudaStreamSynchronize(0));
+  return UV_OK;
+}
+
+namespace {
+__global__ void iota_ids(int64_t *ids, int64_t n) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ids[i] = i;
+}
+}  // namespace
+
+static int index_add_impl(uv_index *ix, const int64_t *ids, const float *rows, int64_t n,
+                          void *stream) {
+  if (ix == nullptr || (n > 0 && rows == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (n < 0) return fail(UV_EINVAL, "negative size");
+  if (n == 0) return UV_OK;
+  const uv_codec *c = ix->codec;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  const float *d_rows = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * c->cfg.dim, c->cfg.device, sc, &d_rows));
+  UV_TRY(index_ensure(ix, ix->n + n, st));
+  const int64_t o = ix->n;
+  if (ids != nullptr) {
+    UV_CK(cudaMemcpyAsync(ix->ids + o, ids, sizeof(int64_t) * n, cudaMemcpyDefault, st));
+  } else {
+    iota_ids<<<(int)((n + 255) / 256), 256, 0, st>>>(ix->ids + o, n);
+    UV_CK(cudaGetLastError());
+  }
+  UV_TRY(encode_device(c, d_rows, n, ix->centroids, ix->n_centroids, false,
+                       ix->codes + o * c->code_stride, ix->start + o, ix->rescale + o,
+                       ix->rnorm + o, ix->cidx + o, ix->norms + o, st, sc));
+  ix->n += n;
+  bool rows_dev = false;
+  classify(rows, c->cfg.device, &rows_dev);
+  if (!rows_dev) UV_CK(cudaStreamSynchronize(st));
+  return UV_OK;
+}
+
+int uv_index_add(uv_index *ix, const int64_t *ids, const float *rows, int64_t n, void *stream) {
+  if (ids == nullptr && n > 0) return fail(UV_EINVAL, "null ids");
+  return index_add_impl(ix, ids, rows, n, stream);
+}
+
+int uv_index_add_batch(uv_index *ix, const float *rows, int64_t n, void *stream) {
+  return index_add_impl(ix, nullptr, rows, n, stream);
+}
+
+int uv_index_len(const uv_index *ix, int64_t *len) {
+  if (ix == nullptr || len == nullptr) return fail(UV_EINVAL, "null argument");
+  *len = ix->n;
+  return UV_OK;
+}
+
+int uv_index_dimensions(const uv_index *ix, int32_t *dim) {
+  if (ix == nullptr || dim == nullptr) return fail(UV_EINVAL, "null argument");
+  *dim = ix->codec->cfg.dim;
+  return UV_OK;
+}
+
+// mem_bytes (src/trellis.rs:2184-2201): codes + rescale + start (+ the
+// centering bytes of src/lib.rs:229-237) per record.
+int uv_index_mem_bytes(const uv_index *ix, int64_t *bytes) {
+  if (ix == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
+  int32_t cb = 0, sb = 0, rb = 0;
+  uv_codec_record_bytes(ix->codec, &cb, &sb, &rb);
+  int64_t center = 0;
+  if (ix->n_centroids == 1) {
+    center = 4;
+  } else if (ix->n_centroids > 1) {
+    int bitsn = 0;
+    uint64_t v = (uint64_t)(ix->n_centroids - 1);
+    while (v) {
+      bitsn++;
+      v >>= 1;
+    }
+    center = 4 + (bitsn + 7) / 8;
+  }
+  *bytes = ix->n * (int64_t)(cb + sb + rb + center);
+  return UV_OK;
+}
+
+int uv_index_export(const uv_index *ix, uint8_t *codes, uint32_t *start, float *rescale,
+                    float *rnorm, float *norms, int64_t *ids, void *stream) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  const uv_codec *c = ix->codec;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = ix->n;
+  if (n == 0) return UV_OK;
+  if (codes)
+    UV_CK(cudaMemcpy2DAsync(codes, c->code_bytes, ix->codes, c->code_stride, c->code_bytes, n,
+                            cudaMemcpyDefault, st));
+  if (start) UV_CK(cudaMemcpyAsync(start, ix->start, 4 * n, cudaMemcpyDefault, st));
+  if (rescale) UV_CK(cudaMemcpyAsync(rescale, ix->rescale, 4 * n, cudaMemcpyDefault, st));
+  if (rnorm) UV_CK(cudaMemcpyAsync(rnorm, ix->rnorm, 4 * n, cudaMemcpyDefault, st));
+  if (norms) UV_CK(cudaMemcpyAsync(norms, ix->norms, 4 * n, cudaMemcpyDefault, st));
+  if (ids) UV_CK(cudaMemcpyAsync(ids, ix->ids, 8 * n, cudaMemcpyDefault, st));
+  UV_CK(cudaStreamSynchronize(st));
+  return UV_OK;
+}
+
+int uv_index_digest(const uv_index *ix, uint64_t *digest, void *stream) {
+  if (ix == nullptr || digest == nullptr) return fail(UV_EINVAL, "null argument");
+  const uv_codec *c = ix->codec;
+  *digest = 0;
+  if (ix->n == 0) return UV_OK;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  unsigned long long *d_acc = nullptr;
+  UV_TRY(sc.alloc(&d_acc, 1));
+  UV_CK(cudaMemsetAsync(d_acc, 0, sizeof(unsigned long long), st));
+  UV_CK(uvb::launch_digest(ix->codes, c->code_stride, c->code_bytes, ix->start, ix->n, d_acc, st));
+  unsigned long long h = 0;
+  UV_CK(cudaMemcpyAsync(&h, d_acc, sizeof(h), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  *digest = h;
+  return UV_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_key,
+                 const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
+                 cudaStream_t st) {
+  uvb::MergeParams m;
+  std::memset(&m, 0, sizeof(m));
+  m.nq = nq;
+  m.n_lists = n_lists;
+  m.k_in = k_in;
+  m.k = k;
+  int pow2 = 32;
+  while (pow2 < n_lists * k_in) pow2 <<= 1;
+  if (pow2 > 8192) return fail(UV_EUNSUPPORTED, "merge of more than 8192 candidates per query");
+  m.pow2 = pow2;
+  const size_t per_warp = (size_t)pow2 * 16;
+  m.warps = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / per_warp));
+  m.in_key = in_key;
+  m.in_score = in_score;
+  m.in_id = in_id;
+  m.out_id = out_id;
+  m.out_score = out_score;
+  const size_t smem = per_warp * m.warps;
+  UV_CK(cudaFuncSetAttribute(uvb::merge_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem));
+  const int grid = (int)((nq + m.warps - 1) / m.warps);
+  void *args[] = {&m};
+  UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_kernel, dim3(grid), dim3(32 * m.warps), args,
+                         smem, st));
+  return UV_OK;
+}
+
+int sm_count(int dev) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms;
+}
+
+}  // namespace
+
+extern "C" {
+
+int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                    int64_t *ids_out, float *scores_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
+  if (nq == 0) return UV_OK;
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  if (d % 16 != 0 || d > 512)
+    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16, at most 512");
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * d, dev, sc, &d_q));
+  int64_t *d_ids = nullptr;
+  float *d_scores = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  // 1) prepare queries
+  const int dim_pad = (d + 3) & ~3;
+  float *q_r = nullptr, *qc = nullptr;
+  uint32_t *degen = nullptr;
+  UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
+  UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
+  UV_TRY(sc.alloc(&degen, (size_t)nq));
+  {
+    uvb::PrepParams pp;
+    std::memset(&pp, 0, sizeof(pp));
+    pp.dim = d;
+    pp.dim_pad = dim_pad;
+    pp.nq = nq;
+    pp.queries = d_q;
+    pp.rot = c->rot;
+    pp.centroids = ix->centroids;
+    pp.n_centroids = ix->n_centroids;
+    pp.q_r = q_r;
+    pp.qc = qc;
+    pp.degenerate = degen;
+    const size_t smem = (size_t)(dim_pad + 4) * 4 * 8;
+    UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
+    void *args[] = {&pp};
+    UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,
+                           smem, st));
+  }
+  // 2) scan with a per-split top-k
+  const int64_t n = ix->n;
+  int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;
+  const int rw = c->code_stride / 4;
+  int img_words = 4 + rw + 3;
+  if ((img_words & 1) == 0) img_words++;
+  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
+  const size_t smem = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
+  UV_CK(cudaFuncSetAttribute(uvb::flat_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem));
+  int per_sm = 1;
+  UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, uvb::flat_scan_kernel, 256, smem));
+  per_sm = std::max(per_sm, 1);
+  const int64_t slots = (int64_t)sm_count(dev) * per_sm;
+  int64_t splits = std::max<int64_t>(1, (slots * 4 + qtiles - 1) / qtiles);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, 2048 / k));
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, n / 256));
+  uint32_t *part_key = nullptr;
+  int64_t *part_id = nullptr;
+  UV_TRY(sc.alloc(&part_key, (size_t)nq * splits * k));
+  UV_TRY(sc.alloc(&part_id, (size_t)nq * splits * k));
+  if (n == 0) {
+    UV_CK(cudaMemsetAsync(part_key, 0, sizeof(uint32_t) * nq * splits * k, st));
+    UV_CK(cudaMemsetAsync(part_id, 0xff, sizeof(int64_t) * nq * splits * k, st));
+  } else {
+    uvb::ScanParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    sp.dim = d;
+    sp.mem = c->cfg.mem;
+    sp.bits = c->cfg.bits;
+    sp.nq = nq;
+    sp.n = n;
+    sp.q_r = q_r;
+    sp.q_stride = dim_pad;
+    sp.qc = qc;
+    sp.n_centroids = ix->n_centroids;
+    sp.degenerate = degen;
+    sp.codes = ix->codes;
+    sp.code_stride = c->code_stride;
+    sp.start = ix->start;
+    sp.rescale = ix->rescale;
+    sp.rnorm = ix->rnorm;
+    sp.norms = ix->norms;
+    sp.cidx = ix->cidx;
+    sp.code = c->d_table;
+    sp.table_len = c->table_len;
+    sp.table_in_smem = table_smem ? 1 : 0;
+    sp.img_words = img_words;
+    sp.mips = mode == UV_SEARCH_MIPS ? 1 : 0;
+    sp.k = k;
+    sp.ids = ix->ids;
+    sp.id_base = 0;
+    sp.part_key = part_key;
+    sp.part_id = part_id;
+    void *args[] = {&sp};
+    UV_CK(cudaLaunchKernel((const void *)uvb::flat_scan_kernel, dim3((unsigned)qtiles, (unsigned)splits),
+                           dim3(256), args, smem, st));
+  }
+  // 3) merge the splits
+  UV_TRY(merge_launch(nq, (int)splits, k, k, part_key, nullptr, part_id, d_ids, d_scores, st));
+  return outs.finish(st);
+}
+
+int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
+                  int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
+                  void *stream) {
+  if (in_ids == nullptr || in_scores == nullptr || out_ids == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || n_lists < 1 || k_in < 1 || k < 1 || k > n_lists * k_in)
+    return fail(UV_EINVAL, "bad sizes");
+  if (nq == 0) return UV_OK;
+  DeviceGuard g(device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const size_t nin = (size_t)nq * n_lists * k_in;
+  const int64_t *d_in_ids = nullptr;
+  const float *d_in_scores = nullptr;
+  UV_TRY(stage_in(in_ids, nin, device, sc, &d_in_ids));
+  UV_TRY(stage_in(in_scores, nin, device, sc, &d_in_scores));
+  int64_t *d_out_ids = nullptr;
+  float *d_out_scores = nullptr;
+  UV_TRY(outs.stage(out_ids, (size_t)nq * k, device, sc, &d_out_ids));
+  if (out_scores != nullptr) {
+    UV_TRY(outs.stage(out_scores, (size_t)nq * k, device, sc, &d_out_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_out_scores, (size_t)nq * k));
+  }
+  UV_TRY(merge_launch(nq, n_lists, k_in, k, nullptr, d_in_scores, d_in_ids, d_out_ids,
+                      d_out_scores, st));
+  return outs.finish(st);
+}
+
+}  // extern "C"

@@ -1,0 +1,440 @@
+// encode.cu -- batched free-start Viterbi trellis encoder for sm_100a.
+//
+// One team of T threads encodes one row at a time (persistent grid, teams
+// stride over rows).  Per row, fully on device:
+//   prep        unit row (or unit residual to its centroid), src/trellis.rs:1144-1160
+//   rotation    R x (sign flip, normalized FWHT), src/lib.rs:472-484
+//   standardize u_rs = u_r / max(std(u_r), EPS), src/trellis.rs:1172-1176
+//   forward     2^M-state add-compare-select over the dim steps,
+//               src/trellis.rs:1296-1332, 1688-1751, 1878-2001
+//   traceback   from the total_cmp argmin, src/trellis.rs:1783-1802
+//   finalize    rescale = sum code[w_i] * u_r[i] and MSB-first packing,
+//               src/trellis.rs:1009-1133, src/lib.rs:610-627
+//
+// Thread mapping of the trellis.  The window of state ns and candidate k is
+// w = ns + k*2^M, whose predecessor is s = w >> B = (ns >> B) + k*2^(M-B): the
+// 2^B states that share ns >> B (a "group") share their 2^B predecessors.  A
+// thread owns SPT consecutive states, i.e. whole groups (or a slice of one
+// group when 2^B > SPT), so every min over k is thread-local.  Its WPT =
+// SPT*2^B windows are fixed for the whole encode, so their table values live
+// in registers.  Path costs are exchanged through shared memory (ping-pong,
+// one team barrier per step) and each thread packs its SPT back-pointer k's
+// (B bits each) into 32-bit words: shared memory when the whole back-pointer
+// array fits, otherwise a per-team global scratch slot that the traceback
+// reads back in coalesced chunks.
+//
+// Tie rule (src/trellis.rs:1724-1750): the k = 0 candidate seeds the minimum,
+// later k replace it only when strictly smaller, so the smallest k (smallest
+// predecessor) wins an exact tie.  Every f32 op is a separately rounded
+// intrinsic, matching the reference bit for bit.
+#include "uv_kernels.h"
+#include "uv_team.cuh"
+
+namespace uvb {
+
+// Team-wide maximum of a 64-bit key.  `scratch` holds 32 u64 in shared memory
+// (only used when the team spans the CTA).
+__device__ __forceinline__ uint64_t team_max_u64(uint64_t v, const Team &tm,
+                                                 uint64_t *scratch) {
+  if (!tm.cta) {
+    for (int o = tm.T >> 1; o > 0; o >>= 1) {
+      uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = w > v ? w : v;
+    }
+    return v;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  uint64_t r = scratch[0];
+  for (int w = 1; w < (tm.T >> 5); w++) r = scratch[w] > r ? scratch[w] : r;
+  __syncthreads();
+  return r;
+}
+
+// Ordered key of a float for a first-maximum argmax (NaN never wins).
+__device__ __forceinline__ uint32_t max_key32(float f) {
+  if (f != f) f = -INFINITY;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int B, int WPT, bool BACK_SMEM>
+__global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
+  constexpr int NE = 1 << B;
+  constexpr int SPT = WPT / NE;                 // states per thread
+  constexpr int GPT = SPT >= NE ? SPT / NE : 1;  // groups per thread
+  constexpr int BPS = SPT * B;                  // back-pointer bits per thread per step
+  constexpr int SPW = 32 / BPS;                 // steps per 32-bit word
+  constexpr uint32_t EMASK = NE - 1;
+  static_assert(SPT >= 1 && BPS <= 32, "bad trellis tiling");
+
+  extern __shared__ __align__(16) float smem[];
+  const int T = p.T;
+  Team tm;
+  tm.T = T;
+  tm.cta = T > 32;
+  const int team = threadIdx.x / T;
+  tm.t = threadIdx.x - team * T;
+
+  float *ts = smem + (size_t)team * p.team_smem_words;
+  const int d = p.dim;
+  const int NS = p.n_states;
+  const int GS = NS >> B;
+  float *xbuf = ts;                                // row -> unit -> u_r
+  float *ubuf = ts + p.dim_pad;                    // u_rs, then windows
+  float *cost0 = ubuf + p.dim_pad;
+  float *cost1 = cost0 + NS;
+  float *misc = cost1 + NS;                        // 16 words
+  uint64_t *red = (uint64_t *)(misc + 16);         // 32 u64
+  uint32_t *backs = (uint32_t *)(misc + 80);       // back-pointers or a traceback chunk
+  uint32_t *misc_u = (uint32_t *)misc;
+
+  const int s0 = tm.t * SPT;
+  const int q0 = s0 >> B;
+
+  float creg[WPT];
+#pragma unroll
+  for (int j = 0; j < SPT; j++)
+#pragma unroll
+    for (int k = 0; k < NE; k++) creg[j * NE + k] = __ldg(p.code + s0 + j + k * NS);
+
+  const int64_t slot = (int64_t)blockIdx.x * p.teams_per_cta + team;
+  uint32_t *backg = BACK_SMEM ? nullptr : p.back_global + slot * p.back_words_team;
+  const int64_t team_stride = (int64_t)gridDim.x * p.teams_per_cta;
+  const int64_t iters = (p.n + team_stride - 1) / team_stride;
+  const bool aniso = p.lambda != 0.0f;
+  const uint32_t free_states = 1u << p.start_bits;
+
+  for (int64_t it = 0; it < iters; it++) {
+    const int64_t v = slot + it * team_stride;
+    const bool valid = v < p.n;
+    const int64_t vv = valid ? v : p.n - 1;
+
+    // ---- prep: load, normalize, center, rotate, standardize ----
+    const float *row = p.rows + vv * (int64_t)d;
+    for (int i = tm.t; i < d; i += T) xbuf[i] = row[i];
+    tm.sync();
+    if (!p.rotated_input) {
+      if (tm.leader()) {
+        float l2 = fsqrt(seq_sum_sq(xbuf, d));
+        misc[0] = l2;
+        misc[1] = fmax_rs(l2, kF32Eps);
+        misc[2] = 1.0f;
+        misc_u[4] = 0u;
+      }
+      tm.sync();
+      const float nrm = misc[1];
+      for (int i = tm.t; i < d; i += T) xbuf[i] = fdiv(xbuf[i], nrm);
+      tm.sync();
+      const float *cen = nullptr;
+      if (p.list_centroids != nullptr) {
+        cen = p.list_centroids + (size_t)p.row_list[vv] * d;
+      } else if (p.n_centroids > 0) {
+        // assign (src/trellis.rs:993-1004): first strict maximum of <u, c_j>
+        uint64_t best = 0;
+        for (int j = tm.t; j < p.n_centroids; j += T) {
+          float dj = seq_dot(xbuf, p.centroids + (size_t)j * d, d);
+          uint64_t key = ((uint64_t)max_key32(dj) << 32) | (uint32_t)(~(uint32_t)j);
+          best = key > best ? key : best;
+        }
+        best = team_max_u64(best, tm, red);
+        uint32_t j = ~(uint32_t)(best & 0xffffffffu);
+        // every dot NaN or -inf: the reference keeps index 0
+        if ((uint32_t)(best >> 32) <= max_key32(-INFINITY)) j = 0;
+        if (tm.leader()) misc_u[4] = j;
+        cen = p.centroids + (size_t)j * d;
+      }
+      if (cen != nullptr) {
+        for (int i = tm.t; i < d; i += T) xbuf[i] = fsub(xbuf[i], cen[i]);
+        tm.sync();
+        if (tm.leader()) misc[2] = fmax_rs(fsqrt(seq_sum_sq(xbuf, d)), kF32Eps);
+        tm.sync();
+        const float rn = misc[2];
+        for (int i = tm.t; i < d; i += T) xbuf[i] = fdiv(xbuf[i], rn);
+        tm.sync();
+      }
+      team_rotate(xbuf, p.rot, tm, false);
+    }
+    if (tm.leader()) misc[3] = fmax_rs(seq_std_about_mean(xbuf, d), kF32Eps);
+    tm.sync();
+    const float scale = misc[3];
+    for (int i = tm.t; i < d; i += T) ubuf[i] = fdiv(xbuf[i], scale);
+    for (int s = tm.t; s < NS; s += T) cost0[s] = ((uint32_t)s < free_states) ? 0.0f : INFINITY;
+    tm.sync();
+
+    // ---- forward: add-compare-select over d steps ----
+    float *cur = cost0, *nxt = cost1;
+    float last[SPT];
+    uint32_t word = 0;
+    for (int step = 0; step < d; step++) {
+      const float xi = ubuf[step];
+      const float wi = aniso ? fadd(1.0f, fmul(fmul(p.lambda, xi), xi)) : 1.0f;
+      float cp[GPT][NE];
+#pragma unroll
+      for (int g = 0; g < GPT; g++)
+#pragma unroll
+        for (int k = 0; k < NE; k++) cp[g][k] = cur[q0 + g + k * GS];
+      const int slot_bits = (step % SPW) * BPS;
+#pragma unroll
+      for (int j = 0; j < SPT; j++) {
+        const int g = (SPT >= NE) ? j / NE : 0;
+        float best = 0.0f;
+        uint32_t bk = 0;
+#pragma unroll
+        for (int k = 0; k < NE; k++) {
+          const float dd = fsub(xi, creg[j * NE + k]);
+          const float m = aniso ? fmul(fmul(wi, dd), dd) : fmul(dd, dd);
+          const float c = fadd(cp[g][k], m);
+          if (k == 0) {
+            best = c;
+          } else if (c < best) {
+            best = c;
+            bk = (uint32_t)k;
+          }
+        }
+        nxt[s0 + j] = best;
+        last[j] = best;
+        word |= bk << (slot_bits + j * B);
+      }
+      if ((step % SPW) == SPW - 1 || step == d - 1) {
+        const int widx = (step / SPW) * T + tm.t;
+        if (BACK_SMEM)
+          backs[widx] = word;
+        else
+          backg[widx] = word;
+        word = 0;
+      }
+      float *tmp = cur;
+      cur = nxt;
+      nxt = tmp;
+      tm.sync();
+    }
+
+    // ---- argmin under total_cmp, first index on ties ----
+    uint64_t bkey = 0;
+#pragma unroll
+    for (int j = 0; j < SPT; j++) {
+      uint32_t k32 = (uint32_t)total_key(last[j]) ^ 0x80000000u;
+      uint64_t key = ((uint64_t)(~k32) << 32) | (uint32_t)(~(uint32_t)(s0 + j));
+      bkey = key > bkey ? key : bkey;
+    }
+    bkey = team_max_u64(bkey, tm, red);
+    uint32_t s = ~(uint32_t)(bkey & 0xffffffffu);
+
+    // ---- traceback: windows w_i into ubuf ----
+    uint32_t *wv = (uint32_t *)ubuf;
+    if (BACK_SMEM) {
+      if (tm.leader()) {
+        for (int step = d - 1; step >= 0; step--) {
+          const uint32_t wd = backs[(step / SPW) * T + (int)(s / SPT)];
+          const uint32_t k = (wd >> ((step % SPW) * BPS + (int)(s % SPT) * B)) & EMASK;
+          const uint32_t w = s + k * (uint32_t)NS;
+          wv[step] = w;
+          s = w >> B;
+        }
+        misc_u[5] = s;
+      }
+    } else {
+      constexpr int CH = 64;  // steps per traceback chunk (a multiple of SPW)
+      const int nch = (d + CH - 1) / CH;
+      for (int c = nch - 1; c >= 0; c--) {
+        const int lo = c * CH, hi = min(d, lo + CH);
+        const int wlo = (lo / SPW) * T, whi = ((hi - 1) / SPW + 1) * T;
+        for (int i = wlo + tm.t; i < whi; i += T) backs[i - wlo] = backg[i];
+        tm.sync();
+        if (tm.leader()) {
+          for (int step = hi - 1; step >= lo; step--) {
+            const uint32_t wd = backs[(step / SPW) * T - wlo + (int)(s / SPT)];
+            const uint32_t k = (wd >> ((step % SPW) * BPS + (int)(s % SPT) * B)) & EMASK;
+            const uint32_t w = s + k * (uint32_t)NS;
+            wv[step] = w;
+            s = w >> B;
+          }
+          misc_u[5] = s;
+        }
+        tm.sync();
+      }
+    }
+    tm.sync();
+
+    // ---- finalize: rescale (leader, sequential) and packing (team) ----
+    if (tm.leader()) {
+      float rs = 0.0f;
+      for (int i = 0; i < d; i++) rs = fadd(rs, fmul(__ldg(p.code + wv[i]), xbuf[i]));
+      if (p.rescale_bits > 0 && rs > 1e-6f) {
+        const float levels = (float)((1u << p.rescale_bits) - 1u);
+        const float sq = fsqrt((float)d);
+        const float lo = fmul(0.0f, sq), hi = fmul(1.25f, sq);
+        float t = fdiv(fsub(rs, lo), fsub(hi, lo));
+        t = t < 0.0f ? 0.0f : (t > 1.0f ? 1.0f : t);
+        rs = fadd(lo, fmul(fdiv(roundf(fmul(t, levels)), levels), fsub(hi, lo)));
+      }
+      misc[6] = rs > 1e-6f ? rs : INFINITY;
+    }
+    if (valid && p.codes != nullptr) {
+      uint8_t *out = p.codes + vv * (int64_t)p.code_stride;
+      const int nbits = d * B;
+      for (int bi = tm.t; bi < p.code_stride; bi += T) {
+        uint32_t val = 0;
+        if (bi < p.code_bytes) {
+#pragma unroll
+          for (int bit = 0; bit < 8; bit++) {
+            const int pos = bi * 8 + bit;
+            if (pos < nbits) {
+              const int i = pos / B;
+              const int off = B - 1 - (pos - i * B);
+              val |= ((wv[i] >> off) & 1u) << (7 - bit);
+            }
+          }
+        }
+        out[bi] = (uint8_t)val;
+      }
+    }
+    tm.sync();
+    if (valid && tm.leader()) {
+      if (p.start) p.start[vv] = misc_u[5];
+      if (p.rescale) p.rescale[vv] = misc[6];
+      if (p.rnorm) p.rnorm[vv] = p.rotated_input ? 1.0f : misc[2];
+      if (p.cidx) p.cidx[vv] = p.rotated_input ? 0u : misc_u[4];
+      if (p.norms) p.norms[vv] = p.rotated_input ? 0.0f : misc[0];
+    }
+    tm.sync();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host-side launch planning.
+// ---------------------------------------------------------------------------
+namespace {
+
+template <int B, int WPT, bool SM>
+const void *kernel_ptr() {
+  return (const void *)encode_kernel<B, WPT, SM>;
+}
+
+const void *pick_kernel(int B, int WPT, bool smem_back) {
+#define UV_CASE(b, w)                                                           \
+  if (B == b && WPT == w) return smem_back ? kernel_ptr<b, w, true>() : kernel_ptr<b, w, false>();
+  UV_CASE(1, 4)
+  UV_CASE(1, 8)
+  UV_CASE(1, 16)
+  UV_CASE(1, 32)
+  UV_CASE(2, 16)
+  UV_CASE(2, 32)
+  UV_CASE(3, 32)
+  UV_CASE(4, 32)
+#undef UV_CASE
+  return nullptr;
+}
+
+}  // namespace
+
+int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) {
+  if (bits < 1 || bits > 4) {
+    *why = "bits must be 1..4";
+    return 1;
+  }
+  if (mem < bits) {
+    *why = "mem < bits takes the reference's general Viterbi pass, not built for the GPU";
+    return 2;
+  }
+  const int64_t nw = (int64_t)1 << (mem + bits);
+  const int wpt = nw >= 32 ? 32 : (int)nw;
+  const int64_t T = nw / wpt;
+  if (T > 512) {
+    *why = "2^(mem+bits) > 16384 windows needs the multi-CTA encoder (not built yet)";
+    return 2;
+  }
+  const int spt = wpt >> bits;
+  const int bps = spt * bits;
+  const int spw = 32 / bps;
+  plan->B = bits;
+  plan->WPT = wpt;
+  plan->T = (int)T;
+  plan->n_states = 1 << mem;
+  plan->dim_pad = (dim + 3) & ~3;
+  const int64_t back_words = (int64_t)((dim + spw - 1) / spw) * T;
+  const int64_t chunk_words = (int64_t)((64 + spw - 1) / spw + 1) * T;
+  const int64_t base_words = 2 * (int64_t)plan->dim_pad + 2 * (int64_t)plan->n_states + 80;
+  plan->back_words_team = back_words;
+  // Shared-memory back-pointers when at least 8 warps per SM still fit.
+  const int64_t budget = 200 * 1024;
+  int tpc_warp = T >= 32 ? 1 : (int)(32 / T);  // teams per warp
+  int tpc = T >= 32 ? 1 : tpc_warp * (256 / 32);
+  auto fits = [&](int64_t team_words, int teams) { return team_words * 4 * teams <= budget; };
+  int64_t team_words_smem = (base_words + back_words + 3) & ~3LL;
+  int64_t team_words_glob = (base_words + chunk_words + 3) & ~3LL;
+  bool smem = false;
+  int teams = tpc;
+  // largest team count (whole warps) that fits
+  for (int tc = tpc; tc >= tpc_warp && tc >= 1; tc -= tpc_warp) {
+    if (fits(team_words_smem, tc)) {
+      const int64_t cta_bytes = team_words_smem * 4 * tc;
+      const int threads = (int)(tc * T);
+      const int ctas = (int)std::min<int64_t>(228 * 1024 / std::max<int64_t>(cta_bytes, 1), 2048 / threads);
+      if ((int64_t)ctas * threads >= 256) {
+        smem = true;
+        teams = tc;
+      }
+      break;
+    }
+  }
+  if (!smem) {
+    teams = tpc;
+    while (teams > tpc_warp && !fits(team_words_glob, teams)) teams -= tpc_warp;
+    if (!fits(team_words_glob, teams)) {
+      *why = "encode working set exceeds shared memory";
+      return 2;
+    }
+  }
+  plan->back_smem = smem;
+  plan->teams_per_cta = teams;
+  plan->threads = teams * (int)T;
+  plan->team_smem_words = (int)(smem ? team_words_smem : team_words_glob);
+  plan->smem_bytes = (size_t)plan->team_smem_words * 4 * teams;
+  plan->kernel = pick_kernel(bits, wpt, smem);
+  if (plan->kernel == nullptr) {
+    *why = "no encoder instantiation for this (bits, window) shape";
+    return 2;
+  }
+  return 0;
+}
+
+cudaError_t encode_launch(const EncodePlan &plan, EncodeParams p, int grid, cudaStream_t st) {
+  p.T = plan.T;
+  p.teams_per_cta = plan.teams_per_cta;
+  p.team_smem_words = plan.team_smem_words;
+  p.n_states = plan.n_states;
+  p.dim_pad = plan.dim_pad;
+  p.back_words_team = plan.back_words_team;
+  cudaError_t e = cudaFuncSetAttribute(plan.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)plan.smem_bytes);
+  if (e != cudaSuccess) return e;
+  void *args[] = {&p};
+  return cudaLaunchKernel(plan.kernel, dim3(grid), dim3(plan.threads), args, plan.smem_bytes, st);
+}
+
+cudaError_t encode_grid(const EncodePlan &plan, int64_t n, int *grid) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(plan.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)plan.smem_bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan.kernel, plan.threads,
+                                                    plan.smem_bytes);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t need = (n + plan.teams_per_cta - 1) / plan.teams_per_cta;
+  *grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sms * per_sm));
+  return cudaSuccess;
+}
+
+}  // namespace uvb

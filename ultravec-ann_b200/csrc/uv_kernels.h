@@ -1,0 +1,106 @@
+// uv_kernels.h -- launch interface between the C ABI (capi.cpp) and the
+// CUDA kernels (encode.cu, scan.cu, ivf.cu).  Internal; not installed.
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <algorithm>
+#include <cuda_runtime.h>
+
+#include "uv_common.cuh"
+
+namespace uvb {
+
+struct EncodeParams {
+  int dim, dim_pad, n_states, T, teams_per_cta, team_smem_words;
+  int64_t n;
+  const float *rows;        // n x dim
+  const float *code;        // 2^(mem+bits) table
+  RotParams rot;
+  float lambda;
+  int start_bits, rescale_bits;
+  const float *centroids;   // flat centering (assign among n_centroids)
+  int n_centroids;
+  const float *list_centroids;  // IVF centering: row i uses list_centroids[row_list[i]]
+  const uint32_t *row_list;
+  uint8_t *codes;           // n x code_stride
+  int code_stride, code_bytes;
+  uint32_t *start;
+  float *rescale, *rnorm;
+  uint32_t *cidx;
+  float *norms;             // exact l2 norm of the raw row (MIPS sidecar)
+  int rotated_input;        // rows are already rotated units (encode_rotated)
+  uint32_t *back_global;    // per-team back-pointer slots (global mode)
+  int64_t back_words_team;
+};
+
+struct EncodePlan {
+  int B, WPT, T, n_states, dim_pad, teams_per_cta, threads, team_smem_words;
+  bool back_smem;
+  int64_t back_words_team;
+  size_t smem_bytes;
+  const void *kernel;
+};
+
+// 0 ok, 1 invalid, 2 unsupported (message in *why)
+int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
+cudaError_t encode_grid(const EncodePlan &plan, int64_t n, int *grid);
+cudaError_t encode_launch(const EncodePlan &plan, EncodeParams p, int grid, cudaStream_t st);
+
+struct PrepParams {
+  int dim, dim_pad;
+  int64_t nq;
+  const float *queries;  // nq x dim
+  RotParams rot;
+  const float *centroids;
+  int n_centroids;
+  float *q_r;            // nq x dim_pad
+  float *qc;             // nq x n_centroids
+  uint32_t *degenerate;  // nq
+};
+
+struct ScanParams {
+  int dim, mem, bits;
+  int64_t nq, n;
+  const float *q_r;   // nq x q_stride
+  int q_stride;
+  const float *qc;    // nq x n_centroids
+  int n_centroids;
+  const uint32_t *degenerate;
+  const uint8_t *codes;  // n x code_stride
+  int code_stride;
+  const uint32_t *start;
+  const float *rescale, *rnorm, *norms;
+  const uint32_t *cidx;
+  const float *code;  // table
+  int table_len, table_in_smem;
+  int img_words;
+  int mips, k;
+  const int64_t *ids;  // record -> id (may be null: id_base + record)
+  int64_t id_base;
+  uint32_t *part_key;  // nq x splits x k
+  int64_t *part_id;
+};
+
+struct MergeParams {
+  int64_t nq;
+  int n_lists, k_in, k, pow2, warps;
+  const uint32_t *in_key;  // or null
+  const float *in_score;   // or null
+  const int64_t *in_id;
+  int64_t *out_id;
+  float *out_score;
+};
+
+__global__ void prep_queries_kernel(const PrepParams p);
+__global__ void flat_scan_kernel(const ScanParams p);
+__global__ void merge_topk_kernel(const MergeParams p);
+
+// scan tiling constants shared with the host planner
+constexpr int kScanTQ = 32;
+constexpr int kScanTN = 32;
+constexpr int kScanKCap = 128;
+
+size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem);
+
+}  // namespace uvb
