@@ -1,0 +1,422 @@
+#!/usr/bin/env python3
+"""Benchmark of the two trellis hot paths on B200: encode and codes-only scan.
+
+Workload (N=1 default): the 1,000,000-row x 10,000-query flat MIPS scan at
+d=128 -- non-negative heavy-tailed integer rows (about 40% zeros, the rest
+geometric with mean 20, clipped at 255) cast to f32 and mean-centered by the
+base mean, 2 bits per coordinate, trellis memory M=8, top-100 (top-10 is also
+reported).  Seeded synthetic data stand in for the public corpora.
+
+One step = one pass of both hot paths over the resident inputs:
+  encode   every base row -> codes-only trellis records (the index build),
+  scan     every query against every record, per-query top-100 by MIPS score.
+`value` is queries/s of the scan phase; `encode.value` is rows/s of the
+encode phase; `ms_per_step` covers both.  With N GPUs the base is sharded in
+contiguous row ranges (strong scaling: same 1M x 10k job), every rank scans
+its shard for all queries, and the per-rank top-k lists meet in one NCCL
+all-gather plus a device merge.
+
+`--impl reference` times the CPU restatement of the reference algorithm
+(oracle/, OpenMP over queries, all host threads) on a bounded sample of the
+same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+DIM, BITS, MEM = 128, 2, 8
+N_BASE, N_QUERY = 1_000_000, 10_000
+K_MAIN, K_ALT = 100, 10
+FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n-base", type=int, default=N_BASE)
+    ap.add_argument("--n-query", type=int, default=N_QUERY)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ data ---
+
+def make_data(n_base: int, n_query: int, seed: int = 0):
+    """Heavy-tailed integer rows in [0, 255]: P(0) = 0.4, else geometric(1/20)
+    clipped at 255; base mean (f64) subtracted from base and queries in f32."""
+    rng = np.random.default_rng(seed)
+    out = np.empty((n_base + n_query, DIM), np.float32)
+    step = 131072
+    for a in range(0, n_base + n_query, step):
+        b = min(a + step, n_base + n_query)
+        zero = rng.random((b - a, DIM)) < 0.4
+        geo = np.minimum(rng.geometric(1.0 / 20.0, (b - a, DIM)), 255)
+        out[a:b] = np.where(zero, 0, geo).astype(np.float32)
+    base, query = out[:n_base], out[n_base:]
+    mean = base.mean(axis=0, dtype=np.float64).astype(np.float32)
+    base -= mean
+    query -= mean
+    return base, query
+
+
+# ---------------------------------------------------------------- clocks ---
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = REPO / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        smax = max(r[1] for r in rows)
+        load = [r for r in rows if r[0] > 0.5 * smax] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2][1:5])
+                          if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------- reference ---
+
+def run_reference(args, rank: int):
+    """CPU restatement of the reference path (oracle/), all host threads."""
+    if rank != 0:
+        return
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O
+
+    threads = O.threads_available()
+    base, query = make_data(args.n_base, args.n_query)
+    codec = O.Codec(DIM, BITS, MEM)
+    t0 = time.time()
+    index = codec.encode_batch(base, threads=threads)
+    build_s = time.time() - t0
+    norms = O.l2_norms(base, threads=threads)
+    sample_q = max(threads, 16)
+    times = []
+    for step in range(args.warmup + args.steps):
+        qs = query[(step * sample_q) % len(query):][:sample_q]
+        t = time.perf_counter()
+        codec.search_topk(index, qs, K_MAIN, norms=norms, threads=threads)
+        dt = time.perf_counter() - t
+        if step >= args.warmup:
+            times.append(dt)
+    qps = sample_q * len(times) / sum(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args),
+        "encode": {"value": args.n_base / build_s, "unit": "rows/s",
+                   "note": "one untimed-by-steps build of the full base"},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample_q} queries x {args.n_base} records per step"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ ours ---
+
+METRIC = "flat codes-only MIPS queries/s and encode vectors/s at 1/2/4/8 B200; % HBM roofline"
+
+
+def config_dict(args):
+    return {"workload": "flat-mips-1Mx10k-d128", "n_base": args.n_base, "n_query": args.n_query,
+            "dim": DIM, "bits": BITS, "mem": MEM, "k": K_MAIN, "metric_space": "mips",
+            "parallelism": f"shard{args.gpus}", "l2": "flushed between steps (256 MiB write); "
+            "base rows 512 MB > L2"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from ultravec_ann_b200_loader import load
+
+    uv = load()
+    dev = torch.device("cuda", local)
+
+    base_np, query_np = make_data(args.n_base, args.n_query)
+    lo, hi = rank * args.n_base // world, (rank + 1) * args.n_base // world
+    shard = torch.from_numpy(base_np[lo:hi]).to(dev)
+    ids = torch.arange(lo, hi, dtype=torch.int64, device=dev)
+    queries = torch.from_numpy(query_np).to(dev)
+    nq = queries.shape[0]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    codec = uv.Codec(DIM, BITS, MEM, device=local)
+    index = uv.Index(codec)
+    index.reserve(hi - lo)
+
+    def scan(k):
+        out_ids, out_scores = index.search(queries, k, mips=True)
+        if world > 1:
+            g_ids = torch.empty((world,) + tuple(out_ids.shape), dtype=torch.int64, device=dev)
+            g_sc = torch.empty((world,) + tuple(out_scores.shape), dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(g_ids, out_ids)
+            dist.all_gather_into_tensor(g_sc, out_scores)
+            out_ids, out_scores = uv.topk_merge(g_ids.permute(1, 0, 2).contiguous(),
+                                                g_sc.permute(1, 0, 2).contiguous(), k,
+                                                device=local)
+        return out_ids, out_scores
+
+    def step(ev=None):
+        index.clear()
+        if ev:
+            ev[0].record()
+        index.add(ids, shard)
+        if ev:
+            ev[1].record()
+        res = scan(K_MAIN)
+        if ev:
+            ev[2].record()
+        return res
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    uv.profile_enable(True)
+    enc_ms, scan_ms = [], []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        step(ev)
+        torch.cuda.synchronize()
+        enc_ms.append(ev[0].elapsed_time(ev[1]))
+        scan_ms.append(ev[1].elapsed_time(ev[2]))
+    barrier()
+    kern = {name: uv.profile_read(name) for name in ("encode", "flat_scan", "prep_queries",
+                                                     "merge_topk")}
+    launches_total = uv.profile_read("*")[1]
+    uv.profile_enable(False)
+    clk = clocks.stop() if clocks else None
+
+    # top-10 throughput (same index), timed the same way
+    k10_ms = []
+    for _ in range(max(2, args.steps // 2)):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        scan(K_ALT)
+        e1.record()
+        torch.cuda.synchronize()
+        k10_ms.append(e0.elapsed_time(e1))
+
+    tot = torch.tensor([sum(enc_ms), sum(scan_ms), sum(k10_ms)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    enc_tot, scan_tot, k10_tot = tot.tolist()
+
+    # End to end through the public API: pinned host queries in, host results
+    # out.  At N=1 the host buffers go straight into uv_index_search (the
+    # library stages them); with N ranks each rank copies its queries up, scans
+    # its shard, and the merged top-k is read back to the host.
+    e2e = None
+    if not args.no_e2e:
+        q_host = torch.from_numpy(query_np).pin_memory()
+        e_ms = []
+        h2d = d2h = 0
+        for s_i in range(args.warmup + max(2, args.steps // 2)):
+            barrier()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            if world == 1:
+                h_ids, h_sc = index.search(q_host, K_MAIN, mips=True)
+            else:
+                out_ids, out_scores = index.search(q_host.to(dev, non_blocking=True), K_MAIN,
+                                                   mips=True)
+                g_ids = torch.empty((world,) + tuple(out_ids.shape), dtype=torch.int64, device=dev)
+                g_sc = torch.empty((world,) + tuple(out_scores.shape), dtype=torch.float32,
+                                   device=dev)
+                dist.all_gather_into_tensor(g_ids, out_ids)
+                dist.all_gather_into_tensor(g_sc, out_scores)
+                out_ids, out_scores = uv.topk_merge(g_ids.permute(1, 0, 2).contiguous(),
+                                                    g_sc.permute(1, 0, 2).contiguous(), K_MAIN,
+                                                    device=local)
+                h_ids, h_sc = out_ids.cpu(), out_scores.cpu()
+            t1.record()
+            torch.cuda.synchronize()
+            if s_i >= args.warmup:
+                e_ms.append(t0.elapsed_time(t1))
+            h2d = int(q_host.numel() * 4)
+            d2h = int(h_ids.size * 8 + h_sc.size * 4) if world == 1 else \
+                int(h_ids.numel() * 8 + h_sc.numel() * 4)
+        et = torch.tensor([sum(e_ms)], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": nq * len(e_ms) / (et.item() / 1e3), "unit": "queries/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "uv_index_search with host buffers" if world == 1 else
+                      "uv_index_search + NCCL all-gather + uv_topk_merge, host copies"}
+
+    # CPU baseline: the oracle on a bounded sample, rank 0 at N=1
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(index, base_np, query_np, codec)
+
+    if rank == 0:
+        qps = nq * args.steps / (scan_tot / 1e3)
+        rows_s = args.n_base * args.steps / (enc_tot / 1e3)
+        scan_k_ms, scan_k_n = kern["flat_scan"]
+        avg_scan = scan_k_ms / max(scan_k_n, 1)
+        n_local = hi - lo
+        flops = 2.0 * nq * n_local * DIM
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        peaks = load_peaks()
+        smax = peaks.get("sm_max_mhz", 1965.0)
+        fp32_peak = sms * FP32_LANES_PER_SM * 2 * smax * 1e6 / 1e12
+        achieved = flops / (avg_scan / 1e3) / 1e12
+        rec_bytes = 32 + 1 + 4 + 4
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        line = {
+            "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": (enc_tot + scan_tot) / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args),
+            "encode": {"value": rows_s, "unit": "rows/s", "ms_per_step": enc_tot / args.steps},
+            "scan_ms_per_step": scan_tot / args.steps,
+            "top10": {"value": nq * len(k10_ms) / (k10_tot / 1e3), "unit": "queries/s"},
+            "roofline": {
+                "bound": "fp32", "kernel": "flat_scan_kernel", "achieved": achieved,
+                "peak": fp32_peak, "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                "traffic": None,
+                "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA/clk x 2 x "
+                               f"{smax:.0f} MHz (sm_max_mhz of MEASURED_PEAKS.json)",
+                "flops_per_launch": flops, "avg_launch_ms": avg_scan,
+                "hbm_model": {"bytes_per_query": n_local * rec_bytes,
+                              "gbs": qps / world * n_local * rec_bytes / 1e9,
+                              "peak_gbs": hbm,
+                              "frac": qps / world * n_local * rec_bytes / 1e9 / hbm,
+                              "note": "streaming model (every query re-reads its shard); >1 "
+                                      "means on-chip reuse across the query tile"},
+            },
+            "kernels_ms": {k: v[0] / max(v[1], 1) for k, v in kern.items()},
+            "gpu_launches": launches_total,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def load_peaks():
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+def cpu_baseline(index, base_np, query_np, codec):
+    """The oracle (C restatement of the reference CPU path) on a bounded
+    sample: scan of a few queries over the full index, all host threads."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O
+
+    threads = O.threads_available()
+    ex = index.export()
+    rec = {"codes": ex["codes"], "start": ex["start"], "rescale": ex["rescale"]}
+    oc = O.Codec(DIM, BITS, MEM)
+    sample = max(16, threads)
+    qs = query_np[:sample]
+    oc.search_topk(rec, qs[:threads], K_MAIN, norms=ex["norms"], threads=threads)  # warm
+    t = time.perf_counter()
+    oc.search_topk(rec, qs, K_MAIN, norms=ex["norms"], threads=threads)
+    dt = time.perf_counter() - t
+    enc_rows = 8192
+    t = time.perf_counter()
+    oc.encode_batch(base_np[:enc_rows], threads=threads)
+    de = time.perf_counter() - t
+    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} queries x {len(ex['start'])} records (scan); encode {enc_rows} "
+                      f"rows",
+            "encode_rows_s": enc_rows / de}
+
+
+if __name__ == "__main__":
+    main()

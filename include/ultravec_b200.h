@@ -152,12 +152,25 @@ int uv_index_export(const uv_index *index, uint8_t *codes, uint32_t *start, floa
 /* encode_digest of the stored records. */
 int uv_index_digest(const uv_index *index, uint64_t *digest, void *stream);
 
+/* Drop every record but keep the device capacity: the state of a freshly
+ * constructed codec after reserve(len) (src/trellis.rs:2100-2102). */
+int uv_index_clear(uv_index *index);
+
 /* Merge per-shard top-k lists (the multi-GPU combine after an all-gather):
  * in_ids/in_scores are nq x n_lists x k_in, each list sorted by the ranking
  * above; out is nq x k.  Device or host memory. */
 int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream);
+
+/* Measurement aid, no counterpart in the reference: while enabled, every
+ * kernel the library launches is bracketed by CUDA events on its launch
+ * stream.  uv_profile_read waits for those events and returns the summed
+ * device time and launch count of one kernel family ("encode",
+ * "prep_queries", "flat_scan", "merge_topk", or "*" for all).  Enabling
+ * clears previous records.  Not for concurrent use. */
+int uv_profile_enable(int32_t on);
+int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,7 @@ def lib():
             "uvo_inv_norm_cdf": (C.c_double, [C.c_double]),
             "uvo_gaussian_code": (C.c_float, [C.c_uint32]),
             "uvo_l2_norm": (C.c_float, [_f32p, C.c_int]),
+            "uvo_l2_norms": (None, [_f32p, C.c_int64, C.c_int, _f32p, C.c_int]),
             "uvo_std_about_mean": (C.c_float, [_f32p, C.c_int]),
             "uvo_fwht": (None, [_f32p, C.c_int]),
             "uvo_pack_indices": (C.c_int, [_u16p, C.c_int, C.c_int, _u8p]),
@@ -266,9 +267,12 @@ def l2_norm(v):
     return float(lib().uvo_l2_norm(np.ascontiguousarray(v, np.float32), len(v)))
 
 
-def l2_norms(rows):
+def l2_norms(rows, threads=0):
+    """bench.rs:1019: exact l2 norm of every row (the MIPS sidecar)."""
     rows = np.ascontiguousarray(rows, np.float32)
-    return np.array([l2_norm(r) for r in rows], np.float32)
+    out = np.empty(rows.shape[0], np.float32)
+    lib().uvo_l2_norms(rows, rows.shape[0], rows.shape[1], out, threads)
+    return out
 
 
 def std_about_mean(v):

@@ -1105,3 +1105,12 @@ void uvo_ivf_search_topk(const uvo_codec *c, const float *centroids, int nlist,
         free(h);
     }
 }
+
+/* bench.rs:1019 norms[i] = l2_norm(db[i]) over a batch */
+void uvo_l2_norms(const float *rows, int64_t n, int dim, float *out, int threads) {
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(threads)
+#endif
+    for (int64_t i = 0; i < n; i++) out[i] = uvo_l2_norm(rows + (size_t)i * dim, dim);
+}

@@ -27,6 +27,7 @@ float uvo_gaussian_code(uint32_t w);
 uint64_t uvo_splitmix64(uint64_t *state);
 double uvo_next_f64(uint64_t *state);
 float uvo_l2_norm(const float *v, int n);
+void uvo_l2_norms(const float *rows, int64_t n, int dim, float *out, int threads);
 float uvo_std_about_mean(const float *v, int n);
 void uvo_fwht(float *buf, int n);
 int uvo_pack_indices(const uint16_t *idx, int n, int bits, uint8_t *out);

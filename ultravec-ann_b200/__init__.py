@@ -6,4 +6,5 @@ as `ultravec_ann_b200` by `load()` in ultravec_ann_b200_loader.py (repo root)
 or by any importer that points importlib at this directory.
 """
 from .binding import (Codec, Index, UVError, build, check, lib, topk_merge,  # noqa: F401
+                      profile_enable, profile_read,
                       UV_SEARCH_COSINE, UV_SEARCH_MIPS, SYMBOLS)

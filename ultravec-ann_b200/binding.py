@@ -29,7 +29,8 @@ SYMBOLS = [
     "uv_rotate", "uv_decode", "uv_windows", "uv_digest", "uv_index_create", "uv_index_destroy",
     "uv_index_set_centroids", "uv_index_reserve", "uv_index_add", "uv_index_add_batch",
     "uv_index_len", "uv_index_dimensions", "uv_index_mem_bytes", "uv_index_search",
-    "uv_index_export", "uv_index_digest", "uv_topk_merge",
+    "uv_index_export", "uv_index_digest", "uv_index_clear", "uv_topk_merge",
+    "uv_profile_enable", "uv_profile_read",
 ]
 
 
@@ -88,6 +89,9 @@ def lib():
             "uv_index_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp]),
             "uv_index_digest": (C.c_int, [vp, C.POINTER(u64), vp]),
             "uv_topk_merge": (C.c_int, [i32, vp, vp, i64, i32, i32, i32, vp, vp, vp]),
+            "uv_index_clear": (C.c_int, [vp]),
+            "uv_profile_enable": (C.c_int, [i32]),
+            "uv_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(i64)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -284,6 +288,9 @@ class Index:
         cen = _f32(centroids)
         check(lib().uv_index_set_centroids(self.h, _ptr(cen), cen.shape[0]))
 
+    def clear(self):
+        check(lib().uv_index_clear(self.h))
+
     def reserve(self, additional: int):
         check(lib().uv_index_reserve(self.h, additional))
 
@@ -342,6 +349,17 @@ def topk_merge(in_ids, in_scores, k: int, device: int = 0):
     check(lib().uv_topk_merge(device, _ptr(in_ids), _ptr(in_scores), nq, n_lists, k_in, k,
                               _ptr(ids), _ptr(scores), _stream(in_ids)))
     return ids, scores
+
+
+def profile_enable(on: bool = True):
+    check(lib().uv_profile_enable(1 if on else 0))
+
+
+def profile_read(kernel: str = "*"):
+    """(total device ms, launches) of one kernel family since profile_enable."""
+    ms, n = C.c_double(), C.c_int64()
+    check(lib().uv_profile_read(kernel.encode(), C.byref(ms), C.byref(n)))
+    return ms.value, n.value
 
 
 def build(verbose: bool = False) -> Path:

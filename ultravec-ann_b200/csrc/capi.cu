@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -136,6 +137,35 @@ struct Outputs {
     for (auto &p : pend) UV_CK(cudaMemcpyAsync(p.host, p.dev, p.bytes, cudaMemcpyDeviceToHost, st));
     if (!pend.empty()) UV_CK(cudaStreamSynchronize(st));
     return UV_OK;
+  }
+};
+
+// ---- kernel timing hook (uv_profile_enable / uv_profile_read) ----
+struct ProfRec {
+  const char *name;
+  cudaEvent_t a, b;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRec> g_prof;
+
+struct ProfScope {
+  const char *name;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(const char *n, cudaStream_t s) : name(n), st(s) {
+    if (!g_prof_on) return;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      a = b = nullptr;
+      return;
+    }
+    cudaEventRecord(a, st);
+  }
+  ~ProfScope() {
+    if (a == nullptr) return;
+    cudaEventRecord(b, st);
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof.push_back({name, a, b});
   }
 };
 
@@ -334,7 +364,10 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
     const size_t words = (size_t)grid * c->plan.teams_per_cta * (size_t)c->plan.back_words_team;
     UV_TRY(sc.alloc(&p.back_global, words));
   }
-  UV_CK(uvb::encode_launch(c->plan, p, grid, st));
+  {
+    ProfScope ps("encode", st);
+    UV_CK(uvb::encode_launch(c->plan, p, grid, st));
+  }
   UV_CK(cudaGetLastError());
   return UV_OK;
 }
@@ -546,6 +579,12 @@ static int index_ensure(uv_index *ix, int64_t need, cudaStream_t st) {
   return UV_OK;
 }
 
+int uv_index_clear(uv_index *ix) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  ix->n = 0;
+  return UV_OK;
+}
+
 int uv_index_reserve(uv_index *ix, int64_t additional) {
   if (ix == nullptr || additional < 0) return fail(UV_EINVAL, "bad argument");
   DeviceGuard g(ix->codec->cfg.device);
@@ -701,6 +740,7 @@ int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_ke
                              (int)smem));
   const int grid = (int)((nq + m.warps - 1) / m.warps);
   void *args[] = {&m};
+  ProfScope ps("merge_topk", st);
   UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_kernel, dim3(grid), dim3(32 * m.warps), args,
                          smem, st));
   return UV_OK;
@@ -768,6 +808,7 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
     void *args[] = {&pp};
+    ProfScope ps("prep_queries", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,
                            smem, st));
   }
@@ -826,6 +867,7 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
     sp.part_key = part_key;
     sp.part_id = part_id;
     void *args[] = {&sp};
+    ProfScope ps("flat_scan", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::flat_scan_kernel, dim3((unsigned)qtiles, (unsigned)splits),
                            dim3(256), args, smem, st));
   }
@@ -862,6 +904,37 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
   UV_TRY(merge_launch(nq, n_lists, k_in, k, nullptr, d_in_scores, d_in_ids, d_out_ids,
                       d_out_scores, st));
   return outs.finish(st);
+}
+
+int uv_profile_enable(int32_t on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto &r : g_prof) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  g_prof.clear();
+  g_prof_on = on != 0;
+  return UV_OK;
+}
+
+int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
+  if (kernel == nullptr || total_ms == nullptr || launches == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  double tot = 0.0;
+  int64_t cnt = 0;
+  const bool all = std::strcmp(kernel, "*") == 0;
+  for (auto &r : g_prof) {
+    if (!all && std::strcmp(r.name, kernel) != 0) continue;
+    UV_CK(cudaEventSynchronize(r.b));
+    float ms = 0.0f;
+    UV_CK(cudaEventElapsedTime(&ms, r.a, r.b));
+    tot += ms;
+    cnt++;
+  }
+  *total_ms = tot;
+  *launches = cnt;
+  return UV_OK;
 }
 
 }  // extern "C"
