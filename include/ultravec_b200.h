@@ -163,6 +163,12 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream);
 
+/* Launch-shape tuning, no counterpart in the reference (results never depend
+ * on it): "scan_splits" fixes the number of record ranges each query tile is
+ * split into (0 = automatic).  Process-wide; returns UV_EINVAL for an unknown
+ * key. */
+int uv_set_tuning(const char *key, int64_t value);
+
 /* Measurement aid, no counterpart in the reference: while enabled, every
  * kernel the library launches is bracketed by CUDA events on its launch
  * stream.  uv_profile_read waits for those events and returns the summed

@@ -6,5 +6,5 @@ as `ultravec_ann_b200` by `load()` in ultravec_ann_b200_loader.py (repo root)
 or by any importer that points importlib at this directory.
 """
 from .binding import (Codec, Index, UVError, build, check, lib, topk_merge,  # noqa: F401
-                      profile_enable, profile_read,
+                      profile_enable, profile_read, set_tuning,
                       UV_SEARCH_COSINE, UV_SEARCH_MIPS, SYMBOLS)

@@ -30,7 +30,7 @@ SYMBOLS = [
     "uv_index_set_centroids", "uv_index_reserve", "uv_index_add", "uv_index_add_batch",
     "uv_index_len", "uv_index_dimensions", "uv_index_mem_bytes", "uv_index_search",
     "uv_index_export", "uv_index_digest", "uv_index_clear", "uv_topk_merge",
-    "uv_profile_enable", "uv_profile_read",
+    "uv_profile_enable", "uv_profile_read", "uv_set_tuning",
 ]
 
 
@@ -91,6 +91,7 @@ def lib():
             "uv_topk_merge": (C.c_int, [i32, vp, vp, i64, i32, i32, i32, vp, vp, vp]),
             "uv_index_clear": (C.c_int, [vp]),
             "uv_profile_enable": (C.c_int, [i32]),
+            "uv_set_tuning": (C.c_int, [C.c_char_p, i64]),
             "uv_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(i64)]),
         }
         for name, (res, args) in sig.items():
@@ -349,6 +350,11 @@ def topk_merge(in_ids, in_scores, k: int, device: int = 0):
     check(lib().uv_topk_merge(device, _ptr(in_ids), _ptr(in_scores), nq, n_lists, k_in, k,
                               _ptr(ids), _ptr(scores), _stream(in_ids)))
     return ids, scores
+
+
+def set_tuning(key: str, value: int):
+    """Launch-shape tuning (never changes results), e.g. ("scan_splits", 8)."""
+    check(lib().uv_set_tuning(key.encode(), int(value)))
 
 
 def profile_enable(on: bool = True):

@@ -146,6 +146,7 @@ struct ProfRec {
   cudaEvent_t a, b;
 };
 std::mutex g_prof_mu;
+int64_t g_scan_splits = 0;  // uv_set_tuning("scan_splits")
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
 
@@ -766,8 +767,8 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   if (nq == 0) return UV_OK;
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
-  if (d % 16 != 0 || d > 512)
-    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16, at most 512");
+  if (d % 16 != 0)
+    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
   const int dev = c->cfg.device;
   DeviceGuard g(dev);
   cudaStream_t st = (cudaStream_t)stream;
@@ -820,15 +821,31 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   if ((img_words & 1) == 0) img_words++;
   const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
   const size_t smem = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
-  UV_CK(cudaFuncSetAttribute(uvb::flat_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem));
+  if (smem > 227 * 1024)
+    return fail(UV_EUNSUPPORTED, "flat scan tile for this dim exceeds shared memory (dim <= 384)");
+  const void *scan_k = uvb::flat_scan_kernel_ptr(c->cfg.bits);
+  UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 1;
-  UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, uvb::flat_scan_kernel, 256, smem));
+  UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
   per_sm = std::max(per_sm, 1);
   const int64_t slots = (int64_t)sm_count(dev) * per_sm;
-  int64_t splits = std::max<int64_t>(1, (slots * 4 + qtiles - 1) / qtiles);
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, 2048 / k));
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, n / 256));
+  // Split each query tile's records so that the grid fills whole waves: the
+  // smallest split count whose last wave is at least 90% full, else the best.
+  const int64_t max_splits =
+      std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(2048 / k, 32), n / 1024));
+  int64_t splits = 1;
+  double best_eff = 0.0;
+  for (int64_t s = 1; s <= max_splits; s++) {
+    const int64_t ctas = qtiles * s;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double eff = (double)ctas / (double)(waves * slots);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      splits = s;
+    }
+    if (eff >= 0.9) break;
+  }
+  if (g_scan_splits > 0) splits = std::min<int64_t>(g_scan_splits, std::max<int64_t>(1, n));
   uint32_t *part_key = nullptr;
   int64_t *part_id = nullptr;
   UV_TRY(sc.alloc(&part_key, (size_t)nq * splits * k));
@@ -868,8 +885,8 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
     sp.part_id = part_id;
     void *args[] = {&sp};
     ProfScope ps("flat_scan", st);
-    UV_CK(cudaLaunchKernel((const void *)uvb::flat_scan_kernel, dim3((unsigned)qtiles, (unsigned)splits),
-                           dim3(256), args, smem, st));
+    UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)qtiles, (unsigned)splits), dim3(256), args,
+                           smem, st));
   }
   // 3) merge the splits
   UV_TRY(merge_launch(nq, (int)splits, k, k, part_key, nullptr, part_id, d_ids, d_scores, st));
@@ -904,6 +921,16 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
   UV_TRY(merge_launch(nq, n_lists, k_in, k, nullptr, d_in_scores, d_in_ids, d_out_ids,
                       d_out_scores, st));
   return outs.finish(st);
+}
+
+int uv_set_tuning(const char *key, int64_t value) {
+  if (key == nullptr) return fail(UV_EINVAL, "null key");
+  if (std::strcmp(key, "scan_splits") == 0) {
+    if (value < 0 || value > 4096) return fail(UV_EINVAL, "scan_splits must be 0..4096");
+    g_scan_splits = value;
+    return UV_OK;
+  }
+  return fail(UV_EINVAL, std::string("unknown tuning key: ") + key);
 }
 
 int uv_profile_enable(int32_t on) {

@@ -94,14 +94,28 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
   uint32_t *backs = (uint32_t *)(misc + 80);       // back-pointers or a traceback chunk
   uint32_t *misc_u = (uint32_t *)misc;
 
-  const int s0 = tm.t * SPT;
-  const int q0 = s0 >> B;
+  // State ownership.  Whole groups (SPT >= 2^B): thread t owns groups
+  // t, t+T, t+2T, ... so that at every step the predecessor loads and the
+  // next-cost stores of a warp touch consecutive words (no bank conflicts).
+  // Partial groups (SPT < 2^B): thread t owns states t*SPT .. t*SPT+SPT-1.
+  auto state_of = [&](int j) -> int {
+    if (SPT >= NE) return ((tm.t + (j / NE) * T) << B) + (j % NE);
+    return tm.t * SPT + j;
+  };
+  auto group_of = [&](int g) -> int {
+    if (SPT >= NE) return tm.t + g * T;
+    return (tm.t * SPT) >> B;
+  };
 
-  float creg[WPT];
+  // negated table values of the owned windows: xi - c == xi + (-c) exactly
+  float2 ncode[SPT][NE / 2];
 #pragma unroll
-  for (int j = 0; j < SPT; j++)
+  for (int j = 0; j < SPT; j++) {
+    const int ns = state_of(j);
 #pragma unroll
-    for (int k = 0; k < NE; k++) creg[j * NE + k] = __ldg(p.code + s0 + j + k * NS);
+    for (int k = 0; k < NE; k += 2)
+      ncode[j][k / 2] = make_float2(-__ldg(p.code + ns + k * NS), -__ldg(p.code + ns + (k + 1) * NS));
+  }
 
   const int64_t slot = (int64_t)blockIdx.x * p.teams_per_cta + team;
   uint32_t *backg = BACK_SMEM ? nullptr : p.back_global + slot * p.back_words_team;
@@ -168,38 +182,72 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     tm.sync();
 
     // ---- forward: add-compare-select over d steps ----
+    // metric (xi - c)^2 as paired IEEE ops: (xi + (-c)) then d*d, then the
+    // predecessor cost added -- three roundings per window, as the reference.
     float *cur = cost0, *nxt = cost1;
     float last[SPT];
     uint32_t word = 0;
     for (int step = 0; step < d; step++) {
       const float xi = ubuf[step];
+      const float2 xi2 = make_float2(xi, xi);
       const float wi = aniso ? fadd(1.0f, fmul(fmul(p.lambda, xi), xi)) : 1.0f;
-      float cp[GPT][NE];
+      const float2 wi2 = make_float2(wi, wi);
+      float2 cp[GPT][NE / 2];
 #pragma unroll
-      for (int g = 0; g < GPT; g++)
+      for (int g = 0; g < GPT; g++) {
+        const int q = group_of(g);
 #pragma unroll
-        for (int k = 0; k < NE; k++) cp[g][k] = cur[q0 + g + k * GS];
+        for (int k = 0; k < NE; k += 2)
+          cp[g][k / 2] = make_float2(cur[q + k * GS], cur[q + (k + 1) * GS]);
+      }
       const int slot_bits = (step % SPW) * BPS;
+      float best[SPT];
 #pragma unroll
       for (int j = 0; j < SPT; j++) {
         const int g = (SPT >= NE) ? j / NE : 0;
-        float best = 0.0f;
         uint32_t bk = 0;
 #pragma unroll
-        for (int k = 0; k < NE; k++) {
-          const float dd = fsub(xi, creg[j * NE + k]);
-          const float m = aniso ? fmul(fmul(wi, dd), dd) : fmul(dd, dd);
-          const float c = fadd(cp[g][k], m);
+        for (int k = 0; k < NE; k += 2) {
+          const float2 dd = __fadd2_rn(xi2, ncode[j][k / 2]);
+          const float2 m = aniso ? __fmul2_rn(__fmul2_rn(wi2, dd), dd) : __fmul2_rn(dd, dd);
+          const float2 c = __fadd2_rn(cp[g][k / 2], m);
           if (k == 0) {
-            best = c;
-          } else if (c < best) {
-            best = c;
+            best[j] = c.x;
+          } else if (c.x < best[j]) {
+            best[j] = c.x;
             bk = (uint32_t)k;
           }
+          if (c.y < best[j]) {
+            best[j] = c.y;
+            bk = (uint32_t)(k + 1);
+          }
         }
-        nxt[s0 + j] = best;
-        last[j] = best;
+        last[j] = best[j];
         word |= bk << (slot_bits + j * B);
+      }
+      // next-cost stores: one vector store per owned run of states
+      if (SPT >= NE) {
+#pragma unroll
+        for (int g = 0; g < GPT; g++) {
+          float *dst = nxt + (group_of(g) << B);
+          if (NE == 2) {
+            *(float2 *)dst = make_float2(best[g * NE], best[g * NE + 1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < NE; e += 4)
+              *(float4 *)(dst + e) = make_float4(best[g * NE + e], best[g * NE + e + 1],
+                                                 best[g * NE + e + 2], best[g * NE + e + 3]);
+          }
+        }
+      } else {
+        float *dst = nxt + tm.t * SPT;
+        if (SPT == 2) {
+          *(float2 *)dst = make_float2(best[0], best[1]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < SPT; e += 4)
+            *(float4 *)(dst + e) = make_float4(best[e], best[e + 1], best[e + 2], best[e + 3]);
+        }
       }
       if ((step % SPW) == SPW - 1 || step == d - 1) {
         const int widx = (step / SPW) * T + tm.t;
@@ -220,19 +268,28 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
 #pragma unroll
     for (int j = 0; j < SPT; j++) {
       uint32_t k32 = (uint32_t)total_key(last[j]) ^ 0x80000000u;
-      uint64_t key = ((uint64_t)(~k32) << 32) | (uint32_t)(~(uint32_t)(s0 + j));
+      uint64_t key = ((uint64_t)(~k32) << 32) | (uint32_t)(~(uint32_t)state_of(j));
       bkey = key > bkey ? key : bkey;
     }
     bkey = team_max_u64(bkey, tm, red);
     uint32_t s = ~(uint32_t)(bkey & 0xffffffffu);
 
     // ---- traceback: windows w_i into ubuf ----
+    // owner of state s and its slot j in that thread's back-pointer field
+    auto owner_thread = [&](uint32_t st) -> int {
+      if (SPT >= NE) return (int)((st >> B) % (uint32_t)T);
+      return (int)(st / SPT);
+    };
+    auto owner_slot = [&](uint32_t st) -> int {
+      if (SPT >= NE) return (int)(((st >> B) / (uint32_t)T) * NE + (st & EMASK));
+      return (int)(st % SPT);
+    };
     uint32_t *wv = (uint32_t *)ubuf;
     if (BACK_SMEM) {
       if (tm.leader()) {
         for (int step = d - 1; step >= 0; step--) {
-          const uint32_t wd = backs[(step / SPW) * T + (int)(s / SPT)];
-          const uint32_t k = (wd >> ((step % SPW) * BPS + (int)(s % SPT) * B)) & EMASK;
+          const uint32_t wd = backs[(step / SPW) * T + owner_thread(s)];
+          const uint32_t k = (wd >> ((step % SPW) * BPS + owner_slot(s) * B)) & EMASK;
           const uint32_t w = s + k * (uint32_t)NS;
           wv[step] = w;
           s = w >> B;
@@ -249,8 +306,8 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
         tm.sync();
         if (tm.leader()) {
           for (int step = hi - 1; step >= lo; step--) {
-            const uint32_t wd = backs[(step / SPW) * T - wlo + (int)(s / SPT)];
-            const uint32_t k = (wd >> ((step % SPW) * BPS + (int)(s % SPT) * B)) & EMASK;
+            const uint32_t wd = backs[(step / SPW) * T - wlo + owner_thread(s)];
+            const uint32_t k = (wd >> ((step % SPW) * BPS + owner_slot(s) * B)) & EMASK;
             const uint32_t w = s + k * (uint32_t)NS;
             wv[step] = w;
             s = w >> B;
@@ -364,8 +421,9 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
   plan->back_words_team = back_words;
   // Shared-memory back-pointers when at least 8 warps per SM still fit.
   const int64_t budget = 200 * 1024;
+  // a team larger than a warp is the whole CTA; smaller teams pack 256 threads
   int tpc_warp = T >= 32 ? 1 : (int)(32 / T);  // teams per warp
-  int tpc = T >= 32 ? 1 : tpc_warp * (256 / 32);
+  int tpc = T > 32 ? 1 : (int)(256 / T);
   auto fits = [&](int64_t team_words, int teams) { return team_words * 4 * teams <= budget; };
   int64_t team_words_smem = (base_words + back_words + 3) & ~3LL;
   int64_t team_words_glob = (base_words + chunk_words + 3) & ~3LL;

@@ -78,238 +78,287 @@ __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
 // ---------------------------------------------------------------------------
 // Flat scan + top-k.
 // ---------------------------------------------------------------------------
-constexpr int TQ = 32;       // queries per CTA
-constexpr int TN = 32;       // records per tile
-constexpr int QSTR = TQ + 4;  // padded row of the transposed query tile
-constexpr int XSTR = TN + 4;  // padded row of the transposed record tile
+constexpr int TQ = 32;        // queries per CTA
+constexpr int TN = 32;        // records per tile
+constexpr int QSTR = TQ + 4;  // padded row of the transposed query tile (LDS.128)
+constexpr int XSTR = TN + 4;  // padded row of the transposed record tile (LDS.128)
 constexpr int KCAP = 128;     // top-k capacity per query
-constexpr int BCAP = 128;     // candidate buffer per query
-constexpr int SLOTS = KCAP + BCAP;
+constexpr int BCAP = 64;      // candidate buffer per query (power of two)
 
-// Bitonic sort (descending) of n = 256 keys in shared memory by one warp.
-__device__ __forceinline__ void warp_sort_desc_256(uint64_t *a) {
+// Sort 64 keys descending (bitonic, one warp, two keys per lane).
+__device__ __forceinline__ void warp_sort_desc_64(uint64_t *a) {
   const int lane = threadIdx.x & 31;
-  for (int size = 2; size <= SLOTS; size <<= 1) {
+  for (int size = 2; size <= BCAP; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int pi = lane; pi < SLOTS / 2; pi += 32) {
-        const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
-        const int jx = i + stride;
-        const bool desc = (i & size) == 0;
-        const uint64_t x = a[i], y = a[jx];
-        const bool swap = desc ? (x < y) : (x > y);
-        if (swap) {
-          a[i] = y;
-          a[jx] = x;
-        }
+      const int pi = lane;
+      const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
+      const int jx = i + stride;
+      const bool desc = (i & size) == 0;
+      const uint64_t x = a[i], y = a[jx];
+      if (desc ? (x < y) : (x > y)) {
+        a[i] = y;
+        a[jx] = x;
       }
       __syncwarp();
     }
   }
 }
 
-// Merge the candidate buffer of one query into its top-k (one warp).
-__device__ __forceinline__ void flush_query(uint64_t *slots, int *cnt, uint64_t *theta, int k) {
-  warp_sort_desc_256(slots);
+// Number of keys in the descending array a[0..n) that are larger than x.
+__device__ __forceinline__ int count_larger(const uint64_t *a, int n, uint64_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] > x)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// Merge one query's candidate buffer into its sorted top-k list (one warp).
+// Keys are unique, so every element's merged position is its own rank plus
+// the number of larger keys in the other list; positions >= KCAP drop out.
+__device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *cnt, uint64_t *theta,
+                                            int k) {
   const int lane = threadIdx.x & 31;
-  for (int i = KCAP + lane; i < SLOTS; i += 32) slots[i] = kEmptyKey;
+  const int m = *cnt;
+  for (int i = m + lane; i < BCAP; i += 32) buf[i] = kEmptyKey;
+  __syncwarp();
+  warp_sort_desc_64(buf);
+  uint64_t tv[KCAP / 32], bv[BCAP / 32];
+  int tp[KCAP / 32], bp[BCAP / 32];
+#pragma unroll
+  for (int u = 0; u < KCAP / 32; u++) {
+    const int i = lane + 32 * u;
+    tv[u] = top[i];
+    tp[u] = i + count_larger(buf, BCAP, tv[u]);
+  }
+#pragma unroll
+  for (int u = 0; u < BCAP / 32; u++) {
+    const int i = lane + 32 * u;
+    bv[u] = buf[i];
+    bp[u] = i + count_larger(top, KCAP, bv[u]);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < KCAP / 32; u++)
+    if (tv[u] != kEmptyKey && tp[u] < KCAP) top[tp[u]] = tv[u];
+#pragma unroll
+  for (int u = 0; u < BCAP / 32; u++)
+    if (bv[u] != kEmptyKey && bp[u] < KCAP) top[bp[u]] = bv[u];
   __syncwarp();
   if (lane == 0) {
     *cnt = 0;
-    *theta = slots[k - 1];
+    *theta = top[k - 1];
   }
   __syncwarp();
 }
 
-// Read the 64 bits that start at bit `pos` of a big-endian byte image held as
-// little-endian u32 words in shared memory.
-__device__ __forceinline__ uint64_t read_bits64(const uint32_t *w, int pos) {
-  const int wi = pos >> 5, off = pos & 31;
-  const uint32_t a = __byte_perm(w[wi], 0, 0x0123);
-  const uint32_t b = __byte_perm(w[wi + 1], 0, 0x0123);
-  const uint32_t c = __byte_perm(w[wi + 2], 0, 0x0123);
-  const uint64_t hi = ((uint64_t)a << 32) | b;
-  return off ? (hi << off) | (c >> (32 - off)) : hi;
+// Decode one record tile into x-bar (transposed) and stage its scalars.
+// Thread (r, c) decodes windows [c*d/8, (c+1)*d/8) of record r in chunks of
+// 16, reading the packed stream straight from global memory: window i is the
+// field [i*B, i*B + M + B) of [start (M bits) || codes] (src/trellis.rs:
+// 1576-1600), i.e. bits [32 + i*B - M, ...) of the image whose first 32-bit
+// word is the start state.
+template <int B>
+__device__ __forceinline__ void decode_tile(const ScanParams &p, const float *code, int64_t r0,
+                                            int nr, float *xT, float *rs_s, float *rn_s,
+                                            float *nm_s, uint32_t *ci_s) {
+  const int tid = threadIdx.x;
+  const int d = p.dim;
+  const int W = p.mem + B;
+  const uint32_t wmask = (1u << W) - 1u;
+  const int r = tid & 31;
+  const int c = tid >> 5;
+  const int per_thread = d >> 3;
+  const bool ok = r < nr;
+  const int64_t rec = ok ? r0 + r : r0;
+  const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
+  const int rw = p.code_stride >> 2;
+  const uint32_t st = __ldg(p.start + rec);
+  const int end = (c + 1) * per_thread;
+  for (int base = c * per_thread; base < end; base += 16) {
+    const int lim = end - base;  // windows of this chunk (<= 16)
+    // image bit offset of the chunk's first window and the word holding it
+    const int pos0 = 32 + base * B - p.mem;
+    const int w0 = pos0 >> 5;
+    uint32_t w[5];
+#pragma unroll
+    for (int u = 0; u < 5; u++) {
+      const int wi = w0 + u;
+      w[u] = wi == 0 ? st : (wi <= rw ? __byte_perm(__ldg(cw + wi - 1), 0, 0x0123) : 0u);
+    }
+    // align the chunk to bit 0 of w[0..3]
+    const int sh = pos0 & 31;
+    uint32_t a[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) a[u] = __funnelshift_l(w[u + 1], w[u], sh);
+#pragma unroll
+    for (int g = 0; g < 16; g++) {
+      const int bit = g * B;  // compile-time
+      const int wd = bit >> 5;
+      const uint64_t v = ((uint64_t)a[wd] << 32) | a[wd + 1];
+      const uint32_t win = (uint32_t)(v >> (64 - (bit & 31) - W)) & wmask;
+      const int coord = base + g;
+      // row `coord` is read only by accumulator lane coord & 15, whose record
+      // half is bit 1 of that lane: store the record pre-permuted for it
+      if (g < lim) xT[(size_t)coord * XSTR + (r ^ (((coord >> 1) & 1) << 2))] = ok ? code[win] : 0.0f;
+    }
+  }
+  if (tid < TN) {
+    const bool okr = tid < nr;
+    rs_s[tid] = okr ? __ldg(p.rescale + r0 + tid) : INFINITY;
+    rn_s[tid] = (okr && p.rnorm) ? __ldg(p.rnorm + r0 + tid) : 1.0f;
+    nm_s[tid] = (okr && p.norms) ? __ldg(p.norms + r0 + tid) : 1.0f;
+    ci_s[tid] = (okr && p.cidx) ? __ldg(p.cidx + r0 + tid) : 0u;
+  }
 }
 
-__global__ void __launch_bounds__(256) flat_scan_kernel(const ScanParams p) {
+template <int B>
+__global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int tid = threadIdx.x;
   const int d = p.dim;
-  const int W = p.mem + p.bits;
-  const uint32_t wmask = (1u << W) - 1u;
 
-  // shared-memory carve-up (all offsets 16-byte aligned)
-  float *qT = (float *)sm;                                   // d x QSTR
-  float *xT = qT + (size_t)d * QSTR;                         // d x XSTR
-  uint64_t *slots = (uint64_t *)(xT + (size_t)d * XSTR);     // TQ x SLOTS
-  uint64_t *theta = slots + (size_t)TQ * SLOTS;              // TQ
+  // shared-memory carve-up (must match scan_smem_bytes)
+  float *xT0 = (float *)sm;                                  // d x XSTR
+  float *xT1 = xT0 + (size_t)d * XSTR;                       // d x XSTR
+  float *qT = xT1 + (size_t)d * XSTR;                        // d x QSTR
+  uint64_t *top = (uint64_t *)(qT + (((size_t)d * QSTR + 3) & ~(size_t)3));  // TQ x KCAP
+  uint64_t *buf = top + (size_t)TQ * KCAP;                   // TQ x BCAP
+  uint64_t *theta = buf + (size_t)TQ * BCAP;                 // TQ
   int *cnt = (int *)(theta + TQ);                            // TQ
-  float *qm_s = (float *)(cnt + TQ);                         // TQ
-  uint32_t *degen = (uint32_t *)(qm_s + TQ);                 // TQ
-  float *rs_s = (float *)(degen + TQ);                       // TN rescale
-  float *rn_s = rs_s + TN;                                   // TN rnorm
-  float *nm_s = rn_s + TN;                                   // TN norm
-  uint32_t *ci_s = (uint32_t *)(nm_s + TN);                  // TN cidx
-  int *flag = (int *)(ci_s + TN);                            // 4
-  uint32_t *img = (uint32_t *)(flag + 4);                    // TN x img_words
-  const int img_words = p.img_words;                         // per record
-  float *table = (float *)(img + (size_t)TN * img_words + 4);  // code table (optional)
+  uint32_t *degen = (uint32_t *)(cnt + TQ);                  // TQ
+  float *sc = (float *)(degen + TQ);                         // 2 x 4 x TN scalars
+  int *flag = (int *)(sc + 8 * TN);                          // 4
+  float *table = (float *)(flag + 4);                        // optional code table
   const float *code = p.table_in_smem ? table : p.code;
 
   const int64_t q_base = (int64_t)blockIdx.x * TQ;
   const int split = blockIdx.y;
   const int64_t r_begin = p.n * split / gridDim.y;
   const int64_t r_end = p.n * (split + 1) / gridDim.y;
+  const int ntiles = (int)((r_end - r_begin + TN - 1) / TN);
 
-  // ---- load queries (transposed), per-query state, table ----
   for (int e = tid; e < TQ * d; e += 256) {
     const int qi = e / d, i = e - qi * d;
     const int64_t q = q_base + qi;
-    qT[(size_t)i * QSTR + qi] = q < p.nq ? p.q_r[q * (int64_t)p.q_stride + i] : 0.0f;
+    // row i is read only by accumulator lane j = i & 15: store its queries
+    // pre-permuted by that lane's mask (bits 3, 2, 0 of j)
+    const int jm = i & 15;
+    const int qm = (((jm >> 3) & 1) << 2) | (((jm >> 2) & 1) << 1) | (jm & 1);
+    qT[(size_t)i * QSTR + (qi ^ qm)] = q < p.nq ? p.q_r[q * (int64_t)p.q_stride + i] : 0.0f;
   }
-  for (int e = tid; e < TQ * SLOTS; e += 256) slots[e] = kEmptyKey;
+  for (int e = tid; e < TQ * KCAP; e += 256) top[e] = kEmptyKey;
   if (tid < TQ) {
     const int64_t q = q_base + tid;
     theta[tid] = kEmptyKey;
     cnt[tid] = 0;
     degen[tid] = q < p.nq ? p.degenerate[q] : 1u;
-    qm_s[tid] = 0.0f;
   }
+  if (tid == 0) flag[0] = 0;
   if (p.table_in_smem)
     for (int e = tid; e < p.table_len; e += 256) table[e] = __ldg(p.code + e);
   __syncthreads();
+  if (ntiles > 0) {
+    const int nr0 = (int)min((int64_t)TN, r_end - r_begin);
+    decode_tile<B>(p, code, r_begin, nr0, xT0, sc, sc + TN, sc + 2 * TN, (uint32_t *)(sc + 3 * TN));
+  }
+  __syncthreads();
 
-  const int j = tid & 15;         // accumulator lane
-  const int pp = tid >> 4;        // position 0..15
-  const int pq = pp >> 2;         // query octet
-  const int pn = pp & 3;          // record octet
-  // after the reduction this thread owns queries qsel and records rsel..rsel+3
-  const int qsel = pq * 8 + (((j >> 3) & 1) << 2) + (((j >> 2) & 1) << 1) + (j & 1);
-  const int rsel = pn * 8 + (((j >> 1) & 1) << 2);
-
+  // Thread (j, pq, pn): lane j of queries pq*8.. and records pn*8...  Shared
+  // rows are stored permuted per reading lane -- queries by the lane bits
+  // (j3 j2 j0), records by j1 -- so register slot a holds query a ^ qmask and
+  // slot c record c ^ rhalf.  Each level of the transpose-reduction then keeps
+  // the low half of its registers and sends the high half (the partner lane
+  // holds the same outputs in the swapped order), with no per-lane select.
+  const int j = tid & 15;
+  const int pp = tid >> 4;
+  const int pq = pp >> 2;
+  const int pn = pp & 3;
+  const int qmask = (((j >> 3) & 1) << 2) | (((j >> 2) & 1) << 1) | (j & 1);
+  const int rhalf = ((j >> 1) & 1) << 2;
+  const int qsel = pq * 8 + qmask;  // the query this thread finalizes
+  const int rsel = pn * 8 + rhalf;  // its first record
   const int kblocks = d >> 4;
-  const int per_thread_win = d / 8;  // windows decoded per thread per tile
 
-  for (int64_t r0 = r_begin; r0 < r_end; r0 += TN) {
-    const int nr = (int)((r_end - r0) < (int64_t)TN ? (r_end - r0) : (int64_t)TN);
-    // ---- stage the tile: record images (start word + codes) and scalars ----
-    {
-      const int rw = p.code_stride >> 2;  // code words per record
-      for (int e = tid; e < TN * rw; e += 256) {
-        const int r = e / rw, wi = e - r * rw;
-        uint32_t val = 0;
-        if (r < nr) val = __ldg((const uint32_t *)(p.codes + (r0 + r) * (int64_t)p.code_stride) + wi);
-        img[r * img_words + 4 + wi] = val;
-      }
-      if (tid < TN) {
-        const int r = tid;
-        const bool ok = r < nr;
-        const uint32_t st = ok ? __ldg(p.start + r0 + r) : 0u;
-        img[r * img_words + 3] = __byte_perm(st, 0, 0x0123);  // big-endian start word
-        img[r * img_words + 0] = 0u;
-        img[r * img_words + 1] = 0u;
-        img[r * img_words + 2] = 0u;
-        for (int w = 4 + rw; w < img_words; w++) img[r * img_words + w] = 0u;
-        rs_s[r] = ok ? __ldg(p.rescale + r0 + r) : INFINITY;
-        rn_s[r] = (ok && p.rnorm) ? __ldg(p.rnorm + r0 + r) : 1.0f;
-        nm_s[r] = (ok && p.norms) ? __ldg(p.norms + r0 + r) : 1.0f;
-        ci_s[r] = (ok && p.cidx) ? __ldg(p.cidx + r0 + r) : 0u;
-      }
-    }
-    __syncthreads();
-    // ---- decode: x-bar[i][r] = code[window_i(r)] ----
-    {
-      const int r = tid & 31;
-      const int c = tid >> 5;  // 8 coordinate chunks
-      const uint32_t *rec = img + r * img_words;
-      const int i0 = c * per_thread_win;
-      // window i = image bits [128 + i*B - M, 128 + i*B + B)
-      int done = 0;
-      while (done < per_thread_win) {
-        const int i = i0 + done;
-        const int pos = 128 + i * p.bits - p.mem;
-        const uint64_t bits64 = read_bits64(rec, pos);
-        const int group = min(per_thread_win - done, (64 - W) / p.bits + 1);
-        for (int g = 0; g < group; g++) {
-          const uint32_t w = (uint32_t)(bits64 >> (64 - W - g * p.bits)) & wmask;
-          xT[(size_t)(i + g) * XSTR + r] = code[w];
-        }
-        done += group;
-      }
-    }
-    __syncthreads();
+  for (int t = 0; t < ntiles; t++) {
+    const int64_t r0 = r_begin + (int64_t)t * TN;
+    const int nr = (int)min((int64_t)TN, r_end - r0);
+    const float *xT = (t & 1) ? xT1 : xT0;
+    const float *scs = sc + (t & 1) * 4 * TN;
 
-    // ---- decode-GEMM: acc[a][c] = lane j of dot(query a, record c) ----
-    float acc[8][8];
+    // ---- decode-GEMM in paired f32 FMAs: acc[a][c] = lane j, query a, records 2c,2c+1
+    float2 acc[8][4];
 #pragma unroll
     for (int a = 0; a < 8; a++)
 #pragma unroll
-      for (int c = 0; c < 8; c++) acc[a][c] = 0.0f;
+      for (int c = 0; c < 4; c++) acc[a][c] = make_float2(0.0f, 0.0f);
+#pragma unroll 2
     for (int b = 0; b < kblocks; b++) {
       const int coord = (b << 4) + j;
-      const float4 qa = *(const float4 *)(qT + (size_t)coord * QSTR + pq * 8);
-      const float4 qb = *(const float4 *)(qT + (size_t)coord * QSTR + pq * 8 + 4);
-      const float4 xa = *(const float4 *)(xT + (size_t)coord * XSTR + pn * 8);
-      const float4 xb = *(const float4 *)(xT + (size_t)coord * XSTR + pn * 8 + 4);
-      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const float *qrow = qT + (size_t)coord * QSTR + pq * 8;
+      const float *xrow = xT + (size_t)coord * XSTR + pn * 8;
+      const float4 x0 = *(const float4 *)(xrow);
+      const float4 x1 = *(const float4 *)(xrow + 4);
+      const float4 q0 = *(const float4 *)(qrow);
+      const float4 q1 = *(const float4 *)(qrow + 4);
+      const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      const float2 xv[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w),
+                            make_float2(x1.x, x1.y), make_float2(x1.z, x1.w)};
 #pragma unroll
-      for (int a = 0; a < 8; a++)
+      for (int a = 0; a < 8; a++) {
+        const float2 q2 = make_float2(qv[a], qv[a]);
 #pragma unroll
-        for (int c = 0; c < 8; c++) acc[a][c] = fmaf(qv[a], xv[c], acc[a][c]);
-    }
-
-    // ---- order-preserving transpose-reduction over the 16 lanes ----
-    // level 1 (xor 8): keep query half by bit 3 of j    -> 32 values
-    float l1[4][8];
-    {
-      const bool hi = (j & 8) != 0;
-#pragma unroll
-      for (int a = 0; a < 4; a++)
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const float keep = hi ? acc[a + 4][c] : acc[a][c];
-          const float send = hi ? acc[a][c] : acc[a + 4][c];
-          l1[a][c] = fadd(keep, __shfl_xor_sync(0xffffffffu, send, 8));
-        }
-    }
-    // level 2 (xor 4): keep query pair by bit 2          -> 16 values
-    float l2[2][8];
-    {
-      const bool hi = (j & 4) != 0;
-#pragma unroll
-      for (int a = 0; a < 2; a++)
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const float keep = hi ? l1[a + 2][c] : l1[a][c];
-          const float send = hi ? l1[a][c] : l1[a + 2][c];
-          l2[a][c] = fadd(keep, __shfl_xor_sync(0xffffffffu, send, 4));
-        }
-    }
-    // level 3 (xor 1): keep query by bit 0               -> 8 values
-    float l3[8];
-    {
-      const bool hi = (j & 1) != 0;
-#pragma unroll
-      for (int c = 0; c < 8; c++) {
-        const float keep = hi ? l2[1][c] : l2[0][c];
-        const float send = hi ? l2[0][c] : l2[1][c];
-        l3[c] = fadd(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+        for (int c = 0; c < 4; c++) acc[a][c] = __ffma2_rn(q2, xv[c], acc[a][c]);
       }
     }
-    // level 4 (xor 2): keep record half by bit 1         -> 4 values
-    float dot4[4];
-    {
-      const bool hi = (j & 2) != 0;
+
+    // ---- transpose-reduction: xor 8, 4, 1 over queries, xor 2 over records.
+    // The additions pair lanes (j, j^8), (j, j^4), (j, j^1), (j, j^2):
+    // v_j = a_j + a_{j+8}, s_j = v_j + v_{j+4}, (s0+s1), (s2+s3), total --
+    // exactly the hsum256 tree of src/simd.rs:251-262.
+    float2 l1[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        const float keep = hi ? l3[c + 4] : l3[c];
-        const float send = hi ? l3[c] : l3[c + 4];
-        dot4[c] = fadd(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+        float2 o;
+        o.x = __shfl_xor_sync(0xffffffffu, acc[a + 4][c].x, 8);
+        o.y = __shfl_xor_sync(0xffffffffu, acc[a + 4][c].y, 8);
+        l1[a][c] = __fadd2_rn(acc[a][c], o);
       }
+    float2 l2[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        float2 o;
+        o.x = __shfl_xor_sync(0xffffffffu, l1[a + 2][c].x, 4);
+        o.y = __shfl_xor_sync(0xffffffffu, l1[a + 2][c].y, 4);
+        l2[a][c] = __fadd2_rn(l1[a][c], o);
+      }
+    float2 l3[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      float2 o;
+      o.x = __shfl_xor_sync(0xffffffffu, l2[1][c].x, 1);
+      o.y = __shfl_xor_sync(0xffffffffu, l2[1][c].y, 1);
+      l3[c] = __fadd2_rn(l2[0][c], o);
     }
+    float2 dot2[2];
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      float2 o;
+      o.x = __shfl_xor_sync(0xffffffffu, l3[c + 2].x, 2);
+      o.y = __shfl_xor_sync(0xffffffffu, l3[c + 2].y, 2);
+      dot2[c] = __fadd2_rn(l3[c], o);
+    }
+    const float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
 
-    // ---- estimator, MIPS norm, threshold test ----
+    // ---- estimator (src/trellis.rs:1517), MIPS norm, threshold test ----
     if (!degen[qsel]) {
       const uint64_t th = theta[qsel];
       const int64_t q = q_base + qsel;
@@ -317,25 +366,39 @@ __global__ void __launch_bounds__(256) flat_scan_kernel(const ScanParams p) {
       for (int c = 0; c < 4; c++) {
         const int r = rsel + c;
         if (r < nr) {
-          const float qm = p.n_centroids > 0 ? p.qc[q * p.n_centroids + ci_s[r]] : 0.0f;
-          float s = fadd(qm, fmul(rn_s[r], fdiv(dot4[c], rs_s[r])));
-          if (p.mips) s = fmul(s, nm_s[r]);
+          const float qm = p.n_centroids > 0
+                               ? p.qc[q * p.n_centroids + ((const uint32_t *)(scs + 3 * TN))[r]]
+                               : 0.0f;
+          float s = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
+          if (p.mips) s = fmul(s, scs[2 * TN + r]);
           const uint64_t key = rank_key(s, (uint32_t)(r0 - r_begin + r));
           if (key > th) {
             const int pos = atomicAdd(&cnt[qsel], 1);
-            slots[(size_t)qsel * SLOTS + KCAP + pos] = key;
+            buf[(size_t)qsel * BCAP + pos] = key;
+            if (pos == BCAP - TN) flag[0] = t + 1;
           }
         }
       }
     }
-    __syncthreads();
-    // ---- merge buffers that are close to full ----
-    {
-      const int warp = tid >> 5;
-      for (int qi = warp; qi < TQ; qi += 8)
-        if (cnt[qi] > BCAP - TN) flush_query(slots + (size_t)qi * SLOTS, &cnt[qi], &theta[qi], p.k);
+
+    // ---- decode the next tile into the other buffer ----
+    if (t + 1 < ntiles) {
+      const int64_t rn0 = r0 + TN;
+      const int nrn = (int)min((int64_t)TN, r_end - rn0);
+      float *xn = (t & 1) ? xT0 : xT1;
+      float *scn = sc + ((t + 1) & 1) * 4 * TN;
+      decode_tile<B>(p, code, rn0, nrn, xn, scn, scn + TN, scn + 2 * TN, (uint32_t *)(scn + 3 * TN));
     }
     __syncthreads();
+
+    // ---- merge candidate buffers that could overflow on the next tile ----
+    if (flag[0] == t + 1) {
+      const int warp = tid >> 5;
+      for (int qi = warp; qi < TQ; qi += 8)
+        if (cnt[qi] > BCAP - TN)
+          flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi], p.k);
+      __syncthreads();
+    }
   }
 
   // ---- final merge and write-out of this split's top-k ----
@@ -343,12 +406,13 @@ __global__ void __launch_bounds__(256) flat_scan_kernel(const ScanParams p) {
     const int warp = tid >> 5, lane = tid & 31;
     for (int qi = warp; qi < TQ; qi += 8) {
       const int64_t q = q_base + qi;
-      if (cnt[qi] > 0) flush_query(slots + (size_t)qi * SLOTS, &cnt[qi], &theta[qi], p.k);
+      if (cnt[qi] > 0)
+        flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi], p.k);
       if (q < p.nq) {
         uint32_t *ok = p.part_key + (q * gridDim.y + split) * (int64_t)p.k;
         int64_t *oid = p.part_id + (q * gridDim.y + split) * (int64_t)p.k;
         for (int i = lane; i < p.k; i += 32) {
-          const uint64_t key = slots[(size_t)qi * SLOTS + i];
+          const uint64_t key = top[(size_t)qi * KCAP + i];
           if (key == kEmptyKey) {
             ok[i] = 0u;
             oid[i] = -1;
@@ -362,6 +426,21 @@ __global__ void __launch_bounds__(256) flat_scan_kernel(const ScanParams p) {
       }
     }
   }
+}
+
+template __global__ void flat_scan_kernel<1>(const ScanParams p);
+template __global__ void flat_scan_kernel<2>(const ScanParams p);
+template __global__ void flat_scan_kernel<3>(const ScanParams p);
+template __global__ void flat_scan_kernel<4>(const ScanParams p);
+
+const void *flat_scan_kernel_ptr(int bits) {
+  switch (bits) {
+    case 1: return (const void *)flat_scan_kernel<1>;
+    case 2: return (const void *)flat_scan_kernel<2>;
+    case 3: return (const void *)flat_scan_kernel<3>;
+    case 4: return (const void *)flat_scan_kernel<4>;
+  }
+  return nullptr;
 }
 
 // ---------------------------------------------------------------------------
@@ -431,15 +510,13 @@ namespace uvb {
 
 // Must match the carve-up at the top of flat_scan_kernel.
 size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem) {
+  (void)img_words;
   size_t b = 0;
-  b += (size_t)dim * QSTR * 4;
-  b += (size_t)dim * XSTR * 4;
-  b += (size_t)TQ * SLOTS * 8;
-  b += (size_t)TQ * 8;          // theta
-  b += (size_t)TQ * 4 * 3;      // cnt, qm, degenerate
-  b += (size_t)TN * 4 * 4;      // rescale, rnorm, norm, cidx
-  b += 16;                      // flags
-  b += (size_t)TN * img_words * 4 + 16;
+  b += 2 * (size_t)dim * XSTR * 4;                      // x-bar tiles
+  b += (((size_t)dim * QSTR + 3) & ~(size_t)3) * 4;     // queries
+  b += (size_t)TQ * KCAP * 8 + (size_t)TQ * BCAP * 8;   // top-k + buffers
+  b += (size_t)TQ * 8 + (size_t)TQ * 4 * 2;             // theta, cnt, degenerate
+  b += 8 * (size_t)TN * 4 + 16;                         // scalars, flag
   if (table_in_smem) b += (size_t)table_len * 4;
   return b;
 }

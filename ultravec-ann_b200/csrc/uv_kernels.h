@@ -93,7 +93,7 @@ struct MergeParams {
 };
 
 __global__ void prep_queries_kernel(const PrepParams p);
-__global__ void flat_scan_kernel(const ScanParams p);
+const void *flat_scan_kernel_ptr(int bits);
 __global__ void merge_topk_kernel(const MergeParams p);
 
 // scan tiling constants shared with the host planner
