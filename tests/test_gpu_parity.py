@@ -182,7 +182,8 @@ def test_flat_search_matches_oracle(uv, oracle, mips):
 
 
 @pytest.mark.parametrize("dim,bits,mem", [(32, 2, 12), (64, 1, 8), (96, 3, 7), (256, 4, 6),
-                                          (384, 2, 8), (128, 2, 4), (16, 1, 12)])
+                                          (384, 2, 8), (128, 2, 4), (16, 1, 12),
+                                          (80, 2, 8), (48, 3, 6)])
 def test_flat_search_shapes(uv, oracle, dim, bits, mem):
     rows = rand_rows(777, dim, dim)
     qs = rand_rows(45, dim, dim + 1)

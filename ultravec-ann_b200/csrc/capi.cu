@@ -823,7 +823,7 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   const size_t smem = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
   if (smem > 227 * 1024)
     return fail(UV_EUNSUPPORTED, "flat scan tile for this dim exceeds shared memory (dim <= 384)");
-  const void *scan_k = uvb::flat_scan_kernel_ptr(c->cfg.bits);
+  const void *scan_k = uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
   UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 1;
   UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));

@@ -121,7 +121,7 @@ __device__ __forceinline__ int count_larger(const uint64_t *a, int n, uint64_t x
 // Keys are unique, so every element's merged position is its own rank plus
 // the number of larger keys in the other list; positions >= KCAP drop out.
 __device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *cnt, uint64_t *theta,
-                                            int k) {
+                                            float *theta_s, int k) {
   const int lane = threadIdx.x & 31;
   const int m = *cnt;
   for (int i = m + lane; i < BCAP; i += 32) buf[i] = kEmptyKey;
@@ -151,10 +151,16 @@ __device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *c
   __syncwarp();
   if (lane == 0) {
     *cnt = 0;
-    *theta = top[k - 1];
+    const uint64_t th = top[k - 1];
+    *theta = th;
+    *theta_s = th == kEmptyKey ? -INFINITY : key32_score((uint32_t)(th >> 32));
   }
   __syncwarp();
 }
+
+// Per-tile record scalars in shared memory: rescale, rnorm, norm, cidx and
+// the ratio g = rnorm / rescale used by the cheap pre-filter below.
+constexpr int NSC = 5;
 
 // Decode one record tile into x-bar (transposed) and stage its scalars.
 // Thread (r, c) decodes windows [c*d/8, (c+1)*d/8) of record r in chunks of
@@ -162,14 +168,13 @@ __device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *c
 // field [i*B, i*B + M + B) of [start (M bits) || codes] (src/trellis.rs:
 // 1576-1600), i.e. bits [32 + i*B - M, ...) of the image whose first 32-bit
 // word is the start state.
-template <int B>
+template <int B, bool TSMEM>
 __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *code, int64_t r0,
-                                            int nr, float *xT, float *rs_s, float *rn_s,
-                                            float *nm_s, uint32_t *ci_s) {
+                                            int nr, float *xT, float *sc) {
   const int tid = threadIdx.x;
   const int d = p.dim;
   const int W = p.mem + B;
-  const uint32_t wmask = (1u << W) - 1u;
+  const int rshift = 32 - W;
   const int r = tid & 31;
   const int c = tid >> 5;
   const int per_thread = d >> 3;
@@ -178,10 +183,12 @@ __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *co
   const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
   const int rw = p.code_stride >> 2;
   const uint32_t st = __ldg(p.start + rec);
+  // column of record r in rows read by lanes with bit 1 clear / set
+  float *col0 = xT + r;
+  float *col1 = xT + (r ^ 4);
   const int end = (c + 1) * per_thread;
   for (int base = c * per_thread; base < end; base += 16) {
-    const int lim = end - base;  // windows of this chunk (<= 16)
-    // image bit offset of the chunk's first window and the word holding it
+    const int lim = end - base;  // windows in this chunk: 16 unless d < 128
     const int pos0 = 32 + base * B - p.mem;
     const int w0 = pos0 >> 5;
     uint32_t w[5];
@@ -190,33 +197,38 @@ __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *co
       const int wi = w0 + u;
       w[u] = wi == 0 ? st : (wi <= rw ? __byte_perm(__ldg(cw + wi - 1), 0, 0x0123) : 0u);
     }
-    // align the chunk to bit 0 of w[0..3]
     const int sh = pos0 & 31;
     uint32_t a[4];
 #pragma unroll
     for (int u = 0; u < 4; u++) a[u] = __funnelshift_l(w[u + 1], w[u], sh);
+    // row base+g is read by accumulator lane (base+g) & 15, whose record half
+    // is bit 1 of that lane; base is even, so that bit is (base>>1 ^ g>>1) & 1
+    const bool fb = (base >> 1) & 1;
+    float *row0 = (fb ? col1 : col0) + (size_t)base * XSTR;
+    float *row1 = (fb ? col0 : col1) + (size_t)base * XSTR;
 #pragma unroll
     for (int g = 0; g < 16; g++) {
-      const int bit = g * B;  // compile-time
-      const int wd = bit >> 5;
-      const uint64_t v = ((uint64_t)a[wd] << 32) | a[wd + 1];
-      const uint32_t win = (uint32_t)(v >> (64 - (bit & 31) - W)) & wmask;
-      const int coord = base + g;
-      // row `coord` is read only by accumulator lane coord & 15, whose record
-      // half is bit 1 of that lane: store the record pre-permuted for it
-      if (g < lim) xT[(size_t)coord * XSTR + (r ^ (((coord >> 1) & 1) << 2))] = ok ? code[win] : 0.0f;
+      const int bit = g * B;  // compile-time: word and offset of window g
+      const uint32_t top = __funnelshift_l(a[(bit >> 5) + 1], a[bit >> 5], bit & 31);
+      const uint32_t win = top >> rshift;
+      float v = 0.0f;
+      if (ok) v = TSMEM ? code[win] : __ldg(code + win);
+      if (g < lim) ((g >> 1) & 1 ? row1 : row0)[g * XSTR] = v;
     }
   }
   if (tid < TN) {
     const bool okr = tid < nr;
-    rs_s[tid] = okr ? __ldg(p.rescale + r0 + tid) : INFINITY;
-    rn_s[tid] = (okr && p.rnorm) ? __ldg(p.rnorm + r0 + tid) : 1.0f;
-    nm_s[tid] = (okr && p.norms) ? __ldg(p.norms + r0 + tid) : 1.0f;
-    ci_s[tid] = (okr && p.cidx) ? __ldg(p.cidx + r0 + tid) : 0u;
+    const float rs = okr ? __ldg(p.rescale + r0 + tid) : INFINITY;
+    const float rn = (okr && p.rnorm) ? __ldg(p.rnorm + r0 + tid) : 1.0f;
+    sc[tid] = rs;
+    sc[TN + tid] = rn;
+    sc[2 * TN + tid] = (okr && p.norms) ? __ldg(p.norms + r0 + tid) : 1.0f;
+    ((uint32_t *)sc)[3 * TN + tid] = (okr && p.cidx) ? __ldg(p.cidx + r0 + tid) : 0u;
+    sc[4 * TN + tid] = fdiv(rn, rs);
   }
 }
 
-template <int B>
+template <int B, bool TSMEM>
 __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int tid = threadIdx.x;
@@ -231,10 +243,11 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   uint64_t *theta = buf + (size_t)TQ * BCAP;                 // TQ
   int *cnt = (int *)(theta + TQ);                            // TQ
   uint32_t *degen = (uint32_t *)(cnt + TQ);                  // TQ
-  float *sc = (float *)(degen + TQ);                         // 2 x 4 x TN scalars
-  int *flag = (int *)(sc + 8 * TN);                          // 4
+  float *theta_s = (float *)(degen + TQ);                    // TQ: score of theta
+  float *sc = theta_s + TQ;                                  // 2 x NSC x TN scalars
+  int *flag = (int *)(sc + 2 * NSC * TN);                    // 4
   float *table = (float *)(flag + 4);                        // optional code table
-  const float *code = p.table_in_smem ? table : p.code;
+  const float *code = TSMEM ? table : p.code;
 
   const int64_t q_base = (int64_t)blockIdx.x * TQ;
   const int split = blockIdx.y;
@@ -255,16 +268,17 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   if (tid < TQ) {
     const int64_t q = q_base + tid;
     theta[tid] = kEmptyKey;
+    theta_s[tid] = -INFINITY;
     cnt[tid] = 0;
     degen[tid] = q < p.nq ? p.degenerate[q] : 1u;
   }
   if (tid == 0) flag[0] = 0;
-  if (p.table_in_smem)
+  if (TSMEM)
     for (int e = tid; e < p.table_len; e += 256) table[e] = __ldg(p.code + e);
   __syncthreads();
   if (ntiles > 0) {
     const int nr0 = (int)min((int64_t)TN, r_end - r_begin);
-    decode_tile<B>(p, code, r_begin, nr0, xT0, sc, sc + TN, sc + 2 * TN, (uint32_t *)(sc + 3 * TN));
+    decode_tile<B, TSMEM>(p, code, r_begin, nr0, xT0, sc);
   }
   __syncthreads();
 
@@ -288,7 +302,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     const int64_t r0 = r_begin + (int64_t)t * TN;
     const int nr = (int)min((int64_t)TN, r_end - r0);
     const float *xT = (t & 1) ? xT1 : xT0;
-    const float *scs = sc + (t & 1) * 4 * TN;
+    const float *scs = sc + (t & 1) * NSC * TN;
 
     // ---- decode-GEMM in paired f32 FMAs: acc[a][c] = lane j, query a, records 2c,2c+1
     float2 acc[8][4];
@@ -359,19 +373,31 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     const float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
 
     // ---- estimator (src/trellis.rs:1517), MIPS norm, threshold test ----
+    // A cheap bound first: a = qm + dot*(rnorm/rescale) (x norm) differs from
+    // the exact score by at most a few roundings (< 5e-7 of its magnitude), so
+    // records below theta - 1e-6*|magnitude| cannot enter the top-k and skip
+    // the exact IEEE division.  Survivors get the exact score and key.
     if (!degen[qsel]) {
       const uint64_t th = theta[qsel];
+      const float ths = theta_s[qsel];
       const int64_t q = q_base + qsel;
+      const uint32_t *cis = (const uint32_t *)(scs + 3 * TN);
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         const int r = rsel + c;
-        if (r < nr) {
-          const float qm = p.n_centroids > 0
-                               ? p.qc[q * p.n_centroids + ((const uint32_t *)(scs + 3 * TN))[r]]
-                               : 0.0f;
-          float s = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
-          if (p.mips) s = fmul(s, scs[2 * TN + r]);
-          const uint64_t key = rank_key(s, (uint32_t)(r0 - r_begin + r));
+        const float qm = p.n_centroids > 0 ? p.qc[q * p.n_centroids + cis[r]] : 0.0f;
+        const float tt = fmul(dot4[c], scs[4 * TN + r]);
+        float a = fadd(qm, tt);
+        float mag = fadd(fabsf(qm), fabsf(tt));
+        if (p.mips) {
+          a = fmul(a, scs[2 * TN + r]);
+          mag = fmul(mag, scs[2 * TN + r]);
+        }
+        const bool maybe = !(a < fsub(fsub(ths, fmul(1e-6f, mag)), 1e-30f));
+        if (maybe && r < nr) {
+          float sx = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
+          if (p.mips) sx = fmul(sx, scs[2 * TN + r]);
+          const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
           if (key > th) {
             const int pos = atomicAdd(&cnt[qsel], 1);
             buf[(size_t)qsel * BCAP + pos] = key;
@@ -386,8 +412,8 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       const int64_t rn0 = r0 + TN;
       const int nrn = (int)min((int64_t)TN, r_end - rn0);
       float *xn = (t & 1) ? xT0 : xT1;
-      float *scn = sc + ((t + 1) & 1) * 4 * TN;
-      decode_tile<B>(p, code, rn0, nrn, xn, scn, scn + TN, scn + 2 * TN, (uint32_t *)(scn + 3 * TN));
+      float *scn = sc + ((t + 1) & 1) * NSC * TN;
+      decode_tile<B, TSMEM>(p, code, rn0, nrn, xn, scn);
     }
     __syncthreads();
 
@@ -396,7 +422,8 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       const int warp = tid >> 5;
       for (int qi = warp; qi < TQ; qi += 8)
         if (cnt[qi] > BCAP - TN)
-          flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi], p.k);
+          flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
+                      &theta_s[qi], p.k);
       __syncthreads();
     }
   }
@@ -407,7 +434,8 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     for (int qi = warp; qi < TQ; qi += 8) {
       const int64_t q = q_base + qi;
       if (cnt[qi] > 0)
-        flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi], p.k);
+        flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
+                    &theta_s[qi], p.k);
       if (q < p.nq) {
         uint32_t *ok = p.part_key + (q * gridDim.y + split) * (int64_t)p.k;
         int64_t *oid = p.part_id + (q * gridDim.y + split) * (int64_t)p.k;
@@ -428,18 +456,18 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   }
 }
 
-template __global__ void flat_scan_kernel<1>(const ScanParams p);
-template __global__ void flat_scan_kernel<2>(const ScanParams p);
-template __global__ void flat_scan_kernel<3>(const ScanParams p);
-template __global__ void flat_scan_kernel<4>(const ScanParams p);
-
-const void *flat_scan_kernel_ptr(int bits) {
+const void *flat_scan_kernel_ptr(int bits, bool table_in_smem) {
+#define UV_SCAN_CASE(b)                                                                   \
+  case b:                                                                                 \
+    return table_in_smem ? (const void *)flat_scan_kernel<b, true>                        \
+                         : (const void *)flat_scan_kernel<b, false>;
   switch (bits) {
-    case 1: return (const void *)flat_scan_kernel<1>;
-    case 2: return (const void *)flat_scan_kernel<2>;
-    case 3: return (const void *)flat_scan_kernel<3>;
-    case 4: return (const void *)flat_scan_kernel<4>;
+    UV_SCAN_CASE(1)
+    UV_SCAN_CASE(2)
+    UV_SCAN_CASE(3)
+    UV_SCAN_CASE(4)
   }
+#undef UV_SCAN_CASE
   return nullptr;
 }
 
@@ -515,8 +543,8 @@ size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem
   b += 2 * (size_t)dim * XSTR * 4;                      // x-bar tiles
   b += (((size_t)dim * QSTR + 3) & ~(size_t)3) * 4;     // queries
   b += (size_t)TQ * KCAP * 8 + (size_t)TQ * BCAP * 8;   // top-k + buffers
-  b += (size_t)TQ * 8 + (size_t)TQ * 4 * 2;             // theta, cnt, degenerate
-  b += 8 * (size_t)TN * 4 + 16;                         // scalars, flag
+  b += (size_t)TQ * 8 + (size_t)TQ * 4 * 3;             // theta, cnt, degenerate, theta_s
+  b += 2 * NSC * (size_t)TN * 4 + 16;                   // scalars, flag
   if (table_in_smem) b += (size_t)table_len * 4;
   return b;
 }

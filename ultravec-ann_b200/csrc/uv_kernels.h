@@ -93,7 +93,7 @@ struct MergeParams {
 };
 
 __global__ void prep_queries_kernel(const PrepParams p);
-const void *flat_scan_kernel_ptr(int bits);
+const void *flat_scan_kernel_ptr(int bits, bool table_in_smem);
 __global__ void merge_topk_kernel(const MergeParams p);
 
 // scan tiling constants shared with the host planner
