@@ -152,6 +152,26 @@ int uv_index_export(const uv_index *index, uint8_t *codes, uint32_t *start, floa
 /* encode_digest of the stored records. */
 int uv_index_digest(const uv_index *index, uint64_t *digest, void *stream);
 
+/* uv_index_search without any device allocation.  No counterpart in the
+ * reference: it exists for callers that must not allocate device memory while
+ * they serve queries -- a process that reserves its whole GPU memory budget at
+ * start-up, or a latency-bound thread that cannot accept the device-wide
+ * synchronization that cudaMalloc/cudaFree may bring.  Same arguments and
+ * results as uv_index_search, with these limits:
+ *   - queries, ids_out and scores_out (if given) must be device memory of the
+ *     index's GPU; host buffers are rejected (copying them would allocate);
+ *   - per-call scratch comes from one 16 MiB array that the library keeps on
+ *     every GPU that loads it, until the process exits; a query batch whose
+ *     scratch (about nq * (4*dim + 8 + 12*k) bytes) does not fit is rejected
+ *     with UV_EINVAL -- search fewer queries per call;
+ *   - the first call on a device looks up that array's device address, so
+ *     make it before any stream capture;
+ *   - all calls on a device share the array: calls whose GPU work overlaps
+ *     (different streams or threads without ordering) race and corrupt each
+ *     other's results; order them on one stream. */
+int uv_index_search_noalloc(const uv_index *index, const float *queries, int64_t nq, int32_t k,
+                            int32_t mode, int64_t *ids_out, float *scores_out, void *stream);
+
 /* Drop every record but keep the device capacity: the state of a freshly
  * constructed codec after reserve(len) (src/trellis.rs:2100-2102). */
 int uv_index_clear(uv_index *index);

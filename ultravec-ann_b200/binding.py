@@ -30,7 +30,7 @@ SYMBOLS = [
     "uv_index_set_centroids", "uv_index_reserve", "uv_index_add", "uv_index_add_batch",
     "uv_index_len", "uv_index_dimensions", "uv_index_mem_bytes", "uv_index_search",
     "uv_index_export", "uv_index_digest", "uv_index_clear", "uv_topk_merge",
-    "uv_profile_enable", "uv_profile_read", "uv_set_tuning",
+    "uv_profile_enable", "uv_profile_read", "uv_set_tuning", "uv_index_search_noalloc",
 ]
 
 
@@ -92,6 +92,7 @@ def lib():
             "uv_index_clear": (C.c_int, [vp]),
             "uv_profile_enable": (C.c_int, [i32]),
             "uv_set_tuning": (C.c_int, [C.c_char_p, i64]),
+            "uv_index_search_noalloc": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp]),
             "uv_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(i64)]),
         }
         for name, (res, args) in sig.items():

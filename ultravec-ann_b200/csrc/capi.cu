@@ -965,3 +965,220 @@ int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Search without device allocation (uv_index_search_noalloc).
+//
+// Some callers cannot allocate device memory at search time: a serving
+// process that reserves its whole GPU budget at start-up, or a latency-bound
+// thread that cannot accept the device-wide synchronization cudaMalloc and
+// cudaFree may imply.  This entry point takes its per-call scratch from one
+// fixed file-scope device array instead, carved into the same buffers
+// uv_index_search allocates.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+constexpr int kNoAllocMaxDevices = 64;
+void *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// The device address of g_noalloc_scratch on the current device, looked up
+// once per device (the caller made that device current).
+int noalloc_scratch(int dev, unsigned char **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(UV_EINVAL, "device ordinal out of range");
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(UV_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = (unsigned char *)g_noalloc_ptr[dev];
+  return UV_OK;
+}
+
+size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace
+
+extern "C" {
+
+int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq, int32_t k,
+                            int32_t mode, int64_t *ids_out, float *scores_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  if (d % 16 != 0) return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  // every buffer must already be on this GPU: staging would allocate
+  for (const void *ptr : {(const void *)queries, (const void *)ids_out, (const void *)scores_out}) {
+    if (ptr == nullptr) continue;
+    bool on_dev = false;
+    UV_TRY(classify(ptr, dev, &on_dev));
+    if (!on_dev)
+      return fail(UV_EINVAL, "uv_index_search_noalloc needs queries and outputs in device memory");
+  }
+  unsigned char *arena = nullptr;
+  UV_TRY(noalloc_scratch(dev, &arena));
+  if (nq == 0) return UV_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = ix->n;
+  const int dim_pad = (d + 3) & ~3;
+  const int ncen = std::max(1, ix->n_centroids);
+  const int rw = c->code_stride / 4;
+  int img_words = 4 + rw + 3;
+  if ((img_words & 1) == 0) img_words++;
+  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
+  const size_t smem = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
+  if (smem > 227 * 1024)
+    return fail(UV_EUNSUPPORTED, "flat scan tile for this dim exceeds shared memory (dim <= 384)");
+  const void *scan_k = uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
+  UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 1;
+  UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
+  per_sm = std::max(per_sm, 1);
+  const int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;
+  const int64_t slots = (int64_t)sm_count(dev) * per_sm;
+  const int64_t max_splits =
+      std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(2048 / k, 32), n / 1024));
+  int64_t splits = 1;
+  double best_eff = 0.0;
+  for (int64_t sp = 1; sp <= max_splits; sp++) {
+    const int64_t ctas = qtiles * sp;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double eff = (double)ctas / (double)(waves * slots);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      splits = sp;
+    }
+    if (eff >= 0.9) break;
+  }
+  // carve the arena; fewer splits when the batch would not fit
+  auto layout = [&](int64_t sp) {
+    size_t b = 0;
+    b += align256(sizeof(float) * (size_t)nq * dim_pad);
+    b += align256(sizeof(float) * (size_t)nq * ncen);
+    b += align256(sizeof(uint32_t) * (size_t)nq);
+    if (scores_out == nullptr) b += align256(sizeof(float) * (size_t)nq * k);
+    b += align256(sizeof(uint32_t) * (size_t)nq * sp * k);
+    b += align256(sizeof(int64_t) * (size_t)nq * sp * k);
+    return b;
+  };
+  while (splits > 1 && layout(splits) > kNoAllocScratchBytes) splits--;
+  if (layout(splits) > kNoAllocScratchBytes)
+    return fail(UV_EINVAL, "this query batch needs " + std::to_string(layout(1)) +
+                               " bytes of scratch but the no-allocation search has " +
+                               std::to_string(kNoAllocScratchBytes) +
+                               "; search fewer queries per call");
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    unsigned char *ptr = arena + off;
+    off += align256(bytes);
+    return ptr;
+  };
+  float *q_r = (float *)take(sizeof(float) * (size_t)nq * dim_pad);
+  float *qc = (float *)take(sizeof(float) * (size_t)nq * ncen);
+  uint32_t *degen = (uint32_t *)take(sizeof(uint32_t) * (size_t)nq);
+  float *d_scores = scores_out;
+  if (d_scores == nullptr) d_scores = (float *)take(sizeof(float) * (size_t)nq * k);
+  uint32_t *part_key = (uint32_t *)take(sizeof(uint32_t) * (size_t)nq * splits * k);
+  int64_t *part_id = (int64_t *)take(sizeof(int64_t) * (size_t)nq * splits * k);
+
+  // 1) prepare queries
+  {
+    uvb::PrepParams pp;
+    std::memset(&pp, 0, sizeof(pp));
+    pp.dim = d;
+    pp.dim_pad = dim_pad;
+    pp.nq = nq;
+    pp.queries = queries;
+    pp.rot = c->rot;
+    pp.centroids = ix->centroids;
+    pp.n_centroids = ix->n_centroids;
+    pp.q_r = q_r;
+    pp.qc = qc;
+    pp.degenerate = degen;
+    const size_t psmem = (size_t)(dim_pad + 4) * 4 * 8;
+    UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
+    void *args[] = {&pp};
+    UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,
+                           psmem, st));
+  }
+  // 2) scan with a per-split top-k
+  if (n == 0) {
+    UV_CK(cudaMemsetAsync(part_key, 0, sizeof(uint32_t) * nq * splits * k, st));
+    UV_CK(cudaMemsetAsync(part_id, 0xff, sizeof(int64_t) * nq * splits * k, st));
+  } else {
+    uvb::ScanParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    sp.dim = d;
+    sp.mem = c->cfg.mem;
+    sp.bits = c->cfg.bits;
+    sp.nq = nq;
+    sp.n = n;
+    sp.q_r = q_r;
+    sp.q_stride = dim_pad;
+    sp.qc = qc;
+    sp.n_centroids = ix->n_centroids;
+    sp.degenerate = degen;
+    sp.codes = ix->codes;
+    sp.code_stride = c->code_stride;
+    sp.start = ix->start;
+    sp.rescale = ix->rescale;
+    sp.rnorm = ix->rnorm;
+    sp.norms = ix->norms;
+    sp.cidx = ix->cidx;
+    sp.code = c->d_table;
+    sp.table_len = c->table_len;
+    sp.table_in_smem = table_smem ? 1 : 0;
+    sp.img_words = img_words;
+    sp.mips = mode == UV_SEARCH_MIPS ? 1 : 0;
+    sp.k = k;
+    sp.ids = ix->ids;
+    sp.id_base = 0;
+    sp.part_key = part_key;
+    sp.part_id = part_id;
+    void *args[] = {&sp};
+    UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)qtiles, (unsigned)splits), dim3(256), args,
+                           smem, st));
+  }
+  // 3) merge the splits
+  {
+    uvb::MergeParams m;
+    std::memset(&m, 0, sizeof(m));
+    m.nq = nq;
+    m.n_lists = (int)splits;
+    m.k_in = k;
+    m.k = k;
+    int pow2 = 32;
+    while (pow2 < (int)splits * k) pow2 <<= 1;
+    m.pow2 = pow2;
+    const size_t per_warp = (size_t)pow2 * 16;
+    m.warps = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / per_warp));
+    m.in_key = part_key;
+    m.in_id = part_id;
+    m.out_id = ids_out;
+    m.out_score = d_scores;
+    const size_t msmem = per_warp * m.warps;
+    UV_CK(cudaFuncSetAttribute(uvb::merge_topk_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    const int grid = (int)((nq + m.warps - 1) / m.warps);
+    void *args[] = {&m};
+    UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_kernel, dim3(grid), dim3(32 * m.warps),
+                           args, msmem, st));
+  }
+  return UV_OK;
+}
+
+}  // extern "C"
