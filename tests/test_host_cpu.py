@@ -1,0 +1,139 @@
+"""CPU-only checks of the product side: the library loads and exports every
+entry point the header declares; the host sharding and top-k merge logic
+(including a world_size-2 gloo run); the bench's input generator."""
+from __future__ import annotations
+
+import os
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (REPO / "include" / "ultravec_b200.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|void|const char \*)\s*(uv_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol(uv):
+    declared = header_symbols()
+    assert len(declared) >= 30
+    lib = uv.lib()
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    assert sorted(declared) == sorted(uv.SYMBOLS)
+    assert lib.uv_abi_version() == 1
+
+
+def test_codec_create_without_gpu_fails_cleanly(uv):
+    """No panic across the ABI: without a device the call returns a status."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(uv.UVError) as e:
+        uv.Codec(128, 2, 8)
+    assert e.value.code in (1, 3)
+
+
+def test_bad_configs_are_rejected_before_any_device_work(uv):
+    import ctypes as C
+
+    cfg = uv.binding.uv_config()
+    for dim, bits, mem in [(0, 2, 8), (128, 0, 8), (128, 5, 8), (128, 2, 0), (128, 4, 21)]:
+        uv.lib().uv_config_default(C.byref(cfg), dim, bits, mem)
+        h = C.c_void_p()
+        assert uv.lib().uv_codec_create(C.byref(cfg), C.byref(h)) == 1
+        assert uv.lib().uv_last_error()
+
+
+def test_shard_ranges_partition_the_rows(uv):
+    from ultravec_ann_b200.shard import shard_range
+
+    for n in (0, 1, 7, 1000, 1_000_000):
+        for world in (1, 2, 3, 8):
+            spans = [shard_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_host_merge_orders_by_score_then_id(uv):
+    from ultravec_ann_b200.shard import merge_host
+
+    ids = np.array([[[5, 9, -1], [2, 3, 4]]], np.int64)
+    sc = np.array([[[3.0, 1.0, -np.inf], [3.0, 2.0, 1.0]]], np.float32)
+    oi, os_ = merge_host(ids, sc, 4)
+    assert list(oi[0]) == [2, 5, 3, 4]
+    assert list(os_[0]) == [3.0, 3.0, 2.0, 1.0]
+
+
+def _gloo_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    import sys
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    sys.path.insert(0, str(REPO / "tests"))
+    sys.path.insert(0, str(REPO))
+    import oracle as O
+    from fixtures import rand_rows
+    from ultravec_ann_b200_loader import load
+
+    uv = load()
+    from ultravec_ann_b200.shard import gather_topk, merge_host, shard_range
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rows = rand_rows(600, 64, 3)
+    qs = rand_rows(12, 64, 4)
+    lo, hi = shard_range(len(rows), rank, world)
+    codec = O.Codec(64, 2, 6)
+    enc = codec.encode_batch(rows[lo:hi])
+    ids, sc = codec.search_topk(enc, qs, 10, norms=O.l2_norms(rows[lo:hi]))
+    ids = np.where(ids >= 0, ids + lo, -1)
+    g_ids, g_sc = gather_topk(torch.from_numpy(ids), torch.from_numpy(sc), 10, dist, merge_host)
+    if rank == 0:
+        full = codec.encode_batch(rows)
+        want_ids, want_sc = codec.search_topk(full, qs, 10, norms=O.l2_norms(rows))
+        ok = np.array_equal(g_ids.numpy(), want_ids) and np.array_equal(
+            g_sc.numpy().view(np.uint32), want_sc.view(np.uint32))
+        Path(result_dir, "ok").write_text("1" if ok else "0")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
+    """world_size 2 on CPU: shard, local top-k (the oracle stands in for the
+    device scan), all-gather, merge == the top-k of the whole index."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_gloo_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    assert (tmp_path / "ok").read_text() == "1"
+
+
+def test_bench_generator_shapes_and_centering():
+    import sys
+
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    base, query = bench.make_data(5000, 50)
+    assert base.shape == (5000, 128) and query.shape == (50, 128)
+    assert abs(float(base.mean(0, dtype=np.float64).max())) < 1e-3
+    # the raw zeros (about 40%) become each column's minimum after centering
+    zeros = np.mean(base == base.min(0, keepdims=True))
+    assert 0.35 < zeros < 0.45
