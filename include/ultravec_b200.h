@@ -185,7 +185,9 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
 
 /* Launch-shape tuning, no counterpart in the reference (results never depend
  * on it): "scan_splits" fixes the number of record ranges each query tile is
- * split into (0 = automatic).  Process-wide; returns UV_EINVAL for an unknown
+ * split into (0 = automatic); "encode_back" places the encoder's
+ * back-pointers for codecs created afterwards (0 automatic, 1 global scratch,
+ * 2 shared memory whenever one row's array fits).  Process-wide; returns UV_EINVAL for an unknown
  * key. */
 int uv_set_tuning(const char *key, int64_t value);
 

@@ -278,3 +278,19 @@ def test_device_tensors_round_trip(uv, oracle):
     torch.cuda.synchronize()
     ids_h, _ = ix.search(qs.cpu().numpy(), 10, mips=True)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_h)
+
+
+@pytest.mark.parametrize("dim,bits,k", [(1024, 2, 10), (1024, 1, 100), (1024, 4, 17),
+                                        (2048, 2, 10), (400, 3, 33)])
+def test_flat_search_wide_rows(uv, oracle, dim, bits, k):
+    """Rows wider than 384 take the K-chunked scan (128-coordinate chunks)."""
+    rows = rand_rows(1500, dim, dim + bits)
+    qs = rand_rows(70, dim, dim + bits + 1)
+    g, ix = _index(uv, dim, bits, 8, rows)
+    o = oracle.Codec(dim, bits, 8)
+    enc = o.encode_batch(rows)
+    for mips in (True, False):
+        ids, scores = ix.search(qs, k, mips=mips)
+        wids, wscores = o.search_topk(enc, qs, k, norms=oracle.l2_norms(rows) if mips else None)
+        np.testing.assert_array_equal(ids, wids)
+        np.testing.assert_array_equal(_bits(scores), _bits(wscores))

@@ -346,6 +346,7 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   p.code = c->d_table;
   p.rot = c->rot;
   p.lambda = c->cfg.branch_lambda;
+  p.one2 = make_float2(1.0f, 1.0f);
   p.start_bits = c->cfg.start_bits;
   p.rescale_bits = c->cfg.rescale_bits;
   p.centroids = centroids;
@@ -820,10 +821,14 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   int img_words = 4 + rw + 3;
   if ((img_words & 1) == 0) img_words++;
   const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
-  const size_t smem = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
-  if (smem > 227 * 1024)
-    return fail(UV_EUNSUPPORTED, "flat scan tile for this dim exceeds shared memory (dim <= 384)");
-  const void *scan_k = uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
+  // rows up to 384 keep the whole query tile resident; wider rows stream it in
+  // 128-coordinate chunks (chunked_scan_kernel)
+  const bool chunked = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem) > 227 * 1024;
+  const bool small_k = k <= 32;
+  const size_t smem = chunked ? uvb::chunked_scan_smem_bytes(c->table_len, table_smem, small_k)
+                              : uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
+  const void *scan_k = chunked ? uvb::chunked_scan_kernel_ptr(c->cfg.bits, table_smem, small_k)
+                               : uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
   UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 1;
   UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
@@ -883,7 +888,9 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
     sp.id_base = 0;
     sp.part_key = part_key;
     sp.part_id = part_id;
-    void *args[] = {&sp};
+    uvb::ScanWork work;
+    std::memset(&work, 0, sizeof(work));
+    void *args[] = {&sp, &work};
     ProfScope ps("flat_scan", st);
     UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)qtiles, (unsigned)splits), dim3(256), args,
                            smem, st));
@@ -925,6 +932,11 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
 
 int uv_set_tuning(const char *key, int64_t value) {
   if (key == nullptr) return fail(UV_EINVAL, "null key");
+  if (std::strcmp(key, "encode_back") == 0) {
+    if (value < 0 || value > 2) return fail(UV_EINVAL, "encode_back must be 0, 1 or 2");
+    uvb::g_encode_back_mode = (int)value;
+    return UV_OK;
+  }
   if (std::strcmp(key, "scan_splits") == 0) {
     if (value < 0 || value > 4096) return fail(UV_EINVAL, "scan_splits must be 0..4096");
     g_scan_splits = value;

@@ -184,6 +184,12 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     // ---- forward: add-compare-select over d steps ----
     // metric (xi - c)^2 as paired IEEE ops: (xi + (-c)) then d*d, then the
     // predecessor cost added -- three roundings per window, as the reference.
+    // A paired multiply whose only use is a paired add is fused into one
+    // paired FMA by the code generator even from the .rn forms (one rounding
+    // instead of two, measured on sm_100a).  The add is therefore written as
+    // fma(m, one, cost) with `one` a run-time 1.0f (a kernel parameter, read
+    // as an operand from the constant bank): m * 1 is exact, so the result is
+    // round(cost + m) and nothing is left to contract.
     float *cur = cost0, *nxt = cost1;
     float last[SPT];
     uint32_t word = 0;
@@ -210,7 +216,7 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
         for (int k = 0; k < NE; k += 2) {
           const float2 dd = __fadd2_rn(xi2, ncode[j][k / 2]);
           const float2 m = aniso ? __fmul2_rn(__fmul2_rn(wi2, dd), dd) : __fmul2_rn(dd, dd);
-          const float2 c = __fadd2_rn(cp[g][k / 2], m);
+          const float2 c = __ffma2_rn(m, p.one2, cp[g][k / 2]);
           if (k == 0) {
             best[j] = c.x;
           } else if (c.x < best[j]) {
@@ -391,6 +397,8 @@ const void *pick_kernel(int B, int WPT, bool smem_back) {
 
 }  // namespace
 
+int g_encode_back_mode = 0;  // uv_set_tuning("encode_back"): 0 auto, 1 global, 2 shared
+
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) {
   if (bits < 1 || bits > 4) {
     *why = "bits must be 1..4";
@@ -430,12 +438,12 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
   bool smem = false;
   int teams = tpc;
   // largest team count (whole warps) that fits
-  for (int tc = tpc; tc >= tpc_warp && tc >= 1; tc -= tpc_warp) {
+  for (int tc = tpc; tc >= tpc_warp && tc >= 1 && g_encode_back_mode != 1; tc -= tpc_warp) {
     if (fits(team_words_smem, tc)) {
       const int64_t cta_bytes = team_words_smem * 4 * tc;
       const int threads = (int)(tc * T);
       const int ctas = (int)std::min<int64_t>(228 * 1024 / std::max<int64_t>(cta_bytes, 1), 2048 / threads);
-      if ((int64_t)ctas * threads >= 256) {
+      if ((int64_t)ctas * threads >= 256 || g_encode_back_mode == 2) {
         smem = true;
         teams = tc;
       }

@@ -85,19 +85,21 @@ constexpr int XSTR = TN + 4;  // padded row of the transposed record tile (LDS.1
 constexpr int KCAP = 128;     // top-k capacity per query
 constexpr int BCAP = 64;      // candidate buffer per query (power of two)
 
-// Sort 64 keys descending (bitonic, one warp, two keys per lane).
-__device__ __forceinline__ void warp_sort_desc_64(uint64_t *a) {
+// Sort N keys descending (bitonic, one warp).
+template <int N>
+__device__ __forceinline__ void warp_sort_desc(uint64_t *a) {
   const int lane = threadIdx.x & 31;
-  for (int size = 2; size <= BCAP; size <<= 1) {
+  for (int size = 2; size <= N; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      const int pi = lane;
-      const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
-      const int jx = i + stride;
-      const bool desc = (i & size) == 0;
-      const uint64_t x = a[i], y = a[jx];
-      if (desc ? (x < y) : (x > y)) {
-        a[i] = y;
-        a[jx] = x;
+      for (int pi = lane; pi < N / 2; pi += 32) {
+        const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
+        const int jx = i + stride;
+        const bool desc = (i & size) == 0;
+        const uint64_t x = a[i], y = a[jx];
+        if (desc ? (x < y) : (x > y)) {
+          a[i] = y;
+          a[jx] = x;
+        }
       }
       __syncwarp();
     }
@@ -119,35 +121,36 @@ __device__ __forceinline__ int count_larger(const uint64_t *a, int n, uint64_t x
 
 // Merge one query's candidate buffer into its sorted top-k list (one warp).
 // Keys are unique, so every element's merged position is its own rank plus
-// the number of larger keys in the other list; positions >= KCAP drop out.
+// the number of larger keys in the other list; positions >= KC_ drop out.
+template <int KC_, int BC_>
 __device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *cnt, uint64_t *theta,
                                             float *theta_s, int k) {
   const int lane = threadIdx.x & 31;
   const int m = *cnt;
-  for (int i = m + lane; i < BCAP; i += 32) buf[i] = kEmptyKey;
+  for (int i = m + lane; i < BC_; i += 32) buf[i] = kEmptyKey;
   __syncwarp();
-  warp_sort_desc_64(buf);
-  uint64_t tv[KCAP / 32], bv[BCAP / 32];
-  int tp[KCAP / 32], bp[BCAP / 32];
+  warp_sort_desc<BC_>(buf);
+  uint64_t tv[KC_ / 32], bv[BC_ / 32];
+  int tp[KC_ / 32], bp[BC_ / 32];
 #pragma unroll
-  for (int u = 0; u < KCAP / 32; u++) {
+  for (int u = 0; u < KC_ / 32; u++) {
     const int i = lane + 32 * u;
     tv[u] = top[i];
-    tp[u] = i + count_larger(buf, BCAP, tv[u]);
+    tp[u] = i + count_larger(buf, BC_, tv[u]);
   }
 #pragma unroll
-  for (int u = 0; u < BCAP / 32; u++) {
+  for (int u = 0; u < BC_ / 32; u++) {
     const int i = lane + 32 * u;
     bv[u] = buf[i];
-    bp[u] = i + count_larger(top, KCAP, bv[u]);
+    bp[u] = i + count_larger(top, KC_, bv[u]);
   }
   __syncwarp();
 #pragma unroll
-  for (int u = 0; u < KCAP / 32; u++)
-    if (tv[u] != kEmptyKey && tp[u] < KCAP) top[tp[u]] = tv[u];
+  for (int u = 0; u < KC_ / 32; u++)
+    if (tv[u] != kEmptyKey && tp[u] < KC_) top[tp[u]] = tv[u];
 #pragma unroll
-  for (int u = 0; u < BCAP / 32; u++)
-    if (bv[u] != kEmptyKey && bp[u] < KCAP) top[bp[u]] = bv[u];
+  for (int u = 0; u < BC_ / 32; u++)
+    if (bv[u] != kEmptyKey && bp[u] < KC_) top[bp[u]] = bv[u];
   __syncwarp();
   if (lane == 0) {
     *cnt = 0;
@@ -162,22 +165,23 @@ __device__ __forceinline__ void flush_query(uint64_t *top, uint64_t *buf, int *c
 // the ratio g = rnorm / rescale used by the cheap pre-filter below.
 constexpr int NSC = 5;
 
-// Decode one record tile into x-bar (transposed) and stage its scalars.
-// Thread (r, c) decodes windows [c*d/8, (c+1)*d/8) of record r in chunks of
-// 16, reading the packed stream straight from global memory: window i is the
-// field [i*B, i*B + M + B) of [start (M bits) || codes] (src/trellis.rs:
-// 1576-1600), i.e. bits [32 + i*B - M, ...) of the image whose first 32-bit
-// word is the start state.
+// Decode coordinates [k0, k0 + kc) of one record tile into x-bar (transposed,
+// rows relative to k0) and, when `scalars` is set, stage its scalars.
+// Thread (r, c) decodes windows [k0 + c*kc/8, k0 + (c+1)*kc/8) of record r in
+// chunks of 16, reading the packed stream straight from global memory:
+// window i is the field [i*B, i*B + M + B) of [start (M bits) || codes]
+// (src/trellis.rs:1576-1600), i.e. bits [32 + i*B - M, ...) of the image whose
+// first 32-bit word is the start state.  k0 is a multiple of 16.
 template <int B, bool TSMEM>
 __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *code, int64_t r0,
-                                            int nr, float *xT, float *sc) {
+                                            int nr, float *xT, float *sc, int k0, int kc,
+                                            bool scalars) {
   const int tid = threadIdx.x;
-  const int d = p.dim;
   const int W = p.mem + B;
   const int rshift = 32 - W;
   const int r = tid & 31;
   const int c = tid >> 5;
-  const int per_thread = d >> 3;
+  const int per_thread = kc >> 3;
   const bool ok = r < nr;
   const int64_t rec = ok ? r0 + r : r0;
   const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
@@ -188,8 +192,8 @@ __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *co
   float *col1 = xT + (r ^ 4);
   const int end = (c + 1) * per_thread;
   for (int base = c * per_thread; base < end; base += 16) {
-    const int lim = end - base;  // windows in this chunk: 16 unless d < 128
-    const int pos0 = 32 + base * B - p.mem;
+    const int lim = end - base;  // windows in this chunk: 16 unless kc < 128
+    const int pos0 = 32 + (k0 + base) * B - p.mem;
     const int w0 = pos0 >> 5;
     uint32_t w[5];
 #pragma unroll
@@ -216,7 +220,7 @@ __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *co
       if (g < lim) ((g >> 1) & 1 ? row1 : row0)[g * XSTR] = v;
     }
   }
-  if (tid < TN) {
+  if (scalars && tid < TN) {
     const bool okr = tid < nr;
     const float rs = okr ? __ldg(p.rescale + r0 + tid) : INFINITY;
     const float rn = (okr && p.rnorm) ? __ldg(p.rnorm + r0 + tid) : 1.0f;
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   __syncthreads();
   if (ntiles > 0) {
     const int nr0 = (int)min((int64_t)TN, r_end - r_begin);
-    decode_tile<B, TSMEM>(p, code, r_begin, nr0, xT0, sc);
+    decode_tile<B, TSMEM>(p, code, r_begin, nr0, xT0, sc, 0, d, true);
   }
   __syncthreads();
 
@@ -413,7 +417,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       const int nrn = (int)min((int64_t)TN, r_end - rn0);
       float *xn = (t & 1) ? xT0 : xT1;
       float *scn = sc + ((t + 1) & 1) * NSC * TN;
-      decode_tile<B, TSMEM>(p, code, rn0, nrn, xn, scn);
+      decode_tile<B, TSMEM>(p, code, rn0, nrn, xn, scn, 0, d, true);
     }
     __syncthreads();
 
@@ -422,7 +426,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       const int warp = tid >> 5;
       for (int qi = warp; qi < TQ; qi += 8)
         if (cnt[qi] > BCAP - TN)
-          flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
+          flush_query<KCAP, BCAP>(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
                       &theta_s[qi], p.k);
       __syncthreads();
     }
@@ -434,7 +438,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     for (int qi = warp; qi < TQ; qi += 8) {
       const int64_t q = q_base + qi;
       if (cnt[qi] > 0)
-        flush_query(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
+        flush_query<KCAP, BCAP>(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
                     &theta_s[qi], p.k);
       if (q < p.nq) {
         uint32_t *ok = p.part_key + (q * gridDim.y + split) * (int64_t)p.k;
@@ -469,6 +473,313 @@ const void *flat_scan_kernel_ptr(int bits, bool table_in_smem) {
   }
 #undef UV_SCAN_CASE
   return nullptr;
+}
+
+// ---------------------------------------------------------------------------
+// K-chunked scan: the same tile computation as flat_scan_kernel for rows
+// wider than the query tile can hold in shared memory, and for IVF lists.
+// Coordinates are processed in chunks of KCH = 128: for each (record tile,
+// chunk) step the query chunk and the decoded record chunk are staged in one
+// buffer while the previous step's buffer feeds the FMAs, with one barrier
+// per step.  The 16-lane accumulators persist across chunks, so the FMA order
+// per lane is still ascending blocks -- the same association.
+// ---------------------------------------------------------------------------
+constexpr int KCH = kScanKChunk;
+
+template <int KC_, int BC_>
+struct ChunkLayout {
+  static constexpr size_t xT = 0;                                   // 2 x KCH x XSTR f32
+  static constexpr size_t qT = xT + 2 * KCH * XSTR * 4;             // 2 x KCH x QSTR f32
+  static constexpr size_t top = qT + 2 * KCH * QSTR * 4;            // TQ x KC_ u64
+  static constexpr size_t buf = top + TQ * KC_ * 8;                 // TQ x BC_ u64
+  static constexpr size_t theta = buf + TQ * BC_ * 8;               // TQ u64
+  static constexpr size_t qrow = theta + TQ * 8;                    // TQ i64 (query row)
+  static constexpr size_t slot = qrow + TQ * 8;                     // TQ i64 (output slot)
+  static constexpr size_t theta_s = slot + TQ * 8;                  // TQ f32
+  static constexpr size_t qm = theta_s + TQ * 4;                    // TQ f32
+  static constexpr size_t cnt = qm + TQ * 4;                        // TQ i32
+  static constexpr size_t degen = cnt + TQ * 4;                     // TQ u32
+  static constexpr size_t sc = degen + TQ * 4;                      // 2 x NSC x TN f32
+  static constexpr size_t flag = sc + 2 * NSC * TN * 4;             // 4 i32
+  static constexpr size_t table = flag + 16;
+};
+
+template <int B, bool TSMEM, int KC_, int BC_>
+__global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p, const ScanWork w) {
+  using L = ChunkLayout<KC_, BC_>;
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int tid = threadIdx.x;
+  const int d = p.dim;
+  float *const xT0 = (float *)(sm + L::xT);
+  float *const xT1 = xT0 + KCH * XSTR;
+  float *const qT0 = (float *)(sm + L::qT);
+  float *const qT1 = qT0 + KCH * QSTR;
+  uint64_t *top = (uint64_t *)(sm + L::top);
+  uint64_t *buf = (uint64_t *)(sm + L::buf);
+  uint64_t *theta = (uint64_t *)(sm + L::theta);
+  int64_t *qrow = (int64_t *)(sm + L::qrow);
+  int64_t *slot = (int64_t *)(sm + L::slot);
+  float *theta_s = (float *)(sm + L::theta_s);
+  float *qm_s = (float *)(sm + L::qm);
+  int *cnt = (int *)(sm + L::cnt);
+  uint32_t *degen = (uint32_t *)(sm + L::degen);
+  float *sc = (float *)(sm + L::sc);
+  int *flag = (int *)(sm + L::flag);
+  float *table = (float *)(sm + L::table);
+  const float *code = TSMEM ? table : p.code;
+
+  // ---- this CTA's work: record range and up to 32 (query, slot) pairs ----
+  int64_t r_begin, r_end;
+  int nql;
+  if (!w.ivf) {
+    const int64_t q_base = (int64_t)blockIdx.x * TQ;
+    const int split = blockIdx.y;
+    r_begin = p.n * split / gridDim.y;
+    r_end = p.n * (split + 1) / gridDim.y;
+    nql = (int)min((int64_t)TQ, p.nq - q_base);
+    if (tid < TQ) {
+      const int64_t q = q_base + tid;
+      qrow[tid] = tid < nql ? q : -1;
+      slot[tid] = tid < nql ? q * gridDim.y + split : -1;
+      qm_s[tid] = 0.0f;
+    }
+  } else {
+    const int item = blockIdx.x;
+    const int list = w.item_list[item];
+    const int pair0 = w.item_pair[item];
+    nql = w.item_npairs[item];
+    r_begin = w.list_off[list];
+    r_end = w.list_off[list + 1];
+    if (tid < TQ) {
+      qrow[tid] = tid < nql ? (int64_t)w.pair_query[pair0 + tid] : -1;
+      slot[tid] = tid < nql ? (int64_t)w.pair_slot[pair0 + tid] : -1;
+      qm_s[tid] = (tid < nql && w.pair_qm) ? w.pair_qm[pair0 + tid] : 0.0f;
+    }
+  }
+  for (int e = tid; e < TQ * KC_; e += 256) top[e] = kEmptyKey;
+  if (tid < TQ) {
+    theta[tid] = kEmptyKey;
+    theta_s[tid] = -INFINITY;
+    cnt[tid] = 0;
+  }
+  if (tid == 0) flag[0] = 0;
+  if (TSMEM)
+    for (int e = tid; e < p.table_len; e += 256) table[e] = __ldg(p.code + e);
+  __syncthreads();
+  if (tid < TQ) degen[tid] = qrow[tid] >= 0 ? p.degenerate[qrow[tid]] : 1u;
+
+  const int nchunks = (d + KCH - 1) / KCH;
+  const int ntiles = (int)((r_end - r_begin + TN - 1) / TN);
+  const int64_t steps = (int64_t)ntiles * nchunks;
+
+  // stage the query chunk [k0, k0 + kc) pre-permuted per reading lane
+  auto load_q = [&](float *qT, int k0, int kc) {
+    for (int e = tid; e < TQ * kc; e += 256) {
+      const int qi = e / kc, i = e - qi * kc;
+      const int jm = i & 15;
+      const int qmk = (((jm >> 3) & 1) << 2) | (((jm >> 2) & 1) << 1) | (jm & 1);
+      const int64_t q = qrow[qi];
+      qT[(size_t)i * QSTR + (qi ^ qmk)] =
+          q >= 0 ? __ldg(p.q_r + q * (int64_t)p.q_stride + k0 + i) : 0.0f;
+    }
+  };
+  if (steps > 0) {
+    __syncthreads();  // qrow visible
+    const int kc0 = min(KCH, d);
+    load_q(qT0, 0, kc0);
+    decode_tile<B, TSMEM>(p, code, r_begin, (int)min((int64_t)TN, r_end - r_begin), xT0, sc, 0,
+                          kc0, true);
+  }
+  __syncthreads();
+
+  const int j = tid & 15;
+  const int pp = tid >> 4;
+  const int pq = pp >> 2;
+  const int pn = pp & 3;
+  const int qmask = (((j >> 3) & 1) << 2) | (((j >> 2) & 1) << 1) | (j & 1);
+  const int rhalf = ((j >> 1) & 1) << 2;
+  const int qsel = pq * 8 + qmask;
+  const int rsel = pn * 8 + rhalf;
+
+  float2 acc[8][4];
+  for (int64_t s = 0; s < steps; s++) {
+    const int tile = (int)(s / nchunks);
+    const int ch = (int)(s - (int64_t)tile * nchunks);
+    const int bsel = (int)(s & 1);
+    const int64_t r0 = r_begin + (int64_t)tile * TN;
+    const int nr = (int)min((int64_t)TN, r_end - r0);
+    const int kc = min(KCH, d - ch * KCH);
+    if (ch == 0) {
+#pragma unroll
+      for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[a][c] = make_float2(0.0f, 0.0f);
+    }
+    {
+      const float *xT = bsel ? xT1 : xT0;
+      const float *qT = bsel ? qT1 : qT0;
+      const int kb = kc >> 4;
+#pragma unroll 2
+      for (int b = 0; b < kb; b++) {
+        const int coord = (b << 4) + j;
+        const float *qr = qT + (size_t)coord * QSTR + pq * 8;
+        const float *xr = xT + (size_t)coord * XSTR + pn * 8;
+        const float4 x0 = *(const float4 *)(xr);
+        const float4 x1 = *(const float4 *)(xr + 4);
+        const float4 q0 = *(const float4 *)(qr);
+        const float4 q1 = *(const float4 *)(qr + 4);
+        const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const float2 xv[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w),
+                              make_float2(x1.x, x1.y), make_float2(x1.z, x1.w)};
+#pragma unroll
+        for (int a = 0; a < 8; a++) {
+          const float2 q2 = make_float2(qv[a], qv[a]);
+#pragma unroll
+          for (int c = 0; c < 4; c++) acc[a][c] = __ffma2_rn(q2, xv[c], acc[a][c]);
+        }
+      }
+    }
+    if (ch == nchunks - 1) {
+      // transpose-reduction (xor 8, 4, 1, 2) -- see flat_scan_kernel
+      float2 l1[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          float2 o;
+          o.x = __shfl_xor_sync(0xffffffffu, acc[a + 4][c].x, 8);
+          o.y = __shfl_xor_sync(0xffffffffu, acc[a + 4][c].y, 8);
+          l1[a][c] = __fadd2_rn(acc[a][c], o);
+        }
+      float2 l2[2][4];
+#pragma unroll
+      for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          float2 o;
+          o.x = __shfl_xor_sync(0xffffffffu, l1[a + 2][c].x, 4);
+          o.y = __shfl_xor_sync(0xffffffffu, l1[a + 2][c].y, 4);
+          l2[a][c] = __fadd2_rn(l1[a][c], o);
+        }
+      float2 l3[4];
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        float2 o;
+        o.x = __shfl_xor_sync(0xffffffffu, l2[1][c].x, 1);
+        o.y = __shfl_xor_sync(0xffffffffu, l2[1][c].y, 1);
+        l3[c] = __fadd2_rn(l2[0][c], o);
+      }
+      float2 dot2[2];
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        float2 o;
+        o.x = __shfl_xor_sync(0xffffffffu, l3[c + 2].x, 2);
+        o.y = __shfl_xor_sync(0xffffffffu, l3[c + 2].y, 2);
+        dot2[c] = __fadd2_rn(l3[c], o);
+      }
+      const float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
+      const float *scs = sc + (tile & 1) * NSC * TN;
+      if (!degen[qsel]) {
+        const uint64_t th = theta[qsel];
+        const float ths = theta_s[qsel];
+        const int64_t q = qrow[qsel];
+        const uint32_t *cis = (const uint32_t *)(scs + 3 * TN);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int r = rsel + c;
+          const float qm = w.ivf ? qm_s[qsel]
+                                 : (p.n_centroids > 0 ? p.qc[q * p.n_centroids + cis[r]] : 0.0f);
+          const float tt = fmul(dot4[c], scs[4 * TN + r]);
+          float a = fadd(qm, tt);
+          float mag = fadd(fabsf(qm), fabsf(tt));
+          if (p.mips) {
+            a = fmul(a, scs[2 * TN + r]);
+            mag = fmul(mag, scs[2 * TN + r]);
+          }
+          const bool maybe = !(a < fsub(fsub(ths, fmul(1e-6f, mag)), 1e-30f));
+          if (maybe && r < nr) {
+            float sx = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
+            if (p.mips) sx = fmul(sx, scs[2 * TN + r]);
+            const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
+            if (key > th) {
+              const int pos = atomicAdd(&cnt[qsel], 1);
+              buf[(size_t)qsel * BC_ + pos] = key;
+              if (pos == BC_ - TN) flag[0] = tile + 1;
+            }
+          }
+        }
+      }
+    }
+    // ---- stage the next step into the other buffer ----
+    if (s + 1 < steps) {
+      const int64_t sn = s + 1;
+      const int tn = (int)(sn / nchunks);
+      const int chn = (int)(sn - (int64_t)tn * nchunks);
+      const int64_t rn0 = r_begin + (int64_t)tn * TN;
+      const int kcn = min(KCH, d - chn * KCH);
+      load_q(bsel ? qT0 : qT1, chn * KCH, kcn);
+      decode_tile<B, TSMEM>(p, code, rn0, (int)min((int64_t)TN, r_end - rn0), bsel ? xT0 : xT1,
+                            sc + (tn & 1) * NSC * TN, chn * KCH, kcn, chn == 0);
+    }
+    __syncthreads();
+    if (ch == nchunks - 1 && flag[0] == tile + 1) {
+      const int warp = tid >> 5;
+      for (int qi = warp; qi < TQ; qi += 8)
+        if (cnt[qi] > BC_ - TN)
+          flush_query<KC_, BC_>(top + (size_t)qi * KC_, buf + (size_t)qi * BC_, &cnt[qi],
+                                &theta[qi], &theta_s[qi], p.k);
+      __syncthreads();
+    }
+  }
+
+  // ---- final merge and write-out ----
+  {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int qi = warp; qi < TQ; qi += 8) {
+      if (cnt[qi] > 0)
+        flush_query<KC_, BC_>(top + (size_t)qi * KC_, buf + (size_t)qi * BC_, &cnt[qi],
+                              &theta[qi], &theta_s[qi], p.k);
+      const int64_t sl = slot[qi];
+      if (sl >= 0) {
+        uint32_t *ok = p.part_key + sl * (int64_t)p.k;
+        int64_t *oid = p.part_id + sl * (int64_t)p.k;
+        for (int i = lane; i < p.k; i += 32) {
+          const uint64_t key = top[(size_t)qi * KC_ + i];
+          if (key == kEmptyKey) {
+            ok[i] = 0u;
+            oid[i] = -1;
+          } else {
+            const int64_t rec = r_begin + rank_key_index(key);
+            ok[i] = (uint32_t)(key >> 32);
+            oid[i] = p.ids ? p.ids[rec] : p.id_base + rec;
+          }
+        }
+      }
+    }
+  }
+}
+
+const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k) {
+#define UV_CH_CASE(b)                                                                      \
+  case b:                                                                                  \
+    if (small_k)                                                                           \
+      return table_in_smem ? (const void *)chunked_scan_kernel<b, true, 32, 32>            \
+                           : (const void *)chunked_scan_kernel<b, false, 32, 32>;          \
+    return table_in_smem ? (const void *)chunked_scan_kernel<b, true, 128, 64>             \
+                         : (const void *)chunked_scan_kernel<b, false, 128, 64>;
+  switch (bits) {
+    UV_CH_CASE(1)
+    UV_CH_CASE(2)
+    UV_CH_CASE(3)
+    UV_CH_CASE(4)
+  }
+#undef UV_CH_CASE
+  return nullptr;
+}
+
+size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k) {
+  const size_t base = small_k ? ChunkLayout<32, 32>::table : ChunkLayout<128, 64>::table;
+  return base + (table_in_smem ? (size_t)table_len * 4 : 0);
 }
 
 // ---------------------------------------------------------------------------

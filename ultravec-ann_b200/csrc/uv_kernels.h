@@ -18,6 +18,7 @@ struct EncodeParams {
   const float *code;        // 2^(mem+bits) table
   RotParams rot;
   float lambda;
+  float2 one2;              // (1.0f, 1.0f), passed at run time (see the forward loop)
   int start_bits, rescale_bits;
   const float *centroids;   // flat centering (assign among n_centroids)
   int n_centroids;
@@ -41,6 +42,8 @@ struct EncodePlan {
   size_t smem_bytes;
   const void *kernel;
 };
+
+extern int g_encode_back_mode;  // placement of back-pointers; never changes results
 
 // 0 ok, 1 invalid, 2 unsupported (message in *why)
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
@@ -82,6 +85,21 @@ struct ScanParams {
   int64_t *part_id;
 };
 
+// Work items of the chunked scan.  Flat (ivf == 0): the grid is query tiles x
+// record splits, as for flat_scan_kernel.  IVF: item i scans the records of
+// list item_list[i] for up to 32 (query, probe) pairs starting at
+// item_pair[i]; each pair writes its top-k to output slot pair_slot[j].
+struct ScanWork {
+  int ivf;
+  const int32_t *item_list;
+  const int32_t *item_pair;
+  const int32_t *item_npairs;
+  const int64_t *list_off;    // nlist + 1
+  const int32_t *pair_query;  // query row of q_r
+  const int32_t *pair_slot;   // output slot: query * nprobe + probe rank
+  const float *pair_qm;       // <u, c_list> (centered lists) or null
+};
+
 struct MergeParams {
   int64_t nq;
   int n_lists, k_in, k, pow2, warps;
@@ -94,6 +112,11 @@ struct MergeParams {
 
 __global__ void prep_queries_kernel(const PrepParams p);
 const void *flat_scan_kernel_ptr(int bits, bool table_in_smem);
+// K-chunked scan for wide rows and IVF lists; small_k selects the 32-entry
+// top-k (k <= 32) that keeps two CTAs per SM.
+const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k);
+size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k);
+constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
 
 // scan tiling constants shared with the host planner
