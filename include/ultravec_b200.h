@@ -200,6 +200,77 @@ int uv_set_tuning(const char *key, int64_t value);
 int uv_profile_enable(int32_t on);
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches);
 
+/* ---- IVF: coarse quantizer, posting lists of trellis records ----------- */
+
+/* Every dot below is the reference's sequential f32 fold from -0.0 (product
+ * and sum rounded separately), so centroids, assignments, probes and scores
+ * are bit-identical to the reference's CPU results. */
+
+/* bench.rs:298-349 kmeans: nlist centroids of the unit-normalized rows.
+ * Initial centroids are units[splitmix64(seed) % n] (with replacement); each
+ * of `iters` Lloyd rounds (the reference runs 5) assigns every unit to the
+ * first strict maximum of <u, c_j>, then sets each non-empty list's centroid
+ * to the sum of its units in row order from +0.0 divided by the count.
+ * rows n x dim and centroids_out nlist x dim, host or device. */
+int uv_kmeans(int32_t device, const float *rows, int64_t n, int32_t dim, int32_t nlist,
+              uint64_t seed, int32_t iters, float *centroids_out, void *stream);
+
+/* ivf.rs:405-421: assign[i] = the first strict maximum over j of
+ * <rows[i] / max(|rows[i]|, EPS), c_j> (index 0 when every dot is NaN). */
+int uv_ivf_assign(int32_t device, const float *rows, int64_t n, int32_t dim,
+                  const float *centroids, int32_t nlist, uint32_t *assign_out, void *stream);
+
+typedef struct uv_ivf uv_ivf;
+
+/* IvfIndex (ivf.rs:155-170) over one codec: nlist centroids (copied) and one
+ * posting list per centroid.  centered != 0 is ULTRAVEC_IVF_CENTER=1
+ * (ivf.rs:98-150): each list's codec holds that list's centroid, so records
+ * are residuals to it (rnorm kept) and scores add qm = <u, c_list>. */
+int uv_ivf_create(const uv_codec *codec, const float *centroids, int32_t nlist, int32_t centered,
+                  uv_ivf **out);
+int uv_ivf_destroy(uv_ivf *ivf);
+
+/* IvfIndex::build (ivf.rs:171-205): bucket the rows by assign (NULL computes
+ * it as uv_ivf_assign does), rows in input order inside each list, encode
+ * every list.  ids NULL gives id = row index.  Replaces earlier content. */
+int uv_ivf_build(uv_ivf *ivf, const float *rows, int64_t n, const uint32_t *assign,
+                 const int64_t *ids, void *stream);
+
+int uv_ivf_len(const uv_ivf *ivf, int64_t *len);
+int uv_ivf_nlist(const uv_ivf *ivf, int32_t *nlist);
+/* Sum over the lists of the trellis mem_bytes (src/trellis.rs:2184-2201). */
+int uv_ivf_mem_bytes(const uv_ivf *ivf, int64_t *bytes);
+
+/* probe (ivf.rs:209-223): the min(nprobe, nlist) lists of best exact cosine
+ * (lib.rs:240-248) to each raw query, ordered (cosine desc, list asc; the
+ * reference leaves exact ties in any order).  lists_out is nq x nprobe;
+ * columns past nlist hold -1. */
+int uv_ivf_probe(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t nprobe,
+                 int32_t *lists_out, void *stream);
+
+/* search (ivf.rs:229-239): each probed list scores its records with the list
+ * codec (qm + rnorm * (dot / rescale)); the best k over the probed lists,
+ * ranked as uv_index_search.  1 <= k <= 128. */
+int uv_ivf_search(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t k,
+                  int32_t nprobe, int64_t *ids_out, float *scores_out, void *stream);
+
+/* search_with_rerank (ivf.rs:248-274): the best r = max(rdepth, k) <= 128 by
+ * the codec score, then exact fp32 cosine(query, db[id]) of those r, best k
+ * by (cosine desc, id asc).  db is n_db x dim, host or device; an id >= n_db
+ * returns UV_EINVAL. */
+int uv_ivf_search_rerank(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t k,
+                         int32_t nprobe, int32_t rdepth, const float *db, int64_t n_db,
+                         int64_t *ids_out, float *scores_out, void *stream);
+
+/* The posting lists as one list-major SoA (the on-disk layout): list_off
+ * (nlist + 1 entries), ids, codes (dense code_bytes per record), start,
+ * rescale, rnorm.  NULL skips a field; host or device. */
+int uv_ivf_export(const uv_ivf *ivf, int64_t *list_off, int64_t *ids, uint8_t *codes,
+                  uint32_t *start, float *rescale, float *rnorm, void *stream);
+
+/* XOR-folded per-record FNV-1a digest of every posting (as uv_digest). */
+int uv_ivf_digest(const uv_ivf *ivf, uint64_t *digest, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,9 @@ def lib():
             "uvo_ivf_search_topk": (None, [_vp, _f32p, C.c_int, _i64p, _i64p, _u8p, _u32p,
                                            _f32p, _f32p, C.c_int, _f32p, C.c_int64, C.c_int,
                                            C.c_int, _i64p, _f32p, C.c_int]),
+            "uvo_ivf_search_rerank": (None, [_vp, _f32p, C.c_int, _i64p, _i64p, _u8p, _u32p,
+                                             _f32p, _f32p, C.c_int, _f32p, C.c_int64, C.c_int,
+                                             C.c_int, C.c_int, _f32p, _i64p, _f32p, C.c_int]),
             "uvo_rand_unit": (None, [C.c_int64, C.c_int, C.c_uint64, _f32p]),
         }
         for name, (res, args) in sig.items():
@@ -260,6 +263,23 @@ class Codec:
             np.ascontiguousarray(index["rescale"], np.float32),
             np.ascontiguousarray(index["rnorm"], np.float32), int(centered), queries, nq,
             nprobe, k, out_ids, scores, threads)
+        return out_ids, scores
+
+    def ivf_search_rerank(self, centroids, list_off, ids, index, centered, queries, nprobe, k,
+                          rdepth, db, threads=0):
+        """ivf.rs:248-274: codec top-max(rdepth, k), then exact cosine vs db."""
+        queries = np.ascontiguousarray(queries, np.float32)
+        nq = queries.shape[0]
+        out_ids = np.empty((nq, k), np.int64)
+        scores = np.empty((nq, k), np.float32)
+        cen = np.ascontiguousarray(centroids, np.float32)
+        lib().uvo_ivf_search_rerank(
+            self.h, cen, cen.shape[0], np.ascontiguousarray(list_off, np.int64),
+            np.ascontiguousarray(ids, np.int64), np.ascontiguousarray(index["codes"], np.uint8),
+            np.ascontiguousarray(index["start"], np.uint32),
+            np.ascontiguousarray(index["rescale"], np.float32),
+            np.ascontiguousarray(index["rnorm"], np.float32), int(centered), queries, nq,
+            nprobe, k, rdepth, np.ascontiguousarray(db, np.float32), out_ids, scores, threads)
         return out_ids, scores
 
 

@@ -1106,6 +1106,49 @@ void uvo_ivf_search_topk(const uvo_codec *c, const float *centroids, int nlist,
     }
 }
 
+/* ivf.rs:248-274 search_with_rerank: the global top-r (r = max(rdepth, k))
+ * by the codec score (uvo_ivf_search_topk), then the exact fp32 cosine of
+ * each candidate against db (lib.rs:240-248), best k by (cosine desc, id
+ * asc; the reference leaves exact ties unordered). */
+void uvo_ivf_search_rerank(const uvo_codec *c, const float *centroids, int nlist,
+                           const int64_t *list_off, const int64_t *ids, const uint8_t *codes,
+                           const uint32_t *start, const float *rescale, const float *rnorm,
+                           int centered, const float *queries, int64_t nq, int nprobe, int k,
+                           int rdepth, const float *db, int64_t *ids_out, float *scores_out,
+                           int threads) {
+    int d = c->dim;
+    int r = rdepth > k ? rdepth : k;
+    int64_t *cand = (int64_t *)malloc(sizeof(int64_t) * (size_t)(nq > 0 ? nq : 1) * r);
+    uvo_ivf_search_topk(c, centroids, nlist, list_off, ids, codes, start, rescale, rnorm, centered,
+                        queries, nq, nprobe, r, cand, NULL, threads);
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+        cand_t *h = (cand_t *)malloc(sizeof(cand_t) * (size_t)r);
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t qi = 0; qi < nq; qi++) {
+            const float *q = queries + (size_t)qi * d;
+            int nh = 0;
+            for (int j = 0; j < r; j++) {
+                int64_t id = cand[(size_t)qi * r + j];
+                if (id < 0) continue;
+                const float *x = db + (size_t)id * d;
+                float dot = seq_dot(q, x, d);
+                float na = uvo_l2_norm(q, d), nb = uvo_l2_norm(x, d);
+                float cs = (na < F32_EPS || nb < F32_EPS) ? 0.0f : dot / (na * nb);
+                heap_push_bounded(h, &nh, r, cs, id);
+            }
+            emit_topk(h, nh, k, ids_out + (size_t)qi * k, scores_out ? scores_out + (size_t)qi * k : NULL);
+        }
+        free(h);
+    }
+    free(cand);
+}
+
 /* bench.rs:1019 norms[i] = l2_norm(db[i]) over a batch */
 void uvo_l2_norms(const float *rows, int64_t n, int dim, float *out, int threads) {
 #ifdef _OPENMP

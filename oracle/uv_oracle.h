@@ -104,6 +104,13 @@ void uvo_ivf_search_topk(const uvo_codec *c, const float *centroids, int nlist,
                          int centered, const float *queries, int64_t nq, int nprobe, int k,
                          int64_t *ids_out, float *scores_out, int threads);
 
+void uvo_ivf_search_rerank(const uvo_codec *c, const float *centroids, int nlist,
+                           const int64_t *list_off, const int64_t *ids, const uint8_t *codes,
+                           const uint32_t *start, const float *rescale, const float *rnorm,
+                           int centered, const float *queries, int64_t nq, int nprobe, int k,
+                           int rdepth, const float *db, int64_t *ids_out, float *scores_out,
+                           int threads);
+
 /* synthetic inputs used by the reference's own tests (trellis.rs:2387-2403) */
 void uvo_rand_unit(int64_t n, int dim, uint64_t seed, float *out);
 

@@ -31,6 +31,9 @@ SYMBOLS = [
     "uv_index_len", "uv_index_dimensions", "uv_index_mem_bytes", "uv_index_search",
     "uv_index_export", "uv_index_digest", "uv_index_clear", "uv_topk_merge",
     "uv_profile_enable", "uv_profile_read", "uv_set_tuning", "uv_index_search_noalloc",
+    "uv_kmeans", "uv_ivf_assign", "uv_ivf_create", "uv_ivf_destroy", "uv_ivf_build",
+    "uv_ivf_len", "uv_ivf_nlist", "uv_ivf_mem_bytes", "uv_ivf_probe", "uv_ivf_search",
+    "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest",
 ]
 
 
@@ -94,6 +97,20 @@ def lib():
             "uv_set_tuning": (C.c_int, [C.c_char_p, i64]),
             "uv_index_search_noalloc": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp]),
             "uv_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(i64)]),
+            "uv_kmeans": (C.c_int, [i32, vp, i64, i32, i32, u64, i32, vp, vp]),
+            "uv_ivf_assign": (C.c_int, [i32, vp, i64, i32, vp, i32, vp, vp]),
+            "uv_ivf_create": (C.c_int, [vp, vp, i32, i32, vpp]),
+            "uv_ivf_destroy": (C.c_int, [vp]),
+            "uv_ivf_build": (C.c_int, [vp, vp, i64, vp, vp, vp]),
+            "uv_ivf_len": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_ivf_nlist": (C.c_int, [vp, C.POINTER(i32)]),
+            "uv_ivf_mem_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_ivf_probe": (C.c_int, [vp, vp, i64, i32, vp, vp]),
+            "uv_ivf_search": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp]),
+            "uv_ivf_search_rerank": (C.c_int, [vp, vp, i64, i32, i32, i32, vp, i64, vp, vp,
+                                               vp]),
+            "uv_ivf_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp]),
+            "uv_ivf_digest": (C.c_int, [vp, C.POINTER(u64), vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -340,6 +357,117 @@ class Index:
     def digest(self) -> int:
         h = C.c_uint64()
         check(lib().uv_index_digest(self.h, C.byref(h), None))
+        return h.value
+
+
+# ------------------------------------------------------------------- IVF ---
+
+def kmeans(rows, nlist: int, seed: int = 42, iters: int = 5, device: int = 0):
+    """bench.rs:298-349 k-means of the unit-normalized rows (nlist x dim)."""
+    rows = _f32(rows)
+    out = _Alloc(rows)((nlist, rows.shape[1]), np.float32)
+    check(lib().uv_kmeans(device, _ptr(rows), rows.shape[0], rows.shape[1], nlist, seed, iters,
+                          _ptr(out), _stream(rows)))
+    return out
+
+
+def ivf_assign(rows, centroids, device: int = 0):
+    """ivf.rs:405-421: first strict maximum of <row / |row|, c_j>."""
+    rows, cen = _f32(rows), _f32(centroids)
+    out = _Alloc(rows)((rows.shape[0],), np.uint32)
+    check(lib().uv_ivf_assign(device, _ptr(rows), rows.shape[0], rows.shape[1], _ptr(cen),
+                              cen.shape[0], _ptr(out), _stream(rows)))
+    return out
+
+
+class IvfIndex:
+    """IvfIndex (ivf.rs:155-274) over one codec: centroids + posting lists."""
+
+    def __init__(self, codec: Codec, centroids, centered: bool = False):
+        cen = _f32(centroids)
+        h = C.c_void_p()
+        check(lib().uv_ivf_create(codec.h, _ptr(cen), cen.shape[0], 1 if centered else 0,
+                                  C.byref(h)))
+        self.h, self.codec, self.centered = h, codec, centered
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uv_ivf_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def build(self, rows, assign=None, ids=None):
+        """IvfIndex::build (ivf.rs:171-205); assign None computes it."""
+        rows = _f32(rows)
+        if assign is not None and not _is_torch(assign):
+            assign = np.ascontiguousarray(assign, np.uint32)
+        if ids is not None and not _is_torch(ids):
+            ids = np.ascontiguousarray(ids, np.int64)
+        check(lib().uv_ivf_build(self.h, _ptr(rows), rows.shape[0], _ptr(assign), _ptr(ids),
+                                 _stream(rows)))
+
+    def __len__(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_ivf_len(self.h, C.byref(n)))
+        return n.value
+
+    @property
+    def nlist(self) -> int:
+        n = C.c_int32()
+        check(lib().uv_ivf_nlist(self.h, C.byref(n)))
+        return n.value
+
+    def mem_bytes(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_ivf_mem_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def probe(self, queries, nprobe: int):
+        queries = _f32(queries)
+        out = _Alloc(queries)((queries.shape[0], nprobe), np.int32)
+        check(lib().uv_ivf_probe(self.h, _ptr(queries), queries.shape[0], nprobe, _ptr(out),
+                                 _stream(queries)))
+        return out
+
+    def search(self, queries, k: int, nprobe: int):
+        """search (ivf.rs:229-239): top-k (ids, scores) per query."""
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        alloc = _Alloc(queries)
+        ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+        check(lib().uv_ivf_search(self.h, _ptr(queries), nq, k, nprobe, _ptr(ids), _ptr(scores),
+                                  _stream(queries)))
+        return ids, scores
+
+    def search_with_rerank(self, queries, k: int, nprobe: int, rdepth: int, db):
+        """search_with_rerank (ivf.rs:248-274): exact fp32 cosine of the top-rdepth."""
+        queries, db = _f32(queries), _f32(db)
+        nq = queries.shape[0]
+        alloc = _Alloc(queries)
+        ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+        check(lib().uv_ivf_search_rerank(self.h, _ptr(queries), nq, k, nprobe, rdepth, _ptr(db),
+                                         db.shape[0], _ptr(ids), _ptr(scores),
+                                         _stream(queries)))
+        return ids, scores
+
+    def export(self):
+        n, cb = len(self), self.codec.code_bytes
+        out = dict(list_off=np.zeros(self.nlist + 1, np.int64), ids=np.zeros(n, np.int64),
+                   codes=np.zeros((n, cb), np.uint8), start=np.zeros(n, np.uint32),
+                   rescale=np.zeros(n, np.float32), rnorm=np.zeros(n, np.float32))
+        check(lib().uv_ivf_export(self.h, _ptr(out["list_off"]), _ptr(out["ids"]),
+                                  _ptr(out["codes"]), _ptr(out["start"]), _ptr(out["rescale"]),
+                                  _ptr(out["rnorm"]), None))
+        return out
+
+    def digest(self) -> int:
+        h = C.c_uint64()
+        check(lib().uv_ivf_digest(self.h, C.byref(h), None))
         return h.value
 
 

@@ -4,209 +4,19 @@
 // stages host buffers through stream-ordered device allocations, plans and
 // launches the kernels, and turns every failure into a status code plus a
 // thread-local message.  No exception or abort crosses the ABI.
-#include "ultravec_b200.h"
+#include "capi_internal.h"
 
-#include <algorithm>
-#include <cstring>
-#include <mutex>
-#include <new>
-#include <string>
-#include <vector>
-
-#include "codebook.h"
-#include "uv_kernels.h"
-#include "uv_util.h"
-
-namespace {
+namespace uvcapi {
 
 thread_local std::string g_err;
-
-int fail(int code, const std::string &msg) {
-  g_err = msg;
-  return code;
-}
-
-#define UV_CK(call)                                                                  \
-  do {                                                                               \
-    cudaError_t e_ = (call);                                                         \
-    if (e_ != cudaSuccess)                                                           \
-      return fail(e_ == cudaErrorMemoryAllocation ? UV_ENOMEM : UV_ECUDA,            \
-                  std::string(#call) + ": " + cudaGetErrorString(e_));               \
-  } while (0)
-
-#define UV_TRY(expr)        \
-  do {                      \
-    int rc_ = (expr);       \
-    if (rc_ != UV_OK) return rc_; \
-  } while (0)
-
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
-// Where a caller pointer lives.  Returns UV_EINVAL for device memory of
-// another GPU.
-int classify(const void *p, int device, bool *on_device) {
-  *on_device = false;
-  if (p == nullptr) return UV_OK;
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();
-    return UV_OK;  // unregistered host memory
-  }
-  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
-    if (a.type == cudaMemoryTypeDevice && a.device != device)
-      return fail(UV_EINVAL, "device buffer belongs to another GPU");
-    *on_device = true;
-  }
-  return UV_OK;
-}
-
-// Stream-ordered scratch freed at scope exit (on the same stream).
-struct Scratch {
-  cudaStream_t st;
-  std::vector<void *> ptrs;
-  explicit Scratch(cudaStream_t s) : st(s) {}
-  ~Scratch() {
-    for (void *p : ptrs) cudaFreeAsync(p, st);
-  }
-  template <class T>
-  int alloc(T **out, size_t count) {
-    *out = nullptr;
-    if (count == 0) count = 1;
-    void *p = nullptr;
-    cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), st);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return fail(UV_ENOMEM, std::string("cudaMallocAsync: ") + cudaGetErrorString(e));
-    }
-    ptrs.push_back(p);
-    *out = (T *)p;
-    return UV_OK;
-  }
-};
-
-// A caller input viewed on the device: used in place when it is device
-// memory, otherwise copied through scratch.
-template <class T>
-int stage_in(const T *src, size_t count, int device, Scratch &sc, const T **dev) {
-  bool on_dev = false;
-  UV_TRY(classify(src, device, &on_dev));
-  if (src == nullptr || on_dev) {
-    *dev = src;
-    return UV_OK;
-  }
-  T *d = nullptr;
-  UV_TRY(sc.alloc(&d, count));
-  UV_CK(cudaMemcpyAsync(d, src, count * sizeof(T), cudaMemcpyHostToDevice, sc.st));
-  *dev = d;
-  return UV_OK;
-}
-
-// A caller output: written in place on the device, or produced in scratch
-// and copied back (see Outputs::finish).
-struct Outputs {
-  struct Pending {
-    void *host;
-    const void *dev;
-    size_t bytes;
-  };
-  std::vector<Pending> pend;
-  template <class T>
-  int stage(T *dst, size_t count, int device, Scratch &sc, T **dev) {
-    bool on_dev = false;
-    UV_TRY(classify(dst, device, &on_dev));
-    if (dst == nullptr || on_dev) {
-      *dev = dst;
-      return UV_OK;
-    }
-    T *d = nullptr;
-    UV_TRY(sc.alloc(&d, count));
-    pend.push_back({(void *)dst, (const void *)d, count * sizeof(T)});
-    *dev = d;
-    return UV_OK;
-  }
-  int finish(cudaStream_t st) {
-    for (auto &p : pend) UV_CK(cudaMemcpyAsync(p.host, p.dev, p.bytes, cudaMemcpyDeviceToHost, st));
-    if (!pend.empty()) UV_CK(cudaStreamSynchronize(st));
-    return UV_OK;
-  }
-};
-
-// ---- kernel timing hook (uv_profile_enable / uv_profile_read) ----
-struct ProfRec {
-  const char *name;
-  cudaEvent_t a, b;
-};
 std::mutex g_prof_mu;
-int64_t g_scan_splits = 0;  // uv_set_tuning("scan_splits")
+int64_t g_scan_splits = 0;
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
 
-struct ProfScope {
-  const char *name;
-  cudaStream_t st;
-  cudaEvent_t a = nullptr, b = nullptr;
-  ProfScope(const char *n, cudaStream_t s) : name(n), st(s) {
-    if (!g_prof_on) return;
-    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
-      a = b = nullptr;
-      return;
-    }
-    cudaEventRecord(a, st);
-  }
-  ~ProfScope() {
-    if (a == nullptr) return;
-    cudaEventRecord(b, st);
-    std::lock_guard<std::mutex> lk(g_prof_mu);
-    g_prof.push_back({name, a, b});
-  }
-};
+}  // namespace uvcapi
 
-template <class T>
-int grow(T **buf, int64_t old_n, int64_t new_cap, cudaStream_t st) {
-  T *nb = nullptr;
-  UV_CK(cudaMallocAsync((void **)&nb, (size_t)std::max<int64_t>(new_cap, 1) * sizeof(T), st));
-  if (*buf != nullptr && old_n > 0)
-    UV_CK(cudaMemcpyAsync(nb, *buf, (size_t)old_n * sizeof(T), cudaMemcpyDeviceToDevice, st));
-  if (*buf != nullptr) cudaFreeAsync(*buf, st);
-  *buf = nb;
-  return UV_OK;
-}
-
-}  // namespace
-
-struct uv_codec {
-  uv_config cfg;
-  int code_bytes = 0, code_stride = 0, table_len = 0;
-  std::vector<float> h_table;
-  uvb::RotationHost rot_host;
-  float *d_table = nullptr;
-  float *d_signs = nullptr;
-  uvb::RotParams rot;
-  uvb::EncodePlan plan;
-  int plan_status = 0;
-  std::string plan_why;
-};
-
-struct uv_index {
-  const uv_codec *codec = nullptr;
-  int64_t n = 0, cap = 0;
-  uint8_t *codes = nullptr;
-  uint32_t *start = nullptr;
-  float *rescale = nullptr, *rnorm = nullptr, *norms = nullptr;
-  uint32_t *cidx = nullptr;
-  int64_t *ids = nullptr;
-  float *centroids = nullptr;
-  int n_centroids = 0;
-};
+using namespace uvcapi;
 
 extern "C" {
 
@@ -327,14 +137,17 @@ int uv_codec_record_bytes(const uv_codec *c, int32_t *code_bytes, int32_t *start
 
 }  // extern "C"
 
-namespace {
+namespace uvcapi {
 
 // Encode rows already on the device into device outputs (codes at
-// code_stride).  The common core of uv_encode, uv_encode_rotated and
-// uv_index_add.
+// code_stride).  The common core of uv_encode, uv_encode_rotated,
+// uv_index_add and the IVF build (list centroids, rows read through
+// row_index in list-major order).
 int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
                   int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
-                  float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc) {
+                  float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,
+                  const float *list_centroids, const uint32_t *row_list,
+                  const int64_t *row_index) {
   if (c->plan_status == 1) return fail(UV_EINVAL, c->plan_why);
   if (c->plan_status != 0) return fail(UV_EUNSUPPORTED, c->plan_why);
   if (n == 0) return UV_OK;
@@ -360,6 +173,9 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   p.cidx = cidx;
   p.norms = norms;
   p.rotated_input = rotated ? 1 : 0;
+  p.list_centroids = list_centroids;
+  p.row_list = row_list;
+  p.row_index = row_index;
   int grid = 0;
   UV_CK(uvb::encode_grid(c->plan, n, &grid));
   if (!c->plan.back_smem) {
@@ -374,7 +190,7 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   return UV_OK;
 }
 
-}  // namespace
+}  // namespace uvcapi
 
 extern "C" {
 
@@ -715,7 +531,7 @@ int uv_index_digest(const uv_index *ix, uint64_t *digest, void *stream) {
 
 }  // extern "C"
 
-namespace {
+namespace uvcapi {
 
 int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_key,
                  const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
@@ -754,7 +570,40 @@ int sm_count(int dev) {
   return sms;
 }
 
-}  // namespace
+// Normalize and rotate the queries (trellis.rs:2120-2183): q_r (rotated
+// unit), qc (dots with the flat centroids), degenerate flags, and optionally
+// the unrotated unit query u.  All buffers have rows of dim rounded up to 4.
+int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *centroids,
+                int n_centroids, float *q_r, float *qc, uint32_t *degen, float *u,
+                cudaStream_t st) {
+  const int d = c->cfg.dim;
+  const int dim_pad = (d + 3) & ~3;
+  uvb::PrepParams pp;
+  std::memset(&pp, 0, sizeof(pp));
+  pp.dim = d;
+  pp.dim_pad = dim_pad;
+  pp.nq = nq;
+  pp.queries = d_q;
+  pp.rot = c->rot;
+  pp.centroids = centroids;
+  pp.n_centroids = n_centroids;
+  pp.q_r = q_r;
+  pp.qc = qc;
+  pp.degenerate = degen;
+  pp.u = u;
+  const size_t smem = (size_t)(dim_pad + 4) * 4 * 8;
+  UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem));
+  const int grid =
+      (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(c->cfg.device) * 8));
+  void *args[] = {&pp};
+  ProfScope ps("prep_queries", st);
+  UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args, smem,
+                         st));
+  return UV_OK;
+}
+
+}  // namespace uvcapi
 
 extern "C" {
 
@@ -792,28 +641,7 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
   UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
   UV_TRY(sc.alloc(&degen, (size_t)nq));
-  {
-    uvb::PrepParams pp;
-    std::memset(&pp, 0, sizeof(pp));
-    pp.dim = d;
-    pp.dim_pad = dim_pad;
-    pp.nq = nq;
-    pp.queries = d_q;
-    pp.rot = c->rot;
-    pp.centroids = ix->centroids;
-    pp.n_centroids = ix->n_centroids;
-    pp.q_r = q_r;
-    pp.qc = qc;
-    pp.degenerate = degen;
-    const size_t smem = (size_t)(dim_pad + 4) * 4 * 8;
-    UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
-    void *args[] = {&pp};
-    ProfScope ps("prep_queries", st);
-    UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,
-                           smem, st));
-  }
+  UV_TRY(prep_launch(c, d_q, nq, ix->centroids, ix->n_centroids, q_r, qc, degen, nullptr, st));
   // 2) scan with a per-split top-k
   const int64_t n = ix->n;
   int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;

@@ -1,0 +1,228 @@
+// capi_internal.h -- helpers shared by the extern "C" translation units
+// (capi.cu: codec and flat index; capi_ivf.cu: the IVF index).  Internal.
+#pragma once
+
+#include "ultravec_b200.h"
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "codebook.h"
+#include "uv_kernels.h"
+#include "uv_util.h"
+
+namespace uvcapi {
+
+extern thread_local std::string g_err;
+
+inline int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+
+#define UV_CK(call)                                                                  \
+  do {                                                                               \
+    cudaError_t e_ = (call);                                                         \
+    if (e_ != cudaSuccess)                                                           \
+      return fail(e_ == cudaErrorMemoryAllocation ? UV_ENOMEM : UV_ECUDA,            \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));               \
+  } while (0)
+
+#define UV_TRY(expr)        \
+  do {                      \
+    int rc_ = (expr);       \
+    if (rc_ != UV_OK) return rc_; \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// Where a caller pointer lives.  Returns UV_EINVAL for device memory of
+// another GPU.
+inline int classify(const void *p, int device, bool *on_device) {
+  *on_device = false;
+  if (p == nullptr) return UV_OK;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return UV_OK;  // unregistered host memory
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    if (a.type == cudaMemoryTypeDevice && a.device != device)
+      return fail(UV_EINVAL, "device buffer belongs to another GPU");
+    *on_device = true;
+  }
+  return UV_OK;
+}
+
+// Stream-ordered scratch freed at scope exit (on the same stream).
+struct Scratch {
+  cudaStream_t st;
+  std::vector<void *> ptrs;
+  explicit Scratch(cudaStream_t s) : st(s) {}
+  ~Scratch() {
+    for (void *p : ptrs) cudaFreeAsync(p, st);
+  }
+  template <class T>
+  int alloc(T **out, size_t count) {
+    *out = nullptr;
+    if (count == 0) count = 1;
+    void *p = nullptr;
+    cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(UV_ENOMEM, std::string("cudaMallocAsync: ") + cudaGetErrorString(e));
+    }
+    ptrs.push_back(p);
+    *out = (T *)p;
+    return UV_OK;
+  }
+};
+
+// A caller input viewed on the device: used in place when it is device
+// memory, otherwise copied through scratch.
+template <class T>
+int stage_in(const T *src, size_t count, int device, Scratch &sc, const T **dev) {
+  bool on_dev = false;
+  UV_TRY(classify(src, device, &on_dev));
+  if (src == nullptr || on_dev) {
+    *dev = src;
+    return UV_OK;
+  }
+  T *d = nullptr;
+  UV_TRY(sc.alloc(&d, count));
+  UV_CK(cudaMemcpyAsync(d, src, count * sizeof(T), cudaMemcpyHostToDevice, sc.st));
+  *dev = d;
+  return UV_OK;
+}
+
+// A caller output: written in place on the device, or produced in scratch
+// and copied back (see Outputs::finish).
+struct Outputs {
+  struct Pending {
+    void *host;
+    const void *dev;
+    size_t bytes;
+  };
+  std::vector<Pending> pend;
+  template <class T>
+  int stage(T *dst, size_t count, int device, Scratch &sc, T **dev) {
+    bool on_dev = false;
+    UV_TRY(classify(dst, device, &on_dev));
+    if (dst == nullptr || on_dev) {
+      *dev = dst;
+      return UV_OK;
+    }
+    T *d = nullptr;
+    UV_TRY(sc.alloc(&d, count));
+    pend.push_back({(void *)dst, (const void *)d, count * sizeof(T)});
+    *dev = d;
+    return UV_OK;
+  }
+  int finish(cudaStream_t st) {
+    for (auto &p : pend) UV_CK(cudaMemcpyAsync(p.host, p.dev, p.bytes, cudaMemcpyDeviceToHost, st));
+    if (!pend.empty()) UV_CK(cudaStreamSynchronize(st));
+    return UV_OK;
+  }
+};
+
+// ---- kernel timing hook (uv_profile_enable / uv_profile_read) ----
+struct ProfRec {
+  const char *name;
+  cudaEvent_t a, b;
+};
+extern std::mutex g_prof_mu;
+extern int64_t g_scan_splits;  // uv_set_tuning("scan_splits")
+extern bool g_prof_on;
+extern std::vector<ProfRec> g_prof;
+
+struct ProfScope {
+  const char *name;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(const char *n, cudaStream_t s) : name(n), st(s) {
+    if (!g_prof_on) return;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      a = b = nullptr;
+      return;
+    }
+    cudaEventRecord(a, st);
+  }
+  ~ProfScope() {
+    if (a == nullptr) return;
+    cudaEventRecord(b, st);
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof.push_back({name, a, b});
+  }
+};
+
+template <class T>
+int grow(T **buf, int64_t old_n, int64_t new_cap, cudaStream_t st) {
+  T *nb = nullptr;
+  UV_CK(cudaMallocAsync((void **)&nb, (size_t)std::max<int64_t>(new_cap, 1) * sizeof(T), st));
+  if (*buf != nullptr && old_n > 0)
+    UV_CK(cudaMemcpyAsync(nb, *buf, (size_t)old_n * sizeof(T), cudaMemcpyDeviceToDevice, st));
+  if (*buf != nullptr) cudaFreeAsync(*buf, st);
+  *buf = nb;
+  return UV_OK;
+}
+
+// Shared launchers (capi.cu).
+int sm_count(int dev);
+
+}  // namespace uvcapi
+
+struct uv_codec {
+  uv_config cfg;
+  int code_bytes = 0, code_stride = 0, table_len = 0;
+  std::vector<float> h_table;
+  uvb::RotationHost rot_host;
+  float *d_table = nullptr;
+  float *d_signs = nullptr;
+  uvb::RotParams rot;
+  uvb::EncodePlan plan;
+  int plan_status = 0;
+  std::string plan_why;
+};
+
+struct uv_index {
+  const uv_codec *codec = nullptr;
+  int64_t n = 0, cap = 0;
+  uint8_t *codes = nullptr;
+  uint32_t *start = nullptr;
+  float *rescale = nullptr, *rnorm = nullptr, *norms = nullptr;
+  uint32_t *cidx = nullptr;
+  int64_t *ids = nullptr;
+  float *centroids = nullptr;
+  int n_centroids = 0;
+};
+
+
+namespace uvcapi {
+
+int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
+                  int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
+                  float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,
+                  const float *list_centroids = nullptr, const uint32_t *row_list = nullptr,
+                  const int64_t *row_index = nullptr);
+int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_key,
+                 const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
+                 cudaStream_t st);
+// normalize + rotate queries; u (unit, unrotated) optional
+int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *centroids,
+                int n_centroids, float *q_r, float *qc, uint32_t *degen, float *u,
+                cudaStream_t st);
+
+}  // namespace uvcapi

@@ -1,0 +1,645 @@
+// capi_ivf.cu -- the IVF index behind the C ABI (ivf.rs, bench.rs:298-349).
+//
+// Device layout: the posting lists are one list-major SoA (codes at the
+// codec's padded stride, start, rescale, rnorm, ids) with list offsets, so a
+// probed list is one contiguous record range for the scan kernel.  Build and
+// search never leave the device except for the stable bucketing of rows by
+// list (a counting sort of n u32 on the host, the reference's bucket loop).
+#include "capi_internal.h"
+
+using namespace uvcapi;
+
+struct uv_ivf {
+  const uv_codec *codec = nullptr;
+  int nlist = 0, centered = 0;
+  float *centroids = nullptr;  // nlist x dim
+  float *cnorm = nullptr;      // |c_j| (lib.rs:215-217)
+  int64_t n = 0;
+  std::vector<int64_t> off;    // nlist + 1
+  int64_t *d_off = nullptr;
+  uint8_t *codes = nullptr;
+  uint32_t *start = nullptr;
+  float *rescale = nullptr, *rnorm = nullptr;
+  int64_t *ids = nullptr;
+};
+
+namespace {
+
+unsigned blocks(int64_t n, int per) { return (unsigned)((n + per - 1) / per); }
+
+int seqdot_launch(int mode, const float *A, int64_t nA, const float *B, int64_t nB, int dim,
+                  uint64_t *out_key, float *out, const float *a_norm, const float *b_norm,
+                  cudaStream_t st) {
+  if (nA == 0 || nB == 0) return UV_OK;
+  uvb::SeqDotParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.dim = dim;
+  p.lda = dim;
+  p.ldb = dim;
+  p.nA = nA;
+  p.nB = nB;
+  p.A = A;
+  p.B = B;
+  p.one2 = make_float2(1.0f, 1.0f);
+  p.out_key = out_key;
+  p.out = out;
+  p.a_norm = a_norm;
+  p.b_norm = b_norm;
+  const int T = uvb::seqdot_tile();
+  const dim3 grid(blocks(nB, T), (unsigned)std::min<int64_t>((nA + T - 1) / T, 65535));
+  void *args[] = {&p};
+  const void *fn = mode == 0 ? (const void *)uvb::seqdot_kernel<0> : (const void *)uvb::seqdot_kernel<1>;
+  ProfScope ps(mode == 0 ? "ivf_argmax" : "ivf_cosine", st);
+  UV_CK(cudaLaunchKernel(fn, grid, dim3(256), args, 0, st));
+  return UV_OK;
+}
+
+// units = rows / max(|row|, EPS) (device)
+int units_launch(const float *rows, int64_t n, int dim, float *norms, float *units,
+                 cudaStream_t st) {
+  if (n == 0) return UV_OK;
+  uvb::row_norms_kernel<<<blocks(n, 128), 128, 0, st>>>(rows, n, dim, norms);
+  UV_CK(cudaGetLastError());
+  uvb::normalize_rows_kernel<<<blocks(n * dim, 256), 256, 0, st>>>(rows, norms, n, dim, units);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
+// asg[i] = first strict maximum of <units[i], c_j> (device in and out)
+int argmax_launch(const float *units, int64_t n, int dim, const float *cent, int nlist,
+                  uint64_t *keys, uint32_t *asg, cudaStream_t st) {
+  if (n == 0) return UV_OK;
+  UV_CK(cudaMemsetAsync(keys, 0, sizeof(uint64_t) * n, st));
+  UV_TRY(seqdot_launch(0, units, n, cent, nlist, dim, keys, nullptr, nullptr, nullptr, st));
+  uvb::argmax_index_kernel<<<blocks(n, 256), 256, 0, st>>>(keys, n, asg);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
+// ivf.rs:405-421 over raw device rows, in row chunks that bound the scratch.
+int assign_device(const float *rows, int64_t n, int dim, const float *cent, int nlist,
+                  uint32_t *asg, cudaStream_t st, Scratch &sc) {
+  const int64_t chunk = std::max<int64_t>(64, std::min<int64_t>(n, ((int64_t)256 << 20) / (4 * dim)));
+  float *units = nullptr, *norms = nullptr;
+  uint64_t *keys = nullptr;
+  UV_TRY(sc.alloc(&units, (size_t)chunk * dim));
+  UV_TRY(sc.alloc(&norms, (size_t)chunk));
+  UV_TRY(sc.alloc(&keys, (size_t)chunk));
+  for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+    const int64_t m = std::min(chunk, n - r0);
+    UV_TRY(units_launch(rows + r0 * dim, m, dim, norms, units, st));
+    UV_TRY(argmax_launch(units, m, dim, cent, nlist, keys, asg + r0, st));
+  }
+  return UV_OK;
+}
+
+// Stable bucketing of rows by list (ivf.rs:179-183): order = rows grouped by
+// list, input order inside a list; off has nlist + 1 entries.
+int bucket_host(const std::vector<uint32_t> &asg, int nlist, std::vector<int64_t> &order,
+                std::vector<int64_t> &off) {
+  off.assign((size_t)nlist + 1, 0);
+  for (uint32_t a : asg) {
+    if (a >= (uint32_t)nlist) return fail(UV_EINVAL, "assignment outside 0..nlist-1");
+    off[a + 1]++;
+  }
+  for (int j = 0; j < nlist; j++) off[j + 1] += off[j];
+  std::vector<int64_t> fill(off.begin(), off.end() - 1);
+  order.resize(asg.size());
+  for (size_t i = 0; i < asg.size(); i++) order[(size_t)fill[asg[i]]++] = (int64_t)i;
+  return UV_OK;
+}
+
+int copy_to_host(void *dst, const void *src, size_t bytes, cudaStream_t st) {
+  UV_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st));
+  UV_CK(cudaStreamSynchronize(st));
+  return UV_OK;
+}
+
+template <class T>
+int upload(const std::vector<T> &h, Scratch &sc, T **d, cudaStream_t st) {
+  UV_TRY(sc.alloc(d, h.size()));
+  if (!h.empty()) UV_CK(cudaMemcpyAsync(*d, h.data(), sizeof(T) * h.size(), cudaMemcpyHostToDevice, st));
+  return UV_OK;
+}
+
+void free_lists(uv_ivf *ix) {
+  cudaFree(ix->codes);
+  cudaFree(ix->start);
+  cudaFree(ix->rescale);
+  cudaFree(ix->rnorm);
+  cudaFree(ix->ids);
+  cudaFree(ix->d_off);
+  ix->codes = nullptr;
+  ix->start = nullptr;
+  ix->rescale = ix->rnorm = nullptr;
+  ix->ids = nullptr;
+  ix->d_off = nullptr;
+  ix->n = 0;
+}
+
+// Probe on device: lists (nq x ld, first np columns) of the best np lists by
+// exact cosine of the raw queries.
+int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld, int32_t *lists,
+                 cudaStream_t st, Scratch &sc) {
+  const int d = ix->codec->cfg.dim;
+  if (np == 0 || nq == 0) return UV_OK;
+  int pow2 = 32;
+  while (pow2 < ix->nlist) pow2 <<= 1;
+  if (pow2 > 16384) return fail(UV_EUNSUPPORTED, "probe supports nlist <= 16384");
+  float *qn = nullptr, *cos = nullptr;
+  UV_TRY(sc.alloc(&qn, (size_t)nq));
+  uvb::row_norms_kernel<<<blocks(nq, 128), 128, 0, st>>>(d_q, nq, d, qn);
+  UV_CK(cudaGetLastError());
+  const int64_t chunk =
+      std::max<int64_t>(1, std::min<int64_t>(nq, ((int64_t)256 << 20) / (4 * (int64_t)ix->nlist)));
+  UV_TRY(sc.alloc(&cos, (size_t)chunk * ix->nlist));
+  const size_t smem = (size_t)pow2 * 8;
+  UV_CK(cudaFuncSetAttribute(uvb::select_top_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem));
+  for (int64_t q0 = 0; q0 < nq; q0 += chunk) {
+    const int64_t m = std::min(chunk, nq - q0);
+    UV_TRY(seqdot_launch(1, d_q + q0 * d, m, ix->centroids, ix->nlist, d, nullptr, cos, qn + q0,
+                         ix->cnorm, st));
+    ProfScope ps("ivf_select", st);
+    uvb::select_top_kernel<<<(unsigned)std::min<int64_t>(m, 65535), 256, smem, st>>>(
+        cos, m, ix->nlist, pow2, np, ld, lists + q0 * ld);
+    UV_CK(cudaGetLastError());
+  }
+  return UV_OK;
+}
+
+// ivf.rs:229-239 on device: per-list top-k of every probed (query, list)
+// pair, merged per query.  Device inputs and outputs.
+int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np, int64_t *d_ids,
+                  float *d_scores, cudaStream_t st, Scratch &sc) {
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  if (np == 0 || ix->n == 0) {
+    // no list probed, or no records: every slot empty
+    uvb::fill_empty_kernel<<<blocks(nq * k, 256), 256, 0, st>>>(d_ids, d_scores, nq * k);
+    UV_CK(cudaGetLastError());
+    return UV_OK;
+  }
+  if (d % 16 != 0) return fail(UV_EUNSUPPORTED, "scan is built for dim a multiple of 16");
+  const int dim_pad = (d + 3) & ~3;
+  float *q_r = nullptr, *qc = nullptr, *u = nullptr;
+  uint32_t *degen = nullptr;
+  UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
+  UV_TRY(sc.alloc(&qc, 1));
+  UV_TRY(sc.alloc(&degen, (size_t)nq));
+  if (ix->centered) UV_TRY(sc.alloc(&u, (size_t)nq * dim_pad));
+  UV_TRY(prep_launch(c, d_q, nq, nullptr, 0, q_r, qc, degen, u, st));
+  // probe
+  const int64_t npairs = nq * np;
+  if (npairs > INT32_MAX) return fail(UV_EINVAL, "nq * nprobe exceeds 2^31 - 1");
+  int32_t *lists = nullptr;
+  UV_TRY(sc.alloc(&lists, (size_t)npairs));
+  UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc));
+  // bucket the (query, list) pairs by list into scan items of <= 32 pairs
+  const int nlist = ix->nlist;
+  const int64_t max_items = std::min<int64_t>(nlist, npairs) + (npairs + uvb::kScanTQ - 1) / uvb::kScanTQ;
+  int32_t *cnt = nullptr, *fill = nullptr, *pair_off = nullptr, *item_off = nullptr,
+          *n_items = nullptr, *pair_query = nullptr, *pair_slot = nullptr, *item_list = nullptr,
+          *item_pair = nullptr, *item_npairs = nullptr;
+  UV_TRY(sc.alloc(&cnt, (size_t)nlist * 2));
+  fill = cnt + nlist;
+  UV_TRY(sc.alloc(&pair_off, (size_t)nlist));
+  UV_TRY(sc.alloc(&item_off, (size_t)nlist));
+  UV_TRY(sc.alloc(&n_items, 1));
+  UV_TRY(sc.alloc(&pair_query, (size_t)npairs));
+  UV_TRY(sc.alloc(&pair_slot, (size_t)npairs));
+  UV_TRY(sc.alloc(&item_list, (size_t)max_items));
+  UV_TRY(sc.alloc(&item_pair, (size_t)max_items));
+  UV_TRY(sc.alloc(&item_npairs, (size_t)max_items));
+  UV_CK(cudaMemsetAsync(cnt, 0, sizeof(int32_t) * nlist * 2, st));
+  {
+    ProfScope ps("ivf_bucket", st);
+    uvb::pair_count_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, npairs, cnt);
+    uvb::pair_scan_kernel<<<1, 1024, 0, st>>>(cnt, nlist, pair_off, item_off, n_items);
+    uvb::pair_scatter_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, nq, np, pair_off, fill,
+                                                                  pair_query, pair_slot);
+    uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(cnt, pair_off, item_off, nlist,
+                                                              item_list, item_pair, item_npairs);
+    UV_CK(cudaGetLastError());
+  }
+  float *pair_qm = nullptr;
+  if (ix->centered) {
+    UV_TRY(sc.alloc(&pair_qm, (size_t)npairs));
+    ProfScope ps("ivf_pair_qm", st);
+    uvb::pair_qm_kernel<<<blocks(npairs, 128), 128, 0, st>>>(u, dim_pad, ix->centroids, d,
+                                                             pair_query, pair_slot, np, lists,
+                                                             (int)npairs, pair_qm);
+    UV_CK(cudaGetLastError());
+  }
+  // scan every item, one top-k per pair slot
+  uint32_t *part_key = nullptr;
+  int64_t *part_id = nullptr;
+  UV_TRY(sc.alloc(&part_key, (size_t)npairs * k));
+  UV_TRY(sc.alloc(&part_id, (size_t)npairs * k));
+  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
+  const bool small_k = k <= 32;
+  const size_t smem = uvb::chunked_scan_smem_bytes(c->table_len, table_smem, small_k);
+  const void *scan_k = uvb::chunked_scan_kernel_ptr(c->cfg.bits, table_smem, small_k);
+  if (scan_k == nullptr) return fail(UV_EUNSUPPORTED, "no scan kernel for these bits");
+  UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int rw = c->code_stride / 4;
+  int img_words = 4 + rw + 3;
+  if ((img_words & 1) == 0) img_words++;
+  uvb::ScanParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  sp.dim = d;
+  sp.mem = c->cfg.mem;
+  sp.bits = c->cfg.bits;
+  sp.nq = nq;
+  sp.n = ix->n;
+  sp.q_r = q_r;
+  sp.q_stride = dim_pad;
+  sp.qc = qc;
+  sp.n_centroids = 0;
+  sp.degenerate = degen;
+  sp.codes = ix->codes;
+  sp.code_stride = c->code_stride;
+  sp.start = ix->start;
+  sp.rescale = ix->rescale;
+  sp.rnorm = ix->centered ? ix->rnorm : nullptr;
+  sp.norms = nullptr;
+  sp.cidx = nullptr;
+  sp.code = c->d_table;
+  sp.table_len = c->table_len;
+  sp.table_in_smem = table_smem ? 1 : 0;
+  sp.img_words = img_words;
+  sp.mips = 0;
+  sp.k = k;
+  sp.ids = ix->ids;
+  sp.id_base = 0;
+  sp.part_key = part_key;
+  sp.part_id = part_id;
+  uvb::ScanWork work;
+  std::memset(&work, 0, sizeof(work));
+  work.ivf = 1;
+  work.item_list = item_list;
+  work.item_pair = item_pair;
+  work.item_npairs = item_npairs;
+  work.list_off = ix->d_off;
+  work.pair_query = pair_query;
+  work.pair_slot = pair_slot;
+  work.pair_qm = pair_qm;
+  work.n_items = n_items;
+  if (max_items > INT32_MAX) return fail(UV_EINVAL, "too many scan items");
+  {
+    void *args[] = {&sp, &work};
+    ProfScope ps("ivf_scan", st);
+    UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)max_items), dim3(256), args, smem, st));
+  }
+  return merge_launch(nq, np, k, k, part_key, nullptr, part_id, d_ids, d_scores, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int uv_kmeans(int32_t device, const float *rows, int64_t n, int32_t dim, int32_t nlist,
+              uint64_t seed, int32_t iters, float *centroids_out, void *stream) {
+  if (rows == nullptr || centroids_out == nullptr) return fail(UV_EINVAL, "null argument");
+  if (n < 1 || dim < 1 || nlist < 1 || iters < 0) return fail(UV_EINVAL, "bad size");
+  DeviceGuard g(device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_rows = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * dim, device, sc, &d_rows));
+  float *cent = nullptr, *units = nullptr, *norms = nullptr;
+  UV_TRY(outs.stage(centroids_out, (size_t)nlist * dim, device, sc, &cent));
+  UV_TRY(sc.alloc(&units, (size_t)n * dim));
+  UV_TRY(sc.alloc(&norms, (size_t)n));
+  UV_TRY(units_launch(d_rows, n, dim, norms, units, st));
+  // seeded init: units[splitmix64 % n], with replacement (bench.rs:307-310)
+  std::vector<int64_t> pick((size_t)nlist);
+  uint64_t state = seed;
+  for (int j = 0; j < nlist; j++) pick[j] = (int64_t)(uvb::splitmix64(&state) % (uint64_t)n);
+  int64_t *d_pick = nullptr;
+  UV_TRY(upload(pick, sc, &d_pick, st));
+  uvb::gather_rows_kernel<<<blocks((int64_t)nlist * dim, 256), 256, 0, st>>>(units, d_pick, nlist,
+                                                                           dim, cent);
+  UV_CK(cudaGetLastError());
+  uint64_t *keys = nullptr;
+  uint32_t *asg = nullptr;
+  int64_t *d_order = nullptr, *d_off = nullptr;
+  UV_TRY(sc.alloc(&keys, (size_t)n));
+  UV_TRY(sc.alloc(&asg, (size_t)n));
+  UV_TRY(sc.alloc(&d_order, (size_t)n));
+  UV_TRY(sc.alloc(&d_off, (size_t)nlist + 1));
+  std::vector<uint32_t> h_asg((size_t)n);
+  std::vector<int64_t> order, off;
+  for (int it = 0; it < iters; it++) {
+    UV_TRY(argmax_launch(units, n, dim, cent, nlist, keys, asg, st));
+    UV_TRY(copy_to_host(h_asg.data(), asg, sizeof(uint32_t) * n, st));
+    UV_TRY(bucket_host(h_asg, nlist, order, off));
+    UV_CK(cudaMemcpyAsync(d_order, order.data(), sizeof(int64_t) * n, cudaMemcpyHostToDevice, st));
+    UV_CK(cudaMemcpyAsync(d_off, off.data(), sizeof(int64_t) * (nlist + 1), cudaMemcpyHostToDevice,
+                          st));
+    ProfScope ps("ivf_means", st);
+    uvb::list_means_kernel<<<blocks((int64_t)nlist * dim, 256), 256, 0, st>>>(units, d_order, d_off,
+                                                                            nlist, dim, cent);
+    UV_CK(cudaGetLastError());
+    UV_CK(cudaStreamSynchronize(st));  // host order/off are reused next round
+  }
+  return outs.finish(st);
+}
+
+int uv_ivf_assign(int32_t device, const float *rows, int64_t n, int32_t dim,
+                  const float *centroids, int32_t nlist, uint32_t *assign_out, void *stream) {
+  if (rows == nullptr || centroids == nullptr || assign_out == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  if (n < 0 || dim < 1 || nlist < 1) return fail(UV_EINVAL, "bad size");
+  if (n == 0) return UV_OK;
+  DeviceGuard g(device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_rows = nullptr, *d_cent = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * dim, device, sc, &d_rows));
+  UV_TRY(stage_in(centroids, (size_t)nlist * dim, device, sc, &d_cent));
+  uint32_t *asg = nullptr;
+  UV_TRY(outs.stage(assign_out, (size_t)n, device, sc, &asg));
+  UV_TRY(assign_device(d_rows, n, dim, d_cent, nlist, asg, st, sc));
+  return outs.finish(st);
+}
+
+int uv_ivf_create(const uv_codec *codec, const float *centroids, int32_t nlist, int32_t centered,
+                  uv_ivf **out) {
+  if (codec == nullptr || centroids == nullptr || out == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  *out = nullptr;
+  if (nlist < 1) return fail(UV_EINVAL, "nlist must be positive");
+  const int d = codec->cfg.dim;
+  DeviceGuard g(codec->cfg.device);
+  uv_ivf *ix = new (std::nothrow) uv_ivf();
+  if (ix == nullptr) return fail(UV_ENOMEM, "host allocation failed");
+  ix->codec = codec;
+  ix->nlist = nlist;
+  ix->centered = centered ? 1 : 0;
+  ix->off.assign((size_t)nlist + 1, 0);
+  cudaError_t e = cudaMalloc(&ix->centroids, sizeof(float) * (size_t)nlist * d);
+  if (e == cudaSuccess) e = cudaMalloc(&ix->cnorm, sizeof(float) * (size_t)nlist);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(ix->centroids, centroids, sizeof(float) * (size_t)nlist * d, cudaMemcpyDefault);
+  if (e == cudaSuccess) {
+    uvb::row_norms_kernel<<<blocks(nlist, 128), 128>>>(ix->centroids, nlist, d, ix->cnorm);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(ix->centroids);
+    cudaFree(ix->cnorm);
+    delete ix;
+    return fail(e == cudaErrorMemoryAllocation ? UV_ENOMEM : UV_ECUDA,
+                std::string("ivf create: ") + cudaGetErrorString(e));
+  }
+  *out = ix;
+  return UV_OK;
+}
+
+int uv_ivf_destroy(uv_ivf *ix) {
+  if (ix == nullptr) return UV_OK;
+  {
+    DeviceGuard g(ix->codec->cfg.device);
+    free_lists(ix);
+    cudaFree(ix->centroids);
+    cudaFree(ix->cnorm);
+  }
+  delete ix;
+  return UV_OK;
+}
+
+int uv_ivf_build(uv_ivf *ix, const float *rows, int64_t n, const uint32_t *assign,
+                 const int64_t *ids, void *stream) {
+  if (ix == nullptr || (n > 0 && rows == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (n < 0) return fail(UV_EINVAL, "negative size");
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  UV_CK(cudaStreamSynchronize(st));
+  free_lists(ix);
+  ix->off.assign((size_t)ix->nlist + 1, 0);
+  Scratch sc(st);
+  const float *d_rows = nullptr;
+  UV_TRY(stage_in(rows, (size_t)n * d, dev, sc, &d_rows));
+  // assignment and stable bucketing
+  std::vector<uint32_t> h_asg((size_t)n);
+  if (assign != nullptr) {
+    if (n > 0) UV_TRY(copy_to_host(h_asg.data(), assign, sizeof(uint32_t) * n, st));
+  } else if (n > 0) {
+    uint32_t *asg = nullptr;
+    UV_TRY(sc.alloc(&asg, (size_t)n));
+    UV_TRY(assign_device(d_rows, n, d, ix->centroids, ix->nlist, asg, st, sc));
+    UV_TRY(copy_to_host(h_asg.data(), asg, sizeof(uint32_t) * n, st));
+  }
+  std::vector<int64_t> order, off;
+  UV_TRY(bucket_host(h_asg, ix->nlist, order, off));
+  std::vector<int64_t> h_ids((size_t)n);
+  if (ids != nullptr && n > 0) {
+    std::vector<int64_t> in((size_t)n);
+    UV_TRY(copy_to_host(in.data(), ids, sizeof(int64_t) * n, st));
+    for (int64_t i = 0; i < n; i++) h_ids[i] = in[(size_t)order[i]];
+  } else {
+    for (int64_t i = 0; i < n; i++) h_ids[i] = order[i];
+  }
+  std::vector<uint32_t> row_list((size_t)n);
+  for (int j = 0; j < ix->nlist; j++)
+    for (int64_t i = off[j]; i < off[j + 1]; i++) row_list[(size_t)i] = (uint32_t)j;
+  // device lists
+  const int64_t cap = std::max<int64_t>(n, 1);
+  UV_CK(cudaMalloc(&ix->codes, (size_t)cap * c->code_stride));
+  UV_CK(cudaMalloc(&ix->start, sizeof(uint32_t) * cap));
+  UV_CK(cudaMalloc(&ix->rescale, sizeof(float) * cap));
+  UV_CK(cudaMalloc(&ix->rnorm, sizeof(float) * cap));
+  UV_CK(cudaMalloc(&ix->ids, sizeof(int64_t) * cap));
+  UV_CK(cudaMalloc(&ix->d_off, sizeof(int64_t) * (ix->nlist + 1)));
+  UV_CK(cudaMemcpyAsync(ix->d_off, off.data(), sizeof(int64_t) * (ix->nlist + 1),
+                        cudaMemcpyHostToDevice, st));
+  if (n > 0) {
+    UV_CK(cudaMemcpyAsync(ix->ids, h_ids.data(), sizeof(int64_t) * n, cudaMemcpyHostToDevice, st));
+    int64_t *d_order = nullptr;
+    uint32_t *d_list = nullptr;
+    UV_TRY(upload(order, sc, &d_order, st));
+    UV_TRY(upload(row_list, sc, &d_list, st));
+    UV_TRY(encode_device(c, d_rows, n, nullptr, 0, false, ix->codes, ix->start, ix->rescale,
+                         ix->rnorm, nullptr, nullptr, st, sc,
+                         ix->centered ? ix->centroids : nullptr, d_list, d_order));
+  }
+  UV_CK(cudaStreamSynchronize(st));  // the host vectors above end with this call
+  ix->off = off;
+  ix->n = n;
+  return UV_OK;
+}
+
+int uv_ivf_len(const uv_ivf *ix, int64_t *len) {
+  if (ix == nullptr || len == nullptr) return fail(UV_EINVAL, "null argument");
+  *len = ix->n;
+  return UV_OK;
+}
+
+int uv_ivf_nlist(const uv_ivf *ix, int32_t *nlist) {
+  if (ix == nullptr || nlist == nullptr) return fail(UV_EINVAL, "null argument");
+  *nlist = ix->nlist;
+  return UV_OK;
+}
+
+int uv_ivf_mem_bytes(const uv_ivf *ix, int64_t *bytes) {
+  if (ix == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
+  int32_t cb = 0, sb = 0, rb = 0;
+  uv_codec_record_bytes(ix->codec, &cb, &sb, &rb);
+  *bytes = ix->n * (int64_t)(cb + sb + rb + (ix->centered ? 4 : 0));
+  return UV_OK;
+}
+
+int uv_ivf_probe(const uv_ivf *ix, const float *queries, int64_t nq, int32_t nprobe,
+                 int32_t *lists_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || lists_out == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || nprobe < 0) return fail(UV_EINVAL, "negative size");
+  if (nq == 0 || nprobe == 0) return UV_OK;
+  const int dev = ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * ix->codec->cfg.dim, dev, sc, &d_q));
+  int32_t *lists = nullptr;
+  UV_TRY(outs.stage(lists_out, (size_t)nq * nprobe, dev, sc, &lists));
+  const int np = std::min(nprobe, ix->nlist);
+  if (np < nprobe) UV_CK(cudaMemsetAsync(lists, 0xff, sizeof(int32_t) * nq * nprobe, st));
+  UV_TRY(probe_device(ix, d_q, nq, np, nprobe, lists, st, sc));
+  return outs.finish(st);
+}
+
+int uv_ivf_search(const uv_ivf *ix, const float *queries, int64_t nq, int32_t k, int32_t nprobe,
+                  int64_t *ids_out, float *scores_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || nprobe < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (nq == 0) return UV_OK;
+  const int dev = ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * ix->codec->cfg.dim, dev, sc, &d_q));
+  int64_t *d_ids = nullptr;
+  float *d_scores = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  UV_TRY(search_device(ix, d_q, nq, k, std::min(nprobe, ix->nlist), d_ids, d_scores, st, sc));
+  return outs.finish(st);
+}
+
+int uv_ivf_search_rerank(const uv_ivf *ix, const float *queries, int64_t nq, int32_t k,
+                         int32_t nprobe, int32_t rdepth, const float *db, int64_t n_db,
+                         int64_t *ids_out, float *scores_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr || db == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || nprobe < 0 || n_db < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  const int r = std::max(rdepth, k);
+  if (r > uvb::kScanKCap) return fail(UV_EUNSUPPORTED, "rerank depth above 128");
+  if (nq == 0) return UV_OK;
+  const int d = ix->codec->cfg.dim;
+  const int dev = ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr, *d_db = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * d, dev, sc, &d_q));
+  UV_TRY(stage_in(db, (size_t)n_db * d, dev, sc, &d_db));
+  int64_t *d_ids = nullptr, *cand = nullptr;
+  float *d_scores = nullptr, *cand_s = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  UV_TRY(sc.alloc(&cand, (size_t)nq * r));
+  UV_TRY(sc.alloc(&cand_s, (size_t)nq * r));
+  UV_TRY(search_device(ix, d_q, nq, r, std::min(nprobe, ix->nlist), cand, cand_s, st, sc));
+  int *err = nullptr;
+  UV_TRY(sc.alloc(&err, 1));
+  UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  uvb::RerankParams rp;
+  std::memset(&rp, 0, sizeof(rp));
+  rp.nq = nq;
+  rp.dim = d;
+  rp.r = r;
+  rp.k = k;
+  rp.queries = d_q;
+  rp.db = d_db;
+  rp.n_db = n_db;
+  rp.err = err;
+  rp.cand = cand;
+  rp.out_id = d_ids;
+  rp.out_score = d_scores;
+  {
+    void *args[] = {&rp};
+    ProfScope ps("ivf_rerank", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::rerank_kernel, dim3(blocks(nq, 8)), dim3(256), args,
+                           0, st));
+  }
+  int h_err = 0;
+  UV_TRY(copy_to_host(&h_err, err, sizeof(int), st));
+  if (h_err) return fail(UV_EINVAL, "a candidate id does not index db (id >= n_db)");
+  return outs.finish(st);
+}
+
+int uv_ivf_export(const uv_ivf *ix, int64_t *list_off, int64_t *ids, uint8_t *codes,
+                  uint32_t *start, float *rescale, float *rnorm, void *stream) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  const uv_codec *c = ix->codec;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = ix->n;
+  if (list_off)
+    UV_CK(cudaMemcpyAsync(list_off, ix->off.data(), sizeof(int64_t) * (ix->nlist + 1),
+                          cudaMemcpyDefault, st));
+  if (n > 0) {
+    if (codes)
+      UV_CK(cudaMemcpy2DAsync(codes, c->code_bytes, ix->codes, c->code_stride, c->code_bytes, n,
+                              cudaMemcpyDefault, st));
+    if (ids) UV_CK(cudaMemcpyAsync(ids, ix->ids, 8 * n, cudaMemcpyDefault, st));
+    if (start) UV_CK(cudaMemcpyAsync(start, ix->start, 4 * n, cudaMemcpyDefault, st));
+    if (rescale) UV_CK(cudaMemcpyAsync(rescale, ix->rescale, 4 * n, cudaMemcpyDefault, st));
+    if (rnorm) UV_CK(cudaMemcpyAsync(rnorm, ix->rnorm, 4 * n, cudaMemcpyDefault, st));
+  }
+  UV_CK(cudaStreamSynchronize(st));
+  return UV_OK;
+}
+
+int uv_ivf_digest(const uv_ivf *ix, uint64_t *digest, void *stream) {
+  if (ix == nullptr || digest == nullptr) return fail(UV_EINVAL, "null argument");
+  const uv_codec *c = ix->codec;
+  *digest = 0;
+  if (ix->n == 0) return UV_OK;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  unsigned long long *d_acc = nullptr;
+  UV_TRY(sc.alloc(&d_acc, 1));
+  UV_CK(cudaMemsetAsync(d_acc, 0, sizeof(unsigned long long), st));
+  UV_CK(uvb::launch_digest(ix->codes, c->code_stride, c->code_bytes, ix->start, ix->n, d_acc, st));
+  unsigned long long h = 0;
+  UV_TRY(copy_to_host(&h, d_acc, sizeof(h), st));
+  *digest = h;
+  return UV_OK;
+}
+
+}  // extern "C"

@@ -71,7 +71,7 @@ std::vector<float> build_code_table(int mem, int bits) {
 }
 
 // lib.rs:259-265
-static uint64_t splitmix64(uint64_t *state) {
+uint64_t splitmix64(uint64_t *state) {
   *state += 0x9E3779B97F4A7C15ULL;
   uint64_t z = *state;
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;

@@ -15,5 +15,7 @@ struct RotationHost {
 
 std::vector<float> build_code_table(int mem, int bits);
 RotationHost build_rotation(int dim, uint64_t seed, int rounds);
+// lib.rs:259-265: one splitmix64 step (advances *state, returns the mix)
+uint64_t splitmix64(uint64_t *state);
 
 }  // namespace uvb

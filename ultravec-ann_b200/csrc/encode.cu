@@ -56,12 +56,6 @@ __device__ __forceinline__ uint64_t team_max_u64(uint64_t v, const Team &tm,
   return r;
 }
 
-// Ordered key of a float for a first-maximum argmax (NaN never wins).
-__device__ __forceinline__ uint32_t max_key32(float f) {
-  if (f != f) f = -INFINITY;
-  uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 template <int B, int WPT, bool BACK_SMEM>
 __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
@@ -130,7 +124,7 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     const int64_t vv = valid ? v : p.n - 1;
 
     // ---- prep: load, normalize, center, rotate, standardize ----
-    const float *row = p.rows + vv * (int64_t)d;
+    const float *row = p.rows + (p.row_index ? p.row_index[vv] : vv) * (int64_t)d;
     for (int i = tm.t; i < d; i += T) xbuf[i] = row[i];
     tm.sync();
     if (!p.rotated_input) {
@@ -153,13 +147,13 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
         uint64_t best = 0;
         for (int j = tm.t; j < p.n_centroids; j += T) {
           float dj = seq_dot(xbuf, p.centroids + (size_t)j * d, d);
-          uint64_t key = ((uint64_t)max_key32(dj) << 32) | (uint32_t)(~(uint32_t)j);
+          uint64_t key = ((uint64_t)score_key32(dj) << 32) | (uint32_t)(~(uint32_t)j);
           best = key > best ? key : best;
         }
         best = team_max_u64(best, tm, red);
         uint32_t j = ~(uint32_t)(best & 0xffffffffu);
         // every dot NaN or -inf: the reference keeps index 0
-        if ((uint32_t)(best >> 32) <= max_key32(-INFINITY)) j = 0;
+        if ((uint32_t)(best >> 32) <= score_key32(-INFINITY)) j = 0;
         if (tm.leader()) misc_u[4] = j;
         cen = p.centroids + (size_t)j * d;
       }

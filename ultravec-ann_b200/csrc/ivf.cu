@@ -1,0 +1,349 @@
+// ivf.cu -- the IVF coarse stage and list bookkeeping for sm_100a.
+//
+//   k-means       bench.rs:298-349 (units, splitmix64 picks, 5 Lloyd rounds,
+//                 strict-> argmax, sums in original row order, mean = sum / count)
+//   assignment    ivf.rs:405-421 (normalize the row, first strict maximum)
+//   probe         ivf.rs:209-223 (exact cosine, lib.rs:240-248, best nprobe)
+//   search        ivf.rs:229-239 (each probed list scores its own records;
+//                 the per-list top-k are merged)
+//   rerank        ivf.rs:248-274 (exact fp32 cosine of the global top-r)
+//
+// Every dot here is the reference's `a.iter().zip(b).map(|(x, y)| x * y).sum()`:
+// a left fold from -0.0 with the product and the sum rounded separately.  The
+// tile kernel evaluates one such chain per (row, centroid) pair; 16 chains per
+// thread give the ILP.  Products are paired f32x2 multiplies and the fold adds
+// are written fma(product, one, acc) with a run-time one: the code generator
+// fuses a paired multiply into a following paired add (one rounding instead
+// of two), and an fma whose multiplier is 1.0 rounds exactly like the add.
+#include "uv_kernels.h"
+
+namespace uvb {
+
+namespace {
+
+constexpr int SD_T = 64;   // rows and centroids per tile
+constexpr int SD_K = 32;   // coordinates per staged chunk
+constexpr int SD_S = SD_T + 4;
+
+}  // namespace
+
+// C[a][b] = seq_dot(A[a], B[b]) over `dim` terms.  MODE 0: per A row, the
+// first strict maximum over b as a 64-bit key (score key, ~b) folded into
+// out_key[a] with atomicMax.  MODE 1: cosine(A[a], B[b]) into out[a * nB + b].
+template <int MODE>
+__global__ void __launch_bounds__(256) seqdot_kernel(const SeqDotParams p) {
+  __shared__ __align__(16) float As[SD_K][SD_S];
+  __shared__ __align__(16) float Bs[SD_K][SD_S];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int d = p.dim;
+  const int64_t b0 = (int64_t)blockIdx.x * SD_T;
+  const float2 one2 = p.one2;
+  for (int64_t a0 = (int64_t)blockIdx.y * SD_T; a0 < p.nA; a0 += (int64_t)gridDim.y * SD_T) {
+    float2 acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = make_float2(-0.0f, -0.0f);
+    const int lr = tid >> 2, lk = (tid & 3) * 8;
+    const int64_t ar = a0 + lr, br = b0 + lr;
+    const float *arow = p.A + (ar < p.nA ? ar : 0) * (int64_t)p.lda;
+    const float *brow = p.B + (br < p.nB ? br : 0) * (int64_t)p.ldb;
+    for (int k0 = 0; k0 < d; k0 += SD_K) {
+      const int kc = min(SD_K, d - k0);
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int k = lk + e;
+        As[k][lr] = (k < kc && ar < p.nA) ? __ldg(arow + k0 + k) : 0.0f;
+        Bs[k][lr] = (k < kc && br < p.nB) ? __ldg(brow + k0 + k) : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int k = 0; k < kc; k++) {
+        const float4 a4 = *(const float4 *)&As[k][ty * 4];
+        const float4 b4 = *(const float4 *)&Bs[k][tx * 4];
+        const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 ai = make_float2(av[i], av[i]);
+          acc[i][0] = __ffma2_rn(__fmul2_rn(ai, b01), one2, acc[i][0]);
+          acc[i][1] = __ffma2_rn(__fmul2_rn(ai, b23), one2, acc[i][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int64_t a = a0 + ty * 4 + i;
+      const float dv[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
+      if (MODE == 0) {
+        uint64_t best = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int64_t b = b0 + tx * 4 + j;
+          const uint64_t key = b < p.nB ? rank_key(dv[j], (uint32_t)b) : 0ull;
+          best = key > best ? key : best;
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          const uint64_t w = __shfl_xor_sync(0xffffffffu, best, o);
+          best = w > best ? w : best;
+        }
+        if (tx == 0 && a < p.nA) atomicMax((unsigned long long *)&p.out_key[a], best);
+      } else if (a < p.nA) {
+        const float na = p.a_norm[a];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int64_t b = b0 + tx * 4 + j;
+          if (b >= p.nB) continue;
+          const float nb = p.b_norm[b];
+          p.out[a * p.nB + b] =
+              (na < kF32Eps || nb < kF32Eps) ? 0.0f : fdiv(dv[j], fmul(na, nb));
+        }
+      }
+    }
+  }
+}
+
+// Key of the first strict maximum -> its index (rank_key puts ~b low).
+__global__ void argmax_index_kernel(const uint64_t *key, int64_t n, uint32_t *out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = rank_key_index(key[i]);
+}
+
+// norms[i] = sqrt(seq_sum_sq(row i)) (lib.rs:215-217), one thread per row.
+__global__ void row_norms_kernel(const float *rows, int64_t n, int dim, float *norms) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float *r = rows + i * (int64_t)dim;
+  float s = -0.0f;
+  for (int t = 0; t < dim; t++) {
+    const float x = __ldg(r + t);
+    s = fadd(s, fmul(x, x));
+  }
+  norms[i] = fsqrt(s);
+}
+
+// units[i] = row[i] / max(norm, EPS), elementwise.
+__global__ void normalize_rows_kernel(const float *rows, const float *norms, int64_t n, int dim,
+                                      float *units) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n * (int64_t)dim) return;
+  const int64_t i = e / dim;
+  units[e] = fdiv(rows[e], fmax_rs(norms[i], kF32Eps));
+}
+
+// cent[j] = units[pick[j]]
+__global__ void gather_rows_kernel(const float *src, const int64_t *pick, int nrows, int dim,
+                                   float *dst) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (int64_t)nrows * dim) return;
+  const int64_t j = e / dim, t = e - j * dim;
+  dst[e] = src[pick[j] * (int64_t)dim + t];
+}
+
+// Lloyd update (bench.rs:334-346): per (list, coordinate) the sum of the
+// member units in original row order from +0.0, then sum / (count as f32);
+// empty lists keep their centroid.  `order` lists rows by list, stable.
+__global__ void list_means_kernel(const float *units, const int64_t *order, const int64_t *off,
+                                  int nlist, int dim, float *cent) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (int64_t)nlist * dim) return;
+  const int j = (int)(e / dim);
+  const int t = (int)(e - (int64_t)j * dim);
+  const int64_t lo = off[j], hi = off[j + 1];
+  if (hi == lo) return;
+  float s = 0.0f;
+  for (int64_t m = lo; m < hi; m++) s = fadd(s, units[order[m] * (int64_t)dim + t]);
+  cent[e] = fdiv(s, (float)(hi - lo));
+}
+
+// Best `np` of each row of an (n x nb) score matrix by (score desc, index
+// asc), NaN as -inf (the probe order of ivf.rs:209-223).  One CTA per row,
+// bitonic sort of the row's keys in shared memory (pow2 >= nb).
+__global__ void __launch_bounds__(256) select_top_kernel(const float *scores, int64_t n, int nb,
+                                                         int pow2, int np, int ld_out,
+                                                         int32_t *out) {
+  extern __shared__ uint64_t keys[];
+  for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+    const float *s = scores + row * (int64_t)nb;
+    for (int i = threadIdx.x; i < pow2; i += blockDim.x)
+      keys[i] = i < nb ? rank_key(s[i], (uint32_t)i) : 0ull;
+    __syncthreads();
+    for (int size = 2; size <= pow2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int pi = threadIdx.x; pi < pow2 / 2; pi += blockDim.x) {
+          const int lo = 2 * pi - (pi & (stride - 1));
+          const int hi = lo + stride;
+          const bool desc = (lo & size) == 0;
+          const uint64_t x = keys[lo], y = keys[hi];
+          if ((x < y) == desc) {
+            keys[lo] = y;
+            keys[hi] = x;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = threadIdx.x; i < np; i += blockDim.x)
+      out[row * ld_out + i] = (int32_t)rank_key_index(keys[i]);
+    __syncthreads();
+  }
+}
+
+// Empty result slots: id -1, score -inf (as the merge writes them).
+__global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  ids[i] = -1;
+  scores[i] = -INFINITY;
+}
+
+// ---- (query, list) pairs bucketed by list ----
+__global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < npairs && lists[i] >= 0) atomicAdd(&cnt[lists[i]], 1);
+}
+
+// One CTA: exclusive scans of the pair counts and of the items per list
+// (ceil(count / 32)); n_items[0] = total items.
+__global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt, int nlist,
+                                                         int32_t *pair_off, int32_t *item_off,
+                                                         int32_t *n_items) {
+  __shared__ int32_t sp[1024], si[1024];
+  const int t = threadIdx.x;
+  const int per = (nlist + 1023) / 1024;
+  const int lo = min(nlist, t * per), hi = min(nlist, lo + per);
+  int32_t ps = 0, is = 0;
+  for (int l = lo; l < hi; l++) {
+    ps += cnt[l];
+    is += (cnt[l] + kScanTQ - 1) / kScanTQ;
+  }
+  sp[t] = ps;
+  si[t] = is;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const int32_t a = t >= o ? sp[t - o] : 0, b = t >= o ? si[t - o] : 0;
+    __syncthreads();
+    sp[t] += a;
+    si[t] += b;
+    __syncthreads();
+  }
+  int32_t pbase = sp[t] - ps, ibase = si[t] - is;
+  for (int l = lo; l < hi; l++) {
+    pair_off[l] = pbase;
+    item_off[l] = ibase;
+    pbase += cnt[l];
+    ibase += (cnt[l] + kScanTQ - 1) / kScanTQ;
+  }
+  if (t == 1023) n_items[0] = si[1023];
+}
+
+__global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
+                                    const int32_t *pair_off, int32_t *fill, int32_t *pair_query,
+                                    int32_t *pair_slot) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * np) return;
+  const int l = lists[i];
+  if (l < 0) return;
+  const int pos = pair_off[l] + atomicAdd(&fill[l], 1);
+  pair_query[pos] = (int32_t)(i / np);
+  pair_slot[pos] = (int32_t)i;
+}
+
+__global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
+                                 const int32_t *item_off, int nlist, int32_t *item_list,
+                                 int32_t *item_pair, int32_t *item_npairs) {
+  const int l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= nlist) return;
+  const int c = cnt[l];
+  for (int i = 0; i * kScanTQ < c; i++) {
+    const int it = item_off[l] + i;
+    item_list[it] = l;
+    item_pair[it] = pair_off[l] + i * kScanTQ;
+    item_npairs[it] = min(kScanTQ, c - i * kScanTQ);
+  }
+}
+
+// qm of each pair: seq_dot(u_query, centroid_list) (trellis.rs:2120-2183 with
+// the list codec's single centroid).  One thread per pair.
+__global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, int dim,
+                               const int32_t *pair_query, const int32_t *pair_slot, int np,
+                               const int32_t *lists, int npairs, float *qm) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= npairs) return;
+  const int64_t q = pair_query[i];
+  const int l = lists[pair_slot[i]];
+  const float *a = u + q * (int64_t)u_stride;
+  const float *c = cent + (int64_t)l * dim;
+  float s = -0.0f;
+  for (int t = 0; t < dim; t++) s = fadd(s, fmul(a[t], __ldg(c + t)));
+  qm[i] = s;
+}
+
+// Exact fp32 rerank (ivf.rs:248-274): cosine(query, db[id]) for each of the r
+// candidates of a query, then the best k by (cosine desc, id asc).  One warp
+// per query; r <= 128.
+__global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p) {
+  __shared__ uint64_t keys[8][128];
+  __shared__ int64_t cid[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q = (int64_t)blockIdx.x * 8 + warp;
+  if (q >= p.nq) return;
+  const float *qv = p.queries + q * (int64_t)p.dim;
+  float qs = -0.0f;
+  for (int t = 0; t < p.dim; t++) qs = fadd(qs, fmul(qv[t], qv[t]));
+  const float na = fsqrt(qs);
+  for (int c = lane; c < 128; c += 32) {
+    const int64_t id = c < p.r ? p.cand[q * p.r + c] : -1;
+    cid[warp][c] = id;
+    uint64_t key = 0;
+    if (id >= p.n_db) atomicExch(p.err, 1);  // an id that does not index db
+    if (id >= 0 && id < p.n_db) {
+      const float *x = p.db + id * (int64_t)p.dim;
+      float dot = -0.0f, xs = -0.0f;
+      for (int t = 0; t < p.dim; t++) {
+        const float xv = __ldg(x + t);
+        dot = fadd(dot, fmul(qv[t], xv));
+        xs = fadd(xs, fmul(xv, xv));
+      }
+      const float nb = fsqrt(xs);
+      const float cs = (na < kF32Eps || nb < kF32Eps) ? 0.0f : fdiv(dot, fmul(na, nb));
+      key = ((uint64_t)score_key32(cs) << 32) | (uint32_t)c;
+    }
+    keys[warp][c] = key;
+  }
+  __syncwarp();
+  // order: key desc, then id asc; ids are compared after the sort below
+  for (int size = 2; size <= 128; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int pi = lane; pi < 64; pi += 32) {
+        const int lo = 2 * pi - (pi & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t x = keys[warp][lo], y = keys[warp][hi];
+        const int64_t ix = cid[warp][(uint32_t)x], iy = cid[warp][(uint32_t)y];
+        const bool x_first = x == 0 ? false
+                             : y == 0 ? true
+                                      : ((x >> 32) > (y >> 32) || ((x >> 32) == (y >> 32) && ix < iy));
+        if (x_first != desc) {
+          keys[warp][lo] = y;
+          keys[warp][hi] = x;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  for (int i = lane; i < p.k; i += 32) {
+    const uint64_t key = keys[warp][i];
+    const bool ok = i < p.r && key != 0;
+    p.out_id[q * p.k + i] = ok ? cid[warp][(uint32_t)key] : -1;
+    p.out_score[q * p.k + i] = ok ? key32_score((uint32_t)(key >> 32)) : -INFINITY;
+  }
+}
+
+template __global__ void seqdot_kernel<0>(const SeqDotParams p);
+template __global__ void seqdot_kernel<1>(const SeqDotParams p);
+
+int seqdot_tile() { return SD_T; }
+
+}  // namespace uvb

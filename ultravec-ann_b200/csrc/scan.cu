@@ -56,6 +56,8 @@ __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
     if (!degenerate) {
       for (int i = tm.t; i < d; i += 32) x[i] = fdiv(x[i], qn);
       tm.sync();
+      if (p.u != nullptr && valid)
+        for (int i = tm.t; i < d; i += 32) p.u[qq * (int64_t)p.dim_pad + i] = x[i];
       for (int j = tm.t; j < p.n_centroids; j += 32) {
         float dj = seq_dot(x, p.centroids + (size_t)j * d, d);
         if (valid) p.qc[qq * p.n_centroids + j] = dj;
@@ -63,6 +65,8 @@ __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
       team_rotate(x, p.rot, tm, false);
     } else {
       for (int i = tm.t; i < d; i += 32) x[i] = 0.0f;
+      if (p.u != nullptr && valid)
+        for (int i = tm.t; i < d; i += 32) p.u[qq * (int64_t)p.dim_pad + i] = 0.0f;
       for (int j = tm.t; j < p.n_centroids; j += 32)
         if (valid) p.qc[qq * p.n_centroids + j] = 0.0f;
       tm.sync();
@@ -545,6 +549,7 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
     }
   } else {
     const int item = blockIdx.x;
+    if (item >= w.n_items[0]) return;  // before any barrier: the whole CTA leaves
     const int list = w.item_list[item];
     const int pair0 = w.item_pair[item];
     nql = w.item_npairs[item];

@@ -24,6 +24,7 @@ struct EncodeParams {
   int n_centroids;
   const float *list_centroids;  // IVF centering: row i uses list_centroids[row_list[i]]
   const uint32_t *row_list;
+  const int64_t *row_index;   // or null: position i encodes rows[row_index[i]]
   uint8_t *codes;           // n x code_stride
   int code_stride, code_bytes;
   uint32_t *start;
@@ -60,6 +61,7 @@ struct PrepParams {
   float *q_r;            // nq x dim_pad
   float *qc;             // nq x n_centroids
   uint32_t *degenerate;  // nq
+  float *u;              // or null: nq x dim_pad unit queries (before rotation)
 };
 
 struct ScanParams {
@@ -98,6 +100,30 @@ struct ScanWork {
   const int32_t *pair_query;  // query row of q_r
   const int32_t *pair_slot;   // output slot: query * nprobe + probe rank
   const float *pair_qm;       // <u, c_list> (centered lists) or null
+  const int32_t *n_items;     // IVF: CTAs at or past *n_items exit
+};
+
+// Sequential-dot tiles of the IVF coarse stage (ivf.cu).
+struct SeqDotParams {
+  int dim, lda, ldb;
+  int64_t nA, nB;
+  const float *A, *B;
+  float2 one2;              // (1.0f, 1.0f), passed at run time
+  uint64_t *out_key;        // mode 0: nA keys (zeroed before the launch)
+  float *out;               // mode 1: nA x nB cosines
+  const float *a_norm, *b_norm;
+};
+
+struct RerankParams {
+  int64_t nq;
+  int dim, r, k;
+  const float *queries;     // nq x dim, raw
+  const float *db;          // n_db x dim, raw
+  int64_t n_db;
+  int *err;                 // set to 1 when a candidate id is >= n_db
+  const int64_t *cand;      // nq x r ids (-1 = empty)
+  int64_t *out_id;
+  float *out_score;
 };
 
 struct MergeParams {
@@ -118,6 +144,35 @@ const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k);
 size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k);
 constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
+
+// ivf.cu
+template <int MODE>
+__global__ void seqdot_kernel(const SeqDotParams p);
+int seqdot_tile();
+__global__ void argmax_index_kernel(const uint64_t *key, int64_t n, uint32_t *out);
+__global__ void row_norms_kernel(const float *rows, int64_t n, int dim, float *norms);
+__global__ void normalize_rows_kernel(const float *rows, const float *norms, int64_t n, int dim,
+                                      float *units);
+__global__ void gather_rows_kernel(const float *src, const int64_t *pick, int nrows, int dim,
+                                   float *dst);
+__global__ void list_means_kernel(const float *units, const int64_t *order, const int64_t *off,
+                                  int nlist, int dim, float *cent);
+__global__ void select_top_kernel(const float *scores, int64_t n, int nb, int pow2, int np,
+                                  int ld_out, int32_t *out);
+__global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n);
+__global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt);
+__global__ void pair_scan_kernel(const int32_t *cnt, int nlist, int32_t *pair_off,
+                                 int32_t *item_off, int32_t *n_items);
+__global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
+                                    const int32_t *pair_off, int32_t *fill, int32_t *pair_query,
+                                    int32_t *pair_slot);
+__global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
+                                 const int32_t *item_off, int nlist, int32_t *item_list,
+                                 int32_t *item_pair, int32_t *item_npairs);
+__global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, int dim,
+                               const int32_t *pair_query, const int32_t *pair_slot, int np,
+                               const int32_t *lists, int npairs, float *qm);
+__global__ void rerank_kernel(const RerankParams p);
 
 // scan tiling constants shared with the host planner
 constexpr int kScanTQ = 32;
