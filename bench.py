@@ -40,6 +40,9 @@ DIM, BITS, MEM = 128, 2, 8
 N_BASE, N_QUERY = 1_000_000, 10_000
 K_MAIN, K_ALT = 100, 10
 FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
+# DRAM bytes (read + write) of one tensor-core scan launch at the bench
+# workload, from the ncu capture summarized in profiles/; None until measured.
+TC_TRAFFIC_PER_LAUNCH = None
 
 
 def parse():
@@ -52,6 +55,9 @@ def parse():
     ap.add_argument("--n-query", type=int, default=N_QUERY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--scan", choices=["auto", "exact", "tc"], default="auto",
+                    help="auto: tensor-core prefilter where it is built; exact: the CUDA-core "
+                         "kernel only; tc: prefilter wherever it is built")
     return ap.parse_args()
 
 
@@ -174,6 +180,11 @@ def run_reference(args, rank: int):
 METRIC = "flat codes-only MIPS queries/s and encode vectors/s at 1/2/4/8 B200; % HBM roofline"
 
 
+# kernel families of one step (uv_profile_read names)
+SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_bounds", "tc_pass1",
+                 "tc_theta", "tc_pass2", "tc_rescore")
+
+
 def config_dict(args):
     return {"workload": "flat-mips-1Mx10k-d128", "n_base": args.n_base, "n_query": args.n_query,
             "dim": DIM, "bits": BITS, "mem": MEM, "k": K_MAIN, "metric_space": "mips",
@@ -213,6 +224,7 @@ def main():
     nq = queries.shape[0]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    uv.set_tuning("tc_scan", {"auto": 0, "exact": 1, "tc": 2}[args.scan])
     codec = uv.Codec(DIM, BITS, MEM, device=local)
     index = uv.Index(codec)
     index.reserve(hi - lo)
@@ -266,8 +278,7 @@ def main():
         enc_ms.append(ev[0].elapsed_time(ev[1]))
         scan_ms.append(ev[1].elapsed_time(ev[2]))
     barrier()
-    kern = {name: uv.profile_read(name) for name in ("encode", "flat_scan", "prep_queries",
-                                                     "merge_topk")}
+    kern = {name: uv.profile_read(name) for name in SCAN_FAMILIES}
     launches_total = uv.profile_read("*")[1]
     uv.profile_enable(False)
     clk = clocks.stop() if clocks else None
@@ -339,17 +350,45 @@ def main():
     if rank == 0:
         qps = nq * args.steps / (scan_tot / 1e3)
         rows_s = args.n_base * args.steps / (enc_tot / 1e3)
-        scan_k_ms, scan_k_n = kern["flat_scan"]
-        avg_scan = scan_k_ms / max(scan_k_n, 1)
         n_local = hi - lo
-        flops = 2.0 * nq * n_local * DIM
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         peaks = load_peaks()
         smax = peaks.get("sm_max_mhz", 1965.0)
-        fp32_peak = sms * FP32_LANES_PER_SM * 2 * smax * 1e6 / 1e12
-        achieved = flops / (avg_scan / 1e3) / 1e12
         rec_bytes = 32 + 1 + 4 + 4
         hbm = peaks.get("hbm_gbs", 6650.0)
+        flops = 2.0 * nq * n_local * DIM
+        hbm_model = {"bytes_per_query": n_local * rec_bytes,
+                     "gbs": qps / world * n_local * rec_bytes / 1e9, "peak_gbs": hbm,
+                     "frac": qps / world * n_local * rec_bytes / 1e9 / hbm,
+                     "note": "streaming model (every query re-reads its shard); >1 means "
+                             "on-chip reuse across the query tile"}
+        if kern["tc_pass2"][1] > 0:
+            # tensor-core prefilter: the dominant kernels are the two fp16 MMA
+            # passes; each launch does the full Q x N x d contraction
+            t_ms = kern["tc_pass1"][0] + kern["tc_pass2"][0]
+            t_n = kern["tc_pass1"][1] + kern["tc_pass2"][1]
+            avg = t_ms / max(t_n, 1)
+            achieved = flops / (avg / 1e3) / 1e12
+            peak = peaks.get("bf16_tflops", 1590.0)
+            roof = {"bound": "tensor", "kernel": "tc_scan_kernel (pass 1 and pass 2)",
+                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": TC_TRAFFIC_PER_LAUNCH,
+                    "peak_source": "bf16_tflops of MEASURED_PEAKS.json (dense f16 and bf16 "
+                                   "tensor peaks are equal)" if "bf16_tflops" in peaks
+                                   else "fallback 1.59 PFLOP/s",
+                    "flops_per_launch": flops, "avg_launch_ms": avg, "hbm_model": hbm_model}
+        else:
+            scan_k_ms, scan_k_n = kern["flat_scan"]
+            avg_scan = scan_k_ms / max(scan_k_n, 1)
+            fp32_peak = sms * FP32_LANES_PER_SM * 2 * smax * 1e6 / 1e12
+            achieved = flops / (avg_scan / 1e3) / 1e12
+            roof = {"bound": "fp32", "kernel": "flat_scan_kernel", "achieved": achieved,
+                    "peak": fp32_peak, "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                    "traffic": None,
+                    "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA/clk x 2 x "
+                                   f"{smax:.0f} MHz (sm_max_mhz of MEASURED_PEAKS.json)",
+                    "flops_per_launch": flops, "avg_launch_ms": avg_scan,
+                    "hbm_model": hbm_model}
         line = {
             "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -359,20 +398,7 @@ def main():
             "encode": {"value": rows_s, "unit": "rows/s", "ms_per_step": enc_tot / args.steps},
             "scan_ms_per_step": scan_tot / args.steps,
             "top10": {"value": nq * len(k10_ms) / (k10_tot / 1e3), "unit": "queries/s"},
-            "roofline": {
-                "bound": "fp32", "kernel": "flat_scan_kernel", "achieved": achieved,
-                "peak": fp32_peak, "unit": "TFLOP/s", "frac": achieved / fp32_peak,
-                "traffic": None,
-                "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA/clk x 2 x "
-                               f"{smax:.0f} MHz (sm_max_mhz of MEASURED_PEAKS.json)",
-                "flops_per_launch": flops, "avg_launch_ms": avg_scan,
-                "hbm_model": {"bytes_per_query": n_local * rec_bytes,
-                              "gbs": qps / world * n_local * rec_bytes / 1e9,
-                              "peak_gbs": hbm,
-                              "frac": qps / world * n_local * rec_bytes / 1e9 / hbm,
-                              "note": "streaming model (every query re-reads its shard); >1 "
-                                      "means on-chip reuse across the query tile"},
-            },
+            "roofline": roof,
             "kernels_ms": {k: v[0] / max(v[1], 1) for k, v in kern.items()},
             "gpu_launches": launches_total,
             "e2e": e2e,

@@ -1,0 +1,126 @@
+"""The tensor-core prefilter of the flat scan (tcscan.cu) returns exactly what
+the exact scan returns: ids and scores bit-identical to the oracle at sizes
+the oracle finishes in seconds, and to the exact CUDA-core kernel at the full
+1M-record size.  `tc_scan` = 2 forces the prefilter wherever it is built,
+1 disables it."""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from fixtures import rand_rows
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+
+@pytest.fixture
+def tc_mode(uv):
+    yield lambda v: uv.set_tuning("tc_scan", v)
+    uv.set_tuning("tc_scan", 0)
+
+
+def search_both(uv, index, queries, k, mips, tc_mode):
+    tc_mode(2)
+    a = index.search(queries, k, mips=mips)
+    tc_mode(1)
+    b = index.search(queries, k, mips=mips)
+    return a, b
+
+
+def same(a, b):
+    return np.array_equal(a[0], b[0]) and np.array_equal(
+        np.asarray(a[1], np.float32).view(np.uint32), np.asarray(b[1], np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("mips", [True, False])
+@pytest.mark.parametrize("k", [10, 100])
+def test_matches_oracle(oracle, uv, tc_mode, mips, k):
+    n, nq, dim = 70_000, 48, 128
+    base = rand_rows(n, dim, 5) * np.float32(2.5)
+    base[::7] *= np.float32(0.1)  # spread the norms (MIPS)
+    queries = rand_rows(nq, dim, 6)
+    ocodec = oracle.Codec(dim, 2, 8)
+    enc = ocodec.encode_batch(base)
+    want = ocodec.search_topk(enc, queries, k, norms=oracle.l2_norms(base) if mips else None)
+    codec = uv.Codec(dim, 2, 8)
+    index = uv.Index(codec)
+    index.add_batch(base)
+    tc_mode(2)
+    got = index.search(queries, k, mips=mips)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(got[1].view(np.uint32), want[1].view(np.uint32))
+
+
+@pytest.mark.parametrize("bits,mem", [(1, 8), (2, 6), (3, 6), (4, 8), (2, 10)])
+def test_code_shapes_match_exact_kernel(uv, tc_mode, bits, mem):
+    """Pair table (mem + 2 bits <= 13) and single-value table paths."""
+    n, nq, dim = 120_000, 200, 128
+    base = rand_rows(n, dim, bits * 10 + mem)
+    queries = rand_rows(nq, dim, 99)
+    index = uv.Index(uv.Codec(dim, bits, mem))
+    index.add_batch(base)
+    a, b = search_both(uv, index, queries, 32, True, tc_mode)
+    assert same(a, b)
+
+
+def test_full_size_bench_workload_matches_exact_kernel(uv, tc_mode):
+    """1M heavy-tailed, mean-centered rows (the bench generator), k = 100 and
+    10, MIPS: identical to the exact kernel."""
+    import bench
+
+    base, queries = bench.make_data(1_000_000, 1000)
+    index = uv.Index(uv.Codec(128, 2, 8))
+    index.add_batch(base)
+    for k in (100, 10):
+        a, b = search_both(uv, index, queries, k, True, tc_mode)
+        assert same(a, b), k
+
+
+def test_ties_zero_rows_degenerate_queries_ragged_sizes(uv, tc_mode):
+    n, nq, dim = 65_537, 131, 128  # neither a multiple of the tile sizes
+    base = rand_rows(n, dim, 17)
+    base[1000:1400] = base[5]      # exact ties: ranked by record index
+    base[2000:2100] = 0.0          # zero rows
+    queries = rand_rows(nq, dim, 18)
+    queries[3] = 0.0               # degenerate query: empty result
+    queries[7] = base[5]
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    index.add_batch(base)
+    for mips in (True, False):
+        a, b = search_both(uv, index, queries, 100, mips, tc_mode)
+        assert same(a, b), mips
+        assert (a[0][3] == -1).all()
+
+
+def test_candidate_overflow_falls_back_to_the_exact_scan(uv, tc_mode):
+    """Every row identical: every record ties with the k-th score, so every
+    record is a candidate and the list overflows; the exact scan answers."""
+    n, nq, dim = 40_000, 20, 128
+    base = np.repeat(rand_rows(1, dim, 3), n, axis=0)
+    base[::2] *= np.float32(3.0)
+    queries = rand_rows(nq, dim, 4)
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    index.add_batch(base)
+    a, b = search_both(uv, index, queries, 50, True, tc_mode)
+    assert same(a, b)
+
+
+def test_device_tensors(uv, tc_mode):
+    import torch
+
+    n, nq, dim = 70_000, 64, 128
+    base = rand_rows(n, dim, 8)
+    queries = rand_rows(nq, dim, 9)
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    index.add_batch(torch.from_numpy(base).cuda())
+    tc_mode(2)
+    ids, sc = index.search(torch.from_numpy(queries).cuda(), 10, mips=True)
+    tc_mode(1)
+    ids2, sc2 = index.search(queries, 10, mips=True)
+    assert np.array_equal(ids.cpu().numpy(), ids2)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint32), sc2.view(np.uint32))

@@ -11,6 +11,7 @@ namespace uvcapi {
 thread_local std::string g_err;
 std::mutex g_prof_mu;
 int64_t g_scan_splits = 0;
+int g_tc_mode = 0;
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
 
@@ -91,6 +92,37 @@ int uv_codec_create(const uv_config *cfg, uv_codec **out) {
   }
   r.signs = c->d_signs;
   c->plan_status = uvb::encode_plan(cfg->dim, cfg->bits, cfg->mem, &c->plan, &c->plan_why);
+  // fp16 decode table of the tensor-core prefilter: two code values per
+  // (W + b)-bit field when that table is at most 32 KB, else one per window
+  {
+    const int W = cfg->mem + cfg->bits;
+    std::vector<uint32_t> t;
+    if (W + cfg->bits <= 13) {
+      c->tc_pair = 1;
+      t.resize((size_t)1 << (W + cfg->bits));
+      const uint32_t wmask = (1u << W) - 1u;
+      for (size_t f = 0; f < t.size(); f++) {
+        const __half lo = __float2half_rn(c->h_table[f >> cfg->bits]);
+        const __half hi = __float2half_rn(c->h_table[f & wmask]);
+        t[f] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+      }
+    } else if (W <= 14) {
+      c->tc_pair = 0;
+      t.assign(((size_t)1 << W) / 2, 0u);
+      for (size_t w = 0; w < ((size_t)1 << W); w++) {
+        const uint32_t h = __half_as_ushort(__float2half_rn(c->h_table[w]));
+        t[w / 2] |= (w & 1) ? (h << 16) : h;
+      }
+    }
+    if (!t.empty() && cudaMalloc(&c->d_tc_table, sizeof(uint32_t) * t.size()) == cudaSuccess &&
+        cudaMemcpy(c->d_tc_table, t.data(), sizeof(uint32_t) * t.size(), cudaMemcpyHostToDevice) ==
+            cudaSuccess) {
+      c->tc_table_words = (int)t.size();
+      c->tc_ok = true;
+    } else {
+      cudaGetLastError();
+    }
+  }
   *out = c;
   return UV_OK;
 }
@@ -101,6 +133,7 @@ int uv_codec_destroy(uv_codec *c) {
     DeviceGuard g(c->cfg.device);
     cudaFree(c->d_table);
     cudaFree(c->d_signs);
+    cudaFree(c->d_tc_table);
   }
   delete c;
   return UV_OK;
@@ -605,44 +638,17 @@ int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *ce
 
 }  // namespace uvcapi
 
-extern "C" {
+namespace {
 
-int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_t k, int32_t mode,
-                    int64_t *ids_out, float *scores_out, void *stream) {
-  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
-    return fail(UV_EINVAL, "null argument");
-  if (nq < 0) return fail(UV_EINVAL, "negative size");
-  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
-  if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
-  if (nq == 0) return UV_OK;
+// The exact CUDA-core scan over prepared queries (flat_scan_kernel, or the
+// K-chunked kernel for wide rows) with a per-split top-k, then the merge.
+int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+               int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+               Scratch &sc) {
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
-  if (d % 16 != 0)
-    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
   const int dev = c->cfg.device;
-  DeviceGuard g(dev);
-  cudaStream_t st = (cudaStream_t)stream;
-  Scratch sc(st);
-  Outputs outs;
-  const float *d_q = nullptr;
-  UV_TRY(stage_in(queries, (size_t)nq * d, dev, sc, &d_q));
-  int64_t *d_ids = nullptr;
-  float *d_scores = nullptr;
-  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
-  if (scores_out != nullptr) {
-    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
-  } else {
-    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
-  }
-  // 1) prepare queries
   const int dim_pad = (d + 3) & ~3;
-  float *q_r = nullptr, *qc = nullptr;
-  uint32_t *degen = nullptr;
-  UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
-  UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
-  UV_TRY(sc.alloc(&degen, (size_t)nq));
-  UV_TRY(prep_launch(c, d_q, nq, ix->centroids, ix->n_centroids, q_r, qc, degen, nullptr, st));
-  // 2) scan with a per-split top-k
   const int64_t n = ix->n;
   int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;
   const int rw = c->code_stride / 4;
@@ -725,6 +731,242 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   }
   // 3) merge the splits
   UV_TRY(merge_launch(nq, (int)splits, k, k, part_key, nullptr, part_id, d_ids, d_scores, st));
+  return UV_OK;
+}
+
+// Tensor-core prefilter + exact rescoring (tcscan.cu).  Sets *used = false
+// when the configuration is outside what the kernels are built for.
+int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+              int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+              Scratch &sc, bool *used) {
+  *used = false;
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int64_t n = ix->n;
+  if (g_tc_mode == 1 || !c->tc_ok || d != 128 || ix->n_centroids != 0) return UV_OK;
+  const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
+  const int64_t n_tiles = (n + TN - 1) / TN;
+  // a useful threshold needs several tiles per top-k slot
+  if (n_tiles < (g_tc_mode == 2 ? (int64_t)k : 4 * (int64_t)k)) return UV_OK;
+  const size_t smem = uvb::tc_scan_smem_bytes(d, c->tc_table_words * 4);
+  const void *k1 = uvb::tc_scan_kernel_ptr(1, c->cfg.bits, d, c->tc_pair != 0);
+  const void *k2 = uvb::tc_scan_kernel_ptr(2, c->cfg.bits, d, c->tc_pair != 0);
+  if (smem == 0 || smem > 227 * 1024 || k1 == nullptr || k2 == nullptr) return UV_OK;
+  *used = true;
+  const int dev = c->cfg.device;
+  const int dim_pad = (d + 3) & ~3;
+  const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
+  (void)qc;
+  // per-record bound constants
+  float *g = nullptr, *cc = nullptr;
+  UV_TRY(sc.alloc(&g, (size_t)n));
+  UV_TRY(sc.alloc(&cc, (size_t)n));
+  {
+    uvb::TcBoundsParams bp;
+    std::memset(&bp, 0, sizeof(bp));
+    bp.dim = d;
+    bp.mem = c->cfg.mem;
+    bp.bits = c->cfg.bits;
+    bp.code_stride = c->code_stride;
+    bp.mips = mips;
+    bp.n = n;
+    bp.eps = 1.5e-3;
+    bp.codes = ix->codes;
+    bp.start = ix->start;
+    bp.code = c->d_table;
+    bp.rescale = ix->rescale;
+    bp.rnorm = ix->rnorm;
+    bp.norms = ix->norms;
+    bp.g = g;
+    bp.c = cc;
+    void *args[] = {&bp};
+    ProfScope ps("tc_bounds", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::tc_record_bounds_kernel, dim3((unsigned)((n + 127) / 128)),
+                           dim3(128), args, 0, st));
+  }
+  // units: query tiles x record splits, filling whole waves of one CTA per SM
+  const int64_t qtiles = (nq + TM - 1) / TM;
+  const int64_t slots = sm_count(dev);
+  const int64_t max_splits = std::max<int64_t>(1, std::min<int64_t>(n_tiles / 8, 64));
+  int64_t splits = 1;
+  double best_eff = 0.0;
+  for (int64_t s2 = 1; s2 <= max_splits; s2++) {
+    const int64_t ctas = qtiles * s2;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double eff = (double)ctas / (double)(waves * slots) - 0.002 * (double)waves;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      splits = s2;
+    }
+  }
+  float *tmax = nullptr, *theta = nullptr;
+  uint32_t *cand = nullptr;
+  int *cand_cnt = nullptr, *flags = nullptr;
+  int32_t *over_list = nullptr;
+  const int cap = 2048;
+  UV_TRY(sc.alloc(&tmax, (size_t)nq * n_tiles));
+  UV_TRY(sc.alloc(&theta, (size_t)nq));
+  UV_TRY(sc.alloc(&cand, (size_t)nq * cap));
+  UV_TRY(sc.alloc(&cand_cnt, (size_t)nq));
+  UV_TRY(sc.alloc(&flags, 2));  // [0] kernel timeout, [1] overflowed queries
+  UV_TRY(sc.alloc(&over_list, (size_t)nq));
+  UV_CK(cudaMemsetAsync(cand_cnt, 0, sizeof(int) * nq, st));
+  UV_CK(cudaMemsetAsync(flags, 0, sizeof(int) * 2, st));
+  uvb::TcScanParams tp;
+  std::memset(&tp, 0, sizeof(tp));
+  tp.mem = c->cfg.mem;
+  tp.q_stride = dim_pad;
+  tp.table_words = c->tc_table_words;
+  tp.cand_cap = cap;
+  tp.nq = nq;
+  tp.n = n;
+  tp.n_tiles = n_tiles;
+  tp.q_r = q_r;
+  tp.degenerate = degen;
+  tp.codes = ix->codes;
+  tp.code_stride = c->code_stride;
+  tp.start = ix->start;
+  tp.table = c->d_tc_table;
+  tp.g = g;
+  tp.c = cc;
+  tp.tmax = tmax;
+  tp.theta = theta;
+  tp.cand = cand;
+  tp.cand_cnt = cand_cnt;
+  tp.err = flags;
+  const dim3 grid((unsigned)qtiles, (unsigned)splits);
+  UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  {
+    void *args[] = {&tp};
+    ProfScope ps("tc_pass1", st);
+    UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), args, smem, st));
+  }
+  {
+    ProfScope ps("tc_theta", st);
+    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_tiles, nq, k, theta);
+    UV_CK(cudaGetLastError());
+  }
+  {
+    void *args[] = {&tp};
+    ProfScope ps("tc_pass2", st);
+    UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), args, smem, st));
+  }
+  {
+    uvb::TcRescoreParams rp;
+    std::memset(&rp, 0, sizeof(rp));
+    rp.dim = d;
+    rp.mem = c->cfg.mem;
+    rp.bits = c->cfg.bits;
+    rp.code_stride = c->code_stride;
+    rp.q_stride = dim_pad;
+    rp.cap = cap;
+    rp.k = k;
+    rp.mips = mips;
+    rp.table_len = c->table_len;
+    rp.table_in_smem = (size_t)c->table_len * 4 <= 64 * 1024 ? 1 : 0;
+    rp.nq = nq;
+    rp.q_r = q_r;
+    rp.degenerate = degen;
+    rp.codes = ix->codes;
+    rp.start = ix->start;
+    rp.code = c->d_table;
+    rp.rescale = ix->rescale;
+    rp.rnorm = ix->rnorm;
+    rp.norms = ix->norms;
+    rp.cand = cand;
+    rp.cand_cnt = cand_cnt;
+    rp.ids = ix->ids;
+    rp.out_id = d_ids;
+    rp.out_score = d_scores;
+    rp.over_list = over_list;
+    rp.n_over = flags + 1;
+    const size_t rsmem = (size_t)cap * 8 + (size_t)d * 4 + (rp.table_in_smem ? (size_t)c->table_len * 4 : 0);
+    UV_CK(cudaFuncSetAttribute(uvb::tc_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)rsmem));
+    void *args[] = {&rp};
+    ProfScope ps("tc_rescore", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::tc_rescore_kernel, dim3((unsigned)nq), dim3(256), args,
+                           rsmem, st));
+  }
+  int h_flags[2] = {0, 0};
+  UV_CK(cudaMemcpyAsync(h_flags, flags, sizeof(h_flags), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  if (h_flags[0]) return fail(UV_ETIMEDOUT, "tensor-core scan: a pipeline wait timed out");
+  if (h_flags[1] > 0) {
+    // queries whose candidate list overflowed: exact scan of those rows
+    const int64_t m = h_flags[1];
+    std::vector<int32_t> rows((size_t)m);
+    UV_CK(cudaMemcpyAsync(rows.data(), over_list, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, st));
+    UV_CK(cudaStreamSynchronize(st));
+    float *sub_q = nullptr;
+    uint32_t *sub_deg = nullptr;
+    int64_t *sub_ids = nullptr;
+    float *sub_sc = nullptr;
+    UV_TRY(sc.alloc(&sub_q, (size_t)m * dim_pad));
+    UV_TRY(sc.alloc(&sub_deg, (size_t)m));
+    UV_TRY(sc.alloc(&sub_ids, (size_t)m * k));
+    UV_TRY(sc.alloc(&sub_sc, (size_t)m * k));
+    for (int64_t i = 0; i < m; i++) {
+      UV_CK(cudaMemcpyAsync(sub_q + i * dim_pad, q_r + (int64_t)rows[i] * dim_pad,
+                            sizeof(float) * dim_pad, cudaMemcpyDeviceToDevice, st));
+      UV_CK(cudaMemcpyAsync(sub_deg + i, degen + rows[i], sizeof(uint32_t),
+                            cudaMemcpyDeviceToDevice, st));
+    }
+    UV_TRY(exact_scan(ix, sub_q, qc, sub_deg, m, k, mode, sub_ids, sub_sc, st, sc));
+    for (int64_t i = 0; i < m; i++) {
+      UV_CK(cudaMemcpyAsync(d_ids + (int64_t)rows[i] * k, sub_ids + i * k, sizeof(int64_t) * k,
+                            cudaMemcpyDeviceToDevice, st));
+      UV_CK(cudaMemcpyAsync(d_scores + (int64_t)rows[i] * k, sub_sc + i * k, sizeof(float) * k,
+                            cudaMemcpyDeviceToDevice, st));
+    }
+    UV_CK(cudaStreamSynchronize(st));  // `rows` is host memory of this frame
+  }
+  return UV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                    int64_t *ids_out, float *scores_out, void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
+  if (nq == 0) return UV_OK;
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  if (d % 16 != 0)
+    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * d, dev, sc, &d_q));
+  int64_t *d_ids = nullptr;
+  float *d_scores = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  // 1) prepare queries
+  const int dim_pad = (d + 3) & ~3;
+  float *q_r = nullptr, *qc = nullptr;
+  uint32_t *degen = nullptr;
+  UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
+  UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
+  UV_TRY(sc.alloc(&degen, (size_t)nq));
+  UV_TRY(prep_launch(c, d_q, nq, ix->centroids, ix->n_centroids, q_r, qc, degen, nullptr, st));
+  bool used = false;
+  UV_TRY(tc_search(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc, &used));
+  if (!used) UV_TRY(exact_scan(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc));
   return outs.finish(st);
 }
 
@@ -763,6 +1005,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "encode_back") == 0) {
     if (value < 0 || value > 2) return fail(UV_EINVAL, "encode_back must be 0, 1 or 2");
     uvb::g_encode_back_mode = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "tc_scan") == 0) {
+    if (value < 0 || value > 2) return fail(UV_EINVAL, "tc_scan must be 0, 1 or 2");
+    g_tc_mode = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "scan_splits") == 0) {

@@ -4,6 +4,8 @@
 
 #include "ultravec_b200.h"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -145,6 +147,7 @@ struct ProfRec {
 };
 extern std::mutex g_prof_mu;
 extern int64_t g_scan_splits;  // uv_set_tuning("scan_splits")
+extern int g_tc_mode;          // uv_set_tuning("tc_scan")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 
@@ -195,6 +198,9 @@ struct uv_codec {
   uvb::EncodePlan plan;
   int plan_status = 0;
   std::string plan_why;
+  uint32_t *d_tc_table = nullptr;  // fp16 decode table of the tensor-core prefilter
+  int tc_table_words = 0, tc_pair = 0;
+  bool tc_ok = false;
 };
 
 struct uv_index {

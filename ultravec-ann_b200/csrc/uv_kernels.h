@@ -126,6 +126,52 @@ struct RerankParams {
   float *out_score;
 };
 
+// Tensor-core prefilter of the flat scan (tcscan.cu).
+struct TcScanParams {
+  int mem, q_stride, table_words, cand_cap;
+  int64_t nq, n, n_tiles;
+  const float *q_r;            // nq x q_stride rotated unit queries
+  const uint32_t *degenerate;  // nq
+  const uint8_t *codes;
+  int code_stride;
+  const uint32_t *start;
+  const uint32_t *table;       // fp16 pair table (half2 words) or fp16 table
+  const float *g, *c;          // per-record bound constants
+  float *tmax;                 // mode 1: nq x n_tiles lower-bound tile maxima
+  const float *theta;          // mode 2: per-query threshold
+  uint32_t *cand;              // mode 2: nq x cand_cap record indices
+  int *cand_cnt;               // mode 2: nq (zeroed before the launch)
+  int *err;
+};
+
+struct TcBoundsParams {
+  int dim, mem, bits, code_stride, mips;
+  int64_t n;
+  double eps;
+  const uint8_t *codes;
+  const uint32_t *start;
+  const float *code;           // f32 code table
+  const float *rescale, *rnorm, *norms;
+  float *g, *c;
+};
+
+struct TcRescoreParams {
+  int dim, mem, bits, code_stride, q_stride, cap, k, mips, table_len, table_in_smem;
+  int64_t nq;
+  const float *q_r;
+  const uint32_t *degenerate;
+  const uint8_t *codes;
+  const uint32_t *start;
+  const float *code, *rescale, *rnorm, *norms;
+  const uint32_t *cand;
+  const int *cand_cnt;
+  const int64_t *ids;
+  int64_t *out_id;
+  float *out_score;
+  int32_t *over_list;
+  int *n_over;
+};
+
 struct MergeParams {
   int64_t nq;
   int n_lists, k_in, k, pow2, warps;
@@ -144,6 +190,17 @@ const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k);
 size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k);
 constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
+
+// tcscan.cu
+const void *tc_scan_kernel_ptr(int mode, int bits, int dim, bool pair);
+size_t tc_scan_smem_bytes(int dim, int table_bytes);
+int tc_threads();
+int tc_tile_records();
+int tc_tile_queries();
+__global__ void tc_record_bounds_kernel(const TcBoundsParams p);
+__global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
+                                float *theta);
+__global__ void tc_rescore_kernel(const TcRescoreParams p);
 
 // ivf.cu
 template <int MODE>
