@@ -181,7 +181,7 @@ METRIC = "flat codes-only MIPS queries/s and encode vectors/s at 1/2/4/8 B200; %
 
 
 # kernel families of one step (uv_profile_read names)
-SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_bounds", "tc_pass1",
+SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
                  "tc_theta", "tc_pass2", "tc_rescore")
 
 
@@ -280,6 +280,7 @@ def main():
     barrier()
     kern = {name: uv.profile_read(name) for name in SCAN_FAMILIES}
     launches_total = uv.profile_read("*")[1]
+    tc_candidates = uv.profile_read("tc_candidates")[1]
     uv.profile_enable(False)
     clk = clocks.stop() if clocks else None
 
@@ -376,7 +377,8 @@ def main():
                     "peak_source": "bf16_tflops of MEASURED_PEAKS.json (dense f16 and bf16 "
                                    "tensor peaks are equal)" if "bf16_tflops" in peaks
                                    else "fallback 1.59 PFLOP/s",
-                    "flops_per_launch": flops, "avg_launch_ms": avg, "hbm_model": hbm_model}
+                    "flops_per_launch": flops, "avg_launch_ms": avg, "hbm_model": hbm_model,
+                    "candidates_per_query": tc_candidates / nq}
         else:
             scan_k_ms, scan_k_n = kern["flat_scan"]
             avg_scan = scan_k_ms / max(scan_k_n, 1)

@@ -187,16 +187,20 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * on it): "scan_splits" fixes the number of record ranges each query tile is
  * split into (0 = automatic); "encode_back" places the encoder's
  * back-pointers for codecs created afterwards (0 automatic, 1 global scratch,
- * 2 shared memory whenever one row's array fits).  Process-wide; returns UV_EINVAL for an unknown
- * key. */
+ * 2 shared memory whenever one row's array fits); "tc_scan" selects the flat
+ * search's tensor-core prefilter (0 automatic, 1 never, 2 wherever it is
+ * built).  Process-wide; returns UV_EINVAL for an unknown key. */
 int uv_set_tuning(const char *key, int64_t value);
 
 /* Measurement aid, no counterpart in the reference: while enabled, every
  * kernel the library launches is bracketed by CUDA events on its launch
  * stream.  uv_profile_read waits for those events and returns the summed
  * device time and launch count of one kernel family ("encode",
- * "prep_queries", "flat_scan", "merge_topk", or "*" for all).  Enabling
- * clears previous records.  Not for concurrent use. */
+ * "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
+ * "tc_theta", "tc_pass2", "tc_rescore", the IVF families "ivf_*", or "*" for
+ * all).  "tc_candidates" returns, as the count, the number of candidates the
+ * last tensor-core search scored exactly.  Enabling clears previous records.
+ * Not for concurrent use. */
 int uv_profile_enable(int32_t on);
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches);
 

@@ -6,14 +6,47 @@
 // thread-local message.  No exception or abort crosses the ABI.
 #include "capi_internal.h"
 
+#include <atomic>
+
+#include <cuda.h>
+
 namespace uvcapi {
 
 thread_local std::string g_err;
 std::mutex g_prof_mu;
 int64_t g_scan_splits = 0;
 int g_tc_mode = 0;
+std::atomic<int64_t> g_tc_last_candidates{0};
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
+
+cudaMemPool_t scratch_pool() {
+  static std::mutex mu;
+  static std::vector<cudaMemPool_t> pools;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)pools.size() <= dev) pools.resize(dev + 1, nullptr);
+  if (pools[dev] == nullptr) {
+    cudaMemPoolProps props;
+    std::memset(&props, 0, sizeof(props));
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    pools[dev] = pool;
+  }
+  return pools[dev];
+}
 
 }  // namespace uvcapi
 
@@ -92,37 +125,6 @@ int uv_codec_create(const uv_config *cfg, uv_codec **out) {
   }
   r.signs = c->d_signs;
   c->plan_status = uvb::encode_plan(cfg->dim, cfg->bits, cfg->mem, &c->plan, &c->plan_why);
-  // fp16 decode table of the tensor-core prefilter: two code values per
-  // (W + b)-bit field when that table is at most 32 KB, else one per window
-  {
-    const int W = cfg->mem + cfg->bits;
-    std::vector<uint32_t> t;
-    if (W + cfg->bits <= 13) {
-      c->tc_pair = 1;
-      t.resize((size_t)1 << (W + cfg->bits));
-      const uint32_t wmask = (1u << W) - 1u;
-      for (size_t f = 0; f < t.size(); f++) {
-        const __half lo = __float2half_rn(c->h_table[f >> cfg->bits]);
-        const __half hi = __float2half_rn(c->h_table[f & wmask]);
-        t[f] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-      }
-    } else if (W <= 14) {
-      c->tc_pair = 0;
-      t.assign(((size_t)1 << W) / 2, 0u);
-      for (size_t w = 0; w < ((size_t)1 << W); w++) {
-        const uint32_t h = __half_as_ushort(__float2half_rn(c->h_table[w]));
-        t[w / 2] |= (w & 1) ? (h << 16) : h;
-      }
-    }
-    if (!t.empty() && cudaMalloc(&c->d_tc_table, sizeof(uint32_t) * t.size()) == cudaSuccess &&
-        cudaMemcpy(c->d_tc_table, t.data(), sizeof(uint32_t) * t.size(), cudaMemcpyHostToDevice) ==
-            cudaSuccess) {
-      c->tc_table_words = (int)t.size();
-      c->tc_ok = true;
-    } else {
-      cudaGetLastError();
-    }
-  }
   *out = c;
   return UV_OK;
 }
@@ -133,7 +135,6 @@ int uv_codec_destroy(uv_codec *c) {
     DeviceGuard g(c->cfg.device);
     cudaFree(c->d_table);
     cudaFree(c->d_signs);
-    cudaFree(c->d_tc_table);
   }
   delete c;
   return UV_OK;
@@ -734,6 +735,32 @@ int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint
   return UV_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tiled_fn(EncodeTiledFn *out) {
+  static std::mutex mu;
+  static EncodeTiledFn fn = nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (fn == nullptr) {
+    void *pfn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &pfn, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || pfn == nullptr) {
+      cudaGetLastError();
+      return fail(UV_ECUDA, "cuTensorMapEncodeTiled is not available");
+    }
+    fn = (EncodeTiledFn)pfn;
+  }
+  *out = fn;
+  return UV_OK;
+}
+
 // Tensor-core prefilter + exact rescoring (tcscan.cu).  Sets *used = false
 // when the configuration is outside what the kernels are built for.
 int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
@@ -743,46 +770,61 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   const int64_t n = ix->n;
-  if (g_tc_mode == 1 || !c->tc_ok || d != 128 || ix->n_centroids != 0) return UV_OK;
+  if (g_tc_mode == 1 || d != uvb::tc_dim() || ix->n_centroids != 0) return UV_OK;
   const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
   const int64_t n_tiles = (n + TN - 1) / TN;
-  // a useful threshold needs several tiles per top-k slot
-  if (n_tiles < (g_tc_mode == 2 ? (int64_t)k : 4 * (int64_t)k)) return UV_OK;
-  const size_t smem = uvb::tc_scan_smem_bytes(d, c->tc_table_words * 4);
-  const void *k1 = uvb::tc_scan_kernel_ptr(1, c->cfg.bits, d, c->tc_pair != 0);
-  const void *k2 = uvb::tc_scan_kernel_ptr(2, c->cfg.bits, d, c->tc_pair != 0);
-  if (smem == 0 || smem > 227 * 1024 || k1 == nullptr || k2 == nullptr) return UV_OK;
+  const int64_t n_groups = 2 * n_tiles;
+  // a useful threshold needs several groups per top-k slot
+  if (n_groups < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
+  if (n_tiles * TN > INT32_MAX) return UV_OK;
   *used = true;
   const int dev = c->cfg.device;
   const int dim_pad = (d + 3) & ~3;
   const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
   (void)qc;
-  // per-record bound constants
-  float *g = nullptr, *cc = nullptr;
-  UV_TRY(sc.alloc(&g, (size_t)n));
-  UV_TRY(sc.alloc(&cc, (size_t)n));
+  // fp16 records and per-record bound constants
+  const int64_t n_pad = n_tiles * TN;
+  uint16_t *x16 = nullptr;
+  float2 *gc = nullptr;
+  UV_TRY(sc.alloc(&x16, (size_t)n_pad * d));
+  UV_TRY(sc.alloc(&gc, (size_t)n_pad));
   {
-    uvb::TcBoundsParams bp;
-    std::memset(&bp, 0, sizeof(bp));
-    bp.dim = d;
-    bp.mem = c->cfg.mem;
-    bp.bits = c->cfg.bits;
-    bp.code_stride = c->code_stride;
-    bp.mips = mips;
-    bp.n = n;
-    bp.eps = 1.5e-3;
-    bp.codes = ix->codes;
-    bp.start = ix->start;
-    bp.code = c->d_table;
-    bp.rescale = ix->rescale;
-    bp.rnorm = ix->rnorm;
-    bp.norms = ix->norms;
-    bp.g = g;
-    bp.c = cc;
-    void *args[] = {&bp};
-    ProfScope ps("tc_bounds", st);
-    UV_CK(cudaLaunchKernel((const void *)uvb::tc_record_bounds_kernel, dim3((unsigned)((n + 127) / 128)),
-                           dim3(128), args, 0, st));
+    uvb::TcPrepareParams pp;
+    std::memset(&pp, 0, sizeof(pp));
+    pp.mem = c->cfg.mem;
+    pp.bits = c->cfg.bits;
+    pp.code_stride = c->code_stride;
+    pp.mips = mips;
+    pp.n = n;
+    pp.n_pad = n_pad;
+    pp.eps = 1.5e-3;
+    pp.codes = ix->codes;
+    pp.start = ix->start;
+    pp.code = c->d_table;
+    pp.rescale = ix->rescale;
+    pp.rnorm = ix->rnorm;
+    pp.norms = ix->norms;
+    pp.x16 = x16;
+    pp.gc = gc;
+    void *args[] = {&pp};
+    ProfScope ps("tc_prepare", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
+                           dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
+  }
+  // TMA map of the fp16 records: rows of 128 fp16 (256 B), boxes of 64 x 256
+  // with the 128-byte swizzle of the MMA operand layout
+  CUtensorMap tmap;
+  {
+    EncodeTiledFn enc = nullptr;
+    UV_TRY(encode_tiled_fn(&enc));
+    const cuuint64_t gdim[2] = {(cuuint64_t)d, (cuuint64_t)n_pad};
+    const cuuint64_t gstride[1] = {(cuuint64_t)d * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)TN};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)x16, gdim, gstride,
+                           box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled failed");
   }
   // units: query tiles x record splits, filling whole waves of one CTA per SM
   const int64_t qtiles = (nq + TM - 1) / TM;
@@ -804,51 +846,48 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   int *cand_cnt = nullptr, *flags = nullptr;
   int32_t *over_list = nullptr;
   const int cap = 2048;
-  UV_TRY(sc.alloc(&tmax, (size_t)nq * n_tiles));
+  UV_TRY(sc.alloc(&tmax, (size_t)nq * n_groups));
   UV_TRY(sc.alloc(&theta, (size_t)nq));
   UV_TRY(sc.alloc(&cand, (size_t)nq * cap));
   UV_TRY(sc.alloc(&cand_cnt, (size_t)nq));
-  UV_TRY(sc.alloc(&flags, 2));  // [0] kernel timeout, [1] overflowed queries
+  UV_TRY(sc.alloc(&flags, 4));  // [0] timeout, [1] overflowed queries, [2..3] candidates
   UV_TRY(sc.alloc(&over_list, (size_t)nq));
   UV_CK(cudaMemsetAsync(cand_cnt, 0, sizeof(int) * nq, st));
-  UV_CK(cudaMemsetAsync(flags, 0, sizeof(int) * 2, st));
+  UV_CK(cudaMemsetAsync(flags, 0, sizeof(int) * 4, st));
   uvb::TcScanParams tp;
   std::memset(&tp, 0, sizeof(tp));
-  tp.mem = c->cfg.mem;
   tp.q_stride = dim_pad;
-  tp.table_words = c->tc_table_words;
   tp.cand_cap = cap;
   tp.nq = nq;
   tp.n = n;
   tp.n_tiles = n_tiles;
+  tp.n_groups = n_groups;
   tp.q_r = q_r;
   tp.degenerate = degen;
-  tp.codes = ix->codes;
-  tp.code_stride = c->code_stride;
-  tp.start = ix->start;
-  tp.table = c->d_tc_table;
-  tp.g = g;
-  tp.c = cc;
+  tp.gc = gc;
   tp.tmax = tmax;
   tp.theta = theta;
   tp.cand = cand;
   tp.cand_cnt = cand_cnt;
   tp.err = flags;
+  const size_t smem = uvb::tc_scan_smem_bytes();
+  const void *k1 = uvb::tc_scan_kernel_ptr(1);
+  const void *k2 = uvb::tc_scan_kernel_ptr(2);
   const dim3 grid((unsigned)qtiles, (unsigned)splits);
   UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   {
-    void *args[] = {&tp};
+    void *args[] = {&tp, &tmap};
     ProfScope ps("tc_pass1", st);
     UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), args, smem, st));
   }
   {
     ProfScope ps("tc_theta", st);
-    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_tiles, nq, k, theta);
+    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_groups, nq, k, theta);
     UV_CK(cudaGetLastError());
   }
   {
-    void *args[] = {&tp};
+    void *args[] = {&tp, &tmap};
     ProfScope ps("tc_pass2", st);
     UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), args, smem, st));
   }
@@ -881,6 +920,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     rp.out_score = d_scores;
     rp.over_list = over_list;
     rp.n_over = flags + 1;
+    rp.n_cand = (unsigned long long *)(flags + 2);
     const size_t rsmem = (size_t)cap * 8 + (size_t)d * 4 + (rp.table_in_smem ? (size_t)c->table_len * 4 : 0);
     UV_CK(cudaFuncSetAttribute(uvb::tc_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
@@ -889,9 +929,14 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_rescore_kernel, dim3((unsigned)nq), dim3(256), args,
                            rsmem, st));
   }
-  int h_flags[2] = {0, 0};
+  int h_flags[4] = {0, 0, 0, 0};
   UV_CK(cudaMemcpyAsync(h_flags, flags, sizeof(h_flags), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
+  {
+    unsigned long long nc = 0;
+    std::memcpy(&nc, h_flags + 2, sizeof(nc));
+    g_tc_last_candidates = (int64_t)nc;
+  }
   if (h_flags[0]) return fail(UV_ETIMEDOUT, "tensor-core scan: a pipeline wait timed out");
   if (h_flags[1] > 0) {
     // queries whose candidate list overflowed: exact scan of those rows
@@ -1034,6 +1079,12 @@ int uv_profile_enable(int32_t on) {
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
   if (kernel == nullptr || total_ms == nullptr || launches == nullptr)
     return fail(UV_EINVAL, "null argument");
+  if (std::strcmp(kernel, "tc_candidates") == 0) {
+    // statistic of the last tensor-core search: candidates scored exactly
+    *total_ms = 0.0;
+    *launches = g_tc_last_candidates.load();
+    return UV_OK;
+  }
   std::lock_guard<std::mutex> lk(g_prof_mu);
   double tot = 0.0;
   int64_t cnt = 0;

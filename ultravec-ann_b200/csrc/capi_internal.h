@@ -69,6 +69,11 @@ inline int classify(const void *p, int device, bool *on_device) {
   return UV_OK;
 }
 
+// The library's own stream-ordered memory pool on the current device.  It
+// keeps freed blocks (release threshold = max) so that back-to-back calls
+// reuse their scratch instead of mapping it again after every synchronize.
+cudaMemPool_t scratch_pool();
+
 // Stream-ordered scratch freed at scope exit (on the same stream).
 struct Scratch {
   cudaStream_t st;
@@ -82,7 +87,9 @@ struct Scratch {
     *out = nullptr;
     if (count == 0) count = 1;
     void *p = nullptr;
-    cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), st);
+    cudaMemPool_t pool = scratch_pool();
+    cudaError_t e = pool ? cudaMallocFromPoolAsync(&p, count * sizeof(T), pool, st)
+                         : cudaMallocAsync(&p, count * sizeof(T), st);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return fail(UV_ENOMEM, std::string("cudaMallocAsync: ") + cudaGetErrorString(e));
@@ -198,9 +205,6 @@ struct uv_codec {
   uvb::EncodePlan plan;
   int plan_status = 0;
   std::string plan_why;
-  uint32_t *d_tc_table = nullptr;  // fp16 decode table of the tensor-core prefilter
-  int tc_table_words = 0, tc_pair = 0;
-  bool tc_ok = false;
 };
 
 struct uv_index {

@@ -16,20 +16,27 @@
 //   g_r = rnorm_r / rescale_r (x norm_r) and c_r = (beta_r + 10u A_r) g_r,
 //   A_r = |q| |x_r| + beta_r bounding every f32 rounding of the score.
 //
-// Pass 1 (MODE 1) writes, per query and 256-record tile, the largest lower
-// bound; the k-th largest of those tile maxima is a score that at least k
+// Pass 1 (MODE 1) writes, per query and 128-record half tile, the largest
+// lower bound; the k-th largest of those maxima is a score that at least k
 // records reach, so it lower-bounds the exact k-th best (theta).  Pass 2
 // (MODE 2) appends every record whose upper bound reaches theta to the
 // query's candidate list; the exact top-k is among them, ties included.
 // The candidates are then scored exactly (tc_rescore_kernel) and ranked.
 //
+// Records are first decoded once per search into an fp16 row-major copy
+// (tc_prepare_records_kernel, which also computes the bound constants).  The
+// scan kernel then streams 256-record tiles of it into shared memory by TMA
+// (128-byte swizzle, the K-major operand layout of the MMA).
+//
 // CTA = one unit of 128 queries x a record range.  Warp roles:
-//   warps 0-3  epilogue: thread = query = TMEM lane; reads 256 dots per tile
-//   warps 4-7  decoders: windows -> fp16 code values in the swizzled K-major
-//              operand layout (a pair table gives two values per lookup)
+//   warps 0-7  epilogue: warp w reads TMEM lane quarter w % 4 (thread =
+//              query) and column half w / 4 (128 records) of each tile
 //   warp 8     TMEM allocation; lane 0 issues the MMAs
-// Two shared-memory operand stages and two TMEM accumulators (2 x 256
-// columns) are handed over with mbarriers; every wait is bounded.
+//   warp 9     lane 0 issues the TMA loads
+// Three shared-memory stages and two TMEM accumulators (2 x 256 columns)
+// are handed over with mbarriers; every wait is bounded.
+#include <cuda.h>
+
 #include "uv_kernels.h"
 #include "uv_tc.cuh"
 
@@ -39,37 +46,43 @@ namespace {
 
 constexpr int TC_M = 128;      // queries per unit
 constexpr int TC_N = 256;      // records per MMA tile
-constexpr int TC_THREADS = 288;
+constexpr int TC_D = 128;      // coordinates (K)
+constexpr int TC_STAGES = 3;
+constexpr int TC_THREADS = 320;
+constexpr int TC_EPI = 256;    // epilogue threads
 constexpr uint32_t kWaitLimit = 1u << 20;
 
-template <int D>
 struct TcLayout {
-  static constexpr int a_bytes = TC_M * D * 2;
-  static constexpr int b_bytes = TC_N * D * 2;
+  static constexpr int a_bytes = TC_M * TC_D * 2;        // 32 KB
+  static constexpr int b_bytes = TC_N * TC_D * 2;        // 64 KB per stage
   static constexpr int a = 0;
-  static constexpr int b0 = a + a_bytes;
-  static constexpr int b1 = b0 + b_bytes;
-  static constexpr int scal = b1 + b_bytes;               // 2 x 256 float2
-  static constexpr int bars = scal + 2 * TC_N * 8;        // 8 mbarriers
-  static constexpr int misc = bars + 8 * 8;               // tmem base, abort flag
-  static constexpr int table = misc + 64;                 // decode table
+  static constexpr int b = a + a_bytes;
+  static constexpr int bars = b + TC_STAGES * b_bytes;   // 10 mbarriers
+  static constexpr int misc = bars + 16 * 8;             // tmem base, abort flag
+  static constexpr int total = misc + 64;
 };
+
+// 3-input maximum (NaN-ignoring like fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 }  // namespace
 
-template <int MODE, int B, int D, bool PAIR>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_scan_kernel(const TcScanParams p) {
-  using L = TcLayout<D>;
+template <int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap) {
+  using L = TcLayout;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t *sa = sm + L::a;
-  float2 *scal = (float2 *)(sm + L::scal);
-  uint64_t *full = (uint64_t *)(sm + L::bars);  // [2]
-  uint64_t *empty = full + 2;                   // [2]
-  uint64_t *accf = full + 4;                    // [2]
-  uint64_t *acce = full + 6;                    // [2]
+  uint64_t *full = (uint64_t *)(sm + L::bars);  // [3]
+  uint64_t *empty = full + 3;                   // [3]
+  uint64_t *accf = full + 6;                    // [2]
+  uint64_t *acce = full + 8;                    // [2]
   uint32_t *tbase_s = (uint32_t *)(sm + L::misc);
   volatile int *abort_s = (volatile int *)(sm + L::misc + 4);
-  uint32_t *table = (uint32_t *)(sm + L::table);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t q0 = (int64_t)blockIdx.x * TC_M;
@@ -77,24 +90,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_scan_kernel(const TcScanPara
   const int64_t t_end = p.n_tiles * (blockIdx.y + 1) / gridDim.y;
   const int ntiles = (int)(t_end - t_begin);
 
-  // ---- setup: barriers, TMEM, decode table, query tile ----
+  // ---- setup: barriers, TMEM, query tile ----
   if (tid == 0) {
-    tc::mbar_init(&full[0], 128);
-    tc::mbar_init(&full[1], 128);
-    tc::mbar_init(&empty[0], 1);
-    tc::mbar_init(&empty[1], 1);
-    tc::mbar_init(&accf[0], 1);
-    tc::mbar_init(&accf[1], 1);
-    tc::mbar_init(&acce[0], 128);
-    tc::mbar_init(&acce[1], 128);
+    for (int s = 0; s < TC_STAGES; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      tc::mbar_init(&accf[a], 1);
+      tc::mbar_init(&acce[a], TC_EPI);
+    }
     *abort_s = 0;
     tc::mbar_fence_init();
   }
   if (warp == 8) tc::tmem_alloc(tbase_s, 512);
-  for (int e = tid; e < p.table_words; e += TC_THREADS) table[e] = __ldg(p.table + e);
   // queries -> fp16, swizzled K-major (zeros past nq and for degenerate rows)
-  for (int e = tid; e < TC_M * (D / 8); e += TC_THREADS) {
-    const int r = e / (D / 8), c = e - r * (D / 8);
+  for (int e = tid; e < TC_M * (TC_D / 8); e += TC_THREADS) {
+    const int r = e / (TC_D / 8), c = e - r * (TC_D / 8);
     const int64_t q = q0 + r;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (q < p.nq && !p.degenerate[q]) {
@@ -112,163 +124,148 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_scan_kernel(const TcScanPara
   tc::tc_fence_after();
   const uint32_t tmem = *tbase_s;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ================= epilogue =================
-    const int64_t q = q0 + tid;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int64_t q = q0 + quarter * 32 + lane;
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 128);
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
+      const int64_t tile = t_begin + it;
+      const int64_t rec0 = tile * TC_N + half * 128;
+      const float4 *gc = (const float4 *)(p.gc + rec0);  // (g, c) of two records
       if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
       }
       if (*abort_s) break;
       tc::tc_fence_after();
-      const int64_t tile = t_begin + it;
-      const int64_t rec0 = tile * TC_N;
-      const float2 *sc = scal + a * TC_N;
+      const uint32_t base = lane_base + (uint32_t)(a * TC_N);
       float best = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < TC_N; c0 += 32) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(a * TC_N + c0), r);
-        tc::tmem_ld_wait();
+      uint32_t mask0 = 0u, mask1 = 0u, mask2 = 0u, mask3 = 0u;
+      uint32_t ra[32], rb[32];
+      // bound of every record of 32-column chunk c, its max, and (pass 2)
+      // the mask of records that can reach theta
+      auto chunk = [&](const uint32_t(&cur)[32], int c) {
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float4 gc = *(const float4 *)&sc[c0 + j];  // (g, c) of two records
-          const float2 dd = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
-          const float2 g2 = make_float2(gc.x, gc.z);
-          const float2 c2 = MODE == 1 ? make_float2(-gc.y, -gc.w) : make_float2(gc.y, gc.w);
+          const float4 g4 = __ldg(gc + (32 * c + j) / 2);
+          const float2 dd = make_float2(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1]));
+          const float2 g2 = make_float2(g4.x, g4.z);
+          const float2 c2 = MODE == 1 ? make_float2(-g4.y, -g4.w) : make_float2(g4.y, g4.w);
           const float2 t2 = __ffma2_rn(dd, g2, c2);
           v[j] = t2.x;
           v[j + 1] = t2.y;
         }
-        float m = v[0];
+        float m = max3(v[0], v[1], v[2]);
 #pragma unroll
-        for (int j = 1; j < 31; j += 2) m = fmaxf(m, fmaxf(v[j], v[j + 1]));
+        for (int j = 3; j < 31; j += 2) m = max3(m, v[j], v[j + 1]);
         m = fmaxf(m, v[31]);
         if (MODE == 1) {
           best = fmaxf(best, m);
         } else if (qok && !(m < theta)) {
-          // rare: append every record of this chunk that can reach theta
-          // (unrolled so that v stays in registers)
+          uint32_t mk = 0;
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int64_t rec = rec0 + c0 + j;
-            if (!(v[j] < theta) && rec < p.n) {
-              const int pos = atomicAdd(&p.cand_cnt[q], 1);
-              if (pos < p.cand_cap) p.cand[q * (int64_t)p.cand_cap + pos] = (uint32_t)rec;
-            }
-          }
+          for (int j = 0; j < 32; j++) mk |= (!(v[j] < theta) ? 1u : 0u) << j;
+          // selects, not an indexed store: the masks stay in registers
+          mask0 = c == 0 ? mk : mask0;
+          mask1 = c == 1 ? mk : mask1;
+          mask2 = c == 2 ? mk : mask2;
+          mask3 = c == 3 ? mk : mask3;
         }
+      };
+      // TMEM -> registers two chunks at a time: the next load is in flight
+      // while the current chunk is processed
+      tc::tmem_ld32(base, ra);
+      tc::tmem_ld_wait();
+#pragma unroll 1
+      for (int c = 0; c < 4; c += 2) {
+        tc::tmem_ld32(base + (uint32_t)(32 * (c + 1)), rb);
+        chunk(ra, c);
+        tc::tmem_ld_wait();
+        if (c + 2 < 4) tc::tmem_ld32(base + (uint32_t)(32 * (c + 2)), ra);
+        chunk(rb, c + 1);
+        if (c + 2 < 4) tc::tmem_ld_wait();
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&acce[a]);
-      if (MODE == 1 && q < p.nq) p.tmax[q * p.n_tiles + tile] = qok ? best : -INFINITY;
-    }
-  } else if (warp < 8) {
-    // ================= decoders =================
-    const int u = tid - 128;
-    const int W = p.mem + B;
-    const int fshift = 32 - (PAIR ? W + B : W);
-    const uint32_t fmask = PAIR ? ((1u << (W + B)) - 1u) : ((1u << W) - 1u);
-    constexpr int CW = D * B / 32;  // code words per record
-    for (int it = 0; it < ntiles; it++) {
-      const int s = it & 1;
-      const int64_t rec0 = (t_begin + it) * TC_N;
-      // record images: [start | codes big-endian], shifted so window k starts at bit k*B
-      uint32_t img[2][CW + 1];
-      bool ok[2];
+      if (MODE == 1 && q < p.nq)
+        p.tmax[q * p.n_groups + 2 * tile + half] = qok ? best : -INFINITY;
+      if (MODE == 2) {
+        uint32_t mask[4] = {mask0, mask1, mask2, mask3};
+        // one reservation per thread and tile for all of its candidates
+        if (rec0 + 128 > p.n) {
+          const int64_t lim = p.n - rec0;  // records past n are padding
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int64_t rec = rec0 + u + h * 128;
-        ok[h] = rec < p.n;
-        const int64_t rr = ok[h] ? rec : 0;
-        const uint32_t *cw = (const uint32_t *)(p.codes + rr * (int64_t)p.code_stride);
-        uint32_t raw[CW + 2];
-        raw[0] = __ldg(p.start + rr);
-#pragma unroll
-        for (int w = 0; w < CW; w += 4) {
-          const uint4 x = __ldg((const uint4 *)(cw + w));
-          raw[w + 1] = __byte_perm(x.x, 0, 0x0123);
-          raw[w + 2] = __byte_perm(x.y, 0, 0x0123);
-          raw[w + 3] = __byte_perm(x.z, 0, 0x0123);
-          raw[w + 4] = __byte_perm(x.w, 0, 0x0123);
+          for (int c = 0; c < 4; c++) {
+            const int64_t room = lim - 32 * c;
+            mask[c] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
+          }
         }
-        raw[CW + 1] = 0u;
+        const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
+        if (cnt > 0) {
+          int pos = atomicAdd(&p.cand_cnt[q], cnt);
+          uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
 #pragma unroll
-        for (int w = 0; w <= CW; w++) img[h][w] = __funnelshift_l(raw[w + 1], raw[w], 32 - p.mem);
-      }
-      if (!tc::mbar_wait(&empty[s], ((it >> 1) & 1) ^ 1, kWaitLimit) ||
-          !tc::mbar_wait(&acce[s], ((it >> 1) & 1) ^ 1, kWaitLimit)) {
-        *abort_s = 1;
-        atomicExch(p.err, 1);
-      }
-      if (*abort_s) break;
-      uint8_t *sb = sm + (s ? L::b1 : L::b0);
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int row = u + h * 128;
-#pragma unroll
-        for (int c = 0; c < D / 8; c++) {
-          uint32_t o[4];
-          if (PAIR) {
-#pragma unroll
-            for (int pp = 0; pp < 4; pp++) {
-              const int bit = (8 * c + 2 * pp) * B;
-              const uint32_t top = __funnelshift_l(img[h][(bit >> 5) + 1], img[h][bit >> 5], bit & 31);
-              o[pp] = table[(top >> fshift) & fmask];
-            }
-          } else {
-            const uint16_t *t16 = (const uint16_t *)table;
-#pragma unroll
-            for (int pp = 0; pp < 4; pp++) {
-              const int bit0 = (8 * c + 2 * pp) * B, bit1 = bit0 + B;
-              const uint32_t top0 = __funnelshift_l(img[h][(bit0 >> 5) + 1], img[h][bit0 >> 5], bit0 & 31);
-              const uint32_t top1 = __funnelshift_l(img[h][(bit1 >> 5) + 1], img[h][bit1 >> 5], bit1 & 31);
-              o[pp] = (uint32_t)t16[(top0 >> fshift) & fmask] |
-                      ((uint32_t)t16[(top1 >> fshift) & fmask] << 16);
+          for (int c = 0; c < 4; c++) {
+            uint32_t mk = mask[c];
+            while (mk != 0u) {
+              const int j = __ffs(mk) - 1;
+              mk &= mk - 1u;
+              if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * c + j);
+              pos++;
             }
           }
-          const uint4 v = ok[h] ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0, 0, 0, 0);
-          *(uint4 *)(sb + tc::sw128_chunk_offset(row, c, TC_N)) = v;
         }
-        const int64_t rec = rec0 + row;
-        scal[s * TC_N + row] = ok[h] ? make_float2(__ldg(p.g + rec), __ldg(p.c + rec))
-                                     : make_float2(0.0f, INFINITY);
       }
-      tc::fence_async_smem();
-      tc::mbar_arrive(&full[s]);
+    }
+  } else if (warp == 8) {
+    if (lane == 0) {
+      // ================= MMA issue =================
+      const uint32_t idesc = tc::idesc_f16_f32(TC_M, TC_N);
+      const uint32_t a_base = tc::smem_u32(sa);
+      for (int it = 0; it < ntiles; it++) {
+        const int s = it % TC_STAGES, a = it & 1;
+        if (!tc::mbar_wait(&full[s], (it / TC_STAGES) & 1, kWaitLimit) ||
+            !tc::mbar_wait(&acce[a], ((it >> 1) & 1) ^ 1, kWaitLimit)) {
+          *abort_s = 1;
+          atomicExch(p.err, 1);
+        }
+        if (*abort_s) break;
+        tc::tc_fence_after();
+        const uint32_t b_base = tc::smem_u32(sm + L::b + s * L::b_bytes);
+#pragma unroll
+        for (int k = 0; k < TC_D / 16; k++) {
+          const uint32_t off = (uint32_t)((k & 3) * 32);  // 16 fp16 = 32 B per K step
+          const uint64_t ad = tc::sw128_desc(a_base + (k >> 2) * TC_M * 128 + off);
+          const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * TC_N * 128 + off);
+          tc::mma_f16(tmem + (uint32_t)(a * TC_N), ad, bd, idesc, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&empty[s]);
+        tc::mma_commit(&accf[a]);
+      }
     }
   } else if (lane == 0) {
-    // ================= MMA issue =================
-    const uint32_t idesc = tc::idesc_f16_f32(TC_M, TC_N);
-    const uint32_t a_base = tc::smem_u32(sa);
+    // ================= TMA producer =================
     for (int it = 0; it < ntiles; it++) {
-      const int s = it & 1;
-      if (!tc::mbar_wait(&full[s], (it >> 1) & 1, kWaitLimit) ||
-          !tc::mbar_wait(&acce[s], ((it >> 1) & 1) ^ 1, kWaitLimit)) {
+      const int s = it % TC_STAGES;
+      if (!tc::mbar_wait(&empty[s], ((it / TC_STAGES) & 1) ^ 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
       }
       if (*abort_s) break;
-      tc::tc_fence_after();
-      const uint32_t b_base = tc::smem_u32(sm + (s ? L::b1 : L::b0));
-#pragma unroll
-      for (int k = 0; k < D / 16; k++) {
-        const uint32_t off = (uint32_t)((k & 3) * 32);  // 16 fp16 = 32 B per K step
-        const uint64_t ad = tc::sw128_desc(a_base + (k >> 2) * TC_M * 128 + off);
-        const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * TC_N * 128 + off);
-        tc::mma_f16(tmem + (uint32_t)(s * TC_N), ad, bd, idesc, k > 0 ? 1u : 0u);
-      }
-      tc::mma_commit(&empty[s]);
-      tc::mma_commit(&accf[s]);
+      uint8_t *dst = sm + L::b + s * L::b_bytes;
+      const int row = (int)((t_begin + it) * TC_N);
+      tc::mbar_arrive_expect_tx(&full[s], (uint32_t)L::b_bytes);
+      tc::tma_load_2d(dst, &tmap, 0, row, &full[s]);
+      tc::tma_load_2d(dst + TC_N * 128, &tmap, 64, row, &full[s]);
     }
   }
 
-  // ---- teardown: every MMA has been waited for by the epilogue ----
+  // ---- teardown: the epilogue has waited for every MMA ----
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 8) {
@@ -279,26 +276,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_scan_kernel(const TcScanPara
 }
 
 // ---------------------------------------------------------------------------
-// Per-record bound constants: g = (rnorm / rescale) [x norm], and c with
-// score in [fma(dot_tc, g, -c), fma(dot_tc, g, c)].  Non-finite g or c (NaN or
-// infinite sidecars) gives g = 0, c = +inf: never pruned, never a lower bound.
+// Per record: the fp16 row of decoded code values (the scan kernel's MMA
+// operand; padded rows are zero) and the bound constants (g, c): score in
+// [fma(dot_tc, g, -c), fma(dot_tc, g, c)] with g = (rnorm / rescale) [x norm].
+// Non-finite g or c (NaN or infinite sidecars) gives g = 0, c = +inf: never
+// pruned, never a lower bound.
 // ---------------------------------------------------------------------------
-__global__ void tc_record_bounds_kernel(const TcBoundsParams p) {
+__global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= p.n) return;
+  if (r >= p.n_pad) return;
+  uint4 *xrow = (uint4 *)(p.x16 + r * TC_D);
+  if (r >= p.n) {
+    for (int c = 0; c < TC_D / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
+    p.gc[r] = make_float2(0.0f, INFINITY);
+    return;
+  }
   const int W = p.mem + p.bits;
   const uint32_t *cw = (const uint32_t *)(p.codes + r * (int64_t)p.code_stride);
   const uint32_t st = __ldg(p.start + r);
   const int rw = p.code_stride >> 2;
   double xs = 0.0;
-  for (int i = 0; i < p.dim; i++) {
-    const int pos = 32 + i * p.bits - p.mem;
-    const int w0 = pos >> 5, sh = pos & 31;
-    const uint32_t hi = w0 == 0 ? st : (w0 <= rw ? __byte_perm(__ldg(cw + w0 - 1), 0, 0x0123) : 0u);
-    const uint32_t lo = w0 + 1 <= rw ? __byte_perm(__ldg(cw + w0), 0, 0x0123) : 0u;
-    const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
-    const double x = (double)__ldg(p.code + win);
-    xs += x * x;
+  for (int c = 0; c < TC_D / 8; c++) {
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 8; h++) {
+      const int i = 8 * c + h;
+      const int pos = 32 + i * p.bits - p.mem;
+      const int w0 = pos >> 5, sh = pos & 31;
+      const uint32_t hi = w0 == 0 ? st : (w0 <= rw ? __byte_perm(__ldg(cw + w0 - 1), 0, 0x0123) : 0u);
+      const uint32_t lo = w0 + 1 <= rw ? __byte_perm(__ldg(cw + w0), 0, 0x0123) : 0u;
+      const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
+      const float x = __ldg(p.code + win);
+      xs += (double)x * (double)x;
+      const uint32_t hx = __half_as_ushort(__float2half_rn(x));
+      if (h & 1) o[h >> 1] |= hx << 16;
+      else o[h >> 1] = hx;
+    }
+    xrow[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
   const float rs = __ldg(p.rescale + r);
   const float rn = p.rnorm ? __ldg(p.rnorm + r) : 1.0f;
@@ -307,7 +321,8 @@ __global__ void tc_record_bounds_kernel(const TcBoundsParams p) {
   const double u = 5.9604644775390625e-8;  // 2^-24
   const double qn = 1.0001;                // |q_r| of a rotated unit query
   const double xn = sqrt(xs) * (1.0 + 1e-12);
-  const double beta = p.eps * qn * xn + u * sqrt((double)p.dim) * (xn * (1.0 + 4.8828125e-4) + qn) + 1e-30;
+  const double beta =
+      p.eps * qn * xn + u * sqrt((double)TC_D) * (xn * (1.0 + 4.8828125e-4) + qn) + 1e-30;
   const double A = qn * xn + beta;
   const double cd = (beta + 10.0 * u * A) * (double)g * (1.0 + 1e-6);
   float c = __double2float_ru(cd);
@@ -315,8 +330,7 @@ __global__ void tc_record_bounds_kernel(const TcBoundsParams p) {
     g = 0.0f;
     c = INFINITY;
   }
-  p.g[r] = g;
-  p.c[r] = c;
+  p.gc[r] = make_float2(g, c);
 }
 
 // ---------------------------------------------------------------------------
@@ -392,6 +406,7 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     return;
   }
   const int cnt = p.degenerate[q] ? 0 : cnt_raw;
+  if (tid == 0) atomicAdd(p.n_cand, (unsigned long long)cnt);
   int pow2 = 32;
   while (pow2 < cnt) pow2 <<= 1;
   for (int i = tid; i < p.dim; i += 256) qv[i] = p.q_r[q * (int64_t)p.q_stride + i];
@@ -458,32 +473,15 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   }
 }
 
-size_t tc_scan_smem_bytes(int dim, int table_bytes) {
-  if (dim != 128) return 0;
-  return (size_t)TcLayout<128>::table + (size_t)table_bytes;
-}
+size_t tc_scan_smem_bytes() { return (size_t)TcLayout::total; }
 
-const void *tc_scan_kernel_ptr(int mode, int bits, int dim, bool pair) {
-  if (dim != 128) return nullptr;
-#define UV_TC_CASE(b)                                                                  \
-  case b:                                                                              \
-    if (mode == 1)                                                                     \
-      return pair ? (const void *)tc_scan_kernel<1, b, 128, true>                     \
-                  : (const void *)tc_scan_kernel<1, b, 128, false>;                   \
-    return pair ? (const void *)tc_scan_kernel<2, b, 128, true>                       \
-                : (const void *)tc_scan_kernel<2, b, 128, false>;
-  switch (bits) {
-    UV_TC_CASE(1)
-    UV_TC_CASE(2)
-    UV_TC_CASE(3)
-    UV_TC_CASE(4)
-  }
-#undef UV_TC_CASE
-  return nullptr;
+const void *tc_scan_kernel_ptr(int mode) {
+  return mode == 1 ? (const void *)tc_scan_kernel<1> : (const void *)tc_scan_kernel<2>;
 }
 
 int tc_threads() { return TC_THREADS; }
 int tc_tile_records() { return TC_N; }
 int tc_tile_queries() { return TC_M; }
+int tc_dim() { return TC_D; }
 
 }  // namespace uvb

@@ -128,31 +128,28 @@ struct RerankParams {
 
 // Tensor-core prefilter of the flat scan (tcscan.cu).
 struct TcScanParams {
-  int mem, q_stride, table_words, cand_cap;
-  int64_t nq, n, n_tiles;
+  int q_stride, cand_cap;
+  int64_t nq, n, n_tiles, n_groups;
   const float *q_r;            // nq x q_stride rotated unit queries
   const uint32_t *degenerate;  // nq
-  const uint8_t *codes;
-  int code_stride;
-  const uint32_t *start;
-  const uint32_t *table;       // fp16 pair table (half2 words) or fp16 table
-  const float *g, *c;          // per-record bound constants
-  float *tmax;                 // mode 1: nq x n_tiles lower-bound tile maxima
+  const float2 *gc;            // per record (g, c) bound constants, n_tiles * 256
+  float *tmax;                 // mode 1: nq x n_groups lower-bound maxima
   const float *theta;          // mode 2: per-query threshold
   uint32_t *cand;              // mode 2: nq x cand_cap record indices
   int *cand_cnt;               // mode 2: nq (zeroed before the launch)
   int *err;
 };
 
-struct TcBoundsParams {
-  int dim, mem, bits, code_stride, mips;
-  int64_t n;
+struct TcPrepareParams {
+  int mem, bits, code_stride, mips;
+  int64_t n, n_pad;
   double eps;
   const uint8_t *codes;
   const uint32_t *start;
   const float *code;           // f32 code table
   const float *rescale, *rnorm, *norms;
-  float *g, *c;
+  uint16_t *x16;               // n_pad x 128 fp16 code values
+  float2 *gc;                  // n_pad
 };
 
 struct TcRescoreParams {
@@ -170,6 +167,7 @@ struct TcRescoreParams {
   float *out_score;
   int32_t *over_list;
   int *n_over;
+  unsigned long long *n_cand;  // total candidates scored (statistics)
 };
 
 struct MergeParams {
@@ -192,12 +190,13 @@ constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
 
 // tcscan.cu
-const void *tc_scan_kernel_ptr(int mode, int bits, int dim, bool pair);
-size_t tc_scan_smem_bytes(int dim, int table_bytes);
+const void *tc_scan_kernel_ptr(int mode);
+size_t tc_scan_smem_bytes();
 int tc_threads();
 int tc_tile_records();
 int tc_tile_queries();
-__global__ void tc_record_bounds_kernel(const TcBoundsParams p);
+int tc_dim();
+__global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);
 __global__ void tc_rescore_kernel(const TcRescoreParams p);
