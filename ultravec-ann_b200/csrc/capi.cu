@@ -7,6 +7,7 @@
 #include "capi_internal.h"
 
 #include <atomic>
+#include <cmath>
 
 #include <cuda.h>
 
@@ -93,6 +94,7 @@ int uv_codec_create(const uv_config *cfg, uv_codec **out) {
   c->code_stride = (c->code_bytes + 15) & ~15;
   c->h_table = uvb::build_code_table(cfg->mem, cfg->bits);
   c->table_len = (int)c->h_table.size();
+  for (float v : c->h_table) c->code_absmax = std::max(c->code_absmax, std::fabs(v));
   c->rot_host = uvb::build_rotation(cfg->dim, cfg->rotation_seed, c->cfg.rotation_rounds);
   if ((int)c->rot_host.blk_off.size() > uvb::kMaxBlocks) {
     delete c;
@@ -782,12 +784,14 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int dim_pad = (d + 3) & ~3;
   const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
   (void)qc;
-  // fp16 records and per-record bound constants
+  // fp16 operand rows with the bound constants folded in
   const int64_t n_pad = n_tiles * TN;
-  uint16_t *x16 = nullptr;
-  float2 *gc = nullptr;
+  uint16_t *x16 = nullptr, *xext = nullptr;
+  uint32_t *gmax = nullptr;
   UV_TRY(sc.alloc(&x16, (size_t)n_pad * d));
-  UV_TRY(sc.alloc(&gc, (size_t)n_pad));
+  UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
+  UV_TRY(sc.alloc(&gmax, 1));
+  UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
   {
     uvb::TcPrepareParams pp;
     std::memset(&pp, 0, sizeof(pp));
@@ -798,33 +802,44 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     pp.n = n;
     pp.n_pad = n_pad;
     pp.eps = 1.5e-3;
+    pp.code_absmax = c->code_absmax;
     pp.codes = ix->codes;
     pp.start = ix->start;
     pp.code = c->d_table;
     pp.rescale = ix->rescale;
     pp.rnorm = ix->rnorm;
     pp.norms = ix->norms;
+    pp.gmax_bits = gmax;
     pp.x16 = x16;
-    pp.gc = gc;
+    pp.xext = xext;
     void *args[] = {&pp};
     ProfScope ps("tc_prepare", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
+                           dim3(256), args, 0, st));
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
                            dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
   }
-  // TMA map of the fp16 records: rows of 128 fp16 (256 B), boxes of 64 x 256
-  // with the 128-byte swizzle of the MMA operand layout
-  CUtensorMap tmap;
+  // TMA maps: main rows of 128 fp16 (boxes of 64 x TN, 128-byte swizzle) and
+  // the extra slice of 16 fp16 (boxes of 16 x TN, 32-byte swizzle)
+  CUtensorMap tmap_main, tmap_ext;
   {
     EncodeTiledFn enc = nullptr;
     UV_TRY(encode_tiled_fn(&enc));
+    const cuuint32_t estride[2] = {1, 1};
     const cuuint64_t gdim[2] = {(cuuint64_t)d, (cuuint64_t)n_pad};
     const cuuint64_t gstride[1] = {(cuuint64_t)d * 2};
     const cuuint32_t box[2] = {64, (cuuint32_t)TN};
-    const cuuint32_t estride[2] = {1, 1};
-    const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)x16, gdim, gstride,
-                           box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled failed");
+    CUresult r = enc(&tmap_main, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)x16, gdim, gstride,
+                     box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (main rows) failed");
+    const cuuint64_t gdim_x[2] = {16, (cuuint64_t)n_pad};
+    const cuuint64_t gstride_x[1] = {32};
+    const cuuint32_t box_x[2] = {16, (cuuint32_t)TN};
+    r = enc(&tmap_ext, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)xext, gdim_x, gstride_x, box_x,
+            estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (extra slice) failed");
   }
   // units: query tiles x record splits, filling whole waves of one CTA per SM
   const int64_t qtiles = (nq + TM - 1) / TM;
@@ -864,7 +879,6 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   tp.n_groups = n_groups;
   tp.q_r = q_r;
   tp.degenerate = degen;
-  tp.gc = gc;
   tp.tmax = tmax;
   tp.theta = theta;
   tp.cand = cand;
@@ -877,7 +891,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   {
-    void *args[] = {&tp, &tmap};
+    void *args[] = {&tp, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass1", st);
     UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), args, smem, st));
   }
@@ -887,7 +901,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaGetLastError());
   }
   {
-    void *args[] = {&tp, &tmap};
+    void *args[] = {&tp, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass2", st);
     UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), args, smem, st));
   }

@@ -197,6 +197,7 @@ int sm_count(int dev);
 struct uv_codec {
   uv_config cfg;
   int code_bytes = 0, code_stride = 0, table_len = 0;
+  float code_absmax = 0.0f;
   std::vector<float> h_table;
   uvb::RotationHost rot_host;
   float *d_table = nullptr;

@@ -4,7 +4,7 @@
 // rescale), times the row norm for MIPS) needs the f32 dot in the AVX2
 // association of simd.rs:183-262.  Computing every dot that way is FP32-issue
 // bound.  Here every (query, record) dot is first computed on the tensor
-// cores in fp16 x fp16 -> f32 (tcgen05.mma, 128 queries x 256 records per
+// cores in fp16 x fp16 -> f32 (tcgen05.mma, 128 queries x 192 records per
 // MMA tile), and a rigorous per-record bound turns it into an interval that
 // provably contains the exact f32 score:
 //
@@ -12,28 +12,33 @@
 //   eps = 1.5e-3 covers the fp16 rounding of both operands (2 * 2^-11), the
 //   tensor-core accumulation (allowed 2^-12 of sum |q_i x_i|) and the f32
 //   reference accumulation; |q| <= 1.0001 for a rotated unit query.
-//   score in [fma(dot_tc, g_r, -c_r), fma(dot_tc, g_r, c_r)] with
-//   g_r = rnorm_r / rescale_r (x norm_r) and c_r = (beta_r + 10u A_r) g_r,
-//   A_r = |q| |x_r| + beta_r bounding every f32 rounding of the score.
+//   score in [g_r dot_tc - c_r, g_r dot_tc + c_r] with g_r = rnorm_r /
+//   rescale_r (x norm_r) and c_r = g_r beta_r plus the f32 roundings of the
+//   score; both bounds come out of the MMA directly (below).
 //
-// Pass 1 (MODE 1) writes, per query and 128-record half tile, the largest
+// Pass 1 (MODE 1) writes, per query and 96-record half tile, the largest
 // lower bound; the k-th largest of those maxima is a score that at least k
 // records reach, so it lower-bounds the exact k-th best (theta).  Pass 2
 // (MODE 2) appends every record whose upper bound reaches theta to the
 // query's candidate list; the exact top-k is among them, ties included.
 // The candidates are then scored exactly (tc_rescore_kernel) and ranked.
 //
-// Records are first decoded once per search into an fp16 row-major copy
-// (tc_prepare_records_kernel, which also computes the bound constants).  The
-// scan kernel then streams 256-record tiles of it into shared memory by TMA
-// (128-byte swizzle, the K-major operand layout of the MMA).
+// Records are first turned, once per search, into fp16 operand rows that
+// carry the bound constants (tc_prepare_records_kernel):
+//   main  B'_r,i = fp16(g_r * x_r,i * s)             128 coordinates
+//   ext   C'_r   = fp16 rounded up of c_r * s         one extra K slice of 16
+// with s = 2^-e a power of two that keeps every |B'| below 2^14.  The query
+// tile carries an extra column of -1 (pass 1) or +1 (pass 2), so the MMA
+// itself yields s * (lower or upper bound of the exact score): the epilogue
+// only takes maxima or compares.  Tiles of 192 records stream in by TMA
+// (128-byte swizzle for the main rows, 32-byte for the extra slice).
 //
 // CTA = one unit of 128 queries x a record range.  Warp roles:
 //   warps 0-7  epilogue: warp w reads TMEM lane quarter w % 4 (thread =
-//              query) and column half w / 4 (128 records) of each tile
+//              query) and column half w / 4 (96 records) of each tile
 //   warp 8     TMEM allocation; lane 0 issues the MMAs
 //   warp 9     lane 0 issues the TMA loads
-// Three shared-memory stages and two TMEM accumulators (2 x 256 columns)
+// Three shared-memory stages and two TMEM accumulators (2 x 192 columns)
 // are handed over with mbarriers; every wait is bounded.
 #include <cuda.h>
 
@@ -45,22 +50,26 @@ namespace uvb {
 namespace {
 
 constexpr int TC_M = 128;      // queries per unit
-constexpr int TC_N = 256;      // records per MMA tile
-constexpr int TC_D = 128;      // coordinates (K)
+constexpr int TC_N = 192;      // records per MMA tile
+constexpr int TC_D = 128;      // coordinates (K) of the main rows
+constexpr int TC_X = 16;       // the extra K slice (bound constant + zeros)
 constexpr int TC_STAGES = 3;
 constexpr int TC_THREADS = 320;
-constexpr int TC_EPI = 256;    // epilogue threads
 constexpr uint32_t kWaitLimit = 1u << 20;
 
 struct TcLayout {
-  static constexpr int a_bytes = TC_M * TC_D * 2;        // 32 KB
-  static constexpr int b_bytes = TC_N * TC_D * 2;        // 64 KB per stage
+  static constexpr int a_bytes = TC_M * TC_D * 2;             // 32 KB
+  static constexpr int ax_bytes = TC_M * TC_X * 2;            // 4 KB
+  static constexpr int bm_bytes = TC_N * 128;                 // one main atom column
+  static constexpr int b_bytes = 2 * bm_bytes + TC_N * TC_X * 2;  // 54 KB per stage
   static constexpr int a = 0;
-  static constexpr int b = a + a_bytes;
-  static constexpr int bars = b + TC_STAGES * b_bytes;   // 10 mbarriers
-  static constexpr int misc = bars + 16 * 8;             // tmem base, abort flag
+  static constexpr int ax = a + a_bytes;
+  static constexpr int b = ax + ax_bytes;
+  static constexpr int bars = b + TC_STAGES * b_bytes;        // 10 mbarriers
+  static constexpr int misc = bars + 16 * 8;                  // tmem base, abort flag
   static constexpr int total = misc + 64;
 };
+static_assert(TcLayout::b % 1024 == 0 && TcLayout::b_bytes % 1024 == 0, "stage alignment");
 
 // 3-input maximum (NaN-ignoring like fmaxf)
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -73,10 +82,12 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 
 template <int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap) {
+    tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap_main,
+                   const __grid_constant__ CUtensorMap tmap_ext) {
   using L = TcLayout;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t *sa = sm + L::a;
+  uint8_t *sax = sm + L::ax;
   uint64_t *full = (uint64_t *)(sm + L::bars);  // [3]
   uint64_t *empty = full + 3;                   // [3]
   uint64_t *accf = full + 6;                    // [2]
@@ -98,7 +109,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; a++) {
       tc::mbar_init(&accf[a], 1);
-      tc::mbar_init(&acce[a], TC_EPI);
+      tc::mbar_init(&acce[a], 256);
     }
     *abort_s = 0;
     tc::mbar_fence_init();
@@ -118,6 +129,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     *(uint4 *)(sa + tc::sw128_chunk_offset(r, c, TC_M)) = v;
   }
+  // the extra slice: -1 (lower bounds) or +1 (upper bounds) against C'
+  for (int e = tid; e < TC_M * 2; e += TC_THREADS) {
+    const int r = e >> 1, c = e & 1;
+    const int64_t q = q0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (c == 0 && q < p.nq && !p.degenerate[q])
+      v.x = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
+    *(uint4 *)(sax + tc::sw32_chunk_offset(r, c)) = v;
+  }
   tc::fence_async_smem();
   tc::tc_fence_before();
   __syncthreads();
@@ -130,12 +150,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int64_t q = q0 + quarter * 32 + lane;
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
-    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 128);
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 96);
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
       const int64_t tile = t_begin + it;
-      const int64_t rec0 = tile * TC_N + half * 128;
-      const float4 *gc = (const float4 *)(p.gc + rec0);  // (g, c) of two records
+      const int64_t rec0 = tile * TC_N + half * 96;
       if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
@@ -143,74 +162,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (*abort_s) break;
       tc::tc_fence_after();
       const uint32_t base = lane_base + (uint32_t)(a * TC_N);
-      float best = -INFINITY;
-      uint32_t mask0 = 0u, mask1 = 0u, mask2 = 0u, mask3 = 0u;
-      uint32_t ra[32], rb[32];
-      // bound of every record of 32-column chunk c, its max, and (pass 2)
-      // the mask of records that can reach theta
-      auto chunk = [&](const uint32_t(&cur)[32], int c) {
-        float v[32];
+      uint32_t r0[32], r1[32], r2[32];
+      tc::tmem_ld32(base, r0);
+      tc::tmem_ld32(base + 32, r1);
+      tc::tmem_ld32(base + 64, r2);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&acce[a]);  // the accumulator is in registers
+      auto cmax = [](const uint32_t(&r)[32]) {
+        float m = max3(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]));
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float4 g4 = __ldg(gc + (32 * c + j) / 2);
-          const float2 dd = make_float2(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1]));
-          const float2 g2 = make_float2(g4.x, g4.z);
-          const float2 c2 = MODE == 1 ? make_float2(-g4.y, -g4.w) : make_float2(g4.y, g4.w);
-          const float2 t2 = __ffma2_rn(dd, g2, c2);
-          v[j] = t2.x;
-          v[j + 1] = t2.y;
-        }
-        float m = max3(v[0], v[1], v[2]);
-#pragma unroll
-        for (int j = 3; j < 31; j += 2) m = max3(m, v[j], v[j + 1]);
-        m = fmaxf(m, v[31]);
-        if (MODE == 1) {
-          best = fmaxf(best, m);
-        } else if (qok && !(m < theta)) {
+        for (int j = 3; j < 31; j += 2)
+          m = max3(m, __uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+        return fmaxf(m, __uint_as_float(r[31]));
+      };
+      const float m0 = cmax(r0), m1 = cmax(r1), m2 = cmax(r2);
+      if (MODE == 1) {
+        if (q < p.nq)
+          p.tmax[q * p.n_groups + 2 * tile + half] = qok ? max3(m0, m1, m2) : -INFINITY;
+      } else if (qok && !(max3(m0, m1, m2) < theta)) {
+        // rare: every record of the half tile that can reach theta
+        auto cmask = [&](const uint32_t(&r)[32]) {
           uint32_t mk = 0;
 #pragma unroll
-          for (int j = 0; j < 32; j++) mk |= (!(v[j] < theta) ? 1u : 0u) << j;
-          // selects, not an indexed store: the masks stay in registers
-          mask0 = c == 0 ? mk : mask0;
-          mask1 = c == 1 ? mk : mask1;
-          mask2 = c == 2 ? mk : mask2;
-          mask3 = c == 3 ? mk : mask3;
-        }
-      };
-      // TMEM -> registers two chunks at a time: the next load is in flight
-      // while the current chunk is processed
-      tc::tmem_ld32(base, ra);
-      tc::tmem_ld_wait();
-#pragma unroll 1
-      for (int c = 0; c < 4; c += 2) {
-        tc::tmem_ld32(base + (uint32_t)(32 * (c + 1)), rb);
-        chunk(ra, c);
-        tc::tmem_ld_wait();
-        if (c + 2 < 4) tc::tmem_ld32(base + (uint32_t)(32 * (c + 2)), ra);
-        chunk(rb, c + 1);
-        if (c + 2 < 4) tc::tmem_ld_wait();
-      }
-      tc::tc_fence_before();
-      tc::mbar_arrive(&acce[a]);
-      if (MODE == 1 && q < p.nq)
-        p.tmax[q * p.n_groups + 2 * tile + half] = qok ? best : -INFINITY;
-      if (MODE == 2) {
-        uint32_t mask[4] = {mask0, mask1, mask2, mask3};
-        // one reservation per thread and tile for all of its candidates
-        if (rec0 + 128 > p.n) {
+          for (int j = 0; j < 32; j++) mk |= (!(__uint_as_float(r[j]) < theta) ? 1u : 0u) << j;
+          return mk;
+        };
+        uint32_t mask[3] = {cmask(r0), cmask(r1), cmask(r2)};
+        if (rec0 + 96 > p.n) {
           const int64_t lim = p.n - rec0;  // records past n are padding
 #pragma unroll
-          for (int c = 0; c < 4; c++) {
+          for (int c = 0; c < 3; c++) {
             const int64_t room = lim - 32 * c;
             mask[c] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
           }
         }
-        const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
+        const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]);
         if (cnt > 0) {
           int pos = atomicAdd(&p.cand_cnt[q], cnt);
           uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
 #pragma unroll
-          for (int c = 0; c < 4; c++) {
+          for (int c = 0; c < 3; c++) {
             uint32_t mk = mask[c];
             while (mk != 0u) {
               const int j = __ffs(mk) - 1;
@@ -226,7 +218,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       // ================= MMA issue =================
       const uint32_t idesc = tc::idesc_f16_f32(TC_M, TC_N);
-      const uint32_t a_base = tc::smem_u32(sa);
+      const uint32_t a_base = tc::smem_u32(sa), ax_base = tc::smem_u32(sax);
       for (int it = 0; it < ntiles; it++) {
         const int s = it % TC_STAGES, a = it & 1;
         if (!tc::mbar_wait(&full[s], (it / TC_STAGES) & 1, kWaitLimit) ||
@@ -237,13 +229,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (*abort_s) break;
         tc::tc_fence_after();
         const uint32_t b_base = tc::smem_u32(sm + L::b + s * L::b_bytes);
+        const uint32_t d = tmem + (uint32_t)(a * TC_N);
 #pragma unroll
         for (int k = 0; k < TC_D / 16; k++) {
           const uint32_t off = (uint32_t)((k & 3) * 32);  // 16 fp16 = 32 B per K step
           const uint64_t ad = tc::sw128_desc(a_base + (k >> 2) * TC_M * 128 + off);
-          const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * TC_N * 128 + off);
-          tc::mma_f16(tmem + (uint32_t)(a * TC_N), ad, bd, idesc, k > 0 ? 1u : 0u);
+          const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
+          tc::mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
         }
+        tc::mma_f16(d, tc::sw32_desc(ax_base), tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc, 1u);
         tc::mma_commit(&empty[s]);
         tc::mma_commit(&accf[a]);
       }
@@ -260,8 +254,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint8_t *dst = sm + L::b + s * L::b_bytes;
       const int row = (int)((t_begin + it) * TC_N);
       tc::mbar_arrive_expect_tx(&full[s], (uint32_t)L::b_bytes);
-      tc::tma_load_2d(dst, &tmap, 0, row, &full[s]);
-      tc::tma_load_2d(dst + TC_N * 128, &tmap, 64, row, &full[s]);
+      tc::tma_load_2d(dst, &tmap_main, 0, row, &full[s]);
+      tc::tma_load_2d(dst + L::bm_bytes, &tmap_main, 64, row, &full[s]);
+      tc::tma_load_2d(dst + 2 * L::bm_bytes, &tmap_ext, 0, row, &full[s]);
     }
   }
 
@@ -276,25 +271,63 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Per record: the fp16 row of decoded code values (the scan kernel's MMA
-// operand; padded rows are zero) and the bound constants (g, c): score in
-// [fma(dot_tc, g, -c), fma(dot_tc, g, c)] with g = (rnorm / rescale) [x norm].
-// Non-finite g or c (NaN or infinite sidecars) gives g = 0, c = +inf: never
-// pruned, never a lower bound.
+// g_r = (rnorm / rescale) [x norm] of every record and the largest finite one
+// (as the bits of a non-negative float, which order like the float).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float record_g(const TcPrepareParams &p, int64_t r) {
+  const float rs = __ldg(p.rescale + r);
+  const float rn = p.rnorm ? __ldg(p.rnorm + r) : 1.0f;
+  float g = fdiv(rn, rs);
+  if (p.mips) g = fmul(g, __ldg(p.norms + r));
+  return g;
+}
+
+__global__ void tc_gmax_kernel(const TcPrepareParams p) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float g = 0.0f;
+  if (r < p.n) {
+    g = record_g(p, r);
+    if (!isfinite(g) || g < 0.0f) g = 0.0f;
+  }
+  for (int o = 16; o > 0; o >>= 1) g = fmaxf(g, __shfl_xor_sync(0xffffffffu, g, o));
+  if ((threadIdx.x & 31) == 0 && g > 0.0f) atomicMax(p.gmax_bits, __float_as_uint(g));
+}
+
+// ---------------------------------------------------------------------------
+// The operand rows of every record (padded rows are zero, with C' = +inf so
+// that they never bound theta from below):
+//   B'_i = fp16(g * x_i * s),  C' = fp16 rounded up of
+//   c = s * g * eps * |q| * |x| + 2^-23 sqrt(d) (|q| + s * g * |x|)
+// eps = 1.5e-3 covers 2 x 2^-11 (fp16 rounding of q and of g x s), 2^-12 of
+// sum |terms| for the tensor-core accumulation, the f32 reference dot and
+// the five roundings of the score (two in g, three in the estimator); the
+// absolute term covers fp16 subnormals.  |q| <= 1.0001 for a rotated unit
+// query.  Non-finite or negative g: zero row, C' = +inf (never pruned).
 // ---------------------------------------------------------------------------
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= p.n_pad) return;
   uint4 *xrow = (uint4 *)(p.x16 + r * TC_D);
-  if (r >= p.n) {
+  uint4 *xext = (uint4 *)(p.xext + r * TC_X);
+  const uint32_t hinf = 0x7C00u;  // fp16 +inf
+  float g = r < p.n ? record_g(p, r) : 0.0f;
+  const bool bad = r >= p.n || !isfinite(g) || g < 0.0f;
+  // s = 2^-e with gmax * max|code| * s in [2^13, 2^14)
+  const float gmax = __uint_as_float(*p.gmax_bits);
+  const double top = (double)gmax * (double)p.code_absmax;
+  const int e = top > 0.0 ? (int)ceil(log2(top)) - 14 : 0;
+  const double s = ldexp(1.0, -e);
+  if (bad) {
     for (int c = 0; c < TC_D / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
-    p.gc[r] = make_float2(0.0f, INFINITY);
+    xext[0] = make_uint4(hinf, 0, 0, 0);
+    xext[1] = make_uint4(0, 0, 0, 0);
     return;
   }
   const int W = p.mem + p.bits;
   const uint32_t *cw = (const uint32_t *)(p.codes + r * (int64_t)p.code_stride);
   const uint32_t st = __ldg(p.start + r);
   const int rw = p.code_stride >> 2;
+  const float gs = (float)((double)g * s);  // exact: s is a power of two
   double xs = 0.0;
   for (int c = 0; c < TC_D / 8; c++) {
     uint32_t o[4];
@@ -308,29 +341,20 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
       const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
       const float x = __ldg(p.code + win);
       xs += (double)x * (double)x;
-      const uint32_t hx = __half_as_ushort(__float2half_rn(x));
+      const uint32_t hx = __half_as_ushort(__float2half_rn(fmul(gs, x)));
       if (h & 1) o[h >> 1] |= hx << 16;
       else o[h >> 1] = hx;
     }
     xrow[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
-  const float rs = __ldg(p.rescale + r);
-  const float rn = p.rnorm ? __ldg(p.rnorm + r) : 1.0f;
-  float g = fdiv(rn, rs);
-  if (p.mips) g = fmul(g, __ldg(p.norms + r));
-  const double u = 5.9604644775390625e-8;  // 2^-24
-  const double qn = 1.0001;                // |q_r| of a rotated unit query
+  const double qn = 1.0001;
   const double xn = sqrt(xs) * (1.0 + 1e-12);
-  const double beta =
-      p.eps * qn * xn + u * sqrt((double)TC_D) * (xn * (1.0 + 4.8828125e-4) + qn) + 1e-30;
-  const double A = qn * xn + beta;
-  const double cd = (beta + 10.0 * u * A) * (double)g * (1.0 + 1e-6);
-  float c = __double2float_ru(cd);
-  if (!isfinite(g) || !isfinite(c) || g < 0.0f) {
-    g = 0.0f;
-    c = INFINITY;
-  }
-  p.gc[r] = make_float2(g, c);
+  const double sg = s * (double)g;
+  const double cd = (sg * p.eps * qn * xn + 1.1920928955078125e-7 * sqrt((double)TC_D) *
+                                                (qn + sg * xn)) * (1.0 + 1e-6);
+  const uint32_t hc = __half_as_ushort(__float2half_ru(__double2float_ru(cd)));
+  xext[0] = make_uint4(hc, 0, 0, 0);
+  xext[1] = make_uint4(0, 0, 0, 0);
 }
 
 // ---------------------------------------------------------------------------

@@ -132,7 +132,6 @@ struct TcScanParams {
   int64_t nq, n, n_tiles, n_groups;
   const float *q_r;            // nq x q_stride rotated unit queries
   const uint32_t *degenerate;  // nq
-  const float2 *gc;            // per record (g, c) bound constants, n_tiles * 256
   float *tmax;                 // mode 1: nq x n_groups lower-bound maxima
   const float *theta;          // mode 2: per-query threshold
   uint32_t *cand;              // mode 2: nq x cand_cap record indices
@@ -144,12 +143,14 @@ struct TcPrepareParams {
   int mem, bits, code_stride, mips;
   int64_t n, n_pad;
   double eps;
+  float code_absmax;           // max |code table value|
   const uint8_t *codes;
   const uint32_t *start;
   const float *code;           // f32 code table
   const float *rescale, *rnorm, *norms;
-  uint16_t *x16;               // n_pad x 128 fp16 code values
-  float2 *gc;                  // n_pad
+  uint32_t *gmax_bits;         // largest finite g (zeroed before tc_gmax_kernel)
+  uint16_t *x16;               // n_pad x 128 fp16 main operand rows
+  uint16_t *xext;              // n_pad x 16 fp16 extra slice (bound constant)
 };
 
 struct TcRescoreParams {
@@ -196,6 +197,7 @@ int tc_threads();
 int tc_tile_records();
 int tc_tile_queries();
 int tc_dim();
+__global__ void tc_gmax_kernel(const TcPrepareParams p);
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);

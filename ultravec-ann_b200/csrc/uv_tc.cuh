@@ -112,6 +112,23 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
   d |= (uint64_t)2 << 61;
   return d;
 }
+// The same for a K-major tile with the 32-byte swizzle (rows of 16 fp16,
+// 8-row groups 256 B apart, layout type 6): one K step per atom.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(16u >> 4) << 16;
+  d |= (uint64_t)(256u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)6 << 61;
+  return d;
+}
+// Byte offset of the 16-byte chunk c (0 or 1) of row r in a K-major
+// 32-byte-swizzled tile: chunk position c ^ ((r >> 2) & 1).
+__host__ __device__ __forceinline__ uint32_t sw32_chunk_offset(int r, int c) {
+  return (uint32_t)(r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+}
+
 // Instruction descriptor of kind::f16: f32 accumulator (bits 4-5 = 1), A and
 // B fp16 (format 0), both K-major, N >> 3 in [17,23), M >> 4 in [24,29).
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
