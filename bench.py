@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--n-query", type=int, default=N_QUERY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep"], default="flat",
+                    help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
+                         "others measure the remaining configurations, one JSON line each")
     ap.add_argument("--scan", choices=["auto", "exact", "tc"], default="auto",
                     help="auto: tensor-core prefilter where it is built; exact: the CUDA-core "
                          "kernel only; tc: prefilter wherever it is built")
@@ -196,6 +199,9 @@ def config_dict(args):
 
 def main():
     args = parse()
+    if args.workload != "flat":
+        run_secondary(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -446,6 +452,130 @@ def cpu_baseline(index, base_np, query_np, codec):
             "sample": f"{sample} queries x {len(ex['start'])} records (scan); encode {enc_rows} "
                       f"rows",
             "encode_rows_s": enc_rows / de}
+
+
+# ------------------------------------------------------ other workloads ---
+
+def _timed(fn, reps):
+    """Device time of fn() in ms (CUDA events), best of reps after one warm-up."""
+    import torch
+
+    fn()
+    best = float("inf")
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b))
+    return best
+
+
+def run_secondary(args):
+    """One GPU; prints one JSON line per configuration:
+    wide          1M rows, d=960 padded to 1024, x_ij = U[0,1) + 0.5 j / 959,
+                  b in {1, 2, 4}, M=8: encode rows/s and 1k-query top-10 MIPS
+    ivf           1M rows, d=1536 padded to 2048: 64 unit Gaussian centres +
+                  0.3 N(0,1), renormalized; k-means nlist=4096 (seed 42, 5
+                  rounds), centered lists, b=2, M=8; 10k-query top-10 at
+                  nprobe 1/4/16/64
+    encode-sweep  1M rows (a 100k prefix at M=12), d=128 N(0,1), b=2, M in
+                  {2, 4, 8, 12}: encode rows/s"""
+    import torch
+
+    from ultravec_ann_b200_loader import load
+
+    uv = load()
+    uv.set_tuning("tc_scan", {"auto": 0, "exact": 1, "tc": 2}[args.scan])
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+
+    def emit(workload, extra):
+        line = {"metric": METRIC, "workload": workload, "n_gpus": 1, "data": "synthetic"}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    if args.workload == "wide":
+        n, nq, d, d_pad = 1_000_000, 1000, 960, 1024
+        x = np.zeros((n + nq, d_pad), np.float32)
+        for a in range(0, n + nq, 100_000):
+            b = min(a + 100_000, n + nq)
+            x[a:b, :d] = rng.random((b - a, d), dtype=np.float32) + \
+                np.float32(0.5) * (np.arange(d, dtype=np.float32) / np.float32(959))
+        base = torch.from_numpy(x[:n]).to(dev)
+        qs = torch.from_numpy(x[n:]).to(dev)
+        for bits in (1, 2, 4):
+            codec = uv.Codec(d_pad, bits, 8)
+            index = uv.Index(codec)
+            index.reserve(n)
+            enc_ms = _timed(lambda: (index.clear(), index.add_batch(base)), 2)
+            scan_ms = _timed(lambda: index.search(qs, 10, mips=True), 3)
+            emit("wide-1Mx1k-d1024", {"bits": bits, "mem": 8, "encode_rows_s": n / enc_ms * 1e3,
+                                      "queries_s": nq / scan_ms * 1e3, "scan_ms": scan_ms,
+                                      "encode_ms": enc_ms, "k": 10, "mips": True})
+            del index, codec
+    elif args.workload == "ivf":
+        n, nq, d, d_pad, nlist = 1_000_000, 10_000, 1536, 2048, 4096
+        c = rng.standard_normal((64, d)).astype(np.float32)
+        c /= np.linalg.norm(c, axis=1, keepdims=True)
+        x = np.zeros((n + nq, d_pad), np.float32)
+        for a in range(0, n + nq, 50_000):
+            b = min(a + 50_000, n + nq)
+            v = c[rng.integers(0, 64, b - a)] + np.float32(0.3) * \
+                rng.standard_normal((b - a, d), dtype=np.float32)
+            x[a:b, :d] = v / np.linalg.norm(v, axis=1, keepdims=True)
+        base = torch.from_numpy(x[:n]).to(dev)
+        qs = torch.from_numpy(x[n:]).to(dev)
+        del x
+        t0 = time.time()
+        cen = uv.kmeans(base, nlist, seed=42, iters=5)
+        torch.cuda.synchronize()
+        km_s = time.time() - t0
+        codec = uv.Codec(d_pad, 2, 8)
+        ivf = uv.IvfIndex(codec, cen, centered=True)
+        t0 = time.time()
+        ivf.build(base)
+        torch.cuda.synchronize()
+        build_s = time.time() - t0
+        off = np.zeros(nlist + 1, np.int64)
+        import ctypes as C
+        uv.check(uv.lib().uv_ivf_export(ivf.h, C.c_void_p(off.ctypes.data), None, None, None,
+                                        None, None, None))
+        sizes = np.diff(off)
+        list_stats = {"mean": float(sizes.mean()), "max": int(sizes.max()),
+                      "p99": float(np.percentile(sizes, 99)), "empty": int((sizes == 0).sum())}
+        fams = ("prep_queries", "ivf_cosine", "ivf_select", "ivf_bucket", "ivf_pair_qm",
+                "ivf_scan", "merge_topk")
+        for nprobe in (1, 4, 16, 64):
+            ms = _timed(lambda: ivf.search(qs, 10, nprobe), 3)
+            uv.profile_enable(True)
+            ivf.search(qs, 10, nprobe)
+            torch.cuda.synchronize()
+            kern = {f: round(uv.profile_read(f)[0], 3) for f in fams}
+            uv.profile_enable(False)
+            emit("ivf-1Mx10k-d2048-nlist4096", {"nprobe": nprobe, "queries_s": nq / ms * 1e3,
+                                               "search_ms": ms, "kmeans_s": km_s,
+                                               "build_s": build_s, "centered": True, "k": 10,
+                                               "bits": 2, "mem": 8, "kernels_ms": kern,
+                                               "list_sizes": list_stats})
+    else:
+        d = 128
+        rows = rng.standard_normal((1_000_000, d), dtype=np.float32)
+        base = torch.from_numpy(rows).to(dev)
+        for mem in (2, 4, 8, 12):
+            n = 100_000 if mem == 12 else 1_000_000
+            codec = uv.Codec(d, 2, mem)
+            index = uv.Index(codec)
+            index.reserve(n)
+            sub = base[:n]
+            ms = _timed(lambda: (index.clear(), index.add_batch(sub)), 2)
+            emit("encode-sweep-d128-b2", {"mem": mem, "rows": n, "encode_rows_s": n / ms * 1e3,
+                                         "encode_ms": ms})
+            del index, codec
+        emit("encode-sweep-d128-b2", {"mem": 16, "unavailable":
+                                      "mem 16 needs a team of 8192 threads per row; not built"})
 
 
 if __name__ == "__main__":

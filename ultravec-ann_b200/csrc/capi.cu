@@ -571,11 +571,13 @@ namespace uvcapi {
 
 int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_key,
                  const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
-                 cudaStream_t st) {
+                 cudaStream_t st, const int64_t *row_off, const int32_t *out_row) {
   uvb::MergeParams m;
   std::memset(&m, 0, sizeof(m));
   m.nq = nq;
   m.n_lists = n_lists;
+  m.row_off = row_off;
+  m.out_row = out_row;
   m.k_in = k_in;
   m.k = k;
   int pow2 = 32;

@@ -228,9 +228,13 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
                   float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,
                   const float *list_centroids = nullptr, const uint32_t *row_list = nullptr,
                   const int64_t *row_index = nullptr);
+// Merge top-k lists: row q takes n_lists lists of k_in, or with row_off the
+// ragged lists [row_off[q], row_off[q+1]) (n_lists is then their maximum) and
+// writes output row out_row[q] when out_row is given.
 int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_key,
                  const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
-                 cudaStream_t st);
+                 cudaStream_t st, const int64_t *row_off = nullptr,
+                 const int32_t *out_row = nullptr);
 // normalize + rotate queries; u (unit, unrotated) optional
 int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *centroids,
                 int n_centroids, float *q_r, float *qc, uint32_t *degen, float *u,

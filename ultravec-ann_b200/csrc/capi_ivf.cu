@@ -195,32 +195,62 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   int32_t *lists = nullptr;
   UV_TRY(sc.alloc(&lists, (size_t)npairs));
   UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc));
-  // bucket the (query, list) pairs by list into scan items of <= 32 pairs
+  // bucket the (query, list) pairs by list; a scan item is one record range
+  // (at most range_size records: long lists are split for load balance) of
+  // one list for up to 32 of its pairs
   const int nlist = ix->nlist;
-  const int64_t max_items = std::min<int64_t>(nlist, npairs) + (npairs + uvb::kScanTQ - 1) / uvb::kScanTQ;
+  int64_t max_list = 0;
+  for (int l = 0; l < nlist; l++) max_list = std::max(max_list, ix->off[l + 1] - ix->off[l]);
+  // a pair's ranges are merged in one pass of at most about 1024 entries
+  const int64_t range_size =
+      std::max<int64_t>(1024, (max_list * k + 1023) / 1024);
   int32_t *cnt = nullptr, *fill = nullptr, *pair_off = nullptr, *item_off = nullptr,
-          *n_items = nullptr, *pair_query = nullptr, *pair_slot = nullptr, *item_list = nullptr,
-          *item_pair = nullptr, *item_npairs = nullptr;
+          *pair_query = nullptr, *pair_slot = nullptr, *pair_list = nullptr;
+  int64_t *list_rbase = nullptr, *totals = nullptr;
   UV_TRY(sc.alloc(&cnt, (size_t)nlist * 2));
   fill = cnt + nlist;
   UV_TRY(sc.alloc(&pair_off, (size_t)nlist));
   UV_TRY(sc.alloc(&item_off, (size_t)nlist));
-  UV_TRY(sc.alloc(&n_items, 1));
+  UV_TRY(sc.alloc(&list_rbase, (size_t)nlist));
+  UV_TRY(sc.alloc(&totals, 2));
   UV_TRY(sc.alloc(&pair_query, (size_t)npairs));
   UV_TRY(sc.alloc(&pair_slot, (size_t)npairs));
-  UV_TRY(sc.alloc(&item_list, (size_t)max_items));
-  UV_TRY(sc.alloc(&item_pair, (size_t)max_items));
-  UV_TRY(sc.alloc(&item_npairs, (size_t)max_items));
+  UV_TRY(sc.alloc(&pair_list, (size_t)npairs));
   UV_CK(cudaMemsetAsync(cnt, 0, sizeof(int32_t) * nlist * 2, st));
   {
     ProfScope ps("ivf_bucket", st);
     uvb::pair_count_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, npairs, cnt);
-    uvb::pair_scan_kernel<<<1, 1024, 0, st>>>(cnt, nlist, pair_off, item_off, n_items);
+    uvb::pair_scan_kernel<<<1, 1024, 0, st>>>(cnt, ix->d_off, nlist, range_size, pair_off,
+                                                item_off, list_rbase, totals);
     uvb::pair_scatter_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, nq, np, pair_off, fill,
-                                                                  pair_query, pair_slot);
-    uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(cnt, pair_off, item_off, nlist,
-                                                              item_list, item_pair, item_npairs);
+                                                                  pair_query, pair_slot, pair_list);
     UV_CK(cudaGetLastError());
+  }
+  int64_t h_tot[2] = {0, 0};
+  UV_CK(cudaMemcpyAsync(h_tot, totals, sizeof(h_tot), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  const int64_t n_items = h_tot[0], n_rslots = h_tot[1];
+  if (n_items > INT32_MAX) return fail(UV_EINVAL, "too many scan items");
+  int32_t *item_list = nullptr, *item_pair = nullptr, *item_npairs = nullptr,
+          *item_range = nullptr, *d_n_items = nullptr;
+  int64_t *row_off = nullptr;
+  UV_TRY(sc.alloc(&item_list, (size_t)n_items));
+  UV_TRY(sc.alloc(&item_pair, (size_t)n_items));
+  UV_TRY(sc.alloc(&item_npairs, (size_t)n_items));
+  UV_TRY(sc.alloc(&item_range, (size_t)n_items));
+  UV_TRY(sc.alloc(&d_n_items, 1));
+  UV_TRY(sc.alloc(&row_off, (size_t)npairs + 1));
+  {
+    const int32_t ni = (int32_t)n_items;
+    UV_CK(cudaMemcpyAsync(d_n_items, &ni, sizeof(ni), cudaMemcpyHostToDevice, st));
+    ProfScope ps("ivf_bucket", st);
+    uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(cnt, pair_off, item_off, ix->d_off,
+                                                              nlist, range_size, item_list,
+                                                              item_pair, item_npairs, item_range);
+    uvb::pair_rows_kernel<<<blocks(npairs + 1, 256), 256, 0, st>>>(
+        pair_list, pair_off, list_rbase, ix->d_off, range_size, (int)npairs, row_off);
+    UV_CK(cudaGetLastError());
+    UV_CK(cudaStreamSynchronize(st));  // `ni` is a host value of this frame
   }
   float *pair_qm = nullptr;
   if (ix->centered) {
@@ -231,11 +261,11 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                                                              (int)npairs, pair_qm);
     UV_CK(cudaGetLastError());
   }
-  // scan every item, one top-k per pair slot
+  // scan every item: one top-k per (pair, range) slot
   uint32_t *part_key = nullptr;
   int64_t *part_id = nullptr;
-  UV_TRY(sc.alloc(&part_key, (size_t)npairs * k));
-  UV_TRY(sc.alloc(&part_id, (size_t)npairs * k));
+  UV_TRY(sc.alloc(&part_key, (size_t)std::max<int64_t>(n_rslots, 1) * k));
+  UV_TRY(sc.alloc(&part_id, (size_t)std::max<int64_t>(n_rslots, 1) * k));
   const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
   const bool small_k = k <= 32;
   const size_t smem = uvb::chunked_scan_smem_bytes(c->table_len, table_smem, small_k);
@@ -280,18 +310,30 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   work.item_list = item_list;
   work.item_pair = item_pair;
   work.item_npairs = item_npairs;
+  work.item_range = item_range;
   work.list_off = ix->d_off;
+  work.list_pair_off = pair_off;
+  work.list_rbase = list_rbase;
+  work.range_size = range_size;
   work.pair_query = pair_query;
-  work.pair_slot = pair_slot;
   work.pair_qm = pair_qm;
-  work.n_items = n_items;
-  if (max_items > INT32_MAX) return fail(UV_EINVAL, "too many scan items");
-  {
+  work.n_items = d_n_items;
+  if (n_items > 0) {
     void *args[] = {&sp, &work};
     ProfScope ps("ivf_scan", st);
-    UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)max_items), dim3(256), args, smem, st));
+    UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)n_items), dim3(256), args, smem, st));
   }
-  return merge_launch(nq, np, k, k, part_key, nullptr, part_id, d_ids, d_scores, st);
+  // each pair's ranges -> its (query, probe) slot; then the probes per query
+  const int max_ranges = (int)((max_list + range_size - 1) / range_size) + 1;
+  uint32_t *pk = nullptr;
+  int64_t *pid = nullptr;
+  float *psc = nullptr;
+  UV_TRY(sc.alloc(&pid, (size_t)npairs * k));
+  UV_TRY(sc.alloc(&psc, (size_t)npairs * k));
+  (void)pk;
+  UV_TRY(merge_launch(npairs, max_ranges, k, k, part_key, nullptr, part_id, pid, psc, st,
+                      row_off, pair_slot));
+  return merge_launch(nq, np, k, k, nullptr, psc, pid, d_ids, d_scores, st);
 }
 
 }  // namespace

@@ -204,43 +204,63 @@ __global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t 
   if (i < npairs && lists[i] >= 0) atomicAdd(&cnt[lists[i]], 1);
 }
 
-// One CTA: exclusive scans of the pair counts and of the items per list
-// (ceil(count / 32)); n_items[0] = total items.
-__global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt, int nlist,
-                                                         int32_t *pair_off, int32_t *item_off,
-                                                         int32_t *n_items) {
-  __shared__ int32_t sp[1024], si[1024];
+// Record ranges of a list of `size` records: 1 for short lists, else
+// ceil(size / range_size).
+__device__ __forceinline__ int64_t list_ranges(int64_t size, int64_t range_size) {
+  return size <= range_size ? 1 : (size + range_size - 1) / range_size;
+}
+
+// One CTA: exclusive scans over the lists of the pair counts, of the scan
+// items (ranges x ceil(pairs / 32)) and of the range slots (pairs x ranges);
+// totals = {items, range slots}.
+__global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
+                                                         const int64_t *list_off, int nlist,
+                                                         int64_t range_size, int32_t *pair_off,
+                                                         int32_t *item_off, int64_t *list_rbase,
+                                                         int64_t *totals) {
+  __shared__ int64_t sp[1024], si[1024], sr[1024];
   const int t = threadIdx.x;
   const int per = (nlist + 1023) / 1024;
   const int lo = min(nlist, t * per), hi = min(nlist, lo + per);
-  int32_t ps = 0, is = 0;
+  int64_t ps = 0, is = 0, rs = 0;
   for (int l = lo; l < hi; l++) {
+    const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
     ps += cnt[l];
-    is += (cnt[l] + kScanTQ - 1) / kScanTQ;
+    is += nr * ((cnt[l] + kScanTQ - 1) / kScanTQ);
+    rs += nr * cnt[l];
   }
   sp[t] = ps;
   si[t] = is;
+  sr[t] = rs;
   __syncthreads();
   for (int o = 1; o < 1024; o <<= 1) {
-    const int32_t a = t >= o ? sp[t - o] : 0, b = t >= o ? si[t - o] : 0;
+    const int64_t a = t >= o ? sp[t - o] : 0, b = t >= o ? si[t - o] : 0,
+                  c = t >= o ? sr[t - o] : 0;
     __syncthreads();
     sp[t] += a;
     si[t] += b;
+    sr[t] += c;
     __syncthreads();
   }
-  int32_t pbase = sp[t] - ps, ibase = si[t] - is;
+  int64_t pbase = sp[t] - ps, ibase = si[t] - is, rbase = sr[t] - rs;
   for (int l = lo; l < hi; l++) {
-    pair_off[l] = pbase;
-    item_off[l] = ibase;
+    const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
+    pair_off[l] = (int32_t)pbase;
+    item_off[l] = (int32_t)ibase;
+    list_rbase[l] = rbase;
     pbase += cnt[l];
-    ibase += (cnt[l] + kScanTQ - 1) / kScanTQ;
+    ibase += nr * ((cnt[l] + kScanTQ - 1) / kScanTQ);
+    rbase += nr * cnt[l];
   }
-  if (t == 1023) n_items[0] = si[1023];
+  if (t == 1023) {
+    totals[0] = si[1023];
+    totals[1] = sr[1023];
+  }
 }
 
 __global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
                                     const int32_t *pair_off, int32_t *fill, int32_t *pair_query,
-                                    int32_t *pair_slot) {
+                                    int32_t *pair_slot, int32_t *pair_list) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nq * np) return;
   const int l = lists[i];
@@ -248,20 +268,42 @@ __global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
   const int pos = pair_off[l] + atomicAdd(&fill[l], 1);
   pair_query[pos] = (int32_t)(i / np);
   pair_slot[pos] = (int32_t)i;
+  pair_list[pos] = l;
 }
 
 __global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
-                                 const int32_t *item_off, int nlist, int32_t *item_list,
-                                 int32_t *item_pair, int32_t *item_npairs) {
+                                 const int32_t *item_off, const int64_t *list_off, int nlist,
+                                 int64_t range_size, int32_t *item_list, int32_t *item_pair,
+                                 int32_t *item_npairs, int32_t *item_range) {
   const int l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= nlist) return;
   const int c = cnt[l];
-  for (int i = 0; i * kScanTQ < c; i++) {
-    const int it = item_off[l] + i;
-    item_list[it] = l;
-    item_pair[it] = pair_off[l] + i * kScanTQ;
-    item_npairs[it] = min(kScanTQ, c - i * kScanTQ);
+  const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
+  int it = item_off[l];
+  for (int64_t r = 0; r < nr; r++)
+    for (int i = 0; i * kScanTQ < c; i++, it++) {
+      item_list[it] = l;
+      item_pair[it] = pair_off[l] + i * kScanTQ;
+      item_npairs[it] = min(kScanTQ, c - i * kScanTQ);
+      item_range[it] = (int32_t)r;
+    }
+}
+
+// First range slot of every pair (bucketed order) and, at index npairs, the
+// total: the ragged rows of the per-pair range merge.
+__global__ void pair_rows_kernel(const int32_t *pair_list, const int32_t *pair_off,
+                                 const int64_t *list_rbase, const int64_t *list_off,
+                                 int64_t range_size, int npairs, int64_t *row_off) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i > npairs) return;
+  if (i == npairs) {
+    if (npairs == 0) row_off[0] = 0;
+    return;
   }
+  const int l = pair_list[i];
+  const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
+  row_off[i] = list_rbase[l] + (int64_t)(i - pair_off[l]) * nr;
+  if (i == npairs - 1) row_off[npairs] = row_off[i] + nr;
 }
 
 // qm of each pair: seq_dot(u_query, centroid_list) (trellis.rs:2120-2183 with

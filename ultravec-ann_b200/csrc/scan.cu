@@ -552,12 +552,17 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
     if (item >= w.n_items[0]) return;  // before any barrier: the whole CTA leaves
     const int list = w.item_list[item];
     const int pair0 = w.item_pair[item];
+    const int range = w.item_range[item];
     nql = w.item_npairs[item];
-    r_begin = w.list_off[list];
-    r_end = w.list_off[list + 1];
+    const int64_t lo = w.list_off[list], hi = w.list_off[list + 1];
+    const int64_t nr = hi - lo <= w.range_size ? 1 : (hi - lo + w.range_size - 1) / w.range_size;
+    r_begin = min(hi, lo + (int64_t)range * w.range_size);
+    r_end = min(hi, r_begin + w.range_size);
     if (tid < TQ) {
+      // output slot: this pair's block of nr range slots, entry `range`
+      const int64_t pl = (int64_t)(pair0 + tid) - w.list_pair_off[list];
       qrow[tid] = tid < nql ? (int64_t)w.pair_query[pair0 + tid] : -1;
-      slot[tid] = tid < nql ? (int64_t)w.pair_slot[pair0 + tid] : -1;
+      slot[tid] = tid < nql ? w.list_rbase[list] + pl * nr + range : -1;
       qm_s[tid] = (tid < nql && w.pair_qm) ? w.pair_qm[pair0 + tid] : 0.0f;
     }
   }
@@ -807,16 +812,25 @@ __global__ void __launch_bounds__(256) merge_topk_kernel(const MergeParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t q = (int64_t)blockIdx.x * p.warps + warp;
-  const int n = p.pow2;
-  KeyId *a = (KeyId *)sm + (size_t)warp * n;
+  KeyId *a = (KeyId *)sm + (size_t)warp * p.pow2;
   if (q >= p.nq) return;  // whole warp exits together
-  const int total = p.n_lists * p.k_in;
+  // fixed rows: n_lists lists per query; ragged rows: lists [row_off[q], row_off[q+1])
+  const int64_t first = p.row_off ? p.row_off[q] * p.k_in : q * (int64_t)p.n_lists * p.k_in;
+  const int total = p.row_off ? (int)((p.row_off[q + 1] - p.row_off[q]) * p.k_in)
+                              : p.n_lists * p.k_in;
+  const int64_t orow = p.out_row ? (int64_t)p.out_row[q] : q;
+  // ragged rows sort only the next power of two of their own length
+  int n = p.pow2;
+  if (p.row_off) {
+    n = 32;
+    while (n < total) n <<= 1;
+  }
   for (int i = lane; i < n; i += 32) {
     KeyId e;
     e.key = 0u;
     e.id = -1;
     if (i < total) {
-      const int64_t src = q * total + i;
+      const int64_t src = first + i;
       e.id = p.in_id[src];
       e.key = p.in_key ? p.in_key[src] : 0u;
       if (p.in_score) e.key = score_key32(p.in_score[src]);
@@ -843,8 +857,8 @@ __global__ void __launch_bounds__(256) merge_topk_kernel(const MergeParams p) {
   }
   for (int i = lane; i < p.k; i += 32) {
     const KeyId e = a[i];
-    p.out_id[q * p.k + i] = e.id;
-    p.out_score[q * p.k + i] = e.id < 0 ? -INFINITY : key32_score(e.key);
+    p.out_id[orow * p.k + i] = e.id;
+    p.out_score[orow * p.k + i] = e.id < 0 ? -INFINITY : key32_score(e.key);
   }
 }
 

@@ -91,16 +91,22 @@ struct ScanParams {
 // record splits, as for flat_scan_kernel.  IVF: item i scans the records of
 // list item_list[i] for up to 32 (query, probe) pairs starting at
 // item_pair[i]; each pair writes its top-k to output slot pair_slot[j].
+// Long lists are split into record ranges of range_size; item i scans range
+// item_range[i] of list item_list[i] for up to 32 pairs, and pair j of list l
+// writes range r to slot list_rbase[l] + (j - list_pair_off[l]) * nr(l) + r.
 struct ScanWork {
   int ivf;
   const int32_t *item_list;
   const int32_t *item_pair;
   const int32_t *item_npairs;
-  const int64_t *list_off;    // nlist + 1
-  const int32_t *pair_query;  // query row of q_r
-  const int32_t *pair_slot;   // output slot: query * nprobe + probe rank
-  const float *pair_qm;       // <u, c_list> (centered lists) or null
-  const int32_t *n_items;     // IVF: CTAs at or past *n_items exit
+  const int32_t *item_range;
+  const int64_t *list_off;       // nlist + 1
+  const int32_t *list_pair_off;  // first pair of each list (bucketed order)
+  const int64_t *list_rbase;     // first range slot of each list
+  int64_t range_size;
+  const int32_t *pair_query;     // query row of q_r
+  const float *pair_qm;          // <u, c_list> (centered lists) or null
+  const int32_t *n_items;        // IVF: CTAs at or past *n_items exit
 };
 
 // Sequential-dot tiles of the IVF coarse stage (ivf.cu).
@@ -172,8 +178,10 @@ struct TcRescoreParams {
 };
 
 struct MergeParams {
-  int64_t nq;
+  int64_t nq;                // rows to merge
   int n_lists, k_in, k, pow2, warps;
+  const int64_t *row_off;    // or null: row q merges lists [row_off[q], row_off[q+1])
+  const int32_t *out_row;    // or null: row q writes output row out_row[q]
   const uint32_t *in_key;  // or null
   const float *in_score;   // or null
   const int64_t *in_id;
@@ -219,14 +227,19 @@ __global__ void select_top_kernel(const float *scores, int64_t n, int nb, int po
                                   int ld_out, int32_t *out);
 __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n);
 __global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt);
-__global__ void pair_scan_kernel(const int32_t *cnt, int nlist, int32_t *pair_off,
-                                 int32_t *item_off, int32_t *n_items);
+__global__ void pair_scan_kernel(const int32_t *cnt, const int64_t *list_off, int nlist,
+                                 int64_t range_size, int32_t *pair_off, int32_t *item_off,
+                                 int64_t *list_rbase, int64_t *totals);
 __global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
                                     const int32_t *pair_off, int32_t *fill, int32_t *pair_query,
-                                    int32_t *pair_slot);
+                                    int32_t *pair_slot, int32_t *pair_list);
 __global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
-                                 const int32_t *item_off, int nlist, int32_t *item_list,
-                                 int32_t *item_pair, int32_t *item_npairs);
+                                 const int32_t *item_off, const int64_t *list_off, int nlist,
+                                 int64_t range_size, int32_t *item_list, int32_t *item_pair,
+                                 int32_t *item_npairs, int32_t *item_range);
+__global__ void pair_rows_kernel(const int32_t *pair_list, const int32_t *pair_off,
+                                 const int64_t *list_rbase, const int64_t *list_off,
+                                 int64_t range_size, int npairs, int64_t *row_off);
 __global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, int dim,
                                const int32_t *pair_query, const int32_t *pair_slot, int np,
                                const int32_t *lists, int npairs, float *qm);
