@@ -57,6 +57,13 @@ __device__ __forceinline__ uint64_t team_max_u64(uint64_t v, const Team &tm,
 }
 
 
+// 3-input minimum (NaN-ignoring like fminf; NaN only when all three are).
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <int B, int WPT, bool BACK_SMEM>
 __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
   constexpr int NE = 1 << B;
@@ -186,81 +193,94 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     // round(cost + m) and nothing is left to contract.
     float *cur = cost0, *nxt = cost1;
     float last[SPT];
-    uint32_t word = 0;
-    for (int step = 0; step < d; step++) {
-      const float xi = ubuf[step];
-      const float2 xi2 = make_float2(xi, xi);
-      const float wi = aniso ? fadd(1.0f, fmul(fmul(p.lambda, xi), xi)) : 1.0f;
-      const float2 wi2 = make_float2(wi, wi);
-      float2 cp[GPT][NE / 2];
+    // Add-compare-select.  The reference keeps the first candidate and
+    // replaces it only on a strictly smaller cost, i.e. it picks the first k
+    // whose cost equals the minimum.  Here the minimum comes from 3-input
+    // min instructions and the choice is the first k with !(c_k > min): the
+    // same k and the same value (costs are never -0; within one step either
+    // every candidate is NaN -- then min is NaN, no c_k > NaN holds and k = 0
+    // as in the reference -- or none is).  The step loop is unrolled by the
+    // steps per back-pointer word so that the word's shifts are constants.
+    for (int step0 = 0; step0 < d; step0 += SPW) {
+      uint32_t word = 0;
 #pragma unroll
-      for (int g = 0; g < GPT; g++) {
-        const int q = group_of(g);
-#pragma unroll
-        for (int k = 0; k < NE; k += 2)
-          cp[g][k / 2] = make_float2(cur[q + k * GS], cur[q + (k + 1) * GS]);
-      }
-      const int slot_bits = (step % SPW) * BPS;
-      float best[SPT];
-#pragma unroll
-      for (int j = 0; j < SPT; j++) {
-        const int g = (SPT >= NE) ? j / NE : 0;
-        uint32_t bk = 0;
-#pragma unroll
-        for (int k = 0; k < NE; k += 2) {
-          const float2 dd = __fadd2_rn(xi2, ncode[j][k / 2]);
-          const float2 m = aniso ? __fmul2_rn(__fmul2_rn(wi2, dd), dd) : __fmul2_rn(dd, dd);
-          const float2 c = __ffma2_rn(m, p.one2, cp[g][k / 2]);
-          if (k == 0) {
-            best[j] = c.x;
-          } else if (c.x < best[j]) {
-            best[j] = c.x;
-            bk = (uint32_t)k;
-          }
-          if (c.y < best[j]) {
-            best[j] = c.y;
-            bk = (uint32_t)(k + 1);
-          }
-        }
-        last[j] = best[j];
-        word |= bk << (slot_bits + j * B);
-      }
-      // next-cost stores: one vector store per owned run of states
-      if (SPT >= NE) {
+      for (int sub = 0; sub < SPW; sub++) {
+        const int step = step0 + sub;
+        if (step >= d) break;
+        const float xi = ubuf[step];
+        const float2 xi2 = make_float2(xi, xi);
+        const float wi = aniso ? fadd(1.0f, fmul(fmul(p.lambda, xi), xi)) : 1.0f;
+        const float2 wi2 = make_float2(wi, wi);
+        float2 cp[GPT][NE / 2];
 #pragma unroll
         for (int g = 0; g < GPT; g++) {
-          float *dst = nxt + (group_of(g) << B);
+          const int q = group_of(g);
+#pragma unroll
+          for (int k = 0; k < NE; k += 2)
+            cp[g][k / 2] = make_float2(cur[q + k * GS], cur[q + (k + 1) * GS]);
+        }
+        float best[SPT];
+#pragma unroll
+        for (int j = 0; j < SPT; j++) {
+          const int g = (SPT >= NE) ? j / NE : 0;
+          float cv[NE];
+#pragma unroll
+          for (int k = 0; k < NE; k += 2) {
+            const float2 dd = __fadd2_rn(xi2, ncode[j][k / 2]);
+            const float2 m = aniso ? __fmul2_rn(__fmul2_rn(wi2, dd), dd) : __fmul2_rn(dd, dd);
+            const float2 c = __ffma2_rn(m, p.one2, cp[g][k / 2]);
+            cv[k] = c.x;
+            cv[k + 1] = c.y;
+          }
+          float mn;
           if (NE == 2) {
-            *(float2 *)dst = make_float2(best[g * NE], best[g * NE + 1]);
+            mn = fminf(cv[0], cv[1]);
+          } else {
+            mn = min3(cv[0], cv[1], cv[2]);
+#pragma unroll
+            for (int k = 3; k < NE; k += 2) mn = (k + 1 < NE) ? min3(mn, cv[k], cv[k + 1]) : fminf(mn, cv[k]);
+          }
+          uint32_t bk = NE - 1;
+#pragma unroll
+          for (int k = NE - 2; k >= 0; k--) bk = (cv[k] > mn) ? bk : (uint32_t)k;
+          best[j] = mn;
+          last[j] = mn;
+          word |= bk << (sub * BPS + j * B);
+        }
+        // next-cost stores: one vector store per owned run of states
+        if (SPT >= NE) {
+#pragma unroll
+          for (int g = 0; g < GPT; g++) {
+            float *dst = nxt + (group_of(g) << B);
+            if (NE == 2) {
+              *(float2 *)dst = make_float2(best[g * NE], best[g * NE + 1]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < NE; e += 4)
+                *(float4 *)(dst + e) = make_float4(best[g * NE + e], best[g * NE + e + 1],
+                                                   best[g * NE + e + 2], best[g * NE + e + 3]);
+            }
+          }
+        } else {
+          float *dst = nxt + tm.t * SPT;
+          if (SPT == 2) {
+            *(float2 *)dst = make_float2(best[0], best[1]);
           } else {
 #pragma unroll
-            for (int e = 0; e < NE; e += 4)
-              *(float4 *)(dst + e) = make_float4(best[g * NE + e], best[g * NE + e + 1],
-                                                 best[g * NE + e + 2], best[g * NE + e + 3]);
+            for (int e = 0; e < SPT; e += 4)
+              *(float4 *)(dst + e) = make_float4(best[e], best[e + 1], best[e + 2], best[e + 3]);
           }
         }
-      } else {
-        float *dst = nxt + tm.t * SPT;
-        if (SPT == 2) {
-          *(float2 *)dst = make_float2(best[0], best[1]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < SPT; e += 4)
-            *(float4 *)(dst + e) = make_float4(best[e], best[e + 1], best[e + 2], best[e + 3]);
-        }
+        float *tmp = cur;
+        cur = nxt;
+        nxt = tmp;
+        tm.sync();
       }
-      if ((step % SPW) == SPW - 1 || step == d - 1) {
-        const int widx = (step / SPW) * T + tm.t;
-        if (BACK_SMEM)
-          backs[widx] = word;
-        else
-          backg[widx] = word;
-        word = 0;
-      }
-      float *tmp = cur;
-      cur = nxt;
-      nxt = tmp;
-      tm.sync();
+      const int widx = (step0 / SPW) * T + tm.t;
+      if (BACK_SMEM)
+        backs[widx] = word;
+      else
+        backg[widx] = word;
     }
 
     // ---- argmin under total_cmp, first index on ties ----
