@@ -481,8 +481,8 @@ def run_secondary(args):
                   0.3 N(0,1), renormalized; k-means nlist=4096 (seed 42, 5
                   rounds), centered lists, b=2, M=8; 10k-query top-10 at
                   nprobe 1/4/16/64
-    encode-sweep  1M rows (a 100k prefix at M=12), d=128 N(0,1), b=2, M in
-                  {2, 4, 8, 12}: encode rows/s"""
+    encode-sweep  1M rows (a 100k prefix at M=12, 10k at M=16), d=128 N(0,1),
+                  b=2, M in {2, 4, 8, 12, 16}: encode rows/s"""
     import torch
 
     from ultravec_ann_b200_loader import load
@@ -564,8 +564,8 @@ def run_secondary(args):
         d = 128
         rows = rng.standard_normal((1_000_000, d), dtype=np.float32)
         base = torch.from_numpy(rows).to(dev)
-        for mem in (2, 4, 8, 12):
-            n = 100_000 if mem == 12 else 1_000_000
+        for mem in (2, 4, 8, 12, 16):
+            n = {12: 100_000, 16: 10_000}.get(mem, 1_000_000)
             codec = uv.Codec(d, 2, mem)
             index = uv.Index(codec)
             index.reserve(n)
@@ -574,8 +574,6 @@ def run_secondary(args):
             emit("encode-sweep-d128-b2", {"mem": mem, "rows": n, "encode_rows_s": n / ms * 1e3,
                                          "encode_ms": ms})
             del index, codec
-        emit("encode-sweep-d128-b2", {"mem": 16, "unavailable":
-                                      "mem 16 needs a team of 8192 threads per row; not built"})
 
 
 if __name__ == "__main__":

@@ -79,6 +79,28 @@ def test_encode_wide_rows_bit_exact(uv, oracle, dim, bits):
     _assert_records(got, want)
 
 
+@pytest.mark.parametrize("dim,bits,mem,n,kw", [
+    (128, 2, 13, 48, {}),                       # 2 CTAs per row
+    (128, 2, 14, 40, {"branch_lambda": 0.5}),   # 4 CTAs, anisotropic metric
+    (64, 1, 14, 40, {"start_bits": 9}),         # 2 CTAs, restricted free start
+    (64, 2, 16, 24, {}),                        # 16 CTAs (8192 threads per row)
+    (32, 1, 17, 24, {}),                        # 16 CTAs at b = 1
+])
+def test_encode_cluster_bit_exact(uv, oracle, dim, bits, mem, n, kw):
+    """mem + bits >= 15: one thread-block cluster per row (encode_cluster.cu),
+    costs exchanged through distributed shared memory."""
+    rows = oracle.rand_unit(n, dim, 900 + mem + bits)
+    _, _, got, want = _encode_both(uv, oracle, dim, bits, mem, rows, **kw)
+    _assert_records(got, want)
+
+
+def test_encode_cluster_centered_and_raw_rows(uv, oracle):
+    rows = rand_rows(32, 128, 31) * np.float32(7.0)
+    cen = oracle.kmeans(rows, 4, 42)
+    _, _, got, want = _encode_both(uv, oracle, 128, 2, 13, rows, centroids=cen)
+    _assert_records(got, want, cidx=True)
+
+
 def test_encode_raw_heavy_tailed_rows(uv, oracle):
     """Non-unit, non-negative integer rows (the flat-scan corpus shape)."""
     rng = np.random.default_rng(5)

@@ -215,7 +215,10 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   int grid = 0;
   UV_CK(uvb::encode_grid(c->plan, n, &grid));
   if (!c->plan.back_smem) {
-    const size_t words = (size_t)grid * c->plan.teams_per_cta * (size_t)c->plan.back_words_team;
+    // one back-pointer slot per team (per cluster for the cluster encoder)
+    const size_t teams = c->plan.cluster > 0 ? (size_t)(grid / c->plan.cluster)
+                                             : (size_t)grid * c->plan.teams_per_cta;
+    const size_t words = teams * (size_t)c->plan.back_words_team;
     UV_TRY(sc.alloc(&p.back_global, words));
   }
   {

@@ -28,34 +28,9 @@
 // predecessor) wins an exact tie.  Every f32 op is a separately rounded
 // intrinsic, matching the reference bit for bit.
 #include "uv_kernels.h"
-#include "uv_team.cuh"
+#include "uv_encode_row.cuh"
 
 namespace uvb {
-
-// Team-wide maximum of a 64-bit key.  `scratch` holds 32 u64 in shared memory
-// (only used when the team spans the CTA).
-__device__ __forceinline__ uint64_t team_max_u64(uint64_t v, const Team &tm,
-                                                 uint64_t *scratch) {
-  if (!tm.cta) {
-    for (int o = tm.T >> 1; o > 0; o >>= 1) {
-      uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
-      v = w > v ? w : v;
-    }
-    return v;
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
-    v = w > v ? w : v;
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  uint64_t r = scratch[0];
-  for (int w = 1; w < (tm.T >> 5); w++) r = scratch[w] > r ? scratch[w] : r;
-  __syncthreads();
-  return r;
-}
-
 
 // 3-input minimum (NaN-ignoring like fminf; NaN only when all three are).
 __device__ __forceinline__ float min3(float a, float b, float c) {
@@ -131,54 +106,7 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     const int64_t vv = valid ? v : p.n - 1;
 
     // ---- prep: load, normalize, center, rotate, standardize ----
-    const float *row = p.rows + (p.row_index ? p.row_index[vv] : vv) * (int64_t)d;
-    for (int i = tm.t; i < d; i += T) xbuf[i] = row[i];
-    tm.sync();
-    if (!p.rotated_input) {
-      if (tm.leader()) {
-        float l2 = fsqrt(seq_sum_sq(xbuf, d));
-        misc[0] = l2;
-        misc[1] = fmax_rs(l2, kF32Eps);
-        misc[2] = 1.0f;
-        misc_u[4] = 0u;
-      }
-      tm.sync();
-      const float nrm = misc[1];
-      for (int i = tm.t; i < d; i += T) xbuf[i] = fdiv(xbuf[i], nrm);
-      tm.sync();
-      const float *cen = nullptr;
-      if (p.list_centroids != nullptr) {
-        cen = p.list_centroids + (size_t)p.row_list[vv] * d;
-      } else if (p.n_centroids > 0) {
-        // assign (src/trellis.rs:993-1004): first strict maximum of <u, c_j>
-        uint64_t best = 0;
-        for (int j = tm.t; j < p.n_centroids; j += T) {
-          float dj = seq_dot(xbuf, p.centroids + (size_t)j * d, d);
-          uint64_t key = ((uint64_t)score_key32(dj) << 32) | (uint32_t)(~(uint32_t)j);
-          best = key > best ? key : best;
-        }
-        best = team_max_u64(best, tm, red);
-        uint32_t j = ~(uint32_t)(best & 0xffffffffu);
-        // every dot NaN or -inf: the reference keeps index 0
-        if ((uint32_t)(best >> 32) <= score_key32(-INFINITY)) j = 0;
-        if (tm.leader()) misc_u[4] = j;
-        cen = p.centroids + (size_t)j * d;
-      }
-      if (cen != nullptr) {
-        for (int i = tm.t; i < d; i += T) xbuf[i] = fsub(xbuf[i], cen[i]);
-        tm.sync();
-        if (tm.leader()) misc[2] = fmax_rs(fsqrt(seq_sum_sq(xbuf, d)), kF32Eps);
-        tm.sync();
-        const float rn = misc[2];
-        for (int i = tm.t; i < d; i += T) xbuf[i] = fdiv(xbuf[i], rn);
-        tm.sync();
-      }
-      team_rotate(xbuf, p.rot, tm, false);
-    }
-    if (tm.leader()) misc[3] = fmax_rs(seq_std_about_mean(xbuf, d), kF32Eps);
-    tm.sync();
-    const float scale = misc[3];
-    for (int i = tm.t; i < d; i += T) ubuf[i] = fdiv(xbuf[i], scale);
+    encode_row_prep(p, vv, xbuf, ubuf, misc, red, tm);
     for (int s = tm.t; s < NS; s += T) cost0[s] = ((uint32_t)s < free_states) ? 0.0f : INFINITY;
     tm.sync();
 
@@ -340,47 +268,7 @@ __global__ void __launch_bounds__(512) encode_kernel(const EncodeParams p) {
     tm.sync();
 
     // ---- finalize: rescale (leader, sequential) and packing (team) ----
-    if (tm.leader()) {
-      float rs = 0.0f;
-      for (int i = 0; i < d; i++) rs = fadd(rs, fmul(__ldg(p.code + wv[i]), xbuf[i]));
-      if (p.rescale_bits > 0 && rs > 1e-6f) {
-        const float levels = (float)((1u << p.rescale_bits) - 1u);
-        const float sq = fsqrt((float)d);
-        const float lo = fmul(0.0f, sq), hi = fmul(1.25f, sq);
-        float t = fdiv(fsub(rs, lo), fsub(hi, lo));
-        t = t < 0.0f ? 0.0f : (t > 1.0f ? 1.0f : t);
-        rs = fadd(lo, fmul(fdiv(roundf(fmul(t, levels)), levels), fsub(hi, lo)));
-      }
-      misc[6] = rs > 1e-6f ? rs : INFINITY;
-    }
-    if (valid && p.codes != nullptr) {
-      uint8_t *out = p.codes + vv * (int64_t)p.code_stride;
-      const int nbits = d * B;
-      for (int bi = tm.t; bi < p.code_stride; bi += T) {
-        uint32_t val = 0;
-        if (bi < p.code_bytes) {
-#pragma unroll
-          for (int bit = 0; bit < 8; bit++) {
-            const int pos = bi * 8 + bit;
-            if (pos < nbits) {
-              const int i = pos / B;
-              const int off = B - 1 - (pos - i * B);
-              val |= ((wv[i] >> off) & 1u) << (7 - bit);
-            }
-          }
-        }
-        out[bi] = (uint8_t)val;
-      }
-    }
-    tm.sync();
-    if (valid && tm.leader()) {
-      if (p.start) p.start[vv] = misc_u[5];
-      if (p.rescale) p.rescale[vv] = misc[6];
-      if (p.rnorm) p.rnorm[vv] = p.rotated_input ? 1.0f : misc[2];
-      if (p.cidx) p.cidx[vv] = p.rotated_input ? 0u : misc_u[4];
-      if (p.norms) p.norms[vv] = p.rotated_input ? 0.0f : misc[0];
-    }
-    tm.sync();
+    encode_row_finalize<B>(p, vv, valid, wv, xbuf, misc, tm);
   }
 }
 
@@ -425,10 +313,7 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
   const int64_t nw = (int64_t)1 << (mem + bits);
   const int wpt = nw >= 32 ? 32 : (int)nw;
   const int64_t T = nw / wpt;
-  if (T > 512) {
-    *why = "2^(mem+bits) > 16384 windows needs the multi-CTA encoder (not built yet)";
-    return 2;
-  }
+  if (T > 512) return encode_cluster_plan(dim, bits, mem, plan, why);
   const int spt = wpt >> bits;
   const int bps = spt * bits;
   const int spw = 32 / bps;
@@ -486,6 +371,7 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
 }
 
 cudaError_t encode_launch(const EncodePlan &plan, EncodeParams p, int grid, cudaStream_t st) {
+  if (plan.cluster > 0) return encode_cluster_launch(plan, p, grid, st);
   p.T = plan.T;
   p.teams_per_cta = plan.teams_per_cta;
   p.team_smem_words = plan.team_smem_words;
@@ -500,6 +386,7 @@ cudaError_t encode_launch(const EncodePlan &plan, EncodeParams p, int grid, cuda
 }
 
 cudaError_t encode_grid(const EncodePlan &plan, int64_t n, int *grid) {
+  if (plan.cluster > 0) return encode_cluster_grid(plan, n, grid);
   int dev = 0, sms = 0, per_sm = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

@@ -38,6 +38,7 @@ struct EncodeParams {
 
 struct EncodePlan {
   int B, WPT, T, n_states, dim_pad, teams_per_cta, threads, team_smem_words;
+  int cluster = 0;           // > 0: one cluster of this many CTAs per row (encode_cluster.cu)
   bool back_smem;
   int64_t back_words_team;
   size_t smem_bytes;
@@ -50,6 +51,11 @@ extern int g_encode_back_mode;  // placement of back-pointers; never changes res
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
 cudaError_t encode_grid(const EncodePlan &plan, int64_t n, int *grid);
 cudaError_t encode_launch(const EncodePlan &plan, EncodeParams p, int grid, cudaStream_t st);
+// encode_cluster.cu: rows whose trellis needs more than one 512-thread CTA
+int encode_cluster_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
+cudaError_t encode_cluster_grid(const EncodePlan &plan, int64_t n, int *grid);
+cudaError_t encode_cluster_launch(const EncodePlan &plan, EncodeParams p, int grid,
+                                  cudaStream_t st);
 
 struct PrepParams {
   int dim, dim_pad;
