@@ -275,6 +275,20 @@ int uv_ivf_export(const uv_ivf *ivf, int64_t *list_off, int64_t *ids, uint8_t *c
 /* XOR-folded per-record FNV-1a digest of every posting (as uv_digest). */
 int uv_ivf_digest(const uv_ivf *ivf, uint64_t *digest, void *stream);
 
+/* ---- index files: one list-major SoA per index ------------------------- */
+
+/* Build once, search many (and checkpoint): the records, sidecars, ids and
+ * centroids of a flat index, or the lists of an IVF index, as one file of
+ * flat little-endian arrays with a header carrying the codec configuration
+ * and an FNV-1a checksum.  It replaces the reference's in-memory per-entry
+ * records (TVec, src/trellis.rs:158-198).  Load returns UV_EINVAL for a
+ * file that is not an index of this kind, was written by a codec of another
+ * configuration, is truncated, or fails its checksum. */
+int uv_index_save(const uv_index *index, const char *path);
+int uv_index_load(const uv_codec *codec, const char *path, uv_index **out);
+int uv_ivf_save(const uv_ivf *ivf, const char *path);
+int uv_ivf_load(const uv_codec *codec, const char *path, uv_ivf **out);
+
 #ifdef __cplusplus
 }
 #endif

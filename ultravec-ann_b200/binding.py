@@ -33,7 +33,8 @@ SYMBOLS = [
     "uv_profile_enable", "uv_profile_read", "uv_set_tuning", "uv_index_search_noalloc",
     "uv_kmeans", "uv_ivf_assign", "uv_ivf_create", "uv_ivf_destroy", "uv_ivf_build",
     "uv_ivf_len", "uv_ivf_nlist", "uv_ivf_mem_bytes", "uv_ivf_probe", "uv_ivf_search",
-    "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest",
+    "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest", "uv_index_save", "uv_index_load",
+    "uv_ivf_save", "uv_ivf_load",
 ]
 
 
@@ -111,6 +112,10 @@ def lib():
                                                vp]),
             "uv_ivf_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp]),
             "uv_ivf_digest": (C.c_int, [vp, C.POINTER(u64), vp]),
+            "uv_index_save": (C.c_int, [vp, C.c_char_p]),
+            "uv_index_load": (C.c_int, [vp, C.c_char_p, vpp]),
+            "uv_ivf_save": (C.c_int, [vp, C.c_char_p]),
+            "uv_ivf_load": (C.c_int, [vp, C.c_char_p, vpp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -359,6 +364,19 @@ class Index:
         check(lib().uv_index_digest(self.h, C.byref(h), None))
         return h.value
 
+    def save(self, path) -> None:
+        """Write the index file (records, sidecars, ids, centroids)."""
+        check(lib().uv_index_save(self.h, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, codec: Codec, path) -> "Index":
+        """An index read from a file written by a codec of this configuration."""
+        h = C.c_void_p()
+        check(lib().uv_index_load(codec.h, os.fsencode(path), C.byref(h)))
+        ix = cls.__new__(cls)
+        ix.h, ix.codec = h, codec
+        return ix
+
 
 # ------------------------------------------------------------------- IVF ---
 
@@ -469,6 +487,17 @@ class IvfIndex:
         h = C.c_uint64()
         check(lib().uv_ivf_digest(self.h, C.byref(h), None))
         return h.value
+
+    def save(self, path) -> None:
+        check(lib().uv_ivf_save(self.h, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, codec: Codec, path) -> "IvfIndex":
+        h = C.c_void_p()
+        check(lib().uv_ivf_load(codec.h, os.fsencode(path), C.byref(h)))
+        ix = cls.__new__(cls)
+        ix.h, ix.codec, ix.centered = h, codec, None
+        return ix
 
 
 def topk_merge(in_ids, in_scores, k: int, device: int = 0):

@@ -9,20 +9,6 @@
 
 using namespace uvcapi;
 
-struct uv_ivf {
-  const uv_codec *codec = nullptr;
-  int nlist = 0, centered = 0;
-  float *centroids = nullptr;  // nlist x dim
-  float *cnorm = nullptr;      // |c_j| (lib.rs:215-217)
-  int64_t n = 0;
-  std::vector<int64_t> off;    // nlist + 1
-  int64_t *d_off = nullptr;
-  uint8_t *codes = nullptr;
-  uint32_t *start = nullptr;
-  float *rescale = nullptr, *rnorm = nullptr;
-  int64_t *ids = nullptr;
-};
-
 namespace {
 
 unsigned blocks(int64_t n, int per) { return (unsigned)((n + per - 1) / per); }
