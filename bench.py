@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--n-query", type=int, default=N_QUERY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep"], default="flat",
+    ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep", "candidates"],
+                    default="flat",
                     help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
                          "others measure the remaining configurations, one JSON line each")
     ap.add_argument("--scan", choices=["auto", "exact", "tc"], default="auto",
@@ -482,7 +483,10 @@ def run_secondary(args):
                   rounds), centered lists, b=2, M=8; 10k-query top-10 at
                   nprobe 1/4/16/64
     encode-sweep  1M rows (a 100k prefix at M=12, 10k at M=16), d=128 N(0,1),
-                  b=2, M in {2, 4, 8, 12, 16}: encode rows/s"""
+                  b=2, M in {2, 4, 8, 12, 16}: encode rows/s
+    candidates    1M rows d=128 N(0,1), b=2, M=8; 10k prepared queries with
+                  256 uniformly random candidate positions each (a batched
+                  graph-walk expansion): candidates scored per second"""
     import torch
 
     from ultravec_ann_b200_loader import load
@@ -560,6 +564,31 @@ def run_secondary(args):
                                                "build_s": build_s, "centered": True, "k": 10,
                                                "bits": 2, "mem": 8, "kernels_ms": kern,
                                                "list_sizes": list_stats})
+    elif args.workload == "candidates":
+        n, nq, per_q, d = 1_000_000, 10_000, 256, 128
+        base = torch.from_numpy(rng.standard_normal((n, d), dtype=np.float32)).to(dev)
+        qs = torch.from_numpy(rng.standard_normal((nq, d), dtype=np.float32)).to(dev)
+        codec = uv.Codec(d, 2, 8)
+        index = uv.Index(codec)
+        index.add_batch(base)
+        pos = torch.from_numpy(rng.integers(0, n, nq * per_q).astype(np.int64)).to(dev)
+        off = torch.arange(nq + 1, dtype=torch.int64, device=dev) * per_q
+        prep_ms = _timed(lambda: index.prepare(qs).close(), 3)
+        prep = index.prepare(qs)
+        ms = _timed(lambda: prep.score(pos, off), 5)
+        uv.profile_enable(True)
+        prep.score(pos, off)
+        torch.cuda.synchronize()
+        kern_ms = uv.profile_read("score_candidates")[0]
+        uv.profile_enable(False)
+        # algorithmic bytes per candidate: 32 code bytes + start, rescale, rnorm
+        # (4 each) + position (8) + score (4)
+        per_cand = 32 + 4 + 4 + 4 + 8 + 4
+        ncand = nq * per_q
+        emit("candidates-1M-d128-10kx256", {
+            "candidates_s": ncand / ms * 1e3, "score_ms": ms, "kernel_ms": kern_ms,
+            "prepare_ms": prep_ms, "bytes_per_candidate": per_cand,
+            "achieved_gbs": ncand * per_cand / (kern_ms * 1e-3) / 1e9, "bits": 2, "mem": 8})
     else:
         d = 128
         rows = rng.standard_normal((1_000_000, d), dtype=np.float32)

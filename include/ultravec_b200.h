@@ -189,7 +189,9 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * back-pointers for codecs created afterwards (0 automatic, 1 global scratch,
  * 2 shared memory whenever one row's array fits); "tc_scan" selects the flat
  * search's tensor-core prefilter (0 automatic, 1 never, 2 wherever it is
- * built).  Process-wide; returns UV_EINVAL for an unknown key. */
+ * built); "cand_kernel" selects the candidate scorer's kernel (0 automatic:
+ * one thread per candidate at bits 1, 2, 4; 1 half a warp per candidate).
+ * Process-wide; returns UV_EINVAL for an unknown key. */
 int uv_set_tuning(const char *key, int64_t value);
 
 /* Measurement aid, no counterpart in the reference: while enabled, every
@@ -197,12 +199,41 @@ int uv_set_tuning(const char *key, int64_t value);
  * stream.  uv_profile_read waits for those events and returns the summed
  * device time and launch count of one kernel family ("encode",
  * "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
- * "tc_theta", "tc_pass2", "tc_rescore", the IVF families "ivf_*", or "*" for
+ * "tc_theta", "tc_pass2", "tc_rescore", "score_candidates", the IVF families
+ * "ivf_*", or "*" for
  * all).  "tc_candidates" returns, as the count, the number of candidates the
  * last tensor-core search scored exactly.  Enabling clears previous records.
  * Not for concurrent use. */
 int uv_profile_enable(int32_t on);
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches);
+
+/* ---- per-candidate scoring: CandidateScorer / PreparedQuery ----------- */
+
+/* A codes-only graph walk (src/hnsw.rs:346-404) scores scattered records
+ * through CandidateScorer::prepare(query) -> PreparedQuery::score_at(index)
+ * (src/lib.rs:83-102, impl src/trellis.rs:2003-2086).  The batched form
+ * prepares nq queries at once and scores CSR candidate lists: candidate i
+ * belongs to query q where offsets[q] <= i < offsets[q+1] and names the
+ * record at positions[i] (0 .. len-1, insertion order).  Each score is
+ * score_at's: qm + rnorm * (dot / rescale), 0.0 for a query with
+ * |q| < f32::EPSILON.  A position outside the index (the reference panics)
+ * returns UV_EINVAL, with NaN in that slot.  The prepared batch reads the
+ * index's arrays when it scores: keep the index alive while it exists. */
+typedef struct uv_prepared uv_prepared;
+int uv_index_prepare(const uv_index *index, const float *queries, int64_t nq,
+                     uv_prepared **out, void *stream);
+int uv_prepared_destroy(uv_prepared *prepared);
+int uv_prepared_len(const uv_prepared *prepared, int64_t *nq);
+/* offsets: nq + 1 entries from 0 to n, or NULL when one query was prepared. */
+int uv_prepared_score(const uv_prepared *prepared, const int64_t *offsets,
+                      const int64_t *positions, int64_t n, float *scores_out, void *stream);
+/* prepare + score for one query. */
+int uv_index_score_candidates(const uv_index *index, const float *query,
+                              const int64_t *positions, int64_t n, float *scores_out,
+                              void *stream);
+/* scored_len is uv_index_len.  scorer_model_bytes (src/trellis.rs:2084,
+ * 2200-2218): code table + rotation signs + centroids. */
+int uv_index_scorer_model_bytes(const uv_index *index, int64_t *bytes);
 
 /* ---- IVF: coarse quantizer, posting lists of trellis records ----------- */
 

@@ -80,7 +80,9 @@ def lib():
                                       C.c_float]),
             "uvo_search_topk": (None, [_vp, _u8p, _u32p, _f32p, _vp, _vp, _vp, C.c_int64,
                                        _f32p, C.c_int64, C.c_int, _i64p, _f32p, C.c_int]),
-            "uvo_exact_topk": (None, [_f32p, C.c_int64, C.c_int, _f32p, C.c_int64, C.c_int,
+            "uvo_score_candidates": (None, [_vp, _u8p, _u32p, _f32p, _vp, _vp, _f32p, C.c_int64,
+                                            _vp, _i64p, C.c_int64, _f32p, C.c_int]),
+            "uvo_exact_topk": (None,[_f32p, C.c_int64, C.c_int, _f32p, C.c_int64, C.c_int,
                                       C.c_int, _i64p, C.c_int]),
             "uvo_kmeans": (None, [_f32p, C.c_int64, C.c_int, C.c_int, C.c_uint64, C.c_int,
                                   _f32p, C.c_int]),
@@ -248,6 +250,25 @@ class Codec:
             _ptr(None if norms is None else np.ascontiguousarray(norms, np.float32)),
             n, queries, nq, k, ids, scores, threads)
         return ids, scores
+
+    def score_candidates(self, index, queries, positions, offsets=None, threads=0):
+        """trellis.rs:2016-2086: prepare each query, then score_at(positions[i])
+        for the candidates offsets[q] <= i < offsets[q+1] (all on query 0
+        without offsets)."""
+        queries = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+        positions = np.ascontiguousarray(positions, np.int64)
+        out = np.empty(positions.shape[0], np.float32)
+        rnorm = index.get("rnorm")
+        cidx = index.get("cidx")
+        off = None if offsets is None else np.ascontiguousarray(offsets, np.int64)
+        lib().uvo_score_candidates(
+            self.h, np.ascontiguousarray(index["codes"], np.uint8),
+            np.ascontiguousarray(index["start"], np.uint32),
+            np.ascontiguousarray(index["rescale"], np.float32),
+            _ptr(None if rnorm is None else np.ascontiguousarray(rnorm, np.float32)),
+            _ptr(None if cidx is None else np.ascontiguousarray(cidx, np.uint32)),
+            queries, queries.shape[0], _ptr(off), positions, positions.shape[0], out, threads)
+        return out
 
     def ivf_search_topk(self, centroids, list_off, ids, index, centered, queries, nprobe, k,
                         threads=0):

@@ -885,6 +885,46 @@ void uvo_search_topk(const uvo_codec *c, const uint8_t *codes, const uint32_t *s
     }
 }
 
+/* trellis.rs:2016-2086 CandidateScorer::prepare + PreparedQuery::score_at,
+ * batched: candidate i of the CSR batch (offsets[q] <= i < offsets[q+1];
+ * offsets NULL puts every candidate on query 0) is the record at
+ * positions[i].  A degenerate query scores 0.0 (trellis.rs:2031-2033); qm is
+ * qc[cidx] or 0.0 without centroids (trellis.rs:2035). */
+void uvo_score_candidates(const uvo_codec *c, const uint8_t *codes, const uint32_t *start,
+                          const float *rescale, const float *rnorm, const uint32_t *cidx,
+                          const float *queries, int64_t nq, const int64_t *offsets,
+                          const int64_t *positions, int64_t n, float *out, int threads) {
+    int d = c->dim, cb = uvo_codec_code_bytes(c);
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+        float *q_r = (float *)malloc(sizeof(float) * d);
+        float *qc = (float *)malloc(sizeof(float) * (c->n_centroids + 1));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t qi = 0; qi < nq; qi++) {
+            int64_t i0 = offsets ? offsets[qi] : 0, i1 = offsets ? offsets[qi + 1] : n;
+            int degenerate = uvo_prepare_query(c, queries + (size_t)qi * d, q_r, qc);
+            for (int64_t i = i0; i < i1; i++) {
+                int64_t r = positions[i];
+                if (degenerate) {
+                    out[i] = 0.0f;
+                    continue;
+                }
+                float qm = 0.0f;
+                if (c->n_centroids > 0) qm = qc[cidx ? cidx[r] : 0];
+                out[i] = uvo_score(c, q_r, qm, codes + (size_t)r * cb, start[r], rescale[r],
+                                   rnorm ? rnorm[r] : 1.0f);
+            }
+        }
+        free(q_r);
+        free(qc);
+    }
+}
+
 /* bench.rs:989-1001 (raw IP) and bench.rs:126-146 (cosine), ties by id */
 void uvo_exact_topk(const float *db, int64_t n, int dim, const float *queries, int64_t nq,
                     int k, int cosine, int64_t *ids_out, int threads) {

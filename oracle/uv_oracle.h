@@ -81,6 +81,11 @@ void uvo_search_topk(const uvo_codec *c, const uint8_t *codes, const uint32_t *s
                      const float *rescale, const float *rnorm, const uint32_t *cidx,
                      const float *norms, int64_t n, const float *queries, int64_t nq, int k,
                      int64_t *ids_out, float *scores_out, int threads);
+/* batched CandidateScorer::prepare + score_at (trellis.rs:2016-2086) */
+void uvo_score_candidates(const uvo_codec *c, const uint8_t *codes, const uint32_t *start,
+                          const float *rescale, const float *rnorm, const uint32_t *cidx,
+                          const float *queries, int64_t nq, const int64_t *offsets,
+                          const int64_t *positions, int64_t n, float *out, int threads);
 
 /* exact ground truth, raw inner product (bench.rs:989-1001) or cosine
  * (bench.rs:126-146), ties by id */

@@ -315,3 +315,30 @@ def test_digest_is_order_independent(oracle):
     perm = np.random.default_rng(0).permutation(50)
     d2 = oracle.digest(idx["codes"][perm], idx["start"][perm])
     assert d1 == d2 and d1 != 0
+
+
+def test_candidate_scorer_agrees_with_search(oracle):
+    """trellis.rs:2016-2086: prepare + score_at over every record gives the
+    scores search ranks (the same estimator), 0.0 for a zero query, and the
+    centered qm term per record."""
+    dim = 64
+    db = oracle.rand_unit(300, dim, 41)
+    qs = oracle.rand_unit(6, dim, 43)
+    qs[3] = 0.0
+    for cen in (None, oracle.kmeans(db, 4, 42)):
+        c = oracle.Codec(dim, 2, 8, centroids=cen)
+        idx = c.encode_batch(db)
+        pos = np.tile(np.arange(300, dtype=np.int64), len(qs))
+        off = np.arange(len(qs) + 1, dtype=np.int64) * 300
+        s = c.score_candidates(idx, qs, pos, off).reshape(len(qs), 300)
+        ids, top = c.search_topk(idx, qs, 10)
+        for q in range(len(qs)):
+            if q == 3:
+                assert np.all(s[q] == 0.0) and np.all(ids[q] == -1)
+                continue
+            order = sorted(range(300), key=lambda i: (-s[q, i], i))[:10]
+            assert list(ids[q]) == order
+            assert np.array_equal(s[q, ids[q]].view(np.uint32), top[q].view(np.uint32))
+        # one query without offsets: the same numbers
+        one = c.score_candidates(idx, qs[0], np.arange(300))
+        assert np.array_equal(one.view(np.uint32), s[0].view(np.uint32))

@@ -34,7 +34,8 @@ SYMBOLS = [
     "uv_kmeans", "uv_ivf_assign", "uv_ivf_create", "uv_ivf_destroy", "uv_ivf_build",
     "uv_ivf_len", "uv_ivf_nlist", "uv_ivf_mem_bytes", "uv_ivf_probe", "uv_ivf_search",
     "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest", "uv_index_save", "uv_index_load",
-    "uv_ivf_save", "uv_ivf_load",
+    "uv_ivf_save", "uv_ivf_load", "uv_index_prepare", "uv_prepared_destroy", "uv_prepared_len",
+    "uv_prepared_score", "uv_index_score_candidates", "uv_index_scorer_model_bytes",
 ]
 
 
@@ -116,6 +117,12 @@ def lib():
             "uv_index_load": (C.c_int, [vp, C.c_char_p, vpp]),
             "uv_ivf_save": (C.c_int, [vp, C.c_char_p]),
             "uv_ivf_load": (C.c_int, [vp, C.c_char_p, vpp]),
+            "uv_index_prepare": (C.c_int, [vp, vp, i64, vpp, vp]),
+            "uv_prepared_destroy": (C.c_int, [vp]),
+            "uv_prepared_len": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_prepared_score": (C.c_int, [vp, vp, vp, i64, vp, vp]),
+            "uv_index_score_candidates": (C.c_int, [vp, vp, vp, i64, vp, vp]),
+            "uv_index_scorer_model_bytes": (C.c_int, [vp, C.POINTER(i64)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -173,6 +180,14 @@ class _Alloc:
         tmap = {np.uint8: torch.uint8, np.uint32: torch.int32, np.float32: torch.float32,
                 np.int64: torch.int64, np.int32: torch.int32}
         return torch.zeros(shape, dtype=tmap[np_dtype], device=self.torch_dev)
+
+
+def _i64(x):
+    if _is_torch(x):
+        import torch
+
+        return x.to(torch.int64).contiguous()
+    return np.ascontiguousarray(x, dtype=np.int64)
 
 
 def _f32(x):
@@ -348,6 +363,29 @@ class Index:
                                     _ptr(scores), _stream(queries)))
         return ids, scores
 
+    # -- CandidateScorer (src/lib.rs:93-102, src/trellis.rs:2039-2086) --
+    def prepare(self, queries) -> "PreparedQueries":
+        """CandidateScorer::prepare for a batch of queries (one row each)."""
+        return PreparedQueries(self, queries)
+
+    def score_candidates(self, query, positions):
+        """prepare(query) then score_at(p) for every p in positions."""
+        query = _f32(query).reshape(-1)
+        positions = _i64(positions)
+        out = _Alloc(positions)(positions.shape[0], np.float32)
+        check(lib().uv_index_score_candidates(self.h, _ptr(query), _ptr(positions),
+                                              positions.shape[0], _ptr(out),
+                                              _stream(positions, query)))
+        return out
+
+    def scored_len(self) -> int:
+        return len(self)
+
+    def scorer_model_bytes(self) -> int:
+        b = C.c_int64()
+        check(lib().uv_index_scorer_model_bytes(self.h, C.byref(b)))
+        return b.value
+
     def export(self):
         n = len(self)
         cb = self.codec.code_bytes
@@ -376,6 +414,54 @@ class Index:
         ix = cls.__new__(cls)
         ix.h, ix.codec = h, codec
         return ix
+
+
+class PreparedQueries:
+    """A batch of PreparedQuery (src/trellis.rs:2003-2037) on the index's GPU:
+    score(positions, offsets) is score_at over CSR candidate lists."""
+
+    def __init__(self, index: Index, queries):
+        queries = _f32(queries)
+        if queries.ndim == 1:
+            queries = queries.reshape(1, -1)
+        h = C.c_void_p()
+        check(lib().uv_index_prepare(index.h, _ptr(queries), queries.shape[0], C.byref(h),
+                                     _stream(queries)))
+        self.h, self.index, self.nq = h, index, queries.shape[0]
+
+    def close(self):
+        if getattr(self, "h", None):
+            check(lib().uv_prepared_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_prepared_len(self.h, C.byref(n)))
+        return n.value
+
+    def score(self, positions, offsets=None):
+        """Scores of positions[i] against query q for offsets[q] <= i < offsets[q+1]
+        (all against the single query when offsets is None)."""
+        positions = _i64(positions)
+        off = None if offsets is None else _i64(offsets)
+        out = _Alloc(positions)(positions.shape[0], np.float32)
+        check(lib().uv_prepared_score(self.h, _ptr(off), _ptr(positions), positions.shape[0],
+                                      _ptr(out), _stream(positions, off)))
+        return out
+
+    def score_at(self, position: int, query: int = 0) -> float:
+        """One score_at call (a single-candidate batch)."""
+        off = None
+        if self.nq > 1:
+            off = np.zeros(self.nq + 1, np.int64)
+            off[query + 1:] = 1
+        return float(self.score(np.array([position], np.int64), off)[0])
 
 
 # ------------------------------------------------------------------- IVF ---

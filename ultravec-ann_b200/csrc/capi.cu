@@ -17,6 +17,7 @@ thread_local std::string g_err;
 std::mutex g_prof_mu;
 int64_t g_scan_splits = 0;
 int g_tc_mode = 0;
+int g_cand_kernel = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
@@ -1074,6 +1075,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_scan") == 0) {
     if (value < 0 || value > 2) return fail(UV_EINVAL, "tc_scan must be 0, 1 or 2");
     g_tc_mode = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "cand_kernel") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "cand_kernel must be 0 or 1");
+    g_cand_kernel = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "scan_splits") == 0) {

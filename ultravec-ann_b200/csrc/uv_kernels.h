@@ -138,6 +138,23 @@ struct RerankParams {
   float *out_score;
 };
 
+// Batched per-candidate scoring (candidates.cu).
+struct CandParams {
+  int dim, mem, bits, code_stride, q_stride, n_centroids, table_len, table_in_smem;
+  int table_rep;               // lane kernel: copies of the table in shared memory (0: global)
+  int64_t nq, n, n_records;
+  const int64_t *offsets;      // nq + 1 (CSR over candidates), or null: all on query 0
+  const int64_t *positions;    // n record positions
+  const float *q_r;            // nq x q_stride rotated unit queries
+  const float *qc;             // nq x n_centroids
+  const uint32_t *degenerate;  // nq
+  const uint8_t *codes;
+  const uint32_t *start, *cidx;
+  const float *code, *rescale, *rnorm;
+  float *out;
+  int *n_bad;                  // candidates with a position outside the index
+};
+
 // Tensor-core prefilter of the flat scan (tcscan.cu).
 struct TcScanParams {
   int q_stride, cand_cap;
@@ -250,6 +267,8 @@ __global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, 
                                const int32_t *pair_query, const int32_t *pair_slot, int np,
                                const int32_t *lists, int npairs, float *qm);
 __global__ void rerank_kernel(const RerankParams p);
+__global__ void score_candidates_kernel(const CandParams p);
+const void *score_candidates_lane_kernel_ptr(int bits);  // bits 1, 2, 4; else null
 
 // scan tiling constants shared with the host planner
 constexpr int kScanTQ = 32;
