@@ -199,13 +199,33 @@ int uv_set_tuning(const char *key, int64_t value);
  * stream.  uv_profile_read waits for those events and returns the summed
  * device time and launch count of one kernel family ("encode",
  * "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
- * "tc_theta", "tc_pass2", "tc_rescore", "score_candidates", the IVF families
+ * "tc_theta", "tc_pass2", "tc_rescore", "score_candidates", "shortlist", the IVF families
  * "ivf_*", or "*" for
  * all).  "tc_candidates" returns, as the count, the number of candidates the
  * last tensor-core search scored exactly.  Enabling clears previous records.
  * Not for concurrent use. */
 int uv_profile_enable(int32_t on);
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches);
+
+/* ---- the 1-bit companion shortlist ------------------------------------- */
+
+/* with_shortlist(c) + with_shortlist_asym(asym) + with_shortlist_rnorm(rnorm)
+ * (src/trellis.rs:803-839): records added afterwards also store the 1-bit
+ * sign code of u_r (pack_indices(u_r > 0, 1), ceil(dim/8) bytes,
+ * src/trellis.rs:1084-1094), and a cosine search becomes search_shortlist
+ * (src/trellis.rs:854-948): stage 1 keeps the C = max(c, k) entries with the
+ * best sign-code similarity -- dim - 2 * Hamming distance of the query's
+ * sign code (asym 0) or the sequential sum of +-q_r[i] (asym 1), times rnorm
+ * when rnorm is 1 and the index is centered -- and stage 2 scores those
+ * with the codec's estimator.  Entries of equal stage-1 similarity are taken
+ * lowest position first (the reference's select_nth_unstable leaves the
+ * choice unspecified).  c = 0 switches it off.  Switching on or off needs an
+ * empty index.  C is built up to 4096; MIPS searches ask for every record in
+ * the reference (src/bench.rs:1029-1045), which no shortlist prunes, and use
+ * the plain scan. */
+int uv_index_set_shortlist(uv_index *index, int32_t c, int32_t asym, int32_t rnorm);
+/* The sign codes, n x ceil(dim/8) (UV_EINVAL when the shortlist is off). */
+int uv_index_export_signs(const uv_index *index, uint8_t *signs, void *stream);
 
 /* ---- per-candidate scoring: CandidateScorer / PreparedQuery ----------- */
 
@@ -302,6 +322,13 @@ int uv_ivf_search_rerank(const uv_ivf *ivf, const float *queries, int64_t nq, in
  * rescale, rnorm.  NULL skips a field; host or device. */
 int uv_ivf_export(const uv_ivf *ivf, int64_t *list_off, int64_t *ids, uint8_t *codes,
                   uint32_t *start, float *rescale, float *rnorm, void *stream);
+
+/* IvfCodec::TrellisShortlist{c, asym, rnorm} (src/ivf.rs:52-60, 111-135):
+ * every probed list runs search_shortlist(query, k, c) on its own entries
+ * (see uv_index_set_shortlist; the rnorm weight applies to centered lists).
+ * Set before uv_ivf_build; also used by uv_ivf_search_rerank's codec stage. */
+int uv_ivf_set_shortlist(uv_ivf *ivf, int32_t c, int32_t asym, int32_t rnorm);
+int uv_ivf_export_signs(const uv_ivf *ivf, uint8_t *signs, void *stream);
 
 /* XOR-folded per-record FNV-1a digest of every posting (as uv_digest). */
 int uv_ivf_digest(const uv_ivf *ivf, uint64_t *digest, void *stream);

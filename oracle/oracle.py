@@ -80,6 +80,17 @@ def lib():
                                       C.c_float]),
             "uvo_search_topk": (None, [_vp, _u8p, _u32p, _f32p, _vp, _vp, _vp, C.c_int64,
                                        _f32p, C.c_int64, C.c_int, _i64p, _f32p, C.c_int]),
+            "uvo_encode_batch_signs": (None, [_vp, _f32p, C.c_int64, _u8p, _u32p, _f32p, _f32p,
+                                              _u32p, _u8p, C.c_int]),
+            "uvo_ivf_encode_signs": (None, [_vp, _f32p, C.c_int64, _vp, _u32p, _u8p, _u32p,
+                                            _f32p, _f32p, _u8p, C.c_int]),
+            "uvo_search_shortlist": (None, [_vp, _u8p, _u32p, _f32p, _vp, _vp, _u8p, C.c_int64,
+                                            _f32p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int,
+                                            _i64p, _f32p, C.c_int]),
+            "uvo_ivf_search_shortlist": (None, [_vp, _f32p, C.c_int, _i64p, _i64p, _u8p, _u32p,
+                                                _f32p, _f32p, _u8p, C.c_int, _f32p, C.c_int64,
+                                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                _i64p, _f32p, C.c_int]),
             "uvo_score_candidates": (None, [_vp, _u8p, _u32p, _f32p, _vp, _vp, _f32p, C.c_int64,
                                             _vp, _i64p, C.c_int64, _f32p, C.c_int]),
             "uvo_exact_topk": (None,[_f32p, C.c_int64, C.c_int, _f32p, C.c_int64, C.c_int,
@@ -193,6 +204,67 @@ class Codec:
         cidx = np.zeros(n, np.uint32)
         lib().uvo_encode_batch(self.h, rows, n, codes, start, rescale, rnorm, cidx, threads)
         return dict(codes=codes, start=start, rescale=rescale, rnorm=rnorm, cidx=cidx)
+
+    def encode_batch_signs(self, rows, threads=0):
+        """encode_batch plus the shortlist sign codes (trellis.rs:1084-1094)."""
+        rows = np.ascontiguousarray(rows, np.float32)
+        n = rows.shape[0]
+        out = dict(codes=np.zeros((n, self.code_bytes), np.uint8), start=np.zeros(n, np.uint32),
+                   rescale=np.zeros(n, np.float32), rnorm=np.zeros(n, np.float32),
+                   cidx=np.zeros(n, np.uint32),
+                   signs=np.zeros((n, (self.dim + 7) // 8), np.uint8))
+        lib().uvo_encode_batch_signs(self.h, rows, n, out["codes"], out["start"], out["rescale"],
+                                     out["rnorm"], out["cidx"], out["signs"], threads)
+        return out
+
+    def ivf_encode_signs(self, rows, centroids, assign, threads=0):
+        rows = np.ascontiguousarray(rows, np.float32)
+        n = rows.shape[0]
+        cen = None if centroids is None else np.ascontiguousarray(centroids, np.float32)
+        out = dict(codes=np.zeros((n, self.code_bytes), np.uint8), start=np.zeros(n, np.uint32),
+                   rescale=np.zeros(n, np.float32), rnorm=np.zeros(n, np.float32),
+                   signs=np.zeros((n, (self.dim + 7) // 8), np.uint8))
+        lib().uvo_ivf_encode_signs(self.h, rows, n, _ptr(cen),
+                                   np.ascontiguousarray(assign, np.uint32), out["codes"],
+                                   out["start"], out["rescale"], out["rnorm"], out["signs"],
+                                   threads)
+        return out
+
+    def search_shortlist(self, index, queries, k, c, asym=False, weight=True, threads=0):
+        """trellis.rs:854-948 for a flat index encoded with signs."""
+        queries = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+        nq = queries.shape[0]
+        ids = np.empty((nq, k), np.int64)
+        scores = np.empty((nq, k), np.float32)
+        rnorm = index.get("rnorm")
+        cidx = index.get("cidx")
+        lib().uvo_search_shortlist(
+            self.h, np.ascontiguousarray(index["codes"], np.uint8),
+            np.ascontiguousarray(index["start"], np.uint32),
+            np.ascontiguousarray(index["rescale"], np.float32),
+            _ptr(None if rnorm is None else np.ascontiguousarray(rnorm, np.float32)),
+            _ptr(None if cidx is None else np.ascontiguousarray(cidx, np.uint32)),
+            np.ascontiguousarray(index["signs"], np.uint8), index["start"].shape[0], queries, nq,
+            k, c, int(asym), int(weight), ids, scores, threads)
+        return ids, scores
+
+    def ivf_search_shortlist(self, centroids, list_off, ids, index, centered, queries, nprobe,
+                             k, c, asym=False, weight=True, threads=0):
+        """ivf.rs:229-239 with TrellisShortlist{c, asym, rnorm=weight} lists."""
+        queries = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+        nq = queries.shape[0]
+        out_ids = np.empty((nq, k), np.int64)
+        scores = np.empty((nq, k), np.float32)
+        cen = np.ascontiguousarray(centroids, np.float32)
+        lib().uvo_ivf_search_shortlist(
+            self.h, cen, cen.shape[0], np.ascontiguousarray(list_off, np.int64),
+            np.ascontiguousarray(ids, np.int64), np.ascontiguousarray(index["codes"], np.uint8),
+            np.ascontiguousarray(index["start"], np.uint32),
+            np.ascontiguousarray(index["rescale"], np.float32),
+            np.ascontiguousarray(index["rnorm"], np.float32),
+            np.ascontiguousarray(index["signs"], np.uint8), int(centered), queries, nq, nprobe,
+            k, c, int(asym), int(weight), out_ids, scores, threads)
+        return out_ids, scores
 
     def ivf_encode(self, rows, centroids, assign, threads=0):
         rows = np.ascontiguousarray(rows, np.float32)

@@ -562,12 +562,26 @@ static uint32_t run_viterbi(const uvo_codec *c, const float *u_rs, scratch_t *s)
     return viterbi_general(c, u_rs, s->em, 1);
 }
 
+/* trellis.rs:1084-1094: the 1-bit sign code of u_r, pack_indices(u_r > 0, 1)
+ * (MSB-first, ceil(dim/8) bytes) */
+static void sign_code(const float *u_r, int d, uint8_t *out) {
+    for (int b = 0; b < (d + 7) / 8; b++) {
+        uint8_t v = 0;
+        for (int t = 0; t < 8; t++) {
+            int i = 8 * b + t;
+            if (i < d && u_r[i] > 0.0f) v |= (uint8_t)(0x80u >> t);
+        }
+        out[b] = v;
+    }
+}
+
 static void encode_with(const uvo_codec *c, const float *row, const float *list_centroid,
                         uint8_t *codes, uint32_t *start, float *rescale, float *rnorm,
-                        uint32_t *cidx, scratch_t *s) {
+                        uint32_t *cidx, uint8_t *sign, scratch_t *s) {
     int d = c->dim;
     prep_ex(c, row, list_centroid, s->r, rnorm, cidx);
     uvo_rotate(c, s->r, s->u_r);
+    if (sign) sign_code(s->u_r, d, sign);
     float scale = fmaxf(uvo_std_about_mean(s->u_r, d), F32_EPS);
     for (int i = 0; i < d; i++) s->u_rs[i] = s->u_r[i] / scale;
     uint32_t st = run_viterbi(c, s->u_rs, s);
@@ -579,7 +593,7 @@ int uvo_encode(const uvo_codec *c, const float *row, uint8_t *codes, uint32_t *s
                float *rescale, float *rnorm, uint32_t *cidx) {
     scratch_t s;
     scratch_init(c, &s);
-    encode_with(c, row, NULL, codes, start, rescale, rnorm, cidx, &s);
+    encode_with(c, row, NULL, codes, start, rescale, rnorm, cidx, NULL, &s);
     scratch_free(&s);
     return 0;
 }
@@ -621,8 +635,8 @@ int uvo_encode_scalar_ref(const uvo_codec *c, const float *row, uint8_t *codes,
 static void encode_rows(const uvo_codec *c, const float *rows, int64_t n,
                         const float *centroids, const uint32_t *assign, uint8_t *codes,
                         uint32_t *start, float *rescale, float *rnorm, uint32_t *cidx,
-                        int threads) {
-    int cb = uvo_codec_code_bytes(c);
+                        uint8_t *signs, int threads) {
+    int cb = uvo_codec_code_bytes(c), sb = (c->dim + 7) / 8;
 #ifdef _OPENMP
     if (threads <= 0) threads = omp_get_max_threads();
 #pragma omp parallel num_threads(threads)
@@ -638,7 +652,7 @@ static void encode_rows(const uvo_codec *c, const float *rows, int64_t n,
             uint32_t ci;
             const float *lc = centroids ? centroids + (size_t)assign[i] * c->dim : NULL;
             encode_with(c, rows + (size_t)i * c->dim, lc, codes + (size_t)i * cb, start + i, &rs,
-                        &rn, &ci, &s);
+                        &rn, &ci, signs ? signs + (size_t)i * sb : NULL, &s);
             rescale[i] = rs;
             if (rnorm) rnorm[i] = rn;
             if (cidx) cidx[i] = ci;
@@ -650,7 +664,14 @@ static void encode_rows(const uvo_codec *c, const float *rows, int64_t n,
 void uvo_encode_batch(const uvo_codec *c, const float *rows, int64_t n, uint8_t *codes,
                       uint32_t *start, float *rescale, float *rnorm, uint32_t *cidx,
                       int threads) {
-    encode_rows(c, rows, n, NULL, NULL, codes, start, rescale, rnorm, cidx, threads);
+    encode_rows(c, rows, n, NULL, NULL, codes, start, rescale, rnorm, cidx, NULL, threads);
+}
+
+/* encode_batch with the shortlist's sign codes (n x ceil(dim/8)) */
+void uvo_encode_batch_signs(const uvo_codec *c, const float *rows, int64_t n, uint8_t *codes,
+                            uint32_t *start, float *rescale, float *rnorm, uint32_t *cidx,
+                            uint8_t *signs, int threads) {
+    encode_rows(c, rows, n, NULL, NULL, codes, start, rescale, rnorm, cidx, signs, threads);
 }
 
 /* ivf.rs:171-205 + 98-150 (ULTRAVEC_IVF_CENTER=1): row i is encoded by its
@@ -659,7 +680,14 @@ void uvo_encode_batch(const uvo_codec *c, const float *rows, int64_t n, uint8_t 
 void uvo_ivf_encode(const uvo_codec *c, const float *rows, int64_t n, const float *centroids,
                     const uint32_t *assign, uint8_t *codes, uint32_t *start, float *rescale,
                     float *rnorm, int threads) {
-    encode_rows(c, rows, n, centroids, assign, codes, start, rescale, rnorm, NULL, threads);
+    encode_rows(c, rows, n, centroids, assign, codes, start, rescale, rnorm, NULL, NULL, threads);
+}
+
+void uvo_ivf_encode_signs(const uvo_codec *c, const float *rows, int64_t n,
+                          const float *centroids, const uint32_t *assign, uint8_t *codes,
+                          uint32_t *start, float *rescale, float *rnorm, uint8_t *signs,
+                          int threads) {
+    encode_rows(c, rows, n, centroids, assign, codes, start, rescale, rnorm, NULL, signs, threads);
 }
 
 /* trellis.rs:970-990  FNV-1a over start (LE) then codes, XOR-folded */
@@ -1187,6 +1215,168 @@ void uvo_ivf_search_rerank(const uvo_codec *c, const float *centroids, int nlist
         free(h);
     }
     free(cand);
+}
+
+/* ---------------------------------------------------------------------- */
+/* The 1-bit companion shortlist (trellis.rs:854-948, ivf.rs:52-60)        */
+/* ---------------------------------------------------------------------- */
+
+/* Stage-1 similarity of one entry (trellis.rs:887-899): the symmetric
+ * dim - 2 * hamming(q_bits, sign) (2251-2266) or the asymmetric masked_sum
+ * (2271-2279, a sequential fold of +-q_r[i]), times rnorm when weighted. */
+static float shortlist_sim(int d, const float *q_r, const uint8_t *q_bits, const uint8_t *sign,
+                           int asym, int weighted, float rnorm) {
+    float sim;
+    if (asym) {
+        float s = 0.0f;
+        for (int i = 0; i < d; i++) {
+            int bit = (sign[i >> 3] >> (7 - (i & 7))) & 1;
+            s += bit ? q_r[i] : -q_r[i];
+        }
+        sim = s;
+    } else {
+        uint32_t h = 0;
+        for (int b = 0; b < (d + 7) / 8; b++) h += (uint32_t)__builtin_popcount(q_bits[b] ^ sign[b]);
+        sim = (float)d - 2.0f * (float)h;
+    }
+    return weighted ? rnorm * sim : sim;
+}
+
+/* search_shortlist over the n entries [0, n) of one codec (a flat index or
+ * one posting list): the c = min(max(c, limit), n) best by stage-1
+ * similarity (ties: lower entry first -- select_nth_unstable leaves them
+ * unspecified), then the estimator of score() on those, pushed into the
+ * caller's top-limit heap under id ids[i] (or i).  qm is qc_all[cidx[i]]
+ * (qc_all NULL: 0). */
+static void shortlist_scan(const uvo_codec *c, int64_t n, const uint8_t *codes,
+                           const uint32_t *start, const float *rescale, const float *rnorm,
+                           const uint32_t *cidx, const uint8_t *signs, const int64_t *ids,
+                           const float *q_r, const uint8_t *q_bits, const float *qc_all,
+                           int limit, int cs, int asym, int weighted, cand_t *sel, cand_t *h,
+                           int *nh) {
+    int d = c->dim, cb = uvo_codec_code_bytes(c), sb = (d + 7) / 8;
+    if (n <= 0) return;
+    int64_t ce = cs > limit ? cs : limit;
+    if (ce > n) ce = n;
+    int ns = 0;
+    for (int64_t i = 0; i < n; i++) {
+        float rn = rnorm ? rnorm[i] : 1.0f;
+        float sim = shortlist_sim(d, q_r, q_bits, signs + (size_t)i * sb, asym, weighted, rn);
+        heap_push_bounded(sel, &ns, (int)ce, sim, i);
+    }
+    for (int t = 0; t < ns; t++) {
+        int64_t i = sel[t].id;
+        float qm = qc_all ? qc_all[cidx ? cidx[i] : 0] : 0.0f;
+        float s = uvo_score(c, q_r, qm, codes + (size_t)i * cb, start[i], rescale[i],
+                            rnorm ? rnorm[i] : 1.0f);
+        heap_push_bounded(h, nh, limit, s, ids ? ids[i] : i);
+    }
+}
+
+static void query_bits(const float *q_r, int d, uint8_t *out) { sign_code(q_r, d, out); }
+
+/* trellis.rs:2120-2122 -> 854-948: a flat index whose codec has the shortlist
+ * on (with_shortlist(c), with_shortlist_asym, with_shortlist_rnorm).  The
+ * stage-1 weight applies when `weight` and the codec has centroids. */
+void uvo_search_shortlist(const uvo_codec *c, const uint8_t *codes, const uint32_t *start,
+                          const float *rescale, const float *rnorm, const uint32_t *cidx,
+                          const uint8_t *signs, int64_t n, const float *queries, int64_t nq,
+                          int k, int cs, int asym, int weight, int64_t *ids_out,
+                          float *scores_out, int threads) {
+    int d = c->dim;
+    int64_t ce = cs > k ? cs : k;
+    if (ce > n) ce = n;
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+        float *q_r = (float *)malloc(sizeof(float) * d);
+        float *qc = (float *)malloc(sizeof(float) * (c->n_centroids + 1));
+        uint8_t *qb = (uint8_t *)malloc((size_t)(d + 7) / 8);
+        cand_t *sel = (cand_t *)malloc(sizeof(cand_t) * (size_t)(ce > 0 ? ce : 1));
+        cand_t *h = (cand_t *)malloc(sizeof(cand_t) * (k > 0 ? k : 1));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t qi = 0; qi < nq; qi++) {
+            int nh = 0;
+            if (!uvo_prepare_query(c, queries + (size_t)qi * d, q_r, qc)) {
+                query_bits(q_r, d, qb);
+                shortlist_scan(c, n, codes, start, rescale, rnorm, cidx, signs, NULL, q_r, qb,
+                               c->n_centroids > 0 ? qc : NULL, k, cs, asym,
+                               weight && c->n_centroids > 0, sel, h, &nh);
+            }
+            emit_topk(h, nh, k, ids_out + (size_t)qi * k, scores_out ? scores_out + (size_t)qi * k : NULL);
+        }
+        free(q_r);
+        free(qc);
+        free(qb);
+        free(sel);
+        free(h);
+    }
+}
+
+/* ivf.rs:229-239 with IvfCodec::TrellisShortlist{c, asym, rnorm}: each probed
+ * list runs search_shortlist(query, k, c) over its own entries (stage-1
+ * weight only for centered lists), the per-list results merge to top-k. */
+void uvo_ivf_search_shortlist(const uvo_codec *c, const float *centroids, int nlist,
+                              const int64_t *list_off, const int64_t *ids, const uint8_t *codes,
+                              const uint32_t *start, const float *rescale, const float *rnorm,
+                              const uint8_t *signs, int centered, const float *queries,
+                              int64_t nq, int nprobe, int k, int cs, int asym, int weight,
+                              int64_t *ids_out, float *scores_out, int threads) {
+    int d = c->dim, cb = uvo_codec_code_bytes(c), sb = (d + 7) / 8;
+    if (nprobe > nlist) nprobe = nlist;
+    int64_t maxlen = 0;
+    for (int j = 0; j < nlist; j++)
+        if (list_off[j + 1] - list_off[j] > maxlen) maxlen = list_off[j + 1] - list_off[j];
+    int64_t ce = cs > k ? cs : k;
+    if (ce > maxlen) ce = maxlen;
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+        float *u = (float *)malloc(sizeof(float) * d);
+        float *q_r = (float *)malloc(sizeof(float) * d);
+        uint8_t *qb = (uint8_t *)malloc((size_t)sb);
+        int32_t *lists = (int32_t *)malloc(sizeof(int32_t) * (nprobe > 0 ? nprobe : 1));
+        cand_t *sel = (cand_t *)malloc(sizeof(cand_t) * (size_t)(ce > 0 ? ce : 1));
+        cand_t *h = (cand_t *)malloc(sizeof(cand_t) * (k > 0 ? k : 1));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t qi = 0; qi < nq; qi++) {
+            const float *q = queries + (size_t)qi * d;
+            int nh = 0;
+            float qn = uvo_l2_norm(q, d);
+            if (qn >= F32_EPS && nprobe > 0) {
+                uvo_ivf_probe(centroids, nlist, d, q, nprobe, lists);
+                for (int i = 0; i < d; i++) u[i] = q[i] / qn;
+                uvo_rotate(c, u, q_r);
+                query_bits(q_r, d, qb);
+                for (int p = 0; p < nprobe; p++) {
+                    int j = lists[p];
+                    if (j < 0) continue;
+                    int64_t o = list_off[j];
+                    float qm = centered ? seq_dot(u, centroids + (size_t)j * d, d) : 0.0f;
+                    shortlist_scan(c, list_off[j + 1] - o, codes + (size_t)o * cb, start + o,
+                                   rescale + o, rnorm ? rnorm + o : NULL, NULL,
+                                   signs + (size_t)o * sb, ids + o, q_r, qb,
+                                   centered ? &qm : NULL, k, cs, asym, weight && centered, sel, h,
+                                   &nh);
+                }
+            }
+            emit_topk(h, nh, k, ids_out + (size_t)qi * k, scores_out ? scores_out + (size_t)qi * k : NULL);
+        }
+        free(u);
+        free(q_r);
+        free(qb);
+        free(lists);
+        free(sel);
+        free(h);
+    }
 }
 
 /* bench.rs:1019 norms[i] = l2_norm(db[i]) over a batch */

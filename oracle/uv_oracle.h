@@ -81,6 +81,27 @@ void uvo_search_topk(const uvo_codec *c, const uint8_t *codes, const uint32_t *s
                      const float *rescale, const float *rnorm, const uint32_t *cidx,
                      const float *norms, int64_t n, const float *queries, int64_t nq, int k,
                      int64_t *ids_out, float *scores_out, int threads);
+/* encode_batch / ivf_encode plus the shortlist's 1-bit sign codes
+ * (trellis.rs:1084-1094), n x ceil(dim/8) */
+void uvo_encode_batch_signs(const uvo_codec *c, const float *rows, int64_t n, uint8_t *codes,
+                            uint32_t *start, float *rescale, float *rnorm, uint32_t *cidx,
+                            uint8_t *signs, int threads);
+void uvo_ivf_encode_signs(const uvo_codec *c, const float *rows, int64_t n,
+                          const float *centroids, const uint32_t *assign, uint8_t *codes,
+                          uint32_t *start, float *rescale, float *rnorm, uint8_t *signs,
+                          int threads);
+/* search_shortlist (trellis.rs:854-948): flat and per IVF list */
+void uvo_search_shortlist(const uvo_codec *c, const uint8_t *codes, const uint32_t *start,
+                          const float *rescale, const float *rnorm, const uint32_t *cidx,
+                          const uint8_t *signs, int64_t n, const float *queries, int64_t nq,
+                          int k, int cs, int asym, int weight, int64_t *ids_out,
+                          float *scores_out, int threads);
+void uvo_ivf_search_shortlist(const uvo_codec *c, const float *centroids, int nlist,
+                              const int64_t *list_off, const int64_t *ids, const uint8_t *codes,
+                              const uint32_t *start, const float *rescale, const float *rnorm,
+                              const uint8_t *signs, int centered, const float *queries,
+                              int64_t nq, int nprobe, int k, int cs, int asym, int weight,
+                              int64_t *ids_out, float *scores_out, int threads);
 /* batched CandidateScorer::prepare + score_at (trellis.rs:2016-2086) */
 void uvo_score_candidates(const uvo_codec *c, const uint8_t *codes, const uint32_t *start,
                           const float *rescale, const float *rnorm, const uint32_t *cidx,

@@ -342,3 +342,136 @@ def test_candidate_scorer_agrees_with_search(oracle):
         # one query without offsets: the same numbers
         one = c.score_candidates(idx, qs[0], np.arange(300))
         assert np.array_equal(one.view(np.uint32), s[0].view(np.uint32))
+
+
+def _unit(rows):
+    n = np.linalg.norm(rows.astype(np.float64), axis=1, keepdims=True)
+    return (rows / np.maximum(n, 1e-30)).astype(np.float32)
+
+
+def test_sign_code_is_the_packed_sign_of_u_r(oracle):
+    """trellis.rs:1084-1094: sign_code = pack_indices(u_r > 0, 1), dim/8 bytes."""
+    dim = 128
+    rows = oracle.rand_unit(40, dim, 7)
+    c = oracle.Codec(dim, 2, 8)
+    enc = c.encode_batch_signs(rows)
+    plain = c.encode_batch(rows)
+    assert np.array_equal(enc["codes"], plain["codes"])  # the field is inert for the codes
+    for i in range(40):
+        u_r = c.rotate(rows[i] / np.float32(oracle.l2_norm(rows[i])))
+        bits = (u_r > 0).astype(np.uint16)
+        assert np.array_equal(enc["signs"][i], oracle.pack_indices(bits, 1))
+
+
+def test_shortlist_c_eq_n_matches_full_scan(oracle):
+    """trellis.rs:3202-3249: at C = N nothing is pruned, so the two-stage
+    search returns the plain codes-only top-10 (M lowered to 8)."""
+    dim = 128
+    db = oracle.rand_unit(200, dim, 31)
+    c = oracle.Codec(dim, 2, 8)
+    enc = c.encode_batch_signs(db)
+    qs = oracle.rand_unit(20, dim, 37)
+    a, sa = c.search_topk(enc, qs, 10)
+    for asym in (False, True):
+        b, sb = c.search_shortlist(enc, qs, 10, 200, asym=asym)
+        assert np.array_equal(a, b) and np.array_equal(sa.view(np.uint32), sb.view(np.uint32))
+
+
+def test_shortlist_recall_monotone_in_c(oracle):
+    """trellis.rs:3251-3300: recall@10 against C = N never drops as C grows."""
+    dim = 128
+    db = oracle.rand_unit(500, dim, 41)
+    c = oracle.Codec(dim, 2, 8)
+    enc = c.encode_batch_signs(db)
+    qs = oracle.rand_unit(30, dim, 43)
+    gold, _ = c.search_shortlist(enc, qs, 10, 500)
+    prev = 0.0
+    for cs in (50, 100, 200, 500):
+        got, _ = c.search_shortlist(enc, qs, 10, cs)
+        r = np.mean([len(set(gold[q]) & set(got[q])) / 10 for q in range(30)])
+        assert r >= prev - 1e-9
+        prev = r
+    assert prev == 1.0
+
+
+def test_asymmetric_stage1_beats_binarizing_the_query(oracle):
+    """trellis.rs:3136-3200: a tight cluster (0.8 e0 + 0.6 r, one centroid,
+    C = 16): the asymmetric stage 1 keeps the exhaustive top-1 more often
+    than the Hamming one (M lowered to 8)."""
+    dim = 128
+    base = np.zeros(dim, np.float32)
+    base[0] = 1.0
+    r = oracle.rand_unit(600, dim, 71)
+    db = _unit(np.float32(0.8) * base + np.float32(0.6) * r)
+    centroid = np.zeros(dim, np.float32)
+    for v in db:
+        centroid += v
+    centroid = centroid / np.float32(600)
+    c = oracle.Codec(dim, 2, 8, centroids=centroid[None, :])
+    enc = c.encode_batch_signs(db)
+    qs = oracle.rand_unit(150, dim, 73)
+    exact, _ = c.search_shortlist(enc, qs, 1, 600, asym=True)
+    ga, _ = c.search_shortlist(enc, qs, 1, 16, asym=True)
+    gh, _ = c.search_shortlist(enc, qs, 1, 16, asym=False)
+    assert (ga[:, 0] == exact[:, 0]).sum() > (gh[:, 0] == exact[:, 0]).sum()
+
+
+@pytest.mark.parametrize("asym", [False, True])
+def test_shortlist_stages_restated(oracle, asym):
+    """trellis.rs:874-948 restated in numpy: stage-1 similarity (Hamming or
+    the sequential masked sum, times rnorm under centering), the C best by
+    (similarity desc, entry asc), then score() and top-k by (score desc,
+    entry asc)."""
+    dim, n, k, cs = 64, 150, 5, 12
+    db = oracle.rand_unit(n, dim, 91)
+    cen = oracle.kmeans(db, 3, 42)
+    c = oracle.Codec(dim, 2, 6, centroids=cen)
+    enc = c.encode_batch_signs(db)
+    qs = oracle.rand_unit(4, dim, 93)
+    ids, scores = c.search_shortlist(enc, qs, k, cs, asym=asym)
+    bits = np.unpackbits(enc["signs"], axis=1)[:, :dim]
+    for qi, q in enumerate(qs):
+        q_r, _ = c.prepare_query(q)
+        if asym:
+            sims = []
+            for i in range(n):
+                s = np.float32(0.0)
+                for t in range(dim):
+                    s = np.float32(s + (q_r[t] if bits[i, t] else -q_r[t]))
+                sims.append(s)
+            sims = np.array(sims, np.float32)
+        else:
+            qb = (q_r > 0).astype(np.uint8)
+            h = (bits != qb[None, :]).sum(axis=1)
+            sims = np.float32(dim) - np.float32(2.0) * h.astype(np.float32)
+        sims = enc["rnorm"] * sims
+        keep = sorted(range(n), key=lambda i: (-sims[i], i))[:cs]
+        sc = c.score_candidates(enc, q, np.array(keep, np.int64))
+        order = sorted(range(cs), key=lambda j: (-sc[j], keep[j]))[:k]
+        assert list(ids[qi]) == [keep[j] for j in order]
+        assert np.array_equal(scores[qi].view(np.uint32), sc[order].view(np.uint32))
+
+
+def test_ivf_shortlist_full_c_matches_ivf_search(oracle):
+    """ivf.rs:52-60 + 229-239: with C at least the longest list, every probed
+    list reranks all its entries, so the shortlist arm equals the codes arm;
+    centered and uncentered lists."""
+    dim, nlist = 64, 8
+    db = oracle.rand_unit(800, dim, 95)
+    qs = oracle.rand_unit(20, dim, 97)
+    cen = oracle.kmeans(db, nlist, 42)
+    asg = oracle.assign(db, cen)
+    order = np.argsort(asg, kind="stable")
+    off = np.zeros(nlist + 1, np.int64)
+    np.add.at(off, asg.astype(np.int64) + 1, 1)
+    off = np.cumsum(off)
+    c = oracle.Codec(dim, 2, 8)
+    for centered in (False, True):
+        enc = c.ivf_encode_signs(db[order], cen if centered else None, asg[order])
+        a, sa = c.ivf_search_topk(cen, off, order.astype(np.int64), enc, centered, qs, 3, 10)
+        b, sb = c.ivf_search_shortlist(cen, off, order.astype(np.int64), enc, centered, qs, 3,
+                                       10, 800)
+        assert np.array_equal(a, b) and np.array_equal(sa.view(np.uint32), sb.view(np.uint32))
+        s, _ = c.ivf_search_shortlist(cen, off, order.astype(np.int64), enc, centered, qs, 3,
+                                      10, 20, asym=True)
+        assert np.mean([len(set(a[q]) & set(s[q])) for q in range(20)]) > 5

@@ -36,6 +36,8 @@ SYMBOLS = [
     "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest", "uv_index_save", "uv_index_load",
     "uv_ivf_save", "uv_ivf_load", "uv_index_prepare", "uv_prepared_destroy", "uv_prepared_len",
     "uv_prepared_score", "uv_index_score_candidates", "uv_index_scorer_model_bytes",
+    "uv_index_set_shortlist", "uv_index_export_signs", "uv_ivf_set_shortlist",
+    "uv_ivf_export_signs",
 ]
 
 
@@ -123,6 +125,10 @@ def lib():
             "uv_prepared_score": (C.c_int, [vp, vp, vp, i64, vp, vp]),
             "uv_index_score_candidates": (C.c_int, [vp, vp, vp, i64, vp, vp]),
             "uv_index_scorer_model_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_index_set_shortlist": (C.c_int, [vp, i32, i32, i32]),
+            "uv_index_export_signs": (C.c_int, [vp, vp, vp]),
+            "uv_ivf_set_shortlist": (C.c_int, [vp, i32, i32, i32]),
+            "uv_ivf_export_signs": (C.c_int, [vp, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -363,6 +369,17 @@ class Index:
                                     _ptr(scores), _stream(queries)))
         return ids, scores
 
+    # -- the 1-bit shortlist (src/trellis.rs:803-948) --
+    def set_shortlist(self, c: int, asym: bool = False, rnorm: bool = True) -> None:
+        """with_shortlist(c).with_shortlist_asym(asym).with_shortlist_rnorm(rnorm);
+        the index must be empty.  Cosine searches then run search_shortlist."""
+        check(lib().uv_index_set_shortlist(self.h, c, int(asym), int(rnorm)))
+
+    def export_signs(self):
+        out = np.zeros((len(self), (self.codec.dim + 7) // 8), np.uint8)
+        check(lib().uv_index_export_signs(self.h, _ptr(out), None))
+        return out
+
     # -- CandidateScorer (src/lib.rs:93-102, src/trellis.rs:2039-2086) --
     def prepare(self, queries) -> "PreparedQueries":
         """CandidateScorer::prepare for a batch of queries (one row each)."""
@@ -536,6 +553,15 @@ class IvfIndex:
         out = _Alloc(queries)((queries.shape[0], nprobe), np.int32)
         check(lib().uv_ivf_probe(self.h, _ptr(queries), queries.shape[0], nprobe, _ptr(out),
                                  _stream(queries)))
+        return out
+
+    def set_shortlist(self, c: int, asym: bool = False, rnorm: bool = True) -> None:
+        """IvfCodec::TrellisShortlist{c, asym, rnorm} (ivf.rs:52-60); before build."""
+        check(lib().uv_ivf_set_shortlist(self.h, c, int(asym), int(rnorm)))
+
+    def export_signs(self):
+        out = np.zeros((len(self), (self.codec.dim + 7) // 8), np.uint8)
+        check(lib().uv_ivf_export_signs(self.h, _ptr(out), None))
         return out
 
     def search(self, queries, k: int, nprobe: int):

@@ -19,6 +19,7 @@
 // in shared memory when it fits.
 #include "uv_common.cuh"
 #include "uv_kernels.h"
+#include "uv_score_thread.cuh"
 
 namespace uvb {
 
@@ -108,15 +109,12 @@ __global__ void __launch_bounds__(256) score_candidates_kernel(const CandParams 
 }
 
 // ---------------------------------------------------------------------------
-// The lane kernel (bits 1, 2, 4; code rows padded to 16 bytes): one thread
-// per candidate, a warp per 32 consecutive candidates.  The thread keeps the
-// 16 accumulators of the two 8-lane chains itself (acc[c & 15] for c in the
-// 16-blocks, acc[0..7] for the 8-block), reads its record's code words 16
-// bytes at a time and cuts every window out of two adjacent words with
-// shifts known at compile time, then folds the accumulators with the
-// hsum256 tree.  The code table is replicated in shared memory so that lane
-// l reads copy l % R at word e * R + l % R: with R = 32 every lane owns a
-// bank and the table gathers never conflict.
+// The lane kernel: one thread per candidate, a warp per 32
+// consecutive candidates, each thread running record_dot_thread
+// (uv_score_thread.cuh: its own 16 accumulators, windows cut from 16-byte
+// code chunks with compile-time shifts).  The code table is replicated in
+// shared memory so that lane l reads copy l % R at word e * R + l % R: with
+// R = 32 every lane owns a bank and the table gathers never conflict.
 template <int BITS>
 __global__ void __launch_bounds__(1024, 1) score_candidates_lane_kernel(const CandParams p) {
   extern __shared__ __align__(16) float tab[];
@@ -132,10 +130,6 @@ __global__ void __launch_bounds__(1024, 1) score_candidates_lane_kernel(const Ca
   const int rsel = R > 0 ? (lane & (R - 1)) : 0;
   const int rstride = R > 0 ? R : 1;
   const float *table = R > 0 ? tab : p.code;
-  const uint32_t wmask = (1u << (p.mem + BITS)) - 1u;
-  const int nb16 = p.dim >> 4;
-  constexpr int CPC = 128 / BITS;            // coordinates per 16-byte code chunk
-  const int nchunks = (nb16 * 16 + CPC - 1) / CPC;
   const int64_t ngroups = (p.n + 31) >> 5;
   const int warps = blockDim.x >> 5;
 
@@ -186,70 +180,9 @@ __global__ void __launch_bounds__(1024, 1) score_candidates_lane_kernel(const Ca
       continue;
     }
     const float *qv = p.q_r + q * (int64_t)p.q_stride;
-    const uint4 *cw4 = (const uint4 *)(p.codes + rec * (int64_t)p.code_stride);
-    uint32_t prev = __ldg(p.start + rec);
-    float acc[16];
-#pragma unroll
-    for (int t = 0; t < 16; t++) acc[t] = 0.0f;
-    for (int k = 0; k < nchunks; k++) {
-      const uint4 raw = __ldg(cw4 + k);
-      const uint32_t w[4] = {__byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
-                             __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123)};
-#pragma unroll
-      for (int blk = 0; blk < CPC / 16; blk++) {
-        const int c0 = k * CPC + blk * 16;
-        if (c0 < nb16 * 16) {
-          float qq[16];
-#pragma unroll
-          for (int v = 0; v < 4; v++) {
-            const float4 f = __ldg((const float4 *)(qv + c0) + v);
-            qq[4 * v] = f.x;
-            qq[4 * v + 1] = f.y;
-            qq[4 * v + 2] = f.z;
-            qq[4 * v + 3] = f.w;
-          }
-#pragma unroll
-          for (int t = 0; t < 16; t++) {
-            // window of coordinate c0 + t: the W bits ending at chunk bit e
-            const int e = (blk * 16 + t + 1) * BITS;  // bits of the chunk consumed
-            const int wi = (e - 1) >> 5;
-            const int sh = 31 - ((e - 1) & 31);
-            const uint32_t hiw = wi == 0 ? prev : w[wi - 1];
-            const uint64_t v = ((uint64_t)hiw << 32) | w[wi];
-            const uint32_t win = (uint32_t)(v >> sh) & wmask;
-            acc[t] = fmaf(qq[t], table[win * rstride + rsel], acc[t]);
-          }
-        }
-      }
-      prev = w[3];
-    }
-    // the 8-block and the scalar tail (dims not a multiple of 16)
-    const int rw = p.code_stride >> 2;
-    const uint32_t *cw = (const uint32_t *)cw4;
-    const uint32_t st = __ldg(p.start + rec);
-    auto window = [&](int c) -> uint32_t {
-      const int pos = 32 + c * BITS - p.mem;
-      const int w0 = pos >> 5, sh = pos & 31;
-      const uint32_t hi =
-          w0 == 0 ? st : (w0 <= rw ? __byte_perm(__ldg(cw + w0 - 1), 0, 0x0123) : 0u);
-      const uint32_t lo = w0 + 1 <= rw ? __byte_perm(__ldg(cw + w0), 0, 0x0123) : 0u;
-      return __funnelshift_l(lo, hi, sh) >> (32 - p.mem - BITS);
-    };
-    if ((p.dim & 15) >= 8) {
-#pragma unroll
-      for (int t = 0; t < 8; t++) {
-        const int c = nb16 * 16 + t;
-        acc[t] = fmaf(__ldg(qv + c), table[window(c) * rstride + rsel], acc[t]);
-      }
-    }
-    float v8[8];
-#pragma unroll
-    for (int t = 0; t < 8; t++) v8[t] = fadd(acc[t], acc[t + 8]);
-    const float s0 = fadd(v8[0], v8[4]), s1 = fadd(v8[1], v8[5]);
-    const float s2 = fadd(v8[2], v8[6]), s3 = fadd(v8[3], v8[7]);
-    float dot = fadd(fadd(s0, s1), fadd(s2, s3));
-    for (int c = nb16 * 16 + ((p.dim & 15) >= 8 ? 8 : 0); c < p.dim; c++)
-      dot = fadd(dot, fmul(__ldg(qv + c), table[window(c) * rstride + rsel]));
+    const float dot = record_dot_thread<BITS>(qv, p.codes + rec * (int64_t)p.code_stride,
+                                              __ldg(p.start + rec), p.dim, p.mem, p.code_stride,
+                                              table, rstride, rsel);
     float qm = 0.0f;  // qc.get(cidx).unwrap_or(0.0), src/trellis.rs:2035
     if (p.n_centroids > 0) {
       const uint32_t ci = p.cidx ? __ldg(p.cidx + rec) : 0u;
@@ -266,6 +199,8 @@ const void *score_candidates_lane_kernel_ptr(int bits) {
       return (const void *)score_candidates_lane_kernel<1>;
     case 2:
       return (const void *)score_candidates_lane_kernel<2>;
+    case 3:
+      return (const void *)score_candidates_lane_kernel<3>;
     case 4:
       return (const void *)score_candidates_lane_kernel<4>;
   }

@@ -93,6 +93,8 @@ int uv_codec_create(const uv_config *cfg, uv_codec **out) {
   c->cfg.rotation_rounds = std::max(cfg->rotation_rounds, 1);
   c->code_bytes = (cfg->dim * cfg->bits + 7) / 8;
   c->code_stride = (c->code_bytes + 15) & ~15;
+  c->sign_bytes = (cfg->dim + 7) / 8;
+  c->sign_stride = (c->sign_bytes + 15) & ~15;
   c->h_table = uvb::build_code_table(cfg->mem, cfg->bits);
   c->table_len = (int)c->h_table.size();
   for (float v : c->h_table) c->code_absmax = std::max(c->code_absmax, std::fabs(v));
@@ -184,7 +186,7 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
                   int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
                   float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,
                   const float *list_centroids, const uint32_t *row_list,
-                  const int64_t *row_index) {
+                  const int64_t *row_index, uint8_t *signs) {
   if (c->plan_status == 1) return fail(UV_EINVAL, c->plan_why);
   if (c->plan_status != 0) return fail(UV_EUNSUPPORTED, c->plan_why);
   if (n == 0) return UV_OK;
@@ -213,6 +215,8 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   p.list_centroids = list_centroids;
   p.row_list = row_list;
   p.row_index = row_index;
+  p.signs = signs;
+  p.sign_stride = c->sign_stride;
   int grid = 0;
   UV_CK(uvb::encode_grid(c->plan, n, &grid));
   if (!c->plan.back_smem) {
@@ -400,6 +404,7 @@ int uv_index_destroy(uv_index *ix) {
     cudaFree(ix->cidx);
     cudaFree(ix->ids);
     cudaFree(ix->centroids);
+    cudaFree(ix->signs);
   }
   delete ix;
   return UV_OK;
@@ -433,7 +438,31 @@ static int index_ensure(uv_index *ix, int64_t need, cudaStream_t st) {
   UV_TRY(grow(&ix->norms, ix->n, cap, st));
   UV_TRY(grow(&ix->cidx, ix->n, cap, st));
   UV_TRY(grow(&ix->ids, ix->n, cap, st));
+  if (ix->sl_c > 0) UV_TRY(grow(&ix->signs, ix->n * c->sign_stride, cap * c->sign_stride, st));
   ix->cap = cap;
+  return UV_OK;
+}
+
+// with_shortlist(c) / with_shortlist_asym / with_shortlist_rnorm
+// (src/trellis.rs:803-839): sign codes are written as records are added, so
+// the shortlist is switched on while the index is empty.
+int uv_index_set_shortlist(uv_index *ix, int32_t c, int32_t asym, int32_t rnorm) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  if (c < 0 || (asym != 0 && asym != 1) || (rnorm != 0 && rnorm != 1))
+    return fail(UV_EINVAL, "shortlist: c >= 0, asym and rnorm 0 or 1");
+  if (ix->n > 0 && (c > 0) != (ix->sl_c > 0))
+    return fail(UV_EINVAL, "shortlist: switch it on or off while the index is empty");
+  DeviceGuard g(ix->codec->cfg.device);
+  if (c > 0 && ix->signs == nullptr && ix->cap > 0)
+    UV_CK(cudaMalloc(&ix->signs, (size_t)ix->cap * ix->codec->sign_stride));
+  if (c == 0 && ix->signs != nullptr) {
+    UV_CK(cudaDeviceSynchronize());
+    cudaFree(ix->signs);
+    ix->signs = nullptr;
+  }
+  ix->sl_c = c;
+  ix->sl_asym = asym;
+  ix->sl_weight = rnorm;
   return UV_OK;
 }
 
@@ -479,7 +508,8 @@ static int index_add_impl(uv_index *ix, const int64_t *ids, const float *rows, i
   }
   UV_TRY(encode_device(c, d_rows, n, ix->centroids, ix->n_centroids, false,
                        ix->codes + o * c->code_stride, ix->start + o, ix->rescale + o,
-                       ix->rnorm + o, ix->cidx + o, ix->norms + o, st, sc));
+                       ix->rnorm + o, ix->cidx + o, ix->norms + o, st, sc, nullptr, nullptr,
+                       nullptr, ix->sl_c > 0 ? ix->signs + o * c->sign_stride : nullptr));
   ix->n += n;
   bool rows_dev = false;
   classify(rows, c->cfg.device, &rows_dev);
@@ -526,7 +556,23 @@ int uv_index_mem_bytes(const uv_index *ix, int64_t *bytes) {
     }
     center = 4 + (bitsn + 7) / 8;
   }
-  *bytes = ix->n * (int64_t)(cb + sb + rb + center);
+  // + the sign code when the shortlist is on (src/trellis.rs:2196)
+  const int64_t sign = ix->sl_c > 0 ? ix->codec->sign_bytes : 0;
+  *bytes = ix->n * (int64_t)(cb + sb + rb + center + sign);
+  return UV_OK;
+}
+
+// The shortlist's sign codes, n x ceil(dim/8) (host or device).
+int uv_index_export_signs(const uv_index *ix, uint8_t *signs, void *stream) {
+  if (ix == nullptr || signs == nullptr) return fail(UV_EINVAL, "null argument");
+  if (ix->sl_c == 0) return fail(UV_EINVAL, "the shortlist is off: no sign codes");
+  const uv_codec *c = ix->codec;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (ix->n == 0) return UV_OK;
+  UV_CK(cudaMemcpy2DAsync(signs, c->sign_bytes, ix->signs, c->sign_stride, c->sign_bytes, ix->n,
+                          cudaMemcpyDefault, st));
+  UV_CK(cudaStreamSynchronize(st));
   return UV_OK;
 }
 
@@ -1029,6 +1075,16 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
   UV_TRY(sc.alloc(&degen, (size_t)nq));
   UV_TRY(prep_launch(c, d_q, nq, ix->centroids, ix->n_centroids, q_r, qc, degen, nullptr, st));
+  // the 1-bit shortlist (src/trellis.rs:2121-2123) when it prunes anything;
+  // the MIPS wrapper (src/bench.rs:1029-1045) asks for every record, where
+  // the shortlist keeps all of them, so MIPS is the plain scan
+  if (ix->sl_c > 0 && mode == UV_SEARCH_COSINE && std::max(ix->sl_c, k) < ix->n) {
+    UV_TRY(shortlist_launch(c, ix->sl_c, ix->sl_asym, ix->sl_weight && ix->n_centroids > 0, k,
+                            nq, 1, nullptr, nullptr, ix->n, ix->n, q_r, nullptr, nullptr, qc,
+                            ix->n_centroids, degen, ix->codes, ix->signs, ix->start, ix->cidx,
+                            ix->rescale, ix->rnorm, ix->ids, d_ids, d_scores, st));
+    return outs.finish(st);
+  }
   bool used = false;
   UV_TRY(tc_search(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc, &used));
   if (!used) UV_TRY(exact_scan(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc));
@@ -1180,6 +1236,8 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   if (d % 16 != 0) return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
+  if (ix->sl_c > 0 && mode == UV_SEARCH_COSINE && std::max(ix->sl_c, k) < ix->n)
+    return fail(UV_EUNSUPPORTED, "the shortlist search is not built without allocation");
   const int dev = c->cfg.device;
   DeviceGuard g(dev);
   // every buffer must already be on this GPU: staging would allocate

@@ -1,8 +1,76 @@
 // capi_cand.cu -- the batched CandidateScorer / PreparedQuery entry points
-// (src/lib.rs:83-102, impl src/trellis.rs:2003-2086) over a flat index.
+// (src/lib.rs:83-102, impl src/trellis.rs:2003-2086) over a flat index, and
+// the launcher of the 1-bit shortlist search (src/trellis.rs:841-948).
 #include "capi_internal.h"
 
 using namespace uvcapi;
+
+namespace uvcapi {
+
+int shortlist_launch(const uv_codec *c, int cs, int asym, int weight, int k, int64_t npairs,
+                     int per_query, const int32_t *lists, const int64_t *list_off,
+                     int64_t max_len, int64_t n_flat, const float *q_r, const float *u,
+                     const float *centroids, const float *qc, int n_centroids,
+                     const uint32_t *degen, const uint8_t *codes, const uint8_t *signs,
+                     const uint32_t *start, const uint32_t *cidx, const float *rescale,
+                     const float *rnorm, const int64_t *ids, int64_t *out_id, float *out_score,
+                     cudaStream_t st) {
+  if (npairs == 0) return UV_OK;
+  if (npairs > INT32_MAX) return fail(UV_EINVAL, "shortlist: too many (query, list) pairs");
+  const int d = c->cfg.dim;
+  const int64_t ce_max = std::min<int64_t>(std::max(cs, k), std::max<int64_t>(max_len, 1));
+  int cp = 256;
+  while (cp < ce_max) cp <<= 1;
+  if (cp > 4096) return fail(UV_EUNSUPPORTED, "shortlist: C above 4096 is not built");
+  const int q_stride = (d + 3) & ~3;
+  const size_t smem = uvb::shortlist_smem_bytes(cp, q_stride, c->sign_stride, c->table_len);
+  if (smem > 227 * 1024)
+    return fail(UV_EUNSUPPORTED, "shortlist: code table and buffers exceed shared memory");
+  uvb::ShortlistParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.dim = d;
+  p.mem = c->cfg.mem;
+  p.bits = c->cfg.bits;
+  p.code_stride = c->code_stride;
+  p.sign_stride = c->sign_stride;
+  p.q_stride = q_stride;
+  p.u_stride = q_stride;
+  p.cs = cs;
+  p.k = k;
+  p.cp = cp;
+  p.weight = weight;
+  p.table_len = c->table_len;
+  p.n_centroids = n_centroids;
+  p.per_query = per_query;
+  p.npairs = npairs;
+  p.n_flat = n_flat;
+  p.lists = lists;
+  p.list_off = list_off;
+  p.q_r = q_r;
+  p.u = u;
+  p.centroids = centroids;
+  p.qc = qc;
+  p.degenerate = degen;
+  p.codes = codes;
+  p.signs = signs;
+  p.start = start;
+  p.cidx = cidx;
+  p.code = c->d_table;
+  p.rescale = rescale;
+  p.rnorm = rnorm;
+  p.ids = ids;
+  p.out_id = out_id;
+  p.out_score = out_score;
+  const void *kern = uvb::shortlist_kernel_ptr(c->cfg.bits, asym != 0);
+  if (kern == nullptr) return fail(UV_EUNSUPPORTED, "shortlist: bits must be 1..4");
+  UV_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  void *args[] = {&p};
+  ProfScope ps("shortlist", st);
+  UV_CK(cudaLaunchKernel(kern, dim3((unsigned)npairs), dim3(256), args, smem, st));
+  return UV_OK;
+}
+
+}  // namespace uvcapi
 
 // A batch of prepared queries: the hoists prepare() makes once per query
 // (unit query, rotated q_r, per-centroid qc, the degenerate flag), resident

@@ -198,6 +198,7 @@ int sm_count(int dev);
 struct uv_codec {
   uv_config cfg;
   int code_bytes = 0, code_stride = 0, table_len = 0;
+  int sign_bytes = 0, sign_stride = 0;  // shortlist sign code: ceil(dim/8), padded to 16
   float code_absmax = 0.0f;
   std::vector<float> h_table;
   uvb::RotationHost rot_host;
@@ -222,6 +223,8 @@ struct uv_ivf {
   uint32_t *start = nullptr;
   float *rescale = nullptr, *rnorm = nullptr;
   int64_t *ids = nullptr;
+  int sl_c = 0, sl_asym = 0, sl_weight = 1;  // the 1-bit shortlist (0 = off)
+  uint8_t *signs = nullptr;                  // n x sign_stride when the shortlist is on
 };
 
 struct uv_index {
@@ -234,6 +237,8 @@ struct uv_index {
   int64_t *ids = nullptr;
   float *centroids = nullptr;
   int n_centroids = 0;
+  int sl_c = 0, sl_asym = 0, sl_weight = 1;  // the 1-bit shortlist (0 = off)
+  uint8_t *signs = nullptr;                  // cap x sign_stride when the shortlist is on
 };
 
 
@@ -243,7 +248,18 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
                   int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
                   float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,
                   const float *list_centroids = nullptr, const uint32_t *row_list = nullptr,
-                  const int64_t *row_index = nullptr);
+                  const int64_t *row_index = nullptr, uint8_t *signs = nullptr);
+// The shortlist search (shortlist.cu): one pair per (query, list) with IVF
+// lists (lists != null, per_query lists per query, max_len the longest
+// list) or one pair per query over [0, n_flat).  Writes npairs x k results.
+int shortlist_launch(const uv_codec *c, int cs, int asym, int weight, int k, int64_t npairs,
+                     int per_query, const int32_t *lists, const int64_t *list_off,
+                     int64_t max_len, int64_t n_flat, const float *q_r, const float *u,
+                     const float *centroids, const float *qc, int n_centroids,
+                     const uint32_t *degen, const uint8_t *codes, const uint8_t *signs,
+                     const uint32_t *start, const uint32_t *cidx, const float *rescale,
+                     const float *rnorm, const int64_t *ids, int64_t *out_id, float *out_score,
+                     cudaStream_t st);
 // Merge top-k lists: row q takes n_lists lists of k_in, or with row_off the
 // ragged lists [row_off[q], row_off[q+1]) (n_lists is then their maximum) and
 // writes output row out_row[q] when out_row is given.

@@ -115,6 +115,8 @@ void free_lists(uv_ivf *ix) {
   cudaFree(ix->rnorm);
   cudaFree(ix->ids);
   cudaFree(ix->d_off);
+  cudaFree(ix->signs);
+  ix->signs = nullptr;
   ix->codes = nullptr;
   ix->start = nullptr;
   ix->rescale = ix->rnorm = nullptr;
@@ -187,6 +189,21 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   const int nlist = ix->nlist;
   int64_t max_list = 0;
   for (int l = 0; l < nlist; l++) max_list = std::max(max_list, ix->off[l + 1] - ix->off[l]);
+  if (ix->sl_c > 0) {
+    // IvfCodec::TrellisShortlist (src/ivf.rs:52-60): every probed list runs
+    // search_shortlist(query, k, c) (src/trellis.rs:854-948), then the
+    // per-list results merge per query (src/ivf.rs:229-239)
+    int64_t *pid = nullptr;
+    float *psc = nullptr;
+    UV_TRY(sc.alloc(&pid, (size_t)npairs * k));
+    UV_TRY(sc.alloc(&psc, (size_t)npairs * k));
+    UV_TRY(shortlist_launch(c, ix->sl_c, ix->sl_asym, ix->sl_weight && ix->centered, k, npairs,
+                            np, lists, ix->d_off, max_list, 0, q_r, ix->centered ? u : nullptr,
+                            ix->centroids, nullptr, 0, degen, ix->codes, ix->signs, ix->start,
+                            nullptr, ix->rescale, ix->centered ? ix->rnorm : nullptr, ix->ids,
+                            pid, psc, st));
+    return merge_launch(nq, np, k, k, nullptr, psc, pid, d_ids, d_scores, st);
+  }
   // a pair's ranges are merged in one pass of at most about 1024 entries
   const int64_t range_size =
       std::max<int64_t>(1024, (max_list * k + 1023) / 1024);
@@ -486,6 +503,7 @@ int uv_ivf_build(uv_ivf *ix, const float *rows, int64_t n, const uint32_t *assig
   UV_CK(cudaMalloc(&ix->rnorm, sizeof(float) * cap));
   UV_CK(cudaMalloc(&ix->ids, sizeof(int64_t) * cap));
   UV_CK(cudaMalloc(&ix->d_off, sizeof(int64_t) * (ix->nlist + 1)));
+  if (ix->sl_c > 0) UV_CK(cudaMalloc(&ix->signs, (size_t)cap * c->sign_stride));
   UV_CK(cudaMemcpyAsync(ix->d_off, off.data(), sizeof(int64_t) * (ix->nlist + 1),
                         cudaMemcpyHostToDevice, st));
   if (n > 0) {
@@ -496,7 +514,7 @@ int uv_ivf_build(uv_ivf *ix, const float *rows, int64_t n, const uint32_t *assig
     UV_TRY(upload(row_list, sc, &d_list, st));
     UV_TRY(encode_device(c, d_rows, n, nullptr, 0, false, ix->codes, ix->start, ix->rescale,
                          ix->rnorm, nullptr, nullptr, st, sc,
-                         ix->centered ? ix->centroids : nullptr, d_list, d_order));
+                         ix->centered ? ix->centroids : nullptr, d_list, d_order, ix->signs));
   }
   UV_CK(cudaStreamSynchronize(st));  // the host vectors above end with this call
   ix->off = off;
@@ -520,7 +538,35 @@ int uv_ivf_mem_bytes(const uv_ivf *ix, int64_t *bytes) {
   if (ix == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
   int32_t cb = 0, sb = 0, rb = 0;
   uv_codec_record_bytes(ix->codec, &cb, &sb, &rb);
-  *bytes = ix->n * (int64_t)(cb + sb + rb + (ix->centered ? 4 : 0));
+  const int64_t sign = ix->sl_c > 0 ? ix->codec->sign_bytes : 0;  // src/trellis.rs:2196
+  *bytes = ix->n * (int64_t)(cb + sb + rb + (ix->centered ? 4 : 0) + sign);
+  return UV_OK;
+}
+
+// IvfCodec::TrellisShortlist{c, asym, rnorm} (src/ivf.rs:52-60, 111-135):
+// set before build, which writes the sign codes.
+int uv_ivf_set_shortlist(uv_ivf *ix, int32_t c, int32_t asym, int32_t rnorm) {
+  if (ix == nullptr) return fail(UV_EINVAL, "null argument");
+  if (c < 0 || (asym != 0 && asym != 1) || (rnorm != 0 && rnorm != 1))
+    return fail(UV_EINVAL, "shortlist: c >= 0, asym and rnorm 0 or 1");
+  if (ix->n > 0 && (c > 0) != (ix->sl_c > 0))
+    return fail(UV_EINVAL, "shortlist: switch it on or off before build");
+  ix->sl_c = c;
+  ix->sl_asym = asym;
+  ix->sl_weight = rnorm;
+  return UV_OK;
+}
+
+int uv_ivf_export_signs(const uv_ivf *ix, uint8_t *signs, void *stream) {
+  if (ix == nullptr || signs == nullptr) return fail(UV_EINVAL, "null argument");
+  if (ix->sl_c == 0) return fail(UV_EINVAL, "the shortlist is off: no sign codes");
+  const uv_codec *c = ix->codec;
+  DeviceGuard g(c->cfg.device);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (ix->n == 0) return UV_OK;
+  UV_CK(cudaMemcpy2DAsync(signs, c->sign_bytes, ix->signs, c->sign_stride, c->sign_bytes, ix->n,
+                          cudaMemcpyDefault, st));
+  UV_CK(cudaStreamSynchronize(st));
   return UV_OK;
 }
 

@@ -137,6 +137,20 @@ __device__ __forceinline__ void encode_row_finalize(const EncodeParams &p, int64
       out[bi] = (uint8_t)val;
     }
   }
+  if (valid && p.signs != nullptr) {
+    // the shortlist's 1-bit code: pack_indices(u_r > 0, 1), MSB-first
+    // (src/trellis.rs:1084-1094), zero-padded to sign_stride
+    uint8_t *out = p.signs + vv * (int64_t)p.sign_stride;
+    for (int bi = tm.t; bi < p.sign_stride; bi += T) {
+      uint32_t val = 0;
+#pragma unroll
+      for (int bit = 0; bit < 8; bit++) {
+        const int i = bi * 8 + bit;
+        if (i < d && xbuf[i] > 0.0f) val |= 0x80u >> bit;
+      }
+      out[bi] = (uint8_t)val;
+    }
+  }
   tm.sync();
   if (valid && tm.leader()) {
     if (p.start) p.start[vv] = misc_u[5];

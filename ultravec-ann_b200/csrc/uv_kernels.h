@@ -31,6 +31,8 @@ struct EncodeParams {
   float *rescale, *rnorm;
   uint32_t *cidx;
   float *norms;             // exact l2 norm of the raw row (MIPS sidecar)
+  uint8_t *signs;           // or null: n x sign_stride sign codes of u_r (shortlist)
+  int sign_stride;
   int rotated_input;        // rows are already rotated units (encode_rotated)
   uint32_t *back_global;    // per-team back-pointer slots (global mode)
   int64_t back_words_team;
@@ -155,6 +157,28 @@ struct CandParams {
   int *n_bad;                  // candidates with a position outside the index
 };
 
+// The 1-bit companion shortlist (shortlist.cu).  One CTA per pair: pair p
+// is query p / per_query over the records of list lists[p] (IVF) or over
+// [0, n_flat) (flat); it writes its top-k to row p of out_id / out_score.
+struct ShortlistParams {
+  int dim, mem, bits, code_stride, sign_stride, q_stride, u_stride;
+  int cs, k, cp, weight, table_len, n_centroids, per_query;
+  int64_t npairs, n_flat;
+  const int32_t *lists;        // npairs (IVF) or null (flat)
+  const int64_t *list_off;     // nlist + 1 (IVF)
+  const float *q_r;            // rotated unit queries
+  const float *u;              // unit queries (IVF centered: qm = <u, c_list>) or null
+  const float *centroids;      // IVF list centroids (centered) or null
+  const float *qc;             // flat centered: nq x n_centroids
+  const uint32_t *degenerate;
+  const uint8_t *codes, *signs;
+  const uint32_t *start, *cidx;
+  const float *code, *rescale, *rnorm;
+  const int64_t *ids;          // output ids by record, or null: the record position
+  int64_t *out_id;
+  float *out_score;
+};
+
 // Tensor-core prefilter of the flat scan (tcscan.cu).
 struct TcScanParams {
   int q_stride, cand_cap;
@@ -268,7 +292,9 @@ __global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, 
                                const int32_t *lists, int npairs, float *qm);
 __global__ void rerank_kernel(const RerankParams p);
 __global__ void score_candidates_kernel(const CandParams p);
-const void *score_candidates_lane_kernel_ptr(int bits);  // bits 1, 2, 4; else null
+const void *score_candidates_lane_kernel_ptr(int bits);  // bits 1..4; else null
+const void *shortlist_kernel_ptr(int bits, bool asym);
+size_t shortlist_smem_bytes(int cp, int q_stride, int sign_stride, int table_len);
 
 // scan tiling constants shared with the host planner
 constexpr int kScanTQ = 32;
