@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--n-query", type=int, default=N_QUERY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep", "candidates"],
+    ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep", "candidates",
+                                           "shortlist"],
                     default="flat",
                     help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
                          "others measure the remaining configurations, one JSON line each")
@@ -486,7 +487,13 @@ def run_secondary(args):
                   b=2, M in {2, 4, 8, 12, 16}: encode rows/s
     candidates    1M rows d=128 N(0,1), b=2, M=8; 10k prepared queries with
                   256 uniformly random candidate positions each (a batched
-                  graph-walk expansion): candidates scored per second"""
+                  graph-walk expansion): candidates scored per second
+    shortlist     the flat workload's rows (1M x 128 heavy-tailed integers,
+                  mean-removed), b=2, M=8: IVF nlist=1024 (k-means seed 42, 5
+                  rounds), 10k queries top-10 with the 1-bit shortlist
+                  (Hamming stage 1) at C in {128, 256, 512}, nprobe in
+                  {1, 8, 32, 128}, beside the plain codes scan; and the flat
+                  shortlist at C = 512 over all 1M rows (1k queries)"""
     import torch
 
     from ultravec_ann_b200_loader import load
@@ -564,6 +571,47 @@ def run_secondary(args):
                                                "build_s": build_s, "centered": True, "k": 10,
                                                "bits": 2, "mem": 8, "kernels_ms": kern,
                                                "list_sizes": list_stats})
+    elif args.workload == "shortlist":
+        n, nq, nlist = 1_000_000, 10_000, 1024
+        base_np, query_np = make_data(n, nq)
+        base = torch.from_numpy(base_np).to(dev)
+        qs = torch.from_numpy(query_np).to(dev)
+        cen = uv.kmeans(base, nlist, seed=42, iters=5)
+        codec = uv.Codec(DIM, 2, 8)
+        plain = uv.IvfIndex(codec, cen, centered=False)
+        plain.build(base)
+        arms = {}
+        for c in (128, 256, 512):
+            arms[c] = uv.IvfIndex(codec, cen, centered=False)
+            arms[c].set_shortlist(c)
+            arms[c].build(base)
+        for nprobe in (1, 8, 32, 128):
+            ms = _timed(lambda: plain.search(qs, 10, nprobe), 3)
+            ref_ids = plain.search(qs, 10, nprobe)[0].cpu().numpy()
+            emit("ivf-shortlist-1Mx10k-d128-nlist1024", {
+                "arm": "codes", "nprobe": nprobe, "queries_s": nq / ms * 1e3, "search_ms": ms,
+                "k": 10, "bits": 2, "mem": 8})
+            for c, sl in arms.items():
+                ms = _timed(lambda: sl.search(qs, 10, nprobe), 3)
+                ids = sl.search(qs, 10, nprobe)[0].cpu().numpy()
+                agree = float(np.mean([len(set(ids[q]) & set(ref_ids[q])) / 10
+                                       for q in range(0, nq, 10)]))
+                uv.profile_enable(True)
+                sl.search(qs, 10, nprobe)
+                torch.cuda.synchronize()
+                kern = round(uv.profile_read("shortlist")[0], 3)
+                uv.profile_enable(False)
+                emit("ivf-shortlist-1Mx10k-d128-nlist1024", {
+                    "arm": f"shortlist_c{c}", "nprobe": nprobe, "queries_s": nq / ms * 1e3,
+                    "search_ms": ms, "kernel_ms": kern, "top10_agreement_with_codes": agree,
+                    "k": 10, "bits": 2, "mem": 8})
+        flat = uv.Index(codec)
+        flat.set_shortlist(512)
+        flat.add_batch(base)
+        q1k = qs[:1000]
+        ms = _timed(lambda: flat.search(q1k, 10), 2)
+        emit("flat-shortlist-1Mx1k-d128", {"c": 512, "queries_s": 1000 / ms * 1e3,
+                                           "search_ms": ms, "k": 10, "bits": 2, "mem": 8})
     elif args.workload == "candidates":
         n, nq, per_q, d = 1_000_000, 10_000, 256, 128
         base = torch.from_numpy(rng.standard_normal((n, d), dtype=np.float32)).to(dev)

@@ -146,12 +146,17 @@ __global__ void __launch_bounds__(kSlThreads) shortlist_kernel(const ShortlistPa
       const uint64_t key =
           ((uint64_t)score_key32(sim) << 32) | (uint64_t)(0xffffffffu - (uint32_t)li);
       if (key > thr_s) {
+        // at most one append per thread per tile, into a region merged before
+        // it can hold more than cp - 256 keys: slot < cp always
         const int slot = atomicAdd(&app_s, 1);
-        keys[cp + slot] = key;
+        if (slot < cp) keys[cp + slot] = key;
       }
     }
     __syncthreads();
     const int app = app_s;
+    // every thread holds the same count before the next tile appends to it,
+    // so the merge below is entered by all threads or by none
+    __syncthreads();
     if (app > cp - kSlThreads || (t0 + kSlThreads >= len && app > 0)) {
       sort_desc(keys, 2 * cp);
       if (tid == 0) {
