@@ -238,7 +238,8 @@ int uv_index_export_signs(const uv_index *index, uint8_t *signs, void *stream);
  * score_at's: qm + rnorm * (dot / rescale), 0.0 for a query with
  * |q| < f32::EPSILON.  A position outside the index (the reference panics)
  * returns UV_EINVAL, with NaN in that slot.  The prepared batch reads the
- * index's arrays when it scores: keep the index alive while it exists. */
+ * index's arrays when it scores: keep the index alive while scoring
+ * (uv_prepared_destroy may come after uv_index_destroy). */
 typedef struct uv_prepared uv_prepared;
 int uv_index_prepare(const uv_index *index, const float *queries, int64_t nq,
                      uv_prepared **out, void *stream);

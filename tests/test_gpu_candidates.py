@@ -158,3 +158,18 @@ def test_bad_positions_and_offsets_are_refused(uv, kernel):
     out = prep.score(np.array([0, 1, 2, 3], np.int64), ok_off)
     assert np.all(np.isfinite(out))
     assert prep.score(np.zeros(0, np.int64), np.zeros(4, np.int64)).shape == (0,)
+
+
+def test_destroy_order_is_free(uv):
+    """A prepared batch may outlive its index, and an index its codec (the
+    order a garbage collector picks for a cycle)."""
+    codec = uv.Codec(64, 2, 6)
+    index = uv.Index(codec)
+    index.add_batch(rand_rows(200, 64, 67))
+    prep = index.prepare(rand_rows(2, 64, 68))
+    index.close()
+    prep.close()
+    index2 = uv.Index(codec)
+    index2.add_batch(rand_rows(50, 64, 69))
+    codec.close()
+    index2.close()

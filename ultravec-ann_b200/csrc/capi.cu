@@ -387,6 +387,7 @@ int uv_index_create(const uv_codec *c, uv_index **out) {
   uv_index *ix = new (std::nothrow) uv_index();
   if (ix == nullptr) return fail(UV_ENOMEM, "host allocation failed");
   ix->codec = c;
+  ix->device = c->cfg.device;
   *out = ix;
   return UV_OK;
 }
@@ -394,7 +395,7 @@ int uv_index_create(const uv_codec *c, uv_index **out) {
 int uv_index_destroy(uv_index *ix) {
   if (ix == nullptr) return UV_OK;
   {
-    DeviceGuard g(ix->codec->cfg.device);
+    DeviceGuard g(ix->device);
     cudaDeviceSynchronize();
     cudaFree(ix->codes);
     cudaFree(ix->start);

@@ -77,6 +77,7 @@ int shortlist_launch(const uv_codec *c, int cs, int asym, int weight, int k, int
 // on the index's GPU.  Scoring reads the index's arrays at call time.
 struct uv_prepared {
   const uv_index *index = nullptr;
+  int device = 0;  // destroy touches nothing of the index, which may be gone
   int64_t nq = 0;
   float *q_r = nullptr;  // nq x dim_pad
   float *qc = nullptr;   // nq x max(1, n_centroids)
@@ -195,6 +196,7 @@ int uv_index_prepare(const uv_index *ix, const float *queries, int64_t nq, uv_pr
   uv_prepared *p = new (std::nothrow) uv_prepared;
   if (p == nullptr) return fail(UV_ENOMEM, "out of host memory");
   p->index = ix;
+  p->device = dev;
   p->nq = nq;
   p->n_centroids = ix->n_centroids;
   const size_t dim_pad = (size_t)((d + 3) & ~3);
@@ -229,7 +231,7 @@ int uv_index_prepare(const uv_index *ix, const float *queries, int64_t nq, uv_pr
 
 int uv_prepared_destroy(uv_prepared *p) {
   if (p == nullptr) return UV_OK;
-  DeviceGuard g(p->index->codec->cfg.device);
+  DeviceGuard g(p->device);
   return prepared_free(p);
 }
 

@@ -213,6 +213,7 @@ struct uv_codec {
 // The IVF index (capi_ivf.cu): centroids and list-major posting lists.
 struct uv_ivf {
   const uv_codec *codec = nullptr;
+  int device = 0;              // destroy reads this, not the codec (which may be gone)
   int nlist = 0, centered = 0;
   float *centroids = nullptr;  // nlist x dim
   float *cnorm = nullptr;      // |c_j| (lib.rs:215-217)
@@ -229,6 +230,7 @@ struct uv_ivf {
 
 struct uv_index {
   const uv_codec *codec = nullptr;
+  int device = 0;              // destroy reads this, not the codec (which may be gone)
   int64_t n = 0, cap = 0;
   uint8_t *codes = nullptr;
   uint32_t *start = nullptr;

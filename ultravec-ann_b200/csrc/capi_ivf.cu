@@ -422,6 +422,7 @@ int uv_ivf_create(const uv_codec *codec, const float *centroids, int32_t nlist, 
   uv_ivf *ix = new (std::nothrow) uv_ivf();
   if (ix == nullptr) return fail(UV_ENOMEM, "host allocation failed");
   ix->codec = codec;
+  ix->device = codec->cfg.device;
   ix->nlist = nlist;
   ix->centered = centered ? 1 : 0;
   ix->off.assign((size_t)nlist + 1, 0);
@@ -448,7 +449,7 @@ int uv_ivf_create(const uv_codec *codec, const float *centroids, int32_t nlist, 
 int uv_ivf_destroy(uv_ivf *ix) {
   if (ix == nullptr) return UV_OK;
   {
-    DeviceGuard g(ix->codec->cfg.device);
+    DeviceGuard g(ix->device);
     free_lists(ix);
     cudaFree(ix->centroids);
     cudaFree(ix->cnorm);
