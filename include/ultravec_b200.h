@@ -189,7 +189,9 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * back-pointers for codecs created afterwards (0 automatic, 1 global scratch,
  * 2 shared memory whenever one row's array fits); "tc_scan" selects the flat
  * search's tensor-core prefilter (0 automatic, 1 never, 2 wherever it is
- * built); "cand_kernel" selects the candidate scorer's kernel (0 automatic:
+ * built); "tc_shape" where the prefilter keeps its queries (0 automatic =
+ * 3: tensor memory; 1: shared memory); "cand_kernel" selects the
+ * candidate scorer's kernel (0 automatic:
  * one thread per candidate at bits 1, 2, 4; 1 half a warp per candidate).
  * Process-wide; returns UV_EINVAL for an unknown key. */
 int uv_set_tuning(const char *key, int64_t value);

@@ -18,10 +18,14 @@ pytestmark = pytest.mark.gpu
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 
 
-@pytest.fixture
-def tc_mode(uv):
+@pytest.fixture(params=[3, 1], ids=["a_tmem", "a_smem"])
+def tc_mode(uv, request):
+    """Both CTA shapes: the query tile held in TMEM (the default) and in
+    shared memory."""
+    uv.set_tuning("tc_shape", request.param)
     yield lambda v: uv.set_tuning("tc_scan", v)
     uv.set_tuning("tc_scan", 0)
+    uv.set_tuning("tc_shape", 0)
 
 
 def search_both(uv, index, queries, k, mips, tc_mode):

@@ -18,6 +18,7 @@ std::mutex g_prof_mu;
 int64_t g_scan_splits = 0;
 int g_tc_mode = 0;
 int g_cand_kernel = 0;
+int g_tc_shape = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
@@ -826,9 +827,10 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int d = c->cfg.dim;
   const int64_t n = ix->n;
   if (g_tc_mode == 1 || d != uvb::tc_dim() || ix->n_centroids != 0) return UV_OK;
+  const int shape = g_tc_shape == 1 ? 1 : 3;  // CTA shape (tcscan.cu)
   const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
   const int64_t n_tiles = (n + TN - 1) / TN;
-  const int64_t n_groups = 2 * n_tiles;
+  const int64_t n_groups = 2 * n_tiles;  // bound groups of half a tile
   // a useful threshold needs several groups per top-k slot
   if (n_groups < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
   if (n_tiles * TN > INT32_MAX) return UV_OK;
@@ -895,6 +897,11 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (extra slice) failed");
   }
   // units: query tiles x record splits, filling whole waves of one CTA per SM
+  const size_t smem = uvb::tc_scan_smem_bytes(shape);
+  const void *k1 = uvb::tc_scan_kernel_ptr(1, shape);
+  const void *k2 = uvb::tc_scan_kernel_ptr(2, shape);
+  UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t qtiles = (nq + TM - 1) / TM;
   const int64_t slots = sm_count(dev);
   const int64_t max_splits = std::max<int64_t>(1, std::min<int64_t>(n_tiles / 8, 64));
@@ -937,12 +944,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   tp.cand = cand;
   tp.cand_cnt = cand_cnt;
   tp.err = flags;
-  const size_t smem = uvb::tc_scan_smem_bytes();
-  const void *k1 = uvb::tc_scan_kernel_ptr(1);
-  const void *k2 = uvb::tc_scan_kernel_ptr(2);
   const dim3 grid((unsigned)qtiles, (unsigned)splits);
-  UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   {
     void *args[] = {&tp, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass1", st);
@@ -1132,6 +1134,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_scan") == 0) {
     if (value < 0 || value > 2) return fail(UV_EINVAL, "tc_scan must be 0, 1 or 2");
     g_tc_mode = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "tc_shape") == 0) {
+    if (value != 0 && value != 1 && value != 3) return fail(UV_EINVAL, "tc_shape must be 0, 1 or 3");
+    g_tc_shape = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "cand_kernel") == 0) {

@@ -156,6 +156,7 @@ extern std::mutex g_prof_mu;
 extern int64_t g_scan_splits;  // uv_set_tuning("scan_splits")
 extern int g_tc_mode;          // uv_set_tuning("tc_scan")
 extern int g_cand_kernel;      // uv_set_tuning("cand_kernel")
+extern int g_tc_shape;         // uv_set_tuning("tc_shape")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 

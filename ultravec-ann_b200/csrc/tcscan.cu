@@ -5,7 +5,7 @@
 // association of simd.rs:183-262.  Computing every dot that way is FP32-issue
 // bound.  Here every (query, record) dot is first computed on the tensor
 // cores in fp16 x fp16 -> f32 (tcgen05.mma, 128 queries x 192 records per
-// MMA tile), and a rigorous per-record bound turns it into an interval that
+// MMA), and a rigorous per-record bound turns it into an interval that
 // provably contains the exact f32 score:
 //
 //   |dot_tc - dot_exact| <= beta_r = eps * |q| * |x_r| + small absolute terms
@@ -30,16 +30,19 @@
 // with s = 2^-e a power of two that keeps every |B'| below 2^14.  The query
 // tile carries an extra column of -1 (pass 1) or +1 (pass 2), so the MMA
 // itself yields s * (lower or upper bound of the exact score): the epilogue
-// only takes maxima or compares.  Tiles of 192 records stream in by TMA
-// (128-byte swizzle for the main rows, 32-byte for the extra slice).
+// only takes maxima or compares.  Record tiles stream in by TMA (128-byte
+// swizzle for the main rows, 32-byte for the extra slice).
 //
-// CTA = one unit of 128 queries x a record range.  Warp roles:
+// CTA = one unit of 128 queries x a record range, streaming 192-record
+// tiles.  Warp roles:
 //   warps 0-7  epilogue: warp w reads TMEM lane quarter w % 4 (thread =
 //              query) and column half w / 4 (96 records) of each tile
 //   warp 8     TMEM allocation; lane 0 issues the MMAs
 //   warp 9     lane 0 issues the TMA loads
-// Three shared-memory stages and two TMEM accumulators (2 x 192 columns)
-// are handed over with mbarriers; every wait is bounded.
+// The query tile (A) sits in TMEM (default; the MMA reads it there) or in
+// shared memory.  Four (three) shared-memory stages and two TMEM
+// accumulators of 192 columns are handed over with mbarriers; every wait is
+// bounded.
 #include <cuda.h>
 
 #include "uv_kernels.h"
@@ -49,27 +52,65 @@ namespace uvb {
 
 namespace {
 
-constexpr int TC_M = 128;      // queries per unit
-constexpr int TC_N = 192;      // records per MMA tile
+constexpr int TC_M = 128;      // queries per MMA (TMEM lanes)
 constexpr int TC_D = 128;      // coordinates (K) of the main rows
 constexpr int TC_X = 16;       // the extra K slice (bound constant + zeros)
-constexpr int TC_STAGES = 3;
 constexpr int TC_THREADS = 320;
 constexpr uint32_t kWaitLimit = 1u << 20;
 
-struct TcLayout {
-  static constexpr int a_bytes = TC_M * TC_D * 2;             // 32 KB
-  static constexpr int ax_bytes = TC_M * TC_X * 2;            // 4 KB
-  static constexpr int bm_bytes = TC_N * 128;                 // one main atom column
-  static constexpr int b_bytes = 2 * bm_bytes + TC_N * TC_X * 2;  // 54 KB per stage
+// CTA shapes.  S = 1: the queries (A) in shared memory, three stages.
+// S = 3 (the default): A held in TMEM next to the accumulators (tcgen05.mma
+// reads A from TMEM and B from shared memory), which takes A's reads off the
+// shared-memory port the MMAs and the TMA writes share and frees its 36 KB
+// for a fourth stage.  TMEM: two accumulators of 192 columns (+ 72 columns
+// of A for S = 3).
+template <int S>
+struct TcShape {
+  static constexpr bool A_TMEM = S == 3;
+  static constexpr int TN = 192;                       // records per tile
+  static constexpr int STAGES = A_TMEM ? 4 : 3;
+  static constexpr int CW = TN / 2;                    // accumulator columns per epilogue warp
+  static constexpr int NL = CW / 32;                   // 32-column TMEM loads per warp
+  static constexpr int a_tile = A_TMEM ? 0 : TC_M * TC_D * 2;   // 32 KB
+  static constexpr int ax_tile = A_TMEM ? 0 : TC_M * TC_X * 2;  // 4 KB
+  static constexpr int bm_bytes = TN * 128;            // one 64-wide atom column of records
+  static constexpr int b_bytes = 2 * bm_bytes + TN * TC_X * 2;
   static constexpr int a = 0;
-  static constexpr int ax = a + a_bytes;
-  static constexpr int b = ax + ax_bytes;
-  static constexpr int bars = b + TC_STAGES * b_bytes;        // 10 mbarriers
-  static constexpr int misc = bars + 16 * 8;                  // tmem base, abort flag
+  static constexpr int ax = a + a_tile;
+  static constexpr int b = ax + ax_tile;
+  static constexpr int bars = b + STAGES * b_bytes;   // 2 * STAGES + 4 mbarriers
+  static constexpr int misc = bars + 16 * 8;          // tmem base, abort flag
   static constexpr int total = misc + 64;
+  static constexpr uint32_t a_col = 2 * TN;           // first TMEM column of A (S = 3)
 };
-static_assert(TcLayout::b % 1024 == 0 && TcLayout::b_bytes % 1024 == 0, "stage alignment");
+static_assert(TcShape<1>::b % 1024 == 0 && TcShape<1>::b_bytes % 1024 == 0, "stage alignment");
+static_assert(TcShape<3>::b % 1024 == 0 && TcShape<3>::b_bytes % 1024 == 0, "stage alignment");
+static_assert(TcShape<1>::total <= 227 * 1024 && TcShape<3>::total <= 227 * 1024, "shared memory");
+static_assert(TcShape<3>::a_col + (TC_D + TC_X) / 2 <= 512, "TMEM columns");
+
+// registers -> TMEM: 32 lanes x 8 columns
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&w)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+               "r"(w[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// D (+)= A B with A in TMEM (row i in lane i, K pairs packed low-first in
+// 32-bit columns) and B by shared-memory descriptor
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      :
+      : "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // 3-input maximum (NaN-ignoring like fmaxf)
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -80,18 +121,19 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 
 }  // namespace
 
-template <int MODE>
+template <int MODE, int S>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap_main,
                    const __grid_constant__ CUtensorMap tmap_ext) {
-  using L = TcLayout;
+  using L = TcShape<S>;
+  constexpr int TN = L::TN, STAGES = L::STAGES, NL = L::NL;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t *sa = sm + L::a;
   uint8_t *sax = sm + L::ax;
-  uint64_t *full = (uint64_t *)(sm + L::bars);  // [3]
-  uint64_t *empty = full + 3;                   // [3]
-  uint64_t *accf = full + 6;                    // [2]
-  uint64_t *acce = full + 8;                    // [2]
+  uint64_t *full = (uint64_t *)(sm + L::bars);  // [STAGES]
+  uint64_t *empty = full + STAGES;              // [STAGES]
+  uint64_t *accf = empty + STAGES;              // [2]
+  uint64_t *acce = accf + 2;                    // [2]
   uint32_t *tbase_s = (uint32_t *)(sm + L::misc);
   volatile int *abort_s = (volatile int *)(sm + L::misc + 4);
 
@@ -103,40 +145,70 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   // ---- setup: barriers, TMEM, query tile ----
   if (tid == 0) {
-    for (int s = 0; s < TC_STAGES; s++) {
+    for (int s = 0; s < STAGES; s++) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; a++) {
       tc::mbar_init(&accf[a], 1);
-      tc::mbar_init(&acce[a], 256);
+      tc::mbar_init(&acce[a], 8);  // one arrival per epilogue warp
     }
     *abort_s = 0;
     tc::mbar_fence_init();
   }
   if (warp == 8) tc::tmem_alloc(tbase_s, 512);
-  // queries -> fp16, swizzled K-major (zeros past nq and for degenerate rows)
-  for (int e = tid; e < TC_M * (TC_D / 8); e += TC_THREADS) {
-    const int r = e / (TC_D / 8), c = e - r * (TC_D / 8);
-    const int64_t q = q0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (q < p.nq && !p.degenerate[q]) {
-      const float4 *src = (const float4 *)(p.q_r + q * (int64_t)p.q_stride + c * 8);
-      const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
-      __half2 h0 = __floats2half2_rn(x0.x, x0.y), h1 = __floats2half2_rn(x0.z, x0.w);
-      __half2 h2 = __floats2half2_rn(x1.x, x1.y), h3 = __floats2half2_rn(x1.z, x1.w);
-      v = make_uint4(*(uint32_t *)&h0, *(uint32_t *)&h1, *(uint32_t *)&h2, *(uint32_t *)&h3);
+  if constexpr (L::A_TMEM) {
+    // queries -> fp16 rows in TMEM: warp w < 4 writes lanes 32w..32w+31, one
+    // query per lane; 64 columns of coordinate pairs, then the extra slice
+    // (-1 or +1, then zeros) in 8 more
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp < 4) {
+      const int64_t q = q0 + warp * 32 + lane;
+      const bool ok = q < p.nq && !p.degenerate[q];
+      const float *src = p.q_r + (ok ? q : 0) * (int64_t)p.q_stride;
+      const uint32_t ta = *tbase_s + ((uint32_t)(warp * 32) << 16) + L::a_col;
+#pragma unroll
+      for (int g = 0; g < TC_D / 16; g++) {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float2 x = ok ? __ldg((const float2 *)(src + 16 * g + 2 * j)) : make_float2(0.f, 0.f);
+          const __half2 h = __floats2half2_rn(x.x, x.y);  // .x in the low half
+          w[j] = *(const uint32_t *)&h;
+        }
+        tmem_st8(ta + 8 * g, w);
+      }
+      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (ok) w[0] = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
+      tmem_st8(ta + TC_D / 2, w);
+      tmem_st_wait();
     }
-    *(uint4 *)(sa + tc::sw128_chunk_offset(r, c, TC_M)) = v;
-  }
-  // the extra slice: -1 (lower bounds) or +1 (upper bounds) against C'
-  for (int e = tid; e < TC_M * 2; e += TC_THREADS) {
-    const int r = e >> 1, c = e & 1;
-    const int64_t q = q0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (c == 0 && q < p.nq && !p.degenerate[q])
-      v.x = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
-    *(uint4 *)(sax + tc::sw32_chunk_offset(r, c)) = v;
+  } else {
+    // queries -> fp16, swizzled K-major (zeros past nq and for degenerate rows)
+    for (int e = tid; e < TC_M * (TC_D / 8); e += TC_THREADS) {
+      const int r = e / (TC_D / 8), c = e - r * (TC_D / 8);
+      const int64_t q = q0 + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (q < p.nq && !p.degenerate[q]) {
+        const float4 *src = (const float4 *)(p.q_r + q * (int64_t)p.q_stride + c * 8);
+        const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
+        __half2 h0 = __floats2half2_rn(x0.x, x0.y), h1 = __floats2half2_rn(x0.z, x0.w);
+        __half2 h2 = __floats2half2_rn(x1.x, x1.y), h3 = __floats2half2_rn(x1.z, x1.w);
+        v = make_uint4(*(uint32_t *)&h0, *(uint32_t *)&h1, *(uint32_t *)&h2, *(uint32_t *)&h3);
+      }
+      *(uint4 *)(sa + tc::sw128_chunk_offset(r, c, TC_M)) = v;
+    }
+    // the extra slice: -1 (lower bounds) or +1 (upper bounds) against C'
+    for (int e = tid; e < TC_M * 2; e += TC_THREADS) {
+      const int r = e >> 1, c = e & 1;
+      const int64_t q = q0 + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (c == 0 && q < p.nq && !p.degenerate[q])
+        v.x = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
+      *(uint4 *)(sax + tc::sw32_chunk_offset(r, c)) = v;
+    }
   }
   tc::fence_async_smem();
   tc::tc_fence_before();
@@ -146,68 +218,79 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp < 8) {
     // ================= epilogue =================
+    // warp w: TMEM lane quarter w % 4 (thread = query), column half w / 4
     const int quarter = warp & 3, half = warp >> 2;
     const int64_t q = q0 + quarter * 32 + lane;
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
-    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 96);
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * L::CW);
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
       const int64_t tile = t_begin + it;
-      const int64_t rec0 = tile * TC_N + half * 96;
+      const int64_t rec0 = tile * TN + half * L::CW;
       if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
       }
       if (*abort_s) break;
       tc::tc_fence_after();
-      const uint32_t base = lane_base + (uint32_t)(a * TC_N);
-      uint32_t r0[32], r1[32], r2[32];
-      tc::tmem_ld32(base, r0);
-      tc::tmem_ld32(base + 32, r1);
-      tc::tmem_ld32(base + 64, r2);
+      const uint32_t base = lane_base + (uint32_t)(a * TN);
+      uint32_t r[NL][32];
+#pragma unroll
+      for (int l = 0; l < NL; l++) tc::tmem_ld32(base + 32 * l, r[l]);
       tc::tmem_ld_wait();
       tc::tc_fence_before();
-      tc::mbar_arrive(&acce[a]);  // the accumulator is in registers
-      auto cmax = [](const uint32_t(&r)[32]) {
-        float m = max3(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]));
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acce[a]);  // the warp's accumulator part is in registers
+      auto cmax = [](const uint32_t(&v)[32]) {
+        float m = max3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
 #pragma unroll
         for (int j = 3; j < 31; j += 2)
-          m = max3(m, __uint_as_float(r[j]), __uint_as_float(r[j + 1]));
-        return fmaxf(m, __uint_as_float(r[31]));
+          m = max3(m, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+        return fmaxf(m, __uint_as_float(v[31]));
       };
-      const float m0 = cmax(r0), m1 = cmax(r1), m2 = cmax(r2);
-      if (MODE == 1) {
-        if (q < p.nq)
-          p.tmax[q * p.n_groups + 2 * tile + half] = qok ? max3(m0, m1, m2) : -INFINITY;
-      } else if (qok && !(max3(m0, m1, m2) < theta)) {
-        // rare: every record of the half tile that can reach theta
-        auto cmask = [&](const uint32_t(&r)[32]) {
-          uint32_t mk = 0;
+      float mc[NL];
 #pragma unroll
-          for (int j = 0; j < 32; j++) mk |= (!(__uint_as_float(r[j]) < theta) ? 1u : 0u) << j;
-          return mk;
-        };
-        uint32_t mask[3] = {cmask(r0), cmask(r1), cmask(r2)};
-        if (rec0 + 96 > p.n) {
+      for (int l = 0; l < NL; l++) mc[l] = cmax(r[l]);
+      float m = mc[0];
+#pragma unroll
+      for (int l = 1; l < NL; l++) m = fmaxf(m, mc[l]);
+      if (MODE == 1) {
+        if (q < p.nq) p.tmax[q * p.n_groups + 2 * tile + half] = qok ? m : -INFINITY;
+      } else if (qok && !(m < theta)) {
+        // rare: every record of the chunks whose maximum reaches theta
+        uint32_t mask[NL];
+#pragma unroll
+        for (int l = 0; l < NL; l++) {
+          uint32_t mk = 0;
+          if (!(mc[l] < theta)) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              mk |= (!(__uint_as_float(r[l][j]) < theta) ? 1u : 0u) << j;
+          }
+          mask[l] = mk;
+        }
+        if (rec0 + L::CW > p.n) {
           const int64_t lim = p.n - rec0;  // records past n are padding
 #pragma unroll
-          for (int c = 0; c < 3; c++) {
-            const int64_t room = lim - 32 * c;
-            mask[c] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
+          for (int l = 0; l < NL; l++) {
+            const int64_t room = lim - 32 * l;
+            mask[l] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
           }
         }
-        const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]);
+        int cnt = 0;
+#pragma unroll
+        for (int l = 0; l < NL; l++) cnt += __popc(mask[l]);
         if (cnt > 0) {
           int pos = atomicAdd(&p.cand_cnt[q], cnt);
           uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
 #pragma unroll
-          for (int c = 0; c < 3; c++) {
-            uint32_t mk = mask[c];
+          for (int l = 0; l < NL; l++) {
+            uint32_t mk = mask[l];
             while (mk != 0u) {
               const int j = __ffs(mk) - 1;
               mk &= mk - 1u;
-              if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * c + j);
+              if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * l + j);
               pos++;
             }
           }
@@ -217,11 +300,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == 8) {
     if (lane == 0) {
       // ================= MMA issue =================
-      const uint32_t idesc = tc::idesc_f16_f32(TC_M, TC_N);
-      const uint32_t a_base = tc::smem_u32(sa), ax_base = tc::smem_u32(sax);
+      const uint32_t idesc = tc::idesc_f16_f32(TC_M, TN);
       for (int it = 0; it < ntiles; it++) {
-        const int s = it % TC_STAGES, a = it & 1;
-        if (!tc::mbar_wait(&full[s], (it / TC_STAGES) & 1, kWaitLimit) ||
+        const int s = it % STAGES, a = it & 1;
+        if (!tc::mbar_wait(&full[s], (it / STAGES) & 1, kWaitLimit) ||
             !tc::mbar_wait(&acce[a], ((it >> 1) & 1) ^ 1, kWaitLimit)) {
           *abort_s = 1;
           atomicExch(p.err, 1);
@@ -229,15 +311,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (*abort_s) break;
         tc::tc_fence_after();
         const uint32_t b_base = tc::smem_u32(sm + L::b + s * L::b_bytes);
-        const uint32_t d = tmem + (uint32_t)(a * TC_N);
+        const uint32_t d = tmem + (uint32_t)(a * TN);
+        if constexpr (L::A_TMEM) {
+          const uint32_t at = tmem + L::a_col;
 #pragma unroll
-        for (int k = 0; k < TC_D / 16; k++) {
-          const uint32_t off = (uint32_t)((k & 3) * 32);  // 16 fp16 = 32 B per K step
-          const uint64_t ad = tc::sw128_desc(a_base + (k >> 2) * TC_M * 128 + off);
-          const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
-          tc::mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
+          for (int k = 0; k < TC_D / 16; k++) {
+            const uint32_t off = (uint32_t)((k & 3) * 32);  // 16 fp16 = 32 B per K step
+            const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
+            mma_f16_ts(d, at + 8 * k, bd, idesc, k > 0 ? 1u : 0u);
+          }
+          mma_f16_ts(d, at + TC_D / 2, tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc, 1u);
+        } else {
+          const uint32_t a_base = tc::smem_u32(sa), ax_base = tc::smem_u32(sax);
+#pragma unroll
+          for (int k = 0; k < TC_D / 16; k++) {
+            const uint32_t off = (uint32_t)((k & 3) * 32);
+            const uint64_t ad = tc::sw128_desc(a_base + (k >> 2) * TC_M * 128 + off);
+            const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
+            tc::mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
+          }
+          tc::mma_f16(d, tc::sw32_desc(ax_base), tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc,
+                      1u);
         }
-        tc::mma_f16(d, tc::sw32_desc(ax_base), tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc, 1u);
         tc::mma_commit(&empty[s]);
         tc::mma_commit(&accf[a]);
       }
@@ -245,14 +340,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (lane == 0) {
     // ================= TMA producer =================
     for (int it = 0; it < ntiles; it++) {
-      const int s = it % TC_STAGES;
-      if (!tc::mbar_wait(&empty[s], ((it / TC_STAGES) & 1) ^ 1, kWaitLimit)) {
+      const int s = it % STAGES;
+      if (!tc::mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
       }
       if (*abort_s) break;
       uint8_t *dst = sm + L::b + s * L::b_bytes;
-      const int row = (int)((t_begin + it) * TC_N);
+      const int row = (int)((t_begin + it) * TN);
       tc::mbar_arrive_expect_tx(&full[s], (uint32_t)L::b_bytes);
       tc::tma_load_2d(dst, &tmap_main, 0, row, &full[s]);
       tc::tma_load_2d(dst + L::bm_bytes, &tmap_main, 64, row, &full[s]);
@@ -497,14 +592,18 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   }
 }
 
-size_t tc_scan_smem_bytes() { return (size_t)TcLayout::total; }
+size_t tc_scan_smem_bytes(int shape) {
+  return shape == 3 ? (size_t)TcShape<3>::total : (size_t)TcShape<1>::total;
+}
 
-const void *tc_scan_kernel_ptr(int mode) {
-  return mode == 1 ? (const void *)tc_scan_kernel<1> : (const void *)tc_scan_kernel<2>;
+const void *tc_scan_kernel_ptr(int mode, int shape) {
+  if (shape == 3)
+    return mode == 1 ? (const void *)tc_scan_kernel<1, 3> : (const void *)tc_scan_kernel<2, 3>;
+  return mode == 1 ? (const void *)tc_scan_kernel<1, 1> : (const void *)tc_scan_kernel<2, 1>;
 }
 
 int tc_threads() { return TC_THREADS; }
-int tc_tile_records() { return TC_N; }
+int tc_tile_records() { return TcShape<1>::TN; }
 int tc_tile_queries() { return TC_M; }
 int tc_dim() { return TC_D; }
 

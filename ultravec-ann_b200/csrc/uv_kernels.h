@@ -246,8 +246,9 @@ constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
 
 // tcscan.cu
-const void *tc_scan_kernel_ptr(int mode);
-size_t tc_scan_smem_bytes();
+// shape 1: the queries (A) in shared memory; 3: A in TMEM (the default)
+const void *tc_scan_kernel_ptr(int mode, int shape);
+size_t tc_scan_smem_bytes(int shape);
 int tc_threads();
 int tc_tile_records();
 int tc_tile_queries();
