@@ -44,7 +44,7 @@ FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
 # (mean of pass 1, 842.9 MB, and pass 2, 344.4 MB), from the ncu capture in
 # profiles/tc_scan_kernel_1Mx1k-d128.md; a measurement of this build, not
 # recomputed at run time.
-TC_TRAFFIC_PER_LAUNCH = 593.7e6
+TC_TRAFFIC_PER_LAUNCH = 578.3e6
 
 
 def parse():
