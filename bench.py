@@ -41,7 +41,7 @@ N_BASE, N_QUERY = 1_000_000, 10_000
 K_MAIN, K_ALT = 100, 10
 FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
 # DRAM bytes (read + write) per tensor-core scan launch at the bench workload
-# (mean of pass 1, 842.9 MB, and pass 2, 344.4 MB), from the ncu capture in
+# (mean of pass 1, 828.5 MB, and pass 2, 328.0 MB), from the ncu capture in
 # profiles/tc_scan_kernel_1Mx1k-d128.md; a measurement of this build, not
 # recomputed at run time.
 TC_TRAFFIC_PER_LAUNCH = 578.3e6
