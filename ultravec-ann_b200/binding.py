@@ -171,20 +171,29 @@ def _stream(*arrays):
 
 
 class _Alloc:
-    """Output allocation in the same kind (numpy / torch-cuda) as an input."""
+    """Output allocation in the same kind (numpy / torch-cuda) as an input.
+    A pinned host tensor as input gives numpy outputs in pinned memory, so
+    the library's device-to-host copies run at full speed."""
 
     def __init__(self, like):
         self.torch_dev = None
-        if like is not None and _is_torch(like) and like.is_cuda:
-            self.torch_dev = like.device
+        self.pinned = False
+        if like is not None and _is_torch(like):
+            if like.is_cuda:
+                self.torch_dev = like.device
+            else:
+                self.pinned = like.is_pinned()
 
     def __call__(self, shape, np_dtype):
-        if self.torch_dev is None:
+        if self.torch_dev is None and not self.pinned:
             return np.zeros(shape, np_dtype)
         import torch
 
         tmap = {np.uint8: torch.uint8, np.uint32: torch.int32, np.float32: torch.float32,
                 np.int64: torch.int64, np.int32: torch.int32}
+        if self.pinned:
+            t = torch.empty(shape, dtype=tmap[np_dtype], pin_memory=True)
+            return t.numpy().view(np_dtype)
         return torch.zeros(shape, dtype=tmap[np_dtype], device=self.torch_dev)
 
 
