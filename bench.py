@@ -479,6 +479,7 @@ def run_secondary(args):
     """One GPU; prints one JSON line per configuration:
     wide          1M rows, d=960 padded to 1024, x_ij = U[0,1) + 0.5 j / 959,
                   b in {1, 2, 4}, M=8: encode rows/s and 1k-query top-10 MIPS
+                  (the tensor-core prefilter with K streamed in chunks)
     ivf           1M rows, d=1536 padded to 2048: 64 unit Gaussian centres +
                   0.3 N(0,1), renormalized; k-means nlist=4096 (seed 42, 5
                   rounds), centered lists, b=2, M=8; 10k-query top-10 at
@@ -523,9 +524,15 @@ def run_secondary(args):
             index.reserve(n)
             enc_ms = _timed(lambda: (index.clear(), index.add_batch(base)), 2)
             scan_ms = _timed(lambda: index.search(qs, 10, mips=True), 3)
+            uv.profile_enable(True)
+            index.search(qs, 10, mips=True)
+            torch.cuda.synchronize()
+            kern = {f: round(uv.profile_read(f)[0], 3) for f in SCAN_FAMILIES}
+            uv.profile_enable(False)
             emit("wide-1Mx1k-d1024", {"bits": bits, "mem": 8, "encode_rows_s": n / enc_ms * 1e3,
                                       "queries_s": nq / scan_ms * 1e3, "scan_ms": scan_ms,
-                                      "encode_ms": enc_ms, "k": 10, "mips": True})
+                                      "encode_ms": enc_ms, "k": 10, "mips": True,
+                                      "kernels_ms": kern})
             del index, codec
     elif args.workload == "ivf":
         n, nq, d, d_pad, nlist = 1_000_000, 10_000, 1536, 2048, 4096

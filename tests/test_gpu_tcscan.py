@@ -128,3 +128,45 @@ def test_device_tensors(uv, tc_mode):
     ids2, sc2 = index.search(queries, 10, mips=True)
     assert np.array_equal(ids.cpu().numpy(), ids2)
     assert np.array_equal(sc.cpu().numpy().view(np.uint32), sc2.view(np.uint32))
+
+
+@pytest.mark.parametrize("dim", [96, 256, 1024])
+@pytest.mark.parametrize("mips", [True, False])
+def test_wide_rows_match_oracle(oracle, uv, tc_mode, dim, mips):
+    """tcwide.cu: rows of other widths (K streamed in chunks of 64; 96 pads
+    to 128) give the oracle's ids and scores bit for bit."""
+    n, nq, k = 30_000, 32, 10
+    base = rand_rows(n, dim, 17) * np.float32(2.0)
+    base[::5] *= np.float32(0.2)
+    queries = rand_rows(nq, dim, 18)
+    queries[3] = 0.0
+    ocodec = oracle.Codec(dim, 2, 8)
+    enc = ocodec.encode_batch(base)
+    want = ocodec.search_topk(enc, queries, k, norms=oracle.l2_norms(base) if mips else None)
+    codec = uv.Codec(dim, 2, 8)
+    index = uv.Index(codec)
+    index.add_batch(base)
+    tc_mode(2)
+    got = index.search(queries, k, mips=mips)
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(got[1].view(np.uint32), want[1].view(np.uint32))
+    assert np.all(got[0][3] == -1)
+
+
+def test_wide_rows_large_match_exact_kernel(uv, tc_mode):
+    """300k rows of d = 1024 (the wide-row workload's width), top-10 and
+    top-100 MIPS: the prefilter and the exact K-chunked scan agree."""
+    import torch
+
+    dim = 1024
+    rng = np.random.default_rng(19)
+    base = torch.from_numpy(rng.random((300_000, dim), dtype=np.float32) +
+                            np.float32(0.5) * (np.arange(dim, dtype=np.float32) / np.float32(959)))
+    queries = torch.from_numpy(rng.random((200, dim), dtype=np.float32))
+    codec = uv.Codec(dim, 2, 8)
+    index = uv.Index(codec)
+    index.add_batch(base.cuda())
+    qd = queries.cuda()
+    for k in (10, 100):
+        a, b = search_both(uv, index, qd, k, True, tc_mode)
+        assert same((a[0].cpu().numpy(), a[1].cpu().numpy()), (b[0].cpu().numpy(), b[1].cpu().numpy()))

@@ -826,7 +826,13 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   const int64_t n = ix->n;
-  if (g_tc_mode == 1 || d != uvb::tc_dim() || ix->n_centroids != 0) return UV_OK;
+  if (g_tc_mode == 1 || ix->n_centroids != 0) return UV_OK;
+  // d = 128: tcscan.cu (the query tile resident for the CTA's life); any
+  // other width up to 4096: tcwide.cu (queries and records streamed in K
+  // chunks of 64)
+  const bool wide = d != uvb::tc_dim();
+  if (wide && (d % 16 != 0 || d > 4096)) return UV_OK;
+  const int kpad = (d + 63) / 64 * 64;
   const int shape = g_tc_shape == 1 ? 1 : 3;  // CTA shape (tcscan.cu)
   const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
   const int64_t n_tiles = (n + TN - 1) / TN;
@@ -843,7 +849,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int64_t n_pad = n_tiles * TN;
   uint16_t *x16 = nullptr, *xext = nullptr;
   uint32_t *gmax = nullptr;
-  UV_TRY(sc.alloc(&x16, (size_t)n_pad * d));
+  UV_TRY(sc.alloc(&x16, (size_t)n_pad * kpad));
   UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
   UV_TRY(sc.alloc(&gmax, 1));
   UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
@@ -854,6 +860,8 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     pp.bits = c->cfg.bits;
     pp.code_stride = c->code_stride;
     pp.mips = mips;
+    pp.dim = d;
+    pp.kpad = kpad;
     pp.n = n;
     pp.n_pad = n_pad;
     pp.eps = 1.5e-3;
@@ -881,8 +889,8 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     EncodeTiledFn enc = nullptr;
     UV_TRY(encode_tiled_fn(&enc));
     const cuuint32_t estride[2] = {1, 1};
-    const cuuint64_t gdim[2] = {(cuuint64_t)d, (cuuint64_t)n_pad};
-    const cuuint64_t gstride[1] = {(cuuint64_t)d * 2};
+    const cuuint64_t gdim[2] = {(cuuint64_t)kpad, (cuuint64_t)n_pad};
+    const cuuint64_t gstride[1] = {(cuuint64_t)kpad * 2};
     const cuuint32_t box[2] = {64, (cuuint32_t)TN};
     CUresult r = enc(&tmap_main, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)x16, gdim, gstride,
                      box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -896,10 +904,46 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (extra slice) failed");
   }
+  // wide rows: the queries as fp16 rows too, with maps for both extra slices
+  CUtensorMap tmap_a, tmap_ax_lo, tmap_ax_hi;
+  if (wide) {
+    const int64_t nq_pad = (nq + 127) / 128 * 128;
+    uint16_t *a16 = nullptr, *ax_lo = nullptr, *ax_hi = nullptr;
+    UV_TRY(sc.alloc(&a16, (size_t)nq_pad * kpad));
+    UV_TRY(sc.alloc(&ax_lo, (size_t)nq_pad * 16));
+    UV_TRY(sc.alloc(&ax_hi, (size_t)nq_pad * 16));
+    {
+      ProfScope ps("tc_prepare", st);
+      const int64_t chunks = nq_pad * (kpad / 8);
+      uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+          q_r, dim_pad, degen, nq, nq_pad, d, kpad, a16, ax_lo, ax_hi);
+      UV_CK(cudaGetLastError());
+    }
+    EncodeTiledFn enc = nullptr;
+    UV_TRY(encode_tiled_fn(&enc));
+    const cuuint32_t estride[2] = {1, 1};
+    const cuuint64_t gdim[2] = {(cuuint64_t)kpad, (cuuint64_t)nq_pad};
+    const cuuint64_t gstride[1] = {(cuuint64_t)kpad * 2};
+    const cuuint32_t box[2] = {64, 128};
+    CUresult r = enc(&tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)a16, gdim, gstride, box,
+                     estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (query rows) failed");
+    const cuuint64_t gdim_x[2] = {16, (cuuint64_t)nq_pad};
+    const cuuint64_t gstride_x[1] = {32};
+    const cuuint32_t box_x[2] = {16, 128};
+    for (int h = 0; h < 2; h++) {
+      r = enc(h == 0 ? &tmap_ax_lo : &tmap_ax_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+              (void *)(h == 0 ? ax_lo : ax_hi), gdim_x, gstride_x, box_x, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (query slice) failed");
+    }
+  }
   // units: query tiles x record splits, filling whole waves of one CTA per SM
-  const size_t smem = uvb::tc_scan_smem_bytes(shape);
-  const void *k1 = uvb::tc_scan_kernel_ptr(1, shape);
-  const void *k2 = uvb::tc_scan_kernel_ptr(2, shape);
+  const size_t smem = wide ? uvb::tc_wide_smem_bytes() : uvb::tc_scan_smem_bytes(shape);
+  const void *k1 = wide ? uvb::tc_wide_kernel_ptr(1) : uvb::tc_scan_kernel_ptr(1, shape);
+  const void *k2 = wide ? uvb::tc_wide_kernel_ptr(2) : uvb::tc_scan_kernel_ptr(2, shape);
   UV_CK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   UV_CK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t qtiles = (nq + TM - 1) / TM;
@@ -945,10 +989,12 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   tp.cand_cnt = cand_cnt;
   tp.err = flags;
   const dim3 grid((unsigned)qtiles, (unsigned)splits);
+  int kchunks = kpad / 64;
   {
     void *args[] = {&tp, &tmap_main, &tmap_ext};
+    void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax_lo, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass1", st);
-    UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), args, smem, st));
+    UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
   }
   {
     ProfScope ps("tc_theta", st);
@@ -957,8 +1003,9 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   }
   {
     void *args[] = {&tp, &tmap_main, &tmap_ext};
+    void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax_hi, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass2", st);
-    UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), args, smem, st));
+    UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
   }
   {
     uvb::TcRescoreParams rp;

@@ -47,6 +47,7 @@
 
 #include "uv_kernels.h"
 #include "uv_tc.cuh"
+#include "uv_tc_epilogue.cuh"
 
 namespace uvb {
 
@@ -112,12 +113,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-// 3-input maximum (NaN-ignoring like fmaxf)
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 
 }  // namespace
 
@@ -134,6 +129,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *empty = full + STAGES;              // [STAGES]
   uint64_t *accf = empty + STAGES;              // [2]
   uint64_t *acce = accf + 2;                    // [2]
+  uint64_t *drained = acce + 2;                 // MMAs done after an abort
   uint32_t *tbase_s = (uint32_t *)(sm + L::misc);
   volatile int *abort_s = (volatile int *)(sm + L::misc + 4);
 
@@ -153,6 +149,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::mbar_init(&accf[a], 1);
       tc::mbar_init(&acce[a], 8);  // one arrival per epilogue warp
     }
+    tc::mbar_init(drained, 1);
     *abort_s = 0;
     tc::mbar_fence_init();
   }
@@ -242,60 +239,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acce[a]);  // the warp's accumulator part is in registers
-      auto cmax = [](const uint32_t(&v)[32]) {
-        float m = max3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-#pragma unroll
-        for (int j = 3; j < 31; j += 2)
-          m = max3(m, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
-        return fmaxf(m, __uint_as_float(v[31]));
-      };
-      float mc[NL];
-#pragma unroll
-      for (int l = 0; l < NL; l++) mc[l] = cmax(r[l]);
-      float m = mc[0];
-#pragma unroll
-      for (int l = 1; l < NL; l++) m = fmaxf(m, mc[l]);
-      if (MODE == 1) {
-        if (q < p.nq) p.tmax[q * p.n_groups + 2 * tile + half] = qok ? m : -INFINITY;
-      } else if (qok && !(m < theta)) {
-        // rare: every record of the chunks whose maximum reaches theta
-        uint32_t mask[NL];
-#pragma unroll
-        for (int l = 0; l < NL; l++) {
-          uint32_t mk = 0;
-          if (!(mc[l] < theta)) {
-#pragma unroll
-            for (int j = 0; j < 32; j++)
-              mk |= (!(__uint_as_float(r[l][j]) < theta) ? 1u : 0u) << j;
-          }
-          mask[l] = mk;
-        }
-        if (rec0 + L::CW > p.n) {
-          const int64_t lim = p.n - rec0;  // records past n are padding
-#pragma unroll
-          for (int l = 0; l < NL; l++) {
-            const int64_t room = lim - 32 * l;
-            mask[l] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
-          }
-        }
-        int cnt = 0;
-#pragma unroll
-        for (int l = 0; l < NL; l++) cnt += __popc(mask[l]);
-        if (cnt > 0) {
-          int pos = atomicAdd(&p.cand_cnt[q], cnt);
-          uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
-#pragma unroll
-          for (int l = 0; l < NL; l++) {
-            uint32_t mk = mask[l];
-            while (mk != 0u) {
-              const int j = __ffs(mk) - 1;
-              mk &= mk - 1u;
-              if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * l + j);
-              pos++;
-            }
-          }
-        }
-      }
+      tcep::bounds_run<MODE, NL>(p, r, q, qok, theta, 2 * tile + half, rec0);
     }
   } else if (warp == 8) {
     if (lane == 0) {
@@ -336,10 +280,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc::mma_commit(&empty[s]);
         tc::mma_commit(&accf[a]);
       }
+      if (*abort_s) {  // let every issued MMA finish before TMEM is freed
+        tc::mma_commit(drained);
+        tc::mbar_wait(drained, 0, kWaitLimit);
+      }
     }
   } else if (lane == 0) {
     // ================= TMA producer =================
-    for (int it = 0; it < ntiles; it++) {
+    int64_t issued = 0;
+    for (int it = 0; it < ntiles; it++, issued++) {
       const int s = it % STAGES;
       if (!tc::mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, kWaitLimit)) {
         *abort_s = 1;
@@ -353,6 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::tma_load_2d(dst + L::bm_bytes, &tmap_main, 64, row, &full[s]);
       tc::tma_load_2d(dst + 2 * L::bm_bytes, &tmap_ext, 0, row, &full[s]);
     }
+    if (*abort_s) tc::drain_stages(full, STAGES, issued, kWaitLimit);
   }
 
   // ---- teardown: the epilogue has waited for every MMA ----
@@ -402,7 +352,7 @@ __global__ void tc_gmax_kernel(const TcPrepareParams p) {
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= p.n_pad) return;
-  uint4 *xrow = (uint4 *)(p.x16 + r * TC_D);
+  uint4 *xrow = (uint4 *)(p.x16 + r * p.kpad);
   uint4 *xext = (uint4 *)(p.xext + r * TC_X);
   const uint32_t hinf = 0x7C00u;  // fp16 +inf
   float g = r < p.n ? record_g(p, r) : 0.0f;
@@ -413,7 +363,7 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const int e = top > 0.0 ? (int)ceil(log2(top)) - 14 : 0;
   const double s = ldexp(1.0, -e);
   if (bad) {
-    for (int c = 0; c < TC_D / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
+    for (int c = 0; c < p.kpad / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
     xext[0] = make_uint4(hinf, 0, 0, 0);
     xext[1] = make_uint4(0, 0, 0, 0);
     return;
@@ -424,8 +374,12 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const int rw = p.code_stride >> 2;
   const float gs = (float)((double)g * s);  // exact: s is a power of two
   double xs = 0.0;
-  for (int c = 0; c < TC_D / 8; c++) {
+  for (int c = 0; c < p.kpad / 8; c++) {
     uint32_t o[4];
+    if (8 * c >= p.dim) {  // zero padding up to kpad
+      xrow[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
 #pragma unroll
     for (int h = 0; h < 8; h++) {
       const int i = 8 * c + h;
@@ -445,7 +399,7 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   const double qn = 1.0001;
   const double xn = sqrt(xs) * (1.0 + 1e-12);
   const double sg = s * (double)g;
-  const double cd = (sg * p.eps * qn * xn + 1.1920928955078125e-7 * sqrt((double)TC_D) *
+  const double cd = (sg * p.eps * qn * xn + 1.1920928955078125e-7 * sqrt((double)p.dim) *
                                                 (qn + sg * xn)) * (1.0 + 1e-6);
   const uint32_t hc = __half_as_ushort(__float2half_ru(__double2float_ru(cd)));
   xext[0] = make_uint4(hc, 0, 0, 0);

@@ -194,6 +194,7 @@ struct TcScanParams {
 
 struct TcPrepareParams {
   int mem, bits, code_stride, mips;
+  int dim, kpad;               // record dimension; row stride of x16 (dim rounded up to 64)
   int64_t n, n_pad;
   double eps;
   float code_absmax;           // max |code table value|
@@ -202,7 +203,7 @@ struct TcPrepareParams {
   const float *code;           // f32 code table
   const float *rescale, *rnorm, *norms;
   uint32_t *gmax_bits;         // largest finite g (zeroed before tc_gmax_kernel)
-  uint16_t *x16;               // n_pad x 128 fp16 main operand rows
+  uint16_t *x16;               // n_pad x kpad fp16 main operand rows
   uint16_t *xext;              // n_pad x 16 fp16 extra slice (bound constant)
 };
 
@@ -258,6 +259,14 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);
 __global__ void tc_rescore_kernel(const TcRescoreParams p);
+// tcwide.cu: the prefilter for rows of any width (K streamed in chunks of 64)
+const void *tc_wide_kernel_ptr(int mode);
+size_t tc_wide_smem_bytes();
+// queries -> fp16 operand rows (nq_pad x kpad) and the two extra slices
+// (-1 for lower bounds, +1 for upper bounds)
+__global__ void tc_prepare_queries_kernel(const float *q_r, int q_stride, const uint32_t *degen,
+                                          int64_t nq, int64_t nq_pad, int dim, int kpad,
+                                          uint16_t *a16, uint16_t *aext_lo, uint16_t *aext_hi);
 
 // ivf.cu
 template <int MODE>

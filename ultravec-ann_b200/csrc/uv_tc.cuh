@@ -50,6 +50,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
   return false;
 }
 
+// After an abort: wait (bounded) until the last load armed on each of the
+// `stages` barriers has landed, so that no bulk copy is still writing into
+// shared memory when the CTA exits.  `issued` = stage uses armed so far.
+__device__ __forceinline__ void drain_stages(uint64_t *full, int stages, int64_t issued,
+                                             uint32_t limit) {
+  for (int s = 0; s < stages; s++) {
+    if (issued <= s) continue;
+    const int64_t last = issued - 1 - ((issued - 1 - s) % stages);  // last use of stage s
+    for (uint32_t i = 0; i < limit; i++)
+      if (mbar_try_wait(&full[s], (uint32_t)((last / stages) & 1))) break;
+  }
+}
+
 // Arrive and add `bytes` to the transaction count the phase waits for.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),

@@ -1,0 +1,83 @@
+// uv_tc_epilogue.cuh -- the per-tile epilogue of the tensor-core prefilter
+// kernels (tcscan.cu, tcwide.cu): one thread holds one query's bounds for a
+// run of records (nl chunks of 32 accumulator columns, already in
+// registers).  Pass 1 writes the run's largest lower bound; pass 2 appends
+// every record whose upper bound reaches the query's threshold to its
+// candidate list.
+#pragma once
+
+#include "uv_kernels.h"
+
+namespace uvb {
+namespace tcep {
+
+// 3-input maximum (NaN-ignoring like fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
+  float m = max3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+#pragma unroll
+  for (int j = 3; j < 31; j += 2) m = max3(m, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+  return fmaxf(m, __uint_as_float(v[31]));
+}
+
+// r: the bounds of records rec0 .. rec0 + 32 * NL - 1 for query q; group:
+// the tile-maxima slot of this run (pass 1).
+template <int MODE, int NL>
+__device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t (&r)[NL][32],
+                                           int64_t q, bool qok, float theta, int64_t group,
+                                           int64_t rec0) {
+  float mc[NL];
+#pragma unroll
+  for (int l = 0; l < NL; l++) mc[l] = chunk_max(r[l]);
+  float m = mc[0];
+#pragma unroll
+  for (int l = 1; l < NL; l++) m = fmaxf(m, mc[l]);
+  if (MODE == 1) {
+    if (q < p.nq) p.tmax[q * p.n_groups + group] = qok ? m : -INFINITY;
+  } else if (qok && !(m < theta)) {
+    // rare: every record of the chunks whose maximum reaches theta
+    uint32_t mask[NL];
+#pragma unroll
+    for (int l = 0; l < NL; l++) {
+      uint32_t mk = 0;
+      if (!(mc[l] < theta)) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) mk |= (!(__uint_as_float(r[l][j]) < theta) ? 1u : 0u) << j;
+      }
+      mask[l] = mk;
+    }
+    if (rec0 + 32 * NL > p.n) {
+      const int64_t lim = p.n - rec0;  // records past n are padding
+#pragma unroll
+      for (int l = 0; l < NL; l++) {
+        const int64_t room = lim - 32 * l;
+        mask[l] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
+      }
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int l = 0; l < NL; l++) cnt += __popc(mask[l]);
+    if (cnt > 0) {
+      int pos = atomicAdd(&p.cand_cnt[q], cnt);
+      uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
+#pragma unroll
+      for (int l = 0; l < NL; l++) {
+        uint32_t mk = mask[l];
+        while (mk != 0u) {
+          const int j = __ffs(mk) - 1;
+          mk &= mk - 1u;
+          if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * l + j);
+          pos++;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace tcep
+}  // namespace uvb
