@@ -190,7 +190,12 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * 2 shared memory whenever one row's array fits); "tc_scan" selects the flat
  * search's tensor-core prefilter (0 automatic, 1 never, 2 wherever it is
  * built); "tc_shape" where the prefilter keeps its queries (0 automatic =
- * 3: tensor memory; 1: shared memory); "cand_kernel" selects the
+ * 3: tensor memory; 1: shared memory); "tc_cache" keeps the prefilter's
+ * fp16 record rows on the device between searches (1, the default: made on
+ * the first search after a change of the records, per score mode, and held
+ * until the next change or uv_index_destroy; (2 x dim rounded up to 64 + 32)
+ * bytes per record and mode) or makes them in per-search scratch (0);
+ * "cand_kernel" selects the
  * candidate scorer's kernel (0 automatic:
  * one thread per candidate at bits 1, 2, 4; 1 half a warp per candidate).
  * Process-wide; returns UV_EINVAL for an unknown key. */

@@ -170,3 +170,32 @@ def test_wide_rows_large_match_exact_kernel(uv, tc_mode):
     for k in (10, 100):
         a, b = search_both(uv, index, qd, k, True, tc_mode)
         assert same((a[0].cpu().numpy(), a[1].cpu().numpy()), (b[0].cpu().numpy(), b[1].cpu().numpy()))
+
+
+def test_kept_rows_follow_every_change_of_the_records(uv, tc_mode):
+    """The prefilter's record rows are kept between searches: after an add,
+    a clear and a re-add, and a switch between MIPS and cosine, every search
+    equals the exact kernel on the records the index holds at that moment,
+    and equals a search that makes its rows in scratch (tc_cache 0)."""
+    dim, nq, k = 128, 64, 20
+    queries = rand_rows(nq, dim, 41)
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    steps = [("add", rand_rows(60_000, dim, 42)), ("add", rand_rows(30_000, dim, 43) * np.float32(3)),
+             ("clear", None), ("add", rand_rows(50_000, dim, 44))]
+    try:
+        for op, rows in steps:
+            if op == "add":
+                index.add_batch(rows)
+            else:
+                index.clear()
+                continue
+            for mips in (True, False, True):
+                a, b = search_both(uv, index, queries, k, mips, tc_mode)
+                assert same(a, b)
+                tc_mode(2)
+                uv.set_tuning("tc_cache", 0)
+                c = index.search(queries, k, mips=mips)
+                uv.set_tuning("tc_cache", 1)
+                assert same(a, c)
+    finally:
+        uv.set_tuning("tc_cache", 1)

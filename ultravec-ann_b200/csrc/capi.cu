@@ -19,6 +19,7 @@ int64_t g_scan_splits = 0;
 int g_tc_mode = 0;
 int g_cand_kernel = 0;
 int g_tc_shape = 0;
+int g_tc_cache = 1;
 std::atomic<int64_t> g_tc_last_candidates{0};
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
@@ -407,6 +408,11 @@ int uv_index_destroy(uv_index *ix) {
     cudaFree(ix->ids);
     cudaFree(ix->centroids);
     cudaFree(ix->signs);
+    for (auto &t : ix->tc_rows) {
+      cudaFree(t.x16);
+      cudaFree(t.xext);
+      if (t.ready != nullptr) cudaEventDestroy(t.ready);
+    }
   }
   delete ix;
   return UV_OK;
@@ -417,6 +423,7 @@ int uv_index_set_centroids(uv_index *ix, const float *centroids, int32_t n_centr
   if (n_centroids < 0 || (n_centroids > 0 && centroids == nullptr))
     return fail(UV_EINVAL, "bad centroids");
   if (ix->n > 0) return fail(UV_EINVAL, "centroids must be set before the first add");
+  ix->version++;
   DeviceGuard g(ix->codec->cfg.device);
   cudaFree(ix->centroids);
   ix->centroids = nullptr;
@@ -471,6 +478,7 @@ int uv_index_set_shortlist(uv_index *ix, int32_t c, int32_t asym, int32_t rnorm)
 int uv_index_clear(uv_index *ix) {
   if (ix == nullptr) return fail(UV_EINVAL, "null argument");
   ix->n = 0;
+  ix->version++;
   return UV_OK;
 }
 
@@ -513,6 +521,7 @@ static int index_add_impl(uv_index *ix, const int64_t *ids, const float *rows, i
                        ix->rnorm + o, ix->cidx + o, ix->norms + o, st, sc, nullptr, nullptr,
                        nullptr, ix->sl_c > 0 ? ix->signs + o * c->sign_stride : nullptr));
   ix->n += n;
+  ix->version++;
   bool rows_dev = false;
   classify(rows, c->cfg.device, &rows_dev);
   if (!rows_dev) UV_CK(cudaStreamSynchronize(st));
@@ -845,15 +854,19 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int dim_pad = (d + 3) & ~3;
   const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
   (void)qc;
-  // fp16 operand rows with the bound constants folded in
+  // fp16 operand rows with the bound constants folded in.  By default they
+  // are made once per index version and score mode and kept (tuning key
+  // "tc_cache").  A remake after a change of the records rewrites them in
+  // place on this stream (adds do not overlap searches of the same index)
+  // and records an event that later searches on any stream wait for; the
+  // buffers are reallocated only when the index has outgrown them, after the
+  // device has drained.
   const int64_t n_pad = n_tiles * TN;
   uint16_t *x16 = nullptr, *xext = nullptr;
-  uint32_t *gmax = nullptr;
-  UV_TRY(sc.alloc(&x16, (size_t)n_pad * kpad));
-  UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
-  UV_TRY(sc.alloc(&gmax, 1));
-  UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
-  {
+  auto make_rows = [&](uint16_t *rows16, uint16_t *rows_ext) -> int {
+    uint32_t *gmax = nullptr;
+    UV_TRY(sc.alloc(&gmax, 1));
+    UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
     uvb::TcPrepareParams pp;
     std::memset(&pp, 0, sizeof(pp));
     pp.mem = c->cfg.mem;
@@ -873,14 +886,49 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     pp.rnorm = ix->rnorm;
     pp.norms = ix->norms;
     pp.gmax_bits = gmax;
-    pp.x16 = x16;
-    pp.xext = xext;
+    pp.x16 = rows16;
+    pp.xext = rows_ext;
     void *args[] = {&pp};
     ProfScope ps("tc_prepare", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
                            dim3(256), args, 0, st));
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
                            dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
+    return UV_OK;
+  };
+  if (g_tc_cache == 0) {
+    UV_TRY(sc.alloc(&x16, (size_t)n_pad * kpad));
+    UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
+    UV_TRY(make_rows(x16, xext));
+  } else {
+    std::lock_guard<std::mutex> rows_lock(ix->tc_mu);
+    TcRows &rows = ix->tc_rows[mips];
+    if (rows.version != ix->version || rows.n_pad != n_pad || rows.kpad != kpad) {
+      rows.version = ~0ull;
+      if (rows.cap < n_pad || rows.kpad != kpad) {
+        if (rows.x16 != nullptr || rows.xext != nullptr) {
+          UV_CK(cudaDeviceSynchronize());
+          cudaFree(rows.x16);
+          cudaFree(rows.xext);
+          rows.x16 = rows.xext = nullptr;
+          rows.cap = 0;
+        }
+        UV_CK(cudaMalloc((void **)&rows.x16, sizeof(uint16_t) * (size_t)n_pad * kpad));
+        UV_CK(cudaMalloc((void **)&rows.xext, sizeof(uint16_t) * (size_t)n_pad * 16));
+        rows.cap = n_pad;
+        rows.kpad = kpad;
+      }
+      UV_TRY(make_rows(rows.x16, rows.xext));
+      if (rows.ready == nullptr)
+        UV_CK(cudaEventCreateWithFlags(&rows.ready, cudaEventDisableTiming));
+      UV_CK(cudaEventRecord(rows.ready, st));
+      rows.n_pad = n_pad;
+      rows.version = ix->version;
+    } else {
+      UV_CK(cudaStreamWaitEvent(st, rows.ready, 0));
+    }
+    x16 = rows.x16;
+    xext = rows.xext;
   }
   // TMA maps: main rows of 128 fp16 (boxes of 64 x TN, 128-byte swizzle) and
   // the extra slice of 16 fp16 (boxes of 16 x TN, 32-byte swizzle)
@@ -1186,6 +1234,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_shape") == 0) {
     if (value != 0 && value != 1 && value != 3) return fail(UV_EINVAL, "tc_shape must be 0, 1 or 3");
     g_tc_shape = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "tc_cache") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_cache must be 0 or 1");
+    g_tc_cache = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "cand_kernel") == 0) {

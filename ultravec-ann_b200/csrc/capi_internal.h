@@ -157,6 +157,7 @@ extern int64_t g_scan_splits;  // uv_set_tuning("scan_splits")
 extern int g_tc_mode;          // uv_set_tuning("tc_scan")
 extern int g_cand_kernel;      // uv_set_tuning("cand_kernel")
 extern int g_tc_shape;         // uv_set_tuning("tc_shape")
+extern int g_tc_cache;         // uv_set_tuning("tc_cache")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 
@@ -229,9 +230,24 @@ struct uv_ivf {
   uint8_t *signs = nullptr;                  // n x sign_stride when the shortlist is on
 };
 
+// The tensor-core prefilter's fp16 operand rows (tcscan.cu / tcwide.cu),
+// kept between searches: one set per score mode (the MIPS rows carry the row
+// norm), rebuilt when the index has changed since they were made.
+struct TcRows {
+  uint16_t *x16 = nullptr;      // cap x kpad
+  uint16_t *xext = nullptr;     // cap x 16
+  int64_t cap = 0, n_pad = 0;   // rows allocated / rows made
+  int kpad = 0;
+  uint64_t version = ~0ull;     // index version the rows were made from
+  cudaEvent_t ready = nullptr;  // recorded after the rows were made
+};
+
 struct uv_index {
   const uv_codec *codec = nullptr;
   int device = 0;              // destroy reads this, not the codec (which may be gone)
+  uint64_t version = 0;        // bumped by every change of the records
+  mutable std::mutex tc_mu;    // guards tc_rows
+  mutable TcRows tc_rows[2];   // [mips]
   int64_t n = 0, cap = 0;
   uint8_t *codes = nullptr;
   uint32_t *start = nullptr;
