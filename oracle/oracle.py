@@ -24,6 +24,8 @@ _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+_i16p = np.ctypeslib.ndpointer(np.int16, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
 _vp = C.c_void_p
 
 
@@ -57,6 +59,29 @@ def lib():
             "uvo_codec_new": (_vp, [C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_int, C.c_int,
                                     C.c_int, C.c_float]),
             "uvo_codec_free": (None, [_vp]),
+            "uvo_e8_key": (C.c_uint64, [_i16p]),
+            "uvo_e8_unkey": (None, [C.c_uint64, _i16p]),
+            "uvo_coset_of": (C.c_int, [_i16p]),
+            "uvo_e8_nearest": (None, [_f32p, _f32p]),
+            "uvo_e8_enumerate": (C.c_int64, [C.c_float, _vp, C.c_int64]),
+            "uvo_coset_new": (_vp, [C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_int]),
+            "uvo_coset_free": (None, [_vp]),
+            "uvo_coset_set_centroids": (C.c_int, [_vp, _f32p, C.c_int]),
+            "uvo_coset_per_coset": (C.c_int, [_vp]),
+            "uvo_coset_code_len": (C.c_int, [_vp]),
+            "uvo_coset_books": (None, [_vp, _u64p]),
+            "uvo_coset_scale": (None, [_vp, _f32p]),
+            "uvo_coset_index": (C.c_int64, [_vp, C.c_int, _i16p]),
+            "uvo_coset_nearest": (None, [_vp, C.c_int, _f32p, C.POINTER(C.c_int64),
+                                         C.POINTER(C.c_float)]),
+            "uvo_coset_nearest_exhaustive": (None, [_vp, C.c_int, _f32p, C.POINTER(C.c_int64),
+                                                    C.POINTER(C.c_float)]),
+            "uvo_coset_encode_batch": (None, [_vp, _f32p, C.c_int64, _u8p, _f32p, _f32p, _u32p]),
+            "uvo_coset_decode": (None, [_vp, _u8p, _f32p]),
+            "uvo_coset_reconstruct_unit": (None, [_vp, _f32p, _f32p]),
+            "uvo_coset_search": (None, [_vp, _u8p, _f32p, _f32p, _u32p, _vp, C.c_int64, _f32p,
+                                        C.c_int64, C.c_int, _i64p, _f32p]),
+            "uvo_coset_mem_bytes": (C.c_int64, [_vp, C.c_int64]),
             "uvo_codec_set_centroids": (C.c_int, [_vp, _f32p, C.c_int]),
             "uvo_codec_code_bytes": (C.c_int, [_vp]),
             "uvo_codec_table_len": (C.c_int, [_vp]),
@@ -477,3 +502,127 @@ def rand_unit(n, dim, seed):
 
 def threads_available() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+# ---------------------------------------------------------------------------
+# Coset trellis (src/coset_trellis.rs, src/e8.rs)
+# ---------------------------------------------------------------------------
+def e8_key(r):
+    return int(lib().uvo_e8_key(np.ascontiguousarray(r, np.int16)))
+
+
+def e8_unkey(key):
+    out = np.empty(8, np.int16)
+    lib().uvo_e8_unkey(C.c_uint64(int(key)), out)
+    return out
+
+
+def coset_of(r):
+    """coset_trellis.rs:73-79"""
+    return int(lib().uvo_coset_of(np.ascontiguousarray(r, np.int16)))
+
+
+def e8_nearest(y):
+    """e8.rs:37-51"""
+    out = np.empty(8, np.float32)
+    lib().uvo_e8_nearest(np.ascontiguousarray(y, np.float32), out)
+    return out
+
+
+def e8_enumerate(r2_max):
+    """e8.rs:82-92: every E8 point with |x|^2 <= r2_max, raw doubled coords."""
+    n = lib().uvo_e8_enumerate(C.c_float(r2_max), None, 0)
+    keys = np.empty(n, np.uint64)
+    lib().uvo_e8_enumerate(C.c_float(r2_max), keys.ctypes.data, n)
+    out = np.empty((n, 8), np.int16)
+    for i, k in enumerate(keys):
+        out[i] = e8_unkey(k)
+    return out
+
+
+class Coset:
+    """CosetTrellis (coset_trellis.rs:98-190): dim % 8 == 0, bits 1..3, the
+    reference defaults mem 12, rotation seed 42 and 3 rounds."""
+
+    def __init__(self, dim, bits, mem=12, seed=42, rounds=3, centroids=None):
+        self.dim, self.bits, self.mem = dim, bits, mem
+        self.h = lib().uvo_coset_new(dim, bits, mem, seed, rounds)
+        if not self.h:
+            raise ValueError("unsupported coset trellis configuration")
+        self.per_coset = lib().uvo_coset_per_coset(self.h)
+        self.code_len = lib().uvo_coset_code_len(self.h)
+        self.m_bits = 8 * bits - 3
+        self.n_centroids = 0
+        if centroids is not None:
+            cen = np.ascontiguousarray(centroids, dtype=np.float32)
+            lib().uvo_coset_set_centroids(self.h, cen, cen.shape[0])
+            self.n_centroids = cen.shape[0]
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                lib().uvo_coset_free(self.h)
+        except Exception:
+            pass
+
+    def books(self):
+        """8 x per_coset keys (norm << 40 | offset coordinates)."""
+        out = np.empty(8 * self.per_coset, np.uint64)
+        lib().uvo_coset_books(self.h, out)
+        return out.reshape(8, self.per_coset)
+
+    def book_points(self, k):
+        keys = self.books()[k]
+        sh = np.array([35, 30, 25, 20, 15, 10, 5, 0], np.uint64)
+        return (((keys[:, None] >> sh[None, :]) & np.uint64(31)).astype(np.int16) - 16)
+
+    def scale(self):
+        out = np.empty(2, np.float32)
+        lib().uvo_coset_scale(self.h, out)
+        return float(out[0]), float(out[1])
+
+    def index(self, k, r):
+        return int(lib().uvo_coset_index(self.h, k, np.ascontiguousarray(r, np.int16)))
+
+    def nearest(self, k, y, exhaustive=False):
+        i, d = C.c_int64(), C.c_float()
+        fn = lib().uvo_coset_nearest_exhaustive if exhaustive else lib().uvo_coset_nearest
+        fn(self.h, k, np.ascontiguousarray(y, np.float32), C.byref(i), C.byref(d))
+        return i.value, d.value
+
+    def encode_batch(self, rows):
+        rows = np.ascontiguousarray(rows, np.float32)
+        n = rows.shape[0]
+        codes = np.zeros((n, self.code_len), np.uint8)
+        rescale = np.empty(n, np.float32)
+        rnorm = np.empty(n, np.float32)
+        cidx = np.empty(n, np.uint32)
+        lib().uvo_coset_encode_batch(self.h, rows, n, codes, rescale, rnorm, cidx)
+        return {"codes": codes, "rescale": rescale, "rnorm": rnorm, "cidx": cidx}
+
+    def decode(self, rec):
+        out = np.empty(self.dim, np.float32)
+        lib().uvo_coset_decode(self.h, np.ascontiguousarray(rec, np.uint8), out)
+        return out
+
+    def reconstruct_unit(self, row):
+        out = np.empty(self.dim, np.float32)
+        lib().uvo_coset_reconstruct_unit(self.h, np.ascontiguousarray(row, np.float32), out)
+        return out
+
+    def search(self, enc, queries, k, ids=None):
+        queries = np.ascontiguousarray(queries, np.float32)
+        nq = queries.shape[0]
+        n = enc["codes"].shape[0]
+        out_ids = np.empty((nq, k), np.int64)
+        out_sc = np.empty((nq, k), np.float32)
+        ids_arr = None if ids is None else np.ascontiguousarray(ids, np.int64)
+        lib().uvo_coset_search(self.h, np.ascontiguousarray(enc["codes"]), enc["rescale"],
+                               enc["rnorm"], enc["cidx"],
+                               None if ids_arr is None else ids_arr.ctypes.data, n, queries,
+                               nq, k, out_ids, out_sc)
+        return out_ids, out_sc
+
+    def mem_bytes(self, n):
+        return int(lib().uvo_coset_mem_bytes(self.h, n))
+

@@ -140,6 +140,34 @@ void uvo_ivf_search_rerank(const uvo_codec *c, const float *centroids, int nlist
 /* synthetic inputs used by the reference's own tests (trellis.rs:2387-2403) */
 void uvo_rand_unit(int64_t n, int dim, uint64_t seed, float *out);
 
+/* --- coset trellis (coset_trellis.rs, e8.rs): uv_oracle_coset.c --- */
+typedef struct uvo_coset uvo_coset;
+uint64_t uvo_e8_key(const int16_t *r);
+void uvo_e8_unkey(uint64_t key, int16_t *r);
+int uvo_coset_of(const int16_t *r);
+void uvo_e8_nearest(const float *y, float *out);
+int64_t uvo_e8_enumerate(float r2_max, uint64_t *keys, int64_t cap);
+uvo_coset *uvo_coset_new(int dim, int bits, int mem, uint64_t seed, int rounds);
+void uvo_coset_free(uvo_coset *c);
+int uvo_coset_set_centroids(uvo_coset *c, const float *centroids, int n_centroids);
+int uvo_coset_per_coset(const uvo_coset *c);
+int uvo_coset_code_len(const uvo_coset *c);
+void uvo_coset_books(const uvo_coset *c, uint64_t *out);
+void uvo_coset_scale(const uvo_coset *c, float *out);
+int64_t uvo_coset_index(const uvo_coset *c, int k, const int16_t *r);
+void uvo_coset_nearest(const uvo_coset *c, int k, const float *y, int64_t *idx, float *dist);
+void uvo_coset_nearest_exhaustive(const uvo_coset *c, int k, const float *y, int64_t *idx,
+                                  float *dist);
+void uvo_coset_encode_batch(const uvo_coset *c, const float *rows, int64_t n, uint8_t *codes,
+                            float *rescale, float *rnorm, uint32_t *cidx);
+void uvo_coset_decode(const uvo_coset *c, const uint8_t *rec, float *xbar);
+void uvo_coset_reconstruct_unit(const uvo_coset *c, const float *row, float *out);
+void uvo_coset_search(const uvo_coset *c, const uint8_t *codes, const float *rescale,
+                      const float *rnorm, const uint32_t *cidx, const int64_t *ids, int64_t n,
+                      const float *queries, int64_t nq, int k, int64_t *out_ids,
+                      float *out_scores);
+int64_t uvo_coset_mem_bytes(const uvo_coset *c, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif
