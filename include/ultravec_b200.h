@@ -355,6 +355,51 @@ int uv_index_load(const uv_codec *codec, const char *path, uv_index **out);
 int uv_ivf_save(const uv_ivf *ivf, const char *path);
 int uv_ivf_load(const uv_codec *codec, const char *path, uv_ivf **out);
 
+/* ---- coset trellis (src/coset_trellis.rs) ------------------------------ */
+
+/* The reference's research arm behind ULTRAVEC_COSET_TRELLIS=1: trellis-coded
+ * quantization over the eight cosets of an index-8 sublattice of E8, one
+ * 8-wide block per step, 2 branch bits + (8*bits - 3) book-index bits per
+ * block, a free-start Viterbi over 2^mem states with 4 branches each.
+ * One handle is the whole CosetTrellis backend (codec + entries). */
+typedef struct uv_coset uv_coset;
+
+/* CosetTrellis::new (coset_trellis.rs:121-190): dim % 8 == 0 and bits 1..3
+ * (UV_EINVAL otherwise, where the reference panics); mem 1..20 (the
+ * reference reads ULTRAVEC_TRELLIS_MEM, default 12); the rotation as
+ * Rotor::new_oblivious (seed 42, 3 rounds by default).  The books of a bit
+ * width are built once per process (three bits: 2^24 points, seconds). */
+int uv_coset_create(int32_t dim, int32_t bits, int32_t mem, uint64_t rotation_seed,
+                    int32_t rotation_rounds, int32_t device, uv_coset **out);
+int uv_coset_destroy(uv_coset *coset);
+/* with_centroids (192-196); before the first add. */
+int uv_coset_set_centroids(uv_coset *coset, const float *centroids, int32_t n_centroids);
+/* add (ids given) / add_batch (ids NULL: the batch's positions 0..n-1, as
+ * the reference's add_batch assigns them, 454-469).  Rows n x dim f32. */
+int uv_coset_add(uv_coset *coset, const int64_t *ids, const float *rows, int64_t n,
+                 void *stream);
+/* search (471-497), k 1..128: score = <q,c> + rnorm * dot(q_r, x-bar) /
+ * rescale, descending, ties by insertion position; slots past len() hold id
+ * -1 and score -inf.  Host or device buffers. */
+int uv_coset_search(const uv_coset *coset, const float *queries, int64_t nq, int32_t k,
+                    int64_t *ids_out, float *scores_out, void *stream);
+int uv_coset_len(const uv_coset *coset, int64_t *n);
+/* bytes per record as stored by the reference (start state + packed
+ * symbols) and points per coset book */
+int uv_coset_shape(const uv_coset *coset, int32_t *code_len, int32_t *per_coset);
+/* the books (8 x per_coset keys: norm << 40 | raw doubled coordinates + 16,
+ * five bits each, first coordinate highest) and {mean, std}; host memory */
+int uv_coset_books(const uv_coset *coset, uint64_t *keys, float *scale);
+/* mem_bytes (498-504) and memory_breakdown().model_bytes (505-517) */
+int uv_coset_mem_bytes(const uv_coset *coset, int64_t *bytes);
+int uv_coset_model_bytes(const uv_coset *coset, int64_t *bytes);
+/* the records: n x code_len bytes, rescale, rnorm, cidx, ids (NULL skips) */
+int uv_coset_export(const uv_coset *coset, uint8_t *codes, float *rescale, float *rnorm,
+                    uint32_t *cidx, int64_t *ids, void *stream);
+/* reconstruct_unit (521-529) of n rows, n x dim in and out */
+int uv_coset_reconstruct(const uv_coset *coset, const float *rows, int64_t n, float *out,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,7 +37,9 @@ SYMBOLS = [
     "uv_ivf_save", "uv_ivf_load", "uv_index_prepare", "uv_prepared_destroy", "uv_prepared_len",
     "uv_prepared_score", "uv_index_score_candidates", "uv_index_scorer_model_bytes",
     "uv_index_set_shortlist", "uv_index_export_signs", "uv_ivf_set_shortlist",
-    "uv_ivf_export_signs",
+    "uv_ivf_export_signs", "uv_coset_create", "uv_coset_destroy", "uv_coset_set_centroids",
+    "uv_coset_add", "uv_coset_search", "uv_coset_len", "uv_coset_shape", "uv_coset_books",
+    "uv_coset_mem_bytes", "uv_coset_model_bytes", "uv_coset_export", "uv_coset_reconstruct",
 ]
 
 
@@ -129,6 +131,18 @@ def lib():
             "uv_index_export_signs": (C.c_int, [vp, vp, vp]),
             "uv_ivf_set_shortlist": (C.c_int, [vp, i32, i32, i32]),
             "uv_ivf_export_signs": (C.c_int, [vp, vp, vp]),
+            "uv_coset_create": (C.c_int, [i32, i32, i32, u64, i32, i32, vpp]),
+            "uv_coset_destroy": (C.c_int, [vp]),
+            "uv_coset_set_centroids": (C.c_int, [vp, vp, i32]),
+            "uv_coset_add": (C.c_int, [vp, vp, vp, i64, vp]),
+            "uv_coset_search": (C.c_int, [vp, vp, i64, i32, vp, vp, vp]),
+            "uv_coset_len": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_coset_shape": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32)]),
+            "uv_coset_books": (C.c_int, [vp, vp, vp]),
+            "uv_coset_mem_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_coset_model_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+            "uv_coset_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp]),
+            "uv_coset_reconstruct": (C.c_int, [vp, vp, i64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -440,6 +454,95 @@ class Index:
         ix = cls.__new__(cls)
         ix.h, ix.codec = h, codec
         return ix
+
+
+class CosetIndex:
+    """The coset trellis backend (src/coset_trellis.rs, CosetTrellis): E8
+    coset books, a 4-branch free-start Viterbi per row, and the same rescaled
+    estimator.  dim % 8 == 0, bits 1..3; mem defaults to the reference's 12."""
+
+    def __init__(self, dim: int, bits: int, mem: int = 12, seed: int = 42, rounds: int = 3,
+                 device: int = 0):
+        h = C.c_void_p()
+        check(lib().uv_coset_create(dim, bits, mem, seed, rounds, device, C.byref(h)))
+        self.h, self.dim, self.bits, self.mem, self.device = h, dim, bits, mem, device
+        cl, pc = C.c_int32(), C.c_int32()
+        check(lib().uv_coset_shape(h, C.byref(cl), C.byref(pc)))
+        self.code_len, self.per_coset = cl.value, pc.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uv_coset_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_centroids(self, centroids):
+        cen = _f32(centroids)
+        check(lib().uv_coset_set_centroids(self.h, _ptr(cen), cen.shape[0]))
+
+    def add(self, ids, rows):
+        rows = _f32(rows)
+        ids = ids if _is_torch(ids) else np.ascontiguousarray(ids, np.int64)
+        check(lib().uv_coset_add(self.h, _ptr(ids), _ptr(rows), rows.shape[0], _stream(rows)))
+
+    def add_batch(self, rows):
+        """add_batch: ids are the batch's positions 0..n-1."""
+        rows = _f32(rows)
+        check(lib().uv_coset_add(self.h, None, _ptr(rows), rows.shape[0], _stream(rows)))
+
+    def __len__(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_coset_len(self.h, C.byref(n)))
+        return n.value
+
+    def mem_bytes(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_coset_mem_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def model_bytes(self) -> int:
+        n = C.c_int64()
+        check(lib().uv_coset_model_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def search(self, queries, k: int):
+        """search (src/coset_trellis.rs:471-497): top-k (ids, scores)."""
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        alloc = _Alloc(queries)
+        ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+        check(lib().uv_coset_search(self.h, _ptr(queries), nq, k, _ptr(ids), _ptr(scores),
+                                    _stream(queries)))
+        return ids, scores
+
+    def books(self):
+        keys = np.zeros((8, self.per_coset), np.uint64)
+        scale = np.zeros(2, np.float32)
+        check(lib().uv_coset_books(self.h, _ptr(keys), _ptr(scale)))
+        return keys, (float(scale[0]), float(scale[1]))
+
+    def export(self):
+        n = len(self)
+        out = dict(codes=np.zeros((n, self.code_len), np.uint8), rescale=np.zeros(n, np.float32),
+                   rnorm=np.zeros(n, np.float32), cidx=np.zeros(n, np.uint32),
+                   ids=np.zeros(n, np.int64))
+        check(lib().uv_coset_export(self.h, _ptr(out["codes"]), _ptr(out["rescale"]),
+                                    _ptr(out["rnorm"]), _ptr(out["cidx"]), _ptr(out["ids"]),
+                                    None))
+        return out
+
+    def reconstruct(self, rows):
+        """reconstruct_unit of every row."""
+        rows = _f32(rows)
+        out = _Alloc(rows)(tuple(rows.shape), np.float32)
+        check(lib().uv_coset_reconstruct(self.h, _ptr(rows), rows.shape[0], _ptr(out),
+                                         _stream(rows)))
+        return out
 
 
 class PreparedQueries:

@@ -29,7 +29,8 @@ namespace uvb {
 
 // ---------------------------------------------------------------------------
 // Query preparation (src/trellis.rs:2120-2136): u = q/|q| (degenerate when
-// |q| < EPS), qc[j] = <u, c_j>, q_r = rotate(u).  One warp per query.
+// |q| < EPS), qc[j] = <u, c_j>, q_r = rotate(u).  One warp per query.  With
+// clamp_norm (src/coset_trellis.rs:473-476) |q| is clamped at EPS instead.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
   extern __shared__ __align__(16) float smem[];
@@ -49,10 +50,13 @@ __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
     const float *src = p.queries + qq * (int64_t)d;
     for (int i = tm.t; i < d; i += 32) x[i] = src[i];
     tm.sync();
-    if (tm.leader()) misc[0] = fsqrt(seq_sum_sq(x, d));
+    if (tm.leader()) {
+      const float l2 = fsqrt(seq_sum_sq(x, d));
+      misc[0] = p.clamp_norm ? fmax_rs(l2, kF32Eps) : l2;
+    }
     tm.sync();
     const float qn = misc[0];
-    const bool degenerate = !(qn >= kF32Eps);
+    const bool degenerate = !p.clamp_norm && !(qn >= kF32Eps);
     if (!degenerate) {
       for (int i = tm.t; i < d; i += 32) x[i] = fdiv(x[i], qn);
       tm.sync();
@@ -176,10 +180,85 @@ constexpr int NSC = 5;
 // window i is the field [i*B, i*B + M + B) of [start (M bits) || codes]
 // (src/trellis.rs:1576-1600), i.e. bits [32 + i*B - M, ...) of the image whose
 // first 32-bit word is the start state.  k0 is a multiple of 16.
+// Coset records (src/coset_trellis.rs:414-434): [start state, ceil(mem/8)
+// bytes little-endian | (2 + m)-bit symbols (branch << m | book index),
+// MSB first].  Thread (r, c) decodes a contiguous range of 8-wide blocks of
+// record r.  The state entering block b is fixed by the start state and the
+// branches before b, of which only the last ceil(mem/2) still show, so each
+// thread replays at most that many symbols before its range.  x-bar values
+// come from the 32-entry table of (R/2 - mean)/std over raw coordinates R;
+// coordinates from the row's width up to the padded width are zeros.
+__device__ __forceinline__ uint32_t coset_sym(const uint32_t *cw, int rw, int bitpos, int W) {
+  const int wi = bitpos >> 5;
+  const uint32_t w0 = wi < rw ? __byte_perm(__ldg(cw + wi), 0, 0x0123) : 0u;
+  const uint32_t w1 = wi + 1 < rw ? __byte_perm(__ldg(cw + wi + 1), 0, 0x0123) : 0u;
+  const uint32_t top = __funnelshift_l(w1, w0, bitpos & 31);
+  return top >> (32 - W);
+}
+
+__device__ __forceinline__ void decode_tile_coset(const ScanParams &p, int64_t r0, int nr,
+                                                  float *xT, float *sc, int k0, int kc,
+                                                  bool scalars) {
+  const CosetModel &m = p.coset;
+  const int tid = threadIdx.x;
+  const int r = tid & 31;
+  const int c = tid >> 5;
+  const bool ok = r < nr;
+  const int64_t rec = ok ? r0 + r : r0;
+  const uint8_t *bytes = p.codes + rec * (int64_t)p.code_stride;
+  const uint32_t *cw = (const uint32_t *)bytes;
+  const int rw = p.code_stride >> 2;
+  const int nb = m.dim >> 3;
+  const int W = 2 + m.m_bits;
+  const uint32_t mask = (1u << m.mem) - 1, imask = (1u << m.m_bits) - 1;
+  const int L = (m.mem + 1) >> 1;
+  const int sbits = 8 * m.start_bytes;
+  // blocks of coordinates [k0, k0 + kc) that hold data (k0 is a multiple of 16)
+  const int kb0 = k0 >> 3;
+  const int kbn = max(0, min(nb, (k0 + kc) >> 3) - kb0);
+  const int b0 = kb0 + c * kbn / 8, b1 = kb0 + (c + 1) * kbn / 8;
+  uint32_t st = 0;
+  if (b0 <= L)
+    for (int i = 0; i < m.start_bytes; i++) st |= (uint32_t)__ldg(bytes + i) << (8 * i);
+  for (int i = b0 > L ? b0 - L : 0; i < b0; i++)
+    st = ((st << 2) | (coset_sym(cw, rw, sbits + i * W, W) >> m.m_bits)) & mask;
+  for (int b = b0; b < b1; b++) {
+    const uint32_t sym = coset_sym(cw, rw, sbits + b * W, W);
+    const uint32_t br = sym >> m.m_bits;
+    const int cs = (int)(((__popc(st) & 1) << 2) | br);
+    const uint64_t key = __ldg(m.books + (size_t)cs * m.per_coset + (sym & imask));
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int i = b * 8 + j;
+      const int R = (int)((key >> (5 * (7 - j))) & 31);  // R + 16
+      const float v = ok ? __ldg(m.xval + R) : 0.0f;
+      xT[(size_t)(i - k0) * XSTR + (r ^ (((i >> 1) & 1) << 2))] = v;
+    }
+    st = ((st << 2) | br) & mask;
+  }
+  if (c == 7)
+    for (int i = max(m.dim, k0); i < k0 + kc; i++)
+      xT[(size_t)(i - k0) * XSTR + (r ^ (((i >> 1) & 1) << 2))] = 0.0f;
+  if (scalars && tid < TN) {
+    const bool okr = tid < nr;
+    const float rs = okr ? __ldg(p.rescale + r0 + tid) : INFINITY;
+    const float rn = okr ? __ldg(p.rnorm + r0 + tid) : 1.0f;
+    sc[tid] = rs;
+    sc[TN + tid] = rn;
+    sc[2 * TN + tid] = 1.0f;
+    ((uint32_t *)sc)[3 * TN + tid] = (okr && p.cidx) ? __ldg(p.cidx + r0 + tid) : 0u;
+    sc[4 * TN + tid] = fdiv(rn, rs);
+  }
+}
+
 template <int B, bool TSMEM>
 __device__ __forceinline__ void decode_tile(const ScanParams &p, const float *code, int64_t r0,
                                             int nr, float *xT, float *sc, int k0, int kc,
                                             bool scalars) {
+  if constexpr (B == 0) {
+    decode_tile_coset(p, r0, nr, xT, sc, k0, kc, scalars);
+    return;
+  }
   const int tid = threadIdx.x;
   const int W = p.mem + B;
   const int rshift = 32 - W;
@@ -270,7 +349,8 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     // pre-permuted by that lane's mask (bits 3, 2, 0 of j)
     const int jm = i & 15;
     const int qm = (((jm >> 3) & 1) << 2) | (((jm >> 2) & 1) << 1) | (jm & 1);
-    qT[(size_t)i * QSTR + (qi ^ qm)] = q < p.nq ? p.q_r[q * (int64_t)p.q_stride + i] : 0.0f;
+    const bool live = q < p.nq && (B != 0 || i < p.coset.dim);
+    qT[(size_t)i * QSTR + (qi ^ qm)] = live ? p.q_r[q * (int64_t)p.q_stride + i] : 0.0f;
   }
   for (int e = tid; e < TQ * KCAP; e += 256) top[e] = kEmptyKey;
   if (tid < TQ) {
@@ -463,6 +543,11 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     }
   }
 }
+
+// The flat scan over coset records: p.dim is the row width rounded up to 16
+// (the zero lanes of a last 8-wide block add exact zeros, which is how
+// simd::dot's 8-wide tail into the first accumulator comes out).
+const void *coset_scan_kernel_ptr() { return (const void *)flat_scan_kernel<0, false>; }
 
 const void *flat_scan_kernel_ptr(int bits, bool table_in_smem) {
 #define UV_SCAN_CASE(b)                                                                   \
@@ -778,6 +863,9 @@ const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k) 
     return table_in_smem ? (const void *)chunked_scan_kernel<b, true, 128, 64>             \
                          : (const void *)chunked_scan_kernel<b, false, 128, 64>;
   switch (bits) {
+    case 0:  // coset records (decode_tile_coset); no code table
+      return small_k ? (const void *)chunked_scan_kernel<0, false, 32, 32>
+                     : (const void *)chunked_scan_kernel<0, false, 128, 64>;
     UV_CH_CASE(1)
     UV_CH_CASE(2)
     UV_CH_CASE(3)

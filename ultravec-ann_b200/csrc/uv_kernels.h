@@ -70,6 +70,19 @@ struct PrepParams {
   float *qc;             // nq x n_centroids
   uint32_t *degenerate;  // nq
   float *u;              // or null: nq x dim_pad unit queries (before rotation)
+  int clamp_norm;        // |q| clamped at EPS instead of a degenerate query
+};
+
+// The coset trellis's model (coset.cu, src/coset_trellis.rs): book points
+// are 64-bit keys, norm << 40 | the eight raw doubled coordinates offset by
+// 16, five bits each (first coordinate highest), sorted per coset.
+struct CosetModel {
+  int dim, mem, m_bits, per_coset, start_bytes, code_len, code_stride;
+  const uint64_t *books;  // 8 x per_coset sorted keys
+  uint64_t bound[8];      // last key of each coset's book
+  float scale_mean, scale_std;
+  double pi4;             // pi^4 as the reference's constant PI.powi(4)
+  const float *xval;      // 32: (R/2 - mean) / std for raw R = -16..15
 };
 
 struct ScanParams {
@@ -93,6 +106,7 @@ struct ScanParams {
   int64_t id_base;
   uint32_t *part_key;  // nq x splits x k
   int64_t *part_id;
+  CosetModel coset;    // coset records (coset_scan_kernel)
 };
 
 // Work items of the chunked scan.  Flat (ivf == 0): the grid is query tiles x
@@ -305,6 +319,40 @@ __global__ void score_candidates_kernel(const CandParams p);
 const void *score_candidates_lane_kernel_ptr(int bits);  // bits 1..4; else null
 const void *shortlist_kernel_ptr(int bits, bool asym);
 size_t shortlist_smem_bytes(int cp, int q_stride, int sign_stride, int table_len);
+
+// ---------------------------------------------------------------------------
+// Coset trellis (coset.cu): trellis-coded quantization over the eight cosets
+// of an index-8 sublattice of E8 (src/coset_trellis.rs).  Book points are
+// 64-bit keys, norm << 40 | the eight raw doubled coordinates offset by 16,
+// five bits each (first coordinate highest), sorted per coset.
+// ---------------------------------------------------------------------------
+
+struct CosetEncParams {
+  CosetModel m;
+  int64_t n;                 // rows of this launch
+  const float *rows;         // n x dim
+  RotParams rot;
+  const float *centroids;
+  int n_centroids;
+  float *u_r, *y;            // n x dim
+  uint32_t *blk_idx;         // n x (dim/8) x 8
+  float *blk_cost;           // n x (dim/8) x 8
+  uint8_t *back;             // n x (dim/8) x 2^mem, unless in shared memory
+  float *cost;               // n x 2 x 2^mem, unless in shared memory
+  int back_smem, cost_smem;
+  uint8_t *codes;            // n x code_stride
+  float *rescale, *rnorm;
+  uint32_t *cidx;
+  float *recon;              // n x dim (reconstruction kernel)
+};
+
+__global__ void coset_prep_kernel(const CosetEncParams p);
+__global__ void coset_nearest_kernel(const CosetEncParams p);
+__global__ void coset_viterbi_kernel(const CosetEncParams p);
+__global__ void coset_reconstruct_kernel(const CosetEncParams p);
+__global__ void iota_i64_kernel(int64_t *out, int64_t n, int64_t base);
+size_t coset_viterbi_smem_bytes(int dim, int mem, bool back_smem, bool cost_smem);
+const void *coset_scan_kernel_ptr();
 
 // scan tiling constants shared with the host planner
 constexpr int kScanTQ = 32;
