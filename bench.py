@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", choices=["flat", "wide", "ivf", "encode-sweep", "candidates",
-                                           "shortlist"],
+                                           "shortlist", "coset"],
                     default="flat",
                     help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
                          "others measure the remaining configurations, one JSON line each")
@@ -494,7 +494,13 @@ def run_secondary(args):
                   rounds), 10k queries top-10 with the 1-bit shortlist
                   (Hamming stage 1) at C in {128, 256, 512}, nprobe in
                   {1, 8, 32, 128}, beside the plain codes scan; and the flat
-                  shortlist at C = 512 over all 1M rows (1k queries)"""
+                  shortlist at C = 512 over all 1M rows (1k queries)
+    coset         the coset trellis (E8 cosets, 4-branch Viterbi), N(0,1)
+                  rows, b=2: the reference's research cells (d=128 5k rows
+                  and d=960 padded to 1024 20k rows, M=16, 500 queries
+                  top-10) and a throughput cell (d=128, 200k rows, the
+                  default M=12, 1k queries); encode rows/s, queries/s, and
+                  the oracle's rates on a bounded sample of each cell"""
     import torch
 
     from ultravec_ann_b200_loader import load
@@ -644,6 +650,62 @@ def run_secondary(args):
             "candidates_s": ncand / ms * 1e3, "score_ms": ms, "kernel_ms": kern_ms,
             "prepare_ms": prep_ms, "bytes_per_candidate": per_cand,
             "achieved_gbs": ncand * per_cand / (kern_ms * 1e-3) / 1e9, "bits": 2, "mem": 8})
+    elif args.workload == "coset":
+        import os
+        import sys
+        import time
+
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle as O  # the CPU oracle: the timed CPU baseline only
+
+        threads = os.cpu_count() or 1
+        for name, d, mem, n, nq in (("coset-sift-d128-b2-M16-5k", 128, 16, 5_000, 500),
+                                    ("coset-gist-d1024-b2-M16-20k", 1024, 16, 20_000, 500),
+                                    ("coset-d128-b2-M12-200k", 128, 12, 200_000, 1000)):
+            rows = rng.standard_normal((n + nq, d), dtype=np.float32)
+            base = torch.from_numpy(rows[:n]).to(dev)
+            qs = torch.from_numpy(rows[n:]).to(dev)
+            enc_ms = float("inf")
+            for rep in range(3):  # a fresh index each time; the first is warm-up
+                ix = uv.CosetIndex(d, 2, mem=mem)
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                ix.add_batch(base)
+                b.record()
+                torch.cuda.synchronize()
+                if rep > 0:
+                    enc_ms = min(enc_ms, a.elapsed_time(b))
+            scan_ms = _timed(lambda: ix.search(qs, 10), 3)
+            uv.profile_enable(True)
+            ix2 = uv.CosetIndex(d, 2, mem=mem)
+            ix2.add_batch(base)
+            ix2.search(qs, 10)
+            torch.cuda.synchronize()
+            del ix2
+            kern = {f: round(uv.profile_read(f)[0], 3)
+                    for f in ("coset_prep", "coset_nearest", "coset_viterbi", "prep_queries",
+                              "coset_scan", "merge_topk")}
+            uv.profile_enable(False)
+            # the oracle on a bounded sample of the same cell
+            oc = O.Coset(d, 2, mem=mem)
+            ns = 64 if d > 256 else 256
+            t0 = time.perf_counter()
+            enc = oc.encode_batch(rows[:ns])
+            cpu_enc = ns / (time.perf_counter() - t0)
+            big = {k: np.concatenate([v] * (n // ns)) for k, v in enc.items()}
+            t0 = time.perf_counter()
+            oc.search(big, rows[n:n + 16], 10)
+            cpu_q = 16 / (time.perf_counter() - t0)
+            emit(name, {"bits": 2, "mem": mem, "dim": d, "rows": n, "queries": nq, "k": 10,
+                        "encode_rows_s": n / enc_ms * 1e3, "encode_ms": enc_ms,
+                        "queries_s": nq / scan_ms * 1e3, "search_ms": scan_ms,
+                        "kernels_ms": kern,
+                        "cpu_baseline": {"encode_rows_s": cpu_enc, "queries_s": cpu_q,
+                                         "cores": threads, "kind": "port",
+                                         "sample": f"encode {ns} rows; search 16 queries over "
+                                                   f"{(n // ns) * ns} records"}})
+            del ix, oc, enc, big
     else:
         d = 128
         rows = rng.standard_normal((1_000_000, d), dtype=np.float32)

@@ -47,6 +47,9 @@ def test_records_match_oracle(uv, oracle, dim, bits, mem, n):
     rows = rand_rows(n, dim, dim * 7 + mem)
     rows[3] = 0.0                       # zero row: |x| clamped at EPS
     rows[5] *= np.float32(1e-30)        # tiny row
+    rows[7] = 1.0                       # constant and one-hot rows: tied minima
+    rows[9] = 0.0
+    rows[9, 0] = 1.0
     g.add_batch(rows)
     got = g.export()
     want = o.encode_batch(rows)
@@ -55,6 +58,24 @@ def test_records_match_oracle(uv, oracle, dim, bits, mem, n):
     assert _same_f32(got["rnorm"], want["rnorm"])
     assert np.array_equal(got["cidx"], want["cidx"])
     assert np.array_equal(got["ids"], np.arange(n))
+
+
+@pytest.mark.parametrize("mode", [0, 1], ids=["book_scan", "reference_search"])
+def test_nearest_modes_agree(uv, oracle, mode):
+    """Both ways to the nearest kept point (tuning key coset_nearest) give
+    the oracle's records, tied minima included."""
+    uv.set_tuning("coset_nearest", mode)
+    try:
+        g, o = _pair(uv, oracle, 48, 2, 8)
+        rows = rand_rows(150, 48, 77)
+        rows[::10] = np.round(rows[::10])  # integer rows: more exact ties
+        g.add_batch(rows)
+        got = g.export()
+        want = o.encode_batch(rows)
+        assert np.array_equal(got["codes"], want["codes"])
+        assert _same_f32(got["rescale"], want["rescale"])
+    finally:
+        uv.set_tuning("coset_nearest", 0)
 
 
 def test_records_three_bits(uv, oracle):

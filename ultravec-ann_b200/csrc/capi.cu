@@ -20,6 +20,7 @@ int g_tc_mode = 0;
 int g_cand_kernel = 0;
 int g_tc_shape = 0;
 int g_tc_cache = 1;
+int g_coset_nearest = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
@@ -1239,6 +1240,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_cache") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_cache must be 0 or 1");
     g_tc_cache = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "coset_nearest") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "coset_nearest must be 0 or 1");
+    g_coset_nearest = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "cand_kernel") == 0) {

@@ -170,6 +170,11 @@ int coset_encode(const uv_coset *ix, const float *d_rows, int64_t n, uint8_t *co
   const size_t psmem = (size_t)8 * (d + 8) * 4;
   UV_CK(cudaFuncSetAttribute(uvb::coset_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)psmem));
+  const bool brute = g_coset_nearest != 1 && ix->m.per_coset <= 8192;
+  const size_t bsmem = uvb::coset_brute_smem_bytes(ix->m.per_coset);
+  if (brute)
+    UV_CK(cudaFuncSetAttribute(uvb::coset_nearest_brute_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsmem));
   for (int64_t done = 0; done < n; done += chunk) {
     const int64_t rows = std::min(chunk, n - done);
     uvb::CosetEncParams p;
@@ -193,16 +198,33 @@ int coset_encode(const uv_coset *ix, const float *d_rows, int64_t n, uint8_t *co
     p.rnorm = rnorm + done;
     p.cidx = cidx + done;
     void *args[] = {&p};
-    ProfScope ps("coset_encode", st);
-    const int pgrid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sms * 16);
-    UV_CK(cudaLaunchKernel((const void *)uvb::coset_prep_kernel, dim3(pgrid), dim3(256), args,
-                           psmem, st));
-    const int64_t items = rows * nb * 8;
-    const int ngrid = (int)std::min<int64_t>((items + 255) / 256, (int64_t)sms * 64);
-    UV_CK(cudaLaunchKernel((const void *)uvb::coset_nearest_kernel, dim3(ngrid), dim3(256), args,
-                           0, st));
-    UV_CK(cudaLaunchKernel((const void *)uvb::coset_viterbi_kernel,
-                           dim3((unsigned)std::min(vgrid, rows)), dim3(256), args, vsmem, st));
+    {
+      ProfScope ps("coset_prep", st);
+      const int pgrid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sms * 16);
+      UV_CK(cudaLaunchKernel((const void *)uvb::coset_prep_kernel, dim3(pgrid), dim3(256), args,
+                             psmem, st));
+    }
+    {
+      ProfScope ps("coset_nearest", st);
+      if (brute) {
+        // every book point against tiles of y-blocks (books of <= 8192 points)
+        const int64_t ny = rows * nb;
+        const int64_t per_cta = 256 * uvb::kCosetBruteY;
+        UV_CK(cudaLaunchKernel((const void *)uvb::coset_nearest_brute_kernel,
+                               dim3((unsigned)((ny + per_cta - 1) / per_cta), 8), dim3(256), args,
+                               bsmem, st));
+      } else {
+        const int64_t items = rows * nb * 8;
+        const int ngrid = (int)std::min<int64_t>((items + 255) / 256, (int64_t)sms * 64);
+        UV_CK(cudaLaunchKernel((const void *)uvb::coset_nearest_kernel, dim3(ngrid), dim3(256),
+                               args, 0, st));
+      }
+    }
+    {
+      ProfScope ps("coset_viterbi", st);
+      UV_CK(cudaLaunchKernel((const void *)uvb::coset_viterbi_kernel,
+                             dim3((unsigned)std::min(vgrid, rows)), dim3(256), args, vsmem, st));
+    }
   }
   return UV_OK;
 }

@@ -274,6 +274,104 @@ __global__ void __launch_bounds__(256) coset_nearest_kernel(const CosetEncParams
 }
 
 // ---------------------------------------------------------------------------
+// The same results for books of up to 8192 points (one and two bits): every
+// point of the coset's book is scored against tiles of y-blocks held in
+// registers, the book staged in shared memory as eight signed bytes per
+// point.  The minimum is exact, so when one point attains it that point is
+// the reference's answer too; when several do, the reference's choice among
+// them depends on its search order, so that y-block runs nearest_in_coset.
+// Grid: (y-block tiles, coset).
+// ---------------------------------------------------------------------------
+constexpr int kBruteY = kCosetBruteY;
+
+__global__ void __launch_bounds__(256) coset_nearest_brute_kernel(const CosetEncParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const CosetModel &m = p.m;
+  const int c = blockIdx.y;
+  const int nb = m.dim >> 3;
+  const int64_t ny = p.n * nb;
+  const uint64_t *book = m.books + (size_t)c * m.per_coset;
+  uint2 *pts = (uint2 *)sm;  // per point: raw coordinates as signed bytes
+  for (int i = threadIdx.x; i < m.per_coset; i += blockDim.x) {
+    const uint64_t key = __ldg(book + i);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t r = (uint32_t)((int)((key >> (5 * (7 - j))) & 31) - 16) & 0xffu;
+      if (j < 4)
+        lo |= r << (8 * j);
+      else
+        hi |= r << (8 * (j - 4));
+    }
+    pts[i] = make_uint2(lo, hi);
+  }
+  __syncthreads();
+  const int64_t y0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kBruteY;
+  float y[kBruteY][8];
+  float best[kBruteY];
+  int bidx[kBruteY];
+  bool tie[kBruteY];
+#pragma unroll
+  for (int u = 0; u < kBruteY; u++) {
+    const int64_t e = y0 + u < ny ? y0 + u : ny - 1;
+#pragma unroll
+    for (int j = 0; j < 8; j++) y[u][j] = p.y[e * 8 + j];
+    best[u] = INFINITY;
+    bidx[u] = 0;
+    tie[u] = false;
+  }
+  // two y-blocks per paired f32 instruction: y - p/2 is y + (-p/2) exactly
+  float2 y2[kBruteY / 2][8];
+#pragma unroll
+  for (int u = 0; u < kBruteY / 2; u++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) y2[u][j] = make_float2(y[2 * u][j], y[2 * u + 1][j]);
+  for (int i = 0; i < m.per_coset; i++) {
+    const uint2 w = pts[i];
+    float2 nh[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t word = j < 4 ? w.x : w.y;
+      const float h = fmul((float)(int8_t)((word >> (8 * (j & 3))) & 0xffu), -0.5f);
+      nh[j] = make_float2(h, h);
+    }
+#pragma unroll
+    for (int u = 0; u < kBruteY / 2; u++) {
+      float2 d = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float2 e = __fadd2_rn(y2[u][j], nh[j]);
+        d = __fadd2_rn(d, __fmul2_rn(e, e));
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int v = 2 * u + h;
+        const float dv = h ? d.y : d.x;
+        if (dv < best[v]) {
+          best[v] = dv;
+          bidx[v] = i;
+          tie[v] = false;
+        } else if (dv == best[v]) {
+          tie[v] = true;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kBruteY; u++) {
+    const int64_t e = y0 + u;
+    if (e >= ny) continue;
+    uint32_t idx = (uint32_t)bidx[u];
+    float d = best[u];
+    if (tie[u] || !(d < INFINITY)) nearest_in_coset(m, c, y[u], &idx, &d);
+    p.blk_idx[e * 8 + c] = idx;
+    p.blk_cost[e * 8 + c] = d;
+  }
+}
+
+size_t coset_brute_smem_bytes(int per_coset) { return (size_t)per_coset * 8; }
+
+// ---------------------------------------------------------------------------
 // Prep: one warp per row (src/coset_trellis.rs:298-318, 322-326, 335-341).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) coset_prep_kernel(const CosetEncParams p) {
@@ -403,35 +501,49 @@ __global__ void __launch_bounds__(kVitThreads) coset_viterbi_kernel(const CosetE
     for (int b = 0; b < nb; b++) {
       const float *cb = bc + b * 8;
       uint8_t *bk = back + (size_t)b * S;
-      for (int ns = tid; ns < S; ns += kVitThreads) {
-        float best = INFINITY;
-        int sel = 255;
-        if (mem >= 2) {
-          const uint32_t base = (uint32_t)ns >> 2;
-          const int br = ns & 3;
+      if (mem >= 2) {
+        // butterfly of base q: sources q | t << (mem-2) (t = 0..3) feed the
+        // four destinations (q << 2) | br; reads are coalesced over q
+        const int Q = S >> 2;
+        const float c0 = cb[0], c1 = cb[1], c2 = cb[2], c3 = cb[3];
+        const float c4 = cb[4], c5 = cb[5], c6 = cb[6], c7 = cb[7];
+#pragma unroll 2
+        for (int q = tid; q < Q; q += kVitThreads) {
+          float best[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+          uint32_t sel = 0xffffffffu;  // four back bytes, 255 = no finite source
 #pragma unroll
           for (int t = 0; t < 4; t++) {
-            const uint32_t s = base | ((uint32_t)t << (mem - 2));
+            const uint32_t s = (uint32_t)q | ((uint32_t)t << (mem - 2));
             const float cs = cur[s];
             if (cs == INFINITY) continue;
-            const float tot = fadd(cs, cb[coset_for(s, br)]);
-            if (tot < best) {
-              best = tot;
-              sel = t;
+            const bool odd = __popc(s) & 1;
+            const float e[4] = {odd ? c4 : c0, odd ? c5 : c1, odd ? c6 : c2, odd ? c7 : c3};
+#pragma unroll
+            for (int br = 0; br < 4; br++) {
+              const float tot = fadd(cs, e[br]);
+              if (tot < best[br]) {
+                best[br] = tot;
+                sel = (sel & ~(0xffu << (8 * br))) | ((uint32_t)t << (8 * br));
+              }
             }
           }
-        } else {
-          // mem = 1: ns = br & 1; the pairs (s, br) meet it in this order
-          for (int s = 0; s < 2; s++) {
-            const float cs = cur[s];
-            if (cs == INFINITY) continue;
-            for (int h = 0; h < 2; h++) {
-              const int br = ns + 2 * h;
-              const float tot = fadd(cs, cb[coset_for((uint32_t)s, br)]);
-              if (tot < best) {
-                best = tot;
-                sel = (s << 2) | br;
-              }
+          *(float4 *)(nxt + 4 * q) = make_float4(best[0], best[1], best[2], best[3]);
+          *(uint32_t *)(bk + 4 * q) = sel;
+        }
+      } else if (tid < 2) {
+        // mem = 1: ns = br & 1; the pairs (s, br) meet it in this order
+        const int ns = tid;
+        float best = INFINITY;
+        int sel = 255;
+        for (int s = 0; s < 2; s++) {
+          const float cs = cur[s];
+          if (cs == INFINITY) continue;
+          for (int h = 0; h < 2; h++) {
+            const int br = ns + 2 * h;
+            const float tot = fadd(cs, cb[coset_for((uint32_t)s, br)]);
+            if (tot < best) {
+              best = tot;
+              sel = (s << 2) | br;
             }
           }
         }

@@ -348,6 +348,9 @@ struct CosetEncParams {
 
 __global__ void coset_prep_kernel(const CosetEncParams p);
 __global__ void coset_nearest_kernel(const CosetEncParams p);
+__global__ void coset_nearest_brute_kernel(const CosetEncParams p);
+size_t coset_brute_smem_bytes(int per_coset);
+constexpr int kCosetBruteY = 8;  // y-blocks per thread of coset_nearest_brute_kernel
 __global__ void coset_viterbi_kernel(const CosetEncParams p);
 __global__ void coset_reconstruct_kernel(const CosetEncParams p);
 __global__ void iota_i64_kernel(int64_t *out, int64_t n, int64_t base);
