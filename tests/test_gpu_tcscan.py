@@ -199,3 +199,22 @@ def test_kept_rows_follow_every_change_of_the_records(uv, tc_mode):
                 assert same(a, c)
     finally:
         uv.set_tuning("tc_cache", 1)
+
+
+@pytest.mark.parametrize("sample", [1, 5, 16])
+@pytest.mark.parametrize("k", [10, 100])
+def test_sampled_threshold_matches_exact_kernel(uv, tc_mode, sample, k):
+    """Pass 1 bounding every S-th tile (tuning key tc_sample) still returns
+    exactly the exact kernel's top-k; S shrinks when the sample would hold
+    fewer than 8k groups."""
+    n, nq, dim = 300_000, 150, 128
+    base = rand_rows(n, dim, 61) * np.float32(1.7)
+    queries = rand_rows(nq, dim, 62)
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    index.add_batch(base)
+    uv.set_tuning("tc_sample", sample)
+    try:
+        a, b = search_both(uv, index, queries, k, True, tc_mode)
+    finally:
+        uv.set_tuning("tc_sample", 0)
+    assert same(a, b)

@@ -21,7 +21,9 @@ int g_cand_kernel = 0;
 int g_tc_shape = 0;
 int g_tc_cache = 1;
 int g_coset_nearest = 0;
+int g_tc_sample = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
+std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
 
@@ -1009,27 +1011,52 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
       splits = s2;
     }
   }
+  // Pass 1 bounds a sample of the tiles (every S-th): the k-th largest group
+  // maximum of any subset of groups is still a score at least k records
+  // reach, so theta stays valid, and pass 2 admits about k*S candidates
+  // instead of k.  Pass 1 costs ~1/S, the candidates ~k*S: S = sqrt(1100/k)
+  // balances them at the 1M x 10k bench shape (measured optimum 3 at
+  // k = 100, 6-10 at k = 10), capped so that k*S stays well inside the
+  // candidate lists and the sample keeps at least 8k groups.
+  int64_t S = g_tc_sample > 0
+                  ? g_tc_sample
+                  : std::max<int64_t>(1, std::min<int64_t>(
+                                             16, (int64_t)std::lround(std::sqrt(1100.0 / k))));
+  if (g_tc_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
+  while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
+  const int64_t n_tiles1 = (n_tiles + S - 1) / S;
+  g_tc_last_sample = S;
+  const int64_t n_groups1 = 2 * n_tiles1;
   float *tmax = nullptr, *theta = nullptr;
   uint32_t *cand = nullptr;
   int *cand_cnt = nullptr, *flags = nullptr;
   int32_t *over_list = nullptr;
+  // Pass 2's candidate list of a query is cut into one segment per (record
+  // split, column half), each appended by a single thread; the rescoring
+  // gathers at most `cap` of them.
   const int cap = 2048;
-  UV_TRY(sc.alloc(&tmax, (size_t)nq * n_groups));
+  const int regions = (int)(2 * splits);  // <= 128: splits <= 64
+  const int region_cap = std::max(256, cap / regions);
+  const int64_t cand_stride = (int64_t)regions * region_cap;
+  UV_TRY(sc.alloc(&tmax, (size_t)nq * n_groups1));
   UV_TRY(sc.alloc(&theta, (size_t)nq));
-  UV_TRY(sc.alloc(&cand, (size_t)nq * cap));
-  UV_TRY(sc.alloc(&cand_cnt, (size_t)nq));
+  UV_TRY(sc.alloc(&cand, (size_t)nq * cand_stride));
+  UV_TRY(sc.alloc(&cand_cnt, (size_t)nq * regions));
   UV_TRY(sc.alloc(&flags, 4));  // [0] timeout, [1] overflowed queries, [2..3] candidates
   UV_TRY(sc.alloc(&over_list, (size_t)nq));
-  UV_CK(cudaMemsetAsync(cand_cnt, 0, sizeof(int) * nq, st));
+  UV_CK(cudaMemsetAsync(cand_cnt, 0, sizeof(int) * nq * regions, st));
   UV_CK(cudaMemsetAsync(flags, 0, sizeof(int) * 4, st));
   uvb::TcScanParams tp;
   std::memset(&tp, 0, sizeof(tp));
   tp.q_stride = dim_pad;
-  tp.cand_cap = cap;
+  tp.cand_cap = (int)cand_stride;
+  tp.regions = regions;
+  tp.region_cap = region_cap;
   tp.nq = nq;
   tp.n = n;
   tp.n_tiles = n_tiles;
   tp.n_groups = n_groups;
+  tp.tile_stride = 1;
   tp.q_r = q_r;
   tp.degenerate = degen;
   tp.tmax = tmax;
@@ -1040,14 +1067,20 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const dim3 grid((unsigned)qtiles, (unsigned)splits);
   int kchunks = kpad / 64;
   {
-    void *args[] = {&tp, &tmap_main, &tmap_ext};
-    void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax_lo, &tmap_main, &tmap_ext};
+    uvb::TcScanParams tp1 = tp;
+    tp1.n_tiles = n_tiles1;
+    tp1.n_groups = n_groups1;
+    tp1.tile_stride = S;
+    const dim3 grid1((unsigned)qtiles,
+                     (unsigned)std::max<int64_t>(1, std::min<int64_t>(splits, n_tiles1 / 8)));
+    void *args[] = {&tp1, &tmap_main, &tmap_ext};
+    void *wargs[] = {&tp1, &kchunks, &tmap_a, &tmap_ax_lo, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass1", st);
-    UV_CK(cudaLaunchKernel(k1, grid, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
+    UV_CK(cudaLaunchKernel(k1, grid1, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
   }
   {
     ProfScope ps("tc_theta", st);
-    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_groups, nq, k, theta);
+    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_groups1, nq, k, theta);
     UV_CK(cudaGetLastError());
   }
   {
@@ -1080,13 +1113,19 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     rp.norms = ix->norms;
     rp.cand = cand;
     rp.cand_cnt = cand_cnt;
+    rp.regions = regions;
+    rp.region_cap = region_cap;
+    rp.cand_stride = cand_stride;
     rp.ids = ix->ids;
     rp.out_id = d_ids;
     rp.out_score = d_scores;
     rp.over_list = over_list;
     rp.n_over = flags + 1;
     rp.n_cand = (unsigned long long *)(flags + 2);
-    const size_t rsmem = (size_t)cap * 8 + (size_t)d * 4 + (rp.table_in_smem ? (size_t)c->table_len * 4 : 0);
+    const size_t rsmem = (size_t)cap * 12 + (size_t)((regions + 4) & ~3) * 4 + (size_t)d * 4 +
+                         (size_t)16 * (c->code_stride / 4 + 1) * 4 +
+                         (rp.table_in_smem ? (size_t)c->table_len * 4 : 0);
+    if (rsmem > 227 * 1024) return fail(UV_EUNSUPPORTED, "prefilter rescoring exceeds shared memory");
     UV_CK(cudaFuncSetAttribute(uvb::tc_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
     void *args[] = {&rp};
@@ -1242,6 +1281,11 @@ int uv_set_tuning(const char *key, int64_t value) {
     g_tc_cache = (int)value;
     return UV_OK;
   }
+  if (std::strcmp(key, "tc_sample") == 0) {
+    if (value < 0 || value > 64) return fail(UV_EINVAL, "tc_sample must be 0..64");
+    g_tc_sample = (int)value;
+    return UV_OK;
+  }
   if (std::strcmp(key, "coset_nearest") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "coset_nearest must be 0 or 1");
     g_coset_nearest = (int)value;
@@ -1274,6 +1318,12 @@ int uv_profile_enable(int32_t on) {
 int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
   if (kernel == nullptr || total_ms == nullptr || launches == nullptr)
     return fail(UV_EINVAL, "null argument");
+  if (std::strcmp(kernel, "tc_sample") == 0) {
+    // statistic of the last tensor-core search: pass 1 bounded every S-th tile
+    *total_ms = 0.0;
+    *launches = g_tc_last_sample.load();
+    return UV_OK;
+  }
   if (std::strcmp(kernel, "tc_candidates") == 0) {
     // statistic of the last tensor-core search: candidates scored exactly
     *total_ms = 0.0;

@@ -159,6 +159,7 @@ extern int g_cand_kernel;      // uv_set_tuning("cand_kernel")
 extern int g_tc_shape;         // uv_set_tuning("tc_shape")
 extern int g_tc_cache;         // uv_set_tuning("tc_cache")
 extern int g_coset_nearest;    // uv_set_tuning("coset_nearest")
+extern int g_tc_sample;        // uv_set_tuning("tc_sample")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 

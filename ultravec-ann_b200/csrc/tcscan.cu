@@ -221,10 +221,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * L::CW);
+    // pass 2: this thread's segment of the query's candidate list
+    const int region = (int)blockIdx.y * 2 + half;
+    uint32_t *seg = MODE == 2 ? p.cand + q * (int64_t)p.cand_cap + (int64_t)region * p.region_cap
+                              : nullptr;
+    int seg_cnt = 0;
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
-      const int64_t tile = t_begin + it;
-      const int64_t rec0 = tile * TN + half * L::CW;
+      const int64_t tile = t_begin + it;  // group index; records of tile * tile_stride
+      const int64_t rec0 = tile * p.tile_stride * TN + half * L::CW;
       if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
@@ -239,8 +244,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acce[a]);  // the warp's accumulator part is in registers
-      tcep::bounds_run<MODE, NL>(p, r, q, qok, theta, 2 * tile + half, rec0);
+      tcep::bounds_run<MODE, NL>(p, r, q, qok, theta, 2 * tile + half, rec0, seg, &seg_cnt);
     }
+    if (MODE == 2 && q < p.nq) p.cand_cnt[q * p.regions + region] = seg_cnt;
   } else if (warp == 8) {
     if (lane == 0) {
       // ================= MMA issue =================
@@ -296,7 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if (*abort_s) break;
       uint8_t *dst = sm + L::b + s * L::b_bytes;
-      const int row = (int)((t_begin + it) * TN);
+      const int row = (int)((t_begin + it) * p.tile_stride * TN);
       tc::mbar_arrive_expect_tx(&full[s], (uint32_t)L::b_bytes);
       tc::tma_load_2d(dst, &tmap_main, 0, row, &full[s]);
       tc::tma_load_2d(dst + L::bm_bytes, &tmap_main, 64, row, &full[s]);
@@ -468,15 +474,59 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
 __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   uint64_t *keys = (uint64_t *)sm;                    // cap (power of two)
-  float *qv = (float *)(keys + p.cap);                // dim
-  float *table = qv + p.dim;                          // table_len (optional)
+  uint32_t *cidx = (uint32_t *)(keys + p.cap);        // cap gathered candidates
+  int *roff = (int *)(cidx + p.cap);                  // regions + 1 segment offsets
+  float *qv = (float *)(roff + ((p.regions + 4) & ~3));  // dim
+  uint32_t *stage = (uint32_t *)(qv + p.dim);         // 16 x (words per record + 1)
+  float *table = (float *)(stage + 16 * ((p.code_stride >> 2) + 1));  // table_len (optional)
   const int64_t q = blockIdx.x;
   if (q >= p.nq) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cnt_raw = p.cand_cnt[q];
-  if (cnt_raw > p.cap) {
+  // gather the segments pass 2 wrote (one per record split and column half);
+  // a full segment or more than cap candidates in all sends the query to
+  // the exact scan
+  if (warp == 0) {
+    // lane l owns regions [l*per, (l+1)*per); an exclusive scan gives offsets
+    const int per = (p.regions + 31) >> 5;  // <= 4
+    int c_loc[4];
+    int tot = 0;
+    bool over = false;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const int r = lane * per + t;
+      int c = (t < per && r < p.regions) ? p.cand_cnt[q * p.regions + r] : 0;
+      over |= c > p.region_cap;
+      c = min(c, p.region_cap);
+      c_loc[t] = c;
+      tot += c;
+    }
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int ex = incl - tot;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const int r = lane * per + t;
+      if (t < per && r < p.regions) roff[r] = ex;
+      ex += c_loc[t];
+    }
+    const bool any_over = __any_sync(0xffffffffu, over);
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) roff[p.regions] = (any_over || total > p.cap) ? -1 : total;
+  }
+  __syncthreads();
+  const int cnt_raw = roff[p.regions];
+  if (cnt_raw < 0) {
     if (tid == 0) p.over_list[atomicAdd(p.n_over, 1)] = (int32_t)q;
     return;
+  }
+  for (int r = 0; r < p.regions; r++) {
+    const int cr = roff[r + 1] - roff[r];
+    const uint32_t *src = p.cand + q * p.cand_stride + (int64_t)r * p.region_cap;
+    for (int j = tid; j < cr; j += 256) cidx[roff[r] + j] = src[j];
   }
   const int cnt = p.degenerate[q] ? 0 : cnt_raw;
   if (tid == 0) atomicAdd(p.n_cand, (unsigned long long)cnt);
@@ -491,20 +541,31 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   const int W = p.mem + p.bits;
   const int rw = p.code_stride >> 2;
   const int j = lane & 15, half = lane >> 4;
-  const uint32_t *cand = p.cand + q * (int64_t)p.cap;
+  // each half-warp stages its candidate's record image (word 0 = start
+  // state, then the code words byte-swapped) with one coalesced load per
+  // lane, so the window loop runs from shared memory
+  uint32_t *img = stage + (warp * 2 + half) * (rw + 1);
   for (int i0 = warp * 2; i0 < cnt; i0 += 16) {
     const int i = i0 + half;
     const bool ok = i < cnt;
-    const int64_t rec = ok ? (int64_t)cand[i] : 0;
+    const int64_t rec = ok ? (int64_t)cidx[i] : 0;
     const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
-    const uint32_t st = __ldg(p.start + rec);
+    for (int w = j; w <= rw; w += 16)
+      img[w] = w == 0 ? __ldg(p.start + rec) : __byte_perm(__ldg(cw + w - 1), 0, 0x0123);
+    float rs = 1.0f, rn = 1.0f, nm = 1.0f;
+    if (ok && j == 0) {
+      rs = __ldg(p.rescale + rec);
+      if (p.rnorm) rn = __ldg(p.rnorm + rec);
+      if (p.mips) nm = __ldg(p.norms + rec);
+    }
+    __syncwarp();
     float acc = 0.0f;
     for (int b = 0; b < p.dim / 16; b++) {
       const int c = 16 * b + j;
       const int pos = 32 + c * p.bits - p.mem;
       const int w0 = pos >> 5, sh = pos & 31;
-      const uint32_t hi = w0 == 0 ? st : (w0 <= rw ? __byte_perm(__ldg(cw + w0 - 1), 0, 0x0123) : 0u);
-      const uint32_t lo = w0 + 1 <= rw ? __byte_perm(__ldg(cw + w0), 0, 0x0123) : 0u;
+      const uint32_t hi = img[w0];
+      const uint32_t lo = w0 + 1 <= rw ? img[w0 + 1] : 0u;
       const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
       acc = fmaf(qv[c], code[win], acc);
     }
@@ -513,12 +574,11 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
     acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
     if (ok && j == 0) {
-      const float rs = __ldg(p.rescale + rec);
-      const float rn = p.rnorm ? __ldg(p.rnorm + rec) : 1.0f;
       float sx = fadd(0.0f, fmul(rn, fdiv(acc, rs)));
-      if (p.mips) sx = fmul(sx, __ldg(p.norms + rec));
+      if (p.mips) sx = fmul(sx, nm);
       keys[i] = rank_key(sx, (uint32_t)rec);
     }
+    __syncwarp();  // the image is rewritten for the next candidate
   }
   __syncthreads();
   // bitonic sort, descending

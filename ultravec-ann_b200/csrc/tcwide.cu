@@ -90,6 +90,11 @@ __global__ void __launch_bounds__(W_THREADS, 1)
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 96);
+    // pass 2: this thread's segment of the query's candidate list
+    const int region = (int)blockIdx.y * 2 + half;
+    uint32_t *seg = MODE == 2 ? p.cand + q * (int64_t)p.cand_cap + (int64_t)region * p.region_cap
+                              : nullptr;
+    int seg_cnt = 0;
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
       const int64_t tile = t_begin + it;
@@ -107,8 +112,10 @@ __global__ void __launch_bounds__(W_THREADS, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acce[a]);
-      tcep::bounds_run<MODE, 3>(p, r, q, qok, theta, 2 * tile + half, tile * W_N + half * 96);
+      tcep::bounds_run<MODE, 3>(p, r, q, qok, theta, 2 * tile + half,
+                                tile * p.tile_stride * W_N + half * 96, seg, &seg_cnt);
     }
+    if (MODE == 2 && q < p.nq) p.cand_cnt[q * p.regions + region] = seg_cnt;
   } else if (warp == 8) {
     if (lane == 0) {
       // ================= MMA issue =================
@@ -156,7 +163,7 @@ __global__ void __launch_bounds__(W_THREADS, 1)
     // ================= TMA producer =================
     int64_t step = 0;
     for (int it = 0; it < ntiles && !*abort_s; it++) {
-      const int row = (int)((t_begin + it) * W_N);
+      const int row = (int)((t_begin + it) * p.tile_stride * W_N);
       for (int k = 0; k < steps; k++, step++) {
         const int s = (int)(step % W_STAGES);
         if (*abort_s ||

@@ -197,12 +197,15 @@ struct ShortlistParams {
 struct TcScanParams {
   int q_stride, cand_cap;
   int64_t nq, n, n_tiles, n_groups;
+  int64_t tile_stride;         // tile t covers records of tile t * tile_stride (pass-1 sample)
   const float *q_r;            // nq x q_stride rotated unit queries
   const uint32_t *degenerate;  // nq
   float *tmax;                 // mode 1: nq x n_groups lower-bound maxima
   const float *theta;          // mode 2: per-query threshold
-  uint32_t *cand;              // mode 2: nq x cand_cap record indices
-  int *cand_cnt;               // mode 2: nq (zeroed before the launch)
+  uint32_t *cand;              // mode 2: nq x cand_cap record indices, in segments:
+                               // region = split * 2 + column half, region_cap each
+  int *cand_cnt;               // mode 2: nq x regions segment counts
+  int regions, region_cap;
   int *err;
 };
 
@@ -229,8 +232,10 @@ struct TcRescoreParams {
   const uint8_t *codes;
   const uint32_t *start;
   const float *code, *rescale, *rnorm, *norms;
-  const uint32_t *cand;
-  const int *cand_cnt;
+  const uint32_t *cand;        // nq x cand_stride: `regions` segments of region_cap
+  const int *cand_cnt;         // nq x regions
+  int regions, region_cap;
+  int64_t cand_stride;
   const int64_t *ids;
   int64_t *out_id;
   float *out_score;

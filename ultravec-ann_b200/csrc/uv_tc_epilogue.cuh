@@ -26,11 +26,15 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
 }
 
 // r: the bounds of records rec0 .. rec0 + 32 * NL - 1 for query q; group:
-// the tile-maxima slot of this run (pass 1).
+// the tile-maxima slot of this run (pass 1).  Pass 2 appends to this
+// thread's own segment of the query's candidate list (dst, region_cap
+// slots), counting in `count`: one thread per (query, record split, column
+// half) owns a segment, so no append waits on an atomic.
 template <int MODE, int NL>
 __device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t (&r)[NL][32],
                                            int64_t q, bool qok, float theta, int64_t group,
-                                           int64_t rec0) {
+                                           int64_t rec0, uint32_t *dst = nullptr,
+                                           int *count = nullptr) {
   float mc[NL];
 #pragma unroll
   for (int l = 0; l < NL; l++) mc[l] = chunk_max(r[l]);
@@ -59,23 +63,18 @@ __device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t
         mask[l] &= room >= 32 ? 0xffffffffu : (room <= 0 ? 0u : ((1u << room) - 1u));
       }
     }
-    int cnt = 0;
+    int pos = *count;
 #pragma unroll
-    for (int l = 0; l < NL; l++) cnt += __popc(mask[l]);
-    if (cnt > 0) {
-      int pos = atomicAdd(&p.cand_cnt[q], cnt);
-      uint32_t *dst = p.cand + q * (int64_t)p.cand_cap;
-#pragma unroll
-      for (int l = 0; l < NL; l++) {
-        uint32_t mk = mask[l];
-        while (mk != 0u) {
-          const int j = __ffs(mk) - 1;
-          mk &= mk - 1u;
-          if (pos < p.cand_cap) dst[pos] = (uint32_t)(rec0 + 32 * l + j);
-          pos++;
-        }
+    for (int l = 0; l < NL; l++) {
+      uint32_t mk = mask[l];
+      while (mk != 0u) {
+        const int j = __ffs(mk) - 1;
+        mk &= mk - 1u;
+        if (pos < p.region_cap) dst[pos] = (uint32_t)(rec0 + 32 * l + j);
+        pos++;
       }
     }
+    *count = pos;
   }
 }
 
