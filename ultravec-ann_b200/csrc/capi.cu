@@ -1080,7 +1080,11 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   }
   {
     ProfScope ps("tc_theta", st);
-    uvb::tc_theta_kernel<<<(unsigned)nq, 256, 0, st>>>(tmax, n_groups1, nq, k, theta);
+    const size_t tsm = n_groups1 <= uvb::kThetaSmemKeys ? (size_t)n_groups1 * 4 : 0;
+    if (tsm > 48 * 1024)
+      UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)tsm));
+    uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(tmax, n_groups1, nq, k, theta);
     UV_CK(cudaGetLastError());
   }
   {

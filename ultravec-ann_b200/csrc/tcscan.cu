@@ -427,6 +427,7 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 
 __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_t n_tiles,
                                                         int64_t nq, int k, float *theta) {
+  extern __shared__ uint32_t keys_s[];  // n_tiles keys when they fit (see the launch)
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel[2];
   const int64_t q = blockIdx.x;
@@ -436,12 +437,16 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
     if (threadIdx.x == 0) theta[q] = -INFINITY;
     return;
   }
+  // the four radix passes read the maxima from shared memory when they fit
+  const bool staged = n_tiles <= kThetaSmemKeys;
+  if (staged)
+    for (int64_t i = threadIdx.x; i < n_tiles; i += 256) keys_s[i] = fkey(v[i]);
   uint32_t prefix = 0, mask = 0, kk = (uint32_t)k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     hist[threadIdx.x] = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < n_tiles; i += 256) {
-      const uint32_t key = fkey(v[i]);
+      const uint32_t key = staged ? keys_s[i] : fkey(v[i]);
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -581,6 +586,27 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     __syncwarp();  // the image is rewritten for the next candidate
   }
   __syncthreads();
+  if (cnt <= 1024) {
+    // rank selection: keys are unique (they carry the record), so a key's
+    // output slot is the number of larger keys; one pass of broadcast reads
+    // instead of a barrier per bitonic stage
+    for (int i = tid; i < cnt; i += 256) {
+      const uint64_t key = keys[i];
+      int rank = 0;
+#pragma unroll 8
+      for (int j2 = 0; j2 < cnt; j2++) rank += keys[j2] > key ? 1 : 0;
+      if (rank < p.k) {
+        const int64_t rec = rank_key_index(key);
+        p.out_id[q * p.k + rank] = p.ids ? p.ids[rec] : rec;
+        p.out_score[q * p.k + rank] = key32_score((uint32_t)(key >> 32));
+      }
+    }
+    for (int i = cnt + tid; i < p.k; i += 256) {
+      p.out_id[q * p.k + i] = -1;
+      p.out_score[q * p.k + i] = -INFINITY;
+    }
+    return;
+  }
   // bitonic sort, descending
   for (int size = 2; size <= pow2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {

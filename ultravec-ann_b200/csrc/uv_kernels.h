@@ -275,6 +275,9 @@ int tc_tile_queries();
 int tc_dim();
 __global__ void tc_gmax_kernel(const TcPrepareParams p);
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
+// per-query k-th largest tile maximum; the n_tiles keys are staged in dynamic
+// shared memory (4 bytes each) when n_tiles <= kThetaSmemKeys
+constexpr int kThetaSmemKeys = 12288;
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);
 __global__ void tc_rescore_kernel(const TcRescoreParams p);
