@@ -1014,14 +1014,14 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   // Pass 1 bounds a sample of the tiles (every S-th): the k-th largest group
   // maximum of any subset of groups is still a score at least k records
   // reach, so theta stays valid, and pass 2 admits about k*S candidates
-  // instead of k.  Pass 1 costs ~1/S, the candidates ~k*S: S = sqrt(1100/k)
-  // balances them at the 1M x 10k bench shape (measured optimum 3 at
-  // k = 100, 6-10 at k = 10), capped so that k*S stays well inside the
-  // candidate lists and the sample keeps at least 8k groups.
+  // instead of k.  Pass 1 costs ~1/S, the candidates ~k*S: S = sqrt(1600/k)
+  // balances them at the 1M x 10k bench shape (measured optimum 4 at
+  // k = 100, 10 at k = 10), capped at 10 and so that k*S stays well inside
+  // the candidate lists, and the sample keeps at least 8k groups.
   int64_t S = g_tc_sample > 0
                   ? g_tc_sample
                   : std::max<int64_t>(1, std::min<int64_t>(
-                                             16, (int64_t)std::lround(std::sqrt(1100.0 / k))));
+                                             10, (int64_t)std::lround(std::sqrt(1600.0 / k))));
   if (g_tc_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
   const int64_t n_tiles1 = (n_tiles + S - 1) / S;
@@ -1127,14 +1127,17 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     rp.n_over = flags + 1;
     rp.n_cand = (unsigned long long *)(flags + 2);
     const size_t rsmem = (size_t)cap * 12 + (size_t)((regions + 4) & ~3) * 4 + (size_t)d * 4 +
-                         (size_t)16 * (c->code_stride / 4 + 1) * 4 +
-                         (rp.table_in_smem ? (size_t)c->table_len * 4 : 0);
+                         (rp.table_in_smem ? (size_t)c->table_len * 4 : 0) +
+                         (size_t)16 * (c->code_stride / 4 + 1) * 4;
     if (rsmem > 227 * 1024) return fail(UV_EUNSUPPORTED, "prefilter rescoring exceeds shared memory");
-    UV_CK(cudaFuncSetAttribute(uvb::tc_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // long candidate lists (about k*S per query) score one candidate per
+    // thread; short ones half a warp per candidate
+    const void *rk = uvb::tc_rescore_kernel_ptr(c->cfg.bits, (int64_t)k * S >= 128);
+    UV_CK(cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
     void *args[] = {&rp};
     ProfScope ps("tc_rescore", st);
-    UV_CK(cudaLaunchKernel((const void *)uvb::tc_rescore_kernel, dim3((unsigned)nq), dim3(256), args,
+    UV_CK(cudaLaunchKernel(rk, dim3((unsigned)nq), dim3(256), args,
                            rsmem, st));
   }
   int h_flags[4] = {0, 0, 0, 0};

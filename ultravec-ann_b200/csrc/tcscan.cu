@@ -48,6 +48,7 @@
 #include "uv_kernels.h"
 #include "uv_tc.cuh"
 #include "uv_tc_epilogue.cuh"
+#include "uv_score_thread.cuh"
 
 namespace uvb {
 
@@ -476,14 +477,14 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
 // candidates per warp at a time, one per half-warp.  A query whose list
 // overflowed is recorded for the exact fallback scan.
 // ---------------------------------------------------------------------------
+template <int BITS, bool PER_THREAD>
 __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   uint64_t *keys = (uint64_t *)sm;                    // cap (power of two)
   uint32_t *cidx = (uint32_t *)(keys + p.cap);        // cap gathered candidates
   int *roff = (int *)(cidx + p.cap);                  // regions + 1 segment offsets
   float *qv = (float *)(roff + ((p.regions + 4) & ~3));  // dim
-  uint32_t *stage = (uint32_t *)(qv + p.dim);         // 16 x (words per record + 1)
-  float *table = (float *)(stage + 16 * ((p.code_stride >> 2) + 1));  // table_len (optional)
+  float *table = qv + p.dim;                          // table_len (optional)
   const int64_t q = blockIdx.x;
   if (q >= p.nq) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -545,68 +546,67 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   const float *code = p.table_in_smem ? table : p.code;
   const int W = p.mem + p.bits;
   const int rw = p.code_stride >> 2;
-  const int j = lane & 15, half = lane >> 4;
-  // each half-warp stages its candidate's record image (word 0 = start
-  // state, then the code words byte-swapped) with one coalesced load per
-  // lane, so the window loop runs from shared memory
-  uint32_t *img = stage + (warp * 2 + half) * (rw + 1);
-  for (int i0 = warp * 2; i0 < cnt; i0 += 16) {
-    const int i = i0 + half;
-    const bool ok = i < cnt;
-    const int64_t rec = ok ? (int64_t)cidx[i] : 0;
-    const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
-    for (int w = j; w <= rw; w += 16)
-      img[w] = w == 0 ? __ldg(p.start + rec) : __byte_perm(__ldg(cw + w - 1), 0, 0x0123);
-    float rs = 1.0f, rn = 1.0f, nm = 1.0f;
-    if (ok && j == 0) {
-      rs = __ldg(p.rescale + rec);
-      if (p.rnorm) rn = __ldg(p.rnorm + rec);
-      if (p.mips) nm = __ldg(p.norms + rec);
+  if constexpr (!PER_THREAD) {
+    // few candidates: half a warp per candidate, 16 lanes over the
+    // coordinates (the 16 FMA chains), its record image staged in shared
+    // memory by one coalesced load per lane
+    const int W = p.mem + p.bits;
+    const int rw = p.code_stride >> 2;
+    const int j = lane & 15, half = lane >> 4;
+    uint32_t *img = (uint32_t *)(table + (p.table_in_smem ? p.table_len : 0)) +
+                    (warp * 2 + half) * (rw + 1);
+    for (int i0 = warp * 2; i0 < cnt; i0 += 16) {
+      const int i = i0 + half;
+      const bool ok = i < cnt;
+      const int64_t rec = ok ? (int64_t)cidx[i] : 0;
+      const uint32_t *cw = (const uint32_t *)(p.codes + rec * (int64_t)p.code_stride);
+      for (int w = j; w <= rw; w += 16)
+        img[w] = w == 0 ? __ldg(p.start + rec) : __byte_perm(__ldg(cw + w - 1), 0, 0x0123);
+      float rs = 1.0f, rn = 1.0f, nm = 1.0f;
+      if (ok && j == 0) {
+        rs = __ldg(p.rescale + rec);
+        if (p.rnorm) rn = __ldg(p.rnorm + rec);
+        if (p.mips) nm = __ldg(p.norms + rec);
+      }
+      __syncwarp();
+      float acc = 0.0f;
+      for (int b = 0; b < p.dim / 16; b++) {
+        const int c = 16 * b + j;
+        const int pos = 32 + c * p.bits - p.mem;
+        const int w0 = pos >> 5, sh = pos & 31;
+        const uint32_t hi = img[w0];
+        const uint32_t lo = w0 + 1 <= rw ? img[w0 + 1] : 0u;
+        const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
+        acc = fmaf(qv[c], code[win], acc);
+      }
+      acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+      acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+      acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+      acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+      if (ok && j == 0) {
+        float sx = fadd(0.0f, fmul(rn, fdiv(acc, rs)));
+        if (p.mips) sx = fmul(sx, nm);
+        keys[i] = rank_key(sx, (uint32_t)rec);
+      }
+      __syncwarp();  // the image is rewritten for the next candidate
     }
-    __syncwarp();
-    float acc = 0.0f;
-    for (int b = 0; b < p.dim / 16; b++) {
-      const int c = 16 * b + j;
-      const int pos = 32 + c * p.bits - p.mem;
-      const int w0 = pos >> 5, sh = pos & 31;
-      const uint32_t hi = img[w0];
-      const uint32_t lo = w0 + 1 <= rw ? img[w0 + 1] : 0u;
-      const uint32_t win = __funnelshift_l(lo, hi, sh) >> (32 - W);
-      acc = fmaf(qv[c], code[win], acc);
-    }
-    acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-    acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-    acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-    acc = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
-    if (ok && j == 0) {
+  } else {
+    // many candidates: one thread per candidate, the whole record dot in
+    // registers (record_dot_thread, the same association), many candidates
+    // in flight per SM
+    for (int i = tid; i < cnt; i += 256) {
+      const int64_t rec = (int64_t)cidx[i];
+      const uint8_t *rc = p.codes + rec * (int64_t)p.code_stride;
+      const uint32_t st = __ldg(p.start + rec);
+      const float rs = __ldg(p.rescale + rec);
+      const float rn = p.rnorm ? __ldg(p.rnorm + rec) : 1.0f;
+      const float acc = record_dot_thread<BITS>(qv, rc, st, p.dim, p.mem, p.code_stride, code, 1, 0);
       float sx = fadd(0.0f, fmul(rn, fdiv(acc, rs)));
-      if (p.mips) sx = fmul(sx, nm);
+      if (p.mips) sx = fmul(sx, __ldg(p.norms + rec));
       keys[i] = rank_key(sx, (uint32_t)rec);
     }
-    __syncwarp();  // the image is rewritten for the next candidate
   }
   __syncthreads();
-  if (cnt <= 1024) {
-    // rank selection: keys are unique (they carry the record), so a key's
-    // output slot is the number of larger keys; one pass of broadcast reads
-    // instead of a barrier per bitonic stage
-    for (int i = tid; i < cnt; i += 256) {
-      const uint64_t key = keys[i];
-      int rank = 0;
-#pragma unroll 8
-      for (int j2 = 0; j2 < cnt; j2++) rank += keys[j2] > key ? 1 : 0;
-      if (rank < p.k) {
-        const int64_t rec = rank_key_index(key);
-        p.out_id[q * p.k + rank] = p.ids ? p.ids[rec] : rec;
-        p.out_score[q * p.k + rank] = key32_score((uint32_t)(key >> 32));
-      }
-    }
-    for (int i = cnt + tid; i < p.k; i += 256) {
-      p.out_id[q * p.k + i] = -1;
-      p.out_score[q * p.k + i] = -INFINITY;
-    }
-    return;
-  }
   // bitonic sort, descending
   for (int size = 2; size <= pow2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -640,6 +640,21 @@ const void *tc_scan_kernel_ptr(int mode, int shape) {
   if (shape == 3)
     return mode == 1 ? (const void *)tc_scan_kernel<1, 3> : (const void *)tc_scan_kernel<2, 3>;
   return mode == 1 ? (const void *)tc_scan_kernel<1, 1> : (const void *)tc_scan_kernel<2, 1>;
+}
+
+const void *tc_rescore_kernel_ptr(int bits, bool per_thread) {
+#define UV_RS_CASE(b)                                                              \
+  case b:                                                                          \
+    return per_thread ? (const void *)tc_rescore_kernel<b, true>                   \
+                      : (const void *)tc_rescore_kernel<b, false>;
+  switch (bits) {
+    UV_RS_CASE(1)
+    UV_RS_CASE(2)
+    UV_RS_CASE(3)
+    UV_RS_CASE(4)
+  }
+#undef UV_RS_CASE
+  return nullptr;
 }
 
 int tc_threads() { return TC_THREADS; }

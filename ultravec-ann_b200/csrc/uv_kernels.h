@@ -280,7 +280,9 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 constexpr int kThetaSmemKeys = 12288;
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);
-__global__ void tc_rescore_kernel(const TcRescoreParams p);
+// bits 1..4; per_thread: one thread per candidate (long lists), else half a
+// warp per candidate (short lists)
+const void *tc_rescore_kernel_ptr(int bits, bool per_thread);
 // tcwide.cu: the prefilter for rows of any width (K streamed in chunks of 64)
 const void *tc_wide_kernel_ptr(int mode);
 size_t tc_wide_smem_bytes();
