@@ -195,6 +195,9 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * the first search after a change of the records, per score mode, and held
  * until the next change or uv_index_destroy; (2 x dim rounded up to 64 + 32)
  * bytes per record and mode) or makes them in per-search scratch (0);
+ * "tc_sample" fixes the prefilter's first-pass tile stride (0 automatic:
+ * round(sqrt(1600/k)), at most 10); "tc_prepare" 1 makes the prefilter's
+ * rows with the generic kernel (0 automatic);
  * "coset_nearest" selects how the coset trellis finds each block's nearest
  * kept point (0 automatic: every book point scored for books of <= 8192
  * points, the reference's bisection + ball search where the minimum is tied

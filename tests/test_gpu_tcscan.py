@@ -218,3 +218,30 @@ def test_sampled_threshold_matches_exact_kernel(uv, tc_mode, sample, k):
     finally:
         uv.set_tuning("tc_sample", 0)
     assert same(a, b)
+
+
+@pytest.mark.parametrize("bits,mem", [(1, 8), (2, 8), (4, 6), (2, 12)])
+def test_row_kernels_agree(uv, bits, mem):
+    """The shared-memory-table row kernel and the generic one make the same
+    operand rows: same candidates, same results."""
+    n, nq, dim = 150_000, 64, 128
+    base = rand_rows(n, dim, 70 + bits)
+    queries = rand_rows(nq, dim, 71)
+    out = []
+    try:
+        uv.set_tuning("tc_scan", 2)
+        for mode in (0, 1):
+            uv.set_tuning("tc_prepare", mode)
+            index = uv.Index(uv.Codec(dim, bits, mem))
+            index.add_batch(base)
+            uv.profile_enable(True)
+            r = index.search(queries, 50, mips=True)
+            cand = uv.profile_read("tc_candidates")[1]
+            uv.profile_enable(False)
+            out.append((r, cand))
+            index.close()
+    finally:
+        uv.set_tuning("tc_prepare", 0)
+        uv.set_tuning("tc_scan", 0)
+    assert same(out[0][0], out[1][0])
+    assert out[0][1] == out[1][1] > 0

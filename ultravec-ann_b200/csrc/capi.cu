@@ -22,6 +22,7 @@ int g_tc_shape = 0;
 int g_tc_cache = 1;
 int g_coset_nearest = 0;
 int g_tc_sample = 0;
+int g_tc_prepare = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 bool g_prof_on = false;
@@ -895,8 +896,17 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     ProfScope ps("tc_prepare", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
                            dim3(256), args, 0, st));
-    UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
-                           dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
+    // widths 1, 2, 4 with a table of at most 64 KB: the shared-memory
+    // table and 16-byte code reads; otherwise the generic kernel
+    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits);
+    const size_t tsm = (size_t)4 << (c->cfg.mem + c->cfg.bits);
+    if (fk != nullptr && tsm <= 64 * 1024 && g_tc_prepare != 1) {
+      UV_CK(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
+      UV_CK(cudaLaunchKernel(fk, dim3((unsigned)((n_pad + 255) / 256)), dim3(256), args, tsm, st));
+    } else {
+      UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
+                             dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
+    }
     return UV_OK;
   };
   if (g_tc_cache == 0) {
@@ -1286,6 +1296,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_cache") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_cache must be 0 or 1");
     g_tc_cache = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "tc_prepare") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_prepare must be 0 or 1");
+    g_tc_prepare = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "tc_sample") == 0) {

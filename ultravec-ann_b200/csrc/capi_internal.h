@@ -160,6 +160,7 @@ extern int g_tc_shape;         // uv_set_tuning("tc_shape")
 extern int g_tc_cache;         // uv_set_tuning("tc_cache")
 extern int g_coset_nearest;    // uv_set_tuning("coset_nearest")
 extern int g_tc_sample;        // uv_set_tuning("tc_sample")
+extern int g_tc_prepare;       // uv_set_tuning("tc_prepare")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 

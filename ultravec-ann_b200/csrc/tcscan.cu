@@ -413,6 +413,87 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
   xext[1] = make_uint4(0, 0, 0, 0);
 }
 
+// The same rows for widths 1, 2 and 4 with the code table in shared memory:
+// each record's code is read 16 bytes at a time and its windows are cut with
+// shifts known at compile time (code rows are padded to 16 bytes); one
+// thread per record, the same arithmetic as tc_prepare_records_kernel.
+template <int BITS>
+__global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPrepareParams p) {
+  extern __shared__ float tab[];
+  for (int i = threadIdx.x; i < (1 << (p.mem + BITS)); i += blockDim.x) tab[i] = __ldg(p.code + i);
+  __syncthreads();
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= p.n_pad) return;
+  uint4 *xrow = (uint4 *)(p.x16 + r * p.kpad);
+  uint4 *xext = (uint4 *)(p.xext + r * TC_X);
+  const uint32_t hinf = 0x7C00u;  // fp16 +inf
+  float g = r < p.n ? record_g(p, r) : 0.0f;
+  const bool bad = r >= p.n || !isfinite(g) || g < 0.0f;
+  const float gmax = __uint_as_float(*p.gmax_bits);
+  const double top = (double)gmax * (double)p.code_absmax;
+  const int e = top > 0.0 ? (int)ceil(log2(top)) - 14 : 0;
+  const double s = ldexp(1.0, -e);
+  if (bad) {
+    for (int c = 0; c < p.kpad / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
+    xext[0] = make_uint4(hinf, 0, 0, 0);
+    xext[1] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint32_t wmask = (1u << (p.mem + BITS)) - 1u;
+  const uint4 *cw4 = (const uint4 *)(p.codes + r * (int64_t)p.code_stride);
+  const float gs = (float)((double)g * s);  // exact: s is a power of two
+  double xs = 0.0;
+  constexpr int CPC = 128 / BITS;  // coordinates per 16-byte chunk
+  uint32_t prev = __ldg(p.start + r);
+  const int nchunks = (p.dim + CPC - 1) / CPC;
+  for (int k = 0; k < nchunks; k++) {
+    const uint4 raw = __ldg(cw4 + k);
+    const uint32_t w[4] = {__byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
+                           __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123)};
+#pragma unroll
+    for (int g8 = 0; g8 < CPC / 8; g8++) {
+      const int c0 = k * CPC + g8 * 8;
+      if (c0 >= p.dim) break;
+      uint32_t o[4];
+#pragma unroll
+      for (int h = 0; h < 8; h++) {
+        const int e2 = (g8 * 8 + h + 1) * BITS;  // chunk bits consumed through this window
+        const int wi = (e2 - 1) >> 5;
+        const int sh = 31 - ((e2 - 1) & 31);
+        const uint32_t hiw = wi == 0 ? prev : w[wi > 0 ? wi - 1 : 0];
+        const uint64_t v = ((uint64_t)hiw << 32) | w[wi];
+        const float x = tab[(uint32_t)(v >> sh) & wmask];
+        xs += (double)x * (double)x;
+        const uint32_t hx = __half_as_ushort(__float2half_rn(fmul(gs, x)));
+        if (h & 1)
+          o[h >> 1] |= hx << 16;
+        else
+          o[h >> 1] = hx;
+      }
+      xrow[c0 / 8] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    prev = w[3];
+  }
+  for (int c = (p.dim + 7) / 8; c < p.kpad / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
+  const double qn = 1.0001;
+  const double xn = sqrt(xs) * (1.0 + 1e-12);
+  const double sg = s * (double)g;
+  const double cd = (sg * p.eps * qn * xn + 1.1920928955078125e-7 * sqrt((double)p.dim) *
+                                                (qn + sg * xn)) * (1.0 + 1e-6);
+  const uint32_t hc = __half_as_ushort(__float2half_ru(__double2float_ru(cd)));
+  xext[0] = make_uint4(hc, 0, 0, 0);
+  xext[1] = make_uint4(0, 0, 0, 0);
+}
+
+const void *tc_prepare_records_fast_ptr(int bits) {
+  switch (bits) {
+    case 1: return (const void *)tc_prepare_records_fast_kernel<1>;
+    case 2: return (const void *)tc_prepare_records_fast_kernel<2>;
+    case 4: return (const void *)tc_prepare_records_fast_kernel<4>;
+  }
+  return nullptr;
+}
+
 // ---------------------------------------------------------------------------
 // theta[q] = k-th largest of the query's tile maxima (radix select on
 // order-preserving keys, four 8-bit rounds).  Fewer than k tiles: -inf.

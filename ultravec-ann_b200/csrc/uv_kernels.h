@@ -275,6 +275,9 @@ int tc_tile_queries();
 int tc_dim();
 __global__ void tc_gmax_kernel(const TcPrepareParams p);
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
+// widths 1, 2, 4 with the table in shared memory (4 << (mem + bits) bytes,
+// 256 threads); null for other widths
+const void *tc_prepare_records_fast_ptr(int bits);
 // per-query k-th largest tile maximum; the n_tiles keys are staged in dynamic
 // shared memory (4 bytes each) when n_tiles <= kThetaSmemKeys
 constexpr int kThetaSmemKeys = 12288;
