@@ -372,7 +372,8 @@ int uv_ivf_load(const uv_codec *codec, const char *path, uv_ivf **out);
 typedef struct uv_coset uv_coset;
 
 /* CosetTrellis::new (coset_trellis.rs:121-190): dim % 8 == 0 and bits 1..3
- * (UV_EINVAL otherwise, where the reference panics); mem 1..20 (the
+ * (UV_EINVAL otherwise, where the reference panics), dim <= 4096
+ * (UV_EUNSUPPORTED above); mem 1..20 (the
  * reference reads ULTRAVEC_TRELLIS_MEM, default 12); the rotation as
  * Rotor::new_oblivious (seed 42, 3 rounds by default).  The books of a bit
  * width are built once per process (three bits: 2^24 points, seconds). */

@@ -1136,13 +1136,14 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     rp.over_list = over_list;
     rp.n_over = flags + 1;
     rp.n_cand = (unsigned long long *)(flags + 2);
+    const bool per_thread = (int64_t)k * S >= 128;
     const size_t rsmem = (size_t)cap * 12 + (size_t)((regions + 4) & ~3) * 4 + (size_t)d * 4 +
                          (rp.table_in_smem ? (size_t)c->table_len * 4 : 0) +
                          (size_t)16 * (c->code_stride / 4 + 1) * 4;
     if (rsmem > 227 * 1024) return fail(UV_EUNSUPPORTED, "prefilter rescoring exceeds shared memory");
     // long candidate lists (about k*S per query) score one candidate per
     // thread; short ones half a warp per candidate
-    const void *rk = uvb::tc_rescore_kernel_ptr(c->cfg.bits, (int64_t)k * S >= 128);
+    const void *rk = uvb::tc_rescore_kernel_ptr(c->cfg.bits, per_thread);
     UV_CK(cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
     void *args[] = {&rp};

@@ -249,6 +249,8 @@ int uv_coset_create(int32_t dim, int32_t bits, int32_t mem, uint64_t rotation_se
   if (out == nullptr) return fail(UV_EINVAL, "null argument");
   *out = nullptr;
   if (dim <= 0 || dim % 8 != 0) return fail(UV_EINVAL, "coset trellis requires dim % 8 == 0");
+  // one warp stages eight rows of the prep and reconstruction in 227 KB
+  if (dim > 4096) return fail(UV_EUNSUPPORTED, "coset trellis rows wider than 4096 are not built");
   if (bits < 1 || bits > 3) return fail(UV_EINVAL, "coset trellis supports bits in 1..3");
   if (mem < 1 || mem > 20) return fail(UV_EINVAL, "mem must be 1..20");
   int ndev = 0;
