@@ -125,6 +125,91 @@ def test_sharded_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
     assert (tmp_path / "ok").read_text() == "1"
 
 
+def test_ivf_list_owners_balance_bytes(uv):
+    from ultravec_ann_b200.shard import ivf_list_owners, ivf_owned_rows
+
+    rng = np.random.default_rng(5)
+    sizes = rng.geometric(1 / 300, 4096)
+    for world in (1, 2, 4, 8):
+        own = ivf_list_owners(sizes, world)
+        load = np.bincount(own, weights=sizes, minlength=world)
+        assert set(own.tolist()) == set(range(world))
+        assert load.max() - load.min() <= sizes.max()
+        assert np.array_equal(own, ivf_list_owners(sizes, world))
+    assign = rng.integers(0, 16, 500)
+    own = ivf_list_owners(np.bincount(assign, minlength=16), 3)
+    parts = [ivf_owned_rows(assign, own, r) for r in range(3)]
+    assert np.array_equal(np.sort(np.concatenate(parts)), np.arange(500))
+
+
+def _gloo_ivf_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    import sys
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    sys.path.insert(0, str(REPO))
+    import oracle as O
+    from ultravec_ann_b200_loader import load
+
+    load()
+    from ultravec_ann_b200.shard import (gather_topk, ivf_list_owners, ivf_owned_rows,
+                                         merge_host)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dim, nlist = 64, 12
+    db = O.rand_unit(900, dim, 41)
+    qs = O.rand_unit(15, dim, 43)
+    cen = O.kmeans(db, nlist, 42)
+    asg = O.assign(db, cen)
+    c = O.Codec(dim, 2, 8)
+
+    def ivf_search(rows_idx, centered):
+        sub = asg[rows_idx]
+        order = rows_idx[np.argsort(sub, kind="stable")]
+        off = np.zeros(nlist + 1, np.int64)
+        np.add.at(off, asg[order].astype(np.int64) + 1, 1)
+        off = np.cumsum(off)
+        enc = c.ivf_encode(db[order], cen if centered else None, asg[order])
+        return c.ivf_search_topk(cen, off, order.astype(np.int64), enc, centered, qs, 4, 10)
+
+    owners = ivf_list_owners(np.bincount(asg, minlength=nlist), world)
+    ok = True
+    for centered in (False, True):
+        ids, sc = ivf_search(ivf_owned_rows(asg, owners, rank), centered)
+        g_ids, g_sc = gather_topk(torch.from_numpy(ids), torch.from_numpy(sc), 10, dist,
+                                  merge_host)
+        if rank == 0:
+            want_ids, want_sc = ivf_search(np.arange(len(db)), centered)
+            ok &= np.array_equal(g_ids.numpy(), want_ids) and np.array_equal(
+                g_sc.numpy().view(np.uint32), want_sc.view(np.uint32))
+    if rank == 0:
+        Path(result_dir, "ok").write_text("1" if ok else "0")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_ivf_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
+    """world_size 2 on CPU: posting lists dealt by bytes, every rank probes
+    all centroids and scans its own lists (the oracle stands in for the
+    device search), all-gather, merge == the IVF top-k of the whole index,
+    centered and not."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_gloo_ivf_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    assert (tmp_path / "ok").read_text() == "1"
+
+
 def test_bench_generator_shapes_and_centering():
     import sys
 

@@ -1,10 +1,14 @@
-"""Host-side sharding of the flat index across ranks (one process per GPU).
+"""Host-side sharding across ranks (one process per GPU).
 
-The base rows are split into contiguous ranges; every rank encodes and scans
-its own range (records keep their global row ids), and the per-rank top-k
-lists are combined by one all-gather and a merge.  The merge is a function
-argument so that the same sequence runs with the device merge
-(`uv_topk_merge`) under NCCL and with a host merge under gloo.
+Flat index: the base rows are split into contiguous ranges; every rank
+encodes and scans its own range (records keep their global row ids).  IVF
+index: the posting lists are dealt to ranks so that each rank holds about the
+same number of record bytes; every rank keeps all centroids, probes
+redundantly, and scans only the probed lists it owns, so each probed list is
+scanned exactly once.  Either way the per-rank top-k lists are combined by
+one all-gather and a merge.  The merge is a function argument so that the
+same sequence runs with the device merge (`uv_topk_merge`) under NCCL and
+with a host merge under gloo.
 """
 from __future__ import annotations
 
@@ -14,6 +18,34 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     if world < 1 or not 0 <= rank < world:
         raise ValueError("bad rank/world")
     return rank * n // world, (rank + 1) * n // world
+
+
+def ivf_list_owners(list_sizes, world: int):
+    """Owner rank of every posting list, balancing record bytes: lists in
+    descending size (ties by list number) each go to the rank holding the
+    fewest records so far (ties by lower rank).  Deterministic, so every rank
+    computes the same map from the same sizes."""
+    import numpy as np
+
+    if world < 1:
+        raise ValueError("bad world size")
+    sizes = np.asarray(list_sizes, np.int64)
+    order = np.lexsort((np.arange(len(sizes)), -sizes))
+    load = np.zeros(world, np.int64)
+    owner = np.empty(len(sizes), np.int32)
+    for l in order:
+        r = int(np.argmin(load))
+        owner[l] = r
+        load[r] += sizes[l]
+    return owner
+
+
+def ivf_owned_rows(assign, owners, rank: int):
+    """Row numbers (ascending) whose posting list `rank` owns."""
+    import numpy as np
+
+    assign = np.asarray(assign)
+    return np.nonzero(np.asarray(owners)[assign] == rank)[0]
 
 
 def gather_topk(local_ids, local_scores, k: int, dist, merge):
