@@ -744,10 +744,6 @@ def run_secondary(args):
             "prepare_ms": prep_ms, "bytes_per_candidate": per_cand,
             "achieved_gbs": ncand * per_cand / (kern_ms * 1e-3) / 1e9, "bits": 2, "mem": 8})
     elif args.workload == "coset":
-        import os
-        import sys
-        import time
-
         sys.path.insert(0, str(REPO / "oracle"))
         import oracle as O  # the CPU oracle: the timed CPU baseline only
 

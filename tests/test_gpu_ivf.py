@@ -178,3 +178,41 @@ def test_device_tensors_in_and_out(oracle, uv):
     gi, gs = ivf.search(qd, 10, 3)
     hi, hs = ivf.search(rows[:16], 10, 3)
     assert gi.is_cuda and np.array_equal(gi.cpu().numpy(), hi) and bits_equal(gs.cpu().numpy(), hs)
+
+
+@pytest.mark.parametrize("dim,nlist", [(128, 300), (256, 777), (2048, 512)])
+def test_tensor_core_probe_matches_oracle(oracle, uv, dim, nlist):
+    """The probe from tensor-core dots plus exact rechecks (nlist >= 256)
+    returns the oracle's lists: duplicated centroids (exact ties, lower list
+    first), a zero centroid, zero and scaled queries, nprobe up to nlist; and
+    the same lists and search results as the exact device probe."""
+    rng = np.random.default_rng(dim + nlist)
+    cen = clustered(nlist, dim, 8, dim + 5)
+    cen[7] = cen[3]           # exact tie with list 3
+    cen[nlist - 1] = cen[0]   # and with list 0
+    cen[11] = 0.0             # cosine 0 against every query
+    queries = clustered(60, dim, 8, dim + 6) * np.float32(3.0)
+    queries[0] = 0.0          # every cosine 0: lists in index order
+    queries[1] = cen[3] * np.float32(0.5)
+    base = clustered(1500, dim, 8, dim + 7)
+    codec = uv.Codec(dim, 2, 6)
+    ivf = uv.IvfIndex(codec, cen, centered=False)
+    ivf.build(base)
+    try:
+        for nprobe in (1, 4, 37, nlist):
+            uv.set_tuning("ivf_tc_probe", 0)
+            got = ivf.probe(queries, nprobe)
+            if nprobe <= 37:
+                want = np.stack([oracle.ivf_probe(cen, q, nprobe) for q in queries])
+                assert np.array_equal(got, want), nprobe
+            uv.set_tuning("ivf_tc_probe", 1)
+            exact = ivf.probe(queries, nprobe)
+            assert np.array_equal(got, exact), nprobe
+            if nprobe in (1, 4):
+                uv.set_tuning("ivf_tc_probe", 0)
+                a = ivf.search(queries, 10, nprobe)
+                uv.set_tuning("ivf_tc_probe", 1)
+                b = ivf.search(queries, 10, nprobe)
+                assert np.array_equal(a[0], b[0]) and bits_equal(a[1], b[1])
+    finally:
+        uv.set_tuning("ivf_tc_probe", 0)

@@ -23,6 +23,7 @@ int g_tc_cache = 1;
 int g_coset_nearest = 0;
 int g_tc_sample = 0;
 int g_tc_prepare = 0;
+int g_ivf_tc_probe = 0;
 std::atomic<int64_t> g_tc_last_candidates{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 bool g_prof_on = false;
@@ -1194,6 +1195,29 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
 
 }  // namespace
 
+namespace uvcapi {
+
+// A 2D fp16 tensor map over rows x cols elements (row stride cols * 2
+// bytes), boxes of box_cols x box_rows, 128-byte or 32-byte swizzle.
+int fp16_tensor_map(CUtensorMap *m, const void *base, int64_t rows, int cols, int box_cols,
+                    int box_rows, bool sw128) {
+  EncodeTiledFn enc = nullptr;
+  UV_TRY(encode_tiled_fn(&enc));
+  const cuuint32_t estride[2] = {1, 1};
+  const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const CUresult r =
+      enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), gdim, gstride, box,
+          estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled failed");
+  return UV_OK;
+}
+
+}  // namespace uvcapi
+
 extern "C" {
 
 int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_t k, int32_t mode,
@@ -1297,6 +1321,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "tc_cache") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_cache must be 0 or 1");
     g_tc_cache = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "ivf_tc_probe") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "ivf_tc_probe must be 0 or 1");
+    g_ivf_tc_probe = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "tc_prepare") == 0) {

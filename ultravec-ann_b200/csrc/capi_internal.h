@@ -4,6 +4,7 @@
 
 #include "ultravec_b200.h"
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -161,6 +162,7 @@ extern int g_tc_cache;         // uv_set_tuning("tc_cache")
 extern int g_coset_nearest;    // uv_set_tuning("coset_nearest")
 extern int g_tc_sample;        // uv_set_tuning("tc_sample")
 extern int g_tc_prepare;       // uv_set_tuning("tc_prepare")
+extern int g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
 extern bool g_prof_on;
 extern std::vector<ProfRec> g_prof;
 
@@ -231,6 +233,13 @@ struct uv_ivf {
   int64_t *ids = nullptr;
   int sl_c = 0, sl_asym = 0, sl_weight = 1;  // the 1-bit shortlist (0 = off)
   uint8_t *signs = nullptr;                  // n x sign_stride when the shortlist is on
+  // the probe's tensor-core operand rows of the unit centroids (made on the
+  // first probe that can use them; state -1 when a centroid norm is not finite)
+  mutable std::mutex tc_mu;
+  mutable int tc_state = 0;
+  mutable uint16_t *c16 = nullptr;   // c_pad x kpad
+  mutable uint16_t *cext = nullptr;  // c_pad x 16, zero
+  mutable int64_t c_pad = 0;
 };
 
 // The tensor-core prefilter's fp16 operand rows (tcscan.cu / tcwide.cu),
@@ -289,6 +298,9 @@ int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_ke
                  const float *in_score, const int64_t *in_id, int64_t *out_id, float *out_score,
                  cudaStream_t st, const int64_t *row_off = nullptr,
                  const int32_t *out_row = nullptr);
+// a 2D fp16 TMA tensor map (capi.cu)
+int fp16_tensor_map(CUtensorMap *m, const void *base, int64_t rows, int cols, int box_cols,
+                    int box_rows, bool sw128);
 // normalize + rotate queries; u (unit, unrotated) optional
 int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *centroids,
                 int n_centroids, float *q_r, float *qc, uint32_t *degen, float *u,

@@ -5,6 +5,8 @@
 // probed list is one contiguous record range for the scan kernel.  Build and
 // search never leave the device except for the stable bucketing of rows by
 // list (a counting sort of n u32 on the host, the reference's bucket loop).
+#include <cmath>
+
 #include "capi_internal.h"
 
 using namespace uvcapi;
@@ -125,6 +127,168 @@ void free_lists(uv_ivf *ix) {
   ix->n = 0;
 }
 
+// The probe on the tensor cores: every (query, centroid) dot of the unit
+// rows in fp16 (tcwide.cu, mode 3), then per query the exact cosines of the
+// centroids that can still reach the np-th best (probe_refine_kernel) --
+// the same lists as the exact path below.  Sets *used = false outside the
+// shapes it is built for (rows a multiple of 32 up to 4096 wide, 256 to
+// 8192 centroids) and when a centroid norm is not finite.
+//
+// Bound: with u = 2^-24 and unit rows, the fp16 dot differs from the exact
+// cosine by at most 2^-10 (two fp16 roundings) + 2^-12 (tensor-core
+// accumulation, as the flat prefilter's bound) + 4 d u (the f32 norms and
+// divisions of both sides, fp16 subnormals, and the reference's sequential
+// f32 dot); the kernel uses 1.25 times that.
+constexpr int kProbeMinLists = 256;
+
+int tc_probe(const uv_ivf *ix, const float *d_q, const float *qn, int64_t nq, int np, int ld,
+             int32_t *lists, cudaStream_t st, Scratch &sc, bool *used) {
+  *used = false;
+  const int d = ix->codec->cfg.dim;
+  const int nlist = ix->nlist;
+  if (g_ivf_tc_probe == 1 || d % 32 != 0 || d > 4096 || nlist < kProbeMinLists || np > nlist ||
+      nlist > 8192)
+    return UV_OK;
+  const int kpad = (d + 63) / 64 * 64;
+  const int TN = 192, TM = 128;
+  {
+    std::lock_guard<std::mutex> lk(ix->tc_mu);
+    if (ix->tc_state == 0) {
+      std::vector<float> hn(nlist);
+      UV_CK(cudaMemcpyAsync(hn.data(), ix->cnorm, sizeof(float) * nlist, cudaMemcpyDeviceToHost,
+                            st));
+      UV_CK(cudaStreamSynchronize(st));
+      bool finite = true;
+      for (float v : hn) finite &= std::isfinite(v);
+      if (!finite) {
+        ix->tc_state = -1;
+      } else {
+        const int64_t c_pad = (nlist + TN - 1) / TN * TN;
+        UV_CK(cudaMalloc((void **)&ix->c16, sizeof(uint16_t) * (size_t)c_pad * kpad));
+        UV_CK(cudaMalloc((void **)&ix->cext, sizeof(uint16_t) * (size_t)c_pad * 16));
+        float *units = nullptr;
+        uint32_t *flags = nullptr;
+        UV_TRY(sc.alloc(&units, (size_t)nlist * d));
+        UV_TRY(sc.alloc(&flags, (size_t)nlist));
+        uvb::normalize_rows_kernel<<<blocks((int64_t)nlist * d, 256), 256, 0, st>>>(
+            ix->centroids, ix->cnorm, nlist, d, units);
+        uvb::unit_flags_kernel<<<blocks(nlist, 256), 256, 0, st>>>(ix->cnorm, nlist, flags);
+        const int64_t chunks = c_pad * (kpad / 8);
+        uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+            units, d, flags, nlist, c_pad, d, kpad, ix->c16, ix->cext, ix->cext);
+        UV_CK(cudaGetLastError());
+        UV_CK(cudaMemsetAsync(ix->cext, 0, sizeof(uint16_t) * (size_t)c_pad * 16, st));
+        UV_CK(cudaStreamSynchronize(st));
+        ix->c_pad = c_pad;
+        ix->tc_state = 1;
+      }
+    }
+    if (ix->tc_state < 0) return UV_OK;
+  }
+  *used = true;
+  const int64_t ldc = ix->c_pad;
+  const int64_t n_tiles = ldc / TN;
+  const int64_t chunk = std::max<int64_t>(
+      TM, std::min<int64_t>((nq + TM - 1) / TM * TM, ((int64_t)256 << 20) / (4 * ldc) / TM * TM));
+  float *approx = nullptr, *u = nullptr;
+  uint32_t *qflag = nullptr;
+  uint16_t *a16 = nullptr, *ax = nullptr;
+  int *err = nullptr;
+  UV_TRY(sc.alloc(&approx, (size_t)chunk * ldc));
+  UV_TRY(sc.alloc(&u, (size_t)chunk * d));
+  UV_TRY(sc.alloc(&qflag, (size_t)chunk));
+  UV_TRY(sc.alloc(&a16, (size_t)chunk * kpad));
+  UV_TRY(sc.alloc(&ax, (size_t)chunk * 16 * 2));
+  UV_TRY(sc.alloc(&err, 1));
+  UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  CUtensorMap tmap_b, tmap_bx;
+  UV_TRY(fp16_tensor_map(&tmap_b, ix->c16, ldc, kpad, 64, TN, true));
+  UV_TRY(fp16_tensor_map(&tmap_bx, ix->cext, ldc, 16, 16, TN, false));
+  const size_t wsmem = uvb::tc_wide_smem_bytes();
+  const void *wk = uvb::tc_wide_kernel_ptr(3);
+  UV_CK(cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
+  int pow2 = 32;
+  while (pow2 < nlist) pow2 <<= 1;
+  const size_t rsmem = (size_t)pow2 * 8 + (size_t)((nlist + 3) & ~3) * 4 + (size_t)d * 4;
+  UV_CK(cudaFuncSetAttribute(uvb::probe_refine_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem));
+  const int64_t slots = sm_count(ix->device);
+  float bound = (float)(1.25 * (std::ldexp(1.0, -10) + std::ldexp(1.0, -12) +
+                                4.0 * d * std::ldexp(1.0, -24)));
+  for (int64_t q0 = 0; q0 < nq; q0 += chunk) {
+    const int64_t m = std::min(chunk, nq - q0);
+    const int64_t m_pad = (m + TM - 1) / TM * TM;
+    {
+      ProfScope ps("ivf_cosine", st);
+      uvb::normalize_rows_kernel<<<blocks(m * d, 256), 256, 0, st>>>(d_q + q0 * d, qn + q0, m, d,
+                                                                      u);
+      uvb::unit_flags_kernel<<<blocks(m, 256), 256, 0, st>>>(qn + q0, m, qflag);
+      const int64_t chunks = m_pad * (kpad / 8);
+      uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+          u, d, qflag, m, m_pad, d, kpad, a16, ax, ax + m_pad * 16);
+      UV_CK(cudaGetLastError());
+      CUtensorMap tmap_a, tmap_ax;
+      UV_TRY(fp16_tensor_map(&tmap_a, a16, m_pad, kpad, 64, TM, true));
+      UV_TRY(fp16_tensor_map(&tmap_ax, ax, m_pad, 16, 16, TM, false));
+      uvb::TcScanParams tp;
+      std::memset(&tp, 0, sizeof(tp));
+      tp.nq = m;
+      tp.n = nlist;
+      tp.n_tiles = n_tiles;
+      tp.n_groups = ldc;  // leading dimension of approx
+      tp.tile_stride = 1;
+      tp.degenerate = qflag;
+      tp.tmax = approx;
+      tp.err = err;
+      // record splits filling whole waves of one CTA per SM
+      const int64_t qtiles = m_pad / TM;
+      int64_t splits = 1;
+      double best_eff = 0.0;
+      for (int64_t s2 = 1; s2 <= std::min<int64_t>(n_tiles, 64); s2++) {
+        const int64_t ctas = qtiles * s2;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const double eff = (double)ctas / (double)(waves * slots) - 0.002 * (double)waves;
+        if (eff > best_eff + 1e-9) {
+          best_eff = eff;
+          splits = s2;
+        }
+      }
+      int kchunks = kpad / 64;
+      void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax, &tmap_b, &tmap_bx};
+      UV_CK(cudaLaunchKernel(wk, dim3((unsigned)qtiles, (unsigned)splits),
+                             dim3(uvb::tc_threads()), wargs, wsmem, st));
+    }
+    {
+      ProfScope ps("ivf_select", st);
+      uvb::ProbeRefineParams rp;
+      std::memset(&rp, 0, sizeof(rp));
+      rp.m = m;
+      rp.nlist = nlist;
+      rp.np = np;
+      rp.dim = d;
+      rp.pow2 = pow2;
+      rp.ld_out = ld;
+      rp.ld = ldc;
+      rp.bound = bound;
+      rp.approx = approx;
+      rp.queries = d_q + q0 * d;
+      rp.qnorm = qn + q0;
+      rp.cent = ix->centroids;
+      rp.cnorm = ix->cnorm;
+      rp.out = lists + q0 * ld;
+      void *rargs[] = {&rp};
+      UV_CK(cudaLaunchKernel((const void *)uvb::probe_refine_kernel,
+                             dim3((unsigned)std::min<int64_t>(m, 65535)), dim3(256), rargs, rsmem,
+                             st));
+    }
+  }
+  int h_err = 0;
+  UV_CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  if (h_err) return fail(UV_ETIMEDOUT, "a tensor-core probe wait timed out");
+  return UV_OK;
+}
+
 // Probe on device: lists (nq x ld, first np columns) of the best np lists by
 // exact cosine of the raw queries.
 int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld, int32_t *lists,
@@ -138,6 +302,9 @@ int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld,
   UV_TRY(sc.alloc(&qn, (size_t)nq));
   uvb::row_norms_kernel<<<blocks(nq, 128), 128, 0, st>>>(d_q, nq, d, qn);
   UV_CK(cudaGetLastError());
+  bool used = false;
+  UV_TRY(tc_probe(ix, d_q, qn, nq, np, ld, lists, st, sc, &used));
+  if (used) return UV_OK;
   const int64_t chunk =
       std::max<int64_t>(1, std::min<int64_t>(nq, ((int64_t)256 << 20) / (4 * (int64_t)ix->nlist)));
   UV_TRY(sc.alloc(&cos, (size_t)chunk * ix->nlist));
@@ -453,6 +620,8 @@ int uv_ivf_destroy(uv_ivf *ix) {
     free_lists(ix);
     cudaFree(ix->centroids);
     cudaFree(ix->cnorm);
+    cudaFree(ix->c16);
+    cudaFree(ix->cext);
   }
   delete ix;
   return UV_OK;

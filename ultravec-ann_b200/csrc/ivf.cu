@@ -190,6 +190,127 @@ __global__ void __launch_bounds__(256) select_top_kernel(const float *scores, in
   }
 }
 
+// flags[i] = 1 when norms[i] is below EPS or not finite (the probe's
+// tensor-core rows are zero for those)
+__global__ void unit_flags_kernel(const float *norms, int64_t n, uint32_t *flags) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) flags[i] = (norms[i] >= kF32Eps && isfinite(norms[i])) ? 0u : 1u;
+}
+
+// The probe from tensor-core dots (the same lists as seqdot_kernel<1> +
+// select_top_kernel).  approx[q][j] = the fp16 dot of the unit query and the
+// unit centroid, within p.bound of the exact f32 cosine (src/lib.rs:240-248:
+// the sequential dot over the norms' product, 0 below EPS).  One CTA per
+// query: theta = the np-th largest approximate dot; every centroid j with
+// approx >= theta - 2 bound can reach the np-th best exact cosine, so its
+// exact cosine is computed (sequential f32, as the reference) and the
+// candidates are ranked by (cosine desc, index asc, NaN last).
+__device__ __forceinline__ uint32_t ord_key(float f) {
+  if (f == 0.0f) f = 0.0f;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) probe_refine_kernel(const ProbeRefineParams p) {
+  extern __shared__ __align__(16) uint64_t keys[];       // pow2
+  uint32_t *aux = (uint32_t *)(keys + p.pow2);          // nlist: approx keys, then candidates
+  float *qs = (float *)(aux + ((p.nlist + 3) & ~3));    // dim: the query row
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel[3];
+  const int tid = threadIdx.x;
+  const int nl = p.nlist;
+  for (int64_t q = blockIdx.x; q < p.m; q += gridDim.x) {
+    const float *v = p.approx + q * p.ld;
+    for (int j = tid; j < nl; j += 256) aux[j] = ord_key(v[j]);
+    // radix select of the np-th largest key
+    uint32_t prefix = 0, mask = 0, kk = (uint32_t)p.np;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      hist[tid] = 0;
+      __syncthreads();
+      for (int j = tid; j < nl; j += 256) {
+        const uint32_t key = aux[j];
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t above = 0;
+        int b = 255;
+        for (; b > 0; b--) {
+          if (above + hist[b] >= kk) break;
+          above += hist[b];
+        }
+        sel[0] = (uint32_t)b;
+        sel[1] = above;
+      }
+      __syncthreads();
+      prefix |= sel[0] << shift;
+      mask |= 255u << shift;
+      kk -= sel[1];
+      __syncthreads();
+    }
+    const float theta = __uint_as_float((prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix);
+    const float thr = fsub(theta, fmul(2.0001f, p.bound));
+    if (tid == 0) sel[2] = 0;
+    __syncthreads();
+    for (int j = tid; j < nl; j += 256)
+      if (v[j] >= thr) aux[atomicAdd(&sel[2], 1u)] = (uint32_t)j;
+    __syncthreads();
+    const int nc = (int)sel[2];
+    int pow2 = 32;
+    while (pow2 < nc) pow2 <<= 1;
+    const float na = p.qnorm[q];
+    const float *qa = p.queries + q * (int64_t)p.dim;
+    for (int t = tid; t < p.dim; t += 256) qs[t] = qa[t];
+    __syncthreads();
+    for (int i = tid; i < pow2; i += 256) {
+      uint64_t key = 0ull;
+      if (i < nc) {
+        const int j = (int)aux[i];
+        // the centroid row in batches of 32 values (8 independent 16-byte
+        // loads ahead of the sequential sum, which keeps the reference order)
+        const float4 *c4 = (const float4 *)(p.cent + (int64_t)j * p.dim);
+        const float4 *q4 = (const float4 *)qs;
+        float dot = -0.0f;
+        for (int t4 = 0; t4 < p.dim / 4; t4 += 8) {
+          float4 b[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) b[u] = __ldg(c4 + t4 + u);
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const float4 a = q4[t4 + u];
+            dot = fadd(dot, fmul(a.x, b[u].x));
+            dot = fadd(dot, fmul(a.y, b[u].y));
+            dot = fadd(dot, fmul(a.z, b[u].z));
+            dot = fadd(dot, fmul(a.w, b[u].w));
+          }
+        }
+        const float nb = p.cnorm[j];
+        const float cs = (na < kF32Eps || nb < kF32Eps) ? 0.0f : fdiv(dot, fmul(na, nb));
+        key = rank_key(cs, (uint32_t)j);
+      }
+      keys[i] = key;
+    }
+    __syncthreads();
+    for (int size = 2; size <= pow2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int pi = tid; pi < pow2 / 2; pi += 256) {
+          const int lo = 2 * pi - (pi & (stride - 1));
+          const int hi = lo + stride;
+          const bool desc = (lo & size) == 0;
+          const uint64_t x = keys[lo], y = keys[hi];
+          if ((x < y) == desc) {
+            keys[lo] = y;
+            keys[hi] = x;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = tid; i < p.np; i += 256) p.out[q * p.ld_out + i] = (int32_t)rank_key_index(keys[i]);
+    __syncthreads();
+  }
+}
+
 // Empty result slots: id -1, score -inf (as the merge writes them).
 __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -232,6 +232,7 @@ __global__ void tc_prepare_queries_kernel(const float *q_r, int q_stride, const 
 }
 
 const void *tc_wide_kernel_ptr(int mode) {
+  if (mode == 3) return (const void *)tc_wide_kernel<3>;
   return mode == 1 ? (const void *)tc_wide_kernel<1> : (const void *)tc_wide_kernel<2>;
 }
 

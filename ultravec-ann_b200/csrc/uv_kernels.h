@@ -307,6 +307,21 @@ __global__ void gather_rows_kernel(const float *src, const int64_t *pick, int nr
                                    float *dst);
 __global__ void list_means_kernel(const float *units, const int64_t *order, const int64_t *off,
                                   int nlist, int dim, float *cent);
+// the IVF probe from tensor-core dots (ivf.cu)
+struct ProbeRefineParams {
+  int64_t m;             // queries
+  int nlist, np, dim, pow2, ld_out;
+  int64_t ld;            // leading dimension of approx
+  float bound;           // |approx - exact cosine| <= bound
+  const float *approx;   // m x ld fp16-operand dots of unit rows
+  const float *queries;  // m x dim raw queries
+  const float *qnorm;    // m
+  const float *cent;     // nlist x dim
+  const float *cnorm;    // nlist
+  int32_t *out;          // m x ld_out lists
+};
+__global__ void probe_refine_kernel(const ProbeRefineParams p);
+__global__ void unit_flags_kernel(const float *norms, int64_t n, uint32_t *flags);
 __global__ void select_top_kernel(const float *scores, int64_t n, int nb, int pow2, int np,
                                   int ld_out, int32_t *out);
 __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n);

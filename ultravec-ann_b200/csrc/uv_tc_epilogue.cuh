@@ -3,7 +3,7 @@
 // run of records (nl chunks of 32 accumulator columns, already in
 // registers).  Pass 1 writes the run's largest lower bound; pass 2 appends
 // every record whose upper bound reaches the query's threshold to its
-// candidate list.
+// candidate list; mode 3 (the IVF probe) stores every value.
 #pragma once
 
 #include "uv_kernels.h"
@@ -35,6 +35,19 @@ __device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t
                                            int64_t q, bool qok, float theta, int64_t group,
                                            int64_t rec0, uint32_t *dst = nullptr,
                                            int *count = nullptr) {
+  if (MODE == 3) {
+    // every value: row q of p.tmax (leading dimension n_groups), the dot
+    // itself (the IVF probe bounds it on the host side of the contract)
+    if (q < p.nq) {
+      float *dst = p.tmax + q * p.n_groups;
+#pragma unroll
+      for (int l = 0; l < NL; l++)
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (rec0 + 32 * l + j < p.n) dst[rec0 + 32 * l + j] = __uint_as_float(r[l][j]);
+    }
+    return;
+  }
   float mc[NL];
 #pragma unroll
   for (int l = 0; l < NL; l++) mc[l] = chunk_max(r[l]);
