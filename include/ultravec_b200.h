@@ -195,9 +195,10 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * the first search after a change of the records, per score mode, and held
  * until the next change or uv_index_destroy; (2 x dim rounded up to 64 + 32)
  * bytes per record and mode) or makes them in per-search scratch (0);
- * "ivf_tc_probe" 1 makes the IVF probe compute every cosine on the CUDA
- * cores (0 automatic: tensor-core dots, exact cosines for the centroids
- * that can reach the nprobe-th best, the same lists);
+ * "ivf_tc_probe" 1 makes the IVF probe and the k-means / IVF assignment
+ * compute every cosine or dot on the CUDA cores (0 automatic: tensor-core
+ * dots, exact values for the centroids that can still be chosen, the same
+ * lists and assignments);
  * "tc_sample" fixes the prefilter's first-pass tile stride (0 automatic:
  * round(sqrt(1600/k)), at most 10); "tc_prepare" 1 makes the prefilter's
  * rows with the generic kernel (0 automatic);

@@ -49,6 +49,32 @@ def test_kmeans_and_assign_bit_exact(oracle, uv, n, dim, nlist, iters):
     assert np.array_equal(asg_got, asg_want)
 
 
+@pytest.mark.parametrize("n,dim,nlist", [(20_000, 64, 300), (6000, 256, 520)])
+def test_tensor_core_kmeans_and_assign_bit_exact(oracle, uv, n, dim, nlist):
+    """At 256 or more centroids the assignment runs on the tensor cores
+    (fp16 dots, exact dots for the centroids that can still win): k-means
+    centroids and assignments stay bit-identical to the oracle, and equal to
+    the CUDA-core assignment, duplicated centroids (first maximum) and a zero
+    row included."""
+    rows = clustered(n, dim, 12, n + dim)
+    rows[5] = 0.0
+    want = oracle.kmeans(rows, nlist, seed=42, iters=3)
+    got = uv.kmeans(rows, nlist, seed=42, iters=3)
+    assert bits_equal(got, want)
+    cen = want.copy()
+    cen[9] = cen[2]  # exact ties: the lower list wins
+    asg_want = oracle.assign(rows, cen)
+    try:
+        asg_got = uv.ivf_assign(rows, cen)
+        uv.set_tuning("ivf_tc_probe", 1)
+        asg_exact = uv.ivf_assign(rows, cen)
+    finally:
+        uv.set_tuning("ivf_tc_probe", 0)
+    assert np.array_equal(asg_got, asg_want)
+    assert np.array_equal(asg_exact, asg_want)
+    assert asg_got[5] == 0
+
+
 def test_assign_ties_pick_the_first_maximum(oracle, uv):
     # duplicated centroids: every dot ties with its twin, the lower index wins;
     # a zero row dots to +-0 everywhere and lands on list 0

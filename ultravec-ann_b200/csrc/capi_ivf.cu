@@ -53,10 +53,21 @@ int units_launch(const float *rows, int64_t n, int dim, float *norms, float *uni
   return UV_OK;
 }
 
+// the tensor-core paths (below): at least this many centroids
+constexpr int kProbeMinLists = 256;
+int tc_argmax(const float *units, int64_t n, int dim, const float *cent, int nlist,
+              uint32_t *asg, cudaStream_t st, Scratch &sc, bool *used);
+
 // asg[i] = first strict maximum of <units[i], c_j> (device in and out)
 int argmax_launch(const float *units, int64_t n, int dim, const float *cent, int nlist,
                   uint64_t *keys, uint32_t *asg, cudaStream_t st) {
   if (n == 0) return UV_OK;
+  {
+    Scratch sc(st);
+    bool used = false;
+    UV_TRY(tc_argmax(units, n, dim, cent, nlist, asg, st, sc, &used));
+    if (used) return UV_OK;
+  }
   UV_CK(cudaMemsetAsync(keys, 0, sizeof(uint64_t) * n, st));
   UV_TRY(seqdot_launch(0, units, n, cent, nlist, dim, keys, nullptr, nullptr, nullptr, st));
   uvb::argmax_index_kernel<<<blocks(n, 256), 256, 0, st>>>(keys, n, asg);
@@ -127,6 +138,175 @@ void free_lists(uv_ivf *ix) {
   ix->n = 0;
 }
 
+// Per row of a (m x d): the np best of nlist centroids by exact score, via
+// the fp16 dots of tcwide.cu (mode 3; B = c16 / cext, ldc rows, kpad wide)
+// and probe_refine_kernel.  With a_norm the rows are raw and the score is the
+// cosine (the fp16 side uses a / |a|); without it the rows are used as they
+// are and the score is the plain dot.  bound: |fp16 dot - exact score|.
+int tc_rank_rows(const float *a, const float *a_norm, int64_t m_total, int d, const uint16_t *c16,
+                 const uint16_t *cext, int64_t ldc, const float *cent, const float *cnorm,
+                 int nlist, int np, float bound, int32_t *out, int ld_out, int dev,
+                 cudaStream_t st, Scratch &sc) {
+  const int kpad = (d + 63) / 64 * 64;
+  const int TN = 192, TM = 128;
+  const int64_t n_tiles = ldc / TN;
+  const int64_t chunk = std::max<int64_t>(
+      TM,
+      std::min<int64_t>((m_total + TM - 1) / TM * TM, ((int64_t)256 << 20) / (4 * ldc) / TM * TM));
+  float *approx = nullptr, *u = nullptr;
+  uint32_t *aflag = nullptr;
+  uint16_t *a16 = nullptr, *ax = nullptr;
+  int *err = nullptr;
+  UV_TRY(sc.alloc(&approx, (size_t)chunk * ldc));
+  if (a_norm != nullptr) UV_TRY(sc.alloc(&u, (size_t)chunk * d));
+  UV_TRY(sc.alloc(&aflag, (size_t)chunk));
+  UV_TRY(sc.alloc(&a16, (size_t)chunk * kpad));
+  UV_TRY(sc.alloc(&ax, (size_t)chunk * 16 * 2));
+  UV_TRY(sc.alloc(&err, 1));
+  UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  if (a_norm == nullptr) UV_CK(cudaMemsetAsync(aflag, 0, sizeof(uint32_t) * chunk, st));
+  CUtensorMap tmap_b, tmap_bx;
+  UV_TRY(fp16_tensor_map(&tmap_b, c16, ldc, kpad, 64, TN, true));
+  UV_TRY(fp16_tensor_map(&tmap_bx, cext, ldc, 16, 16, TN, false));
+  const size_t wsmem = uvb::tc_wide_smem_bytes();
+  const void *wk = uvb::tc_wide_kernel_ptr(3);
+  UV_CK(cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
+  int pow2 = 32;
+  while (pow2 < nlist) pow2 <<= 1;
+  const size_t rsmem = (size_t)pow2 * 8 + (size_t)((nlist + 3) & ~3) * 4 + (size_t)d * 4;
+  UV_CK(cudaFuncSetAttribute(uvb::probe_refine_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem));
+  const int64_t slots = sm_count(dev);
+  for (int64_t q0 = 0; q0 < m_total; q0 += chunk) {
+    const int64_t m = std::min(chunk, m_total - q0);
+    const int64_t m_pad = (m + TM - 1) / TM * TM;
+    {
+      ProfScope ps("ivf_cosine", st);
+      const float *rows16 = a + q0 * d;
+      if (a_norm != nullptr) {
+        uvb::normalize_rows_kernel<<<blocks(m * d, 256), 256, 0, st>>>(a + q0 * d, a_norm + q0, m,
+                                                                        d, u);
+        uvb::unit_flags_kernel<<<blocks(m, 256), 256, 0, st>>>(a_norm + q0, m, aflag);
+        rows16 = u;
+      }
+      const int64_t chunks = m_pad * (kpad / 8);
+      uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+          rows16, d, aflag, m, m_pad, d, kpad, a16, ax, ax + m_pad * 16);
+      UV_CK(cudaGetLastError());
+      CUtensorMap tmap_a, tmap_ax;
+      UV_TRY(fp16_tensor_map(&tmap_a, a16, m_pad, kpad, 64, TM, true));
+      UV_TRY(fp16_tensor_map(&tmap_ax, ax, m_pad, 16, 16, TM, false));
+      uvb::TcScanParams tp;
+      std::memset(&tp, 0, sizeof(tp));
+      tp.nq = m;
+      tp.n = nlist;
+      tp.n_tiles = n_tiles;
+      tp.n_groups = ldc;  // leading dimension of approx
+      tp.tile_stride = 1;
+      tp.degenerate = aflag;
+      tp.tmax = approx;
+      tp.err = err;
+      // record splits filling whole waves of one CTA per SM
+      const int64_t qtiles = m_pad / TM;
+      int64_t splits = 1;
+      double best_eff = 0.0;
+      for (int64_t s2 = 1; s2 <= std::min<int64_t>(n_tiles, 64); s2++) {
+        const int64_t ctas = qtiles * s2;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const double eff = (double)ctas / (double)(waves * slots) - 0.002 * (double)waves;
+        if (eff > best_eff + 1e-9) {
+          best_eff = eff;
+          splits = s2;
+        }
+      }
+      int kchunks = kpad / 64;
+      void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax, &tmap_b, &tmap_bx};
+      UV_CK(cudaLaunchKernel(wk, dim3((unsigned)qtiles, (unsigned)splits),
+                             dim3(uvb::tc_threads()), wargs, wsmem, st));
+    }
+    {
+      ProfScope ps("ivf_select", st);
+      uvb::ProbeRefineParams rp;
+      std::memset(&rp, 0, sizeof(rp));
+      rp.m = m;
+      rp.nlist = nlist;
+      rp.np = np;
+      rp.dim = d;
+      rp.pow2 = pow2;
+      rp.ld_out = ld_out;
+      rp.cosine = a_norm != nullptr ? 1 : 0;
+      rp.ld = ldc;
+      rp.bound = bound;
+      rp.approx = approx;
+      rp.queries = a + q0 * d;
+      rp.qnorm = a_norm != nullptr ? a_norm + q0 : nullptr;
+      rp.cent = cent;
+      rp.cnorm = cnorm;
+      rp.out = out + q0 * ld_out;
+      void *rargs[] = {&rp};
+      UV_CK(cudaLaunchKernel((const void *)uvb::probe_refine_kernel,
+                             dim3((unsigned)std::min<int64_t>(m, 65535)), dim3(256), rargs, rsmem,
+                             st));
+    }
+  }
+  int h_err = 0;
+  UV_CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  if (h_err) return fail(UV_ETIMEDOUT, "a tensor-core probe wait timed out");
+  return UV_OK;
+}
+
+// The k-means / build assignment on the tensor cores: the first strict
+// maximum of <unit row, c_j> (as seqdot_kernel<0>) through tc_rank_rows with
+// the raw centroids as fp16 rows and np = 1.  Same shape limits as the probe;
+// also off when a centroid norm is not finite or above 1e4 (fp16 range).
+// Bound: as the probe's, times the largest centroid norm (rows are units).
+int tc_argmax(const float *units, int64_t n, int dim, const float *cent, int nlist,
+              uint32_t *asg, cudaStream_t st, Scratch &sc, bool *used) {
+  *used = false;
+  if (g_ivf_tc_probe == 1 || dim % 32 != 0 || dim > 4096 || nlist < kProbeMinLists ||
+      nlist > 8192 || n < 1024)
+    return UV_OK;
+  // both sides are read 16 bytes at a time: a caller's unaligned buffer
+  // takes the CUDA-core path
+  if (((uintptr_t)cent & 15) != 0 || ((uintptr_t)units & 15) != 0) return UV_OK;
+  int dev = 0;
+  UV_CK(cudaGetDevice(&dev));
+  float *cn = nullptr;
+  UV_TRY(sc.alloc(&cn, (size_t)nlist));
+  uvb::row_norms_kernel<<<blocks(nlist, 128), 128, 0, st>>>(cent, nlist, dim, cn);
+  UV_CK(cudaGetLastError());
+  std::vector<float> hn(nlist);
+  UV_CK(cudaMemcpyAsync(hn.data(), cn, sizeof(float) * nlist, cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  double maxc = 0.0;
+  for (float v : hn) {
+    if (!std::isfinite(v)) return UV_OK;
+    maxc = std::max(maxc, (double)v);
+  }
+  if (maxc > 1e4) return UV_OK;
+  *used = true;
+  const int TN = 192;
+  const int kpad = (dim + 63) / 64 * 64;
+  const int64_t c_pad = (nlist + TN - 1) / TN * TN;
+  uint16_t *c16 = nullptr, *cext = nullptr;
+  uint32_t *zf = nullptr;
+  UV_TRY(sc.alloc(&c16, (size_t)c_pad * kpad));
+  UV_TRY(sc.alloc(&cext, (size_t)c_pad * 16));
+  UV_TRY(sc.alloc(&zf, (size_t)nlist));
+  UV_CK(cudaMemsetAsync(zf, 0, sizeof(uint32_t) * nlist, st));
+  const int64_t chunks = c_pad * (kpad / 8);
+  uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+      cent, dim, zf, nlist, c_pad, dim, kpad, c16, cext, cext);
+  UV_CK(cudaGetLastError());
+  UV_CK(cudaMemsetAsync(cext, 0, sizeof(uint16_t) * (size_t)c_pad * 16, st));
+  const float bound = (float)(1.25 * (std::ldexp(1.0, -10) + std::ldexp(1.0, -12) +
+                                      4.0 * dim * std::ldexp(1.0, -24)) *
+                              std::max(1.0, maxc));
+  return tc_rank_rows(units, nullptr, n, dim, c16, cext, c_pad, cent, nullptr, nlist, 1, bound,
+                      (int32_t *)asg, 1, dev, st, sc);
+}
+
 // The probe on the tensor cores: every (query, centroid) dot of the unit
 // rows in fp16 (tcwide.cu, mode 3), then per query the exact cosines of the
 // centroids that can still reach the np-th best (probe_refine_kernel) --
@@ -139,8 +319,6 @@ void free_lists(uv_ivf *ix) {
 // accumulation, as the flat prefilter's bound) + 4 d u (the f32 norms and
 // divisions of both sides, fp16 subnormals, and the reference's sequential
 // f32 dot); the kernel uses 1.25 times that.
-constexpr int kProbeMinLists = 256;
-
 int tc_probe(const uv_ivf *ix, const float *d_q, const float *qn, int64_t nq, int np, int ld,
              int32_t *lists, cudaStream_t st, Scratch &sc, bool *used) {
   *used = false;
@@ -186,107 +364,10 @@ int tc_probe(const uv_ivf *ix, const float *d_q, const float *qn, int64_t nq, in
     if (ix->tc_state < 0) return UV_OK;
   }
   *used = true;
-  const int64_t ldc = ix->c_pad;
-  const int64_t n_tiles = ldc / TN;
-  const int64_t chunk = std::max<int64_t>(
-      TM, std::min<int64_t>((nq + TM - 1) / TM * TM, ((int64_t)256 << 20) / (4 * ldc) / TM * TM));
-  float *approx = nullptr, *u = nullptr;
-  uint32_t *qflag = nullptr;
-  uint16_t *a16 = nullptr, *ax = nullptr;
-  int *err = nullptr;
-  UV_TRY(sc.alloc(&approx, (size_t)chunk * ldc));
-  UV_TRY(sc.alloc(&u, (size_t)chunk * d));
-  UV_TRY(sc.alloc(&qflag, (size_t)chunk));
-  UV_TRY(sc.alloc(&a16, (size_t)chunk * kpad));
-  UV_TRY(sc.alloc(&ax, (size_t)chunk * 16 * 2));
-  UV_TRY(sc.alloc(&err, 1));
-  UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
-  CUtensorMap tmap_b, tmap_bx;
-  UV_TRY(fp16_tensor_map(&tmap_b, ix->c16, ldc, kpad, 64, TN, true));
-  UV_TRY(fp16_tensor_map(&tmap_bx, ix->cext, ldc, 16, 16, TN, false));
-  const size_t wsmem = uvb::tc_wide_smem_bytes();
-  const void *wk = uvb::tc_wide_kernel_ptr(3);
-  UV_CK(cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
-  int pow2 = 32;
-  while (pow2 < nlist) pow2 <<= 1;
-  const size_t rsmem = (size_t)pow2 * 8 + (size_t)((nlist + 3) & ~3) * 4 + (size_t)d * 4;
-  UV_CK(cudaFuncSetAttribute(uvb::probe_refine_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem));
-  const int64_t slots = sm_count(ix->device);
-  float bound = (float)(1.25 * (std::ldexp(1.0, -10) + std::ldexp(1.0, -12) +
-                                4.0 * d * std::ldexp(1.0, -24)));
-  for (int64_t q0 = 0; q0 < nq; q0 += chunk) {
-    const int64_t m = std::min(chunk, nq - q0);
-    const int64_t m_pad = (m + TM - 1) / TM * TM;
-    {
-      ProfScope ps("ivf_cosine", st);
-      uvb::normalize_rows_kernel<<<blocks(m * d, 256), 256, 0, st>>>(d_q + q0 * d, qn + q0, m, d,
-                                                                      u);
-      uvb::unit_flags_kernel<<<blocks(m, 256), 256, 0, st>>>(qn + q0, m, qflag);
-      const int64_t chunks = m_pad * (kpad / 8);
-      uvb::tc_prepare_queries_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
-          u, d, qflag, m, m_pad, d, kpad, a16, ax, ax + m_pad * 16);
-      UV_CK(cudaGetLastError());
-      CUtensorMap tmap_a, tmap_ax;
-      UV_TRY(fp16_tensor_map(&tmap_a, a16, m_pad, kpad, 64, TM, true));
-      UV_TRY(fp16_tensor_map(&tmap_ax, ax, m_pad, 16, 16, TM, false));
-      uvb::TcScanParams tp;
-      std::memset(&tp, 0, sizeof(tp));
-      tp.nq = m;
-      tp.n = nlist;
-      tp.n_tiles = n_tiles;
-      tp.n_groups = ldc;  // leading dimension of approx
-      tp.tile_stride = 1;
-      tp.degenerate = qflag;
-      tp.tmax = approx;
-      tp.err = err;
-      // record splits filling whole waves of one CTA per SM
-      const int64_t qtiles = m_pad / TM;
-      int64_t splits = 1;
-      double best_eff = 0.0;
-      for (int64_t s2 = 1; s2 <= std::min<int64_t>(n_tiles, 64); s2++) {
-        const int64_t ctas = qtiles * s2;
-        const int64_t waves = (ctas + slots - 1) / slots;
-        const double eff = (double)ctas / (double)(waves * slots) - 0.002 * (double)waves;
-        if (eff > best_eff + 1e-9) {
-          best_eff = eff;
-          splits = s2;
-        }
-      }
-      int kchunks = kpad / 64;
-      void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax, &tmap_b, &tmap_bx};
-      UV_CK(cudaLaunchKernel(wk, dim3((unsigned)qtiles, (unsigned)splits),
-                             dim3(uvb::tc_threads()), wargs, wsmem, st));
-    }
-    {
-      ProfScope ps("ivf_select", st);
-      uvb::ProbeRefineParams rp;
-      std::memset(&rp, 0, sizeof(rp));
-      rp.m = m;
-      rp.nlist = nlist;
-      rp.np = np;
-      rp.dim = d;
-      rp.pow2 = pow2;
-      rp.ld_out = ld;
-      rp.ld = ldc;
-      rp.bound = bound;
-      rp.approx = approx;
-      rp.queries = d_q + q0 * d;
-      rp.qnorm = qn + q0;
-      rp.cent = ix->centroids;
-      rp.cnorm = ix->cnorm;
-      rp.out = lists + q0 * ld;
-      void *rargs[] = {&rp};
-      UV_CK(cudaLaunchKernel((const void *)uvb::probe_refine_kernel,
-                             dim3((unsigned)std::min<int64_t>(m, 65535)), dim3(256), rargs, rsmem,
-                             st));
-    }
-  }
-  int h_err = 0;
-  UV_CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
-  UV_CK(cudaStreamSynchronize(st));
-  if (h_err) return fail(UV_ETIMEDOUT, "a tensor-core probe wait timed out");
-  return UV_OK;
+  const float bound = (float)(1.25 * (std::ldexp(1.0, -10) + std::ldexp(1.0, -12) +
+                                      4.0 * d * std::ldexp(1.0, -24)));
+  return tc_rank_rows(d_q, qn, nq, d, ix->c16, ix->cext, ix->c_pad, ix->centroids, ix->cnorm,
+                      nlist, np, bound, lists, ld, ix->device, st, sc);
 }
 
 // Probe on device: lists (nq x ld, first np columns) of the best np lists by

@@ -204,7 +204,9 @@ __global__ void unit_flags_kernel(const float *norms, int64_t n, uint32_t *flags
 // query: theta = the np-th largest approximate dot; every centroid j with
 // approx >= theta - 2 bound can reach the np-th best exact cosine, so its
 // exact cosine is computed (sequential f32, as the reference) and the
-// candidates are ranked by (cosine desc, index asc, NaN last).
+// candidates are ranked by (cosine desc, index asc, NaN last).  With
+// cosine = 0 the score is the plain sequential dot (seqdot_kernel<0>, the
+// k-means assignment's first strict maximum at np = 1).
 __device__ __forceinline__ uint32_t ord_key(float f) {
   if (f == 0.0f) f = 0.0f;
   const uint32_t u = __float_as_uint(f);
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(256) probe_refine_kernel(const ProbeRefinePara
     const int nc = (int)sel[2];
     int pow2 = 32;
     while (pow2 < nc) pow2 <<= 1;
-    const float na = p.qnorm[q];
+    const float na = p.cosine ? p.qnorm[q] : 1.0f;
     const float *qa = p.queries + q * (int64_t)p.dim;
     for (int t = tid; t < p.dim; t += 256) qs[t] = qa[t];
     __syncthreads();
@@ -284,8 +286,11 @@ __global__ void __launch_bounds__(256) probe_refine_kernel(const ProbeRefinePara
             dot = fadd(dot, fmul(a.w, b[u].w));
           }
         }
-        const float nb = p.cnorm[j];
-        const float cs = (na < kF32Eps || nb < kF32Eps) ? 0.0f : fdiv(dot, fmul(na, nb));
+        float cs = dot;  // the k-means assignment ranks the plain dot
+        if (p.cosine) {
+          const float nb = p.cnorm[j];
+          cs = (na < kF32Eps || nb < kF32Eps) ? 0.0f : fdiv(dot, fmul(na, nb));
+        }
         key = rank_key(cs, (uint32_t)j);
       }
       keys[i] = key;

@@ -311,6 +311,7 @@ __global__ void list_means_kernel(const float *units, const int64_t *order, cons
 struct ProbeRefineParams {
   int64_t m;             // queries
   int nlist, np, dim, pow2, ld_out;
+  int cosine;            // 1: cosine over the norms; 0: the plain dot
   int64_t ld;            // leading dimension of approx
   float bound;           // |approx - exact cosine| <= bound
   const float *approx;   // m x ld fp16-operand dots of unit rows
