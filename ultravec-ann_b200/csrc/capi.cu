@@ -416,6 +416,7 @@ int uv_index_destroy(uv_index *ix) {
     for (auto &t : ix->tc_rows) {
       cudaFree(t.x16);
       cudaFree(t.xext);
+      cudaFree(t.cmax);
       if (t.ready != nullptr) cudaEventDestroy(t.ready);
     }
   }
@@ -850,9 +851,12 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int shape = g_tc_shape == 1 ? 1 : 3;  // CTA shape (tcscan.cu)
   const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
   const int64_t n_tiles = (n + TN - 1) / TN;
-  const int64_t n_groups = 2 * n_tiles;  // bound groups of half a tile
-  // a useful threshold needs several groups per top-k slot
-  if (n_groups < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
+  // a useful threshold needs several bound groups per top-k slot (counted as
+  // two per tile, the wide kernel's groups of half a tile)
+  if (2 * n_tiles < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
+  // bound groups per tile: tile slices of the flat kernel, halves of the wide
+  const int gpt = wide ? 2 : uvb::tc_groups_per_tile();
+  const int64_t n_groups = gpt * n_tiles;
   if (n_tiles * TN > INT32_MAX) return UV_OK;
   *used = true;
   const int dev = c->cfg.device;
@@ -868,7 +872,8 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   // device has drained.
   const int64_t n_pad = n_tiles * TN;
   uint16_t *x16 = nullptr, *xext = nullptr;
-  auto make_rows = [&](uint16_t *rows16, uint16_t *rows_ext) -> int {
+  float *cmax = nullptr;
+  auto make_rows = [&](uint16_t *rows16, uint16_t *rows_ext, float *rows_cmax) -> int {
     uint32_t *gmax = nullptr;
     UV_TRY(sc.alloc(&gmax, 1));
     UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
@@ -908,31 +913,38 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
       UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
                              dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
     }
+    uvb::tc_chunk_cmax_kernel<<<(unsigned)((n_pad + 255) / 256), 256, 0, st>>>(rows_ext, n, n_pad,
+                                                                               rows_cmax);
+    UV_CK(cudaGetLastError());
     return UV_OK;
   };
   if (g_tc_cache == 0) {
     UV_TRY(sc.alloc(&x16, (size_t)n_pad * kpad));
     UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
-    UV_TRY(make_rows(x16, xext));
+    UV_TRY(sc.alloc(&cmax, (size_t)n_pad / 16));
+    UV_TRY(make_rows(x16, xext, cmax));
   } else {
     std::lock_guard<std::mutex> rows_lock(ix->tc_mu);
     TcRows &rows = ix->tc_rows[mips];
     if (rows.version != ix->version || rows.n_pad != n_pad || rows.kpad != kpad) {
       rows.version = ~0ull;
       if (rows.cap < n_pad || rows.kpad != kpad) {
-        if (rows.x16 != nullptr || rows.xext != nullptr) {
+        if (rows.x16 != nullptr || rows.xext != nullptr || rows.cmax != nullptr) {
           UV_CK(cudaDeviceSynchronize());
           cudaFree(rows.x16);
           cudaFree(rows.xext);
+          cudaFree(rows.cmax);
           rows.x16 = rows.xext = nullptr;
+          rows.cmax = nullptr;
           rows.cap = 0;
         }
         UV_CK(cudaMalloc((void **)&rows.x16, sizeof(uint16_t) * (size_t)n_pad * kpad));
         UV_CK(cudaMalloc((void **)&rows.xext, sizeof(uint16_t) * (size_t)n_pad * 16));
+        UV_CK(cudaMalloc((void **)&rows.cmax, sizeof(float) * (size_t)n_pad / 16));
         rows.cap = n_pad;
         rows.kpad = kpad;
       }
-      UV_TRY(make_rows(rows.x16, rows.xext));
+      UV_TRY(make_rows(rows.x16, rows.xext, rows.cmax));
       if (rows.ready == nullptr)
         UV_CK(cudaEventCreateWithFlags(&rows.ready, cudaEventDisableTiming));
       UV_CK(cudaEventRecord(rows.ready, st));
@@ -943,6 +955,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     }
     x16 = rows.x16;
     xext = rows.xext;
+    cmax = rows.cmax;
   }
   // TMA maps: main rows of 128 fp16 (boxes of 64 x TN, 128-byte swizzle) and
   // the extra slice of 16 fp16 (boxes of 16 x TN, 32-byte swizzle)
@@ -1037,17 +1050,18 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
   const int64_t n_tiles1 = (n_tiles + S - 1) / S;
   g_tc_last_sample = S;
-  const int64_t n_groups1 = 2 * n_tiles1;
+  const int64_t n_groups1 = gpt * n_tiles1;
   float *tmax = nullptr, *theta = nullptr;
   uint32_t *cand = nullptr;
   int *cand_cnt = nullptr, *flags = nullptr;
   int32_t *over_list = nullptr;
   // Pass 2's candidate list of a query is cut into one segment per (record
-  // split, column half), each appended by a single thread; the rescoring
-  // gathers at most `cap` of them.
+  // split, bound group of a tile), each appended by a single thread; the
+  // rescoring gathers at most `cap` of them.
   const int cap = 2048;
-  const int regions = (int)(2 * splits);  // <= 128: splits <= 64
-  const int region_cap = std::max(256, cap / regions);
+  const int regions = (int)(gpt * splits);  // <= 256: splits <= 64
+  // (the same footprint for both kernels: 2 x 256 or 4 x 128 slots per split)
+  const int region_cap = std::max(512 / gpt, cap / regions);
   const int64_t cand_stride = (int64_t)regions * region_cap;
   UV_TRY(sc.alloc(&tmax, (size_t)nq * n_groups1));
   UV_TRY(sc.alloc(&theta, (size_t)nq));
@@ -1074,6 +1088,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   tp.theta = theta;
   tp.cand = cand;
   tp.cand_cnt = cand_cnt;
+  tp.cmax = cmax;
   tp.err = flags;
   const dim3 grid((unsigned)qtiles, (unsigned)splits);
   int kchunks = kpad / 64;
@@ -1084,10 +1099,11 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     tp1.tile_stride = S;
     const dim3 grid1((unsigned)qtiles,
                      (unsigned)std::max<int64_t>(1, std::min<int64_t>(splits, n_tiles1 / 8)));
-    void *args[] = {&tp1, &tmap_main, &tmap_ext};
+    void *args[] = {&tp1, &tmap_main};
     void *wargs[] = {&tp1, &kchunks, &tmap_a, &tmap_ax_lo, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass1", st);
-    UV_CK(cudaLaunchKernel(k1, grid1, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
+    UV_CK(cudaLaunchKernel(k1, grid1, dim3(wide ? uvb::tc_wide_threads() : uvb::tc_threads()),
+                           wide ? wargs : args, smem, st));
   }
   {
     ProfScope ps("tc_theta", st);
@@ -1099,10 +1115,11 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaGetLastError());
   }
   {
-    void *args[] = {&tp, &tmap_main, &tmap_ext};
+    void *args[] = {&tp, &tmap_main};
     void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax_hi, &tmap_main, &tmap_ext};
     ProfScope ps("tc_pass2", st);
-    UV_CK(cudaLaunchKernel(k2, grid, dim3(uvb::tc_threads()), wide ? wargs : args, smem, st));
+    UV_CK(cudaLaunchKernel(k2, grid, dim3(wide ? uvb::tc_wide_threads() : uvb::tc_threads()),
+                           wide ? wargs : args, smem, st));
   }
   {
     uvb::TcRescoreParams rp;

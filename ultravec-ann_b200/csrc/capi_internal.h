@@ -248,6 +248,7 @@ struct uv_ivf {
 struct TcRows {
   uint16_t *x16 = nullptr;      // cap x kpad
   uint16_t *xext = nullptr;     // cap x 16
+  float *cmax = nullptr;        // cap / 32 chunk maxima of the bound constants
   int64_t cap = 0, n_pad = 0;   // rows allocated / rows made
   int kpad = 0;
   uint64_t version = ~0ull;     // index version the rows were made from

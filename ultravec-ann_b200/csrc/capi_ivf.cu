@@ -222,7 +222,7 @@ int tc_rank_rows(const float *a, const float *a_norm, int64_t m_total, int d, co
       int kchunks = kpad / 64;
       void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax, &tmap_b, &tmap_bx};
       UV_CK(cudaLaunchKernel(wk, dim3((unsigned)qtiles, (unsigned)splits),
-                             dim3(uvb::tc_threads()), wargs, wsmem, st));
+                             dim3(uvb::tc_wide_threads()), wargs, wsmem, st));
     }
     {
       ProfScope ps("ivf_select", st);

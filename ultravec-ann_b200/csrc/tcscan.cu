@@ -14,31 +14,34 @@
 //   reference accumulation; |q| <= 1.0001 for a rotated unit query.
 //   score in [g_r dot_tc - c_r, g_r dot_tc + c_r] with g_r = rnorm_r /
 //   rescale_r (x norm_r) and c_r = g_r beta_r plus the f32 roundings of the
-//   score; both bounds come out of the MMA directly (below).
+//   score; the epilogue forms both bounds from the MMA's g_r dot_tc (below).
 //
-// Pass 1 (MODE 1) writes, per query and 96-record half tile, the largest
-// lower bound; the k-th largest of those maxima is a score that at least k
+// Pass 1 (MODE 1) writes, per query and 48-record tile slice, a lower bound
+// of its best record's score; the k-th largest of those maxima is a score that at least k
 // records reach, so it lower-bounds the exact k-th best (theta).  Pass 2
 // (MODE 2) appends every record whose upper bound reaches theta to the
 // query's candidate list; the exact top-k is among them, ties included.
 // The candidates are then scored exactly (tc_rescore_kernel) and ranked.
 //
-// Records are first turned, once per search, into fp16 operand rows that
-// carry the bound constants (tc_prepare_records_kernel):
+// Records are first turned into fp16 operand rows plus their bound
+// constants (tc_prepare_records_kernel; kept between searches):
 //   main  B'_r,i = fp16(g_r * x_r,i * s)             128 coordinates
 //   ext   C'_r   = fp16 rounded up of c_r * s         one extra K slice of 16
-// with s = 2^-e a power of two that keeps every |B'| below 2^14.  The query
-// tile carries an extra column of -1 (pass 1) or +1 (pass 2), so the MMA
-// itself yields s * (lower or upper bound of the exact score): the epilogue
-// only takes maxima or compares.  Record tiles stream in by TMA (128-byte
-// swizzle for the main rows, 32-byte for the extra slice).
+// with s = 2^-e a power of two that keeps every |B'| below 2^14, and the
+// largest C' of every 16-record chunk (tc_chunk_cmax_kernel).  The MMA runs
+// over the 128 coordinates only (K = 128: the extra slice would cost a ninth
+// more tensor work and record bytes per tile); the epilogue turns
+// s * g * dot into bounds with the chunk's largest C', rounded outwards
+// (bounds_run_cmax in uv_tc_epilogue.cuh).  Record tiles stream in by TMA (128-byte swizzle).
 //
 // CTA = one unit of 128 queries x a record range, streaming 192-record
 // tiles.  Warp roles:
-//   warps 0-7  epilogue: warp w reads TMEM lane quarter w % 4 (thread =
-//              query) and column half w / 4 (96 records) of each tile
-//   warp 8     TMEM allocation; lane 0 issues the MMAs
-//   warp 9     lane 0 issues the TMA loads
+//   warps 0-15 epilogue: warp w reads TMEM lane quarter w % 4 (thread =
+//              query) and column slice w / 4 (48 records) of each tile;
+//              sixteen warps, because the epilogue, not the MMA, sets the
+//              tile rate (four per scheduler hide its latency)
+//   warp 16    TMEM allocation; lane 0 issues the MMAs
+//   warp 17    lane 0 issues the TMA loads
 // The query tile (A) sits in TMEM (default; the MMA reads it there) or in
 // shared memory.  Four (three) shared-memory stages and two TMEM
 // accumulators of 192 columns are handed over with mbarriers; every wait is
@@ -57,29 +60,29 @@ namespace {
 constexpr int TC_M = 128;      // queries per MMA (TMEM lanes)
 constexpr int TC_D = 128;      // coordinates (K) of the main rows
 constexpr int TC_X = 16;       // the extra K slice (bound constant + zeros)
-constexpr int TC_THREADS = 320;
+constexpr int TC_EPI_WARPS = 16;                   // epilogue warps
+constexpr int TC_THREADS = (TC_EPI_WARPS + 2) * 32;  // + MMA warp + TMA warp
 constexpr uint32_t kWaitLimit = 1u << 20;
 
 // CTA shapes.  S = 1: the queries (A) in shared memory, three stages.
 // S = 3 (the default): A held in TMEM next to the accumulators (tcgen05.mma
 // reads A from TMEM and B from shared memory), which takes A's reads off the
-// shared-memory port the MMAs and the TMA writes share and frees its 36 KB
-// for a fourth stage.  TMEM: two accumulators of 192 columns (+ 72 columns
+// shared-memory port the MMAs and the TMA writes share and frees its 32 KB
+// for a fourth stage.  TMEM: two accumulators of 192 columns (+ 64 columns
 // of A for S = 3).
 template <int S>
 struct TcShape {
   static constexpr bool A_TMEM = S == 3;
   static constexpr int TN = 192;                       // records per tile
   static constexpr int STAGES = A_TMEM ? 4 : 3;
-  static constexpr int CW = TN / 2;                    // accumulator columns per epilogue warp
-  static constexpr int NL = CW / 32;                   // 32-column TMEM loads per warp
+  static constexpr int SLICES = TC_EPI_WARPS / 4;      // column slices of a tile
+  static constexpr int CW = TN / SLICES;               // accumulator columns per epilogue warp
+  static constexpr int NC = CW / 16;                   // 16-column TMEM loads (chunks) per warp
   static constexpr int a_tile = A_TMEM ? 0 : TC_M * TC_D * 2;   // 32 KB
-  static constexpr int ax_tile = A_TMEM ? 0 : TC_M * TC_X * 2;  // 4 KB
   static constexpr int bm_bytes = TN * 128;            // one 64-wide atom column of records
-  static constexpr int b_bytes = 2 * bm_bytes + TN * TC_X * 2;
+  static constexpr int b_bytes = 2 * bm_bytes;
   static constexpr int a = 0;
-  static constexpr int ax = a + a_tile;
-  static constexpr int b = ax + ax_tile;
+  static constexpr int b = a + a_tile;
   static constexpr int bars = b + STAGES * b_bytes;   // 2 * STAGES + 4 mbarriers
   static constexpr int misc = bars + 16 * 8;          // tmem base, abort flag
   static constexpr int total = misc + 64;
@@ -88,7 +91,7 @@ struct TcShape {
 static_assert(TcShape<1>::b % 1024 == 0 && TcShape<1>::b_bytes % 1024 == 0, "stage alignment");
 static_assert(TcShape<3>::b % 1024 == 0 && TcShape<3>::b_bytes % 1024 == 0, "stage alignment");
 static_assert(TcShape<1>::total <= 227 * 1024 && TcShape<3>::total <= 227 * 1024, "shared memory");
-static_assert(TcShape<3>::a_col + (TC_D + TC_X) / 2 <= 512, "TMEM columns");
+static_assert(TcShape<3>::a_col + TC_D / 2 <= 512, "TMEM columns");
 
 // registers -> TMEM: 32 lanes x 8 columns
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&w)[8]) {
@@ -119,13 +122,11 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
 
 template <int MODE, int S>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap_main,
-                   const __grid_constant__ CUtensorMap tmap_ext) {
+    tc_scan_kernel(const TcScanParams p, const __grid_constant__ CUtensorMap tmap_main) {
   using L = TcShape<S>;
-  constexpr int TN = L::TN, STAGES = L::STAGES, NL = L::NL;
+  constexpr int TN = L::TN, STAGES = L::STAGES, NC = L::NC, SLICES = L::SLICES;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t *sa = sm + L::a;
-  uint8_t *sax = sm + L::ax;
   uint64_t *full = (uint64_t *)(sm + L::bars);  // [STAGES]
   uint64_t *empty = full + STAGES;              // [STAGES]
   uint64_t *accf = empty + STAGES;              // [2]
@@ -148,17 +149,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; a++) {
       tc::mbar_init(&accf[a], 1);
-      tc::mbar_init(&acce[a], 8);  // one arrival per epilogue warp
+      tc::mbar_init(&acce[a], TC_EPI_WARPS);  // one arrival per epilogue warp
     }
     tc::mbar_init(drained, 1);
     *abort_s = 0;
     tc::mbar_fence_init();
   }
-  if (warp == 8) tc::tmem_alloc(tbase_s, 512);
+  if (warp == TC_EPI_WARPS) tc::tmem_alloc(tbase_s, 512);
   if constexpr (L::A_TMEM) {
     // queries -> fp16 rows in TMEM: warp w < 4 writes lanes 32w..32w+31, one
-    // query per lane; 64 columns of coordinate pairs, then the extra slice
-    // (-1 or +1, then zeros) in 8 more
+    // query per lane; 64 columns of coordinate pairs
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -178,9 +178,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         tmem_st8(ta + 8 * g, w);
       }
-      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (ok) w[0] = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
-      tmem_st8(ta + TC_D / 2, w);
       tmem_st_wait();
     }
   } else {
@@ -198,15 +195,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       *(uint4 *)(sa + tc::sw128_chunk_offset(r, c, TC_M)) = v;
     }
-    // the extra slice: -1 (lower bounds) or +1 (upper bounds) against C'
-    for (int e = tid; e < TC_M * 2; e += TC_THREADS) {
-      const int r = e >> 1, c = e & 1;
-      const int64_t q = q0 + r;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (c == 0 && q < p.nq && !p.degenerate[q])
-        v.x = (uint32_t)__half_as_ushort(__float2half_rn(MODE == 1 ? -1.0f : 1.0f));
-      *(uint4 *)(sax + tc::sw32_chunk_offset(r, c)) = v;
-    }
   }
   tc::fence_async_smem();
   tc::tc_fence_before();
@@ -214,23 +202,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc::tc_fence_after();
   const uint32_t tmem = *tbase_s;
 
-  if (warp < 8) {
+  if (warp < TC_EPI_WARPS) {
     // ================= epilogue =================
-    // warp w: TMEM lane quarter w % 4 (thread = query), column half w / 4
-    const int quarter = warp & 3, half = warp >> 2;
+    // warp w: TMEM lane quarter w % 4 (thread = query), column slice w / 4
+    const int quarter = warp & 3, slice = warp >> 2;
     const int64_t q = q0 + quarter * 32 + lane;
     const bool qok = q < p.nq && !p.degenerate[q];
     const float theta = (MODE == 2 && qok) ? p.theta[q] : INFINITY;
-    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * L::CW);
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slice * L::CW);
     // pass 2: this thread's segment of the query's candidate list
-    const int region = (int)blockIdx.y * 2 + half;
+    const int region = (int)blockIdx.y * SLICES + slice;
     uint32_t *seg = MODE == 2 ? p.cand + q * (int64_t)p.cand_cap + (int64_t)region * p.region_cap
                               : nullptr;
     int seg_cnt = 0;
+    // the chunk constants of a tile are loaded one tile ahead, so their
+    // latency overlaps the wait for the accumulator
+    float cm_next[NC];
+    auto load_cm = [&](int it, float(&c)[NC]) {
+      const int64_t r0 = (t_begin + it) * p.tile_stride * TN + slice * L::CW;
+#pragma unroll
+      for (int l = 0; l < NC; l++) c[l] = __ldg(p.cmax + (r0 >> 4) + l);
+    };
+    if (ntiles > 0) load_cm(0, cm_next);
     for (int it = 0; it < ntiles; it++) {
       const int a = it & 1;
       const int64_t tile = t_begin + it;  // group index; records of tile * tile_stride
-      const int64_t rec0 = tile * p.tile_stride * TN + half * L::CW;
+      const int64_t rec0 = tile * p.tile_stride * TN + slice * L::CW;
+      float cm[NC];
+#pragma unroll
+      for (int l = 0; l < NC; l++) cm[l] = cm_next[l];
+      if (it + 1 < ntiles) load_cm(it + 1, cm_next);
       if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
         *abort_s = 1;
         atomicExch(p.err, 1);
@@ -238,17 +239,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (*abort_s) break;
       tc::tc_fence_after();
       const uint32_t base = lane_base + (uint32_t)(a * TN);
-      uint32_t r[NL][32];
+      uint32_t r[NC][16];
 #pragma unroll
-      for (int l = 0; l < NL; l++) tc::tmem_ld32(base + 32 * l, r[l]);
+      for (int l = 0; l < NC; l++) tc::tmem_ld16(base + 16 * l, r[l]);
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acce[a]);  // the warp's accumulator part is in registers
-      tcep::bounds_run<MODE, NL>(p, r, q, qok, theta, 2 * tile + half, rec0, seg, &seg_cnt);
+      tcep::bounds_run_cmax<MODE, NC>(p, r, cm, q, qok, theta, SLICES * tile + slice, rec0,
+                                      seg, &seg_cnt);
+      // reconverge before the next poll: lanes that found no candidate
+      // would otherwise sit in mbarrier.try_wait (which may suspend them
+      // until the next accumulator is ready) while the others append
+      __syncwarp();
     }
     if (MODE == 2 && q < p.nq) p.cand_cnt[q * p.regions + region] = seg_cnt;
-  } else if (warp == 8) {
+  } else if (warp == TC_EPI_WARPS) {
     if (lane == 0) {
       // ================= MMA issue =================
       const uint32_t idesc = tc::idesc_f16_f32(TC_M, TN);
@@ -271,9 +277,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
             mma_f16_ts(d, at + 8 * k, bd, idesc, k > 0 ? 1u : 0u);
           }
-          mma_f16_ts(d, at + TC_D / 2, tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc, 1u);
         } else {
-          const uint32_t a_base = tc::smem_u32(sa), ax_base = tc::smem_u32(sax);
+          const uint32_t a_base = tc::smem_u32(sa);
 #pragma unroll
           for (int k = 0; k < TC_D / 16; k++) {
             const uint32_t off = (uint32_t)((k & 3) * 32);
@@ -281,8 +286,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint64_t bd = tc::sw128_desc(b_base + (k >> 2) * L::bm_bytes + off);
             tc::mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
           }
-          tc::mma_f16(d, tc::sw32_desc(ax_base), tc::sw32_desc(b_base + 2 * L::bm_bytes), idesc,
-                      1u);
         }
         tc::mma_commit(&empty[s]);
         tc::mma_commit(&accf[a]);
@@ -307,7 +310,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::mbar_arrive_expect_tx(&full[s], (uint32_t)L::b_bytes);
       tc::tma_load_2d(dst, &tmap_main, 0, row, &full[s]);
       tc::tma_load_2d(dst + L::bm_bytes, &tmap_main, 64, row, &full[s]);
-      tc::tma_load_2d(dst + 2 * L::bm_bytes, &tmap_ext, 0, row, &full[s]);
     }
     if (*abort_s) tc::drain_stages(full, STAGES, issued, kWaitLimit);
   }
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // ---- teardown: the epilogue has waited for every MMA ----
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == TC_EPI_WARPS) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
     tc::tmem_relinquish();
@@ -485,6 +487,16 @@ __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPr
   xext[1] = make_uint4(0, 0, 0, 0);
 }
 
+__global__ void __launch_bounds__(256)
+    tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_pad, float *cmax) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n_pad) return;  // whole warps: n_pad % 32 == 0
+  float c = r < n ? __half2float(__ushort_as_half(xext[r * TC_X])) : 0.0f;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) c = fmaxf(c, __shfl_xor_sync(0xffffffffu, c, o));
+  if ((threadIdx.x & 15) == 0) cmax[r >> 4] = c;
+}
+
 const void *tc_prepare_records_fast_ptr(int bits) {
   switch (bits) {
     case 1: return (const void *)tc_prepare_records_fast_kernel<1>;
@@ -569,17 +581,17 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   const int64_t q = blockIdx.x;
   if (q >= p.nq) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // gather the segments pass 2 wrote (one per record split and column half);
+  // gather the segments pass 2 wrote (one per record split and column slice);
   // a full segment or more than cap candidates in all sends the query to
   // the exact scan
   if (warp == 0) {
     // lane l owns regions [l*per, (l+1)*per); an exclusive scan gives offsets
-    const int per = (p.regions + 31) >> 5;  // <= 4
-    int c_loc[4];
+    const int per = (p.regions + 31) >> 5;  // <= 8
+    int c_loc[8];
     int tot = 0;
     bool over = false;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
+    for (int t = 0; t < 8; t++) {
       const int r = lane * per + t;
       int c = (t < per && r < p.regions) ? p.cand_cnt[q * p.regions + r] : 0;
       over |= c > p.region_cap;
@@ -595,7 +607,7 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     }
     int ex = incl - tot;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
+    for (int t = 0; t < 8; t++) {
       const int r = lane * per + t;
       if (t < per && r < p.regions) roff[r] = ex;
       ex += c_loc[t];
@@ -610,10 +622,16 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     if (tid == 0) p.over_list[atomicAdd(p.n_over, 1)] = (int32_t)q;
     return;
   }
-  for (int r = 0; r < p.regions; r++) {
-    const int cr = roff[r + 1] - roff[r];
-    const uint32_t *src = p.cand + q * p.cand_stride + (int64_t)r * p.region_cap;
-    for (int j = tid; j < cr; j += 256) cidx[roff[r] + j] = src[j];
+  // every entry at once: its region is the last r with roff[r] <= i (a
+  // non-empty one, since i < roff[regions]), found by bisection
+  for (int i = tid; i < cnt_raw; i += 256) {
+    int lo = 0, hi = p.regions - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (roff[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    cidx[i] = p.cand[q * p.cand_stride + (int64_t)lo * p.region_cap + (i - roff[lo])];
   }
   const int cnt = p.degenerate[q] ? 0 : cnt_raw;
   if (tid == 0) atomicAdd(p.n_cand, (unsigned long long)cnt);
@@ -739,6 +757,7 @@ const void *tc_rescore_kernel_ptr(int bits, bool per_thread) {
 }
 
 int tc_threads() { return TC_THREADS; }
+int tc_groups_per_tile() { return TcShape<3>::SLICES; }
 int tc_tile_records() { return TcShape<1>::TN; }
 int tc_tile_queries() { return TC_M; }
 int tc_dim() { return TC_D; }

@@ -238,4 +238,6 @@ const void *tc_wide_kernel_ptr(int mode) {
 
 size_t tc_wide_smem_bytes() { return (size_t)W_TOTAL; }
 
+int tc_wide_threads() { return W_THREADS; }
+
 }  // namespace uvb

@@ -206,6 +206,8 @@ struct TcScanParams {
                                // region = split * 2 + column half, region_cap each
   int *cand_cnt;               // mode 2: nq x regions segment counts
   int regions, region_cap;
+  const float *cmax;           // n_pad / 16: largest C' of each 16-record chunk (records
+                               // below n; tc_scan_kernel applies it in the epilogue)
   int *err;
 };
 
@@ -269,7 +271,9 @@ __global__ void merge_topk_kernel(const MergeParams p);
 // shape 1: the queries (A) in shared memory; 3: A in TMEM (the default)
 const void *tc_scan_kernel_ptr(int mode, int shape);
 size_t tc_scan_smem_bytes(int shape);
-int tc_threads();
+int tc_threads();          // tc_scan_kernel's block
+int tc_groups_per_tile();  // pass-1 groups (and pass-2 candidate regions) per tile and split
+int tc_wide_threads();     // tc_wide_kernel's block
 int tc_tile_records();
 int tc_tile_queries();
 int tc_dim();
@@ -278,6 +282,11 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 // widths 1, 2, 4 with the table in shared memory (4 << (mem + bits) bytes,
 // 256 threads); null for other widths
 const void *tc_prepare_records_fast_ptr(int bits);
+// cmax[c] = largest C' (element 0 of the extra slice) of records 16c ..
+// 16c + 15 below n, 0 for a chunk of padding only; n_pad % 16 == 0, blocks
+// of 256 threads
+__global__ void tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_pad,
+                                     float *cmax);
 // per-query k-th largest tile maximum; the n_tiles keys are staged in dynamic
 // shared memory (4 bytes each) when n_tiles <= kThetaSmemKeys
 constexpr int kThetaSmemKeys = 12288;

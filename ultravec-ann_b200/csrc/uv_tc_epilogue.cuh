@@ -4,6 +4,8 @@
 // registers).  Pass 1 writes the run's largest lower bound; pass 2 appends
 // every record whose upper bound reaches the query's threshold to its
 // candidate list; mode 3 (the IVF probe) stores every value.
+// bounds_run takes bounds that the MMA formed (the extra K slice);
+// bounds_run_cmax forms them from s * g * dot and the chunk constants.
 #pragma once
 
 #include "uv_kernels.h"
@@ -89,6 +91,81 @@ __device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t
     }
     *count = pos;
   }
+}
+
+// The same for accumulators of s * g * dot alone (no extra K slice), one
+// thread's run of NC chunks of 16 records: the bound constant is applied per
+// chunk with its largest C' (cm[c], from p.cmax), rounded outwards.
+//   pass 1: max_chunk(dot) - cm rounded down lower-bounds the score of the
+//           chunk's largest-dot record (padding rows of the last tile are
+//           left out of the maximum);
+//   pass 2: a record is kept when dot >= t = theta - cm rounded down, which
+//           every record whose own upper bound dot + C' reaches theta
+//           satisfies (C' <= cm).
+template <int MODE, int NC>
+__device__ __forceinline__ void bounds_run_cmax(const TcScanParams &p,
+                                                const uint32_t (&r)[NC][16],
+                                                const float (&cm)[NC], int64_t q, bool qok,
+                                                float theta, int64_t group, int64_t rec0,
+                                                uint32_t *dst, int *count) {
+  float mc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; c++) {
+    const uint32_t *v = r[c];
+    float m = max3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+#pragma unroll
+    for (int j = 3; j < 15; j += 2) m = max3(m, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+    mc[c] = fmaxf(m, __uint_as_float(v[15]));
+  }
+  if (MODE == 1) {
+    if (rec0 + 16 * NC > p.n) {
+#pragma unroll
+      for (int c = 0; c < NC; c++) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          if (rec0 + 16 * c + j < p.n) mx = fmaxf(mx, __uint_as_float(r[c][j]));
+        mc[c] = mx;
+      }
+    }
+    float m = __fsub_rd(mc[0], cm[0]);
+#pragma unroll
+    for (int c = 1; c < NC; c++) m = fmaxf(m, __fsub_rd(mc[c], cm[c]));
+    if (q < p.nq) p.tmax[q * p.n_groups + group] = qok ? m : -INFINITY;
+    return;
+  }
+  float t[NC];
+  bool any = false;
+#pragma unroll
+  for (int c = 0; c < NC; c++) {
+    t[c] = __fsub_rd(theta, cm[c]);
+    any |= !(mc[c] < t[c]);
+  }
+  if (!qok || !any) return;
+  // rare: every record of the chunks whose maximum reaches their threshold
+  static_assert(NC * 16 <= 64, "one 64-bit mask per run");
+  uint64_t mask = 0;
+#pragma unroll
+  for (int c = 0; c < NC; c++) {
+    if (!(mc[c] < t[c])) {
+      uint32_t mk = 0;
+#pragma unroll
+      for (int j = 0; j < 16; j++) mk |= (!(__uint_as_float(r[c][j]) < t[c]) ? 1u : 0u) << j;
+      mask |= (uint64_t)mk << (16 * c);
+    }
+  }
+  if (rec0 + 16 * NC > p.n) {
+    const int64_t room = p.n - rec0;  // records past n are padding
+    mask &= room <= 0 ? 0ull : ((1ull << room) - 1ull);  // room < 16 * NC <= 64 here
+  }
+  int pos = *count;
+  while (mask != 0ull) {
+    const int j = __ffsll((long long)mask) - 1;
+    mask &= mask - 1ull;
+    if (pos < p.region_cap) dst[pos] = (uint32_t)(rec0 + j);
+    pos++;
+  }
+  *count = pos;
 }
 
 }  // namespace tcep
