@@ -45,8 +45,8 @@ FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
 # profiles/tc_scan_kernel_1Mx1k-d128.md; pass 1 as if it bounded every tile
 # (the bench scales it by the fraction it bounds).  A measurement, not
 # recomputed at run time.
-TC_TRAFFIC_PASS1 = 4 * 239.8e6
-TC_TRAFFIC_PASS2 = 332.0e6
+TC_TRAFFIC_PASS1 = 4 * 135.5e6
+TC_TRAFFIC_PASS2 = 328.7e6
 
 
 def parse():

@@ -854,9 +854,10 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   // a useful threshold needs several bound groups per top-k slot (counted as
   // two per tile, the wide kernel's groups of half a tile)
   if (2 * n_tiles < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
-  // bound groups per tile: tile slices of the flat kernel, halves of the wide
+  // pass 1 bounds half tiles (both kernels); pass 2's candidate segments
+  // follow the epilogue's column slices (2 per tile wide, 4 flat)
   const int gpt = wide ? 2 : uvb::tc_groups_per_tile();
-  const int64_t n_groups = gpt * n_tiles;
+  const int64_t n_groups = 2 * n_tiles;
   if (n_tiles * TN > INT32_MAX) return UV_OK;
   *used = true;
   const int dev = c->cfg.device;
@@ -1050,7 +1051,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
   const int64_t n_tiles1 = (n_tiles + S - 1) / S;
   g_tc_last_sample = S;
-  const int64_t n_groups1 = gpt * n_tiles1;
+  const int64_t n_groups1 = 2 * n_tiles1;
   float *tmax = nullptr, *theta = nullptr;
   uint32_t *cand = nullptr;
   int *cand_cnt = nullptr, *flags = nullptr;

@@ -16,7 +16,7 @@
 //   rescale_r (x norm_r) and c_r = g_r beta_r plus the f32 roundings of the
 //   score; the epilogue forms both bounds from the MMA's g_r dot_tc (below).
 //
-// Pass 1 (MODE 1) writes, per query and 48-record tile slice, a lower bound
+// Pass 1 (MODE 1) writes, per query and 96-record half tile, a lower bound
 // of its best record's score; the k-th largest of those maxima is a score that at least k
 // records reach, so it lower-bounds the exact k-th best (theta).  Pass 2
 // (MODE 2) appends every record whose upper bound reaches theta to the
@@ -38,8 +38,9 @@
 // tiles.  Warp roles:
 //   warps 0-15 epilogue: warp w reads TMEM lane quarter w % 4 (thread =
 //              query) and column slice w / 4 (48 records) of each tile;
-//              sixteen warps, because the epilogue, not the MMA, sets the
-//              tile rate (four per scheduler hide its latency)
+//              sixteen warps, because pass 2's epilogue, not the MMA, sets
+//              the tile rate (four per scheduler hide its latency).  Pass 1
+//              has no candidate path and uses warps 0-7 on half tiles.
 //   warp 16    TMEM allocation; lane 0 issues the MMAs
 //   warp 17    lane 0 issues the TMA loads
 // The query tile (A) sits in TMEM (default; the MMA reads it there) or in
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; a++) {
       tc::mbar_init(&accf[a], 1);
-      tc::mbar_init(&acce[a], TC_EPI_WARPS);  // one arrival per epilogue warp
+      tc::mbar_init(&acce[a], MODE == 1 ? 8 : TC_EPI_WARPS);  // one arrival per epilogue warp
     }
     tc::mbar_init(drained, 1);
     *abort_s = 0;
@@ -202,8 +203,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc::tc_fence_after();
   const uint32_t tmem = *tbase_s;
 
-  if (warp < TC_EPI_WARPS) {
-    // ================= epilogue =================
+  if (MODE == 1 && warp < 8) {
+    // ================= pass-1 epilogue =================
+    // No candidate path, so eight warps keep up: warp w reads TMEM lane
+    // quarter w % 4 (thread = query) and column half w / 4 (96 records, two
+    // loads of 48), and writes one lower bound per (query, half tile), the
+    // best over the half's 16-record chunks of max(dot) - cmax rounded down.
+    const int quarter = warp & 3, half = warp >> 2;
+    constexpr int HC = TN / 2 / 16;  // chunks per half tile
+    const int64_t q = q0 + quarter * 32 + lane;
+    const bool qok = q < p.nq && !p.degenerate[q];
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * TN / 2);
+    float cm_next[HC];
+    auto load_cm = [&](int it, float(&c)[HC]) {
+      const int64_t r0 = (t_begin + it) * p.tile_stride * TN + half * TN / 2;
+#pragma unroll
+      for (int l = 0; l < HC; l++) c[l] = __ldg(p.cmax + (r0 >> 4) + l);
+    };
+    if (ntiles > 0) load_cm(0, cm_next);
+    for (int it = 0; it < ntiles; it++) {
+      const int a = it & 1;
+      const int64_t tile = t_begin + it;
+      const int64_t rec0 = tile * p.tile_stride * TN + half * TN / 2;
+      float cm[HC];
+#pragma unroll
+      for (int l = 0; l < HC; l++) cm[l] = cm_next[l];
+      if (it + 1 < ntiles) load_cm(it + 1, cm_next);
+      if (!tc::mbar_wait(&accf[a], (it >> 1) & 1, kWaitLimit)) {
+        *abort_s = 1;
+        atomicExch(p.err, 1);
+      }
+      if (*abort_s) break;
+      tc::tc_fence_after();
+      const uint32_t base = lane_base + (uint32_t)(a * TN);
+      float m = -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t r[HC / 2][16];
+#pragma unroll
+        for (int l = 0; l < HC / 2; l++) tc::tmem_ld16(base + 16 * (h * HC / 2 + l), r[l]);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int l = 0; l < HC / 2; l++) {
+          const int64_t c0 = rec0 + 16 * (h * HC / 2 + l);
+          float mc = tcep::chunk_max16(r[l]);
+          if (c0 + 16 > p.n) {  // the last tile: padding rows stay out of the maximum
+            mc = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (c0 + j < p.n) mc = fmaxf(mc, __uint_as_float(r[l][j]));
+          }
+          m = fmaxf(m, __fsub_rd(mc, cm[h * HC / 2 + l]));
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acce[a]);
+      if (q < p.nq) p.tmax[q * p.n_groups + 2 * tile + half] = qok ? m : -INFINITY;
+    }
+  } else if (MODE == 2 && warp < TC_EPI_WARPS) {
+    // ================= pass-2 epilogue =================
     // warp w: TMEM lane quarter w % 4 (thread = query), column slice w / 4
     const int quarter = warp & 3, slice = warp >> 2;
     const int64_t q = q0 + quarter * 32 + lane;
@@ -295,7 +354,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc::mbar_wait(drained, 0, kWaitLimit);
       }
     }
-  } else if (lane == 0) {
+  } else if (warp == TC_EPI_WARPS + 1 && lane == 0) {
     // ================= TMA producer =================
     int64_t issued = 0;
     for (int it = 0; it < ntiles; it++, issued++) {

@@ -272,7 +272,7 @@ __global__ void merge_topk_kernel(const MergeParams p);
 const void *tc_scan_kernel_ptr(int mode, int shape);
 size_t tc_scan_smem_bytes(int shape);
 int tc_threads();          // tc_scan_kernel's block
-int tc_groups_per_tile();  // pass-1 groups (and pass-2 candidate regions) per tile and split
+int tc_groups_per_tile();  // pass-2 candidate segments per tile column range and split
 int tc_wide_threads();     // tc_wide_kernel's block
 int tc_tile_records();
 int tc_tile_queries();

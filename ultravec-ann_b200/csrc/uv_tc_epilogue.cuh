@@ -93,6 +93,14 @@ __device__ __forceinline__ void bounds_run(const TcScanParams &p, const uint32_t
   }
 }
 
+// maximum of 16 accumulator values (NaN-ignoring like fmaxf)
+__device__ __forceinline__ float chunk_max16(const uint32_t (&v)[16]) {
+  float m = max3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+#pragma unroll
+  for (int j = 3; j < 15; j += 2) m = max3(m, __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+  return fmaxf(m, __uint_as_float(v[15]));
+}
+
 // The same for accumulators of s * g * dot alone (no extra K slice), one
 // thread's run of NC chunks of 16 records: the bound constant is applied per
 // chunk with its largest C' (cm[c], from p.cmax), rounded outwards.
