@@ -101,6 +101,23 @@ def test_ties_zero_rows_degenerate_queries_ragged_sizes(uv, tc_mode):
         assert (a[0][3] == -1).all()
 
 
+def test_all_scores_negative_with_padding_rows(uv, tc_mode):
+    """Every MIPS score far below zero and a last tile with padding rows
+    (65,537 = 341 tiles of 192 + 65): the padding's zero accumulators must
+    not stand in for a record's lower bound, or the threshold would exceed
+    every real score and drop the true top-k (one group holds the padding,
+    so k = 1 is the case that would show it)."""
+    n, nq, dim = 65_537, 40, 128
+    base = np.abs(rand_rows(n, dim, 23)) + np.float32(0.1)
+    queries = -np.abs(rand_rows(nq, dim, 24)) - np.float32(0.1)
+    index = uv.Index(uv.Codec(dim, 2, 8))
+    index.add_batch(base)
+    for k in (1, 10, 100):
+        a, b = search_both(uv, index, queries, k, True, tc_mode)
+        assert same(a, b), k
+        assert (np.asarray(a[1]) < 0).all() and (np.asarray(a[0]) >= 0).all(), k
+
+
 def test_candidate_overflow_falls_back_to_the_exact_scan(uv, tc_mode):
     """Every row identical: every record ties with the k-th score, so every
     record is a candidate and the list overflows; the exact scan answers."""
