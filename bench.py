@@ -41,10 +41,11 @@ N_BASE, N_QUERY = 1_000_000, 10_000
 K_MAIN, K_ALT = 100, 10
 FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM on sm_100
 # DRAM bytes (read + write) per launch of the two tensor-core passes at the
-# bench workload (1M x 10k), from the ncu capture summarized in
-# profiles/tc_scan_kernel_1Mx1k-d128.md; pass 1 as if it bounded every tile
-# (the bench scales it by the fraction it bounds).  A measurement, not
-# recomputed at run time.
+# bench workload (1M records x 10k queries), from one ncu capture of the
+# dram__bytes_read.sum and dram__bytes_write.sum metrics; pass 1 as if it
+# bounded every tile (the bench scales it by the fraction it bounds, and
+# both by the records of the shard: the operand rows stream once per pass).
+# A measurement, not recomputed at run time.
 TC_TRAFFIC_PASS1 = 4 * 135.5e6
 TC_TRAFFIC_PASS2 = 328.7e6
 
@@ -284,11 +285,12 @@ def main():
         time.sleep(0.3)
     uv.profile_enable(True)
     enc_ms, scan_ms = [], []
+    last = None
     for _ in range(args.steps):
         flush.fill_(1)
         barrier()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        step(ev)
+        last = step(ev)
         torch.cuda.synchronize()
         enc_ms.append(ev[0].elapsed_time(ev[1]))
         scan_ms.append(ev[1].elapsed_time(ev[2]))
@@ -362,9 +364,9 @@ def main():
                       "uv_index_search + NCCL all-gather + uv_topk_merge, host copies"}
 
     # CPU baseline: the oracle on a bounded sample, rank 0 at N=1
-    cpu = None
+    cpu = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(index, base_np, query_np, codec)
+        cpu, parity = cpu_baseline(index, base_np, query_np, last)
 
     if rank == 0:
         qps = nq * args.steps / (scan_tot / 1e3)
@@ -395,7 +397,7 @@ def main():
             roof = {"bound": "tensor", "kernel": "tc_scan_kernel (pass 1 and pass 2 per step)",
                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak,
-                    "traffic": TC_TRAFFIC_PASS1 * frac1 + TC_TRAFFIC_PASS2,
+                    "traffic": (TC_TRAFFIC_PASS1 * frac1 + TC_TRAFFIC_PASS2) * n_local / 1e6,
                     "peak_source": "bf16_tflops of MEASURED_PEAKS.json (dense f16 and bf16 "
                                    "tensor peaks are equal)" if "bf16_tflops" in peaks
                                    else "fallback 1.59 PFLOP/s",
@@ -428,6 +430,7 @@ def main():
             "gpu_launches": launches_total,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -443,9 +446,15 @@ def load_peaks():
         return {}
 
 
-def cpu_baseline(index, base_np, query_np, codec):
+def cpu_baseline(index, base_np, query_np, last):
     """The oracle (C restatement of the reference CPU path) on a bounded
-    sample: scan of a few queries over the full index, all host threads."""
+    sample: scan of a few queries over the full index, all host threads.
+
+    The same sample is the parity check of the measured configuration: the
+    oracle's top-100 ids and score bits for those queries, over the GPU's
+    1M records, against the GPU's answer for them in the last timed step
+    (`last`), and the oracle's encoding of the first 8,192 rows against the
+    GPU's records byte for byte (codes, start states, rescale bits)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle as O
 
@@ -457,16 +466,34 @@ def cpu_baseline(index, base_np, query_np, codec):
     qs = query_np[:sample]
     oc.search_topk(rec, qs[:threads], K_MAIN, norms=ex["norms"], threads=threads)  # warm
     t = time.perf_counter()
-    oc.search_topk(rec, qs, K_MAIN, norms=ex["norms"], threads=threads)
+    wids, wsc = oc.search_topk(rec, qs, K_MAIN, norms=ex["norms"], threads=threads)
     dt = time.perf_counter() - t
     enc_rows = 8192
     t = time.perf_counter()
-    oc.encode_batch(base_np[:enc_rows], threads=threads)
+    enc = oc.encode_batch(base_np[:enc_rows], threads=threads)
     de = time.perf_counter() - t
-    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} queries x {len(ex['start'])} records (scan); encode {enc_rows} "
-                      f"rows",
-            "encode_rows_s": enc_rows / de}
+    gids = last[0][:sample].cpu().numpy()
+    gsc = last[1][:sample].cpu().numpy()
+    norms_ok = bool(np.array_equal(ex["norms"].view(np.uint32),
+                                   O.l2_norms(base_np, threads=threads).view(np.uint32)))
+    parity = {
+        "queries": sample, "records": int(len(ex["start"])), "k": K_MAIN,
+        "ids_equal": bool(np.array_equal(gids, wids)),
+        "scores_bitequal": bool(np.array_equal(gsc.view(np.uint32), wsc.view(np.uint32))),
+        "encode_rows": enc_rows,
+        "encode_rows_equal": bool(
+            np.array_equal(ex["codes"][:enc_rows], enc["codes"])
+            and np.array_equal(ex["start"][:enc_rows], enc["start"])
+            and np.array_equal(ex["rescale"][:enc_rows].view(np.uint32),
+                               enc["rescale"].view(np.uint32))),
+        "norms_bitequal": norms_ok,
+        "oracle": "C restatement of the reference CPU path (oracle/), same inputs",
+    }
+    cpu = {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+           "sample": f"{sample} queries x {len(ex['start'])} records (scan); encode {enc_rows} "
+                     f"rows",
+           "encode_rows_s": enc_rows / de}
+    return cpu, parity
 
 
 # ------------------------------------------------------ other workloads ---

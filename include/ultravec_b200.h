@@ -141,8 +141,15 @@ int uv_index_mem_bytes(const uv_index *index, int64_t *bytes);
 #define UV_SEARCH_COSINE 0 /* VectorBackend::search: the codec's score */
 #define UV_SEARCH_MIPS 1   /* score x exact row norm (src/bench.rs:1029-1045) */
 
-/* search (src/trellis.rs:2120-2183) for nq queries, top-k (k <= 128) per
- * query: ids_out/scores_out are nq x k. */
+/* search (src/trellis.rs:2120-2183) for nq queries, the best k per query:
+ * ids_out/scores_out are nq x k (scores_out may be NULL).  Any k >= 1: up to
+ * 128 the scan keeps a fused per-query top-k; above 128 every record is
+ * ranked (all scores, then a device sort of each query's list), so
+ * k = len() returns the whole index in ranking order, as the reference's
+ * MIPS harness asks for (src/bench.rs:1029-1045); slots past len() are
+ * unfilled.  Rows of any width (the last dim % 8 coordinates are the
+ * reference's scalar tail, src/simd.rs:240-243).  UV_EUNSUPPORTED for a
+ * cosine search with k > 128 on an index whose 1-bit shortlist prunes. */
 int uv_index_search(const uv_index *index, const float *queries, int64_t nq, int32_t k,
                     int32_t mode, int64_t *ids_out, float *scores_out, void *stream);
 
@@ -157,15 +164,26 @@ int uv_index_digest(const uv_index *index, uint64_t *digest, void *stream);
  * they serve queries -- a process that reserves its whole GPU memory budget at
  * start-up, or a latency-bound thread that cannot accept the device-wide
  * synchronization that cudaMalloc/cudaFree may bring.  Same arguments and
- * results as uv_index_search, with these limits:
+ * results (ids and score bits) as uv_index_search, with these limits:
  *   - queries, ids_out and scores_out (if given) must be device memory of the
  *     index's GPU; host buffers are rejected (copying them would allocate);
+ *   - it always runs the exact CUDA-core scan (never the tensor-core
+ *     prefilter, whose scratch is larger), so it is slower than
+ *     uv_index_search on large batches;
+ *   - 1 <= k <= 128;
+ *   - UV_EUNSUPPORTED for dim > 384 (no room for the resident query tile of
+ *     the exact scan) and for a cosine search of an index with the 1-bit
+ *     shortlist on (the shortlist search is not built without allocation);
  *   - per-call scratch comes from one 16 MiB array that the library keeps on
- *     every GPU that loads it, until the process exits; a query batch whose
- *     scratch (about nq * (4*dim + 8 + 12*k) bytes) does not fit is rejected
- *     with UV_EINVAL -- search fewer queries per call;
+ *     every GPU that loads it, until the process exits.  A batch needs, per
+ *     query, 4*dim_pad + 4*max(1, n_centroids) + 4 bytes (dim_pad = dim
+ *     rounded up to 4), plus 12*k bytes per record split (at least one),
+ *     plus 4*k when scores_out is NULL, each of those arrays rounded up to
+ *     256 bytes for the whole batch; a batch that does not fit even with one
+ *     split is rejected with UV_EINVAL -- search fewer queries per call;
  *   - the first call on a device looks up that array's device address, so
- *     make it before any stream capture;
+ *     make it before any stream capture; the address is kept until exit and
+ *     is stale after a cudaDeviceReset of that device;
  *   - all calls on a device share the array: calls whose GPU work overlaps
  *     (different streams or threads without ordering) race and corrupt each
  *     other's results; order them on one stream. */

@@ -15,18 +15,20 @@ namespace uvcapi {
 
 thread_local std::string g_err;
 std::mutex g_prof_mu;
-int64_t g_scan_splits = 0;
-int g_tc_mode = 0;
-int g_cand_kernel = 0;
-int g_tc_shape = 0;
-int g_tc_cache = 1;
-int g_coset_nearest = 0;
-int g_tc_sample = 0;
-int g_tc_prepare = 0;
-int g_ivf_tc_probe = 0;
+// Tuning knobs (uv_set_tuning): atomics, so that a thread that tunes while
+// others search is not a data race; every search reads each knob once.
+std::atomic<int64_t> g_scan_splits{0};
+std::atomic<int> g_tc_mode{0};
+std::atomic<int> g_cand_kernel{0};
+std::atomic<int> g_tc_shape{0};
+std::atomic<int> g_tc_cache{1};
+std::atomic<int> g_coset_nearest{0};
+std::atomic<int> g_tc_sample{0};
+std::atomic<int> g_tc_prepare{0};
+std::atomic<int> g_ivf_tc_probe{0};
 std::atomic<int64_t> g_tc_last_candidates{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
-bool g_prof_on = false;
+std::atomic<bool> g_prof_on{false};
 std::vector<ProfRec> g_prof;
 
 cudaMemPool_t scratch_pool() {
@@ -714,13 +716,51 @@ namespace {
 
 // The exact CUDA-core scan over prepared queries (flat_scan_kernel, or the
 // K-chunked kernel for wide rows) with a per-split top-k, then the merge.
+// The scan kernels' view of an index: rows of any width run as width d16
+// (rounded up to 16) with the real width in dim_data (the decode-GEMM over
+// the 16- and 8-wide blocks, then the reference's scalar tail).
+void fill_scan_params(const uv_index *ix, const float *q_r, const float *qc,
+                      const uint32_t *degen, int64_t nq, int k, int mode, int img_words,
+                      bool table_smem, uvb::ScanParams *out) {
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int d16 = (d + 15) & ~15;
+  uvb::ScanParams &sp = *out;
+  std::memset(&sp, 0, sizeof(sp));
+  sp.dim = d16;
+  sp.dim_data = d16 != d ? d : 0;
+  sp.mem = c->cfg.mem;
+  sp.bits = c->cfg.bits;
+  sp.nq = nq;
+  sp.n = ix->n;
+  sp.q_r = q_r;
+  sp.q_stride = (d + 3) & ~3;
+  sp.qc = qc;
+  sp.n_centroids = ix->n_centroids;
+  sp.degenerate = degen;
+  sp.codes = ix->codes;
+  sp.code_stride = c->code_stride;
+  sp.start = ix->start;
+  sp.rescale = ix->rescale;
+  sp.rnorm = ix->rnorm;
+  sp.norms = ix->norms;
+  sp.cidx = ix->cidx;
+  sp.code = c->d_table;
+  sp.table_len = c->table_len;
+  sp.table_in_smem = table_smem ? 1 : 0;
+  sp.img_words = img_words;
+  sp.mips = mode == UV_SEARCH_MIPS ? 1 : 0;
+  sp.k = k;
+  sp.ids = ix->ids;
+  sp.id_base = 0;
+}
+
 int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
                int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
                Scratch &sc) {
   const uv_codec *c = ix->codec;
-  const int d = c->cfg.dim;
+  const int d = (c->cfg.dim + 15) & ~15;  // kernel width (fill_scan_params)
   const int dev = c->cfg.device;
-  const int dim_pad = (d + 3) & ~3;
   const int64_t n = ix->n;
   int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;
   const int rw = c->code_stride / 4;
@@ -756,7 +796,8 @@ int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint
     }
     if (eff >= 0.9) break;
   }
-  if (g_scan_splits > 0) splits = std::min<int64_t>(g_scan_splits, std::max<int64_t>(1, n));
+  const int64_t fixed_splits = g_scan_splits.load();
+  if (fixed_splits > 0) splits = std::min<int64_t>(fixed_splits, std::max<int64_t>(1, n));
   uint32_t *part_key = nullptr;
   int64_t *part_id = nullptr;
   UV_TRY(sc.alloc(&part_key, (size_t)nq * splits * k));
@@ -766,32 +807,7 @@ int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint
     UV_CK(cudaMemsetAsync(part_id, 0xff, sizeof(int64_t) * nq * splits * k, st));
   } else {
     uvb::ScanParams sp;
-    std::memset(&sp, 0, sizeof(sp));
-    sp.dim = d;
-    sp.mem = c->cfg.mem;
-    sp.bits = c->cfg.bits;
-    sp.nq = nq;
-    sp.n = n;
-    sp.q_r = q_r;
-    sp.q_stride = dim_pad;
-    sp.qc = qc;
-    sp.n_centroids = ix->n_centroids;
-    sp.degenerate = degen;
-    sp.codes = ix->codes;
-    sp.code_stride = c->code_stride;
-    sp.start = ix->start;
-    sp.rescale = ix->rescale;
-    sp.rnorm = ix->rnorm;
-    sp.norms = ix->norms;
-    sp.cidx = ix->cidx;
-    sp.code = c->d_table;
-    sp.table_len = c->table_len;
-    sp.table_in_smem = table_smem ? 1 : 0;
-    sp.img_words = img_words;
-    sp.mips = mode == UV_SEARCH_MIPS ? 1 : 0;
-    sp.k = k;
-    sp.ids = ix->ids;
-    sp.id_base = 0;
+    fill_scan_params(ix, q_r, qc, degen, nq, k, mode, img_words, table_smem, &sp);
     sp.part_key = part_key;
     sp.part_id = part_id;
     uvb::ScanWork work;
@@ -803,6 +819,121 @@ int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint
   }
   // 3) merge the splits
   UV_TRY(merge_launch(nq, (int)splits, k, k, part_key, nullptr, part_id, d_ids, d_scores, st));
+  return UV_OK;
+}
+
+// Full ranking for k above the fused top-k capacity (src/trellis.rs:2120-2183
+// with any limit; the MIPS harness asks for len(), src/bench.rs:1029-1045):
+// per chunk of queries, every (query, record) score from the exact scan
+// kernel (ScanParams::all_key), a sort of each query's n (key, id) pairs
+// (rank.cu), then its first k.  Outputs go straight into device buffers, or
+// through a chunk buffer into host ones.
+int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
+                     const uint32_t *degen, int64_t nq, int64_t k, int mode, int64_t *ids_out,
+                     float *scores_out, cudaStream_t st, Scratch &sc) {
+  const uv_codec *c = ix->codec;
+  const int d = (c->cfg.dim + 15) & ~15;
+  const int dev = c->cfg.device;
+  const int dim_pad = (c->cfg.dim + 3) & ~3;
+  const int64_t n = ix->n;
+  bool ids_dev = false, sc_dev = false;
+  UV_TRY(classify(ids_out, dev, &ids_dev));
+  UV_TRY(classify(scores_out, dev, &sc_dev));
+  const bool direct = ids_dev && (scores_out == nullptr || sc_dev);
+  // queries per chunk: two (key, id) buffers of n entries per query (24 B
+  // each) and, for host outputs, the chunk's k results (12 B each), within
+  // about 1 GiB; at least one query
+  const double budget = 1024.0 * 1024.0 * 1024.0;
+  const double per_q = 24.0 * (double)n + (direct ? 0.0 : 12.0 * (double)k);
+  int64_t qb = (int64_t)std::max(1.0, std::floor(budget / std::max(per_q, 1.0)));
+  qb = std::min<int64_t>(std::min<int64_t>(qb, nq), 65535);
+  uint32_t *key0 = nullptr, *key1 = nullptr;
+  int64_t *id0 = nullptr, *id1 = nullptr;
+  int64_t *c_ids = nullptr;
+  float *c_sc = nullptr;
+  if (n > 0) {
+    UV_TRY(sc.alloc(&key0, (size_t)qb * n));
+    UV_TRY(sc.alloc(&key1, (size_t)qb * n));
+    UV_TRY(sc.alloc(&id0, (size_t)qb * n));
+    UV_TRY(sc.alloc(&id1, (size_t)qb * n));
+  }
+  if (!direct) {
+    UV_TRY(sc.alloc(&c_ids, (size_t)qb * k));
+    if (scores_out != nullptr) UV_TRY(sc.alloc(&c_sc, (size_t)qb * k));
+  }
+  const int rw = c->code_stride / 4;
+  int img_words = 4 + rw + 3;
+  if ((img_words & 1) == 0) img_words++;
+  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
+  const bool chunked = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem) > 227 * 1024;
+  const size_t smem = chunked ? uvb::chunked_scan_smem_bytes(c->table_len, table_smem, true)
+                              : uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
+  const void *scan_k = chunked ? uvb::chunked_scan_kernel_ptr(c->cfg.bits, table_smem, true)
+                               : uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
+  if (scan_k == nullptr) return fail(UV_EUNSUPPORTED, "no scan kernel for these bits");
+  UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 1;
+  UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
+  const int64_t slots = (int64_t)sm_count(dev) * std::max(per_sm, 1);
+  const int span = uvb::rank_merge_span();
+  for (int64_t q0 = 0; q0 < nq; q0 += qb) {
+    const int64_t m = std::min(qb, nq - q0);
+    uint32_t *kin = key0, *kout = key1;
+    int64_t *iin = id0, *iout = id1;
+    if (n > 0) {
+      // every score of the chunk
+      const int64_t qtiles = (m + uvb::kScanTQ - 1) / uvb::kScanTQ;
+      int64_t splits = std::max<int64_t>(1, (2 * slots + qtiles - 1) / qtiles);
+      splits = std::min<int64_t>(std::min<int64_t>(splits, std::max<int64_t>(1, n / 256)), 65535);
+      uvb::ScanParams sp;
+      fill_scan_params(ix, q_r + q0 * dim_pad, qc + q0 * std::max(1, ix->n_centroids),
+                       degen + q0, m, 1, mode, img_words, table_smem, &sp);
+      sp.all_key = key0;
+      sp.all_id = id0;
+      uvb::ScanWork work;
+      std::memset(&work, 0, sizeof(work));
+      void *args[] = {&sp, &work};
+      {
+        ProfScope ps("flat_scan", st);
+        UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)qtiles, (unsigned)splits), dim3(256), args,
+                               smem, st));
+      }
+      // sort each query's n entries: tiles, then merge passes keeping the best k
+      const unsigned tiles = (unsigned)((n + uvb::kRankTile - 1) / uvb::kRankTile);
+      {
+        ProfScope ps("rank_sort", st);
+        uvb::rank_tile_sort_kernel<<<dim3(tiles, (unsigned)m), 256, 0, st>>>(key0, id0, n);
+        UV_CK(cudaGetLastError());
+      }
+      for (int64_t w = uvb::kRankTile; w < n; w *= 2) {
+        ProfScope ps("rank_merge", st);
+        const unsigned g = (unsigned)((n + span - 1) / span);
+        uvb::rank_merge_kernel<<<dim3(g, (unsigned)m), 256, 0, st>>>(kin, iin, kout, iout, n, w,
+                                                                      k);
+        UV_CK(cudaGetLastError());
+        std::swap(kin, kout);
+        std::swap(iin, iout);
+      }
+    }
+    int64_t *o_ids = direct ? ids_out + q0 * k : c_ids;
+    float *o_sc = direct ? (scores_out ? scores_out + q0 * k : nullptr) : c_sc;
+    {
+      ProfScope ps("rank_emit", st);
+      const int64_t total = m * k;
+      const unsigned g = (unsigned)std::min<int64_t>((total + 255) / 256, slots * 8);
+      uvb::rank_emit_kernel<<<std::max(g, 1u), 256, 0, st>>>(kin, iin, n, m, k, degen + q0, o_ids,
+                                                            o_sc);
+      UV_CK(cudaGetLastError());
+    }
+    if (!direct) {
+      UV_CK(cudaMemcpyAsync(ids_out + q0 * k, c_ids, sizeof(int64_t) * m * k,
+                            ids_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+      if (scores_out != nullptr)
+        UV_CK(cudaMemcpyAsync(scores_out + q0 * k, c_sc, sizeof(float) * m * k,
+                              sc_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+      UV_CK(cudaStreamSynchronize(st));  // the chunk buffers are reused
+    }
+  }
   return UV_OK;
 }
 
@@ -841,7 +972,8 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   const int64_t n = ix->n;
-  if (g_tc_mode == 1 || ix->n_centroids != 0) return UV_OK;
+  const int tc_mode = g_tc_mode.load();
+  if (tc_mode == 1 || ix->n_centroids != 0) return UV_OK;
   // d = 128: tcscan.cu (the query tile resident for the CTA's life); any
   // other width up to 4096: tcwide.cu (queries and records streamed in K
   // chunks of 64)
@@ -853,7 +985,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int64_t n_tiles = (n + TN - 1) / TN;
   // a useful threshold needs several bound groups per top-k slot (counted as
   // two per tile, the wide kernel's groups of half a tile)
-  if (2 * n_tiles < (g_tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
+  if (2 * n_tiles < (tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
   // pass 1 bounds half tiles (both kernels); pass 2's candidate segments
   // follow the epilogue's column slices (2 per tile wide, 4 flat)
   const int gpt = wide ? 2 : uvb::tc_groups_per_tile();
@@ -919,7 +1051,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaGetLastError());
     return UV_OK;
   };
-  if (g_tc_cache == 0) {
+  if (g_tc_cache.load() == 0) {
     UV_TRY(sc.alloc(&x16, (size_t)n_pad * kpad));
     UV_TRY(sc.alloc(&xext, (size_t)n_pad * 16));
     UV_TRY(sc.alloc(&cmax, (size_t)n_pad / 16));
@@ -1043,11 +1175,12 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   // balances them at the 1M x 10k bench shape (measured optimum 4 at
   // k = 100, 10 at k = 10), capped at 10 and so that k*S stays well inside
   // the candidate lists, and the sample keeps at least 8k groups.
-  int64_t S = g_tc_sample > 0
-                  ? g_tc_sample
+  const int fixed_sample = g_tc_sample.load();
+  int64_t S = fixed_sample > 0
+                  ? fixed_sample
                   : std::max<int64_t>(1, std::min<int64_t>(
                                              10, (int64_t)std::lround(std::sqrt(1600.0 / k))));
-  if (g_tc_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
+  if (fixed_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
   const int64_t n_tiles1 = (n_tiles + S - 1) / S;
   g_tc_last_sample = S;
@@ -1243,13 +1376,11 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
     return fail(UV_EINVAL, "null argument");
   if (nq < 0) return fail(UV_EINVAL, "negative size");
-  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (k < 1) return fail(UV_EINVAL, "k must be at least 1");
   if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
   if (nq == 0) return UV_OK;
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
-  if (d % 16 != 0)
-    return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
   const int dev = c->cfg.device;
   DeviceGuard g(dev);
   cudaStream_t st = (cudaStream_t)stream;
@@ -1257,6 +1388,23 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   Outputs outs;
   const float *d_q = nullptr;
   UV_TRY(stage_in(queries, (size_t)nq * d, dev, sc, &d_q));
+  if (k > uvb::kScanKCap) {
+    // every record ranked.  A cosine search with the 1-bit shortlist keeps
+    // the best max(c, k) entries by sign code (src/trellis.rs:854-948); that
+    // selection is built for k <= 128 only.
+    if (ix->sl_c > 0 && mode == UV_SEARCH_COSINE && std::max<int64_t>(ix->sl_c, k) < ix->n)
+      return fail(UV_EUNSUPPORTED, "the shortlist search is built for k <= 128");
+    const int dim_pad = (d + 3) & ~3;
+    float *q_r = nullptr, *qc = nullptr;
+    uint32_t *degen = nullptr;
+    UV_TRY(sc.alloc(&q_r, (size_t)nq * dim_pad));
+    UV_TRY(sc.alloc(&qc, (size_t)nq * std::max(1, ix->n_centroids)));
+    UV_TRY(sc.alloc(&degen, (size_t)nq));
+    UV_TRY(prep_launch(c, d_q, nq, ix->centroids, ix->n_centroids, q_r, qc, degen, nullptr, st));
+    UV_TRY(full_rank_search(ix, q_r, qc, degen, nq, k, mode, ids_out, scores_out, st, sc));
+    UV_CK(cudaStreamSynchronize(st));
+    return UV_OK;
+  }
   int64_t *d_ids = nullptr;
   float *d_scores = nullptr;
   UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
@@ -1439,7 +1587,10 @@ constexpr int kNoAllocMaxDevices = 64;
 void *g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
 // The device address of g_noalloc_scratch on the current device, looked up
-// once per device (the caller made that device current).
+// once per device (the caller made that device current) and kept for the
+// life of the process: after a cudaDeviceReset of that device the cached
+// address is stale, so a process that resets a device must not call
+// uv_index_search_noalloc on it again.
 int noalloc_scratch(int dev, unsigned char **out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(UV_EINVAL, "device ordinal out of range");
@@ -1468,8 +1619,7 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
   if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
   if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
   const uv_codec *c = ix->codec;
-  const int d = c->cfg.dim;
-  if (d % 16 != 0) return fail(UV_EUNSUPPORTED, "flat scan is built for dim a multiple of 16");
+  const int d = (c->cfg.dim + 15) & ~15;  // kernel width (fill_scan_params)
   if (ix->sl_c > 0 && mode == UV_SEARCH_COSINE && std::max(ix->sl_c, k) < ix->n)
     return fail(UV_EUNSUPPORTED, "the shortlist search is not built without allocation");
   const int dev = c->cfg.device;
@@ -1487,8 +1637,14 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
   if (nq == 0) return UV_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t n = ix->n;
-  const int dim_pad = (d + 3) & ~3;
+  const int dim_pad = (c->cfg.dim + 3) & ~3;
   const int ncen = std::max(1, ix->n_centroids);
+  // every query needs at least its rotated row: reject batches that cannot
+  // fit before any size product below could wrap
+  if (nq > (int64_t)(kNoAllocScratchBytes / (4 * (size_t)dim_pad)))
+    return fail(UV_EINVAL, "this query batch cannot fit the no-allocation search's " +
+                               std::to_string(kNoAllocScratchBytes) +
+                               "-byte scratch; search fewer queries per call");
   const int rw = c->code_stride / 4;
   int img_words = 4 + rw + 3;
   if ((img_words & 1) == 0) img_words++;
@@ -1552,7 +1708,7 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
   {
     uvb::PrepParams pp;
     std::memset(&pp, 0, sizeof(pp));
-    pp.dim = d;
+    pp.dim = c->cfg.dim;
     pp.dim_pad = dim_pad;
     pp.nq = nq;
     pp.queries = queries;
@@ -1567,6 +1723,7 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
     void *args[] = {&pp};
+    ProfScope ps("prep_queries", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,
                            psmem, st));
   }
@@ -1576,35 +1733,11 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
     UV_CK(cudaMemsetAsync(part_id, 0xff, sizeof(int64_t) * nq * splits * k, st));
   } else {
     uvb::ScanParams sp;
-    std::memset(&sp, 0, sizeof(sp));
-    sp.dim = d;
-    sp.mem = c->cfg.mem;
-    sp.bits = c->cfg.bits;
-    sp.nq = nq;
-    sp.n = n;
-    sp.q_r = q_r;
-    sp.q_stride = dim_pad;
-    sp.qc = qc;
-    sp.n_centroids = ix->n_centroids;
-    sp.degenerate = degen;
-    sp.codes = ix->codes;
-    sp.code_stride = c->code_stride;
-    sp.start = ix->start;
-    sp.rescale = ix->rescale;
-    sp.rnorm = ix->rnorm;
-    sp.norms = ix->norms;
-    sp.cidx = ix->cidx;
-    sp.code = c->d_table;
-    sp.table_len = c->table_len;
-    sp.table_in_smem = table_smem ? 1 : 0;
-    sp.img_words = img_words;
-    sp.mips = mode == UV_SEARCH_MIPS ? 1 : 0;
-    sp.k = k;
-    sp.ids = ix->ids;
-    sp.id_base = 0;
+    fill_scan_params(ix, q_r, qc, degen, nq, k, mode, img_words, table_smem, &sp);
     sp.part_key = part_key;
     sp.part_id = part_id;
     void *args[] = {&sp};
+    ProfScope ps("flat_scan", st);
     UV_CK(cudaLaunchKernel(scan_k, dim3((unsigned)qtiles, (unsigned)splits), dim3(256), args,
                            smem, st));
   }
@@ -1630,6 +1763,7 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
     const int grid = (int)((nq + m.warps - 1) / m.warps);
     void *args[] = {&m};
+    ProfScope ps("merge_topk", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_kernel, dim3(grid), dim3(32 * m.warps),
                            args, msmem, st));
   }

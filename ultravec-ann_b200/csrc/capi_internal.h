@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -154,16 +155,16 @@ struct ProfRec {
   cudaEvent_t a, b;
 };
 extern std::mutex g_prof_mu;
-extern int64_t g_scan_splits;  // uv_set_tuning("scan_splits")
-extern int g_tc_mode;          // uv_set_tuning("tc_scan")
-extern int g_cand_kernel;      // uv_set_tuning("cand_kernel")
-extern int g_tc_shape;         // uv_set_tuning("tc_shape")
-extern int g_tc_cache;         // uv_set_tuning("tc_cache")
-extern int g_coset_nearest;    // uv_set_tuning("coset_nearest")
-extern int g_tc_sample;        // uv_set_tuning("tc_sample")
-extern int g_tc_prepare;       // uv_set_tuning("tc_prepare")
-extern int g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
-extern bool g_prof_on;
+extern std::atomic<int64_t> g_scan_splits;  // uv_set_tuning("scan_splits")
+extern std::atomic<int> g_tc_mode;          // uv_set_tuning("tc_scan")
+extern std::atomic<int> g_cand_kernel;      // uv_set_tuning("cand_kernel")
+extern std::atomic<int> g_tc_shape;         // uv_set_tuning("tc_shape")
+extern std::atomic<int> g_tc_cache;         // uv_set_tuning("tc_cache")
+extern std::atomic<int> g_coset_nearest;    // uv_set_tuning("coset_nearest")
+extern std::atomic<int> g_tc_sample;        // uv_set_tuning("tc_sample")
+extern std::atomic<int> g_tc_prepare;       // uv_set_tuning("tc_prepare")
+extern std::atomic<int> g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
+extern std::atomic<bool> g_prof_on;
 extern std::vector<ProfRec> g_prof;
 
 struct ProfScope {

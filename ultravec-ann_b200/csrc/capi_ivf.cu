@@ -416,7 +416,6 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
     UV_CK(cudaGetLastError());
     return UV_OK;
   }
-  if (d % 16 != 0) return fail(UV_EUNSUPPORTED, "scan is built for dim a multiple of 16");
   const int dim_pad = (d + 3) & ~3;
   float *q_r = nullptr, *qc = nullptr, *u = nullptr;
   uint32_t *degen = nullptr;
@@ -528,7 +527,10 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   if ((img_words & 1) == 0) img_words++;
   uvb::ScanParams sp;
   std::memset(&sp, 0, sizeof(sp));
-  sp.dim = d;
+  // rows of any width: the decode-GEMM over width d rounded up to 16, then
+  // the reference's scalar tail over the last d % 8 coordinates
+  sp.dim = (d + 15) & ~15;
+  sp.dim_data = sp.dim != d ? d : 0;
   sp.mem = c->cfg.mem;
   sp.bits = c->cfg.bits;
   sp.nq = nq;

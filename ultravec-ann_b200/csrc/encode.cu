@@ -299,7 +299,7 @@ const void *pick_kernel(int B, int WPT, bool smem_back) {
 
 }  // namespace
 
-int g_encode_back_mode = 0;  // uv_set_tuning("encode_back"): 0 auto, 1 global, 2 shared
+std::atomic<int> g_encode_back_mode{0};  // uv_set_tuning("encode_back"): 0 auto, 1 global, 2 shared
 
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) {
   if (bits < 1 || bits > 4) {
@@ -337,12 +337,13 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
   bool smem = false;
   int teams = tpc;
   // largest team count (whole warps) that fits
-  for (int tc = tpc; tc >= tpc_warp && tc >= 1 && g_encode_back_mode != 1; tc -= tpc_warp) {
+  const int back_mode = g_encode_back_mode.load();
+  for (int tc = tpc; tc >= tpc_warp && tc >= 1 && back_mode != 1; tc -= tpc_warp) {
     if (fits(team_words_smem, tc)) {
       const int64_t cta_bytes = team_words_smem * 4 * tc;
       const int threads = (int)(tc * T);
       const int ctas = (int)std::min<int64_t>(228 * 1024 / std::max<int64_t>(cta_bytes, 1), 2048 / threads);
-      if ((int64_t)ctas * threads >= 256 || g_encode_back_mode == 2) {
+      if ((int64_t)ctas * threads >= 256 || back_mode == 2) {
         smem = true;
         teams = tc;
       }

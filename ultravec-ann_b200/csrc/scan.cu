@@ -333,8 +333,12 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
   float *theta_s = (float *)(degen + TQ);                    // TQ: score of theta
   float *sc = theta_s + TQ;                                  // 2 x NSC x TN scalars
   int *flag = (int *)(sc + 2 * NSC * TN);                    // 4
-  float *table = (float *)(flag + 4);                        // optional code table
+  float *qtail = (float *)(flag + 4);                        // TQ x 8 tail coordinates
+  float *table = qtail + TQ * 8;                             // optional code table
   const float *code = TSMEM ? table : p.code;
+  // coordinates [d8, d8 + ntail) are the scalar tail (dim_data % 8 of them)
+  const int d8 = p.dim_data > 0 ? (p.dim_data & ~7) : d;
+  const int ntail = p.dim_data > 0 ? p.dim_data - d8 : 0;
 
   const int64_t q_base = (int64_t)blockIdx.x * TQ;
   const int split = blockIdx.y;
@@ -349,8 +353,13 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
     // pre-permuted by that lane's mask (bits 3, 2, 0 of j)
     const int jm = i & 15;
     const int qm = (((jm >> 3) & 1) << 2) | (((jm >> 2) & 1) << 1) | (jm & 1);
-    const bool live = q < p.nq && (B != 0 || i < p.coset.dim);
+    const bool live = q < p.nq && (B != 0 ? i < d8 : i < p.coset.dim);
     qT[(size_t)i * QSTR + (qi ^ qm)] = live ? p.q_r[q * (int64_t)p.q_stride + i] : 0.0f;
+  }
+  for (int e = tid; e < TQ * 8; e += 256) {
+    const int qi = e >> 3, t = e & 7;
+    const int64_t q = q_base + qi;
+    qtail[e] = (t < ntail && q < p.nq) ? p.q_r[q * (int64_t)p.q_stride + d8 + t] : 0.0f;
   }
   for (int e = tid; e < TQ * KCAP; e += 256) top[e] = kEmptyKey;
   if (tid < TQ) {
@@ -458,7 +467,16 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       o.y = __shfl_xor_sync(0xffffffffu, l3[c + 2].y, 2);
       dot2[c] = __fadd2_rn(l3[c], o);
     }
-    const float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
+    float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
+    // scalar tail (src/simd.rs:240-243): total += q[i] * book[idx[i]], in order
+    for (int t2 = 0; t2 < ntail; t2++) {
+      const int i = d8 + t2;
+      const float qv = qtail[qsel * 8 + t2];
+      const float *xr = xT + (size_t)i * XSTR;
+      const int sw = ((i >> 1) & 1) << 2;
+#pragma unroll
+      for (int c = 0; c < 4; c++) dot4[c] = fadd(dot4[c], fmul(qv, xr[(rsel + c) ^ sw]));
+    }
 
     // ---- estimator (src/trellis.rs:1517), MIPS norm, threshold test ----
     // A cheap bound first: a = qm + dot*(rnorm/rescale) (x norm) differs from
@@ -485,11 +503,17 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
         if (maybe && r < nr) {
           float sx = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
           if (p.mips) sx = fmul(sx, scs[2 * TN + r]);
-          const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
-          if (key > th) {
-            const int pos = atomicAdd(&cnt[qsel], 1);
-            buf[(size_t)qsel * BCAP + pos] = key;
-            if (pos == BCAP - TN) flag[0] = t + 1;
+          if (p.all_key != nullptr) {
+            const int64_t rec = r0 + r;
+            p.all_key[q * p.n + rec] = score_key32(sx);
+            p.all_id[q * p.n + rec] = p.ids ? p.ids[rec] : p.id_base + rec;
+          } else {
+            const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
+            if (key > th) {
+              const int pos = atomicAdd(&cnt[qsel], 1);
+              buf[(size_t)qsel * BCAP + pos] = key;
+              if (pos == BCAP - TN) flag[0] = t + 1;
+            }
           }
         }
       }
@@ -524,7 +548,7 @@ __global__ void __launch_bounds__(256, 2) flat_scan_kernel(const ScanParams p) {
       if (cnt[qi] > 0)
         flush_query<KCAP, BCAP>(top + (size_t)qi * KCAP, buf + (size_t)qi * BCAP, &cnt[qi], &theta[qi],
                     &theta_s[qi], p.k);
-      if (q < p.nq) {
+      if (q < p.nq && p.part_key != nullptr) {
         uint32_t *ok = p.part_key + (q * gridDim.y + split) * (int64_t)p.k;
         int64_t *oid = p.part_id + (q * gridDim.y + split) * (int64_t)p.k;
         for (int i = lane; i < p.k; i += 32) {
@@ -590,7 +614,8 @@ struct ChunkLayout {
   static constexpr size_t degen = cnt + TQ * 4;                     // TQ u32
   static constexpr size_t sc = degen + TQ * 4;                      // 2 x NSC x TN f32
   static constexpr size_t flag = sc + 2 * NSC * TN * 4;             // 4 i32
-  static constexpr size_t table = flag + 16;
+  static constexpr size_t qtail = flag + 16;                        // TQ x 8 f32
+  static constexpr size_t table = qtail + TQ * 8 * 4;
 };
 
 template <int B, bool TSMEM, int KC_, int BC_>
@@ -614,8 +639,12 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
   uint32_t *degen = (uint32_t *)(sm + L::degen);
   float *sc = (float *)(sm + L::sc);
   int *flag = (int *)(sm + L::flag);
+  float *qtail = (float *)(sm + L::qtail);
   float *table = (float *)(sm + L::table);
   const float *code = TSMEM ? table : p.code;
+  // coordinates [d8, d8 + ntail) are the scalar tail (dim_data % 8 of them)
+  const int d8 = p.dim_data > 0 ? (p.dim_data & ~7) : d;
+  const int ntail = p.dim_data > 0 ? p.dim_data - d8 : 0;
 
   // ---- this CTA's work: record range and up to 32 (query, slot) pairs ----
   int64_t r_begin, r_end;
@@ -662,6 +691,11 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
     for (int e = tid; e < p.table_len; e += 256) table[e] = __ldg(p.code + e);
   __syncthreads();
   if (tid < TQ) degen[tid] = qrow[tid] >= 0 ? p.degenerate[qrow[tid]] : 1u;
+  for (int e = tid; e < TQ * 8; e += 256) {
+    const int qi = e >> 3, t = e & 7;
+    const int64_t q = qrow[qi];
+    qtail[e] = (t < ntail && q >= 0) ? __ldg(p.q_r + q * (int64_t)p.q_stride + d8 + t) : 0.0f;
+  }
 
   const int nchunks = (d + KCH - 1) / KCH;
   const int ntiles = (int)((r_end - r_begin + TN - 1) / TN);
@@ -675,7 +709,7 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
       const int qmk = (((jm >> 3) & 1) << 2) | (((jm >> 2) & 1) << 1) | (jm & 1);
       const int64_t q = qrow[qi];
       qT[(size_t)i * QSTR + (qi ^ qmk)] =
-          q >= 0 ? __ldg(p.q_r + q * (int64_t)p.q_stride + k0 + i) : 0.0f;
+          (q >= 0 && k0 + i < d8) ? __ldg(p.q_r + q * (int64_t)p.q_stride + k0 + i) : 0.0f;
     }
   };
   if (steps > 0) {
@@ -772,7 +806,16 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
         o.y = __shfl_xor_sync(0xffffffffu, l3[c + 2].y, 2);
         dot2[c] = __fadd2_rn(l3[c], o);
       }
-      const float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
+      float dot4[4] = {dot2[0].x, dot2[0].y, dot2[1].x, dot2[1].y};
+      // scalar tail (src/simd.rs:240-243), rows of this last chunk
+      for (int t2 = 0; t2 < ntail; t2++) {
+        const int i = d8 + t2;
+        const float qv = qtail[qsel * 8 + t2];
+        const float *xr = (bsel ? xT1 : xT0) + (size_t)(i - ch * KCH) * XSTR;
+        const int sw = ((i >> 1) & 1) << 2;
+#pragma unroll
+        for (int c = 0; c < 4; c++) dot4[c] = fadd(dot4[c], fmul(qv, xr[(rsel + c) ^ sw]));
+      }
       const float *scs = sc + (tile & 1) * NSC * TN;
       if (!degen[qsel]) {
         const uint64_t th = theta[qsel];
@@ -795,11 +838,17 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
           if (maybe && r < nr) {
             float sx = fadd(qm, fmul(scs[TN + r], fdiv(dot4[c], scs[r])));
             if (p.mips) sx = fmul(sx, scs[2 * TN + r]);
-            const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
-            if (key > th) {
-              const int pos = atomicAdd(&cnt[qsel], 1);
-              buf[(size_t)qsel * BC_ + pos] = key;
-              if (pos == BC_ - TN) flag[0] = tile + 1;
+            if (p.all_key != nullptr) {
+              const int64_t rec = r0 + r;
+              p.all_key[q * p.n + rec] = score_key32(sx);
+              p.all_id[q * p.n + rec] = p.ids ? p.ids[rec] : p.id_base + rec;
+            } else {
+              const uint64_t key = rank_key(sx, (uint32_t)(r0 - r_begin + r));
+              if (key > th) {
+                const int pos = atomicAdd(&cnt[qsel], 1);
+                buf[(size_t)qsel * BC_ + pos] = key;
+                if (pos == BC_ - TN) flag[0] = tile + 1;
+              }
             }
           }
         }
@@ -835,7 +884,7 @@ __global__ void __launch_bounds__(256, 2) chunked_scan_kernel(const ScanParams p
         flush_query<KC_, BC_>(top + (size_t)qi * KC_, buf + (size_t)qi * BC_, &cnt[qi],
                               &theta[qi], &theta_s[qi], p.k);
       const int64_t sl = slot[qi];
-      if (sl >= 0) {
+      if (sl >= 0 && p.part_key != nullptr) {
         uint32_t *ok = p.part_key + sl * (int64_t)p.k;
         int64_t *oid = p.part_id + sl * (int64_t)p.k;
         for (int i = lane; i < p.k; i += 32) {
@@ -963,6 +1012,7 @@ size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem
   b += (size_t)TQ * KCAP * 8 + (size_t)TQ * BCAP * 8;   // top-k + buffers
   b += (size_t)TQ * 8 + (size_t)TQ * 4 * 3;             // theta, cnt, degenerate, theta_s
   b += 2 * NSC * (size_t)TN * 4 + 16;                   // scalars, flag
+  b += (size_t)TQ * 8 * 4;                              // tail coordinates
   if (table_in_smem) b += (size_t)table_len * 4;
   return b;
 }

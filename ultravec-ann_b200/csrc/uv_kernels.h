@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <string>
 #include <algorithm>
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include "uv_common.cuh"
@@ -47,7 +48,7 @@ struct EncodePlan {
   const void *kernel;
 };
 
-extern int g_encode_back_mode;  // placement of back-pointers; never changes results
+extern std::atomic<int> g_encode_back_mode;  // placement of back-pointers; never changes results
 
 // 0 ok, 1 invalid, 2 unsupported (message in *why)
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
@@ -107,6 +108,17 @@ struct ScanParams {
   uint32_t *part_key;  // nq x splits x k
   int64_t *part_id;
   CosetModel coset;    // coset records (coset_scan_kernel)
+  // Rows whose width is not a multiple of 16: `dim` is the width rounded up
+  // to 16 and dim_data the real width (0: dim).  The 16- and 8-wide blocks
+  // below dim_data & ~7 run through the decode-GEMM (zero query lanes above);
+  // the last dim_data % 8 coordinates are added after the hsum tree, one
+  // separately rounded product and sum at a time (src/simd.rs:240-243).
+  int dim_data;
+  // Full ranking (k above the top-k capacity): every (query, record) score
+  // key (score_key32) and id is written to all_key / all_id [q * n + record]
+  // instead of a per-split top-k; part_key / part_id are unused.
+  uint32_t *all_key;
+  int64_t *all_id;
 };
 
 // Work items of the chunked scan.  Flat (ivf == 0): the grid is query tiles x
@@ -399,6 +411,17 @@ const void *coset_scan_kernel_ptr();
 constexpr int kScanTQ = 32;
 constexpr int kScanTN = 32;
 constexpr int kScanKCap = 128;
+
+// Full ranking (rank.cu) for k above kScanKCap: sort every query's n score
+// keys and ids.
+constexpr int kRankTile = 2048;  // elements per block-sort tile (= rank_merge_span())
+__global__ void rank_tile_sort_kernel(uint32_t *key, int64_t *id, int64_t n);
+__global__ void rank_merge_kernel(const uint32_t *ik, const int64_t *ii, uint32_t *ok, int64_t *oi,
+                                  int64_t n, int64_t w, int64_t klim);
+__global__ void rank_emit_kernel(const uint32_t *key, const int64_t *id, int64_t n, int64_t nq,
+                                 int64_t k, const uint32_t *degen, int64_t *out_id,
+                                 float *out_score);
+int rank_merge_span();
 
 size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem);
 
