@@ -196,10 +196,63 @@ int uv_index_clear(uv_index *index);
 
 /* Merge per-shard top-k lists (the multi-GPU combine after an all-gather):
  * in_ids/in_scores are nq x n_lists x k_in, each list sorted by the ranking
- * above; out is nq x k.  Device or host memory. */
+ * above; out is nq x k (k <= n_lists x k_in).  Device or host memory.  Up
+ * to 8192 entries per row a k-way merge of the sorted lists, above that a
+ * segmented sort. */
 int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream);
+
+/* ---- a base split across GPUs (one index shard per GPU) ---------------- */
+
+/* No counterpart in the reference (a single-process CPU crate): the
+ * multi-GPU form of search (src/trellis.rs:2120-2183) over a base whose
+ * records are split into disjoint shards, one uv_index per GPU, each added
+ * with its rows' global ids.  Every shard answers a search in two phases
+ * around one exchange, and the shards' lists then merge into the answer a
+ * single index over the whole base gives (ids and score bits):
+ *   1. uv_index_search_begin on every shard, with the number of shards:
+ *      query preparation and the prefilter's first pass.  bounds_out
+ *      receives nq x k lower bounds (any order): scores that k distinct
+ *      records of this shard reach (-inf where it has no such bound).
+ *   2. The caller gathers every shard's bounds, shard-major (n_shards x nq x
+ *      k floats: one all-gather), and hands them to uv_search_set_bounds on
+ *      every shard.  The k-th largest of their union is a score that k
+ *      records of the whole base reach, so no shard keeps a record below it;
+ *      each shard then scores exactly only the records that can still be in
+ *      the global top k, instead of its own top k's worth.  Skipping this
+ *      step gives the shard's own top k, as uv_index_search does.
+ *   3. uv_search_finish: this shard's best (at most) k, ranked as
+ *      uv_index_search, unfilled slots (id -1) where fewer records pass.
+ *   4. uv_search_destroy (before the index is destroyed).
+ * The lists of all shards then merge into the global top k: uv_topk_pack
+ * the shard's lists, exchange query slices (all-to-all), and
+ * uv_topk_merge_packed each slice over the shards.  All calls of one search
+ * run on the stream given to begin; a search is used by one thread.  Any k
+ * (above 128 every shard ranks all its records and step 2 changes
+ * nothing); queries and outputs in host or device memory. */
+typedef struct uv_search uv_search;
+int uv_index_search_begin(const uv_index *index, const float *queries, int64_t nq, int32_t k,
+                          int32_t mode, int32_t n_shards, float *bounds_out, uv_search **out,
+                          void *stream);
+int uv_search_set_bounds(uv_search *search, const float *gathered, int32_t n_shards);
+int uv_search_finish(uv_search *search, int64_t *ids_out, float *scores_out);
+int uv_search_destroy(uv_search *search);
+
+/* n (id, score) pairs as 12-byte records -- int32 id low, int32 id high,
+ * f32 score bits -- so that a shard's lists travel in one collective.
+ * Device buffers of `device`. */
+int uv_topk_pack(int32_t device, const int64_t *ids, const float *scores, int64_t n, void *packed,
+                 void *stream);
+/* uv_topk_merge over packed records (device memory): list l of row q starts
+ * at record q * row_stride + l * list_stride (0, 0: rows of n_lists x k_in
+ * contiguous records).  After an all-to-all of query slices the lists of
+ * slice row q from shard l sit at l * (rows * k_in) + q * k_in, i.e.
+ * row_stride = k_in, list_stride = rows * k_in.  Any sizes (above 8192
+ * entries per row a segmented sort replaces the k-way merge). */
+int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t n_lists,
+                         int32_t k_in, int64_t row_stride, int64_t list_stride, int32_t k,
+                         int64_t *out_ids, float *out_scores, void *stream);
 
 /* Launch-shape tuning, no counterpart in the reference (results never depend
  * on it): "scan_splits" fixes the number of record ranges each query tile is

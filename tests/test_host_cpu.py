@@ -125,6 +125,88 @@ def test_sharded_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
     assert (tmp_path / "ok").read_text() == "1"
 
 
+def _gloo_protocol_worker(rank, world, port, result_dir):
+    """One rank of the sharded flat search protocol (shard.sharded_search)
+    on gloo: the oracle stands in for the device phases (bounds = the
+    shard's exact top-k scores, a valid lower bound for k distinct records;
+    finish = its top-k cut at the shared threshold) and host routines for
+    pack / merge."""
+    import torch
+    import torch.distributed as dist
+
+    import sys
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    sys.path.insert(0, str(REPO))
+    import oracle as O
+    from ultravec_ann_b200_loader import load
+
+    load()
+    from ultravec_ann_b200.shard import (merge_packed_host, pack_host, shard_range,
+                                         sharded_search, unpack_host)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rows = O.rand_unit(700, 64, 61) * np.float32(3.0)
+    rows[5] = rows[600]  # an exact tie across shards, broken by id
+    qs = O.rand_unit(16, 64, 62)
+    k = 10
+    codec = O.Codec(64, 2, 8)
+    lo, hi = shard_range(len(rows), rank, world)
+    enc = codec.encode_batch(rows[lo:hi])
+    norms = O.l2_norms(rows[lo:hi])
+
+    class StandIn:
+        def __init__(self):
+            ids, sc = codec.search_topk(enc, qs, k, norms=norms)
+            self.ids = np.where(ids >= 0, ids + lo, -1)
+            self.sc = sc
+            self.bounds = torch.from_numpy(sc.copy())
+            self.theta = None
+
+        def set_bounds(self, gathered, n):
+            g = gathered.numpy().reshape(n, len(qs), k).transpose(1, 0, 2).reshape(len(qs), -1)
+            self.theta = -np.sort(-g, axis=1)[:, k - 1]
+
+        def finish(self):
+            keep = self.sc >= self.theta[:, None]
+            return (torch.from_numpy(np.where(keep, self.ids, -1)),
+                    torch.from_numpy(np.where(keep, self.sc, -np.inf).astype(np.float32)))
+
+        def close(self):
+            pass
+
+    g_ids, g_sc = sharded_search(lambda n: StandIn(), k, dist, pack_host, unpack_host,
+                                 merge_packed_host)
+    full = codec.encode_batch(rows)
+    want_ids, want_sc = codec.search_topk(full, qs, k, norms=O.l2_norms(rows))
+    ok = np.array_equal(g_ids.numpy(), want_ids) and np.array_equal(
+        g_sc.numpy().view(np.uint32), want_sc.view(np.uint32))
+    Path(result_dir, f"ok{rank}").write_text("1" if ok else "0")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_search_protocol_with_gloo_ranks(tmp_path, world):
+    """The flat multi-GPU protocol on CPU ranks: bounds all-gathered, shared
+    threshold, lists packed, all-to-all of query slices (uneven at world 3),
+    per-slice merge, all-gather -- every rank ends with the unsharded top-k."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_gloo_protocol_worker, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    for r in range(world):
+        assert (tmp_path / f"ok{r}").read_text() == "1"
+
+
 def test_ivf_list_owners_balance_bytes(uv):
     from ultravec_ann_b200.shard import ivf_list_owners, ivf_owned_rows
 

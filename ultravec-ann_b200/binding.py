@@ -40,6 +40,8 @@ SYMBOLS = [
     "uv_ivf_export_signs", "uv_coset_create", "uv_coset_destroy", "uv_coset_set_centroids",
     "uv_coset_add", "uv_coset_search", "uv_coset_len", "uv_coset_shape", "uv_coset_books",
     "uv_coset_mem_bytes", "uv_coset_model_bytes", "uv_coset_export", "uv_coset_reconstruct",
+    "uv_index_search_begin", "uv_search_set_bounds", "uv_search_finish", "uv_search_destroy",
+    "uv_topk_pack", "uv_topk_merge_packed",
 ]
 
 
@@ -143,6 +145,13 @@ def lib():
             "uv_coset_model_bytes": (C.c_int, [vp, C.POINTER(i64)]),
             "uv_coset_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp]),
             "uv_coset_reconstruct": (C.c_int, [vp, vp, i64, vp, vp]),
+            "uv_index_search_begin": (C.c_int, [vp, vp, i64, i32, i32, i32, vp, vpp, vp]),
+            "uv_search_set_bounds": (C.c_int, [vp, vp, i32]),
+            "uv_search_finish": (C.c_int, [vp, vp, vp]),
+            "uv_search_destroy": (C.c_int, [vp]),
+            "uv_topk_pack": (C.c_int, [i32, vp, vp, i64, vp, vp]),
+            "uv_topk_merge_packed": (C.c_int, [i32, vp, i64, i32, i32, i64, i64, i32, vp, vp,
+                                               vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -391,6 +400,11 @@ class Index:
                                     UV_SEARCH_MIPS if mips else UV_SEARCH_COSINE, _ptr(ids),
                                     _ptr(scores), _stream(queries)))
         return ids, scores
+
+    def search_begin(self, queries, k: int, mips: bool = False, n_shards: int = 1):
+        """Phase 1 of a search of this index as one shard of n_shards (see
+        ShardSearch): query preparation and the prefilter's first pass."""
+        return ShardSearch(self, queries, k, mips, n_shards)
 
     # -- the 1-bit shortlist (src/trellis.rs:803-948) --
     def set_shortlist(self, c: int, asym: bool = False, rnorm: bool = True) -> None:
@@ -722,6 +736,80 @@ class IvfIndex:
         ix = cls.__new__(cls)
         ix.h, ix.codec, ix.centered = h, codec, None
         return ix
+
+
+class ShardSearch:
+    """A search of one shard of a base split across GPUs
+    (uv_index_search_begin / uv_search_set_bounds / uv_search_finish):
+    `bounds` (nq x k) are this shard's first-pass lower bounds; gather every
+    shard's bounds shard-major into (n_shards * nq, k), pass them to
+    set_bounds, then finish() gives this shard's (ids, scores), at most k per
+    query, of which only records that can be in the global top k remain."""
+
+    def __init__(self, index: Index, queries, k: int, mips: bool, n_shards: int):
+        queries = _f32(queries)
+        self.nq, self.k = queries.shape[0], k
+        self._alloc = _Alloc(queries)
+        self._like = queries
+        self.bounds = self._alloc((self.nq, k), np.float32)
+        h = C.c_void_p()
+        check(lib().uv_index_search_begin(index.h, _ptr(queries), self.nq, k,
+                                          UV_SEARCH_MIPS if mips else UV_SEARCH_COSINE,
+                                          n_shards, _ptr(self.bounds), C.byref(h),
+                                          _stream(queries)))
+        self.h, self.index = h, index
+
+    def set_bounds(self, gathered, n_shards: int):
+        gathered = _f32(gathered)
+        check(lib().uv_search_set_bounds(self.h, _ptr(gathered), n_shards))
+
+    def finish(self):
+        ids = self._alloc((self.nq, self.k), np.int64)
+        scores = self._alloc((self.nq, self.k), np.float32)
+        check(lib().uv_search_finish(self.h, _ptr(ids), _ptr(scores)))
+        return ids, scores
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uv_search_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def topk_pack(ids, scores, device: int = 0):
+    """(nq, k) device ids and scores as one (nq, k, 3) int32 tensor of
+    12-byte records (id low, id high, score bits): one buffer per collective."""
+    import torch
+
+    out = torch.empty(tuple(ids.shape) + (3,), dtype=torch.int32, device=ids.device)
+    check(lib().uv_topk_pack(device, _ptr(ids), _ptr(scores), ids.numel(), _ptr(out),
+                             _stream(ids)))
+    return out
+
+
+def topk_unpack(packed):
+    """Inverse of topk_pack (torch ops): (..., 3) int32 -> ids, scores."""
+    import torch
+
+    lo = packed[..., 0].to(torch.int64) & 0xFFFFFFFF
+    hi = packed[..., 1].to(torch.int64)
+    return (hi << 32) | lo, packed[..., 2].contiguous().view(torch.float32)
+
+
+def topk_merge_packed(packed, nq: int, n_lists: int, k_in: int, k: int, row_stride: int = 0,
+                      list_stride: int = 0, device: int = 0):
+    """Merge packed per-shard lists: list l of row q starts at record
+    q * row_stride + l * list_stride (0, 0: contiguous rows)."""
+    alloc = _Alloc(packed)
+    ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+    check(lib().uv_topk_merge_packed(device, _ptr(packed), nq, n_lists, k_in, row_stride,
+                                     list_stride, k, _ptr(ids), _ptr(scores), _stream(packed)))
+    return ids, scores
 
 
 def topk_merge(in_ids, in_scores, k: int, device: int = 0):

@@ -653,7 +653,7 @@ int merge_launch(int64_t nq, int n_lists, int k_in, int k, const uint32_t *in_ke
   while (pow2 < n_lists * k_in) pow2 <<= 1;
   if (pow2 > 8192) return fail(UV_EUNSUPPORTED, "merge of more than 8192 candidates per query");
   m.pow2 = pow2;
-  const size_t per_warp = (size_t)pow2 * 16;
+  const size_t per_warp = (size_t)pow2 * 12;  // id + key per entry
   m.warps = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / per_warp));
   m.in_key = in_key;
   m.in_score = in_score;
@@ -822,6 +822,40 @@ int exact_scan(const uv_index *ix, const float *q_r, const float *qc, const uint
   return UV_OK;
 }
 
+// Sort `rows` segments of n (key, id) entries (buffers a, spare b) by (key
+// desc, id asc), keeping the best klim of each (rank.cu); *result is the
+// buffer that holds the sorted rows.
+int rank_sort_rows(uint32_t *ka, int64_t *ia, uint32_t *kb, int64_t *ib, int64_t n, int64_t rows,
+                   int64_t klim, cudaStream_t st, bool *in_b) {
+  *in_b = false;
+  if (n <= 0 || rows <= 0) return UV_OK;
+  const int span = uvb::rank_merge_span();
+  const unsigned tiles = (unsigned)((n + uvb::kRankTile - 1) / uvb::kRankTile);
+  const unsigned g = (unsigned)((n + span - 1) / span);
+  bool flip = false;
+  for (int64_t r0 = 0; r0 < rows; r0 += 65535) {
+    const unsigned m = (unsigned)std::min<int64_t>(65535, rows - r0);
+    uint32_t *kin = ka + r0 * n, *kout = kb + r0 * n;
+    int64_t *iin = ia + r0 * n, *iout = ib + r0 * n;
+    {
+      ProfScope ps("rank_sort", st);
+      uvb::rank_tile_sort_kernel<<<dim3(tiles, m), 256, 0, st>>>(kin, iin, n);
+      UV_CK(cudaGetLastError());
+    }
+    flip = false;
+    for (int64_t w = uvb::kRankTile; w < n; w *= 2) {
+      ProfScope ps("rank_merge", st);
+      uvb::rank_merge_kernel<<<dim3(g, m), 256, 0, st>>>(kin, iin, kout, iout, n, w, klim);
+      UV_CK(cudaGetLastError());
+      std::swap(kin, kout);
+      std::swap(iin, iout);
+      flip = !flip;
+    }
+  }
+  *in_b = flip;  // the same number of passes for every row chunk
+  return UV_OK;
+}
+
 // Full ranking for k above the fused top-k capacity (src/trellis.rs:2120-2183
 // with any limit; the MIPS harness asks for len(), src/bench.rs:1029-1045):
 // per chunk of queries, every (query, record) score from the exact scan
@@ -875,11 +909,10 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
   int per_sm = 1;
   UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
   const int64_t slots = (int64_t)sm_count(dev) * std::max(per_sm, 1);
-  const int span = uvb::rank_merge_span();
   for (int64_t q0 = 0; q0 < nq; q0 += qb) {
     const int64_t m = std::min(qb, nq - q0);
-    uint32_t *kin = key0, *kout = key1;
-    int64_t *iin = id0, *iout = id1;
+    uint32_t *kin = key0;
+    int64_t *iin = id0;
     if (n > 0) {
       // every score of the chunk
       const int64_t qtiles = (m + uvb::kScanTQ - 1) / uvb::kScanTQ;
@@ -899,20 +932,11 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
                                smem, st));
       }
       // sort each query's n entries: tiles, then merge passes keeping the best k
-      const unsigned tiles = (unsigned)((n + uvb::kRankTile - 1) / uvb::kRankTile);
-      {
-        ProfScope ps("rank_sort", st);
-        uvb::rank_tile_sort_kernel<<<dim3(tiles, (unsigned)m), 256, 0, st>>>(key0, id0, n);
-        UV_CK(cudaGetLastError());
-      }
-      for (int64_t w = uvb::kRankTile; w < n; w *= 2) {
-        ProfScope ps("rank_merge", st);
-        const unsigned g = (unsigned)((n + span - 1) / span);
-        uvb::rank_merge_kernel<<<dim3(g, (unsigned)m), 256, 0, st>>>(kin, iin, kout, iout, n, w,
-                                                                      k);
-        UV_CK(cudaGetLastError());
-        std::swap(kin, kout);
-        std::swap(iin, iout);
+      bool in_b = false;
+      UV_TRY(rank_sort_rows(key0, id0, key1, id1, n, m, k, st, &in_b));
+      if (in_b) {
+        kin = key1;
+        iin = id1;
       }
     }
     int64_t *o_ids = direct ? ids_out + q0 * k : c_ids;
@@ -965,10 +989,34 @@ int encode_tiled_fn(EncodeTiledFn *out) {
 
 // Tensor-core prefilter + exact rescoring (tcscan.cu).  Sets *used = false
 // when the configuration is outside what the kernels are built for.
-int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
-              int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
-              Scratch &sc, bool *used) {
-  *used = false;
+// The prefilter in two phases, so that shards of one base can exchange their
+// first-pass bounds in between (uv_index_search_begin / uv_search_finish):
+// tc_begin runs pass 1 and the local threshold, tc_finish pass 2, the exact
+// rescoring and the fallback for overflowed queries.
+struct TcState {
+  bool used = false;
+  bool wide = false;
+  const void *k2 = nullptr;
+  dim3 grid;
+  size_t smem = 0;
+  int threads = 0;
+  int kchunks = 0;
+  uvb::TcScanParams tp;
+  alignas(64) CUtensorMap tmap_main;
+  alignas(64) CUtensorMap tmap_ext;
+  alignas(64) CUtensorMap tmap_a;
+  alignas(64) CUtensorMap tmap_ax_hi;
+  int cap = 0, regions = 0, region_cap = 0;
+  int64_t cand_stride = 0, S = 1, n_groups1 = 0;
+  float *tmax = nullptr, *theta = nullptr;
+  uint32_t *cand = nullptr;
+  int *flags = nullptr;
+  int32_t *over_list = nullptr;
+};
+
+int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_t nq, int k,
+             int mode, int n_shards, cudaStream_t st, Scratch &sc, TcState *ts) {
+  ts->used = false;
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   const int64_t n = ix->n;
@@ -984,18 +1032,20 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   const int TN = uvb::tc_tile_records(), TM = uvb::tc_tile_queries();
   const int64_t n_tiles = (n + TN - 1) / TN;
   // a useful threshold needs several bound groups per top-k slot (counted as
-  // two per tile, the wide kernel's groups of half a tile)
-  if (2 * n_tiles < (tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
+  // two per tile, the wide kernel's groups of half a tile), over all shards
+  // whose bounds meet
+  const int64_t shards = std::max(1, n_shards);
+  if (2 * n_tiles * shards < (tc_mode == 2 ? (int64_t)k : 8 * (int64_t)k)) return UV_OK;
   // pass 1 bounds half tiles (both kernels); pass 2's candidate segments
   // follow the epilogue's column slices (2 per tile wide, 4 flat)
   const int gpt = wide ? 2 : uvb::tc_groups_per_tile();
   const int64_t n_groups = 2 * n_tiles;
   if (n_tiles * TN > INT32_MAX) return UV_OK;
-  *used = true;
+  ts->used = true;
+  ts->wide = wide;
   const int dev = c->cfg.device;
   const int dim_pad = (d + 3) & ~3;
   const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
-  (void)qc;
   // fp16 operand rows with the bound constants folded in.  By default they
   // are made once per index version and score mode and kept (tuning key
   // "tc_cache").  A remake after a change of the records rewrites them in
@@ -1092,7 +1142,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
   }
   // TMA maps: main rows of 128 fp16 (boxes of 64 x TN, 128-byte swizzle) and
   // the extra slice of 16 fp16 (boxes of 16 x TN, 32-byte swizzle)
-  CUtensorMap tmap_main, tmap_ext;
+  CUtensorMap &tmap_main = ts->tmap_main, &tmap_ext = ts->tmap_ext;
   {
     EncodeTiledFn enc = nullptr;
     UV_TRY(encode_tiled_fn(&enc));
@@ -1113,7 +1163,8 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     if (r != CUDA_SUCCESS) return fail(UV_ECUDA, "cuTensorMapEncodeTiled (extra slice) failed");
   }
   // wide rows: the queries as fp16 rows too, with maps for both extra slices
-  CUtensorMap tmap_a, tmap_ax_lo, tmap_ax_hi;
+  alignas(64) CUtensorMap tmap_ax_lo;
+  CUtensorMap &tmap_a = ts->tmap_a, &tmap_ax_hi = ts->tmap_ax_hi;
   if (wide) {
     const int64_t nq_pad = (nq + 127) / 128 * 128;
     uint16_t *a16 = nullptr, *ax_lo = nullptr, *ax_hi = nullptr;
@@ -1181,7 +1232,7 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
                   : std::max<int64_t>(1, std::min<int64_t>(
                                              10, (int64_t)std::lround(std::sqrt(1600.0 / k))));
   if (fixed_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
-  while (S > 1 && 2 * ((n_tiles + S - 1) / S) < 8 * (int64_t)k) S--;
+  while (S > 1 && 2 * ((n_tiles + S - 1) / S) * shards < 8 * (int64_t)k) S--;
   const int64_t n_tiles1 = (n_tiles + S - 1) / S;
   g_tc_last_sample = S;
   const int64_t n_groups1 = 2 * n_tiles1;
@@ -1248,12 +1299,45 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(tmax, n_groups1, nq, k, theta);
     UV_CK(cudaGetLastError());
   }
+  ts->k2 = k2;
+  ts->grid = grid;
+  ts->smem = smem;
+  ts->threads = wide ? uvb::tc_wide_threads() : uvb::tc_threads();
+  ts->kchunks = kchunks;
+  ts->tp = tp;
+  ts->cap = cap;
+  ts->regions = regions;
+  ts->region_cap = region_cap;
+  ts->cand_stride = cand_stride;
+  ts->S = S;
+  ts->n_groups1 = n_groups1;
+  ts->tmax = tmax;
+  ts->theta = theta;
+  ts->cand = cand;
+  ts->flags = flags;
+  ts->over_list = over_list;
+  return UV_OK;
+}
+
+int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+              int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+              Scratch &sc, TcState &ts) {
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int dim_pad = (d + 3) & ~3;
+  const int mips = mode == UV_SEARCH_MIPS ? 1 : 0;
+  const int cap = ts.cap, regions = ts.regions, region_cap = ts.region_cap;
+  const int64_t cand_stride = ts.cand_stride, S = ts.S;
+  uint32_t *cand = ts.cand;
+  int *cand_cnt = ts.tp.cand_cnt;
+  int *flags = ts.flags;
+  int32_t *over_list = ts.over_list;
   {
-    void *args[] = {&tp, &tmap_main};
-    void *wargs[] = {&tp, &kchunks, &tmap_a, &tmap_ax_hi, &tmap_main, &tmap_ext};
+    void *args[] = {&ts.tp, &ts.tmap_main};
+    void *wargs[] = {&ts.tp, &ts.kchunks, &ts.tmap_a, &ts.tmap_ax_hi, &ts.tmap_main, &ts.tmap_ext};
     ProfScope ps("tc_pass2", st);
-    UV_CK(cudaLaunchKernel(k2, grid, dim3(wide ? uvb::tc_wide_threads() : uvb::tc_threads()),
-                           wide ? wargs : args, smem, st));
+    UV_CK(cudaLaunchKernel(ts.k2, ts.grid, dim3(ts.threads), ts.wide ? wargs : args, ts.smem,
+                           st));
   }
   {
     uvb::TcRescoreParams rp;
@@ -1342,6 +1426,19 @@ int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaStreamSynchronize(st));  // `rows` is host memory of this frame
   }
   return UV_OK;
+}
+
+// Tensor-core prefilter + exact rescoring (tcscan.cu / tcwide.cu) of one
+// index.  Sets *used = false when the configuration is outside what the
+// kernels are built for.
+int tc_search(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+              int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+              Scratch &sc, bool *used) {
+  TcState ts;
+  UV_TRY(tc_begin(ix, q_r, degen, nq, k, mode, 1, st, sc, &ts));
+  *used = ts.used;
+  if (!ts.used) return UV_OK;
+  return tc_finish(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc, ts);
 }
 
 }  // namespace
@@ -1437,6 +1534,262 @@ int uv_index_search(const uv_index *ix, const float *queries, int64_t nq, int32_
   return outs.finish(st);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Sharded search (uv_index_search_begin ... uv_search_finish): a search of
+// one shard of a base split across GPUs, in two phases around the exchange
+// of first-pass bounds.  Every buffer lives in the search's own stream-ordered
+// scratch until uv_search_destroy.
+// ---------------------------------------------------------------------------
+struct uv_search {
+  const uv_index *ix = nullptr;
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  Scratch sc;
+  int64_t nq = 0;
+  int k = 0, mode = 0;
+  enum Path { kPrefilter, kExact, kShortlist, kFullRank } path = kExact;
+  bool finished = false;
+  const float *d_q = nullptr;
+  float *q_r = nullptr, *qc = nullptr;
+  uint32_t *degen = nullptr;
+  TcState ts;
+  explicit uv_search(cudaStream_t s) : st(s), sc(s) {}
+};
+
+extern "C" {
+
+int uv_index_search_begin(const uv_index *ix, const float *queries, int64_t nq, int32_t k,
+                          int32_t mode, int32_t n_shards, float *bounds_out, uv_search **out,
+                          void *stream) {
+  if (out == nullptr) return fail(UV_EINVAL, "null argument");
+  *out = nullptr;
+  if (ix == nullptr || bounds_out == nullptr || (nq > 0 && queries == nullptr))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1) return fail(UV_EINVAL, "k must be at least 1");
+  if (n_shards < 1) return fail(UV_EINVAL, "n_shards must be at least 1");
+  if (mode != UV_SEARCH_COSINE && mode != UV_SEARCH_MIPS) return fail(UV_EINVAL, "bad mode");
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  uv_search *s = new (std::nothrow) uv_search(st);
+  if (s == nullptr) return fail(UV_ENOMEM, "host allocation failed");
+  auto run = [&]() -> int {
+    s->ix = ix;
+    s->dev = dev;
+    s->nq = nq;
+    s->k = k;
+    s->mode = mode;
+    bool b_dev = false;
+    UV_TRY(classify(bounds_out, dev, &b_dev));
+    float *d_bounds = bounds_out;
+    if (!b_dev) UV_TRY(s->sc.alloc(&d_bounds, (size_t)std::max<int64_t>(nq, 1) * k));
+    if (nq == 0) return UV_OK;
+    // a private copy of the queries: the caller's buffer may go away
+    float *q_copy = nullptr;
+    UV_TRY(s->sc.alloc(&q_copy, (size_t)nq * d));
+    bool q_dev = false;
+    UV_TRY(classify(queries, dev, &q_dev));
+    UV_CK(cudaMemcpyAsync(q_copy, queries, sizeof(float) * nq * d,
+                          q_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+    s->d_q = q_copy;
+    const int dim_pad = (d + 3) & ~3;
+    UV_TRY(s->sc.alloc(&s->q_r, (size_t)nq * dim_pad));
+    UV_TRY(s->sc.alloc(&s->qc, (size_t)nq * std::max(1, ix->n_centroids)));
+    UV_TRY(s->sc.alloc(&s->degen, (size_t)nq));
+    UV_TRY(prep_launch(c, s->d_q, nq, ix->centroids, ix->n_centroids, s->q_r, s->qc, s->degen,
+                       nullptr, st));
+    const bool shortlist = ix->sl_c > 0 && mode == UV_SEARCH_COSINE &&
+                           std::max<int64_t>(ix->sl_c, k) < ix->n;
+    if (k > uvb::kScanKCap) {
+      if (shortlist) return fail(UV_EUNSUPPORTED, "the shortlist search is built for k <= 128");
+      s->path = uv_search::kFullRank;
+    } else if (shortlist) {
+      s->path = uv_search::kShortlist;
+    } else {
+      UV_TRY(tc_begin(ix, s->q_r, s->degen, nq, k, mode, n_shards, st, s->sc, &s->ts));
+      s->path = s->ts.used ? uv_search::kPrefilter : uv_search::kExact;
+    }
+    if (s->path == uv_search::kPrefilter) {
+      ProfScope ps("tc_theta", st);
+      uvb::tc_bounds_kernel<<<(unsigned)nq, 256, 0, st>>>(s->ts.tmax, s->ts.n_groups1, nq, k,
+                                                          s->ts.theta, d_bounds);
+      UV_CK(cudaGetLastError());
+    } else {
+      // no first pass on this shard: it bounds nothing
+      uvb::fill_value_kernel<<<(unsigned)std::min<int64_t>((nq * k + 255) / 256, 4096), 256, 0,
+                               st>>>(d_bounds, nq * k, -INFINITY);
+      UV_CK(cudaGetLastError());
+    }
+    if (!b_dev) {
+      UV_CK(cudaMemcpyAsync(bounds_out, d_bounds, sizeof(float) * nq * k, cudaMemcpyDeviceToHost,
+                            st));
+      UV_CK(cudaStreamSynchronize(st));
+    }
+    return UV_OK;
+  };
+  const int rc = run();
+  if (rc != UV_OK) {
+    delete s;
+    return rc;
+  }
+  *out = s;
+  return UV_OK;
+}
+
+int uv_search_set_bounds(uv_search *s, const float *gathered, int32_t n_shards) {
+  if (s == nullptr || (s->nq > 0 && gathered == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (n_shards < 1) return fail(UV_EINVAL, "n_shards must be at least 1");
+  if (s->finished) return fail(UV_EINVAL, "the search has finished");
+  if (s->nq == 0 || s->path != uv_search::kPrefilter) return UV_OK;
+  const int dev = s->ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  const int64_t nq = s->nq;
+  const int k = s->k;
+  const size_t count = (size_t)n_shards * nq * k;
+  const float *d_g = nullptr;
+  UV_TRY(stage_in(gathered, count, dev, s->sc, &d_g));
+  float *per_q = nullptr;
+  UV_TRY(s->sc.alloc(&per_q, count));
+  ProfScope ps("tc_theta", s->st);
+  uvb::tc_bounds_regroup_kernel<<<(unsigned)std::min<size_t>((count + 255) / 256, 4096), 256, 0,
+                                  s->st>>>(d_g, n_shards, nq, k, per_q);
+  UV_CK(cudaGetLastError());
+  const int64_t per = (int64_t)n_shards * k;
+  const size_t tsm = per <= uvb::kThetaSmemKeys ? (size_t)per * 4 : 0;
+  if (tsm > 48 * 1024)
+    UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)tsm));
+  uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, s->st>>>(per_q, per, nq, k, s->ts.theta);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
+int uv_search_finish(uv_search *s, int64_t *ids_out, float *scores_out) {
+  if (s == nullptr || (s->nq > 0 && ids_out == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (s->finished) return fail(UV_EINVAL, "the search has finished");
+  s->finished = true;
+  if (s->nq == 0) return UV_OK;
+  const uv_index *ix = s->ix;
+  const uv_codec *c = ix->codec;
+  const int dev = c->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = s->st;
+  const int64_t nq = s->nq;
+  const int k = s->k;
+  if (s->path == uv_search::kFullRank) {
+    UV_TRY(full_rank_search(ix, s->q_r, s->qc, s->degen, nq, k, s->mode, ids_out, scores_out, st,
+                            s->sc));
+    UV_CK(cudaStreamSynchronize(st));
+    return UV_OK;
+  }
+  Outputs outs;
+  int64_t *d_ids = nullptr;
+  float *d_scores = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, s->sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, s->sc, &d_scores));
+  } else {
+    UV_TRY(s->sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  switch (s->path) {
+    case uv_search::kShortlist:
+      UV_TRY(shortlist_launch(c, ix->sl_c, ix->sl_asym, ix->sl_weight && ix->n_centroids > 0, k,
+                              nq, 1, nullptr, nullptr, ix->n, ix->n, s->q_r, nullptr, nullptr,
+                              s->qc, ix->n_centroids, s->degen, ix->codes, ix->signs, ix->start,
+                              ix->cidx, ix->rescale, ix->rnorm, ix->ids, d_ids, d_scores, st));
+      break;
+    case uv_search::kPrefilter:
+      UV_TRY(tc_finish(ix, s->q_r, s->qc, s->degen, nq, k, s->mode, d_ids, d_scores, st, s->sc,
+                       s->ts));
+      break;
+    default:
+      UV_TRY(exact_scan(ix, s->q_r, s->qc, s->degen, nq, k, s->mode, d_ids, d_scores, st, s->sc));
+      break;
+  }
+  return outs.finish(st);
+}
+
+int uv_search_destroy(uv_search *s) {
+  if (s == nullptr) return UV_OK;
+  DeviceGuard g(s->dev);
+  delete s;  // frees the scratch on the search's stream
+  return UV_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// The merge of per-shard (or per-split) top-k lists described by m (input
+// pointers, strides, nq, n_lists, k_in, k) into d_ids / d_scores: the k-way
+// merge kernel up to 8192 entries per row, the segmented sort above.
+int merge_rows(uvb::MergeParams m, int64_t *d_ids, float *d_scores, cudaStream_t st, Scratch &sc) {
+  const int64_t total = (int64_t)m.n_lists * m.k_in;
+  m.out_id = d_ids;
+  m.out_score = d_scores;
+  if (total <= 8192) {
+    int pow2 = 32;
+    while (pow2 < total) pow2 <<= 1;
+    m.pow2 = pow2;
+    const size_t per_warp = (size_t)pow2 * 12;  // id + key per entry
+    m.warps = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / per_warp));
+    const size_t smem = per_warp * m.warps;
+    UV_CK(cudaFuncSetAttribute(uvb::merge_topk_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = (int)((m.nq + m.warps - 1) / m.warps);
+    void *args[] = {&m};
+    ProfScope ps("merge_topk", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_kernel, dim3(grid), dim3(32 * m.warps),
+                           args, smem, st));
+    return UV_OK;
+  }
+  // rows in chunks whose two (key, id) buffers stay within about 1 GiB
+  const int64_t rows = std::max<int64_t>(1, std::min<int64_t>(m.nq, (int64_t)(1 << 30) / (24 * total)));
+  uint32_t *k0 = nullptr, *k1 = nullptr;
+  int64_t *i0 = nullptr, *i1 = nullptr;
+  UV_TRY(sc.alloc(&k0, (size_t)rows * total));
+  UV_TRY(sc.alloc(&k1, (size_t)rows * total));
+  UV_TRY(sc.alloc(&i0, (size_t)rows * total));
+  UV_TRY(sc.alloc(&i1, (size_t)rows * total));
+  const int64_t row_stride = m.row_stride > 0 ? m.row_stride : total;
+  for (int64_t r0 = 0; r0 < m.nq; r0 += rows) {
+    uvb::MergeParams part = m;
+    part.nq = std::min(rows, m.nq - r0);
+    if (part.in_packed) part.in_packed += 3 * r0 * row_stride;
+    if (part.in_id) part.in_id += r0 * row_stride;
+    if (part.in_key) part.in_key += r0 * row_stride;
+    if (part.in_score) part.in_score += r0 * row_stride;
+    part.row_stride = row_stride;
+    {
+      ProfScope ps("merge_topk", st);
+      const int64_t all = part.nq * total;
+      uvb::rank_gather_kernel<<<(unsigned)std::min<int64_t>((all + 255) / 256, 148 * 16), 256, 0,
+                                st>>>(part, total, k0, i0);
+      UV_CK(cudaGetLastError());
+    }
+    bool in_b = false;
+    UV_TRY(rank_sort_rows(k0, i0, k1, i1, total, part.nq, m.k, st, &in_b));
+    {
+      ProfScope ps("merge_topk", st);
+      const int64_t outs = part.nq * m.k;
+      uvb::rank_emit_kernel<<<(unsigned)std::min<int64_t>((outs + 255) / 256, 148 * 16), 256, 0,
+                              st>>>(in_b ? k1 : k0, in_b ? i1 : i0, total, part.nq, m.k, nullptr,
+                                    d_ids + r0 * m.k, d_scores ? d_scores + r0 * m.k : nullptr);
+      UV_CK(cudaGetLastError());
+    }
+  }
+  return UV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream) {
@@ -1462,8 +1815,71 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
   } else {
     UV_TRY(sc.alloc(&d_out_scores, (size_t)nq * k));
   }
-  UV_TRY(merge_launch(nq, n_lists, k_in, k, nullptr, d_in_scores, d_in_ids, d_out_ids,
-                      d_out_scores, st));
+  uvb::MergeParams m;
+  std::memset(&m, 0, sizeof(m));
+  m.nq = nq;
+  m.n_lists = n_lists;
+  m.k_in = k_in;
+  m.k = k;
+  m.in_score = d_in_scores;
+  m.in_id = d_in_ids;
+  UV_TRY(merge_rows(m, d_out_ids, d_out_scores, st, sc));
+  return outs.finish(st);
+}
+
+int uv_topk_pack(int32_t device, const int64_t *ids, const float *scores, int64_t n, void *packed,
+                 void *stream) {
+  if (n < 0) return fail(UV_EINVAL, "negative size");
+  if (n == 0) return UV_OK;
+  if (ids == nullptr || scores == nullptr || packed == nullptr)
+    return fail(UV_EINVAL, "null argument");
+  DeviceGuard g(device);
+  for (const void *ptr : {(const void *)ids, (const void *)scores, (const void *)packed}) {
+    bool on_dev = false;
+    UV_TRY(classify(ptr, device, &on_dev));
+    if (!on_dev) return fail(UV_EINVAL, "uv_topk_pack works on device buffers");
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  ProfScope ps("topk_pack", st);
+  uvb::topk_pack_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+      ids, scores, n, (int32_t *)packed);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
+int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t n_lists,
+                         int32_t k_in, int64_t row_stride, int64_t list_stride, int32_t k,
+                         int64_t *out_ids, float *out_scores, void *stream) {
+  if (packed == nullptr || out_ids == nullptr) return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || n_lists < 1 || k_in < 1 || k < 1 || k > n_lists * k_in || row_stride < 0 ||
+      list_stride < 0)
+    return fail(UV_EINVAL, "bad sizes");
+  if (nq == 0) return UV_OK;
+  DeviceGuard g(device);
+  bool on_dev = false;
+  UV_TRY(classify(packed, device, &on_dev));
+  if (!on_dev) return fail(UV_EINVAL, "uv_topk_merge_packed reads device records");
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  int64_t *d_out_ids = nullptr;
+  float *d_out_scores = nullptr;
+  UV_TRY(outs.stage(out_ids, (size_t)nq * k, device, sc, &d_out_ids));
+  if (out_scores != nullptr) {
+    UV_TRY(outs.stage(out_scores, (size_t)nq * k, device, sc, &d_out_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_out_scores, (size_t)nq * k));
+  }
+  uvb::MergeParams m;
+  std::memset(&m, 0, sizeof(m));
+  m.nq = nq;
+  m.n_lists = n_lists;
+  m.k_in = k_in;
+  m.k = k;
+  m.row_stride = row_stride;
+  m.list_stride = list_stride;
+  m.in_packed = (const int32_t *)packed;
+  UV_TRY(merge_rows(m, d_out_ids, d_out_scores, st, sc));
   return outs.finish(st);
 }
 
@@ -1752,7 +2168,7 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
     int pow2 = 32;
     while (pow2 < (int)splits * k) pow2 <<= 1;
     m.pow2 = pow2;
-    const size_t per_warp = (size_t)pow2 * 16;
+    const size_t per_warp = (size_t)pow2 * 12;  // id + key per entry
     m.warps = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / per_warp));
     m.in_key = part_key;
     m.in_id = part_id;

@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(kRankThreads) rank_merge_kernel(const uint32_t
 }
 
 // Slot i < k of query q: element i of its sorted segment, or an unfilled
-// slot (id -1, score -inf) past n or for a degenerate query.
+// slot (id -1, score -inf) past n, for a degenerate query (degen may be
+// null) or for an empty entry (key 0).
 __global__ void rank_emit_kernel(const uint32_t *key, const int64_t *id, int64_t n, int64_t nq,
                                  int64_t k, const uint32_t *degen, int64_t *out_id,
                                  float *out_score) {
@@ -141,10 +142,44 @@ __global__ void rank_emit_kernel(const uint32_t *key, const int64_t *id, int64_t
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t q = e / k, i = e - q * k;
-    const bool fill = i < n && degen[q] == 0u;
+    const bool fill = i < n && (degen == nullptr || degen[q] == 0u) && key[q * n + i] != 0u;
     out_id[e] = fill ? id[q * n + i] : -1;
     if (out_score != nullptr) out_score[e] = fill ? key32_score(key[q * n + i]) : -INFINITY;
   }
+}
+
+// Row q of a merge (MergeParams layout) as one sort segment of `total`
+// entries: keys[q * total + i], ids[q * total + i]; empty entries (id < 0)
+// get key 0, below every score.
+__global__ void rank_gather_kernel(const MergeParams p, int64_t total, uint32_t *keys,
+                                   int64_t *ids) {
+  const int64_t list_stride = p.list_stride > 0 ? p.list_stride : p.k_in;
+  const int64_t row_stride = p.row_stride > 0 ? p.row_stride : (int64_t)p.n_lists * p.k_in;
+  const int64_t all = p.nq * total;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < all;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = e / total, i = e - q * total;
+    const int64_t l = i / p.k_in, j = i - l * p.k_in;
+    const int64_t src = q * row_stride + l * list_stride + j;
+    int64_t id;
+    uint32_t key;
+    if (p.in_packed) {
+      const int32_t *r = p.in_packed + 3 * src;
+      id = (int64_t)(((uint64_t)(uint32_t)r[1] << 32) | (uint32_t)r[0]);
+      key = score_key32(__int_as_float(r[2]));
+    } else {
+      id = p.in_id[src];
+      key = p.in_key ? p.in_key[src] : score_key32(p.in_score[src]);
+    }
+    keys[e] = id < 0 ? 0u : key;
+    ids[e] = id;
+  }
+}
+
+__global__ void fill_value_kernel(float *out, int64_t n, float v) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x)
+    out[e] = v;
 }
 
 int rank_merge_span() { return kRankThreads * kRankPer; }

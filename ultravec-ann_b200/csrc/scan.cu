@@ -931,71 +931,144 @@ size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k) 
 
 // ---------------------------------------------------------------------------
 // Top-k merge of n_lists sorted lists per query (one warp per query).
-// Elements compare by (score key desc, id asc); empty slots (id -1, key 0)
-// sort last.
+// Elements compare by (score key desc, id asc); empty slots (id < 0) sort
+// last.  The lists are already sorted, so an element's place in the merged
+// order is its index in its own list plus, for every other list, the number
+// of that list's elements that precede it (a binary search; equal elements
+// of lower lists precede) -- a k-way merge with no data-dependent loop.
+// Only the first min(k_in, k) elements of each list can land in the top k.
+// A list that is not sorted by (key, id) -- producers that break exact score
+// ties by record position with ids not increasing in position -- sends its
+// query to a bitonic sort of all entries instead.
 // ---------------------------------------------------------------------------
-struct KeyId {
-  uint32_t key;
-  int64_t id;
-};
-
-__device__ __forceinline__ bool kid_better(const KeyId &a, const KeyId &b) {
-  if (a.id < 0) return false;
-  if (b.id < 0) return true;
-  return a.key > b.key || (a.key == b.key && a.id < b.id);
+__device__ __forceinline__ bool kid_better(uint32_t ka, int64_t ia, uint32_t kb, int64_t ib) {
+  if (ia < 0) return false;
+  if (ib < 0) return true;
+  return ka > kb || (ka == kb && ia < ib);
 }
 
 __global__ void __launch_bounds__(256) merge_topk_kernel(const MergeParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t q = (int64_t)blockIdx.x * p.warps + warp;
-  KeyId *a = (KeyId *)sm + (size_t)warp * p.pow2;
+  int64_t *ids = (int64_t *)sm + (size_t)warp * p.pow2;
+  uint32_t *keys = (uint32_t *)((int64_t *)sm + (size_t)p.warps * p.pow2) + (size_t)warp * p.pow2;
   if (q >= p.nq) return;  // whole warp exits together
   // fixed rows: n_lists lists per query; ragged rows: lists [row_off[q], row_off[q+1])
-  const int64_t first = p.row_off ? p.row_off[q] * p.k_in : q * (int64_t)p.n_lists * p.k_in;
-  const int total = p.row_off ? (int)((p.row_off[q + 1] - p.row_off[q]) * p.k_in)
-                              : p.n_lists * p.k_in;
+  const int64_t list_stride = p.list_stride > 0 ? p.list_stride : p.k_in;
+  const int64_t row_stride = p.row_stride > 0 ? p.row_stride : (int64_t)p.n_lists * p.k_in;
+  const int64_t first = p.row_off ? p.row_off[q] * p.k_in : q * row_stride;
+  const int nl = p.row_off ? (int)(p.row_off[q + 1] - p.row_off[q]) : p.n_lists;
+  const int total = nl * p.k_in;
   const int64_t orow = p.out_row ? (int64_t)p.out_row[q] : q;
-  // ragged rows sort only the next power of two of their own length
-  int n = p.pow2;
-  if (p.row_off) {
-    n = 32;
-    while (n < total) n <<= 1;
-  }
+  int n = 32;
+  while (n < total) n <<= 1;
+  bool unsorted = false;
   for (int i = lane; i < n; i += 32) {
-    KeyId e;
-    e.key = 0u;
-    e.id = -1;
+    uint32_t key = 0u;
+    int64_t id = -1;
     if (i < total) {
-      const int64_t src = first + i;
-      e.id = p.in_id[src];
-      e.key = p.in_key ? p.in_key[src] : 0u;
-      if (p.in_score) e.key = score_key32(p.in_score[src]);
-      if (e.id < 0) e.key = 0u;
+      const int l = i / p.k_in, j = i - l * p.k_in;
+      const int64_t src = p.row_off ? first + i : first + l * list_stride + j;
+      if (p.in_packed) {
+        const int32_t *e = p.in_packed + 3 * src;
+        id = (int64_t)(((uint64_t)(uint32_t)e[1] << 32) | (uint32_t)e[0]);
+        key = score_key32(__int_as_float(e[2]));
+      } else {
+        id = p.in_id[src];
+        key = p.in_key ? p.in_key[src] : 0u;
+        if (p.in_score) key = score_key32(p.in_score[src]);
+      }
+      if (id < 0) key = 0u;
     }
-    a[i] = e;
+    ids[i] = id;
+    keys[i] = key;
   }
   __syncwarp();
+  for (int i = lane; i < total; i += 32) {
+    const int j = i % p.k_in;
+    if (j > 0 && kid_better(keys[i], ids[i], keys[i - 1], ids[i - 1])) unsorted = true;
+  }
+  unsorted = __any_sync(0xffffffffu, unsorted);
+  if (!unsorted) {
+    // k-way merge by ranks: at most k entries of each list are placed
+    const int kk = min(p.k_in, p.k);
+    for (int e = lane; e < nl * kk; e += 32) {
+      const int l = e / kk, j = e - l * kk;
+      const int i = l * p.k_in + j;
+      const int64_t id = ids[i];
+      if (id < 0) continue;
+      const uint32_t key = keys[i];
+      int rank = j;
+      for (int l2 = 0; l2 < nl && rank < p.k; l2++) {
+        if (l2 == l) continue;
+        // elements of list l2 before this one: better, or equal and l2 < l
+        const uint32_t *kl = keys + l2 * p.k_in;
+        const int64_t *il = ids + l2 * p.k_in;
+        int lo = 0, hi = min(p.k_in, p.k);
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          const bool before = kid_better(kl[mid], il[mid], key, id) ||
+                              (l2 < l && il[mid] >= 0 && kl[mid] == key && il[mid] == id);
+          if (before)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        rank += lo;
+      }
+      if (rank < p.k) {
+        p.out_id[orow * p.k + rank] = id;
+        p.out_score[orow * p.k + rank] = key32_score(key);
+      }
+    }
+    // slots past the valid entries stay unfilled
+    int valid = 0;
+    for (int i = lane; i < total; i += 32) valid += ids[i] >= 0 && (i % p.k_in) < p.k ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) valid += __shfl_xor_sync(0xffffffffu, valid, o);
+    for (int i = valid + lane; i < p.k; i += 32) {
+      p.out_id[orow * p.k + i] = -1;
+      p.out_score[orow * p.k + i] = -INFINITY;
+    }
+    return;
+  }
   for (int size = 2; size <= n; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int pi = lane; pi < n / 2; pi += 32) {
         const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
         const int jx = i + stride;
         const bool desc = (i & size) == 0;
-        const KeyId x = a[i], y = a[jx];
-        const bool swap = desc ? kid_better(y, x) : kid_better(x, y);
+        const uint32_t ka = keys[i], kb = keys[jx];
+        const int64_t ia = ids[i], ib = ids[jx];
+        const bool swap = desc ? kid_better(kb, ib, ka, ia) : kid_better(ka, ia, kb, ib);
         if (swap) {
-          a[i] = y;
-          a[jx] = x;
+          keys[i] = kb;
+          keys[jx] = ka;
+          ids[i] = ib;
+          ids[jx] = ia;
         }
       }
       __syncwarp();
     }
   }
   for (int i = lane; i < p.k; i += 32) {
-    const KeyId e = a[i];
-    p.out_id[orow * p.k + i] = e.id;
-    p.out_score[orow * p.k + i] = e.id < 0 ? -INFINITY : key32_score(e.key);
+    const bool ok = i < n && ids[i] >= 0;
+    p.out_id[orow * p.k + i] = ok ? ids[i] : -1;
+    p.out_score[orow * p.k + i] = ok ? key32_score(keys[i]) : -INFINITY;
+  }
+}
+
+// Pack ids and scores into 12-byte records (id low, id high, score bits):
+// one buffer for a single collective of a sharded search's lists.
+__global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,
+                                 int32_t *packed) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t id = (uint64_t)ids[e];
+    packed[3 * e] = (int32_t)(uint32_t)id;
+    packed[3 * e + 1] = (int32_t)(uint32_t)(id >> 32);
+    packed[3 * e + 2] = __float_as_int(scores[e]);
   }
 }
 

@@ -622,6 +622,48 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
   if (threadIdx.x == 0) theta[q] = fkey_inv(prefix);
 }
 
+// A shard's contribution to a threshold shared by several shards: the k
+// largest group lower bounds of each query as a multiset (any order) -- the
+// values above the query's k-th largest (theta, from tc_theta_kernel), then
+// theta repeated up to k (-inf when the query has fewer than k groups).
+// Every value is reached by a distinct record of the shard.
+__global__ void __launch_bounds__(256) tc_bounds_kernel(const float *tmax, int64_t n_groups,
+                                                        int64_t nq, int k, const float *theta,
+                                                        float *bounds) {
+  __shared__ int cnt;
+  const int64_t q = blockIdx.x;
+  if (q >= nq) return;
+  if (threadIdx.x == 0) cnt = 0;
+  __syncthreads();
+  const float th = theta[q];
+  const uint32_t tk = fkey(th);
+  const float *v = tmax + q * n_groups;
+  float *out = bounds + q * (int64_t)k;
+  for (int64_t i = threadIdx.x; i < n_groups; i += 256) {
+    const float x = v[i];
+    if (fkey(x) > tk) {
+      const int pos = atomicAdd(&cnt, 1);
+      if (pos < k) out[pos] = x;
+    }
+  }
+  __syncthreads();
+  for (int i = min(cnt, k) + threadIdx.x; i < k; i += 256) out[i] = th;
+}
+
+// The shards' bounds, gathered shard-major (shards x nq x k), regrouped per
+// query (nq x shards*k) for tc_theta_kernel: the k-th largest of their union
+// is a score at least k distinct records of the whole base reach.
+__global__ void tc_bounds_regroup_kernel(const float *gathered, int shards, int64_t nq, int k,
+                                         float *out) {
+  const int64_t per = nq * (int64_t)k, total = per * shards;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sh = e / per, r = e - sh * per;
+    const int64_t q = r / k, j = r - q * k;
+    out[q * shards * (int64_t)k + sh * k + j] = gathered[e];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Exact scores of the candidates (simd.rs:183-262 association: 16 FMA chains
 // over 16-wide blocks, then the hsum256 tree; trellis.rs:1517 estimator) and

@@ -261,6 +261,10 @@ struct TcRescoreParams {
 struct MergeParams {
   int64_t nq;                // rows to merge
   int n_lists, k_in, k, pow2, warps;
+  // fixed rows: list l of row q starts at entry q * row_stride + l * list_stride
+  // (0, 0: rows of n_lists * k_in contiguous entries)
+  int64_t row_stride, list_stride;
+  const int32_t *in_packed;  // or null: 3 x int32 per entry (id low, id high, score bits)
   const int64_t *row_off;    // or null: row q merges lists [row_off[q], row_off[q+1])
   const int32_t *out_row;    // or null: row q writes output row out_row[q]
   const uint32_t *in_key;  // or null
@@ -278,6 +282,8 @@ const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k);
 size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k);
 constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
+__global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,
+                                 int32_t *packed);
 
 // tcscan.cu
 // shape 1: the queries (A) in shared memory; 3: A in TMEM (the default)
@@ -304,6 +310,10 @@ __global__ void tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_
 constexpr int kThetaSmemKeys = 12288;
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
                                 float *theta);
+__global__ void tc_bounds_kernel(const float *tmax, int64_t n_groups, int64_t nq, int k,
+                                 const float *theta, float *bounds);
+__global__ void tc_bounds_regroup_kernel(const float *gathered, int shards, int64_t nq, int k,
+                                         float *out);
 // bits 1..4; per_thread: one thread per candidate (long lists), else half a
 // warp per candidate (short lists)
 const void *tc_rescore_kernel_ptr(int bits, bool per_thread);
@@ -421,6 +431,9 @@ __global__ void rank_merge_kernel(const uint32_t *ik, const int64_t *ii, uint32_
 __global__ void rank_emit_kernel(const uint32_t *key, const int64_t *id, int64_t n, int64_t nq,
                                  int64_t k, const uint32_t *degen, int64_t *out_id,
                                  float *out_score);
+__global__ void rank_gather_kernel(const MergeParams p, int64_t total, uint32_t *keys,
+                                   int64_t *ids);
+__global__ void fill_value_kernel(float *out, int64_t n, float v);
 int rank_merge_span();
 
 size_t scan_smem_bytes(int dim, int img_words, int table_len, bool table_in_smem);

@@ -5,8 +5,9 @@ encodes and scans its own range (records keep their global row ids).  IVF
 index: the posting lists are dealt to ranks so that each rank holds about the
 same number of record bytes; every rank keeps all centroids, probes
 redundantly, and scans only the probed lists it owns, so each probed list is
-scanned exactly once.  Either way the per-rank top-k lists are combined by
-one all-gather and a merge.  The merge is a function argument so that the
+scanned exactly once.  The flat search exchanges first-pass bounds between
+the shards before they keep candidates (sharded_search); the IVF lists are
+combined by one all-gather and a merge (gather_topk).  The merge is a function argument so that the
 same sequence runs with the device merge (`uv_topk_merge`) under NCCL and
 with a host merge under gloo.
 """
@@ -70,6 +71,107 @@ def gather_topk(local_ids, local_scores, k: int, dist, merge):
     g_ids = g_ids.view(world, nq, kin).permute(1, 0, 2).contiguous()
     g_sc = g_sc.view(world, nq, kin).permute(1, 0, 2).contiguous()
     return merge(g_ids, g_sc, k)
+
+
+def query_slice(nq: int, rank: int, world: int) -> tuple[int, int]:
+    """Queries [lo, hi) whose merge `rank` does: contiguous slices."""
+    return rank * nq // world, (rank + 1) * nq // world
+
+
+def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
+    """The flat search of a base split across ranks (one index shard each,
+    global ids), as uv_index_search_begin / set_bounds / finish plus the
+    merge describe it:
+
+    1. `begin(world)` starts the shard's search and exposes its (nq, k)
+       first-pass lower bounds; one all-gather makes them (world * nq, k),
+       shard-major, on every rank, and every shard takes the k-th largest of
+       their union as its threshold (`set_bounds`).
+    2. `finish()` gives the shard's lists: only records that can be in the
+       global top k survive the shared threshold.
+    3. The lists travel once, packed (ids and scores in one 12-byte record,
+       `pack`): an all-to-all hands rank r every shard's lists for its query
+       slice, rank r merges its slice over the shards (`merge_packed` with
+       row stride k and list stride rows * k), and one all-gather of the
+       merged, packed slices (padded to the largest slice) gives every rank
+       the (nq, k) answer.
+
+    Every rank takes the same collective steps in the same order.  `pack`,
+    `unpack` and `merge_packed` are the device routines under NCCL and host
+    stand-ins under gloo."""
+    import torch
+
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    s = begin(world)
+    try:
+        bounds = s.bounds
+        nq = bounds.shape[0]
+        gathered = torch.empty((world * nq, k), dtype=bounds.dtype, device=bounds.device)
+        dist.all_gather_into_tensor(gathered, bounds.contiguous())
+        s.set_bounds(gathered, world)
+        ids, scores = s.finish()
+    finally:
+        s.close()
+    packed = pack(ids, scores).reshape(-1)
+    lo, hi = query_slice(nq, rank, world)
+    rows = hi - lo
+    in_splits = [(query_slice(nq, r, world)[1] - query_slice(nq, r, world)[0]) * k * 3
+                 for r in range(world)]
+    recv = torch.empty(world * rows * k * 3, dtype=packed.dtype, device=packed.device)
+    dist.all_to_all_single(recv, packed, [rows * k * 3] * world, in_splits)
+    m_ids, m_sc = merge_packed(recv, rows, world, k, k, k, rows * k)
+    rows_max = (nq + world - 1) // world
+    mine = torch.zeros((rows_max, k, 3), dtype=packed.dtype, device=packed.device)
+    if rows > 0:
+        mine[:rows] = pack(m_ids, m_sc).reshape(rows, k, 3)
+    allp = torch.empty((world * rows_max, k, 3), dtype=packed.dtype, device=packed.device)
+    dist.all_gather_into_tensor(allp, mine)
+    allp = allp.view(world, rows_max, k, 3)
+    parts = [allp[r, :query_slice(nq, r, world)[1] - query_slice(nq, r, world)[0]]
+             for r in range(world)]
+    return unpack(torch.cat(parts, 0))
+
+
+def pack_host(ids, scores):
+    """Host stand-in of uv_topk_pack: (nq, k) -> (nq, k, 3) int32."""
+    import numpy as np
+    import torch
+
+    i = np.ascontiguousarray(ids.cpu().numpy() if hasattr(ids, "cpu") else ids, np.int64)
+    s = np.ascontiguousarray(scores.cpu().numpy() if hasattr(scores, "cpu") else scores,
+                             np.float32)
+    out = np.empty(i.shape + (3,), np.int32)
+    out[..., 0] = (i & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+    out[..., 1] = (i >> 32).astype(np.int64).astype(np.int32)
+    out[..., 2] = s.view(np.int32)
+    return torch.from_numpy(out)
+
+
+def unpack_host(packed):
+    """Host stand-in of the unpack: (..., 3) int32 -> ids, scores."""
+    import torch
+
+    lo = packed[..., 0].to(torch.int64) & 0xFFFFFFFF
+    hi = packed[..., 1].to(torch.int64)
+    return (hi << 32) | lo, packed[..., 2].contiguous().view(torch.float32)
+
+
+def merge_packed_host(recv, rows: int, n_lists: int, k_in: int, k: int, row_stride: int,
+                      list_stride: int):
+    """Host stand-in of uv_topk_merge_packed with strides."""
+    import numpy as np
+    import torch
+
+    p = recv.cpu().numpy().reshape(-1, 3)
+    ids = np.empty((rows, n_lists, k_in), np.int64)
+    sc = np.empty((rows, n_lists, k_in), np.float32)
+    for q in range(rows):
+        for l in range(n_lists):
+            r = p[q * row_stride + l * list_stride:][:k_in]
+            ids[q, l] = (r[:, 0].astype(np.int64) & 0xFFFFFFFF) | (r[:, 1].astype(np.int64) << 32)
+            sc[q, l] = r[:, 2].view(np.float32)
+    return merge_host(torch.from_numpy(ids), torch.from_numpy(sc), k)
 
 
 def merge_host(ids, scores, k: int):
