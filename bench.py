@@ -13,8 +13,10 @@ One step = one pass of both hot paths over the resident inputs:
 `value` is queries/s of the scan phase; `encode.value` is rows/s of the
 encode phase; `ms_per_step` covers both.  With N GPUs the base is sharded in
 contiguous row ranges (strong scaling: same 1M x 10k job), every rank scans
-its shard for all queries, and the per-rank top-k lists meet in one NCCL
-all-gather plus a device merge.
+its shard for all queries; the ranks share one threshold from their
+first-pass bounds (one NCCL all-gather), exchange their packed lists by
+query slice (all-to-all), merge a slice each on the device and all-gather
+the merged slices.
 
 `--impl reference` times the CPU restatement of the reference algorithm
 (oracle/, OpenMP over queries, all host threads) on a bounded sample of the
@@ -192,7 +194,7 @@ METRIC = "flat codes-only MIPS queries/s and encode vectors/s at 1/2/4/8 B200; %
 
 # kernel families of one step (uv_profile_read names)
 SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
-                 "tc_theta", "tc_pass2", "tc_rescore")
+                 "tc_theta", "tc_pass2", "tc_rescore", "topk_pack")
 
 
 def config_dict(args):
@@ -245,17 +247,22 @@ def main():
     index = uv.Index(codec)
     index.reserve(hi - lo)
 
+    import ultravec_ann_b200.shard as shardlib
+
+    def sharded(qs, k):
+        # the flat multi-GPU protocol: first-pass bounds all-gathered into one
+        # shared threshold, packed lists, all-to-all of query slices, per-slice
+        # k-way merge, all-gather of the merged slices
+        return shardlib.sharded_search(
+            lambda n: index.search_begin(qs, k, mips=True, n_shards=n), k, dist,
+            lambda i, sc: uv.topk_pack(i, sc, device=local), uv.topk_unpack,
+            lambda recv, rows, nl, kin, kk, rs, ls: uv.topk_merge_packed(
+                recv, rows, nl, kin, kk, rs, ls, device=local))
+
     def scan(k):
-        out_ids, out_scores = index.search(queries, k, mips=True)
-        if world > 1:
-            g_ids = torch.empty((world,) + tuple(out_ids.shape), dtype=torch.int64, device=dev)
-            g_sc = torch.empty((world,) + tuple(out_scores.shape), dtype=torch.float32, device=dev)
-            dist.all_gather_into_tensor(g_ids, out_ids)
-            dist.all_gather_into_tensor(g_sc, out_scores)
-            out_ids, out_scores = uv.topk_merge(g_ids.permute(1, 0, 2).contiguous(),
-                                                g_sc.permute(1, 0, 2).contiguous(), k,
-                                                device=local)
-        return out_ids, out_scores
+        if world == 1:
+            return index.search(queries, k, mips=True)
+        return sharded(queries, k)
 
     def step(ev=None):
         index.clear()
@@ -264,9 +271,16 @@ def main():
         index.add(ids, shard)
         if ev:
             ev[1].record()
-        res = scan(K_MAIN)
+        if world > 1:
+            # the index is built on every rank before any rank searches it:
+            # each phase is timed from a common start, so neither carries the
+            # ranks' launch skew
+            barrier()
         if ev:
             ev[2].record()
+        res = scan(K_MAIN)
+        if ev:
+            ev[3].record()
         return res
 
     def barrier():
@@ -289,11 +303,11 @@ def main():
     for _ in range(args.steps):
         flush.fill_(1)
         barrier()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         last = step(ev)
         torch.cuda.synchronize()
         enc_ms.append(ev[0].elapsed_time(ev[1]))
-        scan_ms.append(ev[1].elapsed_time(ev[2]))
+        scan_ms.append(ev[2].elapsed_time(ev[3]))
     barrier()
     kern = {name: uv.profile_read(name) for name in SCAN_FAMILIES}
     launches_total = uv.profile_read("*")[1]
@@ -337,16 +351,7 @@ def main():
             if world == 1:
                 h_ids, h_sc = index.search(q_host, K_MAIN, mips=True)
             else:
-                out_ids, out_scores = index.search(q_host.to(dev, non_blocking=True), K_MAIN,
-                                                   mips=True)
-                g_ids = torch.empty((world,) + tuple(out_ids.shape), dtype=torch.int64, device=dev)
-                g_sc = torch.empty((world,) + tuple(out_scores.shape), dtype=torch.float32,
-                                   device=dev)
-                dist.all_gather_into_tensor(g_ids, out_ids)
-                dist.all_gather_into_tensor(g_sc, out_scores)
-                out_ids, out_scores = uv.topk_merge(g_ids.permute(1, 0, 2).contiguous(),
-                                                    g_sc.permute(1, 0, 2).contiguous(), K_MAIN,
-                                                    device=local)
+                out_ids, out_scores = sharded(q_host.to(dev, non_blocking=True), K_MAIN)
                 h_ids, h_sc = out_ids.cpu(), out_scores.cpu()
             t1.record()
             torch.cuda.synchronize()
@@ -361,7 +366,8 @@ def main():
         e2e = {"value": nq * len(e_ms) / (et.item() / 1e3), "unit": "queries/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "api": "uv_index_search with host buffers" if world == 1 else
-                      "uv_index_search + NCCL all-gather + uv_topk_merge, host copies"}
+                      "uv_index_search_begin / set_bounds / finish + NCCL all-gather, "
+                      "all-to-all and uv_topk_merge_packed, host copies"}
 
     # CPU baseline: the oracle on a bounded sample, rank 0 at N=1
     cpu = parity = None

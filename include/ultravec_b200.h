@@ -277,6 +277,9 @@ int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t
  * kept point (0 automatic: every book point scored for books of <= 8192
  * points, the reference's bisection + ball search where the minimum is tied
  * and for three bits; 1 the reference's search everywhere);
+ * "rescore_warp" 1 makes the prefilter's exact rescoring use one CTA per
+ * query throughout (0 automatic: one warp per query whose candidate list is
+ * short, at widths up to 256 with tables of up to 1024 entries);
  * "cand_kernel" selects the
  * candidate scorer's kernel (0 automatic:
  * one thread per candidate at bits 1, 2, 4; 1 half a warp per candidate).

@@ -41,9 +41,13 @@ def same(a, b):
         np.asarray(a[1], np.float32).view(np.uint32), np.asarray(b[1], np.float32).view(np.uint32))
 
 
+@pytest.mark.parametrize("rescore", [0, 1], ids=["warp_rescore", "cta_rescore"])
 @pytest.mark.parametrize("mips", [True, False])
 @pytest.mark.parametrize("k", [10, 100])
-def test_matches_oracle(oracle, uv, tc_mode, mips, k):
+def test_matches_oracle(oracle, uv, tc_mode, mips, k, rescore):
+    """Both rescoring kernels: one warp per short candidate list (default)
+    and one CTA per query everywhere (tuning key rescore_warp = 1)."""
+    uv.set_tuning("rescore_warp", rescore)
     n, nq, dim = 70_000, 48, 128
     base = rand_rows(n, dim, 5) * np.float32(2.5)
     base[::7] *= np.float32(0.1)  # spread the norms (MIPS)
@@ -55,7 +59,10 @@ def test_matches_oracle(oracle, uv, tc_mode, mips, k):
     index = uv.Index(codec)
     index.add_batch(base)
     tc_mode(2)
-    got = index.search(queries, k, mips=mips)
+    try:
+        got = index.search(queries, k, mips=mips)
+    finally:
+        uv.set_tuning("rescore_warp", 0)
     assert np.array_equal(got[0], want[0])
     assert np.array_equal(got[1].view(np.uint32), want[1].view(np.uint32))
 

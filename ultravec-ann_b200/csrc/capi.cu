@@ -26,6 +26,7 @@ std::atomic<int> g_coset_nearest{0};
 std::atomic<int> g_tc_sample{0};
 std::atomic<int> g_tc_prepare{0};
 std::atomic<int> g_ivf_tc_probe{0};
+std::atomic<int> g_rescore_warp{0};
 std::atomic<int64_t> g_tc_last_candidates{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 std::atomic<bool> g_prof_on{false};
@@ -1377,6 +1378,18 @@ int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint3
                          (rp.table_in_smem ? (size_t)c->table_len * 4 : 0) +
                          (size_t)16 * (c->code_stride / 4 + 1) * 4;
     if (rsmem > 227 * 1024) return fail(UV_EUNSUPPORTED, "prefilter rescoring exceeds shared memory");
+    // queries with short lists first, one warp each; the rest one CTA each
+    const size_t wsmem = uvb::tc_rescore_warp_smem_bytes(c->table_len, regions);
+    const void *wk = uvb::tc_rescore_warp_kernel_ptr(c->cfg.bits);
+    if (g_rescore_warp.load() == 0 && wk != nullptr && d <= uvb::kRescoreWarpDim &&
+        c->table_len <= 1024 && wsmem <= 227 * 1024) {
+      UV_CK(cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
+      void *wargs[] = {&rp};
+      ProfScope ps("tc_rescore", st);
+      UV_CK(cudaLaunchKernel(wk, dim3((unsigned)((nq + uvb::kRescoreWarps - 1) / uvb::kRescoreWarps)),
+                             dim3(32 * uvb::kRescoreWarps), wargs, wsmem, st));
+      rp.warp_cap = uvb::kRescoreWarpCap;
+    }
     // long candidate lists (about k*S per query) score one candidate per
     // thread; short ones half a warp per candidate
     const void *rk = uvb::tc_rescore_kernel_ptr(c->cfg.bits, per_thread);
@@ -1928,6 +1941,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "cand_kernel") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "cand_kernel must be 0 or 1");
     g_cand_kernel = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "rescore_warp") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "rescore_warp must be 0 or 1");
+    g_rescore_warp = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "scan_splits") == 0) {

@@ -164,6 +164,7 @@ extern std::atomic<int> g_coset_nearest;    // uv_set_tuning("coset_nearest")
 extern std::atomic<int> g_tc_sample;        // uv_set_tuning("tc_sample")
 extern std::atomic<int> g_tc_prepare;       // uv_set_tuning("tc_prepare")
 extern std::atomic<int> g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
+extern std::atomic<int> g_rescore_warp;     // uv_set_tuning("rescore_warp")
 extern std::atomic<bool> g_prof_on;
 extern std::vector<ProfRec> g_prof;
 

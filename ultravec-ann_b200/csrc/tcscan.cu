@@ -719,6 +719,7 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   }
   __syncthreads();
   const int cnt_raw = roff[p.regions];
+  if (p.warp_cap > 0 && cnt_raw >= 0 && cnt_raw <= p.warp_cap) return;  // scored per warp
   if (cnt_raw < 0) {
     if (tid == 0) p.over_list[atomicAdd(p.n_over, 1)] = (int32_t)q;
     return;
@@ -830,6 +831,135 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
     p.out_id[q * p.k + i] = full ? (p.ids ? p.ids[rec] : rec) : -1;
     p.out_score[q * p.k + i] = full ? key32_score((uint32_t)(key >> 32)) : -INFINITY;
   }
+}
+
+// The same exact rescoring, one warp per query, for queries whose candidate
+// list holds at most kRescoreWarpCap entries and no full segment (the others
+// are left to tc_rescore_kernel, launched after this one with warp_cap set).
+// Many short lists are the multi-GPU case, where a shared threshold leaves
+// each shard a few dozen candidates per query: a CTA per query would spend
+// most of its time on set-up and block-wide barriers.  The code table sits
+// in kRescoreCopies interleaved copies (entry w of copy c at w * copies + c,
+// lane l reading copy l % copies), so the candidates' random lookups rarely
+// meet in one bank.
+template <int BITS>
+__global__ void __launch_bounds__(32 * kRescoreWarps, 1) tc_rescore_warp_kernel(
+    const TcRescoreParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int CAP = kRescoreWarpCap, NC = kRescoreCopies;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float *table = (float *)sm;
+  const size_t roff_words = ((size_t)p.regions + 4) & ~(size_t)3;
+  const size_t per_warp = (size_t)CAP * 12 + (size_t)kRescoreWarpDim * 4 + roff_words * 4;
+  uint8_t *wb = sm + (size_t)p.table_len * NC * 4 + (size_t)warp * per_warp;
+  uint64_t *keys = (uint64_t *)wb;
+  uint32_t *cidx = (uint32_t *)(keys + CAP);
+  float *qv = (float *)(cidx + CAP);
+  int *roff = (int *)(qv + kRescoreWarpDim);
+  for (int e = tid; e < p.table_len * NC; e += 32 * kRescoreWarps)
+    table[e] = __ldg(p.code + e / NC);
+  __syncthreads();
+  const int64_t q = (int64_t)blockIdx.x * kRescoreWarps + warp;
+  if (q >= p.nq) return;  // whole warps leave, after the only block barrier
+  // segment counts and offsets (as tc_rescore_kernel's warp 0)
+  const int per = (p.regions + 31) >> 5;  // <= 8
+  int c_loc[8];
+  int tot = 0;
+  bool over = false;
+#pragma unroll
+  for (int t = 0; t < 8; t++) {
+    const int r = lane * per + t;
+    int c = (t < per && r < p.regions) ? p.cand_cnt[q * p.regions + r] : 0;
+    over |= c > p.region_cap;
+    c = min(c, p.region_cap);
+    c_loc[t] = c;
+    tot += c;
+  }
+  int incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  int ex = incl - tot;
+#pragma unroll
+  for (int t = 0; t < 8; t++) {
+    const int r = lane * per + t;
+    if (t < per && r < p.regions) roff[r] = ex;
+    ex += c_loc[t];
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (__any_sync(0xffffffffu, over) || total > CAP) return;  // left to tc_rescore_kernel
+  __syncwarp();
+  for (int i = lane; i < total; i += 32) {
+    int lo = 0, hi = p.regions - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (roff[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    cidx[i] = p.cand[q * p.cand_stride + (int64_t)lo * p.region_cap + (i - roff[lo])];
+  }
+  const int cnt = p.degenerate[q] ? 0 : total;
+  if (lane == 0) atomicAdd(p.n_cand, (unsigned long long)cnt);
+  int pow2 = 32;
+  while (pow2 < cnt) pow2 <<= 1;
+  for (int i = lane; i < p.dim; i += 32) qv[i] = p.q_r[q * (int64_t)p.q_stride + i];
+  for (int i = lane; i < pow2; i += 32) keys[i] = kEmptyKey;
+  __syncwarp();
+  for (int i = lane; i < cnt; i += 32) {
+    const int64_t rec = (int64_t)cidx[i];
+    const uint8_t *rc = p.codes + rec * (int64_t)p.code_stride;
+    const uint32_t st = __ldg(p.start + rec);
+    const float rs = __ldg(p.rescale + rec);
+    const float rn = p.rnorm ? __ldg(p.rnorm + rec) : 1.0f;
+    const float acc =
+        record_dot_thread<BITS>(qv, rc, st, p.dim, p.mem, p.code_stride, table, NC, lane % NC);
+    float sx = fadd(0.0f, fmul(rn, fdiv(acc, rs)));
+    if (p.mips) sx = fmul(sx, __ldg(p.norms + rec));
+    keys[i] = rank_key(sx, (uint32_t)rec);
+  }
+  __syncwarp();
+  // bitonic sort of the warp's keys, descending
+  for (int size = 2; size <= pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int pi = lane; pi < pow2 / 2; pi += 32) {
+        const int lo = 2 * pi - (pi & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t x = keys[lo], y = keys[hi];
+        if ((x < y) == desc) {
+          keys[lo] = y;
+          keys[hi] = x;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  for (int i = lane; i < p.k; i += 32) {
+    const uint64_t key = i < pow2 ? keys[i] : kEmptyKey;
+    const bool full = key != kEmptyKey;
+    const int64_t rec = rank_key_index(key);
+    p.out_id[q * p.k + i] = full ? (p.ids ? p.ids[rec] : rec) : -1;
+    p.out_score[q * p.k + i] = full ? key32_score((uint32_t)(key >> 32)) : -INFINITY;
+  }
+}
+
+const void *tc_rescore_warp_kernel_ptr(int bits) {
+  switch (bits) {
+    case 1: return (const void *)tc_rescore_warp_kernel<1>;
+    case 2: return (const void *)tc_rescore_warp_kernel<2>;
+    case 3: return (const void *)tc_rescore_warp_kernel<3>;
+    case 4: return (const void *)tc_rescore_warp_kernel<4>;
+  }
+  return nullptr;
+}
+
+size_t tc_rescore_warp_smem_bytes(int table_len, int regions) {
+  const size_t roff_words = ((size_t)regions + 4) & ~(size_t)3;
+  const size_t per_warp = (size_t)kRescoreWarpCap * 12 + (size_t)kRescoreWarpDim * 4 +
+                          roff_words * 4;
+  return (size_t)table_len * kRescoreCopies * 4 + per_warp * kRescoreWarps;
 }
 
 size_t tc_scan_smem_bytes(int shape) {

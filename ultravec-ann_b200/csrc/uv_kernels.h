@@ -256,6 +256,8 @@ struct TcRescoreParams {
   int32_t *over_list;
   int *n_over;
   unsigned long long *n_cand;  // total candidates scored (statistics)
+  int warp_cap;                // > 0: queries with at most this many candidates (and no
+                               // full segment) were scored by tc_rescore_warp_kernel
 };
 
 struct MergeParams {
@@ -317,6 +319,16 @@ __global__ void tc_bounds_regroup_kernel(const float *gathered, int shards, int6
 // bits 1..4; per_thread: one thread per candidate (long lists), else half a
 // warp per candidate (short lists)
 const void *tc_rescore_kernel_ptr(int bits, bool per_thread);
+// One warp per query for short candidate lists: kRescoreWarps queries per CTA
+// of 32 * kRescoreWarps threads, up to kRescoreWarpCap candidates each, rows
+// up to kRescoreWarpDim wide, the code table (up to 1024 entries) in
+// kRescoreCopies bank-interleaved copies.
+constexpr int kRescoreWarps = 16;
+constexpr int kRescoreWarpCap = 512;
+constexpr int kRescoreWarpDim = 256;
+constexpr int kRescoreCopies = 16;
+const void *tc_rescore_warp_kernel_ptr(int bits);
+size_t tc_rescore_warp_smem_bytes(int table_len, int regions);
 // tcwide.cu: the prefilter for rows of any width (K streamed in chunks of 64)
 const void *tc_wide_kernel_ptr(int mode);
 size_t tc_wide_smem_bytes();
