@@ -258,7 +258,11 @@ int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t
  * on it): "scan_splits" fixes the number of record ranges each query tile is
  * split into (0 = automatic); "encode_back" places the encoder's
  * back-pointers for codecs created afterwards (0 automatic, 1 global scratch,
- * 2 shared memory whenever one row's array fits); "tc_scan" selects the flat
+ * 2 shared memory whenever one row's array fits); "encode_staged" 1 makes
+ * codecs created afterwards encode every window wider than 14 bits with the
+ * staged encoder (batches of rows, one launch per trellis step) instead of
+ * one thread-block cluster per row (0 automatic: clusters up to 18 bits at
+ * 1 and 2 bits per coordinate); "tc_scan" selects the flat
  * search's tensor-core prefilter (0 automatic, 1 never, 2 wherever it is
  * built); "tc_shape" where the prefilter keeps its queries (0 automatic =
  * 3: tensor memory; 1: shared memory); "tc_cache" keeps the prefilter's

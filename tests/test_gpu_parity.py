@@ -80,6 +80,46 @@ def test_encode_wide_rows_bit_exact(uv, oracle, dim, bits):
 
 
 @pytest.mark.parametrize("dim,bits,mem,n,kw", [
+    (128, 3, 12, 40, {}),                       # window 15 at 3 bits: staged
+    (128, 4, 12, 24, {}),                       # window 16 at 4 bits: staged
+    (64, 3, 14, 16, {}),                        # window 17
+    (64, 4, 14, 12, {}),                        # window 18
+    (32, 3, 16, 6, {}),                         # window 19: the 3-bit M = 16 cell
+    (32, 4, 16, 4, {}),                         # window 20: the 4-bit M = 16 cell
+    (64, 3, 13, 16, {"branch_lambda": 0.5, "start_bits": 9}),
+    (64, 2, 1, 200, {}),                        # mem < bits: the general pass
+    (64, 3, 1, 200, {}),
+    (64, 4, 2, 200, {"branch_lambda": 0.5}),
+    (96, 4, 3, 200, {"start_bits": 2}),
+])
+def test_encode_staged_bit_exact(uv, oracle, dim, bits, mem, n, kw):
+    """The shapes the resident encoders do not hold (encode_staged.cu):
+    windows of 15 and more bits at 3 and 4 bits per coordinate, and the
+    reference's general Viterbi pass for mem < bits (src/trellis.rs:1348-1387)."""
+    rows = oracle.rand_unit(n, dim, 700 + mem * 7 + bits)
+    _, _, got, want = _encode_both(uv, oracle, dim, bits, mem, rows, **kw)
+    _assert_records(got, want)
+
+
+def test_encode_staged_centered_raw_rows_and_search(uv, oracle):
+    """Centering, non-unit rows and a search over staged records (a 2^15
+    entry code table, read through L1 by the scan kernels)."""
+    rows = rand_rows(600, 128, 41) * np.float32(5.0)
+    cen = oracle.kmeans(rows, 3, 42)
+    _, _, got, want = _encode_both(uv, oracle, 128, 3, 12, rows, centroids=cen)
+    _assert_records(got, want, cidx=True)
+    qs = rand_rows(20, 128, 42)
+    g, ix = _index(uv, 128, 3, 12, rows)
+    o = oracle.Codec(128, 3, 12)
+    enc = o.encode_batch(rows)
+    for k in (10, 100, 600):
+        ids, scores = ix.search(qs, k, mips=True)
+        wids, wscores = o.search_topk(enc, qs, k, norms=oracle.l2_norms(rows))
+        np.testing.assert_array_equal(ids, wids)
+        np.testing.assert_array_equal(_bits(scores), _bits(wscores))
+
+
+@pytest.mark.parametrize("dim,bits,mem,n,kw", [
     (128, 2, 13, 48, {}),                       # 2 CTAs per row
     (128, 2, 14, 40, {"branch_lambda": 0.5}),   # 4 CTAs, anisotropic metric
     (64, 1, 14, 40, {"start_bits": 9}),         # 2 CTAs, restricted free start

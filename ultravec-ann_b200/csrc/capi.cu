@@ -227,6 +227,18 @@ int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *
   p.row_index = row_index;
   p.signs = signs;
   p.sign_stride = c->sign_stride;
+  if (c->plan.staged > 0) {
+    // batches of rows stepped through the trellis together
+    const int64_t R = uvb::staged_rows_per_batch(c->plan, c->cfg.dim, n);
+    size_t offs[6];
+    const size_t bytes = uvb::staged_scratch_bytes(c->plan, c->cfg.dim, R, offs);
+    uint8_t *scratch = nullptr;
+    UV_TRY(sc.alloc(&scratch, bytes));
+    ProfScope ps("encode", st);
+    for (int64_t row0 = 0; row0 < n; row0 += R)
+      UV_CK(uvb::encode_staged_launch(c->plan, p, row0, std::min(R, n - row0), scratch, offs, st));
+    return UV_OK;
+  }
   int grid = 0;
   UV_CK(uvb::encode_grid(c->plan, n, &grid));
   if (!c->plan.back_smem) {
@@ -1941,6 +1953,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "cand_kernel") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "cand_kernel must be 0 or 1");
     g_cand_kernel = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "encode_staged") == 0) {
+    if (value < 0 || value > 1) return fail(UV_EINVAL, "encode_staged must be 0 or 1");
+    uvb::g_encode_staged = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "rescore_warp") == 0) {

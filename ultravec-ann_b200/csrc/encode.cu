@@ -299,6 +299,7 @@ const void *pick_kernel(int B, int WPT, bool smem_back) {
 
 }  // namespace
 
+std::atomic<int> g_encode_staged{0};  // uv_set_tuning("encode_staged")
 std::atomic<int> g_encode_back_mode{0};  // uv_set_tuning("encode_back"): 0 auto, 1 global, 2 shared
 
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) {
@@ -306,14 +307,19 @@ int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why) 
     *why = "bits must be 1..4";
     return 1;
   }
-  if (mem < bits) {
-    *why = "mem < bits takes the reference's general Viterbi pass, not built for the GPU";
-    return 2;
-  }
+  // mem < bits: the reference's general pass (encode_staged.cu)
+  if (mem < bits) return staged_plan(dim, bits, mem, plan, why);
   const int64_t nw = (int64_t)1 << (mem + bits);
   const int wpt = nw >= 32 ? 32 : (int)nw;
   const int64_t T = nw / wpt;
-  if (T > 512) return encode_cluster_plan(dim, bits, mem, plan, why);
+  if (T > 512) {
+    // one cluster per row where it is built, else batches of rows stepped
+    // through the trellis (encode_staged.cu)
+    if (g_encode_staged.load() == 1) return staged_plan(dim, bits, mem, plan, why);
+    const int rc = encode_cluster_plan(dim, bits, mem, plan, why);
+    if (rc != 2) return rc;
+    return staged_plan(dim, bits, mem, plan, why);
+  }
   const int spt = wpt >> bits;
   const int bps = spt * bits;
   const int spw = 32 / bps;

@@ -843,7 +843,7 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
 // lane l reading copy l % copies), so the candidates' random lookups rarely
 // meet in one bank.
 template <int BITS>
-__global__ void __launch_bounds__(32 * kRescoreWarps, 1) tc_rescore_warp_kernel(
+__global__ void __launch_bounds__(32 * kRescoreWarps, 2) tc_rescore_warp_kernel(
     const TcRescoreParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int CAP = kRescoreWarpCap, NC = kRescoreCopies;

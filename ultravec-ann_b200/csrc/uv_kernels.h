@@ -42,6 +42,8 @@ struct EncodeParams {
 struct EncodePlan {
   int B, WPT, T, n_states, dim_pad, teams_per_cta, threads, team_smem_words;
   int cluster = 0;           // > 0: one cluster of this many CTAs per row (encode_cluster.cu)
+  int staged = 0;            // > 0: batches of rows one step per launch (encode_staged.cu);
+                             // 2: the general pass for mem < bits
   bool back_smem;
   int64_t back_words_team;
   size_t smem_bytes;
@@ -49,6 +51,7 @@ struct EncodePlan {
 };
 
 extern std::atomic<int> g_encode_back_mode;  // placement of back-pointers; never changes results
+extern std::atomic<int> g_encode_staged;     // 1: the staged encoder for every window above 14 bits
 
 // 0 ok, 1 invalid, 2 unsupported (message in *why)
 int encode_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
@@ -59,6 +62,13 @@ int encode_cluster_plan(int dim, int bits, int mem, EncodePlan *plan, std::strin
 cudaError_t encode_cluster_grid(const EncodePlan &plan, int64_t n, int *grid);
 cudaError_t encode_cluster_launch(const EncodePlan &plan, EncodeParams p, int grid,
                                   cudaStream_t st);
+// encode_staged.cu: every other shape (mem + bits >= 15 at 3 and 4 bits, mem
+// + bits above 18, mem < bits), a batch of rows per call, one launch per step
+int staged_plan(int dim, int bits, int mem, EncodePlan *plan, std::string *why);
+int64_t staged_rows_per_batch(const EncodePlan &plan, int dim, int64_t n);
+size_t staged_scratch_bytes(const EncodePlan &plan, int dim, int64_t R, size_t *offs);
+cudaError_t encode_staged_launch(const EncodePlan &plan, EncodeParams p, int64_t row0, int64_t R,
+                                 uint8_t *scratch, const size_t *offs, cudaStream_t st);
 
 struct PrepParams {
   int dim, dim_pad;
@@ -324,9 +334,9 @@ const void *tc_rescore_kernel_ptr(int bits, bool per_thread);
 // up to kRescoreWarpDim wide, the code table (up to 1024 entries) in
 // kRescoreCopies bank-interleaved copies.
 constexpr int kRescoreWarps = 16;
-constexpr int kRescoreWarpCap = 512;
+constexpr int kRescoreWarpCap = 128;
 constexpr int kRescoreWarpDim = 256;
-constexpr int kRescoreCopies = 16;
+constexpr int kRescoreCopies = 8;
 const void *tc_rescore_warp_kernel_ptr(int bits);
 size_t tc_rescore_warp_smem_bytes(int table_len, int regions);
 // tcwide.cu: the prefilter for rows of any width (K streamed in chunks of 64)
