@@ -649,67 +649,9 @@ def run_secondary(args):
         print(json.dumps(line), flush=True)
 
     if args.workload == "wide":
-        n, nq, d, d_pad = 1_000_000, 1000, 960, 1024
-        x = np.zeros((n + nq, d_pad), np.float32)
-        for a in range(0, n + nq, 100_000):
-            b = min(a + 100_000, n + nq)
-            x[a:b, :d] = rng.random((b - a, d), dtype=np.float32) + \
-                np.float32(0.5) * (np.arange(d, dtype=np.float32) / np.float32(959))
-        base = torch.from_numpy(x[:n]).to(dev)
-        qs = torch.from_numpy(x[n:]).to(dev)
-        for bits in (1, 2, 4):
-            codec = uv.Codec(d_pad, bits, 8)
-            index = uv.Index(codec)
-            index.reserve(n)
-            enc_ms = _timed(lambda: (index.clear(), index.add_batch(base)), 2)
-            scan_ms = _timed(lambda: index.search(qs, 10, mips=True), 3)
-            uv.profile_enable(True)
-            index.search(qs, 10, mips=True)
-            torch.cuda.synchronize()
-            kern = {f: round(uv.profile_read(f)[0], 3) for f in SCAN_FAMILIES}
-            uv.profile_enable(False)
-            emit("wide-1Mx1k-d1024", {"bits": bits, "mem": 8, "encode_rows_s": n / enc_ms * 1e3,
-                                      "queries_s": nq / scan_ms * 1e3, "scan_ms": scan_ms,
-                                      "encode_ms": enc_ms, "k": 10, "mips": True,
-                                      "kernels_ms": kern})
-            del index, codec
+        run_wide(uv, dev, emit, rng)
     elif args.workload == "ivf":
-        n, nq, d, d_pad, nlist = 1_000_000, 10_000, 1536, 2048, 4096
-        x = ivf_data(rng, n, nq, d, d_pad)
-        base = torch.from_numpy(x[:n]).to(dev)
-        qs = torch.from_numpy(x[n:]).to(dev)
-        del x
-        t0 = time.time()
-        cen = uv.kmeans(base, nlist, seed=42, iters=5)
-        torch.cuda.synchronize()
-        km_s = time.time() - t0
-        codec = uv.Codec(d_pad, 2, 8)
-        ivf = uv.IvfIndex(codec, cen, centered=True)
-        t0 = time.time()
-        ivf.build(base)
-        torch.cuda.synchronize()
-        build_s = time.time() - t0
-        off = np.zeros(nlist + 1, np.int64)
-        import ctypes as C
-        uv.check(uv.lib().uv_ivf_export(ivf.h, C.c_void_p(off.ctypes.data), None, None, None,
-                                        None, None, None))
-        sizes = np.diff(off)
-        list_stats = {"mean": float(sizes.mean()), "max": int(sizes.max()),
-                      "p99": float(np.percentile(sizes, 99)), "empty": int((sizes == 0).sum())}
-        fams = ("prep_queries", "ivf_cosine", "ivf_select", "ivf_bucket", "ivf_pair_qm",
-                "ivf_scan", "merge_topk")
-        for nprobe in (1, 4, 16, 64):
-            ms = _timed(lambda: ivf.search(qs, 10, nprobe), 3)
-            uv.profile_enable(True)
-            ivf.search(qs, 10, nprobe)
-            torch.cuda.synchronize()
-            kern = {f: round(uv.profile_read(f)[0], 3) for f in fams}
-            uv.profile_enable(False)
-            emit("ivf-1Mx10k-d2048-nlist4096", {"nprobe": nprobe, "queries_s": nq / ms * 1e3,
-                                               "search_ms": ms, "kmeans_s": km_s,
-                                               "build_s": build_s, "centered": True, "k": 10,
-                                               "bits": 2, "mem": 8, "kernels_ms": kern,
-                                               "list_sizes": list_stats})
+        run_ivf(uv, dev, emit, rng)
     elif args.workload == "shortlist":
         n, nq, nlist = 1_000_000, 10_000, 1024
         base_np, query_np = make_data(n, nq)
@@ -829,19 +771,284 @@ def run_secondary(args):
                                                    f"{(n // ns) * ns} records"}})
             del ix, oc, enc, big
     else:
-        d = 128
-        rows = rng.standard_normal((1_000_000, d), dtype=np.float32)
-        base = torch.from_numpy(rows).to(dev)
-        for mem in (2, 4, 8, 12, 16):
-            n = {12: 100_000, 16: 10_000}.get(mem, 1_000_000)
-            codec = uv.Codec(d, 2, mem)
-            index = uv.Index(codec)
-            index.reserve(n)
-            sub = base[:n]
-            ms = _timed(lambda: (index.clear(), index.add_batch(sub)), 2)
-            emit("encode-sweep-d128-b2", {"mem": mem, "rows": n, "encode_rows_s": n / ms * 1e3,
-                                         "encode_ms": ms})
-            del index, codec
+        run_encode_sweep(uv, dev, emit)
+
+def _tc_roofline(uv, flops_full, nq_tiles_flops, peaks):
+    """Tensor-pipe roofline of the prefilter passes of the last profiled
+    search: pass 2 does the full contraction, pass 1 the one over every S-th
+    tile."""
+    p1 = uv.profile_read("tc_pass1")
+    p2 = uv.profile_read("tc_pass2")
+    s_ = max(1, uv.profile_read("tc_sample")[1])
+    if p2[1] == 0:
+        return None
+    flops = flops_full * (1.0 + 1.0 / s_)
+    t = (p1[0] + p2[0]) / p2[1]
+    peak = peaks.get("bf16_tflops", 1590.0)
+    ach = flops / (t / 1e3) / 1e12
+    return {"bound": "tensor", "kernel": "tc_wide_kernel (pass 1 and pass 2 per search)",
+            "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+            "flops_per_search": flops, "ms_per_search": t, "pass1_tile_stride": s_,
+            "peak_source": "bf16_tflops of MEASURED_PEAKS.json" if "bf16_tflops" in peaks
+            else "fallback 1.59 PFLOP/s", "traffic": None}
+
+
+def _e2e_host(fn, q_host, reps=3):
+    """Search timed end to end with host buffers (pinned queries in, host
+    results out), best of reps after one warm-up, in ms."""
+    import torch
+
+    fn(q_host)
+    best = float("inf")
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn(q_host)
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b))
+    return best
+
+
+def run_wide(uv, dev, emit, rng):
+    """1M rows, d=960 padded to 1024, x_ij = U[0,1) + 0.5 j / 959, b in {1,
+    2, 4}, M=8: encode rows/s and 1k-query top-10 MIPS (the tensor-core
+    prefilter with K streamed in chunks), with the oracle's top-10 for 16
+    of the queries over the full GPU index and its encoding of 512 rows as
+    the parity check and CPU baseline."""
+    import torch
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O  # the CPU oracle: baseline and checker only
+
+    threads = O.threads_available()
+    peaks = load_peaks()
+    n, nq, d, d_pad = 1_000_000, 1000, 960, 1024
+    x = np.zeros((n + nq, d_pad), np.float32)
+    for a in range(0, n + nq, 100_000):
+        b = min(a + 100_000, n + nq)
+        x[a:b, :d] = rng.random((b - a, d), dtype=np.float32) + \
+            np.float32(0.5) * (np.arange(d, dtype=np.float32) / np.float32(959))
+    base = torch.from_numpy(x[:n]).to(dev)
+    qs = torch.from_numpy(x[n:]).to(dev)
+    q_host = torch.from_numpy(x[n:]).pin_memory()
+    for bits in (1, 2, 4):
+        codec = uv.Codec(d_pad, bits, 8)
+        index = uv.Index(codec)
+        index.reserve(n)
+        enc_ms = _timed(lambda: (index.clear(), index.add_batch(base)), 2)
+        clocks = ClockSampler(0)
+        clocks.start()
+        scan_ms = _timed(lambda: index.search(qs, 10, mips=True), 3)
+        clk = clocks.stop()
+        uv.profile_enable(True)
+        ids, scores = index.search(qs, 10, mips=True)
+        torch.cuda.synchronize()
+        kern = {f: round(uv.profile_read(f)[0], 3) for f in SCAN_FAMILIES}
+        roof = _tc_roofline(uv, 2.0 * nq * n * d_pad, None, peaks)
+        launches = uv.profile_read("*")[1]
+        uv.profile_enable(False)
+        e2e_ms = _e2e_host(lambda q: index.search(q, 10, mips=True), q_host)
+        ex = index.export()
+        oc = O.Codec(d_pad, bits, 8)
+        rec = {"codes": ex["codes"], "start": ex["start"], "rescale": ex["rescale"]}
+        sample = max(16, threads)
+        t0 = time.perf_counter()
+        wids, wsc = oc.search_topk(rec, x[n:n + sample], 10, norms=ex["norms"], threads=threads)
+        cpu_q = sample / (time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        enc = oc.encode_batch(x[:512], threads=threads)
+        cpu_enc = 512 / (time.perf_counter() - t0)
+        gi, gs = ids[:sample].cpu().numpy(), scores[:sample].cpu().numpy()
+        parity = {"queries": sample, "records": n, "k": 10,
+                  "ids_equal": bool(np.array_equal(gi, wids)),
+                  "scores_bitequal": bool(np.array_equal(gs.view(np.uint32),
+                                                         wsc.view(np.uint32))),
+                  "encode_rows": 512,
+                  "encode_rows_equal": bool(np.array_equal(ex["codes"][:512], enc["codes"])
+                                            and np.array_equal(ex["start"][:512],
+                                                               enc["start"]))}
+        emit("wide-1Mx1k-d1024", {
+            "bits": bits, "mem": 8, "value": nq / scan_ms * 1e3, "unit": "queries/s",
+            "queries_s": nq / scan_ms * 1e3, "scan_ms": scan_ms,
+            "encode_rows_s": n / enc_ms * 1e3, "encode_ms": enc_ms, "k": 10, "mips": True,
+            "kernels_ms": kern, "gpu_launches": launches, "roofline": roof,
+            "e2e": {"value": nq / e2e_ms * 1e3, "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * d_pad * 4, "d2h_bytes_per_step": nq * 10 * 12,
+                    "api": "uv_index_search with host buffers"},
+            "cpu_baseline": {"value": cpu_q, "unit": "queries/s", "cores": threads,
+                             "kind": "port", "sample": f"{sample} queries x {n} records; "
+                                                       f"encode 512 rows",
+                             "encode_rows_s": cpu_enc},
+            "parity": parity, "clocks": clk,
+            "l2": "1M records of 137-521 B exceed L2 at b >= 2"})
+        del index, codec
+
+
+def run_ivf(uv, dev, emit, rng):
+    """1M rows, d=1536 padded to 2048: 64 unit Gaussian centres + 0.3 N(0,1),
+    renormalized; k-means nlist=4096 (seed 42, 5 rounds), centered lists,
+    b=2, M=8; 10k-query top-10 at nprobe 1/4/16/64.  Per nprobe: queries/s,
+    the records the probed lists hold per query and the FP32 rate of the list
+    scan over them, end to end with host buffers, and the oracle's top-10 for
+    16 queries over the GPU's posting lists (parity and CPU baseline)."""
+    import torch
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O  # the CPU oracle: baseline and checker only
+
+    threads = O.threads_available()
+    peaks = load_peaks()
+    smax = peaks.get("sm_max_mhz", 1965.0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    fp32_peak = sms * FP32_LANES_PER_SM * 2 * smax * 1e6
+    n, nq, d, d_pad, nlist = 1_000_000, 10_000, 1536, 2048, 4096
+    x = ivf_data(rng, n, nq, d, d_pad)
+    base = torch.from_numpy(x[:n]).to(dev)
+    qs = torch.from_numpy(x[n:]).to(dev)
+    q_np = x[n:].copy()
+    del x
+    q_host = torch.from_numpy(q_np).pin_memory()
+    t0 = time.time()
+    cen = uv.kmeans(base, nlist, seed=42, iters=5)
+    torch.cuda.synchronize()
+    km_s = time.time() - t0
+    codec = uv.Codec(d_pad, 2, 8)
+    ivf = uv.IvfIndex(codec, cen, centered=True)
+    t0 = time.time()
+    ivf.build(base)
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+    del base
+    ex = ivf.export()
+    sizes = np.diff(ex["list_off"])
+    list_stats = {"mean": float(sizes.mean()), "max": int(sizes.max()),
+                  "p99": float(np.percentile(sizes, 99)), "empty": int((sizes == 0).sum())}
+    cen_np = cen.cpu().numpy() if hasattr(cen, "cpu") else np.asarray(cen)
+    oc = O.Codec(d_pad, 2, 8)
+    lists = {"codes": ex["codes"], "start": ex["start"], "rescale": ex["rescale"],
+             "rnorm": ex["rnorm"]}
+    fams = ("prep_queries", "ivf_cosine", "ivf_select", "ivf_bucket", "ivf_pair_qm",
+            "ivf_scan", "merge_topk")
+    sample = max(16, threads)
+    for nprobe in (1, 4, 16, 64):
+        clocks = ClockSampler(0)
+        clocks.start()
+        ms = _timed(lambda: ivf.search(qs, 10, nprobe), 3)
+        clk = clocks.stop()
+        uv.profile_enable(True)
+        ids, scores = ivf.search(qs, 10, nprobe)
+        torch.cuda.synchronize()
+        kern = {f: round(uv.profile_read(f)[0], 3) for f in fams}
+        launches = uv.profile_read("*")[1]
+        uv.profile_enable(False)
+        probed = ivf.probe(qs, nprobe)
+        probed = probed.cpu().numpy() if hasattr(probed, "cpu") else np.asarray(probed)
+        scanned = float(np.where(probed >= 0, sizes[np.maximum(probed, 0)], 0).sum()) / nq
+        scan_ms = kern["ivf_scan"]
+        flops = 2.0 * scanned * nq * d_pad
+        e2e_ms = _e2e_host(lambda q: ivf.search(q, 10, nprobe), q_host)
+        t0 = time.perf_counter()
+        wids, wsc = oc.ivf_search_topk(cen_np, ex["list_off"], ex["ids"], lists, True,
+                                       q_np[:sample], nprobe, 10, threads=threads)
+        cpu_q = sample / (time.perf_counter() - t0)
+        gi, gs = ids[:sample].cpu().numpy(), scores[:sample].cpu().numpy()
+        emit("ivf-1Mx10k-d2048-nlist4096", {
+            "nprobe": nprobe, "value": nq / ms * 1e3, "unit": "queries/s",
+            "queries_s": nq / ms * 1e3, "search_ms": ms, "kmeans_s": km_s,
+            "build_s": build_s, "centered": True, "k": 10, "bits": 2, "mem": 8,
+            "kernels_ms": kern, "gpu_launches": launches, "list_sizes": list_stats,
+            "records_scanned_per_query": scanned,
+            "roofline": {"bound": "fp32", "kernel": "chunked_scan_kernel (IVF list scan)",
+                         "achieved": flops / (scan_ms / 1e3) / 1e12 if scan_ms > 0 else None,
+                         "peak": fp32_peak / 1e12, "unit": "TFLOP/s",
+                         "frac": flops / (scan_ms / 1e3) / fp32_peak if scan_ms > 0 else None,
+                         "flops_per_search": flops, "scan_ms": scan_ms,
+                         "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA x 2 x "
+                                        f"{smax:.0f} MHz", "traffic": None},
+            "e2e": {"value": nq / e2e_ms * 1e3, "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * d_pad * 4, "d2h_bytes_per_step": nq * 10 * 12,
+                    "api": "uv_ivf_search with host buffers"},
+            "cpu_baseline": {"value": cpu_q, "unit": "queries/s", "cores": threads,
+                             "kind": "port", "sample": f"{sample} queries over the GPU's "
+                                                       f"posting lists"},
+            "parity": {"queries": sample, "k": 10,
+                       "ids_equal": bool(np.array_equal(gi, wids)),
+                       "scores_bitequal": bool(np.array_equal(gs.view(np.uint32),
+                                                              wsc.view(np.uint32)))},
+            "clocks": clk})
+
+
+def run_encode_sweep(uv, dev, emit):
+    """The trellis-memory sweep: 1M rows d=128 N(0,1) from seed 1 (a prefix
+    where a cell would take more than about a second), b = 2 at M in {2, 4,
+    8, 12, 16} and the reference's whole 2-, 3- and 4-bit ladder M = 4..16
+    (its encode-cost table).  Per cell: encode rows/s (CUDA events, best of
+    two after a warm-up), the FP32/ALU lane operations of the add-compare-
+    select against the SMs' issue rate, the direction fidelity of the
+    reconstructions, the oracle's rate on a bounded sample with all host
+    threads, and that sample's records compared byte for byte."""
+    import torch
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O  # the CPU oracle: baseline and checker only
+
+    threads = O.threads_available()
+    d = 128
+    rows = np.random.default_rng(1).standard_normal((1_000_000, d), dtype=np.float32)
+    base = torch.from_numpy(rows).to(dev)
+    peaks = load_peaks()
+    smax = peaks.get("sm_max_mhz", 1965.0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    cells = [(2, 2)] + [(b, m) for b in (2, 3, 4) for m in (4, 6, 8, 10, 12, 14, 16)]
+    for bits, mem in cells:
+        w = mem + bits
+        n = int(min(1_000_000, max(2000, 2e11 / (d * 2 ** w))))
+        codec = uv.Codec(d, bits, mem)
+        index = uv.Index(codec)
+        index.reserve(n)
+        sub = base[:n]
+        clocks = ClockSampler(dev.index if dev.index is not None else 0)
+        clocks.start()
+        ms = _timed(lambda: (index.clear(), index.add_batch(sub)), 2)
+        clk = clocks.stop()
+        rate = n / ms * 1e3
+        # add-compare-select lane operations per row: a subtract, a multiply
+        # and an add per window, a compare-select per extra candidate
+        ops = d * (3 * 2 ** w + (2 ** bits - 1) * 2 ** mem)
+        lane_peak = sms * FP32_LANES_PER_SM * smax * 1e6
+        ex = index.export()
+        m = min(n, 2000)
+        rec = codec.decode(ex["codes"][:m], ex["start"][:m])
+        rec = rec / np.maximum(np.linalg.norm(rec, axis=1, keepdims=True), 1e-30)
+        unit = rows[:m] / np.linalg.norm(rows[:m], axis=1, keepdims=True)
+        fidelity = float(np.mean(np.sum(rec * unit, axis=1)))
+        oc = O.Codec(d, bits, mem)
+        n_cpu = int(max(threads, min(4096, 2e9 / (d * 2 ** w))))
+        t0 = time.perf_counter()
+        enc = oc.encode_batch(rows[:n_cpu], threads=threads)
+        cpu_rate = n_cpu / (time.perf_counter() - t0)
+        same = bool(np.array_equal(ex["codes"][:n_cpu], enc["codes"])
+                    and np.array_equal(ex["start"][:n_cpu], enc["start"])
+                    and np.array_equal(ex["rescale"][:n_cpu].view(np.uint32),
+                                       enc["rescale"].view(np.uint32)))
+        emit("encode-sweep-d128", {
+            "bits": bits, "mem": mem, "window_bits": w, "rows": n, "encode_rows_s": rate,
+            "encode_ms": ms, "encoder": "staged" if (w > 18 or (w >= 15 and bits > 2) or
+                                                     mem < bits) else
+                                       ("cluster" if w >= 15 else "resident"),
+            "roofline": {"bound": "fp32/alu issue", "lane_ops_per_row": ops,
+                         "achieved_lane_ops_s": rate * ops, "peak_lane_ops_s": lane_peak,
+                         "frac": rate * ops / lane_peak,
+                         "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} lanes x "
+                                        f"{smax:.0f} MHz"},
+            "direction_fidelity": fidelity,
+            "cpu_baseline": {"value": cpu_rate, "unit": "rows/s", "cores": threads,
+                             "kind": "port", "sample": f"{n_cpu} rows"},
+            "parity": {"rows": n_cpu, "records_equal": same},
+            "clocks": clk})
+        del index, codec
 
 
 if __name__ == "__main__":
