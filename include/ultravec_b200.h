@@ -213,15 +213,17 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * single index over the whole base gives (ids and score bits):
  *   1. uv_index_search_begin on every shard, with the number of shards:
  *      query preparation and the prefilter's first pass.  bounds_out
- *      receives nq x k lower bounds (any order): scores that k distinct
- *      records of this shard reach (-inf where it has no such bound).
+ *      receives nq x m lower bounds (uv_search_bounds_per_query; any order):
+ *      scores that m distinct records of this shard reach (-inf where it
+ *      has no such bound).
  *   2. The caller gathers every shard's bounds, shard-major (n_shards x nq x
- *      k floats: one all-gather), and hands them to uv_search_set_bounds on
+ *      m floats: one all-gather), and hands them to uv_search_set_bounds on
  *      every shard.  The k-th largest of their union is a score that k
  *      records of the whole base reach, so no shard keeps a record below it;
  *      each shard then scores exactly only the records that can still be in
- *      the global top k, instead of its own top k's worth.  Skipping this
- *      step gives the shard's own top k, as uv_index_search does.
+ *      the global top k, instead of its own top k's worth.  With one shard
+ *      this step may be skipped (the shard's own top k, as uv_index_search);
+ *      with several, uv_search_finish refuses to run before it.
  *   3. uv_search_finish: this shard's best (at most) k, ranked as
  *      uv_index_search, unfilled slots (id -1) where fewer records pass.
  *   4. uv_search_destroy (before the index is destroyed).
@@ -232,6 +234,10 @@ int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores,
  * (above 128 every shard ranks all its records and step 2 changes
  * nothing); queries and outputs in host or device memory. */
 typedef struct uv_search uv_search;
+/* m, the bounds per query each of n_shards shards contributes for a top k:
+ * k for one shard, else min(k, 2 * ceil(k / n_shards)).  bounds_out and
+ * every shard's part of the gathered bounds are nq x m. */
+int uv_search_bounds_per_query(int32_t k, int32_t n_shards, int32_t *m);
 int uv_index_search_begin(const uv_index *index, const float *queries, int64_t nq, int32_t k,
                           int32_t mode, int32_t n_shards, float *bounds_out, uv_search **out,
                           void *stream);

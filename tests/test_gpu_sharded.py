@@ -35,7 +35,8 @@ def _protocol(uv, shards, qs, k, mips, share=True):
     import torch
 
     n = len(shards)
-    ss = [ix.search_begin(qs, k, mips=mips, n_shards=n) for ix in shards]
+    # without sharing, each shard searches as a base of its own (n_shards 1)
+    ss = [ix.search_begin(qs, k, mips=mips, n_shards=n if share else 1) for ix in shards]
     if share:
         gathered = torch.cat([torch.as_tensor(s.bounds).cuda() for s in ss], 0)
         for s in ss:
@@ -90,7 +91,7 @@ def test_shared_threshold_prunes_candidates(uv):
     _, shards = _shards(uv, rows, 4)
     counts = {}
     for share in (False, True):
-        s_all = [x.search_begin(qs, 100, mips=True, n_shards=4) for x in shards]
+        s_all = [x.search_begin(qs, 100, mips=True, n_shards=4 if share else 1) for x in shards]
         if share:
             g = torch.cat([torch.as_tensor(s.bounds).cuda() for s in s_all], 0)
             for s in s_all:
@@ -102,6 +103,12 @@ def test_shared_threshold_prunes_candidates(uv):
             s.close()
         counts[share] = total
     assert counts[True] < counts[False]
+    # with several shards the shared threshold is required before finish
+    s = shards[0].search_begin(qs, 100, mips=True, n_shards=4)
+    assert s.bounds.shape == (256, 50)  # min(k, 2 * ceil(k / 4)) per query
+    with pytest.raises(uv.UVError):
+        s.finish()
+    s.close()
 
 
 def test_sharded_search_other_paths(uv, oracle):

@@ -41,7 +41,7 @@ SYMBOLS = [
     "uv_coset_add", "uv_coset_search", "uv_coset_len", "uv_coset_shape", "uv_coset_books",
     "uv_coset_mem_bytes", "uv_coset_model_bytes", "uv_coset_export", "uv_coset_reconstruct",
     "uv_index_search_begin", "uv_search_set_bounds", "uv_search_finish", "uv_search_destroy",
-    "uv_topk_pack", "uv_topk_merge_packed",
+    "uv_topk_pack", "uv_topk_merge_packed", "uv_search_bounds_per_query",
 ]
 
 
@@ -149,6 +149,7 @@ def lib():
             "uv_search_set_bounds": (C.c_int, [vp, vp, i32]),
             "uv_search_finish": (C.c_int, [vp, vp, vp]),
             "uv_search_destroy": (C.c_int, [vp]),
+            "uv_search_bounds_per_query": (C.c_int, [i32, i32, C.POINTER(i32)]),
             "uv_topk_pack": (C.c_int, [i32, vp, vp, i64, vp, vp]),
             "uv_topk_merge_packed": (C.c_int, [i32, vp, i64, i32, i32, i64, i64, i32, vp, vp,
                                                vp]),
@@ -741,8 +742,8 @@ class IvfIndex:
 class ShardSearch:
     """A search of one shard of a base split across GPUs
     (uv_index_search_begin / uv_search_set_bounds / uv_search_finish):
-    `bounds` (nq x k) are this shard's first-pass lower bounds; gather every
-    shard's bounds shard-major into (n_shards * nq, k), pass them to
+    `bounds` (nq x m) are this shard's best first-pass lower bounds; gather
+    every shard's bounds shard-major into (n_shards * nq, m), pass them to
     set_bounds, then finish() gives this shard's (ids, scores), at most k per
     query, of which only records that can be in the global top k remain."""
 
@@ -750,8 +751,10 @@ class ShardSearch:
         queries = _f32(queries)
         self.nq, self.k = queries.shape[0], k
         self._alloc = _Alloc(queries)
-        self._like = queries
-        self.bounds = self._alloc((self.nq, k), np.float32)
+        m = C.c_int32()
+        check(lib().uv_search_bounds_per_query(k, n_shards, C.byref(m)))
+        self.m = m.value
+        self.bounds = self._alloc((self.nq, self.m), np.float32)
         h = C.c_void_p()
         check(lib().uv_index_search_begin(index.h, _ptr(queries), self.nq, k,
                                           UV_SEARCH_MIPS if mips else UV_SEARCH_COSINE,

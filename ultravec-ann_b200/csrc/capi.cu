@@ -1309,7 +1309,7 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
     if (tsm > 48 * 1024)
       UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)tsm));
-    uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(tmax, n_groups1, nq, k, theta);
+    uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(tmax, n_groups1, nq, k, theta, 1);
     UV_CK(cudaGetLastError());
   }
   ts->k2 = k2;
@@ -1395,12 +1395,14 @@ int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint3
     const void *wk = uvb::tc_rescore_warp_kernel_ptr(c->cfg.bits);
     if (g_rescore_warp.load() == 0 && wk != nullptr && d <= uvb::kRescoreWarpDim &&
         c->table_len <= 1024 && wsmem <= 227 * 1024) {
+      UV_TRY(sc.alloc(&rp.big_list, (size_t)nq));
+      UV_TRY(sc.alloc(&rp.n_big, 1));
+      UV_CK(cudaMemsetAsync(rp.n_big, 0, sizeof(int), st));
       UV_CK(cudaFuncSetAttribute(wk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
       void *wargs[] = {&rp};
       ProfScope ps("tc_rescore", st);
       UV_CK(cudaLaunchKernel(wk, dim3((unsigned)((nq + uvb::kRescoreWarps - 1) / uvb::kRescoreWarps)),
                              dim3(32 * uvb::kRescoreWarps), wargs, wsmem, st));
-      rp.warp_cap = uvb::kRescoreWarpCap;
     }
     // long candidate lists (about k*S per query) score one candidate per
     // thread; short ones half a warp per candidate
@@ -1575,6 +1577,9 @@ struct uv_search {
   int64_t nq = 0;
   int k = 0, mode = 0;
   enum Path { kPrefilter, kExact, kShortlist, kFullRank } path = kExact;
+  int m = 0;                  // bounds per query this shard contributes
+  bool needs_bounds = false;  // several shards: the threshold comes from set_bounds
+  bool bounds_set = false;
   bool finished = false;
   const float *d_q = nullptr;
   float *q_r = nullptr, *qc = nullptr;
@@ -1584,6 +1589,16 @@ struct uv_search {
 };
 
 extern "C" {
+
+int uv_search_bounds_per_query(int32_t k, int32_t n_shards, int32_t *m) {
+  if (m == nullptr) return fail(UV_EINVAL, "null argument");
+  if (k < 1 || n_shards < 1) return fail(UV_EINVAL, "k and n_shards must be at least 1");
+  // every shard's best 2 * ceil(k / n_shards) bounds: the union still holds k
+  // values (its k-th largest stays a valid threshold, any subset's does), and
+  // a shard holds more than that many of the union's best k only rarely
+  *m = n_shards == 1 ? k : std::min<int32_t>(k, 2 * ((k + n_shards - 1) / n_shards));
+  return UV_OK;
+}
 
 int uv_index_search_begin(const uv_index *ix, const float *queries, int64_t nq, int32_t k,
                           int32_t mode, int32_t n_shards, float *bounds_out, uv_search **out,
@@ -1609,10 +1624,13 @@ int uv_index_search_begin(const uv_index *ix, const float *queries, int64_t nq, 
     s->nq = nq;
     s->k = k;
     s->mode = mode;
+    UV_TRY(uv_search_bounds_per_query(k, n_shards, &s->m));
+    const int m = s->m;
+    s->needs_bounds = n_shards > 1;
     bool b_dev = false;
     UV_TRY(classify(bounds_out, dev, &b_dev));
     float *d_bounds = bounds_out;
-    if (!b_dev) UV_TRY(s->sc.alloc(&d_bounds, (size_t)std::max<int64_t>(nq, 1) * k));
+    if (!b_dev) UV_TRY(s->sc.alloc(&d_bounds, (size_t)std::max<int64_t>(nq, 1) * m));
     if (nq == 0) return UV_OK;
     // a private copy of the queries: the caller's buffer may go away
     float *q_copy = nullptr;
@@ -1640,18 +1658,33 @@ int uv_index_search_begin(const uv_index *ix, const float *queries, int64_t nq, 
       s->path = s->ts.used ? uv_search::kPrefilter : uv_search::kExact;
     }
     if (s->path == uv_search::kPrefilter) {
-      ProfScope ps("tc_theta", st);
-      uvb::tc_bounds_kernel<<<(unsigned)nq, 256, 0, st>>>(s->ts.tmax, s->ts.n_groups1, nq, k,
-                                                          s->ts.theta, d_bounds);
+      ProfScope ps("tc_bounds", st);
+      // the m-th largest group bound of each query (the k-th is ts.theta),
+      // then the best m bounds
+      const float *th = s->ts.theta;
+      if (m != k) {
+        float *theta_m = nullptr;
+        UV_TRY(s->sc.alloc(&theta_m, (size_t)nq));
+        const int64_t ng = s->ts.n_groups1;
+        const size_t tsm = ng <= uvb::kThetaSmemKeys ? (size_t)ng * 4 : 0;
+        if (tsm > 48 * 1024)
+          UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
+        uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(s->ts.tmax, ng, nq, m, theta_m, 1);
+        UV_CK(cudaGetLastError());
+        th = theta_m;
+      }
+      uvb::tc_bounds_kernel<<<(unsigned)nq, 256, 0, st>>>(s->ts.tmax, s->ts.n_groups1, nq, m, th,
+                                                          d_bounds);
       UV_CK(cudaGetLastError());
     } else {
       // no first pass on this shard: it bounds nothing
-      uvb::fill_value_kernel<<<(unsigned)std::min<int64_t>((nq * k + 255) / 256, 4096), 256, 0,
-                               st>>>(d_bounds, nq * k, -INFINITY);
+      uvb::fill_value_kernel<<<(unsigned)std::min<int64_t>((nq * m + 255) / 256, 4096), 256, 0,
+                               st>>>(d_bounds, nq * m, -INFINITY);
       UV_CK(cudaGetLastError());
     }
     if (!b_dev) {
-      UV_CK(cudaMemcpyAsync(bounds_out, d_bounds, sizeof(float) * nq * k, cudaMemcpyDeviceToHost,
+      UV_CK(cudaMemcpyAsync(bounds_out, d_bounds, sizeof(float) * nq * m, cudaMemcpyDeviceToHost,
                             st));
       UV_CK(cudaStreamSynchronize(st));
     }
@@ -1670,26 +1703,23 @@ int uv_search_set_bounds(uv_search *s, const float *gathered, int32_t n_shards) 
   if (s == nullptr || (s->nq > 0 && gathered == nullptr)) return fail(UV_EINVAL, "null argument");
   if (n_shards < 1) return fail(UV_EINVAL, "n_shards must be at least 1");
   if (s->finished) return fail(UV_EINVAL, "the search has finished");
+  s->bounds_set = true;
   if (s->nq == 0 || s->path != uv_search::kPrefilter) return UV_OK;
-  const int dev = s->ix->codec->cfg.device;
+  const int dev = s->dev;
   DeviceGuard g(dev);
   const int64_t nq = s->nq;
   const int k = s->k;
-  const size_t count = (size_t)n_shards * nq * k;
+  const size_t count = (size_t)n_shards * nq * s->m;
   const float *d_g = nullptr;
   UV_TRY(stage_in(gathered, count, dev, s->sc, &d_g));
-  float *per_q = nullptr;
-  UV_TRY(s->sc.alloc(&per_q, count));
-  ProfScope ps("tc_theta", s->st);
-  uvb::tc_bounds_regroup_kernel<<<(unsigned)std::min<size_t>((count + 255) / 256, 4096), 256, 0,
-                                  s->st>>>(d_g, n_shards, nq, k, per_q);
-  UV_CK(cudaGetLastError());
-  const int64_t per = (int64_t)n_shards * k;
+  // the k-th largest of the union of every shard's best m bounds
+  ProfScope ps("tc_bounds", s->st);
+  const int64_t per = (int64_t)n_shards * s->m;
   const size_t tsm = per <= uvb::kThetaSmemKeys ? (size_t)per * 4 : 0;
   if (tsm > 48 * 1024)
     UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)tsm));
-  uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, s->st>>>(per_q, per, nq, k, s->ts.theta);
+  uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, s->st>>>(d_g, per, nq, k, s->ts.theta, n_shards);
   UV_CK(cudaGetLastError());
   return UV_OK;
 }
@@ -1697,6 +1727,8 @@ int uv_search_set_bounds(uv_search *s, const float *gathered, int32_t n_shards) 
 int uv_search_finish(uv_search *s, int64_t *ids_out, float *scores_out) {
   if (s == nullptr || (s->nq > 0 && ids_out == nullptr)) return fail(UV_EINVAL, "null argument");
   if (s->finished) return fail(UV_EINVAL, "the search has finished");
+  if (s->needs_bounds && !s->bounds_set)
+    return fail(UV_EINVAL, "a search of several shards needs uv_search_set_bounds before finish");
   s->finished = true;
   if (s->nq == 0) return UV_OK;
   const uv_index *ix = s->ix;

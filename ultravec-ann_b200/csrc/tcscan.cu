@@ -579,13 +579,22 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 }
 
 __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_t n_tiles,
-                                                        int64_t nq, int k, float *theta) {
+                                                        int64_t nq, int k, float *theta,
+                                                        int lists) {
   extern __shared__ uint32_t keys_s[];  // n_tiles keys when they fit (see the launch)
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel[2];
   const int64_t q = blockIdx.x;
   if (q >= nq) return;
-  const float *v = tmax + q * n_tiles;
+  // one list: query q's n_tiles values at tmax[q * n_tiles + i]; several
+  // (gathered shard-major, lists x nq x per): value i is element i % per of
+  // list i / per
+  const int64_t per = n_tiles / lists;
+  auto at = [&](int64_t i) -> float {
+    if (lists == 1) return tmax[q * n_tiles + i];
+    const int64_t l = i / per;
+    return tmax[(l * nq + q) * per + (i - l * per)];
+  };
   if (n_tiles < k) {
     if (threadIdx.x == 0) theta[q] = -INFINITY;
     return;
@@ -593,13 +602,13 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
   // the four radix passes read the maxima from shared memory when they fit
   const bool staged = n_tiles <= kThetaSmemKeys;
   if (staged)
-    for (int64_t i = threadIdx.x; i < n_tiles; i += 256) keys_s[i] = fkey(v[i]);
+    for (int64_t i = threadIdx.x; i < n_tiles; i += 256) keys_s[i] = fkey(at(i));
   uint32_t prefix = 0, mask = 0, kk = (uint32_t)k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     hist[threadIdx.x] = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < n_tiles; i += 256) {
-      const uint32_t key = staged ? keys_s[i] : fkey(v[i]);
+      const uint32_t key = staged ? keys_s[i] : fkey(at(i));
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -650,20 +659,6 @@ __global__ void __launch_bounds__(256) tc_bounds_kernel(const float *tmax, int64
   for (int i = min(cnt, k) + threadIdx.x; i < k; i += 256) out[i] = th;
 }
 
-// The shards' bounds, gathered shard-major (shards x nq x k), regrouped per
-// query (nq x shards*k) for tc_theta_kernel: the k-th largest of their union
-// is a score at least k distinct records of the whole base reach.
-__global__ void tc_bounds_regroup_kernel(const float *gathered, int shards, int64_t nq, int k,
-                                         float *out) {
-  const int64_t per = nq * (int64_t)k, total = per * shards;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t sh = e / per, r = e - sh * per;
-    const int64_t q = r / k, j = r - q * k;
-    out[q * shards * (int64_t)k + sh * k + j] = gathered[e];
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Exact scores of the candidates (simd.rs:183-262 association: 16 FMA chains
 // over 16-wide blocks, then the hsum256 tree; trellis.rs:1517 estimator) and
@@ -679,7 +674,10 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   int *roff = (int *)(cidx + p.cap);                  // regions + 1 segment offsets
   float *qv = (float *)(roff + ((p.regions + 4) & ~3));  // dim
   float *table = qv + p.dim;                          // table_len (optional)
-  const int64_t q = blockIdx.x;
+  // every query, or those the warp kernel left (a device count: CTAs past
+  // it leave at once)
+  if (p.big_list != nullptr && (int)blockIdx.x >= *p.n_big) return;
+  const int64_t q = p.big_list != nullptr ? (int64_t)p.big_list[blockIdx.x] : (int64_t)blockIdx.x;
   if (q >= p.nq) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // gather the segments pass 2 wrote (one per record split and column slice);
@@ -719,7 +717,6 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
   }
   __syncthreads();
   const int cnt_raw = roff[p.regions];
-  if (p.warp_cap > 0 && cnt_raw >= 0 && cnt_raw <= p.warp_cap) return;  // scored per warp
   if (cnt_raw < 0) {
     if (tid == 0) p.over_list[atomicAdd(p.n_over, 1)] = (int32_t)q;
     return;
@@ -835,7 +832,7 @@ __global__ void __launch_bounds__(256) tc_rescore_kernel(const TcRescoreParams p
 
 // The same exact rescoring, one warp per query, for queries whose candidate
 // list holds at most kRescoreWarpCap entries and no full segment (the others
-// are left to tc_rescore_kernel, launched after this one with warp_cap set).
+// are listed for tc_rescore_kernel, launched after this one).
 // Many short lists are the multi-GPU case, where a shared threshold leaves
 // each shard a few dozen candidates per query: a CTA per query would spend
 // most of its time on set-up and block-wide barriers.  The code table sits
@@ -889,7 +886,11 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, 2) tc_rescore_warp_kernel(
     ex += c_loc[t];
   }
   const int total = __shfl_sync(0xffffffffu, incl, 31);
-  if (__any_sync(0xffffffffu, over) || total > CAP) return;  // left to tc_rescore_kernel
+  if (__any_sync(0xffffffffu, over) || total > CAP) {
+    // a long list or a full segment: tc_rescore_kernel takes the query
+    if (lane == 0) p.big_list[atomicAdd(p.n_big, 1)] = (int32_t)q;
+    return;
+  }
   __syncwarp();
   for (int i = lane; i < total; i += 32) {
     int lo = 0, hi = p.regions - 1;

@@ -266,8 +266,8 @@ struct TcRescoreParams {
   int32_t *over_list;
   int *n_over;
   unsigned long long *n_cand;  // total candidates scored (statistics)
-  int warp_cap;                // > 0: queries with at most this many candidates (and no
-                               // full segment) were scored by tc_rescore_warp_kernel
+  int32_t *big_list;           // or null: tc_rescore_warp_kernel scored every query but
+  int *n_big;                  // the *n_big listed here, left to tc_rescore_kernel
 };
 
 struct MergeParams {
@@ -321,11 +321,9 @@ __global__ void tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_
 // shared memory (4 bytes each) when n_tiles <= kThetaSmemKeys
 constexpr int kThetaSmemKeys = 12288;
 __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, int k,
-                                float *theta);
+                                float *theta, int lists);
 __global__ void tc_bounds_kernel(const float *tmax, int64_t n_groups, int64_t nq, int k,
                                  const float *theta, float *bounds);
-__global__ void tc_bounds_regroup_kernel(const float *gathered, int shards, int64_t nq, int k,
-                                         float *out);
 // bits 1..4; per_thread: one thread per candidate (long lists), else half a
 // warp per candidate (short lists)
 const void *tc_rescore_kernel_ptr(int bits, bool per_thread);

@@ -83,10 +83,10 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
     global ids), as uv_index_search_begin / set_bounds / finish plus the
     merge describe it:
 
-    1. `begin(world)` starts the shard's search and exposes its (nq, k)
-       first-pass lower bounds; one all-gather makes them (world * nq, k),
-       shard-major, on every rank, and every shard takes the k-th largest of
-       their union as its threshold (`set_bounds`).
+    1. `begin(world)` starts the shard's search and exposes its (nq, m)
+       best first-pass lower bounds; one all-gather makes them (world * nq,
+       m), shard-major, on every rank, and every shard takes the k-th largest
+       of their union as its threshold (`set_bounds`).
     2. `finish()` gives the shard's lists: only records that can be in the
        global top k survive the shared threshold.
     3. The lists travel once, packed (ids and scores in one 12-byte record,
@@ -106,8 +106,8 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
     s = begin(world)
     try:
         bounds = s.bounds
-        nq = bounds.shape[0]
-        gathered = torch.empty((world * nq, k), dtype=bounds.dtype, device=bounds.device)
+        nq, m = bounds.shape
+        gathered = torch.empty((world * nq, m), dtype=bounds.dtype, device=bounds.device)
         dist.all_gather_into_tensor(gathered, bounds.contiguous())
         s.set_bounds(gathered, world)
         ids, scores = s.finish()
