@@ -86,7 +86,8 @@ def test_shared_threshold_prunes_candidates(uv):
     """The shards score exactly fewer candidates with the shared bound."""
     import torch
 
-    rows = rand_rows(200_000, 128, 91)
+    # shards large enough that each alone also runs the prefilter
+    rows = rand_rows(800_000, 128, 91)
     qs = rand_rows(256, 128, 92)
     _, shards = _shards(uv, rows, 4)
     counts = {}
@@ -157,3 +158,27 @@ def test_merge_packed_large_rows(uv):
     for q in range(nq):
         cand = sorted((-s, i) for s, i in zip(sc[q].ravel(), ids[q].ravel()) if i >= 0)
         assert list(want_i[q]) == [i for _, i in cand[:k]]
+
+
+@pytest.mark.parametrize("L,kin,k", [(8, 100, 100), (5, 12, 9), (4, 200, 150), (16, 64, 40)])
+def test_merge_sorted_and_unsorted_lists(uv, L, kin, k):
+    """The k-way merge (one warp per row below 512 entries, one CTA above)
+    against a host reference, with exact ties, unfilled tails and a row
+    whose lists are not sorted by (score, id) (the bitonic fallback)."""
+    rng = np.random.default_rng(L * 1000 + kin)
+    nq = 7
+    sc = rng.integers(0, 40, (nq, L, kin)).astype(np.float32)
+    ids = rng.permutation(nq * L * kin).reshape(nq, L, kin).astype(np.int64)
+    order = np.lexsort((ids, -sc), axis=-1)
+    sc = np.ascontiguousarray(np.take_along_axis(sc, order, -1))
+    ids = np.ascontiguousarray(np.take_along_axis(ids, order, -1))
+    ids[2, 1, kin // 3:] = -1
+    sc[2, 1, kin // 3:] = -np.inf
+    ids[4, 0, :2] = ids[4, 0, 1::-1].copy()  # ids out of order at a tie or not
+    sc[4, 0, :2] = 50.0
+    got_i, got_s = uv.topk_merge(ids, sc, k)
+    for q in range(nq):
+        cand = sorted((-s, i) for s, i in zip(sc[q].ravel(), ids[q].ravel()) if i >= 0)
+        want = [i for _, i in cand[:k]] + [-1] * max(0, k - len(cand))
+        assert list(got_i[q]) == want, q
+        assert list(got_s[q][:len(cand)]) == [-s for s, _ in cand[:k]][:len(cand)]

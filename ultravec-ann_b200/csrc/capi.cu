@@ -1789,6 +1789,21 @@ int merge_rows(uvb::MergeParams m, int64_t *d_ids, float *d_scores, cudaStream_t
   const int64_t total = (int64_t)m.n_lists * m.k_in;
   m.out_id = d_ids;
   m.out_score = d_scores;
+  if (total >= 512 && total <= 8192) {
+    // one CTA per row: many entries per row
+    int pow2 = 32;
+    while (pow2 < total) pow2 <<= 1;
+    m.pow2 = pow2;
+    m.warps = 8;
+    const size_t smem = (size_t)pow2 * 12;
+    UV_CK(cudaFuncSetAttribute(uvb::merge_topk_block_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    void *args[] = {&m};
+    ProfScope ps("merge_topk", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::merge_topk_block_kernel, dim3((unsigned)m.nq),
+                           dim3(256), args, smem, st));
+    return UV_OK;
+  }
   if (total <= 8192) {
     int pow2 = 32;
     while (pow2 < total) pow2 <<= 1;

@@ -1059,6 +1059,119 @@ __global__ void __launch_bounds__(256) merge_topk_kernel(const MergeParams p) {
   }
 }
 
+// The same merge with one CTA per row, for rows of many entries (several
+// hundred): the rank searches of a row spread over all 256 threads, so a
+// row's latency is a few binary searches per thread instead of a warp's
+// dozens.  Same entry order, tie rule and fallback.
+__global__ void __launch_bounds__(256) merge_topk_block_kernel(const MergeParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int tid = threadIdx.x;
+  const int64_t q = blockIdx.x;
+  int64_t *ids = (int64_t *)sm;
+  uint32_t *keys = (uint32_t *)(ids + p.pow2);
+  __shared__ int valid_s;
+  if (q >= p.nq) return;  // the whole CTA
+  const int64_t list_stride = p.list_stride > 0 ? p.list_stride : p.k_in;
+  const int64_t row_stride = p.row_stride > 0 ? p.row_stride : (int64_t)p.n_lists * p.k_in;
+  const int64_t first = p.row_off ? p.row_off[q] * p.k_in : q * row_stride;
+  const int nl = p.row_off ? (int)(p.row_off[q + 1] - p.row_off[q]) : p.n_lists;
+  const int total = nl * p.k_in;
+  const int64_t orow = p.out_row ? (int64_t)p.out_row[q] : q;
+  int n = 32;
+  while (n < total) n <<= 1;
+  if (tid == 0) valid_s = 0;
+  for (int i = tid; i < n; i += 256) {
+    uint32_t key = 0u;
+    int64_t id = -1;
+    if (i < total) {
+      const int l = i / p.k_in, j = i - l * p.k_in;
+      const int64_t src = p.row_off ? first + i : first + l * list_stride + j;
+      if (p.in_packed) {
+        const int32_t *e = p.in_packed + 3 * src;
+        id = (int64_t)(((uint64_t)(uint32_t)e[1] << 32) | (uint32_t)e[0]);
+        key = score_key32(__int_as_float(e[2]));
+      } else {
+        id = p.in_id[src];
+        key = p.in_key ? p.in_key[src] : 0u;
+        if (p.in_score) key = score_key32(p.in_score[src]);
+      }
+      if (id < 0) key = 0u;
+    }
+    ids[i] = id;
+    keys[i] = key;
+  }
+  __syncthreads();
+  bool unsorted = false;
+  int valid = 0;
+  for (int i = tid; i < total; i += 256) {
+    const int j = i % p.k_in;
+    if (j > 0 && kid_better(keys[i], ids[i], keys[i - 1], ids[i - 1])) unsorted = true;
+    valid += ids[i] >= 0 && j < p.k ? 1 : 0;
+  }
+  if (__syncthreads_or(unsorted ? 1 : 0) == 0) {
+    atomicAdd(&valid_s, valid);
+    const int kk = min(p.k_in, p.k);
+    for (int e = tid; e < nl * kk; e += 256) {
+      const int l = e / kk, j = e - l * kk;
+      const int i = l * p.k_in + j;
+      const int64_t id = ids[i];
+      if (id < 0) continue;
+      const uint32_t key = keys[i];
+      int rank = j;
+      for (int l2 = 0; l2 < nl && rank < p.k; l2++) {
+        if (l2 == l) continue;
+        const uint32_t *kl = keys + l2 * p.k_in;
+        const int64_t *il = ids + l2 * p.k_in;
+        int lo = 0, hi = min(p.k_in, p.k);
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          const bool before = kid_better(kl[mid], il[mid], key, id) ||
+                              (l2 < l && il[mid] >= 0 && kl[mid] == key && il[mid] == id);
+          if (before)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        rank += lo;
+      }
+      if (rank < p.k) {
+        p.out_id[orow * p.k + rank] = id;
+        p.out_score[orow * p.k + rank] = key32_score(key);
+      }
+    }
+    __syncthreads();
+    for (int i = valid_s + tid; i < p.k; i += 256) {
+      p.out_id[orow * p.k + i] = -1;
+      p.out_score[orow * p.k + i] = -INFINITY;
+    }
+    return;
+  }
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int pi = tid; pi < n / 2; pi += 256) {
+        const int i = ((pi & ~(stride - 1)) << 1) | (pi & (stride - 1));
+        const int jx = i + stride;
+        const bool desc = (i & size) == 0;
+        const uint32_t ka = keys[i], kb = keys[jx];
+        const int64_t ia = ids[i], ib = ids[jx];
+        const bool swap = desc ? kid_better(kb, ib, ka, ia) : kid_better(ka, ia, kb, ib);
+        if (swap) {
+          keys[i] = kb;
+          keys[jx] = ka;
+          ids[i] = ib;
+          ids[jx] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < p.k; i += 256) {
+    const bool ok = i < n && ids[i] >= 0;
+    p.out_id[orow * p.k + i] = ok ? ids[i] : -1;
+    p.out_score[orow * p.k + i] = ok ? key32_score(keys[i]) : -INFINITY;
+  }
+}
+
 // Pack ids and scores into 12-byte records (id low, id high, score bits):
 // one buffer for a single collective of a sharded search's lists.
 __global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,

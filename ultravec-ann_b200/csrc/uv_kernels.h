@@ -294,6 +294,7 @@ const void *chunked_scan_kernel_ptr(int bits, bool table_in_smem, bool small_k);
 size_t chunked_scan_smem_bytes(int table_len, bool table_in_smem, bool small_k);
 constexpr int kScanKChunk = 128;
 __global__ void merge_topk_kernel(const MergeParams p);
+__global__ void merge_topk_block_kernel(const MergeParams p);
 __global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,
                                  int32_t *packed);
 
