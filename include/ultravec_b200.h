@@ -250,6 +250,9 @@ int uv_search_destroy(uv_search *search);
  * Device buffers of `device`. */
 int uv_topk_pack(int32_t device, const int64_t *ids, const float *scores, int64_t n, void *packed,
                  void *stream);
+/* The inverse of uv_topk_pack (scores may be NULL).  Device buffers. */
+int uv_topk_unpack(int32_t device, const void *packed, int64_t n, int64_t *ids, float *scores,
+                   void *stream);
 /* uv_topk_merge over packed records (device memory): list l of row q starts
  * at record q * row_stride + l * list_stride (0, 0: rows of n_lists x k_in
  * contiguous records).  After an all-to-all of query slices the lists of

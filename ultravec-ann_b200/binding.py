@@ -41,7 +41,7 @@ SYMBOLS = [
     "uv_coset_add", "uv_coset_search", "uv_coset_len", "uv_coset_shape", "uv_coset_books",
     "uv_coset_mem_bytes", "uv_coset_model_bytes", "uv_coset_export", "uv_coset_reconstruct",
     "uv_index_search_begin", "uv_search_set_bounds", "uv_search_finish", "uv_search_destroy",
-    "uv_topk_pack", "uv_topk_merge_packed", "uv_search_bounds_per_query",
+    "uv_topk_pack", "uv_topk_merge_packed", "uv_search_bounds_per_query", "uv_topk_unpack",
 ]
 
 
@@ -151,6 +151,7 @@ def lib():
             "uv_search_destroy": (C.c_int, [vp]),
             "uv_search_bounds_per_query": (C.c_int, [i32, i32, C.POINTER(i32)]),
             "uv_topk_pack": (C.c_int, [i32, vp, vp, i64, vp, vp]),
+            "uv_topk_unpack": (C.c_int, [i32, vp, i64, vp, vp, vp]),
             "uv_topk_merge_packed": (C.c_int, [i32, vp, i64, i32, i32, i64, i64, i32, vp, vp,
                                                vp]),
         }
@@ -784,24 +785,29 @@ class ShardSearch:
             pass
 
 
-def topk_pack(ids, scores, device: int = 0):
+def topk_pack(ids, scores, device: int = 0, out=None):
     """(nq, k) device ids and scores as one (nq, k, 3) int32 tensor of
-    12-byte records (id low, id high, score bits): one buffer per collective."""
+    12-byte records (id low, id high, score bits): one buffer per collective.
+    `out` (contiguous, nq * k * 3 int32) receives them when given."""
     import torch
 
-    out = torch.empty(tuple(ids.shape) + (3,), dtype=torch.int32, device=ids.device)
+    if out is None:
+        out = torch.empty(tuple(ids.shape) + (3,), dtype=torch.int32, device=ids.device)
     check(lib().uv_topk_pack(device, _ptr(ids), _ptr(scores), ids.numel(), _ptr(out),
                              _stream(ids)))
     return out
 
 
-def topk_unpack(packed):
-    """Inverse of topk_pack (torch ops): (..., 3) int32 -> ids, scores."""
+def topk_unpack(packed, device: int = 0):
+    """Inverse of topk_pack: (..., 3) int32 device records -> ids, scores."""
     import torch
 
-    lo = packed[..., 0].to(torch.int64) & 0xFFFFFFFF
-    hi = packed[..., 1].to(torch.int64)
-    return (hi << 32) | lo, packed[..., 2].contiguous().view(torch.float32)
+    shape = tuple(packed.shape[:-1])
+    ids = torch.empty(shape, dtype=torch.int64, device=packed.device)
+    scores = torch.empty(shape, dtype=torch.float32, device=packed.device)
+    check(lib().uv_topk_unpack(device, _ptr(packed.contiguous()), ids.numel(), _ptr(ids),
+                               _ptr(scores), _stream(packed)))
+    return ids, scores
 
 
 def topk_merge_packed(packed, nq: int, n_lists: int, k_in: int, k: int, row_stride: int = 0,

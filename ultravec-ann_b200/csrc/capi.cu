@@ -1919,6 +1919,26 @@ int uv_topk_pack(int32_t device, const int64_t *ids, const float *scores, int64_
   return UV_OK;
 }
 
+int uv_topk_unpack(int32_t device, const void *packed, int64_t n, int64_t *ids, float *scores,
+                   void *stream) {
+  if (n < 0) return fail(UV_EINVAL, "negative size");
+  if (n == 0) return UV_OK;
+  if (packed == nullptr || ids == nullptr) return fail(UV_EINVAL, "null argument");
+  DeviceGuard g(device);
+  for (const void *ptr : {(const void *)packed, (const void *)ids, (const void *)scores}) {
+    if (ptr == nullptr) continue;
+    bool on_dev = false;
+    UV_TRY(classify(ptr, device, &on_dev));
+    if (!on_dev) return fail(UV_EINVAL, "uv_topk_unpack works on device buffers");
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  ProfScope ps("topk_pack", st);
+  uvb::topk_unpack_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, st>>>(
+      (const int32_t *)packed, n, ids, scores);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
 int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t n_lists,
                          int32_t k_in, int64_t row_stride, int64_t list_stride, int32_t k,
                          int64_t *out_ids, float *out_scores, void *stream) {

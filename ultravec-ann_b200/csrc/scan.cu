@@ -1172,6 +1172,17 @@ __global__ void __launch_bounds__(256) merge_topk_block_kernel(const MergeParams
   }
 }
 
+// The inverse of topk_pack_kernel.
+__global__ void topk_unpack_kernel(const int32_t *packed, int64_t n, int64_t *ids,
+                                   float *scores) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t lo = (uint32_t)packed[3 * e], hi = (uint32_t)packed[3 * e + 1];
+    ids[e] = (int64_t)(((uint64_t)hi << 32) | lo);
+    if (scores != nullptr) scores[e] = __int_as_float(packed[3 * e + 2]);
+  }
+}
+
 // Pack ids and scores into 12-byte records (id low, id high, score bits):
 // one buffer for a single collective of a sharded search's lists.
 __global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,

@@ -590,8 +590,9 @@ __global__ void __launch_bounds__(256) tc_theta_kernel(const float *tmax, int64_
   // (gathered shard-major, lists x nq x per): value i is element i % per of
   // list i / per
   const int64_t per = n_tiles / lists;
+  const float *v1 = tmax + q * n_tiles;
   auto at = [&](int64_t i) -> float {
-    if (lists == 1) return tmax[q * n_tiles + i];
+    if (lists == 1) return v1[i];
     const int64_t l = i / per;
     return tmax[(l * nq + q) * per + (i - l * per)];
   };

@@ -297,6 +297,8 @@ __global__ void merge_topk_kernel(const MergeParams p);
 __global__ void merge_topk_block_kernel(const MergeParams p);
 __global__ void topk_pack_kernel(const int64_t *ids, const float *scores, int64_t n,
                                  int32_t *packed);
+__global__ void topk_unpack_kernel(const int32_t *packed, int64_t n, int64_t *ids,
+                                   float *scores);
 
 // tcscan.cu
 // shape 1: the queries (A) in shared memory; 3: A in TMEM (the default)

@@ -122,11 +122,16 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
     dist.all_to_all_single(recv, packed, [rows * k * 3] * world, in_splits)
     m_ids, m_sc = merge_packed(recv, rows, world, k, k, k, rows * k)
     rows_max = (nq + world - 1) // world
-    mine = torch.zeros((rows_max, k, 3), dtype=packed.dtype, device=packed.device)
-    if rows > 0:
-        mine[:rows] = pack(m_ids, m_sc).reshape(rows, k, 3)
+    if rows == rows_max:
+        mine = pack(m_ids, m_sc).reshape(rows, k, 3)
+    else:
+        mine = torch.zeros((rows_max, k, 3), dtype=packed.dtype, device=packed.device)
+        if rows > 0:
+            mine[:rows] = pack(m_ids, m_sc).reshape(rows, k, 3)
     allp = torch.empty((world * rows_max, k, 3), dtype=packed.dtype, device=packed.device)
     dist.all_gather_into_tensor(allp, mine)
+    if rows_max * world == nq:
+        return unpack(allp)  # equal slices: the gathered rows are the queries in order
     allp = allp.view(world, rows_max, k, 3)
     parts = [allp[r, :query_slice(nq, r, world)[1] - query_slice(nq, r, world)[0]]
              for r in range(world)]
