@@ -283,9 +283,12 @@ int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t
  * compute every cosine or dot on the CUDA cores (0 automatic: tensor-core
  * dots, exact values for the centroids that can still be chosen, the same
  * lists and assignments);
- * "tc_sample" fixes the prefilter's first-pass tile stride (0 automatic:
- * round(sqrt(1600/k)), at most 10); "tc_prepare" 1 makes the prefilter's
- * rows with the generic kernel (0 automatic);
+ * "tc_sample" fixes the prefilter's first-pass sampling stride S (0
+ * automatic: round(sqrt(1600/k)), at most 10); "tc_hot" chooses that
+ * sample (0 automatic: the n/S records of largest score scale g, copied
+ * into their own rows when the index changes; 1: every S-th record tile;
+ * N >= 2: the n/N records of largest g); "tc_prepare" 1 makes the
+ * prefilter's rows with the generic kernel (0 automatic);
  * "coset_nearest" selects how the coset trellis finds each block's nearest
  * kept point (0 automatic: every book point scored for books of <= 8192
  * points, the reference's bisection + ball search where the minimum is tied

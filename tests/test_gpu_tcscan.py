@@ -269,3 +269,31 @@ def test_row_kernels_agree(uv, bits, mem):
         uv.set_tuning("tc_scan", 0)
     assert same(out[0][0], out[1][0])
     assert out[0][1] == out[1][1] > 0
+
+
+@pytest.mark.parametrize("hot", [0, 1, 3, 8])
+def test_pass1_sample_choices_give_the_exact_answer(uv, oracle, hot):
+    """Pass 1 may bound any subset of the records: the records of largest
+    score scale g (tc_hot 0: n/S of them, 3 and 8: n/3 and n/8) or every
+    S-th tile (tc_hot 1).  Ids and score bits equal the oracle's either way,
+    on heavy-tailed MIPS rows whose norms vary widely."""
+    import bench
+
+    base, queries = bench.make_data(150_000, 64)
+    codec = uv.Codec(128, 2, 8)
+    index = uv.Index(codec)
+    index.add_batch(base)
+    ex = index.export()
+    o = oracle.Codec(128, 2, 8)
+    rec = {"codes": ex["codes"], "start": ex["start"], "rescale": ex["rescale"]}
+    try:
+        uv.set_tuning("tc_hot", hot)
+        uv.set_tuning("tc_scan", 2)
+        for k in (10, 100):
+            ids, scores = index.search(queries, k, mips=True)
+            wids, wsc = o.search_topk(rec, queries, k, norms=ex["norms"])
+            assert np.array_equal(ids, wids), (hot, k)
+            assert np.array_equal(scores.view(np.uint32), wsc.view(np.uint32)), (hot, k)
+    finally:
+        uv.set_tuning("tc_hot", 0)
+        uv.set_tuning("tc_scan", 0)

@@ -27,6 +27,7 @@ std::atomic<int> g_tc_sample{0};
 std::atomic<int> g_tc_prepare{0};
 std::atomic<int> g_ivf_tc_probe{0};
 std::atomic<int> g_rescore_warp{0};
+std::atomic<int> g_tc_hot{0};
 std::atomic<int64_t> g_tc_last_candidates{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 std::atomic<bool> g_prof_on{false};
@@ -1153,6 +1154,7 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
     xext = rows.xext;
     cmax = rows.cmax;
   }
+  TcRows *cache = g_tc_cache.load() == 0 ? nullptr : &ix->tc_rows[mips];
   // TMA maps: main rows of 128 fp16 (boxes of 64 x TN, 128-byte swizzle) and
   // the extra slice of 16 fp16 (boxes of 16 x TN, 32-byte swizzle)
   CUtensorMap &tmap_main = ts->tmap_main, &tmap_ext = ts->tmap_ext;
@@ -1246,7 +1248,86 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
                                              10, (int64_t)std::lround(std::sqrt(1600.0 / k))));
   if (fixed_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) * shards < 8 * (int64_t)k) S--;
-  const int64_t n_tiles1 = (n_tiles + S - 1) / S;
+  // Pass 1's sample: by default the n/S records of largest g, copied into
+  // their own rows (tc_hot_*_kernel); tuning key tc_hot 1: every S-th tile
+  // of the full rows; N >= 2: the n/N records of largest g.
+  const int hot_mode = g_tc_hot.load();
+  const int64_t s_hot = hot_mode >= 2 ? hot_mode : S;
+  int64_t hot_cap = ((n + s_hot - 1) / s_hot + TN - 1) / TN * TN;
+  const bool hot = hot_mode != 1 && s_hot > 1 && n >= 8 * (int64_t)TN &&
+                   2 * (hot_cap / TN) * shards >= 8 * (int64_t)k;
+  uint16_t *x16_hot = nullptr, *xext_hot = nullptr;
+  float *cmax_hot = nullptr;
+  if (hot) {
+    auto make_hot = [&](uint16_t *hx, uint16_t *he, float *hc) -> int {
+      uvb::TcPrepareParams hp;
+      std::memset(&hp, 0, sizeof(hp));
+      hp.mips = mips;
+      hp.kpad = kpad;
+      hp.dim = d;
+      hp.n = n;
+      hp.rescale = ix->rescale;
+      hp.rnorm = ix->rnorm;
+      hp.norms = ix->norms;
+      hp.x16 = x16;
+      hp.xext = xext;
+      uint32_t *hist = nullptr, *sel = nullptr;
+      UV_TRY(sc.alloc(&hist, 4096 + 8));
+      sel = hist + 4096;
+      ProfScope ps("tc_prepare", st);
+      const unsigned hg = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 1184));
+      UV_CK(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (4096 + 8), st));
+      uvb::tc_hot_hist_kernel<<<hg, 256, 0, st>>>(hp, 0, sel, hist);
+      uvb::tc_hot_pick_kernel<<<1, 32, 0, st>>>(hist, hot_cap, 0, sel);
+      UV_CK(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 4096, st));
+      uvb::tc_hot_hist_kernel<<<hg, 256, 0, st>>>(hp, 1, sel, hist);
+      uvb::tc_hot_pick_kernel<<<1, 32, 0, st>>>(hist, hot_cap, 1, sel);
+      uvb::tc_hot_gather_kernel<<<hg, 256, 0, st>>>(hp, sel, sel + 4, hot_cap, hx, he);
+      uvb::tc_hot_pad_kernel<<<(unsigned)std::min<int64_t>((hot_cap + 255) / 256, 1184), 256, 0,
+                               st>>>(sel + 4, hot_cap, kpad, hx, he);
+      uvb::tc_chunk_cmax_kernel<<<(unsigned)((hot_cap + 255) / 256), 256, 0, st>>>(
+          he, hot_cap, hot_cap, hc);
+      UV_CK(cudaGetLastError());
+      return UV_OK;
+    };
+    if (cache == nullptr) {
+      UV_TRY(sc.alloc(&x16_hot, (size_t)hot_cap * kpad));
+      UV_TRY(sc.alloc(&xext_hot, (size_t)hot_cap * 16));
+      UV_TRY(sc.alloc(&cmax_hot, (size_t)hot_cap / 16));
+      UV_TRY(make_hot(x16_hot, xext_hot, cmax_hot));
+    } else {
+      std::lock_guard<std::mutex> rows_lock(ix->tc_mu);
+      TcRows &rows = *cache;
+      if (rows.hot_version != ix->version || rows.hot_cap != hot_cap) {
+        rows.hot_version = ~0ull;
+        if (rows.hot_alloc < hot_cap) {
+          if (rows.x16_hot != nullptr) {
+            UV_CK(cudaDeviceSynchronize());
+            cudaFree(rows.x16_hot);
+            cudaFree(rows.xext_hot);
+            cudaFree(rows.cmax_hot);
+            rows.x16_hot = rows.xext_hot = nullptr;
+            rows.cmax_hot = nullptr;
+            rows.hot_alloc = 0;
+          }
+          UV_CK(cudaMalloc((void **)&rows.x16_hot, sizeof(uint16_t) * (size_t)hot_cap * kpad));
+          UV_CK(cudaMalloc((void **)&rows.xext_hot, sizeof(uint16_t) * (size_t)hot_cap * 16));
+          UV_CK(cudaMalloc((void **)&rows.cmax_hot, sizeof(float) * (size_t)hot_cap / 16));
+          rows.hot_alloc = hot_cap;
+        }
+        UV_TRY(make_hot(rows.x16_hot, rows.xext_hot, rows.cmax_hot));
+        UV_CK(cudaEventRecord(rows.ready, st));
+        rows.hot_cap = hot_cap;
+        rows.hot_version = ix->version;
+      } else {
+        UV_CK(cudaStreamWaitEvent(st, rows.ready, 0));
+      }
+      x16_hot = rows.x16_hot;
+      xext_hot = rows.xext_hot;
+      cmax_hot = rows.cmax_hot;
+    }
+  }
+  const int64_t n_tiles1 = hot ? hot_cap / TN : (n_tiles + S - 1) / S;
   g_tc_last_sample = S;
   const int64_t n_groups1 = 2 * n_tiles1;
   float *tmax = nullptr, *theta = nullptr;
@@ -1294,11 +1375,21 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
     uvb::TcScanParams tp1 = tp;
     tp1.n_tiles = n_tiles1;
     tp1.n_groups = n_groups1;
-    tp1.tile_stride = S;
+    tp1.tile_stride = hot ? 1 : S;
+    alignas(64) CUtensorMap hmap_main, hmap_ext;
+    if (hot) {
+      // the sample: every slot a distinct record or a padding row
+      tp1.n = hot_cap;
+      tp1.cmax = cmax_hot;
+      UV_TRY(fp16_tensor_map(&hmap_main, x16_hot, hot_cap, kpad, 64, TN, true));
+      UV_TRY(fp16_tensor_map(&hmap_ext, xext_hot, hot_cap, 16, 16, TN, false));
+    }
     const dim3 grid1((unsigned)qtiles,
                      (unsigned)std::max<int64_t>(1, std::min<int64_t>(splits, n_tiles1 / 8)));
-    void *args[] = {&tp1, &tmap_main};
-    void *wargs[] = {&tp1, &kchunks, &tmap_a, &tmap_ax_lo, &tmap_main, &tmap_ext};
+    CUtensorMap *m1 = hot ? &hmap_main : &tmap_main;
+    CUtensorMap *e1 = hot ? &hmap_ext : &tmap_ext;
+    void *args[] = {&tp1, m1};
+    void *wargs[] = {&tp1, &kchunks, &tmap_a, &tmap_ax_lo, m1, e1};
     ProfScope ps("tc_pass1", st);
     UV_CK(cudaLaunchKernel(k1, grid1, dim3(wide ? uvb::tc_wide_threads() : uvb::tc_threads()),
                            wide ? wargs : args, smem, st));
@@ -2025,6 +2116,11 @@ int uv_set_tuning(const char *key, int64_t value) {
   if (std::strcmp(key, "encode_staged") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "encode_staged must be 0 or 1");
     uvb::g_encode_staged = (int)value;
+    return UV_OK;
+  }
+  if (std::strcmp(key, "tc_hot") == 0) {
+    if (value < 0 || value > 64) return fail(UV_EINVAL, "tc_hot must be 0..64");
+    g_tc_hot = (int)value;
     return UV_OK;
   }
   if (std::strcmp(key, "rescore_warp") == 0) {

@@ -165,6 +165,7 @@ extern std::atomic<int> g_tc_sample;        // uv_set_tuning("tc_sample")
 extern std::atomic<int> g_tc_prepare;       // uv_set_tuning("tc_prepare")
 extern std::atomic<int> g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
 extern std::atomic<int> g_rescore_warp;     // uv_set_tuning("rescore_warp")
+extern std::atomic<int> g_tc_hot;           // uv_set_tuning("tc_hot")
 extern std::atomic<bool> g_prof_on;
 extern std::vector<ProfRec> g_prof;
 
@@ -255,6 +256,11 @@ struct TcRows {
   int kpad = 0;
   uint64_t version = ~0ull;     // index version the rows were made from
   cudaEvent_t ready = nullptr;  // recorded after the rows were made
+  // pass 1's sample of the records of largest g (its own rows and constants)
+  uint16_t *x16_hot = nullptr, *xext_hot = nullptr;
+  float *cmax_hot = nullptr;
+  int64_t hot_alloc = 0, hot_cap = 0;
+  uint64_t hot_version = ~0ull;
 };
 
 struct uv_index {

@@ -546,6 +546,113 @@ __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPr
   xext[1] = make_uint4(0, 0, 0, 0);
 }
 
+// ---------------------------------------------------------------------------
+// The first pass's sample.  The k-th largest lower bound of any set of
+// distinct records is a score k records reach, so pass 1 may bound any
+// subset of the records; the tighter the threshold, the fewer candidates
+// pass 2 admits.  Instead of every S-th tile, pass 1 bounds the n/S records
+// of largest score scale g (rnorm / rescale, times the row norm for MIPS):
+// the records whose scores spread widest, which hold most of every query's
+// best scores when the norms vary (the heavy-tailed MIPS corpora).  They are
+// chosen by a two-level 12-bit histogram of g's bits (positive floats order
+// as unsigned integers) and copied, operand rows and bound constants, into
+// a compact sample that pass 1 streams like the full rows.  Records past the
+// sample's capacity are dropped and unfilled slots are padding rows (zero,
+// bound constant +inf), so any outcome is a subset of distinct records.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t hot_key(const TcPrepareParams &p, int64_t r) {
+  const float g = record_g(p, r);
+  return (isfinite(g) && g > 0.0f) ? __float_as_uint(g) : 0u;
+}
+
+// level 0: histogram of key >> 20 over the records; level 1: of
+// (key >> 8) & 4095 over the records whose key >> 20 is sel[0]
+__global__ void __launch_bounds__(256) tc_hot_hist_kernel(const TcPrepareParams p, int level,
+                                                          const uint32_t *sel, uint32_t *hist) {
+  __shared__ uint32_t h[4096];
+  for (int i = threadIdx.x; i < 4096; i += 256) h[i] = 0u;
+  __syncthreads();
+  const uint32_t b0 = level == 1 ? sel[0] : 0u;
+  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < p.n;
+       r += (int64_t)gridDim.x * 256) {
+    const uint32_t key = hot_key(p, r);
+    if (key == 0u) continue;
+    if (level == 0)
+      atomicAdd(&h[key >> 20], 1u);
+    else if ((key >> 20) == b0)
+      atomicAdd(&h[(key >> 8) & 4095u], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 4096; i += 256)
+    if (h[i] != 0u) atomicAdd(&hist[i], h[i]);
+}
+
+// One thread: the highest bin at which the count from the top reaches
+// `want` (level 0: sel[0] = bin, sel[1] = records in higher bins; level 1:
+// sel[2] = the sample's smallest key, (sel[0] << 20) | (bin << 8); a base
+// with fewer keyed records than `want` takes all of them, key 1).
+__global__ void tc_hot_pick_kernel(const uint32_t *hist, int64_t want, int level, uint32_t *sel) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t above = level == 1 ? sel[1] : 0u;
+  uint64_t acc = above;
+  int b = 4095;
+  for (; b >= 0; b--) {
+    acc += hist[b];
+    if (acc >= (uint64_t)want) break;
+  }
+  if (level == 0) {
+    if (b < 0) {  // every keyed record fits
+      sel[0] = 0u;
+      sel[1] = 0u;
+      sel[2] = 1u;
+      sel[3] = 1u;  // done: level 1 keeps sel[2]
+      return;
+    }
+    sel[0] = (uint32_t)b;
+    sel[1] = (uint32_t)(acc - hist[b]);
+    sel[3] = 0u;
+  } else if (sel[3] == 0u) {
+    sel[2] = (sel[0] << 20) | ((uint32_t)(b < 0 ? 0 : b) << 8);
+  }
+}
+
+// Records with key >= sel[2] append their operand row and bound constants to
+// the sample (at most cap of them).
+__global__ void __launch_bounds__(256) tc_hot_gather_kernel(const TcPrepareParams p,
+                                                            const uint32_t *sel, uint32_t *count,
+                                                            int64_t cap, uint16_t *x16_hot,
+                                                            uint16_t *xext_hot) {
+  const uint32_t t = sel[2];
+  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < p.n;
+       r += (int64_t)gridDim.x * 256) {
+    const uint32_t key = hot_key(p, r);
+    if (key == 0u || key < t) continue;
+    const uint32_t j = atomicAdd(count, 1u);
+    if ((int64_t)j >= cap) continue;
+    const uint4 *src = (const uint4 *)(p.x16 + r * p.kpad);
+    uint4 *dst = (uint4 *)(x16_hot + (int64_t)j * p.kpad);
+    for (int c = 0; c < p.kpad / 8; c++) dst[c] = __ldg(src + c);
+    const uint4 *se = (const uint4 *)(p.xext + r * TC_X);
+    uint4 *de = (uint4 *)(xext_hot + (int64_t)j * TC_X);
+    de[0] = __ldg(se);
+    de[1] = __ldg(se + 1);
+  }
+}
+
+// Unfilled sample slots: padding rows (zero row, bound constant +inf).
+__global__ void tc_hot_pad_kernel(const uint32_t *count, int64_t cap, int kpad, uint16_t *x16_hot,
+                                  uint16_t *xext_hot) {
+  const int64_t filled = min((int64_t)*count, cap);
+  for (int64_t j = filled + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < cap;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    uint4 *dst = (uint4 *)(x16_hot + j * kpad);
+    for (int c = 0; c < kpad / 8; c++) dst[c] = make_uint4(0, 0, 0, 0);
+    uint4 *de = (uint4 *)(xext_hot + j * TC_X);
+    de[0] = make_uint4(0x7C00u, 0, 0, 0);
+    de[1] = make_uint4(0, 0, 0, 0);
+  }
+}
+
 __global__ void __launch_bounds__(256)
     tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_pad, float *cmax) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
