@@ -67,6 +67,9 @@ def parse():
                     default="flat",
                     help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
                          "others measure the remaining configurations, one JSON line each")
+    ap.add_argument("--tune", action="append", default=[], metavar="KEY=VALUE",
+                    help="uv_set_tuning before the run (launch shapes and samples; results "
+                         "never depend on them), e.g. --tune tc_hot=1")
     ap.add_argument("--scan", choices=["auto", "exact", "tc"], default="auto",
                     help="auto: tensor-core prefilter where it is built; exact: the CUDA-core "
                          "kernel only; tc: prefilter wherever it is built")
@@ -243,6 +246,9 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     uv.set_tuning("tc_scan", {"auto": 0, "exact": 1, "tc": 2}[args.scan])
+    for kv in args.tune:
+        key, val = kv.split("=", 1)
+        uv.set_tuning(key, int(val))
     codec = uv.Codec(DIM, BITS, MEM, device=local)
     index = uv.Index(codec)
     index.reserve(hi - lo)
@@ -642,6 +648,9 @@ def run_secondary(args):
 
     uv = load()
     uv.set_tuning("tc_scan", {"auto": 0, "exact": 1, "tc": 2}[args.scan])
+    for kv in args.tune:
+        key, val = kv.split("=", 1)
+        uv.set_tuning(key, int(val))
     dev = torch.device("cuda", 0)
     rng = np.random.default_rng(0)
 

@@ -1271,20 +1271,31 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
       hp.norms = ix->norms;
       hp.x16 = x16;
       hp.xext = xext;
-      uint32_t *hist = nullptr, *sel = nullptr;
+      // blocks of the ordered compaction: at most 4095 (their counts and the
+      // total fit the one-CTA scan of 4096), spans of whole 256s
+      const int64_t span = std::max<int64_t>(256, ((n + 4094) / 4095 + 255) / 256 * 256);
+      const int cblocks = (int)((n + span - 1) / span);
+      uint32_t *hist = nullptr, *sel = nullptr, *keys = nullptr, *offs = nullptr;
       UV_TRY(sc.alloc(&hist, 4096 + 8));
+      UV_TRY(sc.alloc(&keys, (size_t)n));
+      UV_TRY(sc.alloc(&offs, (size_t)cblocks + 1));
       sel = hist + 4096;
       ProfScope ps("tc_prepare", st);
       const unsigned hg = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 1184));
       UV_CK(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (4096 + 8), st));
-      uvb::tc_hot_hist_kernel<<<hg, 256, 0, st>>>(hp, 0, sel, hist);
-      uvb::tc_hot_pick_kernel<<<1, 32, 0, st>>>(hist, hot_cap, 0, sel);
+      uvb::tc_hot_keys_kernel<<<hg, 256, 0, st>>>(hp, keys, hist);
+      uvb::tc_hot_pick_kernel<<<1, 256, 0, st>>>(hist, hot_cap, 0, sel);
       UV_CK(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 4096, st));
-      uvb::tc_hot_hist_kernel<<<hg, 256, 0, st>>>(hp, 1, sel, hist);
-      uvb::tc_hot_pick_kernel<<<1, 32, 0, st>>>(hist, hot_cap, 1, sel);
-      uvb::tc_hot_gather_kernel<<<hg, 256, 0, st>>>(hp, sel, sel + 4, hot_cap, hx, he);
+      uvb::tc_hot_hist_kernel<<<hg, 256, 0, st>>>(keys, n, sel, hist);
+      uvb::tc_hot_pick_kernel<<<1, 256, 0, st>>>(hist, hot_cap, 1, sel);
+      uvb::tc_hot_count_kernel<<<(unsigned)cblocks, 256, 0, st>>>(keys, n, span, sel, offs);
+      // one more count slot past the last block: the scan turns it into the total
+      UV_CK(cudaMemsetAsync(offs + cblocks, 0, sizeof(uint32_t), st));
+      uvb::tc_hot_scan_kernel<<<1, 1024, 0, st>>>(offs, cblocks + 1);
+      uvb::tc_hot_gather_kernel<<<(unsigned)cblocks, 256, 0, st>>>(hp, keys, span, sel, offs,
+                                                                    hot_cap, hx, he);
       uvb::tc_hot_pad_kernel<<<(unsigned)std::min<int64_t>((hot_cap + 255) / 256, 1184), 256, 0,
-                               st>>>(sel + 4, hot_cap, kpad, hx, he);
+                               st>>>(offs + cblocks, hot_cap, kpad, hx, he);
       uvb::tc_chunk_cmax_kernel<<<(unsigned)((hot_cap + 255) / 256), 256, 0, st>>>(
           he, hot_cap, hot_cap, hc);
       UV_CK(cudaGetLastError());

@@ -565,84 +565,188 @@ __device__ __forceinline__ uint32_t hot_key(const TcPrepareParams &p, int64_t r)
   return (isfinite(g) && g > 0.0f) ? __float_as_uint(g) : 0u;
 }
 
-// level 0: histogram of key >> 20 over the records; level 1: of
-// (key >> 8) & 4095 over the records whose key >> 20 is sel[0]
-__global__ void __launch_bounds__(256) tc_hot_hist_kernel(const TcPrepareParams p, int level,
-                                                          const uint32_t *sel, uint32_t *hist) {
+// The keys, and the level-0 histogram (key >> 20).  Lanes that meet in one
+// bin add once (__match_any_sync): the scales of a corpus fall in a few
+// bins, and plain shared atomics would serialize on them.
+__global__ void __launch_bounds__(256) tc_hot_keys_kernel(const TcPrepareParams p, uint32_t *keys,
+                                                          uint32_t *hist) {
   __shared__ uint32_t h[4096];
   for (int i = threadIdx.x; i < 4096; i += 256) h[i] = 0u;
   __syncthreads();
-  const uint32_t b0 = level == 1 ? sel[0] : 0u;
-  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < p.n;
-       r += (int64_t)gridDim.x * 256) {
-    const uint32_t key = hot_key(p, r);
-    if (key == 0u) continue;
-    if (level == 0)
-      atomicAdd(&h[key >> 20], 1u);
-    else if ((key >> 20) == b0)
-      atomicAdd(&h[(key >> 8) & 4095u], 1u);
+  const int64_t stride = (int64_t)gridDim.x * 256;
+  const int64_t n_round = (p.n + 255) / 256 * 256;  // whole warps in every round
+  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < n_round; r += stride) {
+    const uint32_t key = r < p.n ? hot_key(p, r) : 0u;
+    if (r < p.n) keys[r] = key;
+    const uint32_t bin = key >> 20;
+    const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+    if (key != 0u && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&h[bin], __popc(peers));
   }
   __syncthreads();
   for (int i = threadIdx.x; i < 4096; i += 256)
     if (h[i] != 0u) atomicAdd(&hist[i], h[i]);
 }
 
-// One thread: the highest bin at which the count from the top reaches
-// `want` (level 0: sel[0] = bin, sel[1] = records in higher bins; level 1:
-// sel[2] = the sample's smallest key, (sel[0] << 20) | (bin << 8); a base
-// with fewer keyed records than `want` takes all of them, key 1).
-__global__ void tc_hot_pick_kernel(const uint32_t *hist, int64_t want, int level, uint32_t *sel) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const uint64_t above = level == 1 ? sel[1] : 0u;
-  uint64_t acc = above;
-  int b = 4095;
-  for (; b >= 0; b--) {
-    acc += hist[b];
-    if (acc >= (uint64_t)want) break;
+// Level 1: histogram of (key >> 8) & 4095 over the keys in bin sel[0].
+__global__ void __launch_bounds__(256) tc_hot_hist_kernel(const uint32_t *keys, int64_t n,
+                                                          const uint32_t *sel, uint32_t *hist) {
+  __shared__ uint32_t h[4096];
+  for (int i = threadIdx.x; i < 4096; i += 256) h[i] = 0u;
+  __syncthreads();
+  const uint32_t b0 = sel[0];
+  const int64_t stride = (int64_t)gridDim.x * 256;
+  const int64_t n_round = (n + 255) / 256 * 256;
+  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < n_round; r += stride) {
+    const uint32_t key = r < n ? keys[r] : 0u;
+    const bool in = key != 0u && (key >> 20) == b0 && sel[3] == 0u;
+    const uint32_t bin = in ? (key >> 8) & 4095u : 0xffffffffu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+    if (in && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&h[bin], __popc(peers));
   }
-  if (level == 0) {
-    if (b < 0) {  // every keyed record fits
-      sel[0] = 0u;
-      sel[1] = 0u;
-      sel[2] = 1u;
-      sel[3] = 1u;  // done: level 1 keeps sel[2]
-      return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 4096; i += 256)
+    if (h[i] != 0u) atomicAdd(&hist[i], h[i]);
+}
+
+// One CTA of 256 threads: the highest bin at which the count from the top
+// reaches `want` (level 0: sel[0] = bin, sel[1] = records in higher bins;
+// level 1: sel[2] = the sample's smallest key, (sel[0] << 20) | (bin << 8);
+// a base with fewer keyed records than `want` takes all of them, key 1).
+__global__ void __launch_bounds__(256) tc_hot_pick_kernel(const uint32_t *hist, int64_t want,
+                                                          int level, uint32_t *sel) {
+  __shared__ unsigned long long part[256];
+  const int t = threadIdx.x;
+  // thread t holds bins [4080 - 16 t, 4096 - 16 t): higher bins on lower t
+  unsigned long long mine = 0;
+  for (int b = 4095 - 16 * t; b > 4095 - 16 * (t + 1); b--) mine += hist[b];
+  part[t] = mine;
+  __syncthreads();
+  if (t == 0) {
+    const unsigned long long above = (level == 1) ? sel[1] : 0ull;
+    if (level == 1 && sel[3] != 0u) return;
+    unsigned long long acc = above;
+    int tt = 0;
+    for (; tt < 256; tt++) {
+      if (acc + part[tt] >= (unsigned long long)want) break;
+      acc += part[tt];
     }
-    sel[0] = (uint32_t)b;
-    sel[1] = (uint32_t)(acc - hist[b]);
-    sel[3] = 0u;
-  } else if (sel[3] == 0u) {
-    sel[2] = (sel[0] << 20) | ((uint32_t)(b < 0 ? 0 : b) << 8);
+    int b = -1;
+    if (tt < 256) {
+      for (b = 4095 - 16 * tt; b > 4095 - 16 * (tt + 1); b--) {
+        acc += hist[b];
+        if (acc >= (unsigned long long)want) break;
+      }
+    }
+    if (level == 0) {
+      if (b < 0) {  // every keyed record fits
+        sel[0] = 0u;
+        sel[1] = 0u;
+        sel[2] = 1u;
+        sel[3] = 1u;
+        return;
+      }
+      sel[0] = (uint32_t)b;
+      sel[1] = (uint32_t)(acc - hist[b]);
+      sel[3] = 0u;
+    } else {
+      sel[2] = (sel[0] << 20) | ((uint32_t)(b < 0 ? 0 : b) << 8);
+    }
   }
 }
 
-// Records with key >= sel[2] append their operand row and bound constants to
-// the sample (at most cap of them).
-__global__ void __launch_bounds__(256) tc_hot_gather_kernel(const TcPrepareParams p,
-                                                            const uint32_t *sel, uint32_t *count,
-                                                            int64_t cap, uint16_t *x16_hot,
-                                                            uint16_t *xext_hot) {
+// The sample in record order: tc_hot_count_kernel counts each CTA's sample
+// records (CTA c covers records [c * span, (c + 1) * span)),
+// tc_hot_scan_kernel turns the counts into offsets, tc_hot_gather_kernel
+// copies every sample record's operand row and bound constants to its slot
+// (slots at or past cap are dropped).  Deterministic: the same index gives
+// the same sample, whatever the order the threads run in.
+__global__ void __launch_bounds__(256) tc_hot_count_kernel(const uint32_t *keys, int64_t n,
+                                                           int64_t span, const uint32_t *sel,
+                                                           uint32_t *counts) {
+  __shared__ uint32_t c;
+  if (threadIdx.x == 0) c = 0u;
+  __syncthreads();
   const uint32_t t = sel[2];
-  for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < p.n;
-       r += (int64_t)gridDim.x * 256) {
-    const uint32_t key = hot_key(p, r);
-    if (key == 0u || key < t) continue;
-    const uint32_t j = atomicAdd(count, 1u);
-    if ((int64_t)j >= cap) continue;
-    const uint4 *src = (const uint4 *)(p.x16 + r * p.kpad);
-    uint4 *dst = (uint4 *)(x16_hot + (int64_t)j * p.kpad);
-    for (int c = 0; c < p.kpad / 8; c++) dst[c] = __ldg(src + c);
-    const uint4 *se = (const uint4 *)(p.xext + r * TC_X);
-    uint4 *de = (uint4 *)(xext_hot + (int64_t)j * TC_X);
-    de[0] = __ldg(se);
-    de[1] = __ldg(se + 1);
+  const int64_t lo = (int64_t)blockIdx.x * span, hi = min(n, lo + span);
+  uint32_t mine = 0;
+  for (int64_t r = lo + threadIdx.x; r < hi; r += 256) mine += (keys[r] != 0u && keys[r] >= t);
+  atomicAdd(&c, mine);
+  __syncthreads();
+  if (threadIdx.x == 0) counts[blockIdx.x] = c;
+}
+
+__global__ void __launch_bounds__(1024) tc_hot_scan_kernel(uint32_t *counts, int blocks) {
+  __shared__ uint32_t s[1024];
+  const int t = threadIdx.x;
+  // up to 1024 x 4 blocks: each thread sums (then offsets) 4 consecutive counts
+  uint32_t v[4], tot = 0;
+  for (int j = 0; j < 4; j++) {
+    const int b = 4 * t + j;
+    v[j] = b < blocks ? counts[b] : 0u;
+    tot += v[j];
+  }
+  s[t] = tot;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const uint32_t x = t >= o ? s[t - o] : 0u;
+    __syncthreads();
+    s[t] += x;
+    __syncthreads();
+  }
+  uint32_t ex = s[t] - tot;
+  for (int j = 0; j < 4; j++) {
+    const int b = 4 * t + j;
+    if (b < blocks) counts[b] = ex;
+    ex += v[j];
+  }
+}
+
+__global__ void __launch_bounds__(256) tc_hot_gather_kernel(const TcPrepareParams p,
+                                                            const uint32_t *keys, int64_t span,
+                                                            const uint32_t *sel,
+                                                            const uint32_t *offs, int64_t cap,
+                                                            uint16_t *x16_hot,
+                                                            uint16_t *xext_hot) {
+  __shared__ uint32_t warp_tot[8];
+  __shared__ uint32_t base_s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t t = sel[2];
+  const int64_t lo = (int64_t)blockIdx.x * span, hi = min(p.n, lo + span);
+  if (tid == 0) base_s = offs[blockIdx.x];
+  __syncthreads();
+  for (int64_t r0 = lo; r0 < hi; r0 += 256) {
+    const int64_t r = r0 + tid;
+    const bool in = r < hi && keys[r] != 0u && keys[r] >= t;
+    const uint32_t ball = __ballot_sync(0xffffffffu, in);
+    if (lane == 0) warp_tot[warp] = __popc(ball);
+    __syncthreads();
+    uint32_t before = base_s;
+    for (int w = 0; w < warp; w++) before += warp_tot[w];
+    const uint32_t j = before + __popc(ball & ((1u << lane) - 1u));
+    if (in && (int64_t)j < cap) {
+      const uint4 *src = (const uint4 *)(p.x16 + r * p.kpad);
+      uint4 *dst = (uint4 *)(x16_hot + (int64_t)j * p.kpad);
+      for (int c = 0; c < p.kpad / 8; c++) dst[c] = __ldg(src + c);
+      const uint4 *se = (const uint4 *)(p.xext + r * TC_X);
+      uint4 *de = (uint4 *)(xext_hot + (int64_t)j * TC_X);
+      de[0] = __ldg(se);
+      de[1] = __ldg(se + 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t add = 0;
+      for (int w = 0; w < 8; w++) add += warp_tot[w];
+      base_s += add;
+    }
+    __syncthreads();
   }
 }
 
 // Unfilled sample slots: padding rows (zero row, bound constant +inf).
-__global__ void tc_hot_pad_kernel(const uint32_t *count, int64_t cap, int kpad, uint16_t *x16_hot,
-                                  uint16_t *xext_hot) {
-  const int64_t filled = min((int64_t)*count, cap);
+// offs_end is the scanned offset past the last CTA (the sample's size).
+__global__ void tc_hot_pad_kernel(const uint32_t *offs_end, int64_t cap, int kpad,
+                                  uint16_t *x16_hot, uint16_t *xext_hot) {
+  const int64_t filled = min((int64_t)*offs_end, cap);
   for (int64_t j = filled + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < cap;
        j += (int64_t)gridDim.x * blockDim.x) {
     uint4 *dst = (uint4 *)(x16_hot + j * kpad);

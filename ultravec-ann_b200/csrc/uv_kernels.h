@@ -321,13 +321,18 @@ const void *tc_prepare_records_fast_ptr(int bits);
 __global__ void tc_chunk_cmax_kernel(const uint16_t *xext, int64_t n, int64_t n_pad,
                                      float *cmax);
 // pass 1's sample: the records of largest score scale g (tcscan.cu)
-__global__ void tc_hot_hist_kernel(const TcPrepareParams p, int level, const uint32_t *sel,
+__global__ void tc_hot_keys_kernel(const TcPrepareParams p, uint32_t *keys, uint32_t *hist);
+__global__ void tc_hot_hist_kernel(const uint32_t *keys, int64_t n, const uint32_t *sel,
                                    uint32_t *hist);
 __global__ void tc_hot_pick_kernel(const uint32_t *hist, int64_t want, int level, uint32_t *sel);
-__global__ void tc_hot_gather_kernel(const TcPrepareParams p, const uint32_t *sel, uint32_t *count,
-                                     int64_t cap, uint16_t *x16_hot, uint16_t *xext_hot);
-__global__ void tc_hot_pad_kernel(const uint32_t *count, int64_t cap, int kpad, uint16_t *x16_hot,
-                                  uint16_t *xext_hot);
+__global__ void tc_hot_count_kernel(const uint32_t *keys, int64_t n, int64_t span,
+                                    const uint32_t *sel, uint32_t *counts);
+__global__ void tc_hot_scan_kernel(uint32_t *counts, int blocks);
+__global__ void tc_hot_gather_kernel(const TcPrepareParams p, const uint32_t *keys, int64_t span,
+                                     const uint32_t *sel, const uint32_t *offs, int64_t cap,
+                                     uint16_t *x16_hot, uint16_t *xext_hot);
+__global__ void tc_hot_pad_kernel(const uint32_t *offs_end, int64_t cap, int kpad,
+                                  uint16_t *x16_hot, uint16_t *xext_hot);
 // per-query k-th largest tile maximum; the n_tiles keys are staged in dynamic
 // shared memory (4 bytes each) when n_tiles <= kThetaSmemKeys
 constexpr int kThetaSmemKeys = 12288;
