@@ -1003,6 +1003,27 @@ int encode_tiled_fn(EncodeTiledFn *out) {
 
 // Tensor-core prefilter + exact rescoring (tcscan.cu).  Sets *used = false
 // when the configuration is outside what the kernels are built for.
+// The k-th largest of each query's n_tiles values (one list: q * n_tiles + i;
+// several lists gathered shard-major): one warp per query with the values
+// in registers up to 2048 of them, else one CTA per query with a radix
+// select.
+int theta_launch(const float *vals, int64_t n_tiles, int64_t nq, int k, float *theta, int lists,
+                 cudaStream_t st) {
+  const void *wk = uvb::tc_theta_warp_kernel_ptr(n_tiles);
+  if (wk != nullptr) {
+    void *args[] = {&vals, &n_tiles, &nq, &k, &theta, &lists};
+    UV_CK(cudaLaunchKernel(wk, dim3((unsigned)((nq + 7) / 8)), dim3(256), args, 0, st));
+    return UV_OK;
+  }
+  const size_t tsm = n_tiles <= uvb::kThetaSmemKeys ? (size_t)n_tiles * 4 : 0;
+  if (tsm > 48 * 1024)
+    UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)tsm));
+  uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(vals, n_tiles, nq, k, theta, lists);
+  UV_CK(cudaGetLastError());
+  return UV_OK;
+}
+
 // The prefilter in two phases, so that shards of one base can exchange their
 // first-pass bounds in between (uv_index_search_begin / uv_search_finish):
 // tc_begin runs pass 1 and the local threshold, tc_finish pass 2, the exact
@@ -1241,12 +1262,22 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
   // balances them at the 1M x 10k bench shape (measured optimum 4 at
   // k = 100, 10 at k = 10), capped at 10 and so that k*S stays well inside
   // the candidate lists, and the sample keeps at least 8k groups.
+  // The sample stride S: pass 1 costs about 1/S of pass 2; the candidates
+  // grow with S.  Every S-th tile (tc_hot 1) admits about k*S candidates, so
+  // S = round(sqrt(1600/k)), at most 10 and 900/k (measured optimum 4 at
+  // k = 100, 10 at k = 10 on the 1M x 10k bench shape); the sample of
+  // largest g keeps the candidates near k much longer (about 1.6k at S = 8,
+  // k = 100), so S = round(sqrt(6400/k)), at most 24 and 2400/k (measured:
+  // 8 at k = 100, 24 at k = 10).  The sample keeps at least 8k groups.
   const int fixed_sample = g_tc_sample.load();
+  const bool hot_default = g_tc_hot.load() != 1;
+  const double s_num = hot_default ? 6400.0 : 1600.0;
+  const int64_t s_cap = hot_default ? 24 : 10, s_kcap = hot_default ? 2400 : 900;
   int64_t S = fixed_sample > 0
                   ? fixed_sample
                   : std::max<int64_t>(1, std::min<int64_t>(
-                                             10, (int64_t)std::lround(std::sqrt(1600.0 / k))));
-  if (fixed_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, 900 / k));
+                                             s_cap, (int64_t)std::lround(std::sqrt(s_num / k))));
+  if (fixed_sample <= 0) S = std::max<int64_t>(1, std::min<int64_t>(S, s_kcap / k));
   while (S > 1 && 2 * ((n_tiles + S - 1) / S) * shards < 8 * (int64_t)k) S--;
   // Pass 1's sample: by default the n/S records of largest g, copied into
   // their own rows (tc_hot_*_kernel); tuning key tc_hot 1: every S-th tile
@@ -1407,12 +1438,7 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
   }
   {
     ProfScope ps("tc_theta", st);
-    const size_t tsm = n_groups1 <= uvb::kThetaSmemKeys ? (size_t)n_groups1 * 4 : 0;
-    if (tsm > 48 * 1024)
-      UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)tsm));
-    uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(tmax, n_groups1, nq, k, theta, 1);
-    UV_CK(cudaGetLastError());
+    UV_TRY(theta_launch(tmax, n_groups1, nq, k, theta, 1, st));
   }
   ts->k2 = k2;
   ts->grid = grid;
@@ -1767,13 +1793,7 @@ int uv_index_search_begin(const uv_index *ix, const float *queries, int64_t nq, 
       if (m != k) {
         float *theta_m = nullptr;
         UV_TRY(s->sc.alloc(&theta_m, (size_t)nq));
-        const int64_t ng = s->ts.n_groups1;
-        const size_t tsm = ng <= uvb::kThetaSmemKeys ? (size_t)ng * 4 : 0;
-        if (tsm > 48 * 1024)
-          UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
-        uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, st>>>(s->ts.tmax, ng, nq, m, theta_m, 1);
-        UV_CK(cudaGetLastError());
+        UV_TRY(theta_launch(s->ts.tmax, s->ts.n_groups1, nq, m, theta_m, 1, st));
         th = theta_m;
       }
       uvb::tc_bounds_kernel<<<(unsigned)nq, 256, 0, st>>>(s->ts.tmax, s->ts.n_groups1, nq, m, th,
@@ -1817,12 +1837,7 @@ int uv_search_set_bounds(uv_search *s, const float *gathered, int32_t n_shards) 
   // the k-th largest of the union of every shard's best m bounds
   ProfScope ps("tc_bounds", s->st);
   const int64_t per = (int64_t)n_shards * s->m;
-  const size_t tsm = per <= uvb::kThetaSmemKeys ? (size_t)per * 4 : 0;
-  if (tsm > 48 * 1024)
-    UV_CK(cudaFuncSetAttribute(uvb::tc_theta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)tsm));
-  uvb::tc_theta_kernel<<<(unsigned)nq, 256, tsm, s->st>>>(d_g, per, nq, k, s->ts.theta, n_shards);
-  UV_CK(cudaGetLastError());
+  UV_TRY(theta_launch(d_g, per, nq, k, s->ts.theta, n_shards, s->st));
   return UV_OK;
 }
 

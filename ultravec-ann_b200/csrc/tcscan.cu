@@ -871,6 +871,58 @@ __global__ void __launch_bounds__(256) tc_bounds_kernel(const float *tmax, int64
   for (int i = min(cnt, k) + threadIdx.x; i < k; i += 256) out[i] = th;
 }
 
+// The same k-th largest value for up to kThetaWarpKeys values per query, one
+// warp per query with the keys in registers: the answer's bits are fixed
+// from the top, each by counting the keys at or above the candidate (a
+// ballot-free count and one warp reduction per bit), with no shared-memory
+// histogram and no block barrier.
+template <int NJ>
+__global__ void __launch_bounds__(256) tc_theta_warp_kernel(const float *tmax, int64_t n_tiles,
+                                                            int64_t nq, int k, float *theta,
+                                                            int lists) {
+  const int lane = threadIdx.x & 31;
+  const int64_t q = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (q >= nq) return;  // whole warps
+  if (n_tiles < k) {
+    if (lane == 0) theta[q] = -INFINITY;
+    return;
+  }
+  const int64_t per = n_tiles / lists;
+  uint32_t v[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int64_t i = lane + 32 * j;
+    float x = -INFINITY;
+    if (i < n_tiles) {
+      if (lists == 1) {
+        x = tmax[q * n_tiles + i];
+      } else {
+        const int64_t l = i / per;
+        x = tmax[(l * nq + q) * per + (i - l * per)];
+      }
+    }
+    v[j] = i < n_tiles ? fkey(x) : 0u;
+  }
+  uint32_t prefix = 0u;
+  for (int bit = 31; bit >= 0; bit--) {
+    const uint32_t cand = prefix | (1u << bit);
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < NJ; j++) c += v[j] >= cand ? 1u : 0u;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c >= (uint32_t)k) prefix = cand;
+  }
+  if (lane == 0) theta[q] = fkey_inv(prefix);
+}
+
+const void *tc_theta_warp_kernel_ptr(int64_t n_tiles) {
+  if (n_tiles <= 32 * 8) return (const void *)tc_theta_warp_kernel<8>;
+  if (n_tiles <= 32 * 16) return (const void *)tc_theta_warp_kernel<16>;
+  if (n_tiles <= 32 * 32) return (const void *)tc_theta_warp_kernel<32>;
+  if (n_tiles <= 32 * 64) return (const void *)tc_theta_warp_kernel<64>;
+  return nullptr;
+}
+
 // ---------------------------------------------------------------------------
 // Exact scores of the candidates (simd.rs:183-262 association: 16 FMA chains
 // over 16-wide blocks, then the hsum256 tree; trellis.rs:1517 estimator) and

@@ -340,6 +340,9 @@ __global__ void tc_theta_kernel(const float *tmax, int64_t n_tiles, int64_t nq, 
                                 float *theta, int lists);
 __global__ void tc_bounds_kernel(const float *tmax, int64_t n_groups, int64_t nq, int k,
                                  const float *theta, float *bounds);
+// the same selection, one warp per query (8 per CTA of 256) with the keys in
+// registers, for up to 2048 values per query (null above)
+const void *tc_theta_warp_kernel_ptr(int64_t n_tiles);
 // bits 1..4; per_thread: one thread per candidate (long lists), else half a
 // warp per candidate (short lists)
 const void *tc_rescore_kernel_ptr(int bits, bool per_thread);
