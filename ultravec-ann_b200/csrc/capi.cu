@@ -1266,12 +1266,13 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
   // grow with S.  Every S-th tile (tc_hot 1) admits about k*S candidates, so
   // S = round(sqrt(1600/k)), at most 10 and 900/k (measured optimum 4 at
   // k = 100, 10 at k = 10 on the 1M x 10k bench shape); the sample of
-  // largest g keeps the candidates near k much longer (about 1.6k at S = 8,
-  // k = 100), so S = round(sqrt(6400/k)), at most 24 and 2400/k (measured:
-  // 8 at k = 100, 24 at k = 10).  The sample keeps at least 8k groups.
+  // largest g keeps the candidates near k much longer (about 1.9k at S =
+  // 12, k = 100), so S = round(sqrt(14400/k)), at most 24 and 2400/k
+  // (measured: 12 at k = 100, 24 at k = 10).  The sample keeps at least 8k
+  // groups.
   const int fixed_sample = g_tc_sample.load();
   const bool hot_default = g_tc_hot.load() != 1;
-  const double s_num = hot_default ? 6400.0 : 1600.0;
+  const double s_num = hot_default ? 14400.0 : 1600.0;
   const int64_t s_cap = hot_default ? 24 : 10, s_kcap = hot_default ? 2400 : 900;
   int64_t S = fixed_sample > 0
                   ? fixed_sample
