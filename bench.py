@@ -67,6 +67,10 @@ def parse():
                     default="flat",
                     help="flat: the headline 1M x 10k d=128 MIPS step (the default line); the "
                          "others measure the remaining configurations, one JSON line each")
+    ap.add_argument("--cell", default=None, metavar="BITS,MEM",
+                    help="encode-sweep: run this one cell only (e.g. 2,16)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="encode-sweep: rows per cell (0: sized to about a second)")
     ap.add_argument("--tune", action="append", default=[], metavar="KEY=VALUE",
                     help="uv_set_tuning before the run (launch shapes and samples; results "
                          "never depend on them), e.g. --tune tc_hot=1")
@@ -782,7 +786,7 @@ def run_secondary(args):
                                                    f"{(n // ns) * ns} records"}})
             del ix, oc, enc, big
     else:
-        run_encode_sweep(uv, dev, emit)
+        run_encode_sweep(uv, dev, emit, args)
 
 def _tc_roofline(uv, flops_full, nq_tiles_flops, peaks):
     """Tensor-pipe roofline of the prefilter passes of the last profiled
@@ -991,7 +995,7 @@ def run_ivf(uv, dev, emit, rng):
             "clocks": clk})
 
 
-def run_encode_sweep(uv, dev, emit):
+def run_encode_sweep(uv, dev, emit, args):
     """The trellis-memory sweep: 1M rows d=128 N(0,1) from seed 1 (a prefix
     where a cell would take more than about a second), b = 2 at M in {2, 4,
     8, 12, 16} and the reference's whole 2-, 3- and 4-bit ladder M = 4..16
@@ -1013,9 +1017,13 @@ def run_encode_sweep(uv, dev, emit):
     smax = peaks.get("sm_max_mhz", 1965.0)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     cells = [(2, 2)] + [(b, m) for b in (2, 3, 4) for m in (4, 6, 8, 10, 12, 14, 16)]
+    if args.cell:
+        cells = [tuple(int(v) for v in args.cell.split(","))]
     for bits, mem in cells:
         w = mem + bits
         n = int(min(1_000_000, max(2000, 2e11 / (d * 2 ** w))))
+        if args.rows > 0:
+            n = min(args.rows, 1_000_000)
         codec = uv.Codec(d, bits, mem)
         index = uv.Index(codec)
         index.reserve(n)
