@@ -666,7 +666,7 @@ def run_secondary(args):
     if args.workload == "wide":
         run_wide(uv, dev, emit, rng)
     elif args.workload == "ivf":
-        run_ivf(uv, dev, emit, rng)
+        run_ivf(uv, dev, emit, rng, args)
     elif args.workload == "shortlist":
         n, nq, nlist = 1_000_000, 10_000, 1024
         base_np, query_np = make_data(n, nq)
@@ -901,7 +901,7 @@ def run_wide(uv, dev, emit, rng):
         del index, codec
 
 
-def run_ivf(uv, dev, emit, rng):
+def run_ivf(uv, dev, emit, rng, args=None):
     """1M rows, d=1536 padded to 2048: 64 unit Gaussian centres + 0.3 N(0,1),
     renormalized; k-means nlist=4096 (seed 42, 5 rounds), centered lists,
     b=2, M=8; 10k-query top-10 at nprobe 1/4/16/64.  Per nprobe: queries/s,
@@ -919,6 +919,9 @@ def run_ivf(uv, dev, emit, rng):
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     fp32_peak = sms * FP32_LANES_PER_SM * 2 * smax * 1e6
     n, nq, d, d_pad, nlist = 1_000_000, 10_000, 1536, 2048, 4096
+    if args is not None and args.n_base != N_BASE:  # a smaller case (profiling)
+        n, nq = args.n_base, args.n_query
+        nlist = max(256, min(4096, n // 244))
     x = ivf_data(rng, n, nq, d, d_pad)
     base = torch.from_numpy(x[:n]).to(dev)
     qs = torch.from_numpy(x[n:]).to(dev)
@@ -969,7 +972,8 @@ def run_ivf(uv, dev, emit, rng):
                                        q_np[:sample], nprobe, 10, threads=threads)
         cpu_q = sample / (time.perf_counter() - t0)
         gi, gs = ids[:sample].cpu().numpy(), scores[:sample].cpu().numpy()
-        emit("ivf-1Mx10k-d2048-nlist4096", {
+        emit("ivf-1Mx10k-d2048-nlist4096" if n == 1_000_000 and nq == 10_000 else
+             f"ivf-{n}x{nq}-d2048-nlist{nlist}", {
             "nprobe": nprobe, "value": nq / ms * 1e3, "unit": "queries/s",
             "queries_s": nq / ms * 1e3, "search_ms": ms, "kmeans_s": km_s,
             "build_s": build_s, "centered": True, "k": 10, "bits": 2, "mem": 8,
