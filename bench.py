@@ -948,7 +948,9 @@ def run_ivf(uv, dev, emit, rng, args=None):
     lists = {"codes": ex["codes"], "start": ex["start"], "rescale": ex["rescale"],
              "rnorm": ex["rnorm"]}
     fams = ("prep_queries", "ivf_cosine", "ivf_select", "ivf_bucket", "ivf_pair_qm",
-            "ivf_scan", "merge_topk")
+            "ivf_scan", "merge_topk", "ivf_tc_prepare", "ivf_tc_pairs", "ivf_tc_scan",
+            "ivf_tc_select")
+    kpad = (d_pad + 63) // 64 * 64
     sample = max(16, threads)
     for nprobe in (1, 4, 16, 64):
         clocks = ClockSampler(0)
@@ -960,12 +962,44 @@ def run_ivf(uv, dev, emit, rng, args=None):
         torch.cuda.synchronize()
         kern = {f: round(uv.profile_read(f)[0], 3) for f in fams}
         launches = uv.profile_read("*")[1]
+        exact = uv.profile_read("tc_candidates")[1]
+        over_slot, over_cand = uv.profile_read("ivf_tc_overflow")
         uv.profile_enable(False)
         probed = ivf.probe(qs, nprobe)
         probed = probed.cpu().numpy() if hasattr(probed, "cpu") else np.asarray(probed)
         scanned = float(np.where(probed >= 0, sizes[np.maximum(probed, 0)], 0).sum()) / nq
-        scan_ms = kern["ivf_scan"]
         flops = 2.0 * scanned * nq * d_pad
+        tc_ms = kern["ivf_tc_scan"]
+        if tc_ms > 0:
+            # tc_ivf_kernel: per item (list, <= 128 pairs, <= 512 records) the
+            # range's fp16 record rows and bound constants once, the pairs'
+            # fp16 query rows once per 256-record tile
+            pairs = np.bincount(probed[probed >= 0].ravel(), minlength=nlist).astype(np.float64)
+            ranges = np.maximum(1, np.ceil(sizes / 512.0))
+            groups = np.ceil(pairs / 128.0)
+            tiles = np.ceil(np.minimum(sizes, 512) / 256.0)
+            alg_bytes = float((groups * sizes * (kpad * 2 + 32)).sum()
+                              + (pairs * ranges * tiles * kpad * 2).sum())
+            roof = {"bound": "hbm", "kernel": "tc_ivf_kernel (IVF list scan, fp16 bounds)",
+                    "achieved": alg_bytes / (tc_ms / 1e3) / 1e9,
+                    "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                    "frac": alg_bytes / (tc_ms / 1e3) / 1e9 / peaks["hbm_gbs"]
+                    if peaks.get("hbm_gbs") else None,
+                    "bytes_per_search": alg_bytes, "scan_ms": tc_ms,
+                    "useful_tflops": flops / (tc_ms / 1e3) / 1e12,
+                    "tensor_frac_of_bf16_peak": flops / (tc_ms / 1e3) / 1e12
+                    / peaks["bf16_tflops"] if peaks.get("bf16_tflops") else None,
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+                    "traffic": None}
+        else:
+            scan_ms = kern["ivf_scan"]
+            roof = {"bound": "fp32", "kernel": "chunked_scan_kernel (IVF list scan)",
+                    "achieved": flops / (scan_ms / 1e3) / 1e12 if scan_ms > 0 else None,
+                    "peak": fp32_peak / 1e12, "unit": "TFLOP/s",
+                    "frac": flops / (scan_ms / 1e3) / fp32_peak if scan_ms > 0 else None,
+                    "flops_per_search": flops, "scan_ms": scan_ms,
+                    "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA x 2 x "
+                                   f"{smax:.0f} MHz", "traffic": None}
         e2e_ms = _e2e_host(lambda q: ivf.search(q, 10, nprobe), q_host)
         t0 = time.perf_counter()
         wids, wsc = oc.ivf_search_topk(cen_np, ex["list_off"], ex["ids"], lists, True,
@@ -979,13 +1013,10 @@ def run_ivf(uv, dev, emit, rng, args=None):
             "build_s": build_s, "centered": True, "k": 10, "bits": 2, "mem": 8,
             "kernels_ms": kern, "gpu_launches": launches, "list_sizes": list_stats,
             "records_scanned_per_query": scanned,
-            "roofline": {"bound": "fp32", "kernel": "chunked_scan_kernel (IVF list scan)",
-                         "achieved": flops / (scan_ms / 1e3) / 1e12 if scan_ms > 0 else None,
-                         "peak": fp32_peak / 1e12, "unit": "TFLOP/s",
-                         "frac": flops / (scan_ms / 1e3) / fp32_peak if scan_ms > 0 else None,
-                         "flops_per_search": flops, "scan_ms": scan_ms,
-                         "peak_source": f"nominal {sms} SMs x {FP32_LANES_PER_SM} FMA x 2 x "
-                                        f"{smax:.0f} MHz", "traffic": None},
+            "records_scored_exactly_per_query": exact / nq if tc_ms > 0 else scanned,
+            "tc_overflow_queries": {"slot_store": int(over_slot), "candidates": int(over_cand)}
+            if tc_ms > 0 else None,
+            "roofline": roof,
             "e2e": {"value": nq / e2e_ms * 1e3, "unit": "queries/s",
                     "h2d_bytes_per_step": nq * d_pad * 4, "d2h_bytes_per_step": nq * 10 * 12,
                     "api": "uv_ivf_search with host buffers"},

@@ -282,9 +282,16 @@ int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t
  * "ivf_tc_probe" 1 makes the IVF probe and the k-means / IVF assignment
  * compute every cosine or dot on the CUDA cores (0 automatic: tensor-core
  * dots, exact values for the centroids that can still be chosen, the same
- * lists and assignments);
+ * lists and assignments); "ivf_tc" selects the IVF list scan (0 automatic:
+ * the tensor-core bounds with exact rescoring for rows of 256 or more
+ * coordinates and k <= 32; 1 the CUDA-core scan of every record; 2 the
+ * tensor-core scan wherever it is built: k <= 32 and widths that are a
+ * multiple of 16; its record rows, (2 x dim rounded up to 64 + 32) bytes per
+ * record, are made on the first such search and kept with the lists);
  * "tc_sample" fixes the prefilter's first-pass sampling stride S (0
- * automatic: round(sqrt(1600/k)), at most 10); "tc_hot" chooses that
+ * automatic: round(sqrt(14400/k)), at most 24 and 2400/k, with the sample
+ * of largest g; round(sqrt(1600/k)), at most 10 and 900/k, with every S-th
+ * tile); "tc_hot" chooses that
  * sample (0 automatic: the n/S records of largest score scale g, copied
  * into their own rows when the index changes; 1: every S-th record tile;
  * N >= 2: the n/N records of largest g); "tc_prepare" 1 makes the

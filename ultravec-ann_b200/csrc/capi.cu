@@ -26,9 +26,11 @@ std::atomic<int> g_coset_nearest{0};
 std::atomic<int> g_tc_sample{0};
 std::atomic<int> g_tc_prepare{0};
 std::atomic<int> g_ivf_tc_probe{0};
+std::atomic<int> g_ivf_tc{0};
 std::atomic<int> g_rescore_warp{0};
 std::atomic<int> g_tc_hot{0};
 std::atomic<int64_t> g_tc_last_candidates{0};
+std::atomic<int64_t> g_ivf_tc_overflow{0};
 std::atomic<int64_t> g_tc_last_sample{1};  // pass-1 tile stride of the last prefilter search
 std::atomic<bool> g_prof_on{false};
 std::vector<ProfRec> g_prof;
@@ -2120,6 +2122,11 @@ int uv_set_tuning(const char *key, int64_t value) {
     g_ivf_tc_probe = (int)value;
     return UV_OK;
   }
+  if (std::strcmp(key, "ivf_tc") == 0) {
+    if (value < 0 || value > 2) return fail(UV_EINVAL, "ivf_tc must be 0, 1 or 2");
+    g_ivf_tc = (int)value;
+    return UV_OK;
+  }
   if (std::strcmp(key, "tc_prepare") == 0) {
     if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_prepare must be 0 or 1");
     g_tc_prepare = (int)value;
@@ -2181,6 +2188,15 @@ int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
     // statistic of the last tensor-core search: pass 1 bounded every S-th tile
     *total_ms = 0.0;
     *launches = g_tc_last_sample.load();
+    return UV_OK;
+  }
+  if (std::strcmp(kernel, "ivf_tc_overflow") == 0) {
+    // statistic of the last tensor-core IVF list scan: queries whose kept
+    // records overflowed a slot's store (total_ms) or the per-query
+    // candidate store (launches); either sends the search to the CUDA-core scan
+    const int64_t v = g_ivf_tc_overflow.load();
+    *total_ms = (double)(v >> 32);
+    *launches = v & 0xffffffffll;
     return UV_OK;
   }
   if (std::strcmp(kernel, "tc_candidates") == 0) {

@@ -164,6 +164,9 @@ extern std::atomic<int> g_coset_nearest;    // uv_set_tuning("coset_nearest")
 extern std::atomic<int> g_tc_sample;        // uv_set_tuning("tc_sample")
 extern std::atomic<int> g_tc_prepare;       // uv_set_tuning("tc_prepare")
 extern std::atomic<int> g_ivf_tc_probe;     // uv_set_tuning("ivf_tc_probe")
+extern std::atomic<int> g_ivf_tc;           // uv_set_tuning("ivf_tc")
+extern std::atomic<int64_t> g_tc_last_candidates;  // uv_profile_read("tc_candidates")
+extern std::atomic<int64_t> g_ivf_tc_overflow;     // uv_profile_read("ivf_tc_overflow")
 extern std::atomic<int> g_rescore_warp;     // uv_set_tuning("rescore_warp")
 extern std::atomic<int> g_tc_hot;           // uv_set_tuning("tc_hot")
 extern std::atomic<bool> g_prof_on;
@@ -220,6 +223,24 @@ struct uv_codec {
   std::string plan_why;
 };
 
+// The tensor-core prefilter's fp16 operand rows (tcscan.cu / tcwide.cu),
+// kept between searches: one set per score mode (the MIPS rows carry the row
+// norm), rebuilt when the index has changed since they were made.
+struct TcRows {
+  uint16_t *x16 = nullptr;      // cap x kpad
+  uint16_t *xext = nullptr;     // cap x 16
+  float *cmax = nullptr;        // cap / 32 chunk maxima of the bound constants
+  int64_t cap = 0, n_pad = 0;   // rows allocated / rows made
+  int kpad = 0;
+  uint64_t version = ~0ull;     // index version the rows were made from
+  cudaEvent_t ready = nullptr;  // recorded after the rows were made
+  // pass 1's sample of the records of largest g (its own rows and constants)
+  uint16_t *x16_hot = nullptr, *xext_hot = nullptr;
+  float *cmax_hot = nullptr;
+  int64_t hot_alloc = 0, hot_cap = 0;
+  uint64_t hot_version = ~0ull;
+};
+
 // The IVF index (capi_ivf.cu): centroids and list-major posting lists.
 struct uv_ivf {
   const uv_codec *codec = nullptr;
@@ -243,25 +264,12 @@ struct uv_ivf {
   mutable uint16_t *c16 = nullptr;   // c_pad x kpad
   mutable uint16_t *cext = nullptr;  // c_pad x 16, zero
   mutable int64_t c_pad = 0;
+  // the records' fp16 operand rows for the tensor-core list scan (made on
+  // the first search that uses them, freed with the lists) and their scale
+  mutable TcRows list_rows;
+  mutable float *list_scale = nullptr;
 };
 
-// The tensor-core prefilter's fp16 operand rows (tcscan.cu / tcwide.cu),
-// kept between searches: one set per score mode (the MIPS rows carry the row
-// norm), rebuilt when the index has changed since they were made.
-struct TcRows {
-  uint16_t *x16 = nullptr;      // cap x kpad
-  uint16_t *xext = nullptr;     // cap x 16
-  float *cmax = nullptr;        // cap / 32 chunk maxima of the bound constants
-  int64_t cap = 0, n_pad = 0;   // rows allocated / rows made
-  int kpad = 0;
-  uint64_t version = ~0ull;     // index version the rows were made from
-  cudaEvent_t ready = nullptr;  // recorded after the rows were made
-  // pass 1's sample of the records of largest g (its own rows and constants)
-  uint16_t *x16_hot = nullptr, *xext_hot = nullptr;
-  float *cmax_hot = nullptr;
-  int64_t hot_alloc = 0, hot_cap = 0;
-  uint64_t hot_version = ~0ull;
-};
 
 struct uv_index {
   const uv_codec *codec = nullptr;

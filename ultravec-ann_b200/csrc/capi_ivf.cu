@@ -136,6 +136,13 @@ void free_lists(uv_ivf *ix) {
   ix->ids = nullptr;
   ix->d_off = nullptr;
   ix->n = 0;
+  // the tensor-core list scan's rows were made from these lists
+  cudaFree(ix->list_rows.x16);
+  cudaFree(ix->list_rows.xext);
+  cudaFree(ix->list_scale);
+  if (ix->list_rows.ready != nullptr) cudaEventDestroy(ix->list_rows.ready);
+  ix->list_rows = TcRows();
+  ix->list_scale = nullptr;
 }
 
 // Per row of a (m x d): the np best of nlist centroids by exact score, via
@@ -404,10 +411,249 @@ int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld,
   return UV_OK;
 }
 
+// The records' fp16 operand rows and bound constants for the tensor-core
+// list scan (tc_prepare_records*_kernel with g = rnorm / rescale, or 1 /
+// rescale for uncentered lists, as the list scan scores them) and their
+// power-of-two scale s; made on the first search that uses them, kept until
+// the lists change (free_lists).  Later searches on other streams wait for
+// the event recorded after they were made.
+int list_rows(const uv_ivf *ix, cudaStream_t st, Scratch &sc, const TcRows **out,
+              const float **scale) {
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int kpad = (d + 63) / 64 * 64;
+  const int64_t n = ix->n;
+  const int64_t n_pad = (n + 255) / 256 * 256;
+  std::lock_guard<std::mutex> lk(ix->tc_mu);
+  TcRows &r = ix->list_rows;
+  if (r.x16 == nullptr) {
+    UV_CK(cudaMalloc((void **)&r.x16, sizeof(uint16_t) * (size_t)n_pad * kpad));
+    UV_CK(cudaMalloc((void **)&r.xext, sizeof(uint16_t) * (size_t)n_pad * 16));
+    UV_CK(cudaMalloc((void **)&ix->list_scale, sizeof(float)));
+    uint32_t *gmax = nullptr;
+    UV_TRY(sc.alloc(&gmax, 1));
+    UV_CK(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), st));
+    uvb::TcPrepareParams pp;
+    std::memset(&pp, 0, sizeof(pp));
+    pp.mem = c->cfg.mem;
+    pp.bits = c->cfg.bits;
+    pp.code_stride = c->code_stride;
+    pp.mips = 0;
+    pp.dim = d;
+    pp.kpad = kpad;
+    pp.n = n;
+    pp.n_pad = n_pad;
+    pp.eps = 1.5e-3;
+    pp.code_absmax = c->code_absmax;
+    pp.codes = ix->codes;
+    pp.start = ix->start;
+    pp.code = c->d_table;
+    pp.rescale = ix->rescale;
+    pp.rnorm = ix->centered ? ix->rnorm : nullptr;
+    pp.gmax_bits = gmax;
+    pp.x16 = r.x16;
+    pp.xext = r.xext;
+    void *args[] = {&pp};
+    ProfScope ps("ivf_tc_prepare", st);
+    UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
+                           dim3(256), args, 0, st));
+    uvb::tc_scale_kernel<<<1, 32, 0, st>>>(gmax, c->code_absmax, ix->list_scale);
+    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits);
+    const size_t tsm = (size_t)4 << (c->cfg.mem + c->cfg.bits);
+    if (fk != nullptr && tsm <= 64 * 1024 && g_tc_prepare != 1) {
+      UV_CK(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
+      UV_CK(cudaLaunchKernel(fk, dim3((unsigned)((n_pad + 255) / 256)), dim3(256), args, tsm, st));
+    } else {
+      UV_CK(cudaLaunchKernel((const void *)uvb::tc_prepare_records_kernel,
+                             dim3((unsigned)((n_pad + 127) / 128)), dim3(128), args, 0, st));
+    }
+    UV_CK(cudaGetLastError());
+    if (r.ready == nullptr) UV_CK(cudaEventCreateWithFlags(&r.ready, cudaEventDisableTiming));
+    UV_CK(cudaEventRecord(r.ready, st));
+    r.cap = r.n_pad = n_pad;
+    r.kpad = kpad;
+  } else {
+    UV_CK(cudaStreamWaitEvent(st, r.ready, 0));
+  }
+  *out = &r;
+  *scale = ix->list_scale;
+  return UV_OK;
+}
+
+// The bucketed pairs of one search, as search_device makes them.
+struct PairBuckets {
+  int64_t npairs = 0, n_items = 0, n_rslots = 0, range_size = 0;
+  const int32_t *pair_query = nullptr, *pair_slot = nullptr, *pair_off = nullptr;
+  const int64_t *list_rbase = nullptr, *row_off = nullptr;
+  const float *pair_qm = nullptr;
+  const int32_t *item_list = nullptr, *item_pair = nullptr, *item_npairs = nullptr,
+                *item_range = nullptr, *n_items_dev = nullptr;
+};
+
+// Whether the tensor-core list scan takes a search (tuning key ivf_tc: 0
+// automatic -- rows of at least 256 coordinates --, 1 never, 2 whenever it
+// can): k <= 32, width a multiple of 16 (the exact rescoring runs 16 FMA
+// chains without a scalar tail), and the rescoring's shared memory.
+bool use_tc_scan(const uv_ivf *ix, int k) {
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const int mode = g_ivf_tc.load();
+  if (mode == 1 || k > 32 || d % 16 != 0 || ix->n > INT32_MAX - 1024) return false;
+  if (uvb::ivf_select_smem_bytes(c->table_len, c->code_stride) > 200 * 1024) return false;
+  return mode == 2 || d >= 256;
+}
+
+// The tensor-core list scan (ivftc.cu) over the bucketed pairs: per-slot
+// thresholds and kept records (tc_ivf_kernel), then per query the shared
+// threshold, the exact scores and the top k (ivf_select_kernel), written to
+// d_ids / d_scores.  *fallback is set when a store overflowed; the caller
+// then runs the CUDA-core scan, whose results replace everything written.
+int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, int q_stride,
+                 const uint32_t *degen, const PairBuckets &b, int64_t *d_ids, float *d_scores,
+                 cudaStream_t st, Scratch &sc, bool *fallback) {
+  *fallback = false;
+  const uv_codec *c = ix->codec;
+  const int d = c->cfg.dim;
+  const TcRows *rows = nullptr;
+  const float *scale = nullptr;
+  UV_TRY(list_rows(ix, st, sc, &rows, &scale));
+  const int kpad = rows->kpad;
+  // the pairs' fp16 query rows (bucketed order; at least one box of rows)
+  const int64_t rows_a = std::max<int64_t>(b.npairs, uvb::kIvfTcRows);
+  uint16_t *pa16 = nullptr, *ax = nullptr;
+  int32_t *pair_of = nullptr;
+  UV_TRY(sc.alloc(&pa16, (size_t)rows_a * kpad));
+  UV_TRY(sc.alloc(&ax, (size_t)uvb::kIvfTcRows * 16));
+  UV_TRY(sc.alloc(&pair_of, (size_t)b.npairs));
+  UV_CK(cudaMemsetAsync(pair_of, 0xff, sizeof(int32_t) * (size_t)b.npairs, st));  // -1: no pair
+  {
+    ProfScope ps("ivf_tc_pairs", st);
+    const int64_t chunks = b.npairs * (kpad / 8);
+    uvb::ivf_pair_rows16_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((chunks + 255) / 256, 148 * 32)),
+                                  256, 0, st>>>(q_r, q_stride, degen, b.pair_query, b.npairs, d,
+                                                kpad, pa16);
+    uvb::ivf_neg_slice_kernel<<<(uvb::kIvfTcRows * 16 + 255) / 256, 256, 0, st>>>(ax);
+    uvb::ivf_pair_of_kernel<<<blocks(b.npairs, 256), 256, 0, st>>>(b.pair_slot, b.npairs, pair_of);
+    UV_CK(cudaGetLastError());
+  }
+  alignas(64) CUtensorMap tmap_a, tmap_ax, tmap_b, tmap_bx;
+  UV_TRY(fp16_tensor_map(&tmap_a, pa16, rows_a, kpad, 64, 32, true));
+  UV_TRY(fp16_tensor_map(&tmap_ax, ax, uvb::kIvfTcRows, 16, 16, uvb::kIvfTcRows, false));
+  UV_TRY(fp16_tensor_map(&tmap_b, rows->x16, rows->n_pad, kpad, 64, 32, true));
+  UV_TRY(fp16_tensor_map(&tmap_bx, rows->xext, rows->n_pad, 16, 16, 32, false));
+  // per-slot thresholds and the store of kept records
+  const int64_t nslots = std::max<int64_t>(b.n_rslots, 1);
+  const int64_t cand_cap = b.n_rslots * (int64_t)(k + 16) + 65536;
+  float *slot_theta = nullptr, *cand_lb = nullptr, *cand_ub = nullptr;
+  int32_t *slot_cnt = nullptr;
+  int64_t *slot_base = nullptr;
+  uint32_t *cand_rec = nullptr;
+  // kept-record count, scored count, err | queries over (slot), queries over (candidates)
+  unsigned long long *flags = nullptr;
+  UV_TRY(sc.alloc(&slot_theta, (size_t)nslots));
+  UV_TRY(sc.alloc(&slot_cnt, (size_t)nslots));
+  UV_TRY(sc.alloc(&slot_base, (size_t)nslots));
+  UV_TRY(sc.alloc(&cand_rec, (size_t)cand_cap));
+  UV_TRY(sc.alloc(&cand_lb, (size_t)cand_cap));
+  UV_TRY(sc.alloc(&cand_ub, (size_t)cand_cap));
+  UV_TRY(sc.alloc(&flags, 4));
+  UV_CK(cudaMemsetAsync(flags, 0, sizeof(unsigned long long) * 4, st));
+  int *err = (int *)(flags + 2), *n_over = err + 1;
+  if (b.n_items > 0) {
+    uvb::TcIvfParams tp;
+    std::memset(&tp, 0, sizeof(tp));
+    tp.k = k;
+    tp.kchunks = kpad / 64;
+    tp.range_size = b.range_size;
+    tp.n_items = b.n_items_dev;
+    tp.item_list = b.item_list;
+    tp.item_pair = b.item_pair;
+    tp.item_npairs = b.item_npairs;
+    tp.item_range = b.item_range;
+    tp.list_off = ix->d_off;
+    tp.list_pair_off = b.pair_off;
+    tp.list_rbase = b.list_rbase;
+    tp.pair_query = b.pair_query;
+    tp.pair_qm = b.pair_qm;
+    tp.degenerate = degen;
+    tp.scale = scale;
+    tp.xext = rows->xext;
+    tp.slot_theta = slot_theta;
+    tp.slot_cnt = slot_cnt;
+    tp.slot_base = slot_base;
+    tp.cand_rec = cand_rec;
+    tp.cand_lb = cand_lb;
+    tp.cand_ub = cand_ub;
+    tp.cand_used = flags;
+    tp.cand_cap = cand_cap;
+    tp.err = err;
+    const void *kfn = uvb::tc_ivf_kernel_ptr(k);
+    if (kfn == nullptr) return fail(UV_EUNSUPPORTED, "no tensor-core list scan for this k");
+    const size_t smem = uvb::tc_ivf_smem_bytes();
+    UV_CK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    void *args[] = {&tp, &tmap_a, &tmap_ax, &tmap_b, &tmap_bx};
+    ProfScope ps("ivf_tc_scan", st);
+    UV_CK(cudaLaunchKernel(kfn, dim3((unsigned)b.n_items), dim3(uvb::tc_ivf_threads()), args, smem,
+                           st));
+  }
+  {
+    uvb::IvfSelectParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    sp.dim = d;
+    sp.mem = c->cfg.mem;
+    sp.bits = c->cfg.bits;
+    sp.code_stride = c->code_stride;
+    sp.q_stride = q_stride;
+    sp.k = k;
+    sp.np = np;
+    sp.table_len = c->table_len;
+    sp.nq = nq;
+    sp.q_r = q_r;
+    sp.degenerate = degen;
+    sp.pair_of = pair_of;
+    sp.row_off = b.row_off;
+    sp.pair_qm = b.pair_qm;
+    sp.slot_theta = slot_theta;
+    sp.slot_cnt = slot_cnt;
+    sp.slot_base = slot_base;
+    sp.cand_rec = cand_rec;
+    sp.cand_lb = cand_lb;
+    sp.cand_ub = cand_ub;
+    sp.codes = ix->codes;
+    sp.start = ix->start;
+    sp.code = c->d_table;
+    sp.rescale = ix->rescale;
+    sp.rnorm = ix->centered ? ix->rnorm : nullptr;
+    sp.ids = ix->ids;
+    sp.out_id = d_ids;
+    sp.out_score = d_scores;
+    sp.n_over = n_over;
+    sp.n_cand = flags + 1;
+    const void *kfn = uvb::ivf_select_kernel_ptr(c->cfg.bits);
+    if (kfn == nullptr) return fail(UV_EUNSUPPORTED, "no rescoring kernel for these bits");
+    const size_t smem = uvb::ivf_select_smem_bytes(c->table_len, c->code_stride);
+    UV_CK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    void *args[] = {&sp};
+    ProfScope ps("ivf_tc_select", st);
+    UV_CK(cudaLaunchKernel(kfn, dim3((unsigned)((nq + uvb::kIvfSelWarps - 1) / uvb::kIvfSelWarps)),
+                           dim3(32 * uvb::kIvfSelWarps), args, smem, st));
+  }
+  unsigned long long h[4] = {0, 0, 0, 0};
+  UV_CK(cudaMemcpyAsync(h, flags, sizeof(h), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaStreamSynchronize(st));
+  // err | queries with a full slot store, queries with too many candidates
+  const int h_err = (int)(h[2] & 0xffffffffull);
+  const int h_slot = (int)(h[2] >> 32), h_cand = (int)(h[3] & 0xffffffffull);
+  g_tc_last_candidates = (int64_t)h[1];
+  g_ivf_tc_overflow = ((int64_t)h_slot << 32) | (int64_t)h_cand;
+  *fallback = h_err != 0 || h_slot != 0 || h_cand != 0;
+  return UV_OK;
+}
+
 // ivf.rs:229-239 on device: per-list top-k of every probed (query, list)
 // pair, merged per query.  Device inputs and outputs.
 int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np, int64_t *d_ids,
-                  float *d_scores, cudaStream_t st, Scratch &sc) {
+                  float *d_scores, cudaStream_t st, Scratch &sc, bool allow_tc = true) {
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   if (np == 0 || ix->n == 0) {
@@ -451,9 +697,13 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                             pid, psc, st));
     return merge_launch(nq, np, k, k, nullptr, psc, pid, d_ids, d_scores, st);
   }
-  // a pair's ranges are merged in one pass of at most about 1024 entries
+  // the tensor-core list scan: items of up to kIvfTcRows pairs and ranges
+  // of kIvfTcRange records; the CUDA-core scan: items of kScanTQ pairs, and
+  // ranges such that a pair's ranges merge in one pass of about 1024 entries
+  const bool tc = allow_tc && use_tc_scan(ix, k);
+  const int per_item = tc ? uvb::kIvfTcRows : uvb::kScanTQ;
   const int64_t range_size =
-      std::max<int64_t>(1024, (max_list * k + 1023) / 1024);
+      tc ? (int64_t)uvb::kIvfTcRange : std::max<int64_t>(1024, (max_list * k + 1023) / 1024);
   int32_t *cnt = nullptr, *fill = nullptr, *pair_off = nullptr, *item_off = nullptr,
           *pair_query = nullptr, *pair_slot = nullptr, *pair_list = nullptr;
   int64_t *list_rbase = nullptr, *totals = nullptr;
@@ -470,8 +720,8 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   {
     ProfScope ps("ivf_bucket", st);
     uvb::pair_count_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, npairs, cnt);
-    uvb::pair_scan_kernel<<<1, 1024, 0, st>>>(cnt, ix->d_off, nlist, range_size, pair_off,
-                                                item_off, list_rbase, totals);
+    uvb::pair_scan_kernel<<<1, 1024, 0, st>>>(cnt, ix->d_off, nlist, range_size, per_item,
+                                                pair_off, item_off, list_rbase, totals);
     uvb::pair_scatter_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, nq, np, pair_off, fill,
                                                                   pair_query, pair_slot, pair_list);
     UV_CK(cudaGetLastError());
@@ -494,9 +744,9 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
     const int32_t ni = (int32_t)n_items;
     UV_CK(cudaMemcpyAsync(d_n_items, &ni, sizeof(ni), cudaMemcpyHostToDevice, st));
     ProfScope ps("ivf_bucket", st);
-    uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(cnt, pair_off, item_off, ix->d_off,
-                                                              nlist, range_size, item_list,
-                                                              item_pair, item_npairs, item_range);
+    uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(
+        cnt, pair_off, item_off, ix->d_off, nlist, range_size, per_item, item_list, item_pair,
+        item_npairs, item_range);
     uvb::pair_rows_kernel<<<blocks(npairs + 1, 256), 256, 0, st>>>(
         pair_list, pair_off, list_rbase, ix->d_off, range_size, (int)npairs, row_off);
     UV_CK(cudaGetLastError());
@@ -510,6 +760,30 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                                                              pair_query, pair_slot, np, lists,
                                                              (int)npairs, pair_qm);
     UV_CK(cudaGetLastError());
+  }
+  if (tc) {
+    PairBuckets b;
+    b.npairs = npairs;
+    b.n_items = n_items;
+    b.n_rslots = n_rslots;
+    b.range_size = range_size;
+    b.pair_query = pair_query;
+    b.pair_slot = pair_slot;
+    b.pair_off = pair_off;
+    b.list_rbase = list_rbase;
+    b.row_off = row_off;
+    b.pair_qm = pair_qm;
+    b.item_list = item_list;
+    b.item_pair = item_pair;
+    b.item_npairs = item_npairs;
+    b.item_range = item_range;
+    b.n_items_dev = d_n_items;
+    bool fallback = false;
+    UV_TRY(tc_list_scan(ix, nq, k, np, q_r, dim_pad, degen, b, d_ids, d_scores, st, sc,
+                        &fallback));
+    if (!fallback) return UV_OK;
+    // a store overflowed: the CUDA-core scan, from the probe on
+    return search_device(ix, d_q, nq, k, np, d_ids, d_scores, st, sc, false);
   }
   // scan every item: one top-k per (pair, range) slot
   uint32_t *part_key = nullptr;

@@ -337,13 +337,13 @@ __device__ __forceinline__ int64_t list_ranges(int64_t size, int64_t range_size)
 }
 
 // One CTA: exclusive scans over the lists of the pair counts, of the scan
-// items (ranges x ceil(pairs / 32)) and of the range slots (pairs x ranges);
-// totals = {items, range slots}.
+// items (ranges x ceil(pairs / per_item)) and of the range slots (pairs x
+// ranges); totals = {items, range slots}.
 __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
                                                          const int64_t *list_off, int nlist,
-                                                         int64_t range_size, int32_t *pair_off,
-                                                         int32_t *item_off, int64_t *list_rbase,
-                                                         int64_t *totals) {
+                                                         int64_t range_size, int per_item,
+                                                         int32_t *pair_off, int32_t *item_off,
+                                                         int64_t *list_rbase, int64_t *totals) {
   __shared__ int64_t sp[1024], si[1024], sr[1024];
   const int t = threadIdx.x;
   const int per = (nlist + 1023) / 1024;
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
   for (int l = lo; l < hi; l++) {
     const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
     ps += cnt[l];
-    is += nr * ((cnt[l] + kScanTQ - 1) / kScanTQ);
+    is += nr * ((cnt[l] + per_item - 1) / per_item);
     rs += nr * cnt[l];
   }
   sp[t] = ps;
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
     item_off[l] = (int32_t)ibase;
     list_rbase[l] = rbase;
     pbase += cnt[l];
-    ibase += nr * ((cnt[l] + kScanTQ - 1) / kScanTQ);
+    ibase += nr * ((cnt[l] + per_item - 1) / per_item);
     rbase += nr * cnt[l];
   }
   if (t == 1023) {
@@ -399,18 +399,18 @@ __global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
 
 __global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
                                  const int32_t *item_off, const int64_t *list_off, int nlist,
-                                 int64_t range_size, int32_t *item_list, int32_t *item_pair,
-                                 int32_t *item_npairs, int32_t *item_range) {
+                                 int64_t range_size, int per_item, int32_t *item_list,
+                                 int32_t *item_pair, int32_t *item_npairs, int32_t *item_range) {
   const int l = blockIdx.x * blockDim.x + threadIdx.x;
   if (l >= nlist) return;
   const int c = cnt[l];
   const int64_t nr = list_ranges(list_off[l + 1] - list_off[l], range_size);
   int it = item_off[l];
   for (int64_t r = 0; r < nr; r++)
-    for (int i = 0; i * kScanTQ < c; i++, it++) {
+    for (int i = 0; i * per_item < c; i++, it++) {
       item_list[it] = l;
-      item_pair[it] = pair_off[l] + i * kScanTQ;
-      item_npairs[it] = min(kScanTQ, c - i * kScanTQ);
+      item_pair[it] = pair_off[l] + i * per_item;
+      item_npairs[it] = min(per_item, c - i * per_item);
       item_range[it] = (int32_t)r;
     }
 }

@@ -397,16 +397,18 @@ __global__ void select_top_kernel(const float *scores, int64_t n, int nb, int po
                                   int ld_out, int32_t *out);
 __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n);
 __global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt);
+// per_item: pairs of one list per scan item (kScanTQ for chunked_scan_kernel,
+// kIvfTcRows for tc_ivf_kernel)
 __global__ void pair_scan_kernel(const int32_t *cnt, const int64_t *list_off, int nlist,
-                                 int64_t range_size, int32_t *pair_off, int32_t *item_off,
-                                 int64_t *list_rbase, int64_t *totals);
+                                 int64_t range_size, int per_item, int32_t *pair_off,
+                                 int32_t *item_off, int64_t *list_rbase, int64_t *totals);
 __global__ void pair_scatter_kernel(const int32_t *lists, int64_t nq, int np,
                                     const int32_t *pair_off, int32_t *fill, int32_t *pair_query,
                                     int32_t *pair_slot, int32_t *pair_list);
 __global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
                                  const int32_t *item_off, const int64_t *list_off, int nlist,
-                                 int64_t range_size, int32_t *item_list, int32_t *item_pair,
-                                 int32_t *item_npairs, int32_t *item_range);
+                                 int64_t range_size, int per_item, int32_t *item_list,
+                                 int32_t *item_pair, int32_t *item_npairs, int32_t *item_range);
 __global__ void pair_rows_kernel(const int32_t *pair_list, const int32_t *pair_off,
                                  const int64_t *list_rbase, const int64_t *list_off,
                                  int64_t range_size, int npairs, int64_t *row_off);
@@ -414,6 +416,75 @@ __global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, 
                                const int32_t *pair_query, const int32_t *pair_slot, int np,
                                const int32_t *lists, int npairs, float *qm);
 __global__ void rerank_kernel(const RerankParams p);
+
+// ivftc.cu: the IVF list scan on the tensor cores.  Work items as for the
+// chunked scan (ScanWork), with up to kIvfTcRows pairs per item and record
+// ranges of at most kIvfTcRange records; (pair, range) slot s gets the
+// threshold slot_theta[s] (k-th largest lower bound of s * score over the
+// range; -inf with fewer than k) and slot_cnt[s] candidates at
+// cand_*[slot_base[s] ...] (-1: the candidate store was full).
+constexpr int kIvfTcRows = 128;
+constexpr int kIvfTcRange = 512;
+struct TcIvfParams {
+  int k, kchunks;              // kchunks: record row width / 64
+  int64_t range_size;
+  const int32_t *n_items;
+  const int32_t *item_list, *item_pair, *item_npairs, *item_range;
+  const int64_t *list_off;
+  const int32_t *list_pair_off;
+  const int64_t *list_rbase;
+  const int32_t *pair_query;
+  const float *pair_qm;        // or null
+  const uint32_t *degenerate;
+  const float *scale;          // s, a power of two (tc_scale_kernel)
+  const uint16_t *xext;        // record extra slices: C' in element 0
+  float *slot_theta;
+  int32_t *slot_cnt;
+  int64_t *slot_base;
+  uint32_t *cand_rec;
+  float *cand_lb, *cand_ub;
+  unsigned long long *cand_used;  // entries handed out so far
+  int64_t cand_cap;
+  int *err;
+};
+// Per query: the threshold over all its slots, the candidates that reach
+// it, their exact scores and the top k by (score desc, id asc).
+struct IvfSelectParams {
+  int dim, mem, bits, code_stride, q_stride, k, np, table_len;
+  int64_t nq;
+  const float *q_r;
+  const uint32_t *degenerate;
+  const int32_t *pair_of;      // nq x np: bucketed pair of probe j of query q
+  const int64_t *row_off;      // pair -> its slots [row_off[p], row_off[p + 1])
+  const float *pair_qm;        // or null
+  const float *slot_theta;
+  const int32_t *slot_cnt;
+  const int64_t *slot_base;
+  const uint32_t *cand_rec;
+  const float *cand_lb, *cand_ub;
+  const uint8_t *codes;
+  const uint32_t *start;
+  const float *code, *rescale, *rnorm;
+  const int64_t *ids;
+  int64_t *out_id;
+  float *out_score;
+  int *n_over;                 // [0] queries with a full slot, [1] with too many candidates
+  unsigned long long *n_cand;  // candidates scored exactly (statistics)
+};
+constexpr int kIvfSelWarps = 8;
+constexpr int kIvfSelLb = 512;     // lower bounds per query at the threshold step
+constexpr int kIvfSelCand = 256;   // candidates per query
+const void *tc_ivf_kernel_ptr(int k);  // k <= 32; null above
+size_t tc_ivf_smem_bytes();
+int tc_ivf_threads();
+const void *ivf_select_kernel_ptr(int bits);
+size_t ivf_select_smem_bytes(int table_len, int code_stride);
+__global__ void ivf_pair_rows16_kernel(const float *q_r, int q_stride, const uint32_t *degen,
+                                       const int32_t *pair_query, int64_t npairs, int dim,
+                                       int kpad, uint16_t *pa16);
+__global__ void ivf_pair_of_kernel(const int32_t *pair_slot, int64_t npairs, int32_t *pair_of);
+__global__ void ivf_neg_slice_kernel(uint16_t *ax);  // kIvfTcRows x 16, one thread per entry
+__global__ void tc_scale_kernel(const uint32_t *gmax_bits, float code_absmax, float *scale);
 __global__ void score_candidates_kernel(const CandParams p);
 const void *score_candidates_lane_kernel_ptr(int bits);  // bits 1..4; else null
 const void *shortlist_kernel_ptr(int bits, bool asym);
