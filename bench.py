@@ -963,7 +963,7 @@ def run_ivf(uv, dev, emit, rng, args=None):
         kern = {f: round(uv.profile_read(f)[0], 3) for f in fams}
         launches = uv.profile_read("*")[1]
         exact = uv.profile_read("tc_candidates")[1]
-        over_slot, over_cand = uv.profile_read("ivf_tc_overflow")
+        store_full, over_cand = uv.profile_read("ivf_tc_overflow")
         uv.profile_enable(False)
         probed = ivf.probe(qs, nprobe)
         probed = probed.cpu().numpy() if hasattr(probed, "cpu") else np.asarray(probed)
@@ -1014,8 +1014,8 @@ def run_ivf(uv, dev, emit, rng, args=None):
             "kernels_ms": kern, "gpu_launches": launches, "list_sizes": list_stats,
             "records_scanned_per_query": scanned,
             "records_scored_exactly_per_query": exact / nq if tc_ms > 0 else scanned,
-            "tc_overflow_queries": {"slot_store": int(over_slot), "candidates": int(over_cand)}
-            if tc_ms > 0 else None,
+            "tc_overflow": {"store_full": bool(store_full), "queries_over_candidates":
+                            int(over_cand)} if tc_ms > 0 else None,
             "roofline": roof,
             "e2e": {"value": nq / e2e_ms * 1e3, "unit": "queries/s",
                     "h2d_bytes_per_step": nq * d_pad * 4, "d2h_bytes_per_step": nq * 10 * 12,

@@ -2191,9 +2191,10 @@ int uv_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
     return UV_OK;
   }
   if (std::strcmp(kernel, "ivf_tc_overflow") == 0) {
-    // statistic of the last tensor-core IVF list scan: queries whose kept
-    // records overflowed a slot's store (total_ms) or the per-query
-    // candidate store (launches); either sends the search to the CUDA-core scan
+    // statistic of the last tensor-core IVF list scan: 1 when its kept-record
+    // store was full (total_ms), and the queries with more candidates than
+    // the per-query store holds (launches); either sends the search to the
+    // CUDA-core scan
     const int64_t v = g_ivf_tc_overflow.load();
     *total_ms = (double)(v >> 32);
     *launches = v & 0xffffffffll;

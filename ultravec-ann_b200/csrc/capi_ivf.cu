@@ -544,13 +544,15 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
   // per-slot thresholds and the store of kept records
   const int64_t nslots = std::max<int64_t>(b.n_rslots, 1);
   const int64_t cand_cap = b.n_rslots * (int64_t)(k + 16) + 65536;
-  float *slot_theta = nullptr, *cand_lb = nullptr, *cand_ub = nullptr;
+  float *cand_lb = nullptr, *cand_ub = nullptr;
+  uint32_t *q_theta0 = nullptr;
   int32_t *slot_cnt = nullptr;
   int64_t *slot_base = nullptr;
   uint32_t *cand_rec = nullptr;
-  // kept-record count, scored count, err | queries over (slot), queries over (candidates)
+  // kept-record count, scored count, err | queries over the candidate store
   unsigned long long *flags = nullptr;
-  UV_TRY(sc.alloc(&slot_theta, (size_t)nslots));
+  UV_TRY(sc.alloc(&q_theta0, (size_t)nq));
+  UV_CK(cudaMemsetAsync(q_theta0, 0, sizeof(uint32_t) * (size_t)nq, st));
   UV_TRY(sc.alloc(&slot_cnt, (size_t)nslots));
   UV_TRY(sc.alloc(&slot_base, (size_t)nslots));
   UV_TRY(sc.alloc(&cand_rec, (size_t)cand_cap));
@@ -578,7 +580,7 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
     tp.degenerate = degen;
     tp.scale = scale;
     tp.xext = rows->xext;
-    tp.slot_theta = slot_theta;
+    tp.q_theta0 = q_theta0;
     tp.slot_cnt = slot_cnt;
     tp.slot_base = slot_base;
     tp.cand_rec = cand_rec;
@@ -613,7 +615,7 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
     sp.pair_of = pair_of;
     sp.row_off = b.row_off;
     sp.pair_qm = b.pair_qm;
-    sp.slot_theta = slot_theta;
+    sp.q_theta0 = q_theta0;
     sp.slot_cnt = slot_cnt;
     sp.slot_base = slot_base;
     sp.cand_rec = cand_rec;
@@ -641,12 +643,12 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
   unsigned long long h[4] = {0, 0, 0, 0};
   UV_CK(cudaMemcpyAsync(h, flags, sizeof(h), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
-  // err | queries with a full slot store, queries with too many candidates
-  const int h_err = (int)(h[2] & 0xffffffffull);
-  const int h_slot = (int)(h[2] >> 32), h_cand = (int)(h[3] & 0xffffffffull);
+  // err (1: a wait timed out, 2: the kept-record store was full) | queries
+  // with more candidates than the per-query store holds
+  const int h_err = (int)(h[2] & 0xffffffffull), h_cand = (int)(h[2] >> 32);
   g_tc_last_candidates = (int64_t)h[1];
-  g_ivf_tc_overflow = ((int64_t)h_slot << 32) | (int64_t)h_cand;
-  *fallback = h_err != 0 || h_slot != 0 || h_cand != 0;
+  g_ivf_tc_overflow = ((int64_t)((h_err & 2) ? 1 : 0) << 32) | (int64_t)h_cand;
+  *fallback = h_err != 0 || h_cand != 0;
   return UV_OK;
 }
 
@@ -756,9 +758,10 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   if (ix->centered) {
     UV_TRY(sc.alloc(&pair_qm, (size_t)npairs));
     ProfScope ps("ivf_pair_qm", st);
-    uvb::pair_qm_kernel<<<blocks(npairs, 128), 128, 0, st>>>(u, dim_pad, ix->centroids, d,
-                                                             pair_query, pair_slot, np, lists,
-                                                             (int)npairs, pair_qm);
+    uvb::pair_qm_kernel<<<(unsigned)((npairs + 32 * uvb::kPairQmWarps - 1) /
+                                     (32 * uvb::kPairQmWarps)),
+                          32 * uvb::kPairQmWarps, 0, st>>>(u, dim_pad, ix->centroids, d, pair_query,
+                                                           pair_list, (int)npairs, pair_qm);
     UV_CK(cudaGetLastError());
   }
   if (tc) {

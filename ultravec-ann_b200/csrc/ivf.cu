@@ -116,7 +116,15 @@ __global__ void row_norms_kernel(const float *rows, int64_t n, int dim, float *n
   if (i >= n) return;
   const float *r = rows + i * (int64_t)dim;
   float s = -0.0f;
-  for (int t = 0; t < dim; t++) {
+  int t = 0;
+  for (; t + 8 <= dim; t += 8) {  // eight loads ahead of the in-order fold
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = __ldg(r + t + u);
+#pragma unroll
+    for (int u = 0; u < 8; u++) s = fadd(s, fmul(v[u], v[u]));
+  }
+  for (; t < dim; t++) {
     const float x = __ldg(r + t);
     s = fadd(s, fmul(x, x));
   }
@@ -268,15 +276,20 @@ __global__ void __launch_bounds__(256) probe_refine_kernel(const ProbeRefinePara
       uint64_t key = 0ull;
       if (i < nc) {
         const int j = (int)aux[i];
-        // the centroid row in batches of 32 values (8 independent 16-byte
-        // loads ahead of the sequential sum, which keeps the reference order)
+        // the centroid row in batches of 32 values, the next batch's eight
+        // 16-byte loads in flight while the current batch is folded in the
+        // reference order (dim is a multiple of 32 here)
         const float4 *c4 = (const float4 *)(p.cent + (int64_t)j * p.dim);
         const float4 *q4 = (const float4 *)qs;
         float dot = -0.0f;
-        for (int t4 = 0; t4 < p.dim / 4; t4 += 8) {
-          float4 b[8];
+        float4 b[8];
 #pragma unroll
-          for (int u = 0; u < 8; u++) b[u] = __ldg(c4 + t4 + u);
+        for (int u = 0; u < 8; u++) b[u] = __ldg(c4 + u);
+        for (int t4 = 0; t4 < p.dim / 4; t4 += 8) {
+          float4 nb[8];
+          const bool more = t4 + 8 < p.dim / 4;
+#pragma unroll
+          for (int u = 0; u < 8; u++) nb[u] = more ? __ldg(c4 + t4 + 8 + u) : b[u];
 #pragma unroll
           for (int u = 0; u < 8; u++) {
             const float4 a = q4[t4 + u];
@@ -285,6 +298,8 @@ __global__ void __launch_bounds__(256) probe_refine_kernel(const ProbeRefinePara
             dot = fadd(dot, fmul(a.z, b[u].z));
             dot = fadd(dot, fmul(a.w, b[u].w));
           }
+#pragma unroll
+          for (int u = 0; u < 8; u++) b[u] = nb[u];
         }
         float cs = dot;  // the k-means assignment ranks the plain dot
         if (p.cosine) {
@@ -433,19 +448,46 @@ __global__ void pair_rows_kernel(const int32_t *pair_list, const int32_t *pair_o
 }
 
 // qm of each pair: seq_dot(u_query, centroid_list) (trellis.rs:2120-2183 with
-// the list codec's single centroid).  One thread per pair.
-__global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, int dim,
-                               const int32_t *pair_query, const int32_t *pair_slot, int np,
-                               const int32_t *lists, int npairs, float *qm) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= npairs) return;
-  const int64_t q = pair_query[i];
-  const int l = lists[pair_slot[i]];
-  const float *a = u + q * (int64_t)u_stride;
-  const float *c = cent + (int64_t)l * dim;
+// the list codec's single centroid): one sequential f32 fold per pair, the
+// product and the sum rounded separately, from -0.0.  A warp takes 32
+// consecutive (bucketed) pairs and stages 32 coordinates at a time in
+// shared memory with coalesced loads: the 32 query rows transposed, and the
+// centroid chunk once when all 32 pairs are on one list (the usual case:
+// a list's pairs are contiguous); lane r then folds row r's 32 products in
+// order.  Blocks of kPairQmWarps warps.
+__global__ void __launch_bounds__(32 * kPairQmWarps) pair_qm_kernel(
+    const float *u, int u_stride, const float *cent, int dim, const int32_t *pair_query,
+    const int32_t *pair_list, int npairs, float *qm) {
+  __shared__ float su[kPairQmWarps][32][33];
+  __shared__ float sc[kPairQmWarps][32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p0 = (blockIdx.x * kPairQmWarps + warp) * 32;
+  if (p0 >= npairs) return;  // whole warps; no block barrier below
+  const int mine = min(p0 + lane, npairs - 1);
+  const int64_t qrow = pair_query[mine];
+  const int lrow = pair_list[mine];
+  const bool one_list = __all_sync(0xffffffffu, lrow == __shfl_sync(0xffffffffu, lrow, 0));
   float s = -0.0f;
-  for (int t = 0; t < dim; t++) s = fadd(s, fmul(a[t], __ldg(c + t)));
-  qm[i] = s;
+  for (int k0 = 0; k0 < dim; k0 += 32) {
+    const int kc = min(32, dim - k0);
+    for (int r = 0; r < 32; r++) {
+      const int64_t q = __shfl_sync(0xffffffffu, qrow, r);
+      if (lane < kc) su[warp][r][lane] = __ldg(u + q * (int64_t)u_stride + k0 + lane);
+    }
+    if (one_list) {
+      if (lane < kc) sc[warp][0][lane] = __ldg(cent + (int64_t)lrow * dim + k0 + lane);
+    } else {
+      for (int r = 0; r < 32; r++) {
+        const int64_t l = __shfl_sync(0xffffffffu, lrow, r);
+        if (lane < kc) sc[warp][r][lane] = __ldg(cent + l * dim + k0 + lane);
+      }
+    }
+    __syncwarp();
+    const float *cr = one_list ? sc[warp][0] : sc[warp][lane];
+    for (int i = 0; i < kc; i++) s = fadd(s, fmul(su[warp][lane][i], cr[i]));
+    __syncwarp();  // the chunk is restaged next
+  }
+  if (p0 + lane < npairs) qm[p0 + lane] = s;
 }
 
 // Exact fp32 rerank (ivf.rs:248-274): cosine(query, db[id]) for each of the r

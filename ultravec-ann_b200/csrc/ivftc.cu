@@ -68,6 +68,15 @@ static_assert(2 * V_STAGES + V_TILES + 1 <= 16, "barrier slots");
 static_assert(V_TILES * V_N <= 512, "TMEM columns");
 static_assert(V_TOTAL <= 227 * 1024, "shared memory");
 
+// the bits of a float as an unsigned key of the same order, and back
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_order(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 }  // namespace
 
 template <int KT>
@@ -227,9 +236,12 @@ __global__ void __launch_bounds__(V_THREADS, 1)
     }
     if (has) {
       const int64_t slot = p.list_rbase[l] + (int64_t)(pp - p.list_pair_off[l]) * nr + rg;
-      p.slot_theta[slot] = ok ? theta : -INFINITY;
       p.slot_cnt[slot] = !alive ? -1 : (!ok ? 0 : (fits ? cnt : -1));
       p.slot_base[slot] = base;
+      // the query's theta0: the largest slot threshold (a score k records reach)
+      if (ok && theta > -INFINITY)
+        atomicMax(p.q_theta0 + p.pair_query[pp], order_key(theta));
+      if (alive && ok && !fits) atomicOr(p.err, 2);  // the store is full
     }
   } else if (warp == V_EPI) {
     if (lane == 0) {
@@ -326,13 +338,57 @@ struct SelWarp {
   int n_lb, n_c;
 };
 
-// the bits of a float as an unsigned key of the same order, and back
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float key_order(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+
+
+// Calls fn(entry, qm) for every kept record of query q's slots, the warp's
+// lanes spread over the slots: probes in chunks of 32 (lane j: probe j0 + j,
+// its bucketed pair and slot range), then the chunk's slots in turn, each
+// lane finding its slot's probe by a bisection over the chunk's prefix.
+template <class Fn>
+__device__ __forceinline__ void for_each_entry(const IvfSelectParams &p, int64_t q, int lane,
+                                               Fn fn) {
+  for (int j0 = 0; j0 < p.np; j0 += 32) {
+    const int j = j0 + lane;
+    int pp = -1;
+    if (j < p.np) pp = p.pair_of[q * p.np + j];
+    int64_t s0 = 0;
+    int ns = 0;
+    float qm = 0.0f;
+    if (pp >= 0) {
+      s0 = p.row_off[pp];
+      ns = (int)(p.row_off[pp + 1] - s0);
+      if (p.pair_qm != nullptr) qm = p.pair_qm[pp];
+    }
+    int incl = ns;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int ex = incl - ns;
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    for (int t0 = 0; t0 < total; t0 += 32) {
+      const int t = t0 + lane;
+      // the last lane whose first slot is at or before t
+      int lo = 0, hi = 31;
+#pragma unroll
+      for (int it = 0; it < 5; it++) {
+        const int mid = (lo + hi + 1) >> 1;
+        const int v = __shfl_sync(0xffffffffu, ex, mid);
+        if (v <= t) lo = mid;
+        else hi = mid - 1;
+      }
+      const int64_t so = __shfl_sync(0xffffffffu, s0, lo);
+      const int eo = __shfl_sync(0xffffffffu, ex, lo);
+      const float qo = __shfl_sync(0xffffffffu, qm, lo);
+      if (t < total) {
+        const int64_t slot = so + (t - eo);
+        const int c = p.slot_cnt[slot];
+        const int64_t b0 = p.slot_base[slot];
+        for (int i = 0; i < c; i++) fn(b0 + i, qo);
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -341,7 +397,7 @@ __device__ __forceinline__ float key_order(uint32_t k) {
 // its slots, the exact scores of the kept records that reach it (half a
 // warp per record: 16 lanes = the 16 FMA chains of simd.rs:202-262, then the
 // hsum256 tree), and the top k.  A query with an overflowed slot or more
-// candidates than the per-query store holds is counted in n_over[0] / [1].
+// candidates than the per-query store holds is counted in *n_over.
 template <int BITS>
 __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const IvfSelectParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -371,20 +427,10 @@ __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const Ivf
     }
     return;
   }
-  // theta0: the largest slot threshold; any overflowed slot
-  float th0 = -INFINITY;
-  bool over = false;
-  for (int j = lane; j < p.np; j += 32) {
-    const int pp = p.pair_of[q * p.np + j];
-    if (pp < 0) continue;  // a probe without a list
-    for (int64_t s = p.row_off[pp]; s < p.row_off[pp + 1]; s++) {
-      th0 = fmaxf(th0, p.slot_theta[s]);
-      over |= p.slot_cnt[s] < 0;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) th0 = fmaxf(th0, __shfl_xor_sync(0xffffffffu, th0, o));
-  over = __any_sync(0xffffffffu, over);
+  // theta0: the largest slot threshold (tc_ivf_kernel's atomicMax; key 0:
+  // no slot of this query holds k records)
+  const uint32_t th0_key = p.q_theta0[q];
+  const float th0 = th0_key == 0u ? -INFINITY : key_order(th0_key);
   if (lane == 0) {
     cw->n_lb = 0;
     cw->n_c = 0;
@@ -393,22 +439,14 @@ __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const Ivf
   // theta_q: the k-th largest lower bound at or above theta0 (at least k:
   // the records behind theta0's own slot)
   float thq = -INFINITY;
-  if (th0 > -INFINITY && !over) {
-    for (int j = lane; j < p.np; j += 32) {
-      const int pp = p.pair_of[q * p.np + j];
-      if (pp < 0) continue;
-      for (int64_t s = p.row_off[pp]; s < p.row_off[pp + 1]; s++) {
-        const int64_t b0 = p.slot_base[s];
-        const int c = p.slot_cnt[s];
-        for (int i = 0; i < c; i++) {
-          const float lb = p.cand_lb[b0 + i];
-          if (lb >= th0) {
-            const int pos = atomicAdd(&cw->n_lb, 1);
-            if (pos < kIvfSelLb) lbv[pos] = lb;
-          }
-        }
+  if (th0 > -INFINITY) {
+    for_each_entry(p, q, lane, [&](int64_t e, float) {
+      const float lb = p.cand_lb[e];
+      if (lb >= th0) {
+        const int pos = atomicAdd(&cw->n_lb, 1);
+        if (pos < kIvfSelLb) lbv[pos] = lb;
       }
-    }
+    });
     __syncwarp();
     const int nlb = cw->n_lb;
     if (nlb > kIvfSelLb) {
@@ -422,19 +460,11 @@ __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const Ivf
       for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = lane; i < 256; i += 32) hist[i] = 0u;
         __syncwarp();
-        for (int j = lane; j < p.np; j += 32) {
-          const int pp = p.pair_of[q * p.np + j];
-          if (pp < 0) continue;
-          for (int64_t s = p.row_off[pp]; s < p.row_off[pp + 1]; s++) {
-            const int64_t b0 = p.slot_base[s];
-            const int c = p.slot_cnt[s];
-            for (int i = 0; i < c; i++) {
-              const float lb = p.cand_lb[b0 + i];
-              const uint32_t key = order_key(lb);
-              if (lb >= th0 && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-            }
-          }
-        }
+        for_each_entry(p, q, lane, [&](int64_t e, float) {
+          const float lb = p.cand_lb[e];
+          const uint32_t key = order_key(lb);
+          if (lb >= th0 && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        });
         __syncwarp();
         // lane l sums bins 8l .. 8l + 7; suffix sums from the top bin down
         uint32_t mine = 0u;
@@ -494,33 +524,20 @@ __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const Ivf
       thq = p.k <= nlb ? lbv[p.k - 1] : th0;
     }
   }
-  if (over) {
-    if (lane == 0) atomicAdd(p.n_over, 1);  // a slot's store was full
-    return;
-  }
   // the kept records that reach theta_q
-  for (int j = lane; j < p.np; j += 32) {
-    const int pp = p.pair_of[q * p.np + j];
-    if (pp < 0) continue;
-    const float qm = p.pair_qm != nullptr ? p.pair_qm[pp] : 0.0f;
-    for (int64_t s = p.row_off[pp]; s < p.row_off[pp + 1]; s++) {
-      const int64_t b0 = p.slot_base[s];
-      const int c = p.slot_cnt[s];
-      for (int i = 0; i < c; i++) {
-        if (!(p.cand_ub[b0 + i] < thq)) {
-          const int pos = atomicAdd(&cw->n_c, 1);
-          if (pos < kIvfSelCand) {
-            crec[pos] = p.cand_rec[b0 + i];
-            cqm[pos] = qm;
-          }
-        }
+  for_each_entry(p, q, lane, [&](int64_t e, float qm) {
+    if (!(p.cand_ub[e] < thq)) {
+      const int pos = atomicAdd(&cw->n_c, 1);
+      if (pos < kIvfSelCand) {
+        crec[pos] = p.cand_rec[e];
+        cqm[pos] = qm;
       }
     }
-  }
+  });
   __syncwarp();
   const int nc = cw->n_c;
   if (nc > kIvfSelCand) {
-    if (lane == 0) atomicAdd(p.n_over + 1, 1);
+    if (lane == 0) atomicAdd(p.n_over, 1);
     return;
   }
   if (lane == 0 && p.n_cand != nullptr) atomicAdd(p.n_cand, (unsigned long long)nc);

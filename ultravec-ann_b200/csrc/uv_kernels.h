@@ -412,17 +412,19 @@ __global__ void item_fill_kernel(const int32_t *cnt, const int32_t *pair_off,
 __global__ void pair_rows_kernel(const int32_t *pair_list, const int32_t *pair_off,
                                  const int64_t *list_rbase, const int64_t *list_off,
                                  int64_t range_size, int npairs, int64_t *row_off);
+constexpr int kPairQmWarps = 4;  // pair_qm_kernel: warps per block (32 pairs each)
 __global__ void pair_qm_kernel(const float *u, int u_stride, const float *cent, int dim,
-                               const int32_t *pair_query, const int32_t *pair_slot, int np,
-                               const int32_t *lists, int npairs, float *qm);
+                               const int32_t *pair_query, const int32_t *pair_list, int npairs,
+                               float *qm);
 __global__ void rerank_kernel(const RerankParams p);
 
 // ivftc.cu: the IVF list scan on the tensor cores.  Work items as for the
 // chunked scan (ScanWork), with up to kIvfTcRows pairs per item and record
-// ranges of at most kIvfTcRange records; (pair, range) slot s gets the
-// threshold slot_theta[s] (k-th largest lower bound of s * score over the
-// range; -inf with fewer than k) and slot_cnt[s] candidates at
-// cand_*[slot_base[s] ...] (-1: the candidate store was full).
+// ranges of at most kIvfTcRange records; (pair, range) slot s gets
+// slot_cnt[s] kept records at cand_*[slot_base[s] ...] (-1: the store was
+// full, *err |= 2), and each query's q_theta0 (zeroed before the launch) the
+// largest of its slots' thresholds (the k-th largest lower bound of s *
+// score over a range) as an order-preserving key.
 constexpr int kIvfTcRows = 128;
 constexpr int kIvfTcRange = 512;
 struct TcIvfParams {
@@ -438,14 +440,14 @@ struct TcIvfParams {
   const uint32_t *degenerate;
   const float *scale;          // s, a power of two (tc_scale_kernel)
   const uint16_t *xext;        // record extra slices: C' in element 0
-  float *slot_theta;
+  uint32_t *q_theta0;
   int32_t *slot_cnt;
   int64_t *slot_base;
   uint32_t *cand_rec;
   float *cand_lb, *cand_ub;
   unsigned long long *cand_used;  // entries handed out so far
   int64_t cand_cap;
-  int *err;
+  int *err;                    // 1: a wait timed out, 2: the store is full
 };
 // Per query: the threshold over all its slots, the candidates that reach
 // it, their exact scores and the top k by (score desc, id asc).
@@ -457,7 +459,7 @@ struct IvfSelectParams {
   const int32_t *pair_of;      // nq x np: bucketed pair of probe j of query q
   const int64_t *row_off;      // pair -> its slots [row_off[p], row_off[p + 1])
   const float *pair_qm;        // or null
-  const float *slot_theta;
+  const uint32_t *q_theta0;
   const int32_t *slot_cnt;
   const int64_t *slot_base;
   const uint32_t *cand_rec;
@@ -468,7 +470,7 @@ struct IvfSelectParams {
   const int64_t *ids;
   int64_t *out_id;
   float *out_score;
-  int *n_over;                 // [0] queries with a full slot, [1] with too many candidates
+  int *n_over;                 // queries with more candidates than kIvfSelCand
   unsigned long long *n_cand;  // candidates scored exactly (statistics)
 };
 constexpr int kIvfSelWarps = 8;

@@ -24,15 +24,36 @@ struct Team {
 };
 
 // Rust `.sum::<f32>()` of x*x: a left fold from -0.0, one rounding per op.
+// Eight operands are read ahead of the fold (the adds stay in order), so
+// the one dependent chain is the adds, not the loads.
 __device__ __forceinline__ float seq_sum_sq(const float *x, int n) {
   float s = -0.0f;
-  for (int i = 0; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
+  int i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) v[t] = x[i + t];
+#pragma unroll
+    for (int t = 0; t < 8; t++) s = fadd(s, fmul(v[t], v[t]));
+  }
+  for (; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
   return s;
 }
 
 __device__ __forceinline__ float seq_dot(const float *a, const float *b, int n) {
   float s = -0.0f;
-  for (int i = 0; i < n; i++) s = fadd(s, fmul(a[i], b[i]));
+  int i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float va[8], vb[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+      va[t] = a[i + t];
+      vb[t] = b[i + t];
+    }
+#pragma unroll
+    for (int t = 0; t < 8; t++) s = fadd(s, fmul(va[t], vb[t]));
+  }
+  for (; i < n; i++) s = fadd(s, fmul(a[i], b[i]));
   return s;
 }
 
