@@ -533,10 +533,13 @@ def ivf_data(rng, n, nq, d, d_pad):
 def run_ivf_sharded(args):
     """The IVF workload on N GPUs (torchrun, one rank per GPU, NCCL): every
     rank computes the same k-means and assignment, owns the posting lists
-    dealt to it by record bytes (shard.ivf_list_owners), builds an IVF index
-    of its rows (global ids), probes all centroids and scans its own probed
-    lists; the per-rank top-10 lists meet in one all-gather and a device
-    merge.  Device time per search is the max over ranks."""
+    dealt to it by record bytes (shard.ivf_list_owners) and builds an IVF
+    index of its rows (global ids); per search, each rank probes its query
+    slice, the lists are shared by one all-gather, every rank scans the
+    probed lists it owns, and the packed per-rank top-10 lists combine by an
+    all-to-all of query slices, device merges and one all-gather
+    (shard.ivf_sharded_search).  Device time per search is the max over
+    ranks."""
     import datetime
 
     import torch
@@ -571,11 +574,17 @@ def run_ivf_sharded(args):
               if hasattr(asg, "index_select") else asg_np[rows],
               ids=rows_t.to(torch.int64))
     del base
-    merge = lambda i, sc, k: uv.topk_merge(i, sc, k, device=local)  # noqa: E731
 
     def search(nprobe):
-        ids, sc = ivf.search(qs, 10, nprobe)
-        return shard.gather_topk(ids, sc, 10, dist, merge)
+        # the probe split by query slices and shared by one all-gather; every
+        # rank scans the probed lists it holds; packed lists, all-to-all of
+        # query slices, per-slice merges, all-gather of the merged slices
+        return shard.ivf_sharded_search(
+            ivf, qs, 10, nprobe, dist,
+            lambda i, sc: uv.topk_pack(i, sc, device=local),
+            lambda p: uv.topk_unpack(p, device=local),
+            lambda recv, rows, nl, kin, kk, rs, ls: uv.topk_merge_packed(
+                recv, rows, nl, kin, kk, rs, ls, device=local))
 
     for nprobe in (1, 4, 16, 64):
         search(nprobe)
@@ -595,6 +604,8 @@ def run_ivf_sharded(args):
         if rank == 0:
             print(json.dumps({"metric": METRIC, "workload": "ivf-1Mx10k-d2048-nlist4096",
                               "n_gpus": world, "data": "synthetic", "nprobe": nprobe,
+                              "value": nq / best * 1e3, "unit": "queries/s",
+                              "higher_is_better": True, "scaling": "strong",
                               "queries_s": nq / best * 1e3, "search_ms": best,
                               "centered": True, "k": 10, "bits": 2, "mem": 8,
                               "parallelism": f"lists dealt by bytes over {world} ranks",

@@ -425,6 +425,18 @@ int uv_ivf_probe(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t np
 int uv_ivf_search(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t k,
                   int32_t nprobe, int64_t *ids_out, float *scores_out, void *stream);
 
+/* search over lists chosen beforehand: lists (host or device, nq x nprobe,
+ * -1 = no list) as uv_ivf_probe returns them, possibly from another index
+ * with the same centroids -- an IVF base split by posting list across GPUs
+ * probes each query once, shares the lists, and every shard scans the
+ * probed lists it holds (lists without records here are skipped).  The
+ * results equal uv_ivf_search's for the same lists.  A list id >= nlist
+ * returns UV_EINVAL.  1 <= k <= 128.  No counterpart in the reference (its
+ * search probes and scans in one call, ivf.rs:229-239). */
+int uv_ivf_search_lists(const uv_ivf *ivf, const float *queries, int64_t nq, int32_t k,
+                        int32_t nprobe, const int32_t *lists, int64_t *ids_out, float *scores_out,
+                        void *stream);
+
 /* search_with_rerank (ivf.rs:248-274): the best r = max(rdepth, k) <= 128 by
  * the codec score, then exact fp32 cosine(query, db[id]) of those r, best k
  * by (cosine desc, id asc).  db is n_db x dim, host or device; an id >= n_db

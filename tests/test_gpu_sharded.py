@@ -182,3 +182,63 @@ def test_merge_sorted_and_unsorted_lists(uv, L, kin, k):
         want = [i for _, i in cand[:k]] + [-1] * max(0, k - len(cand))
         assert list(got_i[q]) == want, q
         assert list(got_s[q][:len(cand)]) == [-s for s, _ in cand[:k]][:len(cand)]
+
+
+@pytest.mark.parametrize("n_shards,nprobe,tc", [(3, 4, 0), (4, 16, 2), (2, 1, 1)])
+def test_ivf_sharded_by_lists_with_a_split_probe(oracle, uv, n_shards, nprobe, tc):
+    """An IVF base dealt to shards by posting list (shard.ivf_list_owners):
+    shard r probes only its query slice, the lists are concatenated (the
+    all-gather's layout), every shard scans the probed lists it holds
+    (search_lists; the others are empty here and skipped), the packed lists
+    merge per query slice -- equal to the unsharded IVF search, with the
+    tensor-core and the CUDA-core list scans."""
+    import torch
+
+    from ultravec_ann_b200.shard import ivf_list_owners, ivf_owned_rows
+
+    rng = np.random.default_rng(n_shards * 10 + nprobe)
+    dim, nlist, n, nq, k = 256, 24, 6000, 37, 10
+    c = rng.standard_normal((8, dim)).astype(np.float32)
+    base = c[rng.integers(0, 8, n)] + np.float32(0.5) * rng.standard_normal((n, dim)).astype(
+        np.float32)
+    qs = base[rng.integers(0, n, nq)] + np.float32(0.1) * rng.standard_normal((nq, dim)).astype(
+        np.float32)
+    cen = oracle.kmeans(base, nlist, seed=42, iters=2)
+    asg = oracle.assign(base, cen)
+    codec = uv.Codec(dim, 2, 8)
+    whole = uv.IvfIndex(codec, cen, centered=True)
+    whole.build(base, assign=asg)
+    owners = ivf_list_owners(np.bincount(asg, minlength=nlist), n_shards)
+    shards = []
+    for r in range(n_shards):
+        rows = ivf_owned_rows(asg, owners, r)
+        ix = uv.IvfIndex(codec, cen, centered=True)
+        ix.build(base[rows], assign=asg[rows], ids=rows.astype(np.int64))
+        shards.append(ix)
+    uv.set_tuning("ivf_tc", tc)
+    try:
+        want_i, want_s = whole.search(qs, k, nprobe)
+        lists = np.concatenate([shards[r].probe(qs[r * nq // n_shards:(r + 1) * nq // n_shards],
+                                                nprobe) for r in range(n_shards)])
+        assert np.array_equal(lists, whole.probe(qs, nprobe))
+        res = [ix.search_lists(qs, k, lists) for ix in shards]
+    finally:
+        uv.set_tuning("ivf_tc", 0)
+    packed = [uv.topk_pack(torch.as_tensor(i).cuda(), torch.as_tensor(s).cuda()) for i, s in res]
+    out_i, out_s = [], []
+    for r in range(n_shards):
+        lo, hi = r * nq // n_shards, (r + 1) * nq // n_shards
+        rows = hi - lo
+        recv = torch.cat([p[lo:hi].reshape(-1) for p in packed])
+        i, s = uv.topk_merge_packed(recv, rows, n_shards, k, k, row_stride=k,
+                                    list_stride=rows * k)
+        out_i.append(i.cpu().numpy())
+        out_s.append(s.cpu().numpy())
+    got_i, got_s = np.concatenate(out_i), np.concatenate(out_s)
+    assert np.array_equal(got_i, want_i)
+    assert np.array_equal(_bits(got_s), _bits(want_s))
+    # a list id past nlist is refused
+    bad = lists.copy()
+    bad[0, 0] = nlist
+    with pytest.raises(uv.UVError):
+        shards[0].search_lists(qs, k, bad)

@@ -237,7 +237,8 @@ def _gloo_ivf_worker(rank, world, port, result_dir):
 
     load()
     from ultravec_ann_b200.shard import (gather_topk, ivf_list_owners, ivf_owned_rows,
-                                         merge_host)
+                                         ivf_sharded_search, merge_host, merge_packed_host,
+                                         pack_host, unpack_host)
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -264,10 +265,32 @@ def _gloo_ivf_worker(rank, world, port, result_dir):
         ids, sc = ivf_search(ivf_owned_rows(asg, owners, rank), centered)
         g_ids, g_sc = gather_topk(torch.from_numpy(ids), torch.from_numpy(sc), 10, dist,
                                   merge_host)
+        want_ids, want_sc = ivf_search(np.arange(len(db)), centered)
         if rank == 0:
-            want_ids, want_sc = ivf_search(np.arange(len(db)), centered)
             ok &= np.array_equal(g_ids.numpy(), want_ids) and np.array_equal(
                 g_sc.numpy().view(np.uint32), want_sc.view(np.uint32))
+
+        # the probe split by query slices, the lists shared, each rank
+        # scanning its own lists (the oracle stands in for the device index)
+        class Shard:
+            def __init__(self, rows_idx):
+                self.rows_idx = rows_idx
+
+            def probe(self, q, nprobe):
+                return torch.from_numpy(np.stack(
+                    [np.asarray(O.ivf_probe(cen, x, nprobe), np.int32) for x in q])
+                    if len(q) else np.zeros((0, nprobe), np.int32))
+
+            def search_lists(self, q, k, lists):
+                full = np.stack([np.asarray(O.ivf_probe(cen, x, 4), np.int32) for x in q])
+                assert np.array_equal(np.asarray(lists), full)
+                i, s = ivf_search(self.rows_idx, centered)
+                return torch.from_numpy(i), torch.from_numpy(s)
+
+        s_ids, s_sc = ivf_sharded_search(Shard(ivf_owned_rows(asg, owners, rank)), qs, 10, 4,
+                                         dist, pack_host, unpack_host, merge_packed_host)
+        ok &= np.array_equal(s_ids.numpy(), want_ids) and np.array_equal(
+            s_sc.numpy().view(np.uint32), want_sc.view(np.uint32))
     if rank == 0:
         Path(result_dir, "ok").write_text("1" if ok else "0")
     dist.barrier()
@@ -278,7 +301,9 @@ def test_sharded_ivf_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
     """world_size 2 on CPU: posting lists dealt by bytes, every rank probes
     all centroids and scans its own lists (the oracle stands in for the
     device search), all-gather, merge == the IVF top-k of the whole index,
-    centered and not."""
+    centered and not; and the same with the probe split by query slices
+    (ivf_sharded_search: probe slice, all-gather of the lists, packed
+    all-to-all and slice merges) on every rank."""
     import socket
 
     import torch.multiprocessing as mp

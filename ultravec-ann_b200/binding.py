@@ -32,7 +32,7 @@ SYMBOLS = [
     "uv_index_export", "uv_index_digest", "uv_index_clear", "uv_topk_merge",
     "uv_profile_enable", "uv_profile_read", "uv_set_tuning", "uv_index_search_noalloc",
     "uv_kmeans", "uv_ivf_assign", "uv_ivf_create", "uv_ivf_destroy", "uv_ivf_build",
-    "uv_ivf_len", "uv_ivf_nlist", "uv_ivf_mem_bytes", "uv_ivf_probe", "uv_ivf_search",
+    "uv_ivf_len", "uv_ivf_nlist", "uv_ivf_mem_bytes", "uv_ivf_probe", "uv_ivf_search", "uv_ivf_search_lists",
     "uv_ivf_search_rerank", "uv_ivf_export", "uv_ivf_digest", "uv_index_save", "uv_index_load",
     "uv_ivf_save", "uv_ivf_load", "uv_index_prepare", "uv_prepared_destroy", "uv_prepared_len",
     "uv_prepared_score", "uv_index_score_candidates", "uv_index_scorer_model_bytes",
@@ -115,6 +115,7 @@ def lib():
             "uv_ivf_mem_bytes": (C.c_int, [vp, C.POINTER(i64)]),
             "uv_ivf_probe": (C.c_int, [vp, vp, i64, i32, vp, vp]),
             "uv_ivf_search": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp]),
+            "uv_ivf_search_lists": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp, vp]),
             "uv_ivf_search_rerank": (C.c_int, [vp, vp, i64, i32, i32, i32, vp, i64, vp, vp,
                                                vp]),
             "uv_ivf_export": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp]),
@@ -228,6 +229,14 @@ def _i64(x):
 
         return x.to(torch.int64).contiguous()
     return np.ascontiguousarray(x, dtype=np.int64)
+
+
+def _i32(x):
+    if _is_torch(x):
+        import torch
+
+        return x.to(torch.int32).contiguous()
+    return np.ascontiguousarray(x, dtype=np.int32)
 
 
 def _f32(x):
@@ -700,6 +709,17 @@ class IvfIndex:
         ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
         check(lib().uv_ivf_search(self.h, _ptr(queries), nq, k, nprobe, _ptr(ids), _ptr(scores),
                                   _stream(queries)))
+        return ids, scores
+
+    def search_lists(self, queries, k: int, lists):
+        """search over probe lists chosen beforehand (nq x nprobe, -1 = no
+        list), e.g. by another shard's probe with the same centroids."""
+        queries, lists = _f32(queries), _i32(lists)
+        nq, nprobe = queries.shape[0], lists.shape[1]
+        alloc = _Alloc(queries)
+        ids, scores = alloc((nq, k), np.int64), alloc((nq, k), np.float32)
+        check(lib().uv_ivf_search_lists(self.h, _ptr(queries), nq, k, nprobe, _ptr(lists),
+                                        _ptr(ids), _ptr(scores), _stream(queries)))
         return ids, scores
 
     def search_with_rerank(self, queries, k: int, nprobe: int, rdepth: int, db):

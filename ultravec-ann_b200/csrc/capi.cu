@@ -714,11 +714,12 @@ int prep_launch(const uv_codec *c, const float *d_q, int64_t nq, const float *ce
   pp.qc = qc;
   pp.degenerate = degen;
   pp.u = u;
-  const size_t smem = (size_t)(dim_pad + 4) * 4 * 8;
+  pp.teams = uvb::prep_teams(d);
+  const size_t smem = (size_t)(dim_pad + 4) * 4 * pp.teams;
   UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem));
-  const int grid =
-      (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(c->cfg.device) * 8));
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((nq + pp.teams - 1) / pp.teams, INT32_MAX));
   void *args[] = {&pp};
   ProfScope ps("prep_queries", st);
   UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args, smem,
@@ -2376,10 +2377,12 @@ int uv_index_search_noalloc(const uv_index *ix, const float *queries, int64_t nq
     pp.q_r = q_r;
     pp.qc = qc;
     pp.degenerate = degen;
-    const size_t psmem = (size_t)(dim_pad + 4) * 4 * 8;
+    pp.teams = uvb::prep_teams(d);
+    const size_t psmem = (size_t)(dim_pad + 4) * 4 * pp.teams;
     UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((nq + pp.teams - 1) / pp.teams, INT32_MAX));
     void *args[] = {&pp};
     ProfScope ps("prep_queries", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,

@@ -501,10 +501,12 @@ int uv_coset_search(const uv_coset *ix, const float *queries, int64_t nq, int32_
     pp.qc = qc;
     pp.degenerate = degen;
     pp.clamp_norm = 1;
-    const size_t smem = (size_t)(d16 + 4) * 4 * 8;
+    pp.teams = uvb::prep_teams(pp.dim);
+    const size_t smem = (size_t)(d16 + 4) * 4 * pp.teams;
     UV_CK(cudaFuncSetAttribute(uvb::prep_queries_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nq + 7) / 8, sm_count(dev) * 8));
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((nq + pp.teams - 1) / pp.teams, INT32_MAX));
     void *args[] = {&pp};
     ProfScope ps("prep_queries", st);
     UV_CK(cudaLaunchKernel((const void *)uvb::prep_queries_kernel, dim3(grid), dim3(256), args,

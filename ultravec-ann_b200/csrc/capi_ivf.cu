@@ -482,7 +482,9 @@ int list_rows(const uv_ivf *ix, cudaStream_t st, Scratch &sc, const TcRows **out
 
 // The bucketed pairs of one search, as search_device makes them.
 struct PairBuckets {
-  int64_t npairs = 0, n_items = 0, n_rslots = 0, range_size = 0;
+  int64_t npairs = 0;   // bucketed pairs (probes of lists with records here)
+  int64_t nprobes = 0;  // nq x nprobe
+  int64_t n_items = 0, n_rslots = 0, range_size = 0;
   const int32_t *pair_query = nullptr, *pair_slot = nullptr, *pair_off = nullptr;
   const int64_t *list_rbase = nullptr, *row_off = nullptr;
   const float *pair_qm = nullptr;
@@ -524,8 +526,8 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
   int32_t *pair_of = nullptr;
   UV_TRY(sc.alloc(&pa16, (size_t)rows_a * kpad));
   UV_TRY(sc.alloc(&ax, (size_t)uvb::kIvfTcRows * 16));
-  UV_TRY(sc.alloc(&pair_of, (size_t)b.npairs));
-  UV_CK(cudaMemsetAsync(pair_of, 0xff, sizeof(int32_t) * (size_t)b.npairs, st));  // -1: no pair
+  UV_TRY(sc.alloc(&pair_of, (size_t)b.nprobes));
+  UV_CK(cudaMemsetAsync(pair_of, 0xff, sizeof(int32_t) * (size_t)b.nprobes, st));  // -1: no pair
   {
     ProfScope ps("ivf_tc_pairs", st);
     const int64_t chunks = b.npairs * (kpad / 8);
@@ -533,7 +535,9 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
                                   256, 0, st>>>(q_r, q_stride, degen, b.pair_query, b.npairs, d,
                                                 kpad, pa16);
     uvb::ivf_neg_slice_kernel<<<(uvb::kIvfTcRows * 16 + 255) / 256, 256, 0, st>>>(ax);
-    uvb::ivf_pair_of_kernel<<<blocks(b.npairs, 256), 256, 0, st>>>(b.pair_slot, b.npairs, pair_of);
+    if (b.npairs > 0)
+      uvb::ivf_pair_of_kernel<<<blocks(b.npairs, 256), 256, 0, st>>>(b.pair_slot, b.npairs,
+                                                                      pair_of);
     UV_CK(cudaGetLastError());
   }
   alignas(64) CUtensorMap tmap_a, tmap_ax, tmap_b, tmap_bx;
@@ -654,8 +658,11 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
 
 // ivf.rs:229-239 on device: per-list top-k of every probed (query, list)
 // pair, merged per query.  Device inputs and outputs.
+// given_lists (device, nq x np, -1 = no list) replaces the probe: lists
+// chosen elsewhere, e.g. by another rank with the same centroids.
 int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np, int64_t *d_ids,
-                  float *d_scores, cudaStream_t st, Scratch &sc, bool allow_tc = true) {
+                  float *d_scores, cudaStream_t st, Scratch &sc, bool allow_tc = true,
+                  const int32_t *given_lists = nullptr) {
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   if (np == 0 || ix->n == 0) {
@@ -677,7 +684,12 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   if (npairs > INT32_MAX) return fail(UV_EINVAL, "nq * nprobe exceeds 2^31 - 1");
   int32_t *lists = nullptr;
   UV_TRY(sc.alloc(&lists, (size_t)npairs));
-  UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc));
+  if (given_lists != nullptr) {
+    UV_CK(cudaMemcpyAsync(lists, given_lists, sizeof(int32_t) * (size_t)npairs,
+                          cudaMemcpyDeviceToDevice, st));
+  } else {
+    UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc));
+  }
   // bucket the (query, list) pairs by list; a scan item is one record range
   // (at most range_size records: long lists are split for load balance) of
   // one list for up to 32 of its pairs
@@ -699,6 +711,14 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                             pid, psc, st));
     return merge_launch(nq, np, k, k, nullptr, psc, pid, d_ids, d_scores, st);
   }
+  // probes of lists without records here (a list owned by another shard,
+  // or empty) make no pair
+  int *bad = nullptr;
+  UV_TRY(sc.alloc(&bad, 1));
+  UV_CK(cudaMemsetAsync(bad, 0, sizeof(int), st));
+  uvb::drop_empty_lists_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, npairs, ix->d_off,
+                                                                    nlist, bad);
+  UV_CK(cudaGetLastError());
   // the tensor-core list scan: items of up to kIvfTcRows pairs and ranges
   // of kIvfTcRange records; the CUDA-core scan: items of kScanTQ pairs, and
   // ranges such that a pair's ranges merge in one pass of about 1024 entries
@@ -714,7 +734,7 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   UV_TRY(sc.alloc(&pair_off, (size_t)nlist));
   UV_TRY(sc.alloc(&item_off, (size_t)nlist));
   UV_TRY(sc.alloc(&list_rbase, (size_t)nlist));
-  UV_TRY(sc.alloc(&totals, 2));
+  UV_TRY(sc.alloc(&totals, 3));
   UV_TRY(sc.alloc(&pair_query, (size_t)npairs));
   UV_TRY(sc.alloc(&pair_slot, (size_t)npairs));
   UV_TRY(sc.alloc(&pair_list, (size_t)npairs));
@@ -728,10 +748,15 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                                                                   pair_query, pair_slot, pair_list);
     UV_CK(cudaGetLastError());
   }
-  int64_t h_tot[2] = {0, 0};
+  int64_t h_tot[3] = {0, 0, 0};
+  int h_bad = 0;
   UV_CK(cudaMemcpyAsync(h_tot, totals, sizeof(h_tot), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaMemcpyAsync(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
   const int64_t n_items = h_tot[0], n_rslots = h_tot[1];
+  if (h_bad) return fail(UV_EINVAL, "a probe list id is outside 0..nlist-1");
+  // the bucketed pairs: probes of lists with records here
+  const int64_t npv = h_tot[2];
   if (n_items > INT32_MAX) return fail(UV_EINVAL, "too many scan items");
   int32_t *item_list = nullptr, *item_pair = nullptr, *item_npairs = nullptr,
           *item_range = nullptr, *d_n_items = nullptr;
@@ -749,24 +774,27 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
     uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(
         cnt, pair_off, item_off, ix->d_off, nlist, range_size, per_item, item_list, item_pair,
         item_npairs, item_range);
-    uvb::pair_rows_kernel<<<blocks(npairs + 1, 256), 256, 0, st>>>(
-        pair_list, pair_off, list_rbase, ix->d_off, range_size, (int)npairs, row_off);
+    uvb::pair_rows_kernel<<<blocks(npv + 1, 256), 256, 0, st>>>(
+        pair_list, pair_off, list_rbase, ix->d_off, range_size, (int)npv, row_off);
     UV_CK(cudaGetLastError());
     UV_CK(cudaStreamSynchronize(st));  // `ni` is a host value of this frame
   }
   float *pair_qm = nullptr;
   if (ix->centered) {
-    UV_TRY(sc.alloc(&pair_qm, (size_t)npairs));
+    UV_TRY(sc.alloc(&pair_qm, (size_t)std::max<int64_t>(npv, 1)));
     ProfScope ps("ivf_pair_qm", st);
-    uvb::pair_qm_kernel<<<(unsigned)((npairs + 32 * uvb::kPairQmWarps - 1) /
-                                     (32 * uvb::kPairQmWarps)),
-                          32 * uvb::kPairQmWarps, 0, st>>>(u, dim_pad, ix->centroids, d, pair_query,
-                                                           pair_list, (int)npairs, pair_qm);
+    if (npv > 0)
+      uvb::pair_qm_kernel<<<(unsigned)((npv + 32 * uvb::kPairQmWarps - 1) /
+                                       (32 * uvb::kPairQmWarps)),
+                            32 * uvb::kPairQmWarps, 0, st>>>(u, dim_pad, ix->centroids, d,
+                                                             pair_query, pair_list, (int)npv,
+                                                             pair_qm);
     UV_CK(cudaGetLastError());
   }
   if (tc) {
     PairBuckets b;
-    b.npairs = npairs;
+    b.npairs = npv;
+    b.nprobes = npairs;
     b.n_items = n_items;
     b.n_rslots = n_rslots;
     b.range_size = range_size;
@@ -786,7 +814,7 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
                         &fallback));
     if (!fallback) return UV_OK;
     // a store overflowed: the CUDA-core scan, from the probe on
-    return search_device(ix, d_q, nq, k, np, d_ids, d_scores, st, sc, false);
+    return search_device(ix, d_q, nq, k, np, d_ids, d_scores, st, sc, false, given_lists);
   }
   // scan every item: one top-k per (pair, range) slot
   uint32_t *part_key = nullptr;
@@ -861,8 +889,13 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   UV_TRY(sc.alloc(&pid, (size_t)npairs * k));
   UV_TRY(sc.alloc(&psc, (size_t)npairs * k));
   (void)pk;
-  UV_TRY(merge_launch(npairs, max_ranges, k, k, part_key, nullptr, part_id, pid, psc, st,
-                      row_off, pair_slot));
+  if (npv < npairs) {  // probes without a pair: empty lists for the per-query merge
+    uvb::fill_empty_kernel<<<blocks(npairs * k, 256), 256, 0, st>>>(pid, psc, npairs * k);
+    UV_CK(cudaGetLastError());
+  }
+  if (npv > 0)
+    UV_TRY(merge_launch(npv, max_ranges, k, k, part_key, nullptr, part_id, pid, psc, st, row_off,
+                        pair_slot));
   return merge_launch(nq, np, k, k, nullptr, psc, pid, d_ids, d_scores, st);
 }
 
@@ -1144,6 +1177,37 @@ int uv_ivf_search(const uv_ivf *ix, const float *queries, int64_t nq, int32_t k,
     UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
   }
   UV_TRY(search_device(ix, d_q, nq, k, std::min(nprobe, ix->nlist), d_ids, d_scores, st, sc));
+  return outs.finish(st);
+}
+
+int uv_ivf_search_lists(const uv_ivf *ix, const float *queries, int64_t nq, int32_t k,
+                        int32_t nprobe, const int32_t *lists, int64_t *ids_out, float *scores_out,
+                        void *stream) {
+  if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr ||
+                                   (nprobe > 0 && lists == nullptr))))
+    return fail(UV_EINVAL, "null argument");
+  if (nq < 0 || nprobe < 0) return fail(UV_EINVAL, "negative size");
+  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (nq == 0) return UV_OK;
+  if (nq * (int64_t)nprobe > INT32_MAX) return fail(UV_EINVAL, "nq * nprobe exceeds 2^31 - 1");
+  const int dev = ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch sc(st);
+  Outputs outs;
+  const float *d_q = nullptr;
+  const int32_t *d_lists = nullptr;
+  UV_TRY(stage_in(queries, (size_t)nq * ix->codec->cfg.dim, dev, sc, &d_q));
+  if (nprobe > 0) UV_TRY(stage_in(lists, (size_t)nq * nprobe, dev, sc, &d_lists));
+  int64_t *d_ids = nullptr;
+  float *d_scores = nullptr;
+  UV_TRY(outs.stage(ids_out, (size_t)nq * k, dev, sc, &d_ids));
+  if (scores_out != nullptr) {
+    UV_TRY(outs.stage(scores_out, (size_t)nq * k, dev, sc, &d_scores));
+  } else {
+    UV_TRY(sc.alloc(&d_scores, (size_t)nq * k));
+  }
+  UV_TRY(search_device(ix, d_q, nq, k, nprobe, d_ids, d_scores, st, sc, true, d_lists));
   return outs.finish(st);
 }
 

@@ -340,6 +340,22 @@ __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n) {
 }
 
 // ---- (query, list) pairs bucketed by list ----
+// Probes of lists that hold no records contribute nothing: they become -1
+// (no pair).  A list id outside 0..nlist-1 sets *bad.
+__global__ void drop_empty_lists_kernel(int32_t *lists, int64_t npairs, const int64_t *list_off,
+                                        int nlist, int *bad) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= npairs) return;
+  const int l = lists[i];
+  if (l < 0) return;
+  if (l >= nlist) {
+    atomicExch(bad, 1);
+    lists[i] = -1;
+    return;
+  }
+  if (list_off[l + 1] == list_off[l]) lists[i] = -1;
+}
+
 __global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < npairs && lists[i] >= 0) atomicAdd(&cnt[lists[i]], 1);
@@ -353,7 +369,7 @@ __device__ __forceinline__ int64_t list_ranges(int64_t size, int64_t range_size)
 
 // One CTA: exclusive scans over the lists of the pair counts, of the scan
 // items (ranges x ceil(pairs / per_item)) and of the range slots (pairs x
-// ranges); totals = {items, range slots}.
+// ranges); totals = {items, range slots, pairs}.
 __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
                                                          const int64_t *list_off, int nlist,
                                                          int64_t range_size, int per_item,
@@ -394,6 +410,7 @@ __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t *cnt,
     rbase += nr * cnt[l];
   }
   if (t == 1023) {
+    totals[2] = sp[1023];
     totals[0] = si[1023];
     totals[1] = sr[1023];
   }

@@ -34,21 +34,25 @@ namespace uvb {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
   extern __shared__ __align__(16) float smem[];
-  const int team = threadIdx.x >> 5;
+  // teams of 256 / teams threads, one query each: warps for narrow rows, the
+  // whole CTA for wide ones (the FWHT stages then spread over 256 threads)
+  const int teams = p.teams > 0 ? p.teams : 8;
   Team tm;
-  tm.T = 32;
-  tm.cta = false;
-  tm.t = threadIdx.x & 31;
+  tm.T = 256 / teams;
+  tm.cta = teams == 1;
+  tm.t = threadIdx.x % tm.T;
+  const int team = threadIdx.x / tm.T;
+  const int T = tm.T;
   float *x = smem + (size_t)team * (p.dim_pad + 4);
   float *misc = x + p.dim_pad;
   const int d = p.dim;
-  const int64_t iters = (p.nq + (int64_t)gridDim.x * 8 - 1) / ((int64_t)gridDim.x * 8);
+  const int64_t per = (int64_t)gridDim.x * teams;
+  const int64_t iters = (p.nq + per - 1) / per;
   for (int64_t it = 0; it < iters; it++) {
-    const int64_t q = ((int64_t)it * gridDim.x + blockIdx.x) * 8 + team;
-    const bool valid = q < p.nq;
-    const int64_t qq = valid ? q : p.nq - 1;
+    const int64_t qq = ((int64_t)it * gridDim.x + blockIdx.x) * teams + team;
+    if (qq >= p.nq) continue;  // uniform over the team; teams never wait on each other
     const float *src = p.queries + qq * (int64_t)d;
-    for (int i = tm.t; i < d; i += 32) x[i] = src[i];
+    for (int i = tm.t; i < d; i += T) x[i] = src[i];
     tm.sync();
     if (tm.leader()) {
       const float l2 = fsqrt(seq_sum_sq(x, d));
@@ -58,30 +62,27 @@ __global__ void __launch_bounds__(256) prep_queries_kernel(const PrepParams p) {
     const float qn = misc[0];
     const bool degenerate = !p.clamp_norm && !(qn >= kF32Eps);
     if (!degenerate) {
-      for (int i = tm.t; i < d; i += 32) x[i] = fdiv(x[i], qn);
+      for (int i = tm.t; i < d; i += T) x[i] = fdiv(x[i], qn);
       tm.sync();
-      if (p.u != nullptr && valid)
-        for (int i = tm.t; i < d; i += 32) p.u[qq * (int64_t)p.dim_pad + i] = x[i];
-      for (int j = tm.t; j < p.n_centroids; j += 32) {
-        float dj = seq_dot(x, p.centroids + (size_t)j * d, d);
-        if (valid) p.qc[qq * p.n_centroids + j] = dj;
-      }
+      if (p.u != nullptr)
+        for (int i = tm.t; i < d; i += T) p.u[qq * (int64_t)p.dim_pad + i] = x[i];
+      for (int j = tm.t; j < p.n_centroids; j += T)
+        p.qc[qq * p.n_centroids + j] = seq_dot(x, p.centroids + (size_t)j * d, d);
       team_rotate(x, p.rot, tm, false);
     } else {
-      for (int i = tm.t; i < d; i += 32) x[i] = 0.0f;
-      if (p.u != nullptr && valid)
-        for (int i = tm.t; i < d; i += 32) p.u[qq * (int64_t)p.dim_pad + i] = 0.0f;
-      for (int j = tm.t; j < p.n_centroids; j += 32)
-        if (valid) p.qc[qq * p.n_centroids + j] = 0.0f;
+      for (int i = tm.t; i < d; i += T) x[i] = 0.0f;
+      if (p.u != nullptr)
+        for (int i = tm.t; i < d; i += T) p.u[qq * (int64_t)p.dim_pad + i] = 0.0f;
+      for (int j = tm.t; j < p.n_centroids; j += T) p.qc[qq * p.n_centroids + j] = 0.0f;
       tm.sync();
     }
-    if (valid) {
-      for (int i = tm.t; i < d; i += 32) p.q_r[qq * (int64_t)p.dim_pad + i] = x[i];
-      if (tm.leader()) p.degenerate[qq] = degenerate ? 1u : 0u;
-    }
+    for (int i = tm.t; i < d; i += T) p.q_r[qq * (int64_t)p.dim_pad + i] = x[i];
+    if (tm.leader()) p.degenerate[qq] = degenerate ? 1u : 0u;
     tm.sync();
   }
 }
+
+int prep_teams(int dim) { return dim >= 512 ? 1 : 8; }
 
 // ---------------------------------------------------------------------------
 // Flat scan + top-k.

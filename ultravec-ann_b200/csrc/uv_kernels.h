@@ -82,7 +82,11 @@ struct PrepParams {
   uint32_t *degenerate;  // nq
   float *u;              // or null: nq x dim_pad unit queries (before rotation)
   int clamp_norm;        // |q| clamped at EPS instead of a degenerate query
+  int teams;             // queries per CTA of 256 threads: 8 (a warp each) or 1 (0: 8)
 };
+// prep_queries_kernel's teams per CTA for rows of width dim (prep_teams(dim)
+// x (dim_pad + 4) floats of dynamic shared memory)
+int prep_teams(int dim);
 
 // The coset trellis's model (coset.cu, src/coset_trellis.rs): book points
 // are 64-bit keys, norm << 40 | the eight raw doubled coordinates offset by
@@ -397,6 +401,8 @@ __global__ void select_top_kernel(const float *scores, int64_t n, int nb, int po
                                   int ld_out, int32_t *out);
 __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n);
 __global__ void pair_count_kernel(const int32_t *lists, int64_t npairs, int32_t *cnt);
+__global__ void drop_empty_lists_kernel(int32_t *lists, int64_t npairs, const int64_t *list_off,
+                                        int nlist, int *bad);
 // per_item: pairs of one list per scan item (kScanTQ for chunked_scan_kernel,
 // kIvfTcRows for tc_ivf_kernel)
 __global__ void pair_scan_kernel(const int32_t *cnt, const int64_t *list_off, int nlist,

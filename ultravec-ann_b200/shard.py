@@ -3,11 +3,14 @@
 Flat index: the base rows are split into contiguous ranges; every rank
 encodes and scans its own range (records keep their global row ids).  IVF
 index: the posting lists are dealt to ranks so that each rank holds about the
-same number of record bytes; every rank keeps all centroids, probes
-redundantly, and scans only the probed lists it owns, so each probed list is
-scanned exactly once.  The flat search exchanges first-pass bounds between
-the shards before they keep candidates (sharded_search); the IVF lists are
-combined by one all-gather and a merge (gather_topk).  The merge is a function argument so that the
+same number of record bytes; every rank keeps all centroids, probes its own
+query slice, shares the probe lists by one all-gather, and scans only the
+probed lists it owns, so each query is probed once and each probed list is
+scanned once (ivf_sharded_search).  The flat search exchanges first-pass
+bounds between the shards before they keep candidates (sharded_search).
+Both combine the per-rank lists with one packed all-to-all of query slices,
+per-slice merges and one all-gather (combine_topk); gather_topk is the plain
+all-gather + merge.  The merge is a function argument so that the
 same sequence runs with the device merge (`uv_topk_merge`) under NCCL and
 with a host merge under gloo.
 """
@@ -113,6 +116,21 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
         ids, scores = s.finish()
     finally:
         s.close()
+    return combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
+
+
+def combine_topk(ids, scores, k: int, dist, pack, unpack, merge_packed):
+    """Every rank's (nq, k) lists -> the global (nq, k) top-k on every rank:
+    the lists travel once, packed (`pack`: ids and scores in one 12-byte
+    record); an all-to-all hands rank r every shard's lists for its query
+    slice, rank r merges its slice (`merge_packed`, row stride k, list stride
+    rows * k), and one all-gather of the merged, packed slices (padded to the
+    largest slice) gives every rank the answer."""
+    import torch
+
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    nq = ids.shape[0]
     packed = pack(ids, scores).reshape(-1)
     lo, hi = query_slice(nq, rank, world)
     rows = hi - lo
@@ -136,6 +154,40 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
     parts = [allp[r, :query_slice(nq, r, world)[1] - query_slice(nq, r, world)[0]]
              for r in range(world)]
     return unpack(torch.cat(parts, 0))
+
+
+def ivf_sharded_search(ivf, queries, k: int, nprobe: int, dist, pack, unpack, merge_packed):
+    """The IVF search of a base whose posting lists are dealt to ranks
+    (ivf_list_owners): rank r probes only its query slice (every rank holds
+    all centroids), one all-gather shares the probe lists, every rank scans
+    the probed lists it holds for all queries (IvfIndex.search_lists; lists
+    held elsewhere are skipped), and the per-rank lists combine as in
+    combine_topk.  The probe is done once per query instead of once per
+    rank."""
+    import torch
+
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    nq = queries.shape[0]
+    lo, hi = query_slice(nq, rank, world)
+    rows_max = (nq + world - 1) // world
+    mine = ivf.probe(queries[lo:hi], nprobe)
+    if not hasattr(mine, "device"):
+        mine = torch.from_numpy(mine)
+    pad = torch.full((rows_max, nprobe), -1, dtype=torch.int32, device=mine.device)
+    pad[:hi - lo] = mine
+    allp = torch.empty((world * rows_max, nprobe), dtype=torch.int32, device=mine.device)
+    dist.all_gather_into_tensor(allp, pad)
+    if rows_max * world == nq:
+        lists = allp
+    else:
+        allp = allp.view(world, rows_max, nprobe)
+        lists = torch.cat([allp[r, :query_slice(nq, r, world)[1] - query_slice(nq, r, world)[0]]
+                           for r in range(world)], 0)
+    ids, scores = ivf.search_lists(queries, k, lists)
+    if not hasattr(ids, "device"):
+        ids, scores = torch.from_numpy(ids), torch.from_numpy(scores)
+    return combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
 
 
 def pack_host(ids, scores):
