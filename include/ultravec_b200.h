@@ -499,9 +499,10 @@ int uv_coset_set_centroids(uv_coset *coset, const float *centroids, int32_t n_ce
  * the reference's add_batch assigns them, 454-469).  Rows n x dim f32. */
 int uv_coset_add(uv_coset *coset, const int64_t *ids, const float *rows, int64_t n,
                  void *stream);
-/* search (471-497), k 1..128: score = <q,c> + rnorm * dot(q_r, x-bar) /
+/* search (471-497), any k >= 1: score = <q,c> + rnorm * dot(q_r, x-bar) /
  * rescale, descending, ties by insertion position; slots past len() hold id
- * -1 and score -inf.  Host or device buffers. */
+ * -1 and score -inf.  Above k = 128 every record's score is ranked (the
+ * reference sorts them all and truncates).  Host or device buffers. */
 int uv_coset_search(const uv_coset *coset, const float *queries, int64_t nq, int32_t k,
                     int64_t *ids_out, float *scores_out, void *stream);
 int uv_coset_len(const uv_coset *coset, int64_t *n);

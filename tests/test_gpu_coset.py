@@ -112,6 +112,9 @@ def test_centered_records_and_search(uv, oracle):
     (24, 1, 3, 1500, 100),    # padded lanes of the last 8-wide block
     (128, 2, 8, 5000, 128),
     (512, 1, 6, 700, 32),     # rows too wide for the flat tile: K-chunked scan
+    (64, 2, 12, 3000, 3000),  # k = n: every record ranked (full ranking above 128)
+    (24, 1, 3, 1500, 200),
+    (512, 1, 6, 700, 701),    # K-chunked scan, k past n: the tail unfilled
 ])
 def test_search_matches_oracle(uv, oracle, dim, bits, mem, n, k):
     g, o = _pair(uv, oracle, dim, bits, mem)
@@ -174,7 +177,9 @@ def test_sizes_and_refusals(uv, oracle):
         with pytest.raises(uv.UVError):
             uv.CosetIndex(dim, bits, mem=mem)
     with pytest.raises(uv.UVError):
-        g.search(rand_rows(2, 128, 3), 129)
+        g.search(rand_rows(2, 128, 3), 0)
+    ids, sc = g.search(rand_rows(2, 128, 3), 129)  # any k: the tail unfilled
+    assert (ids[:, 10:] == -1).all() and (ids[:, :10] >= 0).all()
 
 
 def test_device_tensors(uv, oracle):

@@ -879,14 +879,19 @@ int rank_sort_rows(uint32_t *ka, int64_t *ia, uint32_t *kb, int64_t *ib, int64_t
 // kernel (ScanParams::all_key), a sort of each query's n (key, id) pairs
 // (rank.cu), then its first k.  Outputs go straight into device buffers, or
 // through a chunk buffer into host ones.
-int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
-                     const uint32_t *degen, int64_t nq, int64_t k, int mode, int64_t *ids_out,
-                     float *scores_out, cudaStream_t st, Scratch &sc) {
-  const uv_codec *c = ix->codec;
-  const int d = (c->cfg.dim + 15) & ~15;
-  const int dev = c->cfg.device;
-  const int dim_pad = (c->cfg.dim + 3) & ~3;
-  const int64_t n = ix->n;
+}  // namespace
+
+namespace uvcapi {
+
+// Every (query, record) score of an exact scan kernel with all_key set
+// (p0 describes all nq queries; chunks of queries re-base q_r, qc and
+// degenerate), each query's n keys sorted (rank_sort_rows keeps the best k
+// of every run), then the best k as ids and scores ranked (score desc, id
+// asc); slots past n hold -1 / -inf.  Outputs: host or device memory.
+int rank_all_scores(const uvb::ScanParams &p0, const void *scan_k, size_t smem, int64_t nq,
+                    int64_t k, int64_t *ids_out, float *scores_out, int dev, cudaStream_t st,
+                    Scratch &sc) {
+  const int64_t n = p0.n;
   bool ids_dev = false, sc_dev = false;
   UV_TRY(classify(ids_out, dev, &ids_dev));
   UV_TRY(classify(scores_out, dev, &sc_dev));
@@ -912,20 +917,11 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
     UV_TRY(sc.alloc(&c_ids, (size_t)qb * k));
     if (scores_out != nullptr) UV_TRY(sc.alloc(&c_sc, (size_t)qb * k));
   }
-  const int rw = c->code_stride / 4;
-  int img_words = 4 + rw + 3;
-  if ((img_words & 1) == 0) img_words++;
-  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
-  const bool chunked = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem) > 227 * 1024;
-  const size_t smem = chunked ? uvb::chunked_scan_smem_bytes(c->table_len, table_smem, true)
-                              : uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
-  const void *scan_k = chunked ? uvb::chunked_scan_kernel_ptr(c->cfg.bits, table_smem, true)
-                               : uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
-  if (scan_k == nullptr) return fail(UV_EUNSUPPORTED, "no scan kernel for these bits");
   UV_CK(cudaFuncSetAttribute(scan_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 1;
   UV_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_k, 256, smem));
   const int64_t slots = (int64_t)sm_count(dev) * std::max(per_sm, 1);
+  const int qc_stride = std::max(1, p0.n_centroids);
   for (int64_t q0 = 0; q0 < nq; q0 += qb) {
     const int64_t m = std::min(qb, nq - q0);
     uint32_t *kin = key0;
@@ -935,11 +931,16 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
       const int64_t qtiles = (m + uvb::kScanTQ - 1) / uvb::kScanTQ;
       int64_t splits = std::max<int64_t>(1, (2 * slots + qtiles - 1) / qtiles);
       splits = std::min<int64_t>(std::min<int64_t>(splits, std::max<int64_t>(1, n / 256)), 65535);
-      uvb::ScanParams sp;
-      fill_scan_params(ix, q_r + q0 * dim_pad, qc + q0 * std::max(1, ix->n_centroids),
-                       degen + q0, m, 1, mode, img_words, table_smem, &sp);
+      uvb::ScanParams sp = p0;
+      sp.nq = m;
+      sp.k = 1;
+      sp.q_r = p0.q_r + q0 * (int64_t)p0.q_stride;
+      sp.qc = p0.qc + q0 * (int64_t)qc_stride;
+      sp.degenerate = p0.degenerate + q0;
       sp.all_key = key0;
       sp.all_id = id0;
+      sp.part_key = nullptr;
+      sp.part_id = nullptr;
       uvb::ScanWork work;
       std::memset(&work, 0, sizeof(work));
       void *args[] = {&sp, &work};
@@ -962,8 +963,8 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
       ProfScope ps("rank_emit", st);
       const int64_t total = m * k;
       const unsigned g = (unsigned)std::min<int64_t>((total + 255) / 256, slots * 8);
-      uvb::rank_emit_kernel<<<std::max(g, 1u), 256, 0, st>>>(kin, iin, n, m, k, degen + q0, o_ids,
-                                                            o_sc);
+      uvb::rank_emit_kernel<<<std::max(g, 1u), 256, 0, st>>>(kin, iin, n, m, k,
+                                                            p0.degenerate + q0, o_ids, o_sc);
       UV_CK(cudaGetLastError());
     }
     if (!direct) {
@@ -976,6 +977,31 @@ int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
     }
   }
   return UV_OK;
+}
+
+}  // namespace uvcapi
+
+namespace {
+
+int full_rank_search(const uv_index *ix, const float *q_r, const float *qc,
+                     const uint32_t *degen, int64_t nq, int64_t k, int mode, int64_t *ids_out,
+                     float *scores_out, cudaStream_t st, Scratch &sc) {
+  const uv_codec *c = ix->codec;
+  const int d = (c->cfg.dim + 15) & ~15;
+  const int dev = c->cfg.device;
+  const int rw = c->code_stride / 4;
+  int img_words = 4 + rw + 3;
+  if ((img_words & 1) == 0) img_words++;
+  const bool table_smem = (size_t)c->table_len * 4 <= 16 * 1024;
+  const bool chunked = uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem) > 227 * 1024;
+  const size_t smem = chunked ? uvb::chunked_scan_smem_bytes(c->table_len, table_smem, true)
+                              : uvb::scan_smem_bytes(d, img_words, c->table_len, table_smem);
+  const void *scan_k = chunked ? uvb::chunked_scan_kernel_ptr(c->cfg.bits, table_smem, true)
+                               : uvb::flat_scan_kernel_ptr(c->cfg.bits, table_smem);
+  if (scan_k == nullptr) return fail(UV_EUNSUPPORTED, "no scan kernel for these bits");
+  uvb::ScanParams sp;
+  fill_scan_params(ix, q_r, qc, degen, nq, 1, mode, img_words, table_smem, &sp);
+  return rank_all_scores(sp, scan_k, smem, nq, k, ids_out, scores_out, dev, st, sc);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link

@@ -462,7 +462,7 @@ int uv_coset_search(const uv_coset *ix, const float *queries, int64_t nq, int32_
   if (ix == nullptr || (nq > 0 && (queries == nullptr || ids_out == nullptr)))
     return fail(UV_EINVAL, "null argument");
   if (nq < 0) return fail(UV_EINVAL, "negative size");
-  if (k < 1 || k > uvb::kScanKCap) return fail(UV_EINVAL, "k must be 1..128");
+  if (k < 1) return fail(UV_EINVAL, "k must be at least 1");
   if (nq == 0) return UV_OK;
   const int d = ix->dim, dev = ix->device;
   const int d16 = (d + 15) & ~15;
@@ -516,7 +516,7 @@ int uv_coset_search(const uv_coset *ix, const float *queries, int64_t nq, int32_
   const int64_t n = ix->n;
   const int64_t qtiles = (nq + uvb::kScanTQ - 1) / uvb::kScanTQ;
   const bool chunked = uvb::scan_smem_bytes(d16, 0, 0, false) > 227 * 1024;
-  const bool small_k = k <= 32;
+  const bool small_k = k <= 32 || k > uvb::kScanKCap;
   const size_t smem = chunked ? uvb::chunked_scan_smem_bytes(0, false, small_k)
                               : uvb::scan_smem_bytes(d16, 0, 0, false);
   const void *scan_k =
@@ -539,6 +539,32 @@ int uv_coset_search(const uv_coset *ix, const float *queries, int64_t nq, int32_
     }
     if (eff >= 0.9) break;
   }
+  uvb::ScanParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  sp.dim = d16;
+  sp.mem = ix->mem;
+  sp.bits = 0;
+  sp.nq = nq;
+  sp.n = n;
+  sp.q_r = q_r;
+  sp.q_stride = d16;
+  sp.qc = qc;
+  sp.n_centroids = ix->n_centroids;
+  sp.degenerate = degen;
+  sp.codes = ix->codes;
+  sp.code_stride = ix->m.code_stride;
+  sp.rescale = ix->rescale;
+  sp.rnorm = ix->rnorm;
+  sp.cidx = ix->cidx;
+  sp.k = k;
+  sp.ids = ix->ids;
+  sp.coset = ix->m;
+  if (k > uvb::kScanKCap) {
+    // any k: every score, sorted per query (the reference sorts all, then
+    // truncates, src/coset_trellis.rs:471-497)
+    UV_TRY(rank_all_scores(sp, scan_k, smem, nq, k, d_ids, d_scores, dev, st, sc));
+    return outs.finish(st);
+  }
   uint32_t *part_key = nullptr;
   int64_t *part_id = nullptr;
   UV_TRY(sc.alloc(&part_key, (size_t)nq * splits * k));
@@ -547,28 +573,8 @@ int uv_coset_search(const uv_coset *ix, const float *queries, int64_t nq, int32_
     UV_CK(cudaMemsetAsync(part_key, 0, sizeof(uint32_t) * nq * splits * k, st));
     UV_CK(cudaMemsetAsync(part_id, 0xff, sizeof(int64_t) * nq * splits * k, st));
   } else {
-    uvb::ScanParams sp;
-    std::memset(&sp, 0, sizeof(sp));
-    sp.dim = d16;
-    sp.mem = ix->mem;
-    sp.bits = 0;
-    sp.nq = nq;
-    sp.n = n;
-    sp.q_r = q_r;
-    sp.q_stride = d16;
-    sp.qc = qc;
-    sp.n_centroids = ix->n_centroids;
-    sp.degenerate = degen;
-    sp.codes = ix->codes;
-    sp.code_stride = ix->m.code_stride;
-    sp.rescale = ix->rescale;
-    sp.rnorm = ix->rnorm;
-    sp.cidx = ix->cidx;
-    sp.k = k;
-    sp.ids = ix->ids;
     sp.part_key = part_key;
     sp.part_id = part_id;
-    sp.coset = ix->m;
     uvb::ScanWork work;
     std::memset(&work, 0, sizeof(work));
     void *args[] = {&sp, &work};

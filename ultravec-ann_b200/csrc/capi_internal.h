@@ -292,6 +292,14 @@ struct uv_index {
 
 namespace uvcapi {
 
+// Every (query, record) score of an exact scan kernel (p0 with all_key
+// filled by the routine; nq queries), sorted per query; the best k as ids
+// and scores ranked (score desc, id asc), slots past n -1 / -inf.  Outputs:
+// host or device memory.  For k above the scan's top-k capacity (capi.cu).
+int rank_all_scores(const uvb::ScanParams &p0, const void *scan_k, size_t smem, int64_t nq,
+                    int64_t k, int64_t *ids_out, float *scores_out, int dev, cudaStream_t st,
+                    Scratch &sc);
+
 int encode_device(const uv_codec *c, const float *rows, int64_t n, const float *centroids,
                   int n_centroids, bool rotated, uint8_t *codes, uint32_t *start, float *rescale,
                   float *rnorm, uint32_t *cidx, float *norms, cudaStream_t st, Scratch &sc,

@@ -528,12 +528,19 @@ int tc_list_scan(const uv_ivf *ix, int64_t nq, int k, int np, const float *q_r, 
   UV_TRY(sc.alloc(&ax, (size_t)uvb::kIvfTcRows * 16));
   UV_TRY(sc.alloc(&pair_of, (size_t)b.nprobes));
   UV_CK(cudaMemsetAsync(pair_of, 0xff, sizeof(int32_t) * (size_t)b.nprobes, st));  // -1: no pair
+  // the queries' fp16 rows (zero past d and for degenerate queries), once
+  uint16_t *a16 = nullptr, *axq = nullptr;
+  UV_TRY(sc.alloc(&a16, (size_t)nq * kpad));
+  UV_TRY(sc.alloc(&axq, (size_t)nq * 32));
   {
     ProfScope ps("ivf_tc_pairs", st);
+    const int64_t qchunks = nq * (kpad / 8);
+    uvb::tc_prepare_queries_kernel<<<(unsigned)((qchunks + 255) / 256), 256, 0, st>>>(
+        q_r, q_stride, degen, nq, nq, d, kpad, a16, axq, axq + nq * 16);
     const int64_t chunks = b.npairs * (kpad / 8);
-    uvb::ivf_pair_rows16_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((chunks + 255) / 256, 148 * 32)),
-                                  256, 0, st>>>(q_r, q_stride, degen, b.pair_query, b.npairs, d,
-                                                kpad, pa16);
+    uvb::ivf_pair_rows16_kernel<<<(unsigned)std::max<int64_t>(
+                                      1, std::min<int64_t>((chunks + 255) / 256, 148 * 32)),
+                                  256, 0, st>>>(a16, b.pair_query, b.npairs, kpad, pa16);
     uvb::ivf_neg_slice_kernel<<<(uvb::kIvfTcRows * 16 + 255) / 256, 256, 0, st>>>(ax);
     if (b.npairs > 0)
       uvb::ivf_pair_of_kernel<<<blocks(b.npairs, 256), 256, 0, st>>>(b.pair_slot, b.npairs,

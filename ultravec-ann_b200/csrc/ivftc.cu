@@ -610,29 +610,18 @@ __global__ void __launch_bounds__(32 * kIvfSelWarps) ivf_select_kernel(const Ivf
   }
 }
 
-// The fp16 query operand row of every pair, in bucketed pair order (zero
-// past dim and for degenerate queries): one thread per 8 coordinates.
-__global__ void ivf_pair_rows16_kernel(const float *q_r, int q_stride, const uint32_t *degen,
-                                       const int32_t *pair_query, int64_t npairs, int dim,
-                                       int kpad, uint16_t *pa16) {
+// The fp16 query operand row of every pair, in bucketed pair order: a copy
+// of the query's row of a16 (tc_prepare_queries_kernel), 16 bytes per
+// thread.
+__global__ void ivf_pair_rows16_kernel(const uint16_t *a16, const int32_t *pair_query,
+                                       int64_t npairs, int kpad, uint16_t *pa16) {
   const int cpr = kpad / 8;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < npairs * cpr;
        e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t pp = e / cpr;
     const int c = (int)(e - pp * cpr);
     const int64_t q = pair_query[pp];
-    uint32_t o[4] = {0u, 0u, 0u, 0u};
-    if (!degen[q] && 8 * c < dim) {
-      const float *src = q_r + q * (int64_t)q_stride + 8 * c;
-#pragma unroll
-      for (int h = 0; h < 4; h++) {
-        const float x0 = 8 * c + 2 * h < dim ? __ldg(src + 2 * h) : 0.0f;
-        const float x1 = 8 * c + 2 * h + 1 < dim ? __ldg(src + 2 * h + 1) : 0.0f;
-        const __half2 hv = __floats2half2_rn(x0, x1);
-        o[h] = *(const uint32_t *)&hv;
-      }
-    }
-    *(uint4 *)(pa16 + pp * kpad + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+    ((uint4 *)(pa16 + pp * kpad))[c] = __ldg((const uint4 *)(a16 + q * kpad) + c);
   }
 }
 

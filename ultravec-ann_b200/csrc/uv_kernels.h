@@ -487,9 +487,8 @@ size_t tc_ivf_smem_bytes();
 int tc_ivf_threads();
 const void *ivf_select_kernel_ptr(int bits);
 size_t ivf_select_smem_bytes(int table_len, int code_stride);
-__global__ void ivf_pair_rows16_kernel(const float *q_r, int q_stride, const uint32_t *degen,
-                                       const int32_t *pair_query, int64_t npairs, int dim,
-                                       int kpad, uint16_t *pa16);
+__global__ void ivf_pair_rows16_kernel(const uint16_t *a16, const int32_t *pair_query,
+                                       int64_t npairs, int kpad, uint16_t *pa16);
 __global__ void ivf_pair_of_kernel(const int32_t *pair_slot, int64_t npairs, int32_t *pair_of);
 __global__ void ivf_neg_slice_kernel(uint16_t *ax);  // kIvfTcRows x 16, one thread per entry
 __global__ void tc_scale_kernel(const uint32_t *gmax_bits, float code_absmax, float *scale);
