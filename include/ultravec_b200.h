@@ -243,6 +243,18 @@ int uv_index_search_begin(const uv_index *index, const float *queries, int64_t n
                           void *stream);
 int uv_search_set_bounds(uv_search *search, const float *gathered, int32_t n_shards);
 int uv_search_finish(uv_search *search, int64_t *ids_out, float *scores_out);
+/* Step 3 without waiting for the device: the same work as uv_search_finish
+ * is queued on the search's stream and the call returns at once, so the
+ * caller can queue the merge's collectives behind it.  Device buffers of the
+ * index's GPU only.  The lists are final only after uv_search_check, which
+ * waits for the stream: when a query's candidates overflowed the prefilter
+ * (rare; *overflowed = 1) it scans that query exactly and rewrites its slots
+ * in ids_out / scores_out, and a caller that already exchanged the lists
+ * must merge them again.  A pipeline wait that timed out returns
+ * UV_ETIMEDOUT there.  Searches that take the exact path finish at once
+ * (uv_search_check then only waits). */
+int uv_search_finish_deferred(uv_search *search, int64_t *ids_out, float *scores_out);
+int uv_search_check(uv_search *search, int32_t *overflowed);
 int uv_search_destroy(uv_search *search);
 
 /* n (id, score) pairs as 12-byte records -- int32 id low, int32 id high,

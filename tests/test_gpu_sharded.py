@@ -31,17 +31,21 @@ def _shards(uv, rows, n_shards, dim=128, bits=2, mem=8, centroids=None):
     return codec, out
 
 
-def _protocol(uv, shards, qs, k, mips, share=True):
+def _protocol(uv, shards, qs, k, mips, share=True, deferred=False):
     import torch
 
     n = len(shards)
+    if deferred:  # device queries: the deferred finish takes device buffers
+        qs = torch.from_numpy(np.ascontiguousarray(qs)).cuda()
     # without sharing, each shard searches as a base of its own (n_shards 1)
     ss = [ix.search_begin(qs, k, mips=mips, n_shards=n if share else 1) for ix in shards]
     if share:
         gathered = torch.cat([torch.as_tensor(s.bounds).cuda() for s in ss], 0)
         for s in ss:
             s.set_bounds(gathered, n)
-    res = [s.finish() for s in ss]
+    res = [s.finish(deferred=deferred) for s in ss]
+    if deferred:
+        assert not any(s.check() for s in ss)  # no overflow on these inputs
     for s in ss:
         s.close()
     packed = [uv.topk_pack(torch.as_tensor(i).cuda(), torch.as_tensor(sc).cuda())
@@ -80,6 +84,10 @@ def test_sharded_search_equals_one_index(uv, oracle, n_shards, k, mips):
     # without the shared threshold every shard keeps its own top k: same answer
     ids2, scores2 = _protocol(uv, shards, qs, k, mips, share=False)
     np.testing.assert_array_equal(ids2, wids)
+    # the deferred finish (work queued, outcome checked after the merge)
+    ids3, scores3 = _protocol(uv, shards, qs, k, mips, deferred=True)
+    np.testing.assert_array_equal(ids3, wids)
+    np.testing.assert_array_equal(_bits(scores3), _bits(wsc))
 
 
 def test_shared_threshold_prunes_candidates(uv):

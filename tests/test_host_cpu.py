@@ -169,10 +169,23 @@ def _gloo_protocol_worker(rank, world, port, result_dir):
             g = gathered.numpy().reshape(n, len(qs), k).transpose(1, 0, 2).reshape(len(qs), -1)
             self.theta = -np.sort(-g, axis=1)[:, k - 1]
 
-        def finish(self):
+        def finish(self, deferred=False):
             keep = self.sc >= self.theta[:, None]
-            return (torch.from_numpy(np.where(keep, self.ids, -1)),
-                    torch.from_numpy(np.where(keep, self.sc, -np.inf).astype(np.float32)))
+            self.want = (np.where(keep, self.ids, -1),
+                         np.where(keep, self.sc, -np.inf).astype(np.float32))
+            self.out = (torch.from_numpy(self.want[0].copy()),
+                        torch.from_numpy(self.want[1].copy()))
+            if rank == 0:
+                # rank 0's first query "overflowed": its deferred lists are
+                # wrong until check() rewrites them, as the library does
+                self.out[0][0] = -1
+                self.out[1][0] = -np.inf
+            return self.out
+
+        def check(self):
+            self.out[0][:] = torch.from_numpy(self.want[0])
+            self.out[1][:] = torch.from_numpy(self.want[1])
+            return rank == 0
 
         def close(self):
             pass
@@ -192,7 +205,9 @@ def _gloo_protocol_worker(rank, world, port, result_dir):
 def test_sharded_search_protocol_with_gloo_ranks(tmp_path, world):
     """The flat multi-GPU protocol on CPU ranks: bounds all-gathered, shared
     threshold, lists packed, all-to-all of query slices (uneven at world 3),
-    per-slice merge, all-gather -- every rank ends with the unsharded top-k."""
+    per-slice merge, all-gather -- every rank ends with the unsharded top-k;
+    one rank's deferred lists are rewritten by its outcome check (an
+    overflowed query), and every rank merges again."""
     import socket
 
     import torch.multiprocessing as mp

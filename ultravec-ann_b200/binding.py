@@ -41,6 +41,7 @@ SYMBOLS = [
     "uv_coset_add", "uv_coset_search", "uv_coset_len", "uv_coset_shape", "uv_coset_books",
     "uv_coset_mem_bytes", "uv_coset_model_bytes", "uv_coset_export", "uv_coset_reconstruct",
     "uv_index_search_begin", "uv_search_set_bounds", "uv_search_finish", "uv_search_destroy",
+    "uv_search_finish_deferred", "uv_search_check",
     "uv_topk_pack", "uv_topk_merge_packed", "uv_search_bounds_per_query", "uv_topk_unpack",
 ]
 
@@ -149,6 +150,8 @@ def lib():
             "uv_index_search_begin": (C.c_int, [vp, vp, i64, i32, i32, i32, vp, vpp, vp]),
             "uv_search_set_bounds": (C.c_int, [vp, vp, i32]),
             "uv_search_finish": (C.c_int, [vp, vp, vp]),
+            "uv_search_finish_deferred": (C.c_int, [vp, vp, vp]),
+            "uv_search_check": (C.c_int, [vp, C.POINTER(C.c_int32)]),
             "uv_search_destroy": (C.c_int, [vp]),
             "uv_search_bounds_per_query": (C.c_int, [i32, i32, C.POINTER(i32)]),
             "uv_topk_pack": (C.c_int, [i32, vp, vp, i64, vp, vp]),
@@ -787,11 +790,24 @@ class ShardSearch:
         gathered = _f32(gathered)
         check(lib().uv_search_set_bounds(self.h, _ptr(gathered), n_shards))
 
-    def finish(self):
+    def finish(self, deferred: bool = False):
+        """This shard's (ids, scores).  deferred (device queries only): the
+        work is queued and the call returns at once; the lists are final
+        after check()."""
         ids = self._alloc((self.nq, self.k), np.int64)
         scores = self._alloc((self.nq, self.k), np.float32)
-        check(lib().uv_search_finish(self.h, _ptr(ids), _ptr(scores)))
+        fn = (lib().uv_search_finish_deferred if deferred and _is_torch(ids) and ids.is_cuda
+              else lib().uv_search_finish)
+        check(fn(self.h, _ptr(ids), _ptr(scores)))
         return ids, scores
+
+    def check(self) -> bool:
+        """Waits for the search; True when some query overflowed the
+        prefilter and was rescanned exactly (its slots rewritten in the lists
+        finish returned, which must then be merged again)."""
+        over = C.c_int32()
+        check(lib().uv_search_check(self.h, C.byref(over)))
+        return bool(over.value)
 
     def close(self):
         if getattr(self, "h", None):

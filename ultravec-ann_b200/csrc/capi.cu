@@ -1490,9 +1490,15 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
   return UV_OK;
 }
 
+int tc_check(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+             int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+             Scratch &sc, TcState &ts, bool *overflowed);
+
+// Pass 2 and the exact rescoring; then (unless defer) tc_check.  With defer
+// the results are final only after tc_check has run on the same stream.
 int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
               int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
-              Scratch &sc, TcState &ts) {
+              Scratch &sc, TcState &ts, bool defer = false) {
   const uv_codec *c = ix->codec;
   const int d = c->cfg.dim;
   const int dim_pad = (d + 3) & ~3;
@@ -1572,6 +1578,22 @@ int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint3
     UV_CK(cudaLaunchKernel(rk, dim3((unsigned)nq), dim3(256), args,
                            rsmem, st));
   }
+  if (defer) return UV_OK;
+  bool over = false;
+  return tc_check(ix, q_r, qc, degen, nq, k, mode, d_ids, d_scores, st, sc, ts, &over);
+}
+
+// The prefilter's outcome (waits for the stream): a pipeline wait that
+// timed out is an error; queries whose candidate list overflowed are
+// scanned exactly and their results replaced in d_ids / d_scores
+// (*overflowed = true).
+int tc_check(const uv_index *ix, const float *q_r, const float *qc, const uint32_t *degen,
+             int64_t nq, int k, int mode, int64_t *d_ids, float *d_scores, cudaStream_t st,
+             Scratch &sc, TcState &ts, bool *overflowed) {
+  const int dim_pad = (ix->codec->cfg.dim + 3) & ~3;
+  int *flags = ts.flags;
+  int32_t *over_list = ts.over_list;
+  *overflowed = false;
   int h_flags[4] = {0, 0, 0, 0};
   UV_CK(cudaMemcpyAsync(h_flags, flags, sizeof(h_flags), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
@@ -1583,6 +1605,7 @@ int tc_finish(const uv_index *ix, const float *q_r, const float *qc, const uint3
   if (h_flags[0]) return fail(UV_ETIMEDOUT, "tensor-core scan: a pipeline wait timed out");
   if (h_flags[1] > 0) {
     // queries whose candidate list overflowed: exact scan of those rows
+    *overflowed = true;
     const int64_t m = h_flags[1];
     std::vector<int32_t> rows((size_t)m);
     UV_CK(cudaMemcpyAsync(rows.data(), over_list, sizeof(int32_t) * m, cudaMemcpyDeviceToHost, st));
@@ -1739,6 +1762,9 @@ struct uv_search {
   bool needs_bounds = false;  // several shards: the threshold comes from set_bounds
   bool bounds_set = false;
   bool finished = false;
+  bool deferred = false;      // finished without its outcome check (uv_search_check)
+  int64_t *out_ids = nullptr;  // the deferred search's outputs (device)
+  float *out_scores = nullptr;
   const float *d_q = nullptr;
   float *q_r = nullptr, *qc = nullptr;
   uint32_t *degen = nullptr;
@@ -1916,6 +1942,49 @@ int uv_search_finish(uv_search *s, int64_t *ids_out, float *scores_out) {
       break;
   }
   return outs.finish(st);
+}
+
+int uv_search_finish_deferred(uv_search *s, int64_t *ids_out, float *scores_out) {
+  if (s == nullptr || (s->nq > 0 && ids_out == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (s->path != uv_search::kPrefilter || s->nq == 0)
+    return uv_search_finish(s, ids_out, scores_out);  // nothing to defer
+  if (s->finished) return fail(UV_EINVAL, "the search has finished");
+  if (s->needs_bounds && !s->bounds_set)
+    return fail(UV_EINVAL, "a search of several shards needs uv_search_set_bounds before finish");
+  const uv_index *ix = s->ix;
+  const int dev = ix->codec->cfg.device;
+  DeviceGuard g(dev);
+  bool ids_dev = false, sc_dev = false;
+  UV_TRY(classify(ids_out, dev, &ids_dev));
+  if (scores_out != nullptr) UV_TRY(classify(scores_out, dev, &sc_dev));
+  if (!ids_dev || (scores_out != nullptr && !sc_dev))
+    return fail(UV_EINVAL, "uv_search_finish_deferred takes device buffers of the index's GPU");
+  float *d_scores = scores_out;
+  if (d_scores == nullptr) UV_TRY(s->sc.alloc(&d_scores, (size_t)s->nq * s->k));
+  s->finished = true;
+  UV_TRY(tc_finish(ix, s->q_r, s->qc, s->degen, s->nq, s->k, s->mode, ids_out, d_scores, s->st,
+                   s->sc, s->ts, true));
+  s->deferred = true;
+  s->out_ids = ids_out;
+  s->out_scores = d_scores;
+  return UV_OK;
+}
+
+int uv_search_check(uv_search *s, int32_t *overflowed) {
+  if (s == nullptr || overflowed == nullptr) return fail(UV_EINVAL, "null argument");
+  *overflowed = 0;
+  if (!s->finished) return fail(UV_EINVAL, "the search has not finished");
+  DeviceGuard g(s->dev);
+  if (!s->deferred) {
+    UV_CK(cudaStreamSynchronize(s->st));
+    return UV_OK;
+  }
+  s->deferred = false;
+  bool over = false;
+  UV_TRY(tc_check(s->ix, s->q_r, s->qc, s->degen, s->nq, s->k, s->mode, s->out_ids,
+                  s->out_scores, s->st, s->sc, s->ts, &over));
+  *overflowed = over ? 1 : 0;
+  return UV_OK;
 }
 
 int uv_search_destroy(uv_search *s) {

@@ -90,8 +90,11 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
        best first-pass lower bounds; one all-gather makes them (world * nq,
        m), shard-major, on every rank, and every shard takes the k-th largest
        of their union as its threshold (`set_bounds`).
-    2. `finish()` gives the shard's lists: only records that can be in the
-       global top k survive the shared threshold.
+    2. `finish(deferred=True)` queues the shard's pass 2 and rescoring
+       without waiting: only records that can be in the global top k survive
+       the shared threshold.  After the combine, `check()` on every rank and
+       one all-reduce tell whether any shard rescanned an overflowed query
+       exactly; then the (rewritten) lists are combined again.
     3. The lists travel once, packed (ids and scores in one 12-byte record,
        `pack`): an all-to-all hands rank r every shard's lists for its query
        slice, rank r merges its slice over the shards (`merge_packed` with
@@ -105,7 +108,6 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
     import torch
 
     world = dist.get_world_size()
-    rank = dist.get_rank()
     s = begin(world)
     try:
         bounds = s.bounds
@@ -113,10 +115,18 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
         gathered = torch.empty((world * nq, m), dtype=bounds.dtype, device=bounds.device)
         dist.all_gather_into_tensor(gathered, bounds.contiguous())
         s.set_bounds(gathered, world)
-        ids, scores = s.finish()
+        # queued without waiting for the device; the combine's collectives
+        # follow at once, and the outcome check comes after them
+        ids, scores = s.finish(deferred=True)
+        out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
+        over = torch.tensor([1 if s.check() else 0], dtype=torch.int32, device=bounds.device)
+        dist.all_reduce(over, op=dist.ReduceOp.MAX)
+        if int(over.item()):
+            # a shard rescanned overflowed queries exactly: merge again
+            out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
     finally:
         s.close()
-    return combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
+    return out
 
 
 def combine_topk(ids, scores, k: int, dist, pack, unpack, merge_packed):
