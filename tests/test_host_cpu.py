@@ -191,7 +191,7 @@ def _gloo_protocol_worker(rank, world, port, result_dir):
             pass
 
     g_ids, g_sc = sharded_search(lambda n: StandIn(), k, dist, pack_host, unpack_host,
-                                 merge_packed_host)
+                                 merge_packed_host, deferred=True)
     full = codec.encode_batch(rows)
     want_ids, want_sc = codec.search_topk(full, qs, k, norms=O.l2_norms(rows))
     ok = np.array_equal(g_ids.numpy(), want_ids) and np.array_equal(

@@ -81,7 +81,7 @@ def query_slice(nq: int, rank: int, world: int) -> tuple[int, int]:
     return rank * nq // world, (rank + 1) * nq // world
 
 
-def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
+def sharded_search(begin, k: int, dist, pack, unpack, merge_packed, deferred: bool = False):
     """The flat search of a base split across ranks (one index shard each,
     global ids), as uv_index_search_begin / set_bounds / finish plus the
     merge describe it:
@@ -90,11 +90,12 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
        best first-pass lower bounds; one all-gather makes them (world * nq,
        m), shard-major, on every rank, and every shard takes the k-th largest
        of their union as its threshold (`set_bounds`).
-    2. `finish(deferred=True)` queues the shard's pass 2 and rescoring
-       without waiting: only records that can be in the global top k survive
-       the shared threshold.  After the combine, `check()` on every rank and
-       one all-reduce tell whether any shard rescanned an overflowed query
-       exactly; then the (rewritten) lists are combined again.
+    2. `finish()` gives the shard's lists: only records that can be in the
+       global top k survive the shared threshold.  With `deferred`, finish
+       queues that work without waiting for the device, and after the
+       combine `check()` on every rank and one all-reduce tell whether any
+       shard rescanned an overflowed query exactly, in which case the
+       (rewritten) lists are combined again.
     3. The lists travel once, packed (ids and scores in one 12-byte record,
        `pack`): an all-to-all hands rank r every shard's lists for its query
        slice, rank r merges its slice over the shards (`merge_packed` with
@@ -115,14 +116,19 @@ def sharded_search(begin, k: int, dist, pack, unpack, merge_packed):
         gathered = torch.empty((world * nq, m), dtype=bounds.dtype, device=bounds.device)
         dist.all_gather_into_tensor(gathered, bounds.contiguous())
         s.set_bounds(gathered, world)
-        # queued without waiting for the device; the combine's collectives
-        # follow at once, and the outcome check comes after them
-        ids, scores = s.finish(deferred=True)
-        out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
-        over = torch.tensor([1 if s.check() else 0], dtype=torch.int32, device=bounds.device)
-        dist.all_reduce(over, op=dist.ReduceOp.MAX)
-        if int(over.item()):
-            # a shard rescanned overflowed queries exactly: merge again
+        if deferred:
+            # queued without waiting for the device; the combine's
+            # collectives follow at once, the outcome check after them
+            ids, scores = s.finish(deferred=True)
+            out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
+            over = torch.tensor([1 if s.check() else 0], dtype=torch.int32,
+                                device=bounds.device)
+            dist.all_reduce(over, op=dist.ReduceOp.MAX)
+            if int(over.item()):
+                # a shard rescanned overflowed queries exactly: merge again
+                out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
+        else:
+            ids, scores = s.finish()
             out = combine_topk(ids, scores, k, dist, pack, unpack, merge_packed)
     finally:
         s.close()
