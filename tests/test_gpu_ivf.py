@@ -206,7 +206,7 @@ def test_device_tensors_in_and_out(oracle, uv):
     assert gi.is_cuda and np.array_equal(gi.cpu().numpy(), hi) and bits_equal(gs.cpu().numpy(), hs)
 
 
-@pytest.mark.parametrize("dim,nlist", [(128, 300), (256, 777), (2048, 512)])
+@pytest.mark.parametrize("dim,nlist", [(128, 300), (256, 777), (2048, 512), (128, 1500)])
 def test_tensor_core_probe_matches_oracle(oracle, uv, dim, nlist):
     """The probe from tensor-core dots plus exact rechecks (nlist >= 256)
     returns the oracle's lists: duplicated centroids (exact ties, lower list
