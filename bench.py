@@ -30,6 +30,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -110,7 +111,8 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = REPO / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+        # the samples go to a private temporary file; the line reports them
+        self.path = Path(tempfile.gettempdir()) / f"uvb200_clocks_gpu{gpu_index}_{os.getpid()}.csv"
 
     def start(self):
         try:
