@@ -153,7 +153,7 @@ void free_lists(uv_ivf *ix) {
 int tc_rank_rows(const float *a, const float *a_norm, int64_t m_total, int d, const uint16_t *c16,
                  const uint16_t *cext, int64_t ldc, const float *cent, const float *cnorm,
                  int nlist, int np, float bound, int32_t *out, int ld_out, int dev,
-                 cudaStream_t st, Scratch &sc) {
+                 cudaStream_t st, Scratch &sc, int *err_defer = nullptr) {
   const int kpad = (d + 63) / 64 * 64;
   const int TN = 192, TM = 128;
   const int64_t n_tiles = ldc / TN;
@@ -169,8 +169,12 @@ int tc_rank_rows(const float *a, const float *a_norm, int64_t m_total, int d, co
   UV_TRY(sc.alloc(&aflag, (size_t)chunk));
   UV_TRY(sc.alloc(&a16, (size_t)chunk * kpad));
   UV_TRY(sc.alloc(&ax, (size_t)chunk * 16 * 2));
-  UV_TRY(sc.alloc(&err, 1));
-  UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  if (err_defer != nullptr) {
+    err = err_defer;  // the caller zeroed it and reads it later
+  } else {
+    UV_TRY(sc.alloc(&err, 1));
+    UV_CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  }
   if (a_norm == nullptr) UV_CK(cudaMemsetAsync(aflag, 0, sizeof(uint32_t) * chunk, st));
   CUtensorMap tmap_b, tmap_bx;
   UV_TRY(fp16_tensor_map(&tmap_b, c16, ldc, kpad, 64, TN, true));
@@ -256,6 +260,7 @@ int tc_rank_rows(const float *a, const float *a_norm, int64_t m_total, int d, co
                              st));
     }
   }
+  if (err_defer != nullptr) return UV_OK;
   int h_err = 0;
   UV_CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
@@ -327,7 +332,7 @@ int tc_argmax(const float *units, int64_t n, int dim, const float *cent, int nli
 // divisions of both sides, fp16 subnormals, and the reference's sequential
 // f32 dot); the kernel uses 1.25 times that.
 int tc_probe(const uv_ivf *ix, const float *d_q, const float *qn, int64_t nq, int np, int ld,
-             int32_t *lists, cudaStream_t st, Scratch &sc, bool *used) {
+             int32_t *lists, cudaStream_t st, Scratch &sc, bool *used, int *err_defer = nullptr) {
   *used = false;
   const int d = ix->codec->cfg.dim;
   const int nlist = ix->nlist;
@@ -374,13 +379,15 @@ int tc_probe(const uv_ivf *ix, const float *d_q, const float *qn, int64_t nq, in
   const float bound = (float)(1.25 * (std::ldexp(1.0, -10) + std::ldexp(1.0, -12) +
                                       4.0 * d * std::ldexp(1.0, -24)));
   return tc_rank_rows(d_q, qn, nq, d, ix->c16, ix->cext, ix->c_pad, ix->centroids, ix->cnorm,
-                      nlist, np, bound, lists, ld, ix->device, st, sc);
+                      nlist, np, bound, lists, ld, ix->device, st, sc, err_defer);
 }
 
 // Probe on device: lists (nq x ld, first np columns) of the best np lists by
 // exact cosine of the raw queries.
+// err_defer (device, zeroed): the tensor-core probe's timeout flag is left
+// there for the caller to read with its next host read, instead of a wait.
 int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld, int32_t *lists,
-                 cudaStream_t st, Scratch &sc) {
+                 cudaStream_t st, Scratch &sc, int *err_defer = nullptr) {
   const int d = ix->codec->cfg.dim;
   if (np == 0 || nq == 0) return UV_OK;
   int pow2 = 32;
@@ -391,7 +398,7 @@ int probe_device(const uv_ivf *ix, const float *d_q, int64_t nq, int np, int ld,
   uvb::row_norms_kernel<<<blocks(nq, 128), 128, 0, st>>>(d_q, nq, d, qn);
   UV_CK(cudaGetLastError());
   bool used = false;
-  UV_TRY(tc_probe(ix, d_q, qn, nq, np, ld, lists, st, sc, &used));
+  UV_TRY(tc_probe(ix, d_q, qn, nq, np, ld, lists, st, sc, &used, err_defer));
   if (used) return UV_OK;
   const int64_t chunk =
       std::max<int64_t>(1, std::min<int64_t>(nq, ((int64_t)256 << 20) / (4 * (int64_t)ix->nlist)));
@@ -691,11 +698,17 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   if (npairs > INT32_MAX) return fail(UV_EINVAL, "nq * nprobe exceeds 2^31 - 1");
   int32_t *lists = nullptr;
   UV_TRY(sc.alloc(&lists, (size_t)npairs));
+  // [0] a list id outside 0..nlist-1, [1] the tensor-core probe timed out:
+  // read with the bucket totals below
+  int *bad = nullptr;
+  UV_TRY(sc.alloc(&bad, 2));
+  UV_CK(cudaMemsetAsync(bad, 0, sizeof(int) * 2, st));
   if (given_lists != nullptr) {
     UV_CK(cudaMemcpyAsync(lists, given_lists, sizeof(int32_t) * (size_t)npairs,
                           cudaMemcpyDeviceToDevice, st));
   } else {
-    UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc));
+    // the shortlist path below reads no totals: its probe waits for its own flag
+    UV_TRY(probe_device(ix, d_q, nq, np, np, lists, st, sc, ix->sl_c > 0 ? nullptr : bad + 1));
   }
   // bucket the (query, list) pairs by list; a scan item is one record range
   // (at most range_size records: long lists are split for load balance) of
@@ -720,9 +733,6 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   }
   // probes of lists without records here (a list owned by another shard,
   // or empty) make no pair
-  int *bad = nullptr;
-  UV_TRY(sc.alloc(&bad, 1));
-  UV_CK(cudaMemsetAsync(bad, 0, sizeof(int), st));
   uvb::drop_empty_lists_kernel<<<blocks(npairs, 256), 256, 0, st>>>(lists, npairs, ix->d_off,
                                                                     nlist, bad);
   UV_CK(cudaGetLastError());
@@ -756,12 +766,13 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
     UV_CK(cudaGetLastError());
   }
   int64_t h_tot[3] = {0, 0, 0};
-  int h_bad = 0;
+  int h_bad[2] = {0, 0};
   UV_CK(cudaMemcpyAsync(h_tot, totals, sizeof(h_tot), cudaMemcpyDeviceToHost, st));
-  UV_CK(cudaMemcpyAsync(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
+  UV_CK(cudaMemcpyAsync(h_bad, bad, sizeof(h_bad), cudaMemcpyDeviceToHost, st));
   UV_CK(cudaStreamSynchronize(st));
   const int64_t n_items = h_tot[0], n_rslots = h_tot[1];
-  if (h_bad) return fail(UV_EINVAL, "a probe list id is outside 0..nlist-1");
+  if (h_bad[1]) return fail(UV_ETIMEDOUT, "a tensor-core probe wait timed out");
+  if (h_bad[0]) return fail(UV_EINVAL, "a probe list id is outside 0..nlist-1");
   // the bucketed pairs: probes of lists with records here
   const int64_t npv = h_tot[2];
   if (n_items > INT32_MAX) return fail(UV_EINVAL, "too many scan items");
@@ -775,8 +786,9 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
   UV_TRY(sc.alloc(&d_n_items, 1));
   UV_TRY(sc.alloc(&row_off, (size_t)npairs + 1));
   {
-    const int32_t ni = (int32_t)n_items;
-    UV_CK(cudaMemcpyAsync(d_n_items, &ni, sizeof(ni), cudaMemcpyHostToDevice, st));
+    // the item count as the kernels read it: the low half of the device
+    // total (n_items < 2^31, little-endian), no host copy to wait for
+    UV_CK(cudaMemcpyAsync(d_n_items, totals, sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
     ProfScope ps("ivf_bucket", st);
     uvb::item_fill_kernel<<<blocks(nlist, 256), 256, 0, st>>>(
         cnt, pair_off, item_off, ix->d_off, nlist, range_size, per_item, item_list, item_pair,
@@ -784,7 +796,6 @@ int search_device(const uv_ivf *ix, const float *d_q, int64_t nq, int k, int np,
     uvb::pair_rows_kernel<<<blocks(npv + 1, 256), 256, 0, st>>>(
         pair_list, pair_off, list_rbase, ix->d_off, range_size, (int)npv, row_off);
     UV_CK(cudaGetLastError());
-    UV_CK(cudaStreamSynchronize(st));  // `ni` is a host value of this frame
   }
   float *pair_qm = nullptr;
   if (ix->centered) {
