@@ -202,8 +202,8 @@ METRIC = "flat codes-only MIPS queries/s and encode vectors/s at 1/2/4/8 B200; %
 
 
 # kernel families of one step (uv_profile_read names)
-SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
-                 "tc_theta", "tc_bounds", "tc_pass2", "tc_rescore", "topk_pack")
+SCAN_FAMILIES = ("encode", "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_hot",
+                 "tc_pass1", "tc_theta", "tc_bounds", "tc_pass2", "tc_rescore", "topk_pack")
 
 
 def config_dict(args):

@@ -325,7 +325,8 @@ int uv_set_tuning(const char *key, int64_t value);
  * kernel the library launches is bracketed by CUDA events on its launch
  * stream.  uv_profile_read waits for those events and returns the summed
  * device time and launch count of one kernel family ("encode",
- * "prep_queries", "flat_scan", "merge_topk", "tc_prepare", "tc_pass1",
+ * "prep_queries", "flat_scan", "merge_topk", "tc_prepare" (the prefilter's
+ * operand rows), "tc_hot" (its first pass's sample), "tc_pass1",
  * "tc_theta", "tc_pass2", "tc_rescore", "score_candidates", "shortlist", the IVF families
  * "ivf_*", or "*" for
  * all).  "tc_candidates" returns, as the count, the number of candidates the

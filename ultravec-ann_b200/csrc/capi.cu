@@ -1341,7 +1341,7 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
       UV_TRY(sc.alloc(&keys, (size_t)n));
       UV_TRY(sc.alloc(&offs, (size_t)cblocks + 1));
       sel = hist + 4096;
-      ProfScope ps("tc_prepare", st);
+      ProfScope ps("tc_hot", st);
       const unsigned hg = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 1184));
       UV_CK(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (4096 + 8), st));
       uvb::tc_hot_keys_kernel<<<hg, 256, 0, st>>>(hp, keys, hist);
