@@ -50,6 +50,32 @@ def test_bad_configs_are_rejected_before_any_device_work(uv):
         assert uv.lib().uv_last_error()
 
 
+def test_null_handles_are_refused_without_device_work(uv):
+    """Every entry point whose first argument is a handle returns UV_EINVAL
+    with a message for a null handle (other pointers null, sizes 0), before
+    any device work; the destroy calls accept null like free(NULL).  Nothing
+    crashes or aborts across the ABI."""
+    import ctypes as C
+
+    lib = uv.lib()
+    ints = (C.c_int32, C.c_int64, C.c_uint64, C.c_float, C.c_int)
+    checked = 0
+    for name in uv.SYMBOLS:
+        fn = getattr(lib, name)
+        ats = fn.argtypes or []
+        if not ats or ats[0] is not C.c_void_p:
+            continue
+        args = [0 if t in ints else None for t in ats]
+        rc = fn(*args)
+        if name.endswith("_destroy"):
+            assert rc == 0, name
+        else:
+            assert rc == 1, (name, rc)
+            assert lib.uv_last_error(), name
+        checked += 1
+    assert checked >= 60
+
+
 def test_shard_ranges_partition_the_rows(uv):
     from ultravec_ann_b200.shard import shard_range
 
@@ -201,7 +227,7 @@ def _gloo_protocol_worker(rank, world, port, result_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_sharded_search_protocol_with_gloo_ranks(tmp_path, world):
     """The flat multi-GPU protocol on CPU ranks: bounds all-gathered, shared
     threshold, lists packed, all-to-all of query slices (uneven at world 3),
@@ -312,13 +338,15 @@ def _gloo_ivf_worker(rank, world, port, result_dir):
     dist.destroy_process_group()
 
 
-def test_sharded_ivf_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
-    """world_size 2 on CPU: posting lists dealt by bytes, every rank probes
-    all centroids and scans its own lists (the oracle stands in for the
-    device search), all-gather, merge == the IVF top-k of the whole index,
-    centered and not; and the same with the probe split by query slices
-    (ivf_sharded_search: probe slice, all-gather of the lists, packed
-    all-to-all and slice merges) on every rank."""
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_ivf_search_equals_unsharded_with_gloo_ranks(tmp_path, world):
+    """world_size 2 and 4 on CPU: posting lists dealt by bytes, every rank
+    probes all centroids and scans its own lists (the oracle stands in for
+    the device search), all-gather, merge == the IVF top-k of the whole
+    index, centered and not; and the same with the probe split by query
+    slices (ivf_sharded_search: probe slice, all-gather of the lists, packed
+    all-to-all and slice merges; 15 queries make uneven slices at world 4)
+    on every rank."""
     import socket
 
     import torch.multiprocessing as mp
@@ -327,8 +355,8 @@ def test_sharded_ivf_search_equals_unsharded_with_two_gloo_ranks(tmp_path):
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    mp.start_processes(_gloo_ivf_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_gloo_ivf_worker, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
     assert (tmp_path / "ok").read_text() == "1"
 
 
