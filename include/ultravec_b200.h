@@ -307,7 +307,9 @@ int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t
  * sample (0 automatic: the n/S records of largest score scale g, copied
  * into their own rows when the index changes; 1: every S-th record tile;
  * N >= 2: the n/N records of largest g); "tc_prepare" 1 makes the
- * prefilter's rows with the generic kernel (0 automatic);
+ * prefilter's rows with the generic kernel, 2 with the shared-memory-table
+ * kernel summing |x|^2 in f64 (0 automatic: that kernel for widths 1, 2, 4
+ * summing in f32 under a rigorous inflation);
  * "coset_nearest" selects how the coset trellis finds each block's nearest
  * kept point (0 automatic: every book point scored for books of <= 8192
  * points, the reference's bisection + ball search where the minimum is tied

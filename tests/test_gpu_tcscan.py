@@ -246,15 +246,19 @@ def test_sampled_threshold_matches_exact_kernel(uv, tc_mode, sample, k):
 
 @pytest.mark.parametrize("bits,mem", [(1, 8), (2, 8), (4, 6), (2, 12)])
 def test_row_kernels_agree(uv, bits, mem):
-    """The shared-memory-table row kernel and the generic one make the same
-    operand rows: same candidates, same results."""
+    """The row kernels (tuning key tc_prepare: 0 the shared-memory table
+    with |x|^2 summed in f32, 1 the generic kernel, 2 the shared-memory table
+    summing in f64) make the same fp16 rows B'.  The f64 sums give the same
+    bound constants, hence the same candidates; the f32 sum under its
+    rigorous inflation may make a bound constant one fp16 place larger, so
+    as many or a few more candidates pass.  Results are the same bits."""
     n, nq, dim = 150_000, 64, 128
     base = rand_rows(n, dim, 70 + bits)
     queries = rand_rows(nq, dim, 71)
     out = []
     try:
         uv.set_tuning("tc_scan", 2)
-        for mode in (0, 1):
+        for mode in (0, 1, 2):
             uv.set_tuning("tc_prepare", mode)
             index = uv.Index(uv.Codec(dim, bits, mem))
             index.add_batch(base)
@@ -268,7 +272,9 @@ def test_row_kernels_agree(uv, bits, mem):
         uv.set_tuning("tc_prepare", 0)
         uv.set_tuning("tc_scan", 0)
     assert same(out[0][0], out[1][0])
-    assert out[0][1] == out[1][1] > 0
+    assert same(out[2][0], out[1][0])
+    assert out[2][1] == out[1][1] > 0
+    assert out[1][1] <= out[0][1] <= out[1][1] * 1.01 + 8
 
 
 @pytest.mark.parametrize("hot", [0, 1, 3, 8])

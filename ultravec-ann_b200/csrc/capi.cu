@@ -1150,8 +1150,10 @@ int tc_begin(const uv_index *ix, const float *q_r, const uint32_t *degen, int64_
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
                            dim3(256), args, 0, st));
     // widths 1, 2, 4 with a table of at most 64 KB: the shared-memory
-    // table and 16-byte code reads; otherwise the generic kernel
-    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits);
+    // table and 16-byte code reads (|x|^2 summed in f32; tuning key
+    // tc_prepare 2: in f64); otherwise, or with tc_prepare 1, the generic
+    // kernel
+    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits, g_tc_prepare.load() != 2);
     const size_t tsm = (size_t)4 << (c->cfg.mem + c->cfg.bits);
     if (fk != nullptr && tsm <= 64 * 1024 && g_tc_prepare != 1) {
       UV_CK(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
@@ -2224,7 +2226,7 @@ int uv_set_tuning(const char *key, int64_t value) {
     return UV_OK;
   }
   if (std::strcmp(key, "tc_prepare") == 0) {
-    if (value < 0 || value > 1) return fail(UV_EINVAL, "tc_prepare must be 0 or 1");
+    if (value < 0 || value > 2) return fail(UV_EINVAL, "tc_prepare must be 0, 1 or 2");
     g_tc_prepare = (int)value;
     return UV_OK;
   }

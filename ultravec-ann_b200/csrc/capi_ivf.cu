@@ -465,7 +465,7 @@ int list_rows(const uv_ivf *ix, cudaStream_t st, Scratch &sc, const TcRows **out
     UV_CK(cudaLaunchKernel((const void *)uvb::tc_gmax_kernel, dim3((unsigned)((n + 255) / 256)),
                            dim3(256), args, 0, st));
     uvb::tc_scale_kernel<<<1, 32, 0, st>>>(gmax, c->code_absmax, ix->list_scale);
-    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits);
+    const void *fk = uvb::tc_prepare_records_fast_ptr(c->cfg.bits, g_tc_prepare.load() != 2);
     const size_t tsm = (size_t)4 << (c->cfg.mem + c->cfg.bits);
     if (fk != nullptr && tsm <= 64 * 1024 && g_tc_prepare != 1) {
       UV_CK(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));

@@ -477,8 +477,20 @@ __global__ void tc_prepare_records_kernel(const TcPrepareParams p) {
 // The same rows for widths 1, 2 and 4 with the code table in shared memory:
 // each record's code is read 16 bytes at a time and its windows are cut with
 // shifts known at compile time (code rows are padded to 16 bytes); one
-// thread per record, the same arithmetic as tc_prepare_records_kernel.
-template <int BITS>
+// thread per record.
+//
+// F32SUM (the default): the conversions of tc_prepare_records_kernel run on
+// the SM's conversion (XU) pipe, which bounds this kernel together with the
+// table lookups, so |x|^2 is summed in f32 (one fma per coordinate, no
+// widening to f64) and each pair of B' values is rounded to fp16 by one
+// paired conversion (the same round-to-nearest bits).  Every term is
+// non-negative, so with at most dim roundings of relative size 2^-24 the
+// exact sum is at most the computed one times (1 + (dim + 64) 2^-23); terms
+// below the f32 normal range lose at most 2^-149 each, far inside the
+// bound's absolute term.  C' may then exceed the f64 sum's by a unit of its
+// last fp16 place; both are valid bounds, and B' is the same bits.
+// !F32SUM: the f64 sum and per-value conversions of tc_prepare_records_kernel.
+template <int BITS, bool F32SUM>
 __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPrepareParams p) {
   extern __shared__ float tab[];
   for (int i = threadIdx.x; i < (1 << (p.mem + BITS)); i += blockDim.x) tab[i] = __ldg(p.code + i);
@@ -504,6 +516,7 @@ __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPr
   const uint4 *cw4 = (const uint4 *)(p.codes + r * (int64_t)p.code_stride);
   const float gs = (float)((double)g * s);  // exact: s is a power of two
   double xs = 0.0;
+  float xs32 = 0.0f;
   constexpr int CPC = 128 / BITS;  // coordinates per 16-byte chunk
   uint32_t prev = __ldg(p.start + r);
   const int nchunks = (p.dim + CPC - 1) / CPC;
@@ -516,6 +529,7 @@ __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPr
       const int c0 = k * CPC + g8 * 8;
       if (c0 >= p.dim) break;
       uint32_t o[4];
+      float xv[8];
 #pragma unroll
       for (int h = 0; h < 8; h++) {
         const int e2 = (g8 * 8 + h + 1) * BITS;  // chunk bits consumed through this window
@@ -524,18 +538,32 @@ __global__ void __launch_bounds__(256) tc_prepare_records_fast_kernel(const TcPr
         const uint32_t hiw = wi == 0 ? prev : w[wi > 0 ? wi - 1 : 0];
         const uint64_t v = ((uint64_t)hiw << 32) | w[wi];
         const float x = tab[(uint32_t)(v >> sh) & wmask];
-        xs += (double)x * (double)x;
-        const uint32_t hx = __half_as_ushort(__float2half_rn(fmul(gs, x)));
-        if (h & 1)
-          o[h >> 1] |= hx << 16;
-        else
-          o[h >> 1] = hx;
+        xv[h] = x;
+        if (F32SUM) {
+          xs32 = __fmaf_rn(x, x, xs32);
+        } else {
+          xs += (double)x * (double)x;
+          const uint32_t hx = __half_as_ushort(__float2half_rn(fmul(gs, x)));
+          if (h & 1)
+            o[h >> 1] |= hx << 16;
+          else
+            o[h >> 1] = hx;
+        }
+      }
+      if (F32SUM) {
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          // low half: the even coordinate
+          const __half2 pr = __floats2half2_rn(fmul(gs, xv[2 * h]), fmul(gs, xv[2 * h + 1]));
+          memcpy(&o[h], &pr, sizeof(uint32_t));
+        }
       }
       xrow[c0 / 8] = make_uint4(o[0], o[1], o[2], o[3]);
     }
     prev = w[3];
   }
   for (int c = (p.dim + 7) / 8; c < p.kpad / 8; c++) xrow[c] = make_uint4(0, 0, 0, 0);
+  if (F32SUM) xs = (double)xs32 * (1.0 + (double)(p.dim + 64) * 0x1p-23);
   const double qn = 1.0001;
   const double xn = sqrt(xs) * (1.0 + 1e-12);
   const double sg = s * (double)g;
@@ -767,11 +795,14 @@ __global__ void __launch_bounds__(256)
   if ((threadIdx.x & 15) == 0) cmax[r >> 4] = c;
 }
 
-const void *tc_prepare_records_fast_ptr(int bits) {
+const void *tc_prepare_records_fast_ptr(int bits, bool f32sum) {
   switch (bits) {
-    case 1: return (const void *)tc_prepare_records_fast_kernel<1>;
-    case 2: return (const void *)tc_prepare_records_fast_kernel<2>;
-    case 4: return (const void *)tc_prepare_records_fast_kernel<4>;
+    case 1: return f32sum ? (const void *)tc_prepare_records_fast_kernel<1, true>
+                          : (const void *)tc_prepare_records_fast_kernel<1, false>;
+    case 2: return f32sum ? (const void *)tc_prepare_records_fast_kernel<2, true>
+                          : (const void *)tc_prepare_records_fast_kernel<2, false>;
+    case 4: return f32sum ? (const void *)tc_prepare_records_fast_kernel<4, true>
+                          : (const void *)tc_prepare_records_fast_kernel<4, false>;
   }
   return nullptr;
 }

@@ -317,8 +317,10 @@ int tc_dim();
 __global__ void tc_gmax_kernel(const TcPrepareParams p);
 __global__ void tc_prepare_records_kernel(const TcPrepareParams p);
 // widths 1, 2, 4 with the table in shared memory (4 << (mem + bits) bytes,
-// 256 threads); null for other widths
-const void *tc_prepare_records_fast_ptr(int bits);
+// 256 threads); null for other widths.  f32sum: |x|^2 summed in f32 under a
+// rigorous inflation and paired fp16 conversions; else the f64 sum of
+// tc_prepare_records_kernel
+const void *tc_prepare_records_fast_ptr(int bits, bool f32sum);
 // cmax[c] = largest C' (element 0 of the extra slice) of records 16c ..
 // 16c + 15 below n, 0 for a chunk of padding only; n_pad % 16 == 0, blocks
 // of 256 threads
