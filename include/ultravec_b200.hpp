@@ -10,6 +10,7 @@
  *                                       2036-2247)
  *   IvfCodec, IvfIndex                 (src/ivf.rs:41-60, 98-290)
  *   kmeans, assign                     (src/bench.rs:298-349, src/ivf.rs:405-421)
+ *   CosetTrellis                       (src/coset_trellis.rs:98-530)
  * so that code written against the reference's traits ports line for line.
  *
  * Error behaviour.  Where the reference panics (assert_eq! on a dimension
@@ -33,9 +34,12 @@
 #include "ultravec_b200.h"
 
 #include <algorithm>
+#include <cfloat>
+#include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <memory>
+#include <optional>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -106,6 +110,37 @@ inline bool env_is(const char *name, const char *value) {
   return v != nullptr && std::string(v) == value;
 }
 
+// l2_norm (src/lib.rs:215-217): the f32 sum of squares from -0.0, in
+// order, then the square root.  Each product is rounded by itself (the
+// volatile keeps a compiler from fusing it into the add, which rustc never
+// does), so the result has the reference's bits under any build flags.
+inline float l2_norm(const float *v, size_t n) {
+  float s = -0.0f;
+  for (size_t i = 0; i < n; i++) {
+    volatile float p = v[i] * v[i];
+    s = s + p;
+  }
+  return std::sqrt(s);
+}
+
+// the tail of reconstruct_from (src/trellis.rs:1640-1653): the decoded,
+// inverse-rotated row normalized, then, for a centered record, recomposed
+// as centroid + rnorm * direction and normalized again
+inline std::vector<float> unit_direction(std::vector<float> recon, const float *centroid,
+                                         float rnorm) {
+  const size_t d = recon.size();
+  const float n = std::fmax(l2_norm(recon.data(), d), FLT_EPSILON);
+  for (auto &x : recon) x = x / n;
+  if (centroid == nullptr) return recon;
+  for (size_t i = 0; i < d; i++) {
+    volatile float p = rnorm * recon[i];
+    recon[i] = centroid[i] + p;
+  }
+  const float nf = std::fmax(l2_norm(recon.data(), d), FLT_EPSILON);
+  for (auto &x : recon) x = x / nf;
+  return recon;
+}
+
 struct CodecDel {
   void operator()(uv_codec *c) const { uv_codec_destroy(c); }
 };
@@ -117,6 +152,9 @@ struct IvfDel {
 };
 struct PreparedDel {
   void operator()(uv_prepared *x) const { uv_prepared_destroy(x); }
+};
+struct CosetDel {
+  void operator()(uv_coset *x) const { uv_coset_destroy(x); }
 };
 
 }  // namespace detail
@@ -167,6 +205,11 @@ class VectorBackend {
     return m;
   }
   virtual bool is_approximate() const { return false; }
+  // the unit direction the codec stores for x, or nothing for a backend
+  // that cannot reconstruct
+  virtual std::optional<std::vector<float>> reconstruct_unit(const std::vector<float> &) const {
+    return std::nullopt;
+  }
 };
 
 /* ---- TrellisConfig (src/trellis.rs:352-391) ---------------------------- */
@@ -287,6 +330,7 @@ class TrellisQuantizer : public VectorBackend, public CandidateScorer {
       index_ = std::move(o.index_);
       codec_ = std::move(o.codec_);
       cfg_ = o.cfg_;
+      centroids_ = std::move(o.centroids_);
       sl_c_ = o.sl_c_;
       sl_asym_ = o.sl_asym_;
       sl_rnorm_ = o.sl_rnorm_;
@@ -307,8 +351,9 @@ class TrellisQuantizer : public VectorBackend, public CandidateScorer {
 
   // with_centroids (src/trellis.rs:952-956): centered records, on an empty index
   TrellisQuantizer &with_centroids(const std::vector<std::vector<float>> &centroids) & {
-    const std::vector<float> flat = detail::flatten(centroids, cfg_.dim);
+    std::vector<float> flat = detail::flatten(centroids, cfg_.dim);
     detail::check(uv_index_set_centroids(index_.get(), flat.data(), (int32_t)centroids.size()));
+    centroids_ = std::move(flat);
     return *this;
   }
   TrellisQuantizer with_centroids(const std::vector<std::vector<float>> &centroids) && {
@@ -459,6 +504,22 @@ class TrellisQuantizer : public VectorBackend, public CandidateScorer {
     return m;
   }
   bool is_approximate() const override { return true; }
+  // reconstruct_unit (src/trellis.rs:2241-2246): encode x, decode the
+  // record, normalize (recomposed with its centroid when centered)
+  std::optional<std::vector<float>> reconstruct_unit(const std::vector<float> &x) const override {
+    detail::require(x.size() == cfg_.dim, "row length differs from the codec's dimension");
+    const int32_t n_cen = (int32_t)(centroids_.size() / cfg_.dim);
+    std::vector<uint8_t> codes(code_bytes());
+    uint32_t start = 0, cidx = 0;
+    float rescale = 0.0f, rnorm = 1.0f;
+    detail::check(uv_encode(codec_.get(), x.data(), 1, n_cen ? centroids_.data() : nullptr, n_cen,
+                            codes.data(), &start, &rescale, &rnorm, &cidx, nullptr));
+    std::vector<float> recon(cfg_.dim);
+    detail::check(uv_decode(codec_.get(), codes.data(), &start, 1, recon.data(), nullptr));
+    return detail::unit_direction(std::move(recon),
+                                  n_cen ? centroids_.data() + (size_t)cidx * cfg_.dim : nullptr,
+                                  rnorm);
+  }
 
   // the inner-product harness's ranking for one query (src/bench.rs:1029-1045)
   Hits search_mips(const std::vector<float> &query, size_t limit) const {
@@ -569,6 +630,7 @@ class TrellisQuantizer : public VectorBackend, public CandidateScorer {
   std::unique_ptr<uv_codec, detail::CodecDel> codec_;
   std::unique_ptr<uv_index, detail::IndexDel> index_;
   TrellisConfig cfg_;
+  std::vector<float> centroids_;  // with_centroids, flattened (reconstruct_unit)
   int32_t sl_c_ = 0;
   bool sl_asym_ = false, sl_rnorm_ = true;
 };
@@ -760,6 +822,114 @@ class IvfIndex {
   std::unique_ptr<uv_ivf, detail::IvfDel> ivf_;
   size_t dim_;
   IvfCodec codec_;
+};
+
+/* ---- CosetTrellis (src/coset_trellis.rs) --------------------------------- */
+
+// The reference's research arm behind ULTRAVEC_COSET_TRELLIS=1: trellis-coded
+// quantization over the eight cosets of an E8 sublattice, one handle holding
+// codec and entries.
+class CosetTrellis : public VectorBackend {
+ public:
+  // CosetTrellis::new(dim, bits) (src/coset_trellis.rs:116-190): dim % 8 ==
+  // 0, bits 1..3, memory from ULTRAVEC_TRELLIS_MEM (default 12, clamped to
+  // 1..20), seed 42, three rotation rounds
+  static CosetTrellis make(size_t dim, uint8_t bits, int device = 0) {
+    const long mem = std::min(20L, std::max(1L, detail::env_long("ULTRAVEC_TRELLIS_MEM", 12)));
+    return with_params(dim, bits, (uint8_t)mem, 42, 3, device);
+  }
+  static CosetTrellis with_params(size_t dim, uint8_t bits, uint8_t mem, uint64_t rotation_seed,
+                                  uint8_t rotation_rounds, int device = 0) {
+    uv_coset *c = nullptr;
+    detail::check(uv_coset_create((int32_t)dim, bits, mem, rotation_seed, rotation_rounds,
+                                  device, &c));
+    return CosetTrellis(std::unique_ptr<uv_coset, detail::CosetDel>(c), dim);
+  }
+
+  CosetTrellis(CosetTrellis &&) noexcept = default;
+  CosetTrellis &operator=(CosetTrellis &&) noexcept = default;
+  CosetTrellis(const CosetTrellis &) = delete;
+  CosetTrellis &operator=(const CosetTrellis &) = delete;
+
+  // with_centroids (192-196), before the first add
+  CosetTrellis &with_centroids(const std::vector<std::vector<float>> &centroids) & {
+    const std::vector<float> flat = detail::flatten(centroids, dim_);
+    detail::check(uv_coset_set_centroids(c_.get(), flat.data(), (int32_t)centroids.size()));
+    return *this;
+  }
+  CosetTrellis with_centroids(const std::vector<std::vector<float>> &centroids) && {
+    return std::move(with_centroids(centroids));
+  }
+
+  size_t dimensions() const override { return dim_; }
+  size_t len() const override {
+    int64_t n = 0;
+    detail::check(uv_coset_len(c_.get(), &n));
+    return (size_t)n;
+  }
+  void add(ItemId id, const std::vector<float> &embedding) override {
+    detail::require(embedding.size() == dim_, "row length differs from the codec's dimension");
+    detail::check(uv_coset_add(c_.get(), &id, embedding.data(), 1, nullptr));
+  }
+  // ids 0..n, as the reference's add_batch assigns them (454-469)
+  void add_batch(const std::vector<std::vector<float>> &embeddings) override {
+    const std::vector<float> flat = detail::flatten(embeddings, dim_);
+    detail::check(uv_coset_add(c_.get(), nullptr, embeddings.empty() ? nullptr : flat.data(),
+                               (int64_t)embeddings.size(), nullptr));
+  }
+  // any limit (the reference sorts every score and truncates)
+  Hits search(const std::vector<float> &query, size_t limit) const override {
+    detail::require(query.size() == dim_, "query length differs from the codec's dimension");
+    const size_t k = std::min(limit, len());
+    if (k == 0) return {};
+    std::vector<int64_t> ids(k, -1);
+    std::vector<float> scores(k, 0.0f);
+    detail::require(k <= (size_t)INT32_MAX, "k too large");
+    detail::check(uv_coset_search(c_.get(), query.data(), 1, (int32_t)k, ids.data(),
+                                  scores.data(), nullptr));
+    return detail::collect(ids.data(), scores.data(), k);
+  }
+  SearchBatch search_batch(const float *queries, size_t nq, size_t k,
+                           void *stream = nullptr) const {
+    SearchBatch out;
+    out.nq = nq;
+    out.k = k;
+    out.ids.assign(nq * k, -1);
+    out.scores.assign(nq * k, 0.0f);
+    if (nq == 0 || k == 0) return out;
+    detail::check(uv_coset_search(c_.get(), queries, (int64_t)nq, (int32_t)k, out.ids.data(),
+                                  out.scores.data(), stream));
+    return out;
+  }
+  size_t mem_bytes() const override {
+    int64_t b = 0;
+    detail::check(uv_coset_mem_bytes(c_.get(), &b));
+    return (size_t)b;
+  }
+  MemoryBreakdown memory_breakdown() const override {
+    MemoryBreakdown m;
+    m.code_bytes = mem_bytes();
+    int64_t b = 0;
+    detail::check(uv_coset_model_bytes(c_.get(), &b));
+    m.model_bytes = (size_t)b;
+    return m;
+  }
+  bool is_approximate() const override { return true; }
+  // reconstruct_unit (521-529)
+  std::optional<std::vector<float>> reconstruct_unit(const std::vector<float> &x) const override {
+    detail::require(x.size() == dim_, "row length differs from the codec's dimension");
+    std::vector<float> out(dim_);
+    detail::check(uv_coset_reconstruct(c_.get(), x.data(), 1, out.data(), nullptr));
+    return out;
+  }
+  uv_coset *handle() const { return c_.get(); }
+
+ private:
+  CosetTrellis(std::unique_ptr<uv_coset, detail::CosetDel> c, size_t dim)
+      : c_(std::move(c)), dim_(dim) {}
+
+  std::unique_ptr<uv_coset, detail::CosetDel> c_;
+  size_t dim_;
 };
 
 }  // namespace ultravec

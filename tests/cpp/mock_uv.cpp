@@ -53,6 +53,10 @@ struct uv_ivf {
 struct uv_prepared {
   int64_t nq;
 };
+struct uv_coset {
+  int32_t dim, bits, mem;
+  int64_t n;
+};
 
 extern "C" {
 
@@ -133,11 +137,15 @@ int uv_encode(const uv_codec *c, const float *rows, int64_t n, const float *cent
   (void)centroids, (void)n_centroids, (void)rnorm, (void)cidx, (void)stream;
   if (c == nullptr || (n > 0 && (rows == nullptr || rescale == nullptr)))
     return fail(UV_EINVAL, "null argument");
+  if (n_centroids > 0 && centroids == nullptr) return fail(UV_EINVAL, "null centroids");
+  mock.n_centroids = n_centroids;
   const int cb = (c->cfg.dim * c->cfg.bits + 7) / 8;
   for (int64_t i = 0; i < n; i++) {
     for (int j = 0; j < cb; j++) codes[i * cb + j] = (uint8_t)((int)rows[i * c->cfg.dim] + i + j);
     start[i] = 7u + (uint32_t)i;
     rescale[i] = 1.0f;
+    if (rnorm) rnorm[i] = n_centroids > 0 ? 0.5f : 1.0f;
+    if (cidx) cidx[i] = n_centroids > 0 ? (uint32_t)(n_centroids - 1) : 0u;
   }
   return UV_OK;
 }
@@ -470,6 +478,93 @@ int uv_ivf_mem_bytes(const uv_ivf *x, int64_t *bytes) {
   MOCK_ENTER("uv_ivf_mem_bytes");
   if (x == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
   *bytes = x->n * 45;
+  return UV_OK;
+}
+
+int uv_coset_create(int32_t dim, int32_t bits, int32_t mem, uint64_t rotation_seed,
+                    int32_t rotation_rounds, int32_t device, uv_coset **out) {
+  MOCK_ENTER("uv_coset_create");
+  (void)device;
+  if (out == nullptr) return fail(UV_EINVAL, "null argument");
+  if (dim % 8 != 0 || bits < 1 || bits > 3 || mem < 1 || mem > 20)
+    return fail(UV_EINVAL, "bad coset configuration");
+  mock.cfg.dim = dim;
+  mock.cfg.bits = bits;
+  mock.cfg.mem = mem;
+  mock.cfg.rotation_seed = rotation_seed;
+  mock.cfg.rotation_rounds = rotation_rounds;
+  *out = new uv_coset{dim, bits, mem, 0};
+  mock.live_indexes++;
+  return UV_OK;
+}
+
+int uv_coset_destroy(uv_coset *c) {
+  if (c == nullptr) return UV_OK;
+  mock.live_indexes--;
+  delete c;
+  return UV_OK;
+}
+
+int uv_coset_set_centroids(uv_coset *c, const float *centroids, int32_t n) {
+  MOCK_ENTER("uv_coset_set_centroids");
+  if (c == nullptr || (n > 0 && centroids == nullptr)) return fail(UV_EINVAL, "null argument");
+  if (c->n != 0) return fail(UV_EINVAL, "the index is not empty");
+  mock.n_centroids = n;
+  return UV_OK;
+}
+
+int uv_coset_add(uv_coset *c, const int64_t *ids, const float *rows, int64_t n, void *stream) {
+  MOCK_ENTER("uv_coset_add");
+  (void)stream;
+  if (c == nullptr || (n > 0 && rows == nullptr)) return fail(UV_EINVAL, "null argument");
+  mock.ids.assign(ids ? ids : nullptr, ids ? ids + n : nullptr);
+  mock.rows.assign(rows, rows + (size_t)n * c->dim);
+  c->n += n;
+  return UV_OK;
+}
+
+int uv_coset_search(const uv_coset *c, const float *queries, int64_t nq, int32_t k,
+                    int64_t *ids, float *scores, void *stream) {
+  MOCK_ENTER("uv_coset_search");
+  (void)queries, (void)stream;
+  if (c == nullptr || ids == nullptr || scores == nullptr || k < 1)
+    return fail(UV_EINVAL, "bad argument");
+  mock.k = k;
+  mock.nq = nq;
+  for (int64_t i = 0; i < nq * k; i++) {
+    ids[i] = (i % k) < c->n ? (i % k) : -1;
+    scores[i] = 5.0f - (float)(i % k);
+  }
+  return UV_OK;
+}
+
+int uv_coset_len(const uv_coset *c, int64_t *n) {
+  MOCK_ENTER("uv_coset_len");
+  if (c == nullptr || n == nullptr) return fail(UV_EINVAL, "null argument");
+  *n = c->n;
+  return UV_OK;
+}
+
+int uv_coset_mem_bytes(const uv_coset *c, int64_t *bytes) {
+  MOCK_ENTER("uv_coset_mem_bytes");
+  if (c == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
+  *bytes = c->n * 50;
+  return UV_OK;
+}
+
+int uv_coset_model_bytes(const uv_coset *c, int64_t *bytes) {
+  MOCK_ENTER("uv_coset_model_bytes");
+  if (c == nullptr || bytes == nullptr) return fail(UV_EINVAL, "null argument");
+  *bytes = 777;
+  return UV_OK;
+}
+
+int uv_coset_reconstruct(const uv_coset *c, const float *rows, int64_t n, float *out,
+                         void *stream) {
+  MOCK_ENTER("uv_coset_reconstruct");
+  (void)stream;
+  if (c == nullptr || rows == nullptr || out == nullptr) return fail(UV_EINVAL, "null argument");
+  for (int64_t i = 0; i < n * c->dim; i++) out[i] = -rows[i];
   return UV_OK;
 }
 

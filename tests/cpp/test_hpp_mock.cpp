@@ -259,7 +259,52 @@ static void coarse_and_ivf() {
   unsetenv("ULTRAVEC_TRELLIS_MEM");
 }
 
+static void reconstruct_and_coset() {
+  mock.reset();
+  {
+    // reconstruct_unit: encode (with the centroids when set), decode, normalize
+    TrellisQuantizer q = TrellisQuantizer::from_config(TrellisConfig::make(8, 2, 5));
+    const auto u = q.reconstruct_unit(std::vector<float>(8, 1.0f));
+    CHECK(u.has_value() && u->size() == 8 && mock.n_centroids == 0);
+    float ss = 0.0f;
+    for (float v : *u) ss += v * v;
+    CHECK(ss > 0.999f && ss < 1.001f);
+    TrellisQuantizer c = TrellisQuantizer::from_config(TrellisConfig::make(8, 2, 5))
+                             .with_centroids(rows(2, 8, 0.0f));
+    const auto uc = c.reconstruct_unit(std::vector<float>(8, 1.0f));
+    CHECK(mock.n_centroids == 2 && uc.has_value() && uc->size() == 8);
+    expect_error(UV_EINVAL, [&] { q.reconstruct_unit(std::vector<float>(7)); });
+  }
+  mock.reset();
+  setenv("ULTRAVEC_TRELLIS_MEM", "30", 1);  // clamped to 20, as the reference does
+  {
+    CosetTrellis ct = CosetTrellis::make(16, 2);
+    CHECK(mock.cfg.mem == 20 && mock.cfg.rotation_seed == 42 && mock.cfg.rotation_rounds == 3);
+  }
+  unsetenv("ULTRAVEC_TRELLIS_MEM");
+  // the reference panics on dim % 8 != 0: an error here
+  expect_error(UV_EINVAL, [] { CosetTrellis::make(12, 2); });
+  {
+    CosetTrellis ct = CosetTrellis::with_params(16, 2, 6, 42, 3).with_centroids(rows(2, 16, 0.0f));
+    CHECK(mock.n_centroids == 2);
+    ct.add_batch(rows(3, 16, 1.0f));
+    CHECK(mock.ids.empty() && mock.rows.size() == 48 && ct.len() == 3);  // ids 0..n
+    ct.add(9, std::vector<float>(16, 0.5f));
+    CHECK(mock.ids.size() == 1 && mock.ids[0] == 9 && ct.len() == 4);
+    const Hits h = ct.search(std::vector<float>(16, 1.0f), 1000);
+    CHECK(mock.k == 4 && h.size() == 4 && h[0].second == 5.0f);
+    CHECK(ct.mem_bytes() == 200 && ct.memory_breakdown().model_bytes == 777);
+    const auto r = ct.reconstruct_unit(std::vector<float>(16, 2.0f));
+    CHECK(r.has_value() && (*r)[3] == -2.0f);
+    expect_error(UV_EINVAL, [&] { ct.search(std::vector<float>(8), 3); });
+    VectorBackend &b = ct;  // usable through the reference's trait
+    CHECK(b.dimensions() == 16 && b.is_approximate() && !b.is_empty());
+  }
+  CHECK(mock.live_indexes == 0);
+}
+
 int main() {
+  reconstruct_and_coset();
   config_and_errors();
   environment_constructor();
   backend();
