@@ -242,6 +242,32 @@ struct TrellisConfig {
     return c;
   }
 
+  // the configuration TrellisQuantizer::new(dim, bits) builds from the
+  // environment (src/trellis.rs:460-540): ULTRAVEC_TRELLIS_MEM (default 12),
+  // _ANISO, _START_BITS (at most mem) and _RESCALE_BITS.  Knobs of research
+  // arms that are not built (beam, residual sketch, tail biting, the 1MAD
+  // code, vector trellis V > 1, fixed start) throw UV_EUNSUPPORTED when set
+  // to anything but their default.
+  static TrellisConfig from_env(size_t dim, uint8_t bits, int device = 0) {
+    const long mem = detail::env_long("ULTRAVEC_TRELLIS_MEM", 12);
+    if (detail::env_long("ULTRAVEC_TRELLIS_BEAM", 0) != 0 ||
+        detail::env_long("ULTRAVEC_TRELLIS_RESID", 0) != 0 ||
+        detail::env_is("ULTRAVEC_TRELLIS_TAILBITE", "1") ||
+        detail::env_is("ULTRAVEC_TRELLIS_CODE", "1mad") ||
+        detail::env_long("ULTRAVEC_TRELLIS_V", 1) > 1 ||
+        detail::env_is("ULTRAVEC_TRELLIS_FIXEDSTART", "1"))
+      throw Error(UV_EUNSUPPORTED, "this ULTRAVEC_TRELLIS_* research arm is not built");
+    detail::require(mem >= 1 && mem <= 24, "ULTRAVEC_TRELLIS_MEM out of range");
+    TrellisConfig cfg = make(dim, bits, (uint8_t)mem);
+    const char *aniso = std::getenv("ULTRAVEC_TRELLIS_ANISO");
+    if (aniso != nullptr && *aniso != '\0') cfg.branch_lambda = std::strtof(aniso, nullptr);
+    cfg.start_bits = (uint8_t)std::min<long>(
+        detail::env_long("ULTRAVEC_TRELLIS_START_BITS", mem), mem);
+    cfg.rescale_bits = (uint8_t)detail::env_long("ULTRAVEC_TRELLIS_RESCALE_BITS", 0);
+    cfg.device = device;
+    return cfg;
+  }
+
   uv_config raw() const {
     uv_config r;
     uv_config_default(&r, (int32_t)dim, (int32_t)bits, (int32_t)mem);
@@ -275,30 +301,11 @@ class TrellisQuantizer : public VectorBackend, public CandidateScorer {
  public:
   // TrellisQuantizer::new(dim, bits).with_codes_only(true): the research
   // harness's constructor, which reads its knobs from the environment
-  // (src/trellis.rs:418-420, 460-540): ULTRAVEC_TRELLIS_MEM (default 12),
-  // ULTRAVEC_TRELLIS_ANISO, ULTRAVEC_TRELLIS_START_BITS,
-  // ULTRAVEC_TRELLIS_RESCALE_BITS and the shortlist knobs.  Knobs of
-  // research arms that are not built (beam, residual sketch, tail biting,
-  // the 1MAD code, vector trellis V > 1, fixed start) throw UV_EUNSUPPORTED
-  // when set to anything but their default.
+  // (src/trellis.rs:418-420, 460-540; TrellisConfig::from_env) and the
+  // shortlist knobs ULTRAVEC_TRELLIS_SHORTLIST, _ASYM and _RNORM.
   static TrellisQuantizer make(size_t dim, uint8_t bits, int device = 0) {
-    const long mem = detail::env_long("ULTRAVEC_TRELLIS_MEM", 12);
-    if (detail::env_long("ULTRAVEC_TRELLIS_BEAM", 0) != 0 ||
-        detail::env_long("ULTRAVEC_TRELLIS_RESID", 0) != 0 ||
-        detail::env_is("ULTRAVEC_TRELLIS_TAILBITE", "1") ||
-        detail::env_is("ULTRAVEC_TRELLIS_CODE", "1mad") ||
-        detail::env_long("ULTRAVEC_TRELLIS_V", 1) > 1 ||
-        detail::env_is("ULTRAVEC_TRELLIS_FIXEDSTART", "1"))
-      throw Error(UV_EUNSUPPORTED, "this ULTRAVEC_TRELLIS_* research arm is not built");
-    detail::require(mem >= 1 && mem <= 24, "ULTRAVEC_TRELLIS_MEM out of range");
-    TrellisConfig cfg = TrellisConfig::make(dim, bits, (uint8_t)mem);
-    const char *aniso = std::getenv("ULTRAVEC_TRELLIS_ANISO");
-    if (aniso != nullptr && *aniso != '\0') cfg.branch_lambda = std::strtof(aniso, nullptr);
-    cfg.start_bits = (uint8_t)std::min<long>(
-        detail::env_long("ULTRAVEC_TRELLIS_START_BITS", mem), mem);
-    cfg.rescale_bits = (uint8_t)detail::env_long("ULTRAVEC_TRELLIS_RESCALE_BITS", 0);
+    TrellisConfig cfg = TrellisConfig::from_env(dim, bits, device);
     cfg.codes_only = true;
-    cfg.device = device;
     TrellisQuantizer q = from_config(cfg);
     const long c = detail::env_long("ULTRAVEC_TRELLIS_SHORTLIST", 0);
     if (c > 0) {
@@ -694,15 +701,15 @@ struct IvfCodec {
 class IvfIndex {
  public:
   // IvfIndex::build(dim, db, centroids, assign, codec, bits): each list's
-  // codec is TrellisQuantizer::new(dim, bits) (memory from the
-  // environment), centered on its centroid when ULTRAVEC_IVF_CENTER=1
+  // codec is TrellisQuantizer::new(dim, bits) (its knobs from the
+  // environment, TrellisConfig::from_env; the shortlist from `codec`, set
+  // explicitly as the reference does), centered on its centroid when
+  // ULTRAVEC_IVF_CENTER=1 (src/ivf.rs:98-150)
   static IvfIndex build(size_t dim, const std::vector<std::vector<float>> &db,
                         const std::vector<std::vector<float>> &centroids,
                         const std::vector<uint32_t> &assign, IvfCodec codec, uint8_t bits,
                         int device = 0) {
-    TrellisConfig cfg = TrellisConfig::make(
-        dim, bits, (uint8_t)detail::env_long("ULTRAVEC_TRELLIS_MEM", 12));
-    cfg.device = device;
+    const TrellisConfig cfg = TrellisConfig::from_env(dim, bits, device);
     return build_with(cfg, db, centroids, assign, codec,
                       detail::env_is("ULTRAVEC_IVF_CENTER", "1"));
   }

@@ -250,13 +250,18 @@ static void coarse_and_ivf() {
   mock.reset();
   setenv("ULTRAVEC_IVF_CENTER", "1", 1);
   setenv("ULTRAVEC_TRELLIS_MEM", "7", 1);
+  setenv("ULTRAVEC_TRELLIS_START_BITS", "4", 1);
+  setenv("ULTRAVEC_TRELLIS_SHORTLIST", "99", 1);  // ignored: the codec says no shortlist
   {
     IvfIndex ivf = IvfIndex::build(4, db, cen, asg, IvfCodec::trellis_codes(), 2);
-    CHECK(mock.centered == 1 && mock.cfg.mem == 7 && !mock.called("uv_ivf_set_shortlist"));
+    CHECK(mock.centered == 1 && mock.cfg.mem == 7 && mock.cfg.start_bits == 4);
+    CHECK(!mock.called("uv_ivf_set_shortlist"));
     CHECK(ivf.codec().label() == "trellis_codes");
   }
   unsetenv("ULTRAVEC_IVF_CENTER");
   unsetenv("ULTRAVEC_TRELLIS_MEM");
+  unsetenv("ULTRAVEC_TRELLIS_START_BITS");
+  unsetenv("ULTRAVEC_TRELLIS_SHORTLIST");
 }
 
 static void reconstruct_and_coset() {
