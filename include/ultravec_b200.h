@@ -198,7 +198,7 @@ int uv_index_clear(uv_index *index);
  * in_ids/in_scores are nq x n_lists x k_in, each list sorted by the ranking
  * above; out is nq x k (k <= n_lists x k_in).  Device or host memory.  Up
  * to 8192 entries per row a k-way merge of the sorted lists, above that a
- * segmented sort. */
+ * segmented sort.  nq = 0 returns UV_OK without reading any buffer. */
 int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream);
@@ -270,7 +270,9 @@ int uv_topk_unpack(int32_t device, const void *packed, int64_t n, int64_t *ids, 
  * contiguous records).  After an all-to-all of query slices the lists of
  * slice row q from shard l sit at l * (rows * k_in) + q * k_in, i.e.
  * row_stride = k_in, list_stride = rows * k_in.  Any sizes (above 8192
- * entries per row a segmented sort replaces the k-way merge). */
+ * entries per row a segmented sort replaces the k-way merge); nq = 0 (a
+ * rank with an empty query slice) returns UV_OK without reading any
+ * buffer, as uv_topk_merge does. */
 int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t n_lists,
                          int32_t k_in, int64_t row_stride, int64_t list_stride, int32_t k,
                          int64_t *out_ids, float *out_scores, void *stream);

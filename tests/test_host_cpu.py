@@ -76,6 +76,19 @@ def test_null_handles_are_refused_without_device_work(uv):
     assert checked >= 60
 
 
+def test_merges_of_no_rows_need_no_buffers_or_device(uv):
+    """A rank whose query slice is empty (fewer queries than ranks) merges
+    zero rows: the merges return UV_OK for null buffers and touch no device,
+    while bad sizes and null buffers with rows are still refused."""
+    lib = uv.lib()
+    assert lib.uv_topk_merge_packed(0, None, 0, 4, 10, 10, 0, 10, None, None, None) == 0
+    assert lib.uv_topk_merge(0, None, None, 0, 4, 10, 10, None, None, None) == 0
+    assert lib.uv_topk_merge_packed(0, None, 3, 4, 10, 10, 30, 10, None, None, None) == 1
+    assert lib.uv_topk_merge(0, None, None, 0, 4, 10, 41, None, None, None) == 1
+    assert lib.uv_topk_pack(0, None, None, 0, None, None) == 0
+    assert lib.uv_topk_unpack(0, None, 0, None, None, None) == 0
+
+
 def test_shard_ranges_partition_the_rows(uv):
     from ultravec_ann_b200.shard import shard_range
 

@@ -2083,11 +2083,12 @@ extern "C" {
 int uv_topk_merge(int32_t device, const int64_t *in_ids, const float *in_scores, int64_t nq,
                   int32_t n_lists, int32_t k_in, int32_t k, int64_t *out_ids, float *out_scores,
                   void *stream) {
-  if (in_ids == nullptr || in_scores == nullptr || out_ids == nullptr)
-    return fail(UV_EINVAL, "null argument");
   if (nq < 0 || n_lists < 1 || k_in < 1 || k < 1 || k > n_lists * k_in)
     return fail(UV_EINVAL, "bad sizes");
+  // no rows: nothing to read or write (an empty tensor's buffer may be null)
   if (nq == 0) return UV_OK;
+  if (in_ids == nullptr || in_scores == nullptr || out_ids == nullptr)
+    return fail(UV_EINVAL, "null argument");
   DeviceGuard g(device);
   cudaStream_t st = (cudaStream_t)stream;
   Scratch sc(st);
@@ -2160,11 +2161,13 @@ int uv_topk_unpack(int32_t device, const void *packed, int64_t n, int64_t *ids, 
 int uv_topk_merge_packed(int32_t device, const void *packed, int64_t nq, int32_t n_lists,
                          int32_t k_in, int64_t row_stride, int64_t list_stride, int32_t k,
                          int64_t *out_ids, float *out_scores, void *stream) {
-  if (packed == nullptr || out_ids == nullptr) return fail(UV_EINVAL, "null argument");
   if (nq < 0 || n_lists < 1 || k_in < 1 || k < 1 || k > n_lists * k_in || row_stride < 0 ||
       list_stride < 0)
     return fail(UV_EINVAL, "bad sizes");
+  // a rank whose query slice is empty (fewer queries than ranks) merges
+  // nothing; its buffers are empty tensors, whose pointers may be null
   if (nq == 0) return UV_OK;
+  if (packed == nullptr || out_ids == nullptr) return fail(UV_EINVAL, "null argument");
   DeviceGuard g(device);
   bool on_dev = false;
   UV_TRY(classify(packed, device, &on_dev));
